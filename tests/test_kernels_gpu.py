@@ -1,0 +1,259 @@
+"""Numerics of every sm_100a kernel against the PyTorch fp32 reference of the same op."""
+import math
+
+import pytest
+import torch
+
+from vllm_sly_radiance_b200.ops import kernels as K
+from vllm_sly_radiance_b200.ops import reference as ref
+from vllm_sly_radiance_b200.quant.mxfp4 import MXFP4Weight
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def fp8_close(q, s, qw, sw):
+    """Dequantized e4m3 rows agree up to one e4m3 step (bf16 rounding of the producer input
+    can flip a code when the kernel's rsqrt/exp differ from torch's in the last bit)."""
+    dq = q.cpu().float() * s.cpu().float()[:, None]
+    dw = qw.cpu().float() * sw.cpu().float()[:, None]
+    tol = 0.07 * dw.abs() + 1e-3 * dw.abs().max()
+    bad = ((dq - dw).abs() > tol).float().mean()
+    return float(bad) < 1e-3
+
+
+def rel_err(a, b):
+    a = a.float().cpu()
+    b = b.float().cpu()
+    return float((a - b).abs().max() / b.abs().max().clamp(min=1e-6))
+
+
+@pytest.mark.parametrize("M,N,Kd,splits", [
+    (1, 256, 256, 0), (5, 384, 512, 0), (16, 256, 1024, 4), (37, 200, 768, 0),
+    (64, 512, 512, 2), (128, 256, 256, 0), (300, 512, 1024, 0), (1, 5120, 8704, 0),
+    (8, 16480, 5120, 0), (520, 640, 2048, 1)])
+def test_mxfp4_gemm(M, N, Kd, splits):
+    g = torch.Generator().manual_seed(M * 7 + N)
+    w = torch.randn(N, Kd, generator=g) * 0.02
+    x = torch.randn(M, Kd, generator=g)
+    wq = MXFP4Weight.from_float(w)
+    q, s = ref.quant_fp8_rows(x.to(torch.bfloat16))
+    want = ref.mxfp4_linear(q, s, wq.packed, wq.scales)
+    wg = wq.to(DEV)
+    got = K.mxfp4_gemm(q.to(DEV), s.to(DEV), wg.packed, wg.sf, wg.scales, N, splits=splits)
+    torch.cuda.synchronize()
+    K.check_status(got.device)
+    assert rel_err(got, want) < 1e-2, rel_err(got, want)
+
+
+def test_mxfp4_gemm_repeat_no_stale_state():
+    """Back-to-back launches without a sync between them (split-K reduction must not leak)."""
+    g = torch.Generator().manual_seed(3)
+    N, Kd = 1024, 4096
+    wq = MXFP4Weight.from_float(torch.randn(N, Kd, generator=g) * 0.02)
+    wg = wq.to(DEV)
+    outs, wants = [], []
+    for i in range(4):
+        x = torch.randn(3, Kd, generator=g)
+        q, s = ref.quant_fp8_rows(x.to(torch.bfloat16))
+        wants.append(ref.mxfp4_linear(q, s, wq.packed, wq.scales))
+        outs.append(K.mxfp4_gemm(q.to(DEV), s.to(DEV), wg.packed, wg.sf, wg.scales, N))
+    torch.cuda.synchronize()
+    for o, w_ in zip(outs, wants):
+        assert rel_err(o, w_) < 1e-2
+
+
+@pytest.mark.parametrize("M,H,with_res", [(1, 5120, True), (7, 256, False), (33, 2048, True)])
+def test_add_rms_quant(M, H, with_res):
+    g = torch.Generator().manual_seed(M + H)
+    x = torch.randn(M, H, generator=g).to(torch.bfloat16)
+    r = torch.randn(M, H, generator=g).to(torch.bfloat16) if with_res else None
+    w = (torch.randn(H, generator=g) * 0.1).to(torch.bfloat16)
+    qw, sw, rw = ref.add_rms_quant(x, r, w, 1e-6)
+    q, s, ro = K.add_rms_quant(x.to(DEV), None if r is None else r.to(DEV), w.to(DEV), 1e-6)
+    torch.cuda.synchronize()
+    assert torch.equal(ro.cpu(), rw)
+    torch.testing.assert_close(s.cpu(), sw, rtol=1e-5, atol=0)
+    assert fp8_close(q, s, qw, sw)
+
+
+def test_silu_mul_and_gdn_norm_and_gate():
+    g = torch.Generator().manual_seed(1)
+    gu = torch.randn(9, 2 * 1024, generator=g).to(torch.bfloat16)
+    qw, sw = ref.silu_mul_quant(gu)
+    q, s = K.silu_mul_quant(gu.to(DEV))
+    assert fp8_close(q, s, qw, sw)
+    o = torch.randn(5, 4 * 128, generator=g).to(torch.bfloat16)
+    zbuf = torch.randn(5, 3 * 4 * 128, generator=g).to(torch.bfloat16)
+    z = zbuf[:, 512:1024]
+    w = (1 + 0.1 * torch.randn(128, generator=g)).to(torch.bfloat16)
+    qw, sw = ref.gdn_norm_quant(o, z, w, 1e-6, 128)
+    q, s = K.gdn_norm_quant(o.to(DEV), zbuf.to(DEV)[:, 512:1024], w.to(DEV), 1e-6, 128)
+    assert fp8_close(q, s, qw, sw)
+    a = torch.randn(6, 3 * 64, generator=g).to(torch.bfloat16)
+    qkv = torch.randn(6, 3 * 128, generator=g).to(torch.bfloat16)
+    qw, sw = K.gate_mul_quant(a, qkv[:, 64:], 64, 128)
+    q, s = K.gate_mul_quant(a.to(DEV), qkv.to(DEV)[:, 64:], 64, 128)
+    assert fp8_close(q, s, qw, sw)
+
+
+class _Meta:
+    pass
+
+
+def _attn_meta(q_lens, ctx_lens, block_size, Hq, Hkv, num_splits, dev):
+    B = len(q_lens)
+    m = _Meta()
+    qsl = [0]
+    for ql in q_lens:
+        qsl.append(qsl[-1] + ql)
+    seq_lens = [c + q for c, q in zip(ctx_lens, q_lens)]
+    max_blocks = max((s + block_size - 1) // block_size for s in seq_lens)
+    bt = torch.zeros(B, max_blocks, dtype=torch.int32)
+    nxt = 0
+    perm = torch.randperm(B * max_blocks, generator=torch.Generator().manual_seed(0))
+    for b in range(B):
+        for j in range(max_blocks):
+            bt[b, j] = int(perm[nxt])
+            nxt += 1
+    G = Hq // Hkv
+    ts, tr = [], []
+    for b in range(B):
+        R = q_lens[b] * G
+        for r0 in range(0, R, 64):
+            ts.append(b)
+            tr.append(r0)
+    m.query_start_loc = torch.tensor(qsl, dtype=torch.int32, device=dev)
+    m.seq_lens = torch.tensor(seq_lens, dtype=torch.int32, device=dev)
+    m.block_tables = bt.to(dev)
+    m.tile_seq = torch.tensor(ts, dtype=torch.int32, device=dev)
+    m.tile_row0 = torch.tensor(tr, dtype=torch.int32, device=dev)
+    m.num_splits = num_splits
+    m.scratch_o = lambda s, T, H, D: torch.empty(s, T, H, D, device=dev)
+    m.scratch_ml = lambda s, T, H: torch.empty(s, T, H, 2, device=dev)
+    return m, B * max_blocks
+
+
+@pytest.mark.parametrize("D,Hq,Hkv,q_lens,ctx_lens,splits,fp8", [
+    (256, 24, 4, [1, 1, 1], [100, 1500, 63], 1, True),
+    (256, 24, 4, [1, 1], [3000, 700], 8, True),
+    (256, 24, 4, [8, 8], [500, 1200], 4, True),
+    (256, 24, 4, [200, 70], [0, 130], 1, True),
+    (64, 4, 2, [33, 1], [0, 90], 1, False),
+    (128, 32, 8, [8], [250], 2, True)])
+def test_paged_attention(D, Hq, Hkv, q_lens, ctx_lens, splits, fp8):
+    torch.manual_seed(0)
+    bs = 64
+    meta, nblocks = _attn_meta(q_lens, ctx_lens, bs, Hq, Hkv, splits, DEV)
+    cdt = torch.float8_e4m3fn if fp8 else torch.bfloat16
+    kc = (torch.randn(nblocks, Hkv, bs, D) * 0.5).to(cdt)
+    vc = torch.randn(nblocks, Hkv, bs, D).to(cdt)
+    T = sum(q_lens)
+    q = torch.randn(T, Hq, D).to(torch.bfloat16)
+    if fp8:
+        q = ref.fp8_e4m3(q.float()).to(torch.bfloat16)
+    scale = D ** -0.5
+    metac = _Meta()
+    metac.block_tables = meta.block_tables.cpu()
+    metac.seq_lens = meta.seq_lens.cpu()
+    metac.query_start_loc = meta.query_start_loc.cpu()
+    want = ref.paged_attention(q, kc, vc, metac.block_tables, metac.seq_lens,
+                               metac.query_start_loc, bs, scale)
+    got = K.paged_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), meta, scale)
+    torch.cuda.synchronize()
+    assert rel_err(got, want) < 2e-2, rel_err(got, want)
+
+
+def test_qkv_prologue():
+    torch.manual_seed(1)
+    T, Hq, Hkv, D, rot = 5, 4, 2, 256, 64
+    bs = 64
+    qkv = torch.randn(T, Hq * D * 2 + 2 * Hkv * D).to(torch.bfloat16)
+    pos = torch.tensor([0, 1, 7, 300, 65000], dtype=torch.int32)
+    qn = (0.1 * torch.randn(D)).to(torch.bfloat16)
+    kn = (0.1 * torch.randn(D)).to(torch.bfloat16)
+    slots = torch.tensor([3, 64, 65, 130, 200], dtype=torch.int64)
+    kc = torch.zeros(4, Hkv, bs, D, dtype=torch.float8_e4m3fn)
+    vc = torch.zeros_like(kc)
+    kw = dict(num_q_heads=Hq, num_kv_heads=Hkv, head_dim=D, rotary_dim=rot, theta=1e7, eps=1e-6,
+              gated=True, block_size=bs)
+    qw = K.qkv_prologue(qkv, pos, qn, kn, None, kc, vc, slots, **kw)
+    from vllm_sly_radiance_b200.models.layers import rope_cache
+    cs = rope_cache(70000, rot, 1e7, DEV)
+    kcg, vcg = torch.zeros_like(kc).to(DEV), torch.zeros_like(vc).to(DEV)
+    qg = K.qkv_prologue(qkv.to(DEV), pos.to(DEV), qn.to(DEV), kn.to(DEV), cs, kcg, vcg,
+                        slots.to(DEV), **kw)
+    torch.cuda.synchronize()
+    assert rel_err(qg, qw) < 2e-2
+    assert rel_err(kcg.float(), kc.float()) < 2e-2
+    assert torch.equal(vcg.cpu().float(), vc.float())
+
+
+def test_gdn_conv_and_recurrent():
+    torch.manual_seed(2)
+    Hk, Hv, Dh, W = 2, 4, 64, 4
+    key_dim, vdim = Hk * Dh, Hv * Dh
+    C = 2 * key_dim + vdim
+    q_lens = [1, 5, 70]
+    has_init = [1, 1, 0]
+    slots = [2, 0, 1]
+    qsl = [0, 1, 6, 76]
+    T = qsl[-1]
+    x = torch.randn(T, C + vdim + 2 * Hv).to(torch.bfloat16)
+    conv_w = (0.3 * torch.randn(C, W)).to(torch.bfloat16)
+    conv_state = torch.randn(3, C, W - 1).to(torch.bfloat16)
+    ssm = torch.randn(3, Hv, Dh, Dh) * 0.1
+    A_log = torch.log(torch.rand(Hv) * 15 + 1)
+    dt_bias = torch.randn(Hv) * 0.1
+    m = _Meta()
+    m.num_seqs = 3
+    m.query_start_loc = torch.tensor(qsl, dtype=torch.int32)
+    m.state_slots = torch.tensor(slots, dtype=torch.int32)
+    m.has_initial = torch.tensor(has_init, dtype=torch.int32)
+    m.token_seq = torch.tensor(sum([[b] * l for b, l in enumerate(q_lens)], []), dtype=torch.int32)
+    mg = _Meta()
+    for k_ in ("query_start_loc", "state_slots", "has_initial", "token_seq"):
+        setattr(mg, k_, getattr(m, k_).to(DEV))
+    mg.num_seqs = 3
+    y_w = K.gdn_conv(x[:, :C], conv_w, conv_state, m, key_dim, Dh)
+    y_g = K.gdn_conv(x.to(DEV)[:, :C], conv_w.to(DEV), conv_state.to(DEV), mg, key_dim, Dh)
+    torch.cuda.synchronize()
+    assert rel_err(y_g, y_w) < 2e-2
+    ba = x[:, C + vdim:]
+    ssm_w = ssm.clone()
+    o_w = K.gdn_recurrent(y_w, ba, A_log, dt_bias, ssm_w, m, Hk, Dh ** -0.5)
+    ssm_g = ssm.clone().to(DEV)
+    o_g = K.gdn_recurrent(y_w.to(DEV), ba.to(DEV), A_log.to(DEV), dt_bias.to(DEV), ssm_g, mg, Hk,
+                          Dh ** -0.5)
+    torch.cuda.synchronize()
+    assert rel_err(o_g, o_w) < 2e-2
+    assert rel_err(ssm_g, ssm_w) < 1e-3
+    cs_w = conv_state.clone()
+    K.gdn_conv_state_update(x[:, :C], cs_w, m)
+    cs_g = conv_state.clone().to(DEV)
+    K.gdn_conv_state_update(x.to(DEV)[:, :C], cs_g, mg)
+    torch.cuda.synchronize()
+    assert torch.equal(cs_g.cpu(), cs_w)
+
+
+def test_argmax_and_sampling():
+    torch.manual_seed(3)
+    x = torch.randn(5, 248320).to(torch.bfloat16)
+    ids = K.argmax(x.to(DEV))
+    assert torch.equal(ids.cpu(), x.float().argmax(-1))
+    vals, idx = torch.topk(x.float(), 64, dim=-1)
+    B = 5
+    temp = torch.tensor([0.0, 0.7, 1.0, 0.7, 0.7])
+    topk = torch.tensor([20, 20, 0, 1, 64], dtype=torch.int32)
+    topp = torch.tensor([0.95, 0.95, 1.0, 0.9, 0.5])
+    seeds = torch.arange(B, dtype=torch.int64)
+    out, probs = K.sample_from_topk(vals.to(DEV), idx.to(DEV), temp.to(DEV), topk.to(DEV),
+                                    topp.to(DEV), None, seeds.to(DEV), 0, want_probs=True)
+    torch.cuda.synchronize()
+    out = out.cpu()
+    assert out[0] == idx[0, 0] and out[3] == idx[3, 0]
+    for b in range(B):
+        assert int(out[b]) in idx[b].tolist()
+    # probabilities of the kept window sum to one for sampled rows
+    for b in (1, 2, 4):
+        assert abs(float(probs[b].sum()) - 1.0) < 1e-4

@@ -1,0 +1,496 @@
+// Paged attention for the hybrid model's full-attention layers (head_dim 64 or 256, GQA, fp8 or
+// bf16 KV cache in pages of 64 tokens, layout [block, kv_head, slot, head_dim]).
+//
+// Reference behaviour: the AITER unified attention the reference tunes for decode/verify
+// (sly/radiance_attn_decode.py:115-209: split-KV with segment reduce) and the libr4d paged prefill
+// kernel (r4d_attn_prefill_h256_gqa6, radiance_r4d_hybrid_attn.py:1-97: chunked causal prefill
+// over the paged fp8 cache, e4m3 query).  Here one varlen kernel serves both:
+//
+//  * qkv_prologue : per (token, head) Gemma RMSNorm of q and k, neox RoPE on the first rotary_dim
+//                   dims (cos/sin table precomputed in fp64), k and v written to the paged cache
+//                   (e4m3), q written as bf16 (rounded through e4m3 when the cache is fp8, the
+//                   reference's fp8-query contract).
+//  * paged_attn   : rows = (query token, q head of the GQA group) of one kv head, 64 rows per CTA
+//                   (4 warps x 16), keys in 64-token pages; S = QK^T and O += PV on tensor cores,
+//                   online softmax in registers, causal + sliding-window masks.  Split-KV along the
+//                   context with a per-sequence split length computed on the device (CUDA-graph
+//                   safe); partials merged by attn_merge.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace rad {
+namespace attn {
+
+// ------------------------------------------------------------------------------------------------
+// prologue: one warp per (token, head); heads [0, Hq) are q heads, [Hq, Hq+Hkv) kv heads
+// ------------------------------------------------------------------------------------------------
+template <int D>
+__global__ void __launch_bounds__(256) qkv_prologue_kernel(
+    const __nv_bfloat16* __restrict__ qkv, int ldqkv, int q_head_stride,   // q head h at col h*q_head_stride
+    int k_off, int v_off, const int* __restrict__ positions,
+    const __nv_bfloat16* __restrict__ qn_w, const __nv_bfloat16* __restrict__ kn_w,
+    const float* __restrict__ cos_sin, int rot, int T, int Hq, int Hkv, float eps,
+    __nv_bfloat16* __restrict__ q_out, uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache,
+    int cache_fp8, const int64_t* __restrict__ slot_mapping, int block_size) {
+  constexpr int PER = D / 32;
+  const int gw = blockIdx.x * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int H = Hq + Hkv;
+  if (gw >= T * H) return;
+  const int t = gw / H, h = gw % H;
+  const bool isq = h < Hq;
+  const __nv_bfloat16* src = qkv + (size_t)t * ldqkv + (isq ? h * q_head_stride : k_off + (h - Hq) * D);
+  float x[PER];
+  float ss = 0.f;
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    x[p] = __bfloat162float(src[lane * PER + p]);
+    ss += x[p] * x[p];
+  }
+  ss = warp_sum(ss);
+  const float rs = rsqrtf(ss / (float)D + eps);
+  const __nv_bfloat16* nw = isq ? qn_w : kn_w;
+#pragma unroll
+  for (int p = 0; p < PER; ++p) x[p] = bf16_round(x[p] * rs * (__bfloat162float(nw[lane * PER + p]) + 1.f));
+  // RoPE (neox): element i < rot/2 pairs with i + rot/2
+  const int pos = positions[t];
+  const int half = rot / 2;
+  const int off = half / PER;            // partner lane distance (power of two)
+  float partner[PER];
+#pragma unroll
+  for (int p = 0; p < PER; ++p) partner[p] = __shfl_xor_sync(0xffffffff, x[p], off > 0 ? off : 1);
+  if (lane * PER < rot) {
+#pragma unroll
+    for (int p = 0; p < PER; ++p) {
+      const int i = lane * PER + p;
+      const int fi = i % half;
+      const float c = cos_sin[(size_t)pos * rot + fi];
+      const float s = cos_sin[(size_t)pos * rot + half + fi];
+      x[p] = (i < half) ? (x[p] * c - partner[p] * s) : (x[p] * c + partner[p] * s);
+    }
+  }
+  if (isq) {
+    __nv_bfloat16* dst = q_out + ((size_t)t * Hq + h) * D;
+#pragma unroll
+    for (int p = 0; p < PER; ++p) {
+      float v = bf16_round(x[p]);
+      if (cache_fp8) v = e4m3_to_f32(f32_to_e4m3(v));
+      dst[lane * PER + p] = __float2bfloat16_rn(v);
+    }
+  } else {
+    const int hk = h - Hq;
+    const int64_t slot = slot_mapping[t];
+    if (slot < 0) return;
+    const int64_t blk = slot / block_size, off2 = slot % block_size;
+    const size_t base = (((size_t)blk * Hkv + hk) * block_size + off2) * D;
+    const __nv_bfloat16* vsrc = qkv + (size_t)t * ldqkv + v_off + hk * D;
+    if (cache_fp8) {
+#pragma unroll
+      for (int p = 0; p < PER; ++p) {
+        k_cache[base + lane * PER + p] = f32_to_e4m3(bf16_round(x[p]));
+        v_cache[base + lane * PER + p] = f32_to_e4m3(__bfloat162float(vsrc[lane * PER + p]));
+      }
+    } else {
+      __nv_bfloat16* kc = reinterpret_cast<__nv_bfloat16*>(k_cache);
+      __nv_bfloat16* vc = reinterpret_cast<__nv_bfloat16*>(v_cache);
+#pragma unroll
+      for (int p = 0; p < PER; ++p) {
+        kc[base + lane * PER + p] = __float2bfloat16_rn(x[p]);
+        vc[base + lane * PER + p] = vsrc[lane * PER + p];
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// paged attention
+// ------------------------------------------------------------------------------------------------
+constexpr int BR = 64;        // rows per CTA
+constexpr int BC = 64;        // keys per tile (= one KV page)
+
+DEVI void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+DEVI void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+DEVI void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                   uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+DEVI uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+// swizzled byte offset of (row, 16-byte chunk) in a tile with `chunks` chunks per row
+DEVI uint32_t swz(int row, int chunk, int chunks) { return (uint32_t)(row * chunks + (chunk ^ (row & 7))) * 16u; }
+
+template <int D, bool FP8>
+__global__ void __launch_bounds__(128) paged_attn_kernel(
+    const __nv_bfloat16* __restrict__ q, const uint8_t* __restrict__ k_cache,
+    const uint8_t* __restrict__ v_cache, const int* __restrict__ block_tables, int bt_stride,
+    const int* __restrict__ seq_lens, const int* __restrict__ qsl,
+    const int* __restrict__ tile_seq, const int* __restrict__ tile_row0, int Hq, int Hkv,
+    int block_size, float scale_log2, int causal, int window, int num_splits,
+    __nv_bfloat16* __restrict__ out, float* __restrict__ part_o, float* __restrict__ part_ml,
+    int T) {
+  constexpr int CH = D / 8;               // 16-byte chunks per row (bf16)
+  constexpr int NT = BC / 8;              // n-tiles of S per warp (8 keys each)
+  constexpr int OT = D / 8;               // n-tiles of O per warp
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* sQ = smem;                                   // [BR][D] bf16 swizzled
+  uint8_t* sK = smem + BR * D * 2;                      // [BC][D]
+  uint8_t* sV = sK + BC * D * 2;                        // [BC][D]
+
+  const int tile = blockIdx.x, hk = blockIdx.y, split = blockIdx.z;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int b = tile_seq[tile];
+  const int row0 = tile_row0[tile];
+  const int G = Hq / Hkv;
+  const int s0 = qsl[b];
+  const int ql = qsl[b + 1] - s0;
+  const int L = seq_lens[b];
+  const int R = ql * G;
+  const int rows_here = min(BR, R - row0);
+  // key range needed by this tile: causal -> up to the last row's position
+  const int last_i = (row0 + rows_here - 1) / G;
+  const int first_i = row0 / G;
+  const int kv_end = causal ? (L - ql + last_i + 1) : L;
+  int kv_begin = 0;
+  if (window > 0) kv_begin = max(0, L - ql + first_i - window + 1);
+  // split range (device-side, graph safe)
+  const int ntiles_total = (kv_end + BC - 1) / BC;
+  const int tile_begin = kv_begin / BC;
+  const int ntiles = ntiles_total - tile_begin;
+  const int per = (ntiles + num_splits - 1) / num_splits;
+  const int t_lo = tile_begin + split * per;
+  const int t_hi = min(ntiles_total, t_lo + per);
+
+  // ---- load Q tile (rows beyond R zero) ----
+  for (int idx = threadIdx.x; idx < BR * CH; idx += 128) {
+    const int r = idx / CH, c = idx % CH;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    const int rr = row0 + r;
+    if (rr < R) {
+      const int i = rr / G, g = rr % G;
+      const __nv_bfloat16* src = q + ((size_t)(s0 + i) * Hq + hk * G + g) * D + c * 8;
+      val = *reinterpret_cast<const uint4*>(src);
+    }
+    *reinterpret_cast<uint4*>(sQ + swz(r, c, CH)) = val;
+  }
+
+  float o[OT][4];
+#pragma unroll
+  for (int j = 0; j < OT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  const int g_ = lane / 4, t4 = lane % 4;
+  // query positions of this thread's two rows
+  const int rA = row0 + warp * 16 + g_, rB = rA + 8;
+  const int posA = L - ql + rA / G, posB = L - ql + rB / G;
+  const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV);
+
+  for (int kt = t_lo; kt < t_hi; ++kt) {
+    __syncthreads();
+    // ---- load K/V page kt (fp8 -> bf16 or bf16 copy) ----
+    const int blk = block_tables[(size_t)b * bt_stride + (kt * BC) / block_size];
+    const int in_blk = (kt * BC) % block_size;
+    const size_t base = (((size_t)blk * Hkv + hk) * block_size + in_blk) * D;
+    if constexpr (FP8) {
+      for (int idx = threadIdx.x; idx < BC * D / 16; idx += 128) {
+        const int r = idx / (D / 16), c16 = idx % (D / 16);   // 16 fp8 = two bf16 chunks
+        uint4 kv = *reinterpret_cast<const uint4*>(k_cache + base + (size_t)r * D + c16 * 16);
+        uint4 vv = *reinterpret_cast<const uint4*>(v_cache + base + (size_t)r * D + c16 * 16);
+        const uint8_t* kb = reinterpret_cast<const uint8_t*>(&kv);
+        const uint8_t* vb = reinterpret_cast<const uint8_t*>(&vv);
+        uint32_t kw[8], vw[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          kw[e] = pack_bf16(e4m3_to_f32(kb[2 * e]), e4m3_to_f32(kb[2 * e + 1]));
+          vw[e] = pack_bf16(e4m3_to_f32(vb[2 * e]), e4m3_to_f32(vb[2 * e + 1]));
+        }
+        *reinterpret_cast<uint4*>(sK + swz(r, 2 * c16, CH)) = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+        *reinterpret_cast<uint4*>(sK + swz(r, 2 * c16 + 1, CH)) = make_uint4(kw[4], kw[5], kw[6], kw[7]);
+        *reinterpret_cast<uint4*>(sV + swz(r, 2 * c16, CH)) = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+        *reinterpret_cast<uint4*>(sV + swz(r, 2 * c16 + 1, CH)) = make_uint4(vw[4], vw[5], vw[6], vw[7]);
+      }
+    } else {
+      const __nv_bfloat16* kc = reinterpret_cast<const __nv_bfloat16*>(k_cache);
+      const __nv_bfloat16* vc = reinterpret_cast<const __nv_bfloat16*>(v_cache);
+      for (int idx = threadIdx.x; idx < BC * CH; idx += 128) {
+        const int r = idx / CH, c = idx % CH;
+        *reinterpret_cast<uint4*>(sK + swz(r, c, CH)) = *reinterpret_cast<const uint4*>(kc + base + (size_t)r * D + c * 8);
+        *reinterpret_cast<uint4*>(sV + swz(r, c, CH)) = *reinterpret_cast<const uint4*>(vc + base + (size_t)r * D + c * 8);
+      }
+    }
+    __syncthreads();
+
+    // ---- S = Q K^T (16 rows x 64 keys per warp) ----
+    float s[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t a0, a1, a2, a3;
+      {
+        const int r = warp * 16 + (lane % 16);
+        const int c = kk * 2 + lane / 16;
+        ldsm_x4(sQa + swz(r, c, CH), a0, a1, a2, a3);
+      }
+#pragma unroll
+      for (int jn = 0; jn < NT; jn += 2) {
+        uint32_t b0, b1, b2, b3;
+        const int r = jn * 8 + (lane % 8) + (lane / 16) * 8;
+        const int c = kk * 2 + ((lane / 8) % 2);
+        ldsm_x4(sKa + swz(r, c, CH), b0, b1, b2, b3);
+        mma_bf16(s[jn], a0, a1, a2, a3, b0, b1);
+        mma_bf16(s[jn + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    // ---- masks + online softmax ----
+    const int k0 = kt * BC;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = k0 + j * 8 + 2 * t4 + (e & 1);
+        const int pos = (e < 2) ? posA : posB;
+        bool ok = key < L;
+        if (causal) ok = ok && key <= pos;
+        if (window > 0) ok = ok && key > pos - window;
+        const float v = ok ? s[j][e] * scale_log2 : -INFINITY;
+        s[j][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffff, mx[h], 1));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffff, mx[h], 2));
+    }
+    float alpha[2], mnew[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mnew[h] = fmaxf(m_run[h], mx[h]);
+      const float mref = mnew[h] == -INFINITY ? 0.f : mnew[h];
+      alpha[h] = exp2f(m_run[h] - mref);
+      m_run[h] = mnew[h];
+    }
+    float rsum[2] = {0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int h = e >> 1;
+        const float mref = mnew[h] == -INFINITY ? 0.f : mnew[h];
+        const float p = exp2f(s[j][e] - mref);
+        s[j][e] = p;
+        rsum[h] += p;
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      rsum[h] += __shfl_xor_sync(0xffffffff, rsum[h], 1);
+      rsum[h] += __shfl_xor_sync(0xffffffff, rsum[h], 2);
+      l_run[h] = l_run[h] * alpha[h] + rsum[h];
+    }
+#pragma unroll
+    for (int j = 0; j < OT; ++j) {
+      o[j][0] *= alpha[0]; o[j][1] *= alpha[0];
+      o[j][2] *= alpha[1]; o[j][3] *= alpha[1];
+    }
+    // ---- O += P V ----
+#pragma unroll
+    for (int kk = 0; kk < BC / 16; ++kk) {
+      const uint32_t a0 = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+      const uint32_t a1 = pack_bf16(s[2 * kk][2], s[2 * kk][3]);
+      const uint32_t a2 = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      const uint32_t a3 = pack_bf16(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+#pragma unroll
+      for (int jn = 0; jn < OT; jn += 2) {
+        uint32_t b0, b1, b2, b3;
+        const int r = kk * 16 + (lane % 8) + ((lane / 8) % 2) * 8;
+        const int c = jn + lane / 16;
+        ldsm_x4_t(sVa + swz(r, c, CH), b0, b1, b2, b3);
+        mma_bf16(o[jn], a0, a1, a2, a3, b0, b1);
+        mma_bf16(o[jn + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+  }
+
+  // ---- epilogue ----
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int rr = (h == 0) ? rA : rB;
+    if (rr >= R || rr - row0 >= BR) continue;
+    const int i = rr / G, g = rr % G;
+    const int tok = s0 + i, head = hk * G + g;
+    const float inv = l_run[h] > 0.f ? 1.f / l_run[h] : 0.f;
+    if (num_splits == 1) {
+      __nv_bfloat16* dst = out + ((size_t)tok * Hq + head) * D;
+#pragma unroll
+      for (int j = 0; j < OT; ++j) {
+        const int col = j * 8 + 2 * t4;
+        *reinterpret_cast<__nv_bfloat162*>(dst + col) =
+            __floats2bfloat162_rn(o[j][2 * h] * inv, o[j][2 * h + 1] * inv);
+      }
+    } else {
+      float* dst = part_o + (((size_t)split * T + tok) * Hq + head) * D;
+#pragma unroll
+      for (int j = 0; j < OT; ++j) {
+        const int col = j * 8 + 2 * t4;
+        *reinterpret_cast<float2*>(dst + col) = make_float2(o[j][2 * h] * inv, o[j][2 * h + 1] * inv);
+      }
+      if (t4 == 0) {
+        float* ml = part_ml + (((size_t)split * T + tok) * Hq + head) * 2;
+        ml[0] = m_run[h];
+        ml[1] = l_run[h];
+      }
+    }
+  }
+}
+
+// merge split partials: one warp per (token, head)
+template <int D>
+__global__ void attn_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
+                                  int num_splits, int T, int Hq, __nv_bfloat16* __restrict__ out) {
+  const int gw = blockIdx.x * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (gw >= T * Hq) return;
+  float mmax = -INFINITY;
+  for (int s = 0; s < num_splits; ++s) {
+    const float m = part_ml[((size_t)s * T * Hq + gw) * 2];
+    const float l = part_ml[((size_t)s * T * Hq + gw) * 2 + 1];
+    if (l > 0.f) mmax = fmaxf(mmax, m);
+  }
+  constexpr int PER = D / 32;
+  float acc[PER];
+#pragma unroll
+  for (int p = 0; p < PER; ++p) acc[p] = 0.f;
+  float wsum = 0.f;
+  for (int s = 0; s < num_splits; ++s) {
+    const float m = part_ml[((size_t)s * T * Hq + gw) * 2];
+    const float l = part_ml[((size_t)s * T * Hq + gw) * 2 + 1];
+    if (!(l > 0.f)) continue;
+    const float w = l * exp2f(m - mmax);
+    wsum += w;
+    const float* src = part_o + ((size_t)s * T * Hq + gw) * D;
+#pragma unroll
+    for (int p = 0; p < PER; ++p) acc[p] += w * src[lane * PER + p];
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+#pragma unroll
+  for (int p = 0; p < PER; ++p) out[(size_t)gw * D + lane * PER + p] = __float2bfloat16_rn(acc[p] * inv);
+}
+
+}  // namespace attn
+
+void qkv_prologue(torch::Tensor qkv, int64_t q_head_stride, int64_t k_off, int64_t v_off,
+                  torch::Tensor positions, torch::Tensor qn_w, torch::Tensor kn_w,
+                  torch::Tensor cos_sin, int64_t rot, int64_t Hq, int64_t Hkv, double eps,
+                  torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache,
+                  torch::Tensor slot_mapping) {
+  const int T = qkv.size(0);
+  if (T == 0) return;
+  const int D = q_out.size(2);
+  const int block_size = k_cache.size(2);
+  const bool fp8 = k_cache.scalar_type() == at::kFloat8_e4m3fn;
+  TORCH_CHECK(positions.scalar_type() == at::kInt && slot_mapping.scalar_type() == at::kLong, "index dtypes");
+  TORCH_CHECK(((rot / 2) % (D / 32)) == 0, "rotary dim / lanes");
+  const at::cuda::CUDAGuard guard(qkv.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int warps = T * (Hq + Hkv);
+  dim3 grid((warps + 7) / 8);
+  auto run = [&](auto dtag) {
+    constexpr int Dc = decltype(dtag)::value;
+    attn::qkv_prologue_kernel<Dc><<<grid, 256, 0, stream>>>(
+        (const __nv_bfloat16*)qkv.data_ptr(), qkv.stride(0), q_head_stride, k_off, v_off,
+        positions.data_ptr<int>(), (const __nv_bfloat16*)qn_w.data_ptr(),
+        (const __nv_bfloat16*)kn_w.data_ptr(), cos_sin.data_ptr<float>(), rot, T, Hq, Hkv,
+        (float)eps, (__nv_bfloat16*)q_out.data_ptr(), (uint8_t*)k_cache.data_ptr(),
+        (uint8_t*)v_cache.data_ptr(), fp8 ? 1 : 0, slot_mapping.data_ptr<int64_t>(), block_size);
+  };
+  if (D == 256) run(std::integral_constant<int, 256>{});
+  else if (D == 128) run(std::integral_constant<int, 128>{});
+  else if (D == 64) run(std::integral_constant<int, 64>{});
+  else TORCH_CHECK(false, "qkv_prologue: head_dim 64/128/256");
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// q [T, Hq, D] bf16; caches [blocks, Hkv, block_size(=64k), D]; tile_seq/tile_row0 [num_tiles];
+// part_o [splits, T, Hq, D] fp32 and part_ml [splits, T, Hq, 2] (used when num_splits > 1)
+void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                     torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor qsl,
+                     torch::Tensor tile_seq, torch::Tensor tile_row0, double scale, bool causal,
+                     int64_t window, int64_t num_splits, torch::Tensor part_o,
+                     torch::Tensor part_ml, torch::Tensor out) {
+  const int T = q.size(0), Hq = q.size(1), D = q.size(2);
+  const int Hkv = k_cache.size(1), block_size = k_cache.size(2);
+  const int num_tiles = tile_seq.size(0);
+  if (T == 0 || num_tiles == 0) return;
+  TORCH_CHECK(block_size % attn::BC == 0, "KV page size must be a multiple of 64");
+  TORCH_CHECK(num_splits >= 1, "num_splits");
+  const bool fp8 = k_cache.scalar_type() == at::kFloat8_e4m3fn;
+  const at::cuda::CUDAGuard guard(q.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const float scale_log2 = (float)(scale * 1.4426950408889634);
+  dim3 grid(num_tiles, Hkv, num_splits);
+  auto run = [&](auto dtag, auto ftag) {
+    constexpr int Dc = decltype(dtag)::value;
+    constexpr bool F8 = decltype(ftag)::value;
+    const int smem = (attn::BR + 2 * attn::BC) * Dc * 2;
+    auto kern = attn::paged_attn_kernel<Dc, F8>;
+    static bool set = false;
+    if (!set) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      set = true;
+    }
+    kern<<<grid, 128, smem, stream>>>(
+        (const __nv_bfloat16*)q.data_ptr(), (const uint8_t*)k_cache.data_ptr(),
+        (const uint8_t*)v_cache.data_ptr(), block_tables.data_ptr<int>(), block_tables.stride(0),
+        seq_lens.data_ptr<int>(), qsl.data_ptr<int>(), tile_seq.data_ptr<int>(),
+        tile_row0.data_ptr<int>(), Hq, Hkv, block_size, scale_log2, causal ? 1 : 0, (int)window,
+        (int)num_splits, (__nv_bfloat16*)out.data_ptr(),
+        num_splits > 1 ? part_o.data_ptr<float>() : nullptr,
+        num_splits > 1 ? part_ml.data_ptr<float>() : nullptr, T);
+  };
+  if (D == 256) {
+    if (fp8) run(std::integral_constant<int, 256>{}, std::true_type{});
+    else run(std::integral_constant<int, 256>{}, std::false_type{});
+  } else if (D == 128) {
+    if (fp8) run(std::integral_constant<int, 128>{}, std::true_type{});
+    else run(std::integral_constant<int, 128>{}, std::false_type{});
+  } else if (D == 64) {
+    if (fp8) run(std::integral_constant<int, 64>{}, std::true_type{});
+    else run(std::integral_constant<int, 64>{}, std::false_type{});
+  } else {
+    TORCH_CHECK(false, "paged_attention: head_dim 64/128/256");
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if (num_splits > 1) {
+    dim3 g2((T * Hq + 7) / 8);
+    auto merge = [&](auto dtag) {
+      constexpr int Dc = decltype(dtag)::value;
+      attn::attn_merge_kernel<Dc><<<g2, 256, 0, stream>>>(part_o.data_ptr<float>(),
+                                                          part_ml.data_ptr<float>(), num_splits, T,
+                                                          Hq, (__nv_bfloat16*)out.data_ptr());
+    };
+    if (D == 256) merge(std::integral_constant<int, 256>{});
+    else if (D == 128) merge(std::integral_constant<int, 128>{});
+    else merge(std::integral_constant<int, 64>{});
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+  }
+}
+
+}  // namespace rad

@@ -1,0 +1,57 @@
+// Python bindings of the sm_100a kernel library.
+#include <torch/extension.h>
+
+namespace rad {
+void mxfp4_gemm(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
+                torch::Tensor out, int64_t splits_override, torch::Tensor status);
+void add_rms_quant(torch::Tensor x, torch::Tensor residual, torch::Tensor weight,
+                   torch::Tensor res_out, torch::Tensor q, torch::Tensor scale, torch::Tensor nout,
+                   double eps);
+void silu_mul_quant(torch::Tensor gate_up, torch::Tensor q, torch::Tensor scale);
+void gdn_norm_quant(torch::Tensor o, torch::Tensor z, torch::Tensor weight, int64_t head_dim,
+                    double eps, torch::Tensor q, torch::Tensor scale, torch::Tensor nout);
+void gate_mul_quant(torch::Tensor a, torch::Tensor gate, int64_t head_dim, int64_t gate_head_stride,
+                    torch::Tensor q, torch::Tensor scale, torch::Tensor nout);
+void quant_fp8_rows(torch::Tensor x, torch::Tensor q, torch::Tensor scale);
+void gdn_conv(torch::Tensor x, torch::Tensor w, torch::Tensor conv_state, torch::Tensor qsl,
+              torch::Tensor slots, torch::Tensor has_init, torch::Tensor tok_seq, int64_t qk_dim,
+              int64_t head_dim, torch::Tensor y, double eps);
+void gdn_conv_state_update(torch::Tensor x, torch::Tensor conv_state, torch::Tensor qsl,
+                           torch::Tensor slots, torch::Tensor has_init, torch::Tensor commit_len);
+void gdn_recurrent(torch::Tensor y, torch::Tensor ba, torch::Tensor A_log, torch::Tensor dt_bias,
+                   torch::Tensor state, torch::Tensor qsl, torch::Tensor slots,
+                   torch::Tensor has_init, torch::Tensor commit_len, int64_t Hk, double scale,
+                   torch::Tensor out, bool write_out);
+void qkv_prologue(torch::Tensor qkv, int64_t q_head_stride, int64_t k_off, int64_t v_off,
+                  torch::Tensor positions, torch::Tensor qn_w, torch::Tensor kn_w,
+                  torch::Tensor cos_sin, int64_t rot, int64_t Hq, int64_t Hkv, double eps,
+                  torch::Tensor q_out, torch::Tensor k_cache, torch::Tensor v_cache,
+                  torch::Tensor slot_mapping);
+void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                     torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor qsl,
+                     torch::Tensor tile_seq, torch::Tensor tile_row0, double scale, bool causal,
+                     int64_t window, int64_t num_splits, torch::Tensor part_o,
+                     torch::Tensor part_ml, torch::Tensor out);
+void argmax_rows(torch::Tensor x, torch::Tensor out_ids, torch::Tensor out_vals);
+void sample_from_topk(torch::Tensor vals, torch::Tensor ids, torch::Tensor temperature,
+                      torch::Tensor top_k, torch::Tensor top_p, torch::Tensor min_p,
+                      torch::Tensor seeds, int64_t step, torch::Tensor out,
+                      torch::Tensor out_logprob, torch::Tensor probs_out);
+}  // namespace rad
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "sm_100a kernels of the radiance B200 serving engine";
+  m.def("mxfp4_gemm", &rad::mxfp4_gemm, "MXFP4 W4A8 block-scaled tcgen05 GEMM");
+  m.def("add_rms_quant", &rad::add_rms_quant, "fused residual add + Gemma RMSNorm (+ e4m3 quant)");
+  m.def("silu_mul_quant", &rad::silu_mul_quant, "SiLU(gate)*up + e4m3 quant");
+  m.def("gdn_norm_quant", &rad::gdn_norm_quant, "GDN gated RMSNorm (+ e4m3 quant)");
+  m.def("gate_mul_quant", &rad::gate_mul_quant, "attention sigmoid gate (+ e4m3 quant)");
+  m.def("quant_fp8_rows", &rad::quant_fp8_rows, "per-row e4m3 quant");
+  m.def("gdn_conv", &rad::gdn_conv, "GDN varlen causal conv1d + SiLU + q/k L2 norm");
+  m.def("gdn_conv_state_update", &rad::gdn_conv_state_update, "GDN conv state write-back");
+  m.def("gdn_recurrent", &rad::gdn_recurrent, "GDN varlen recurrent delta rule");
+  m.def("qkv_prologue", &rad::qkv_prologue, "QK RMSNorm + RoPE + paged KV write");
+  m.def("paged_attention", &rad::paged_attention, "varlen paged attention (split-KV)");
+  m.def("argmax_rows", &rad::argmax_rows, "greedy argmax per row");
+  m.def("sample_from_topk", &rad::sample_from_topk, "temperature/top-k/top-p/min-p sampling");
+}

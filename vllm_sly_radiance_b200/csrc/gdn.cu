@@ -1,0 +1,302 @@
+// Gated delta net (GDN) linear-attention kernels.
+//
+// Reference behaviour: libr4d gdn_conv_prep / gdn_conv_update (radiance_gdn.py:444,466), the
+// recurrent update gdn_recurrent_update_* and the fused decode kernel
+// (sly/gdn/radiance_gdn_decode.hip:140), with the fp64 oracle sly/gdn/chunk_scan_ref.py:48-110:
+//   S <- e^g S;  S <- S + beta (v - S k) k^T;  o = scale * S q      (S is [dv, dk] per v-head)
+//   g = -exp(A_log) * softplus(a + dt_bias),  beta = sigmoid(b)
+//
+// Kernels here:
+//  * gdn_conv       : varlen depthwise causal conv (width W) over [q|k|v] channels + SiLU, with the
+//                     per-sequence conv state as left context, q/k L2-normalised per head in the
+//                     same pass.  Serves prefill chunks and decode tokens alike.
+//  * gdn_conv_state : writes each sequence's new conv state (separate launch: the conv kernel
+//                     still reads the old state for the first W-1 tokens of every sequence).
+//  * gdn_recurrent  : varlen token-serial delta rule with the state held in registers, one CTA per
+//                     (sequence, v-head, 32-row slice of dv).  Used for decode / verify rows and,
+//                     until the chunked scan lands, for prefill rows as well.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace rad {
+namespace gdn {
+
+// ------------------------------------------------------------------------------------------------
+// conv: grid (T, ceil(num_chunks / 8)), block 256 (8 warps); warp handles one D-channel chunk
+// (D = head dim, q/k/v heads all D wide) of one token.
+// ------------------------------------------------------------------------------------------------
+template <int D, int W>
+__global__ void __launch_bounds__(256) conv_kernel(
+    const __nv_bfloat16* __restrict__ x, int ldx, const __nv_bfloat16* __restrict__ w,
+    const __nv_bfloat16* __restrict__ conv_state, const int* __restrict__ qsl,
+    const int* __restrict__ slots, const int* __restrict__ has_init, const int* __restrict__ tok_seq,
+    int C, int qk_dim, __nv_bfloat16* __restrict__ y, int ldy, float eps) {
+  constexpr int PER = D / 32;           // channels per lane
+  const int t = blockIdx.x;
+  const int chunk = blockIdx.y * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (chunk * D >= C) return;
+  const int b = tok_seq[t];
+  const int s0 = qsl[b];
+  const int i = t - s0;                 // position within this step's tokens
+  const int slot = slots[b];
+  const bool init = has_init[b] != 0;
+  float acc[PER];
+#pragma unroll
+  for (int p = 0; p < PER; ++p) acc[p] = 0.f;
+#pragma unroll
+  for (int j = 0; j < W; ++j) {
+    // input index i + j - (W-1) relative to the first token of the step
+    const int src = i + j - (W - 1);
+#pragma unroll
+    for (int p = 0; p < PER; ++p) {
+      const int c = chunk * D + lane * PER + p;
+      float xv;
+      if (src >= 0) {
+        xv = __bfloat162float(x[(size_t)(s0 + src) * ldx + c]);
+      } else {
+        // state holds the previous W-1 inputs, oldest first: state[W-1+src]
+        xv = init ? __bfloat162float(conv_state[((size_t)slot * C + c) * (W - 1) + (W - 1 + src)]) : 0.f;
+      }
+      acc[p] += xv * __bfloat162float(w[(size_t)c * W + j]);
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int p = 0; p < PER; ++p) {
+    acc[p] = acc[p] / (1.f + __expf(-acc[p]));
+    ss += acc[p] * acc[p];
+  }
+  if (chunk * D < qk_dim) {
+    ss = warp_sum(ss);
+    const float r = rsqrtf(ss + eps);
+#pragma unroll
+    for (int p = 0; p < PER; ++p) acc[p] *= r;
+  }
+#pragma unroll
+  for (int p = 0; p < PER; ++p)
+    y[(size_t)t * ldy + chunk * D + lane * PER + p] = __float2bfloat16_rn(acc[p]);
+}
+
+// new state for each sequence = the last W-1 inputs of concat(old_state, x_seq[:n_commit])
+template <int W>
+__global__ void conv_state_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
+                                  __nv_bfloat16* __restrict__ conv_state,
+                                  const int* __restrict__ qsl, const int* __restrict__ slots,
+                                  const int* __restrict__ has_init,
+                                  const int* __restrict__ commit_len, int C) {
+  const int b = blockIdx.y;
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const int s0 = qsl[b];
+  const int L = commit_len ? commit_len[b] : (qsl[b + 1] - s0);
+  const int slot = slots[b];
+  const bool init = has_init[b] != 0;
+  __nv_bfloat16* st = conv_state + ((size_t)slot * C + c) * (W - 1);
+  float old[W - 1];
+#pragma unroll
+  for (int j = 0; j < W - 1; ++j) old[j] = init ? __bfloat162float(st[j]) : 0.f;
+  float nw[W - 1];
+#pragma unroll
+  for (int j = 0; j < W - 1; ++j) {
+    // element j of the new state is input index L - (W-1) + j (negative -> old state)
+    const int src = L - (W - 1) + j;
+    nw[j] = src >= 0 ? __bfloat162float(x[(size_t)(s0 + src) * ldx + c]) : old[W - 1 + src];
+  }
+#pragma unroll
+  for (int j = 0; j < W - 1; ++j) st[j] = __float2bfloat16_rn(nw[j]);
+}
+
+// ------------------------------------------------------------------------------------------------
+// recurrent delta rule.  grid (B, Hv, DV / 32), block 128: warp w owns rows [8w, 8w+8) of the
+// 32-row slice, lane owns dk columns [lane*DK/32, ...).
+// ------------------------------------------------------------------------------------------------
+template <int DK, typename ST>
+__global__ void __launch_bounds__(128) recurrent_kernel(
+    const __nv_bfloat16* __restrict__ y, int ldy,        // conv output [T, C]: q | k | v
+    const __nv_bfloat16* __restrict__ ba, int ldba,      // [T, ...]: b at col 0.., a at col Hv..
+    const float* __restrict__ A_log, const float* __restrict__ dt_bias,
+    ST* __restrict__ state,                              // [S, Hv, DV, DK]
+    const int* __restrict__ qsl, const int* __restrict__ slots, const int* __restrict__ has_init,
+    const int* __restrict__ commit_len,                  // optional: rows to apply to the stored state
+    int Hk, int Hv, int DV, float scale, __nv_bfloat16* __restrict__ out, int ldo,
+    int write_out) {
+  constexpr int PL = DK / 32;          // dk columns per lane
+  constexpr int RW = 8;                // rows per warp
+  const int b = blockIdx.x;
+  const int h = blockIdx.y;
+  const int r0 = blockIdx.z * 32 + (threadIdx.x / 32) * RW;
+  const int lane = threadIdx.x % 32;
+  const int s0 = qsl[b];
+  const int L = qsl[b + 1] - s0;
+  const int Lc = commit_len ? commit_len[b] : L;
+  const int slot = slots[b];
+  const int hk = h / (Hv / Hk);
+  const int key_dim = Hk * DK;
+  const float negA = -__expf(A_log[h]);
+  const float dtb = dt_bias[h];
+
+  float S[RW][PL];
+  ST* sp = state + (((size_t)slot * Hv + h) * DV + r0) * DK + lane * PL;
+  if (has_init[b]) {
+#pragma unroll
+    for (int r = 0; r < RW; ++r)
+#pragma unroll
+      for (int p = 0; p < PL; ++p) S[r][p] = to_f(sp[(size_t)r * DK + p]);
+  } else {
+#pragma unroll
+    for (int r = 0; r < RW; ++r)
+#pragma unroll
+      for (int p = 0; p < PL; ++p) S[r][p] = 0.f;
+  }
+
+  for (int i = 0; i < L; ++i) {
+    const size_t t = s0 + i;
+    const __nv_bfloat16* yt = y + t * ldy;
+    float q[PL], k[PL], v[RW];
+#pragma unroll
+    for (int p = 0; p < PL; ++p) {
+      q[p] = __bfloat162float(yt[hk * DK + lane * PL + p]);
+      k[p] = __bfloat162float(yt[key_dim + hk * DK + lane * PL + p]);
+    }
+#pragma unroll
+    for (int r = 0; r < RW; ++r) v[r] = __bfloat162float(yt[2 * key_dim + h * DV + r0 + r]);
+    const float bb = __bfloat162float(ba[t * ldba + h]);
+    const float aa = __bfloat162float(ba[t * ldba + Hv + h]);
+    const float xsp = aa + dtb;
+    const float sp_ = xsp > 20.f ? xsp : log1pf(__expf(xsp));
+    const float decay = __expf(negA * sp_);
+    const float beta = 1.f / (1.f + __expf(-bb));
+    float kv[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+      float acc = 0.f;
+#pragma unroll
+      for (int p = 0; p < PL; ++p) {
+        S[r][p] *= decay;
+        acc += S[r][p] * k[p];
+      }
+      kv[r] = acc;
+    }
+#pragma unroll
+    for (int r = 0; r < RW; ++r) kv[r] = warp_sum(kv[r]);
+    float o[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+      const float d = beta * (v[r] - kv[r]);
+      float acc = 0.f;
+#pragma unroll
+      for (int p = 0; p < PL; ++p) {
+        S[r][p] += d * k[p];
+        acc += S[r][p] * q[p];
+      }
+      o[r] = acc;
+    }
+#pragma unroll
+    for (int r = 0; r < RW; ++r) o[r] = warp_sum(o[r]);
+    if (write_out && lane < RW) {
+      float ov = 0.f;
+#pragma unroll
+      for (int r = 0; r < RW; ++r)
+        if (r == lane) ov = o[r];
+      out[t * ldo + h * DV + r0 + lane] = __float2bfloat16_rn(ov * scale);
+    }
+    if (i + 1 == Lc) {
+#pragma unroll
+      for (int r = 0; r < RW; ++r)
+#pragma unroll
+        for (int p = 0; p < PL; ++p) sp[(size_t)r * DK + p] = from_f<ST>(S[r][p]);
+    }
+  }
+}
+
+}  // namespace gdn
+
+static inline const int* iptr(const torch::Tensor& t) {
+  return t.defined() && t.numel() ? t.data_ptr<int>() : nullptr;
+}
+
+// x: [T, >=C] bf16 (qkv part of in_proj output), w [C, W], conv_state [S, C, W-1] bf16,
+// qsl [B+1], slots [B], has_init [B], tok_seq [T] (sequence index of each token), y [T, C] out
+void gdn_conv(torch::Tensor x, torch::Tensor w, torch::Tensor conv_state, torch::Tensor qsl,
+              torch::Tensor slots, torch::Tensor has_init, torch::Tensor tok_seq, int64_t qk_dim,
+              int64_t head_dim, torch::Tensor y, double eps) {
+  const int T = x.size(0);
+  const int C = w.size(0), W = w.size(1);
+  if (T == 0) return;
+  TORCH_CHECK(W == 4, "gdn_conv: conv width 4 supported");
+  TORCH_CHECK(C % head_dim == 0 && qk_dim % head_dim == 0, "gdn_conv: dims");
+  const at::cuda::CUDAGuard guard(x.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int chunks = C / head_dim;
+  dim3 grid(T, (chunks + 7) / 8);
+  auto run = [&](auto dtag) {
+    constexpr int D = decltype(dtag)::value;
+    gdn::conv_kernel<D, 4><<<grid, 256, 0, stream>>>(
+        (const __nv_bfloat16*)x.data_ptr(), x.stride(0), (const __nv_bfloat16*)w.data_ptr(),
+        (const __nv_bfloat16*)conv_state.data_ptr(), qsl.data_ptr<int>(), slots.data_ptr<int>(),
+        has_init.data_ptr<int>(), tok_seq.data_ptr<int>(), C, qk_dim,
+        (__nv_bfloat16*)y.data_ptr(), y.stride(0), (float)eps);
+  };
+  if (head_dim == 128) run(std::integral_constant<int, 128>{});
+  else if (head_dim == 64) run(std::integral_constant<int, 64>{});
+  else TORCH_CHECK(false, "gdn_conv: head_dim 64 or 128");
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gdn_conv_state_update(torch::Tensor x, torch::Tensor conv_state, torch::Tensor qsl,
+                           torch::Tensor slots, torch::Tensor has_init, torch::Tensor commit_len) {
+  const int B = slots.size(0);
+  const int C = conv_state.size(1), W = conv_state.size(2) + 1;
+  if (B == 0) return;
+  TORCH_CHECK(W == 4, "gdn_conv_state_update: width 4");
+  const at::cuda::CUDAGuard guard(x.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  dim3 grid((C + 255) / 256, B);
+  gdn::conv_state_kernel<4><<<grid, 256, 0, stream>>>(
+      (const __nv_bfloat16*)x.data_ptr(), x.stride(0), (__nv_bfloat16*)conv_state.data_ptr(),
+      qsl.data_ptr<int>(), slots.data_ptr<int>(), has_init.data_ptr<int>(), iptr(commit_len), C);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gdn_recurrent(torch::Tensor y, torch::Tensor ba, torch::Tensor A_log, torch::Tensor dt_bias,
+                   torch::Tensor state, torch::Tensor qsl, torch::Tensor slots,
+                   torch::Tensor has_init, torch::Tensor commit_len, int64_t Hk, double scale,
+                   torch::Tensor out, bool write_out) {
+  const int B = slots.size(0);
+  if (B == 0) return;
+  const int Hv = state.size(1), DV = state.size(2), DK = state.size(3);
+  TORCH_CHECK(DV % 32 == 0, "gdn_recurrent: dv % 32");
+  TORCH_CHECK(A_log.scalar_type() == at::kFloat && dt_bias.scalar_type() == at::kFloat, "fp32 gates");
+  const at::cuda::CUDAGuard guard(y.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  dim3 grid(B, Hv, DV / 32);
+  auto run = [&](auto dtag, auto stag) {
+    constexpr int DKc = decltype(dtag)::value;
+    using ST = typename decltype(stag)::type;
+    gdn::recurrent_kernel<DKc, ST><<<grid, 128, 0, stream>>>(
+        (const __nv_bfloat16*)y.data_ptr(), y.stride(0), (const __nv_bfloat16*)ba.data_ptr(),
+        ba.stride(0), A_log.data_ptr<float>(), dt_bias.data_ptr<float>(), (ST*)state.data_ptr(),
+        qsl.data_ptr<int>(), slots.data_ptr<int>(), has_init.data_ptr<int>(), iptr(commit_len),
+        Hk, Hv, DV, (float)scale, out.defined() && out.numel() ? (__nv_bfloat16*)out.data_ptr() : nullptr,
+        out.defined() && out.numel() ? out.stride(0) : 0, write_out ? 1 : 0);
+  };
+  struct F32 { using type = float; };
+  struct BF16 { using type = __nv_bfloat16; };
+  const bool f32 = state.scalar_type() == at::kFloat;
+  if (DK == 128) {
+    if (f32) run(std::integral_constant<int, 128>{}, F32{});
+    else run(std::integral_constant<int, 128>{}, BF16{});
+  } else if (DK == 64) {
+    if (f32) run(std::integral_constant<int, 64>{}, F32{});
+    else run(std::integral_constant<int, 64>{}, BF16{});
+  } else {
+    TORCH_CHECK(false, "gdn_recurrent: dk 64 or 128");
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace rad

@@ -1,0 +1,380 @@
+// MXFP4 W4A8 linear on 5th-generation tensor cores (sm_100a).
+//
+//   C[m, n] = a_scale[m] * sum_k e4m3(A[m, k]) * e2m1(W[n, k]) * 2^(ws[n, k/32] - 127)
+//
+// Reference behaviour: the W4A8 GEMM family of sly/mxfp4/radiance_mxfp4_fp8.hip (:132 per-block,
+// :327 folded, :666 A-tiled prefill, :983 split-K decode).  The B200 design is different:
+//
+//  * One tcgen05.mma.kind::mxf8f6f4.block_scale instruction does the e2m1 x e4m3 product with the
+//    per-32 UE8M0 weight scales applied inside the tensor core (no folded/PSW weight repack).
+//  * Weights are the MMA "A" operand (M_mma = 128 weight rows) and activations the "B" operand
+//    (N_mma = BN tokens, 16..256).  The same kernel serves decode (BN = 16, tokens padded by TMA
+//    zero-fill) and prefill (BN = 256): the swap-AB orientation the reference emulates with its
+//    separate decode kernel.
+//  * Weight tiles arrive by TMA with the 16U4_ALIGN16B map type, which expands packed nibbles to
+//    the padded form the f8f6f4 MMA reads; scale factors arrive by one 512-byte bulk copy per
+//    128x128 tile and go to tensor memory with tcgen05.cp.  Activation scale factors are a
+//    constant 1.0 in tensor memory: activations carry a per-token fp32 scale applied in the
+//    epilogue (the reference's per-token e4m3 contract).
+//  * Split-K for small M runs as a thread-block cluster along K: each CTA accumulates its K range
+//    in its own TMEM, the partial tiles are reduced through distributed shared memory, and the
+//    cluster writes the output once.  This replaces the reference's global fp32 partials and
+//    self-resetting counter (radiance_mxfp4_fp8.hip:1251-1343) with no global workspace.
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM allocator + MMA issuer,
+// warps 2..5 = epilogue (their warp-in-quad index covers the four TMEM lane quarters).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "tma_host.h"
+
+namespace rad {
+namespace mxfp4 {
+
+constexpr int BM = 128;          // weight rows per tile (MMA M)
+constexpr int BK = 128;          // K elements per pipeline stage (4 MMAs of K = 32)
+constexpr int W_TILE_BYTES = BM * BK;          // padded e2m1: 1 byte per element in smem
+constexpr int W_TILE_TX = BM * BK / 2;         // TMA transaction bytes (packed source)
+constexpr int SF_TILE_BYTES = 512;
+constexpr int kThreads = 192;
+constexpr int kSmemBudget = 227 * 1024;
+
+template <int BN>
+struct Cfg {
+  static constexpr int A_TILE_BYTES = BN * BK;
+  // stages start on 1024-byte boundaries (128B-swizzled tiles need it)
+  static constexpr int STAGE_BYTES = (W_TILE_BYTES + A_TILE_BYTES + SF_TILE_BYTES + 1023) / 1024 * 1024;
+  static constexpr int STAGES_RAW = (kSmemBudget - 2048) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  // TMEM columns: accumulator BN + SFA 4 + SFB 8 -> next power of two
+  static constexpr int TMEM_NEED = BN + 12;
+  static constexpr int TMEM_COLS = TMEM_NEED <= 32 ? 32 : TMEM_NEED <= 64 ? 64 : TMEM_NEED <= 128 ? 128
+                                   : TMEM_NEED <= 256 ? 256 : 512;
+  static constexpr int SFA_COL = BN;
+  static constexpr int SFB_COL = BN + 4;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 1024 /*barriers*/;
+  static_assert(STAGES >= 2, "not enough shared memory for two stages");
+  static_assert(BN * BM * 4 <= STAGES * STAGE_BYTES, "split-K partial tile must fit in stage smem");
+};
+
+__host__ __device__ constexpr uint32_t make_idesc(int bn, int sf_id) {
+  return (0u << 4)                       // b_sf_id set below
+         | (5u << 7)                     // A format: E2M1
+         | (0u << 10)                    // B format: E4M3
+         | ((uint32_t)(bn >> 3) << 17)   // N >> 3
+         | (1u << 23)                    // scale format UE8M0
+         | ((uint32_t)(BM >> 4) << 24)   // M >> 4
+         | ((uint32_t)sf_id << 29)       // A scale-factor id (byte within the TMEM word)
+         | ((uint32_t)sf_id << 4);       // B scale-factor id
+}
+
+template <int BN>
+__global__ void __launch_bounds__(kThreads, 1)
+    mxfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
+                      const __grid_constant__ CUtensorMap tmap_a, const uint8_t* __restrict__ sfw,
+                      const float* __restrict__ a_scale, __nv_bfloat16* __restrict__ out,
+                      int ldo, int M, int N, int K, int k_tiles_per_split, int* __restrict__ status) {
+  using C = Cfg<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stage_base = smem;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + C::STAGES;
+  uint64_t* acc_bar = empty_bar + C::STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_bar + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int n_tile = blockIdx.x;
+  const int m_tile = blockIdx.y;
+  const int split = blockIdx.z;
+  const int num_splits = gridDim.z;
+  const int n0 = n_tile * BM;
+  const int m0 = m_tile * BN;
+  const int k_tiles_total = K / BK;
+  const int kt0 = split * k_tiles_per_split;
+  const int kt1 = min(k_tiles_total, kt0 + k_tiles_per_split);
+  const int nk = kt1 - kt0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(acc_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_w);
+    tma_prefetch_desc(&tmap_a);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  // TMEM address handoff: fence / barrier / fence
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tmem_acc = tmem_base;
+  const uint32_t tmem_sfa = tmem_base + C::SFA_COL;
+  const uint32_t tmem_sfb = tmem_base + C::SFB_COL;
+
+  // activation scale factors = 1.0 (UE8M0 127) for every lane / byte
+  if (warp >= 2) {
+    const int q = warp & 3;
+    uint32_t ones[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ones[i] = 0x7F7F7F7Fu;
+    tmem_st_32x32b_x8(tmem_sfb + ((uint32_t)(q * 32) << 16), ones);
+    tmem_st_wait();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (elect_one()) {
+      const uint64_t w_policy = l2_policy_evict_first();   // weights stream once
+      const uint8_t* sf_row = sfw + (size_t)n_tile * (size_t)k_tiles_total * SF_TILE_BYTES;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % C::STAGES;
+        const uint32_t ph = (i / C::STAGES) & 1;
+        if (!mbar_wait(&empty_bar[s], ph ^ 1, status)) { *abort_flag = 1; break; }
+        uint8_t* st = stage_base + s * C::STAGE_BYTES;
+        const int kt = kt0 + i;
+        mbar_arrive_expect_tx(&full_bar[s], W_TILE_TX + C::A_TILE_BYTES + SF_TILE_BYTES);
+        tma_load_2d_hint(st, &tmap_w, &full_bar[s], kt * BK, n0, w_policy);
+        tma_load_2d(st + W_TILE_BYTES, &tmap_a, &full_bar[s], kt * BK, m0);
+        bulk_load(st + W_TILE_BYTES + C::A_TILE_BYTES, sf_row + (size_t)kt * SF_TILE_BYTES,
+                  SF_TILE_BYTES, &full_bar[s]);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (elect_one()) {
+      bool ok = true;
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % C::STAGES;
+        const uint32_t ph = (i / C::STAGES) & 1;
+        if (!mbar_wait(&full_bar[s], ph, status)) { ok = false; *abort_flag = 1; break; }
+        tc_fence_after();
+        uint8_t* st = stage_base + s * C::STAGE_BYTES;
+        const uint32_t w_addr = smem_u32(st);
+        const uint32_t a_addr = smem_u32(st + W_TILE_BYTES);
+        const uint32_t sf_addr = smem_u32(st + W_TILE_BYTES + C::A_TILE_BYTES);
+        // weight scale factors: 32 rows x 16 B atom -> TMEM lanes (x4 quarters), 4 columns
+        tmem_cp_32x128b_warpx4(tmem_sfa, sdesc_plain(sf_addr, 0, 128));
+#pragma unroll
+        for (int kb = 0; kb < BK / 32; ++kb) {
+          const uint64_t adesc = sdesc_sw128(w_addr + kb * 32);
+          const uint64_t bdesc = sdesc_sw128(a_addr + kb * 32);
+          const uint32_t idesc = make_idesc(BN, kb);
+          mma_mxf8f6f4(tmem_acc, adesc, bdesc, idesc, tmem_sfa | ((uint32_t)kb << 30),
+                       tmem_sfb | ((uint32_t)kb << 30), (i > 0 || kb > 0) ? 1u : 0u);
+        }
+        mma_commit(&empty_bar[s]);     // frees the stage once these MMAs have read it
+      }
+      if (ok) mma_commit(acc_bar);     // accumulator complete
+      else mbar_arrive(acc_bar);
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;            // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;     // weight row within the tile
+    const int n = n0 + row;
+    if (!mbar_wait(acc_bar, 0, status)) *abort_flag = 1;
+    tc_fence_after();
+    const bool have_acc = nk > 0 && !*abort_flag;
+    if (num_splits == 1) {
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(tmem_acc + ((uint32_t)(q * 32) << 16) + c0, r);
+        tmem_ld_wait();
+        if (n < N) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int m = m0 + c0 + j;
+            if (m < M) {
+              const float v = have_acc ? __uint_as_float(r[j]) * a_scale[m] : 0.f;
+              out[(size_t)m * ldo + n] = __float2bfloat16_rn(v);
+            }
+          }
+        }
+      }
+    } else {
+      // partial tile -> own shared memory, layout [BN][128] fp32 (stage buffers are idle now)
+      float* part = reinterpret_cast<float*>(stage_base);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(tmem_acc + ((uint32_t)(q * 32) << 16) + c0, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) part[(c0 + j) * BM + row] = have_acc ? __uint_as_float(r[j]) : 0.f;
+      }
+    }
+  }
+
+  if (num_splits > 1) {
+    // every thread of every CTA in the cluster takes part in both cluster barriers
+    __syncwarp();
+    cluster_sync();
+    if (warp >= 2) {
+      const int q = warp & 3;
+      const int row = q * 32 + lane;
+      const int n = n0 + row;
+      const uint32_t my_rank = cluster_ctarank();
+      const uint32_t part_addr = smem_u32(stage_base);
+      for (int j = my_rank; j < BN; j += num_splits) {
+        const int m = m0 + j;
+        if (m >= M || n >= N) continue;
+        float acc = 0.f;
+        for (int r = 0; r < num_splits; ++r) {
+          const uint32_t a = mapa_shared(part_addr + (uint32_t)((j * BM + row) * 4), (uint32_t)r);
+          float v;
+          asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a));
+          acc += v;
+        }
+        out[(size_t)m * ldo + n] = __float2bfloat16_rn(acc * a_scale[m]);
+      }
+    }
+    __syncwarp();
+    cluster_sync();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------------------------
+struct MapKey {
+  uintptr_t ptr;
+  int64_t rows, cols, stride;
+  int box_rows;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && rows == o.rows && cols == o.cols && stride == o.stride && box_rows == o.box_rows;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    return std::hash<uintptr_t>()(k.ptr) ^ (std::hash<int64_t>()(k.rows) << 1) ^
+           (std::hash<int64_t>()(k.cols) << 7) ^ (std::hash<int>()(k.box_rows) << 13);
+  }
+};
+
+static std::mutex g_map_mu;
+static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_wmaps;
+
+static CUtensorMap weight_map(const torch::Tensor& packed, int64_t N, int64_t K) {
+  MapKey key{(uintptr_t)packed.data_ptr(), N, K, packed.stride(0), BM};
+  std::lock_guard<std::mutex> g(g_map_mu);
+  auto it = g_wmaps.find(key);
+  if (it != g_wmaps.end()) return it->second;
+  CUtensorMap m = make_tma_2d(packed.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B,
+                              /*inner elems*/ K, /*rows*/ N, /*row stride bytes*/ packed.stride(0),
+                              /*box inner*/ BK, /*box rows*/ BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  g_wmaps.emplace(key, m);
+  return m;
+}
+
+template <int BN>
+static void launch(const torch::Tensor& a, const torch::Tensor& a_scale, const torch::Tensor& wp,
+                   const torch::Tensor& sf, torch::Tensor& out, int M, int N, int K, int splits,
+                   int* status, cudaStream_t stream) {
+  using C = Cfg<BN>;
+  CUtensorMap tw = weight_map(wp, N, K);
+  CUtensorMap ta = make_tma_2d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, a.stride(0), BK,
+                               BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  const int k_tiles = K / BK;
+  const int per = (k_tiles + splits - 1) / splits;
+  dim3 grid((N + BM - 1) / BM, (M + BN - 1) / BN, splits);
+  auto kern = mxfp4_gemm_kernel<BN>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[1];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = 1;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = splits;
+  cfg.attrs = attrs;
+  cfg.numAttrs = 1;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tw, ta, (const uint8_t*)sf.data_ptr(),
+                                    (const float*)a_scale.data_ptr(),
+                                    (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), M, N, K,
+                                    per, status));
+}
+
+static int pick_splits(int tiles, int k_tiles) {
+  // fill the 148 SMs: grow the cluster along K while tiles are few and each CTA keeps >= 4 stages
+  int s = 1;
+  while (s < 8 && tiles * s * 2 <= 2 * 148 && k_tiles / (s * 2) >= 4) s *= 2;
+  return s;
+}
+
+}  // namespace mxfp4
+
+// a: fp8 e4m3 [M, K] (row stride multiple of 16 bytes), a_scale fp32 [M], wp uint8 [N, K/2],
+// sf: tiled scale factors, out: bf16 [M, N] (row stride ldo)
+void mxfp4_gemm(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
+                torch::Tensor out, int64_t splits_override, torch::Tensor status) {
+  using namespace mxfp4;
+  TORCH_CHECK(a.is_cuda() && wp.is_cuda() && out.is_cuda(), "mxfp4_gemm: CUDA tensors required");
+  TORCH_CHECK(a.scalar_type() == at::kFloat8_e4m3fn, "activations must be float8_e4m3fn");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16, "output must be bf16");
+  TORCH_CHECK(a.dim() == 2 && a.stride(1) == 1 && out.stride(1) == 1 && wp.stride(1) == 1, "row-major");
+  const int M = a.size(0), K = a.size(1), N = wp.size(0);
+  TORCH_CHECK(wp.size(1) * 2 == K, "weight K mismatch");
+  TORCH_CHECK(K % BK == 0, "K must be a multiple of 128");
+  TORCH_CHECK((a.stride(0) % 16) == 0 && (reinterpret_cast<uintptr_t>(a.data_ptr()) % 16) == 0,
+              "activation rows must be 16-byte aligned");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(wp.data_ptr()) % 32) == 0 && (wp.stride(0) % 32) == 0,
+              "weight rows must be 32-byte aligned");
+  TORCH_CHECK(out.size(0) >= M && out.size(1) >= N, "output too small");
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(a.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  int* st = status.numel() ? status.data_ptr<int>() : nullptr;
+  int bn;
+  if (M <= 16) bn = 16;
+  else if (M <= 32) bn = 32;
+  else if (M <= 64) bn = 64;
+  else if (M <= 128) bn = 128;
+  else bn = 256;
+  const int tiles = ((N + BM - 1) / BM) * ((M + bn - 1) / bn);
+  int splits = splits_override > 0 ? (int)splits_override : pick_splits(tiles, K / BK);
+  switch (bn) {
+    case 16: launch<16>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream); break;
+    case 32: launch<32>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream); break;
+    case 64: launch<64>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream); break;
+    case 128: launch<128>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream); break;
+    default: launch<256>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream); break;
+  }
+}
+
+}  // namespace rad

@@ -1,0 +1,415 @@
+"""Gated-delta-net hybrid decoder (Qwen3-Next / Qwen3.8 family).
+
+Layer i is full attention iff (i+1) % full_attn_interval == 0, else a gated delta net (GDN)
+linear-attention layer; every layer has a SwiGLU MLP (or an MoE block).  Reference model code:
+the vLLM Qwen3-Next files the reference patches (``sly/tests/fixtures/qwen3_next_v0.34.0.py.txt``,
+decoder-layer fused norm ``:113-156``) and the GDN layer (``radiance_gdn.py``).
+
+Forward over a flat varlen batch (prefill chunks and decode tokens mixed).  With MXFP4 weights
+every linear runs W4A8: the fused producers turn the residual stream into (e4m3, scale) rows:
+
+  add_rms_quant -> in_proj | qkv        (GDN | attention)
+  GDN : conv(+SiLU, q/k L2) -> delta rule -> gated norm + quant -> out_proj
+  ATTN: qk-norm + RoPE + KV write -> paged attention -> sigmoid gate + quant -> o_proj
+  add_rms_quant -> gate_up -> silu_mul_quant -> down
+
+Tensor parallelism: heads / intermediate are sharded per rank (column-parallel in_proj, qkv,
+gate_up; row-parallel out_proj, o_proj, down followed by an all-reduce), vocab-parallel lm_head.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Callable, Optional
+
+import torch
+
+from ..config import ModelConfig
+from ..ops import kernels as K
+from .layers import Linear, rope_cache
+
+
+# ---------------------------------------------------------------------------------------------
+# per-step metadata
+# ---------------------------------------------------------------------------------------------
+@dataclass
+class StepMeta:
+    """Device tensors describing one forward step (built by the model runner)."""
+    num_seqs: int
+    num_tokens: int
+    query_start_loc: torch.Tensor      # [B+1] int32
+    seq_lens: torch.Tensor             # [B] int32 (context incl. this step's tokens)
+    has_initial: torch.Tensor          # [B] int32 (sequence has cached state/KV before this step)
+    state_slots: torch.Tensor          # [B] int32 GDN state slot
+    block_tables: torch.Tensor         # [B, max_blocks] int32
+    slot_mapping: torch.Tensor         # [T] int64 KV slot of each token
+    positions: torch.Tensor            # [T] int32
+    token_seq: torch.Tensor            # [T] int32 sequence index of each token
+    tile_seq: torch.Tensor             # [tiles] int32 attention row-tile -> sequence
+    tile_row0: torch.Tensor            # [tiles] int32 first row of the tile
+    num_splits: int = 1
+    commit_len: Optional[torch.Tensor] = None   # spec-decode: tokens of each seq to commit to state
+    gdn_write_out: bool = True
+    _scratch: dict = field(default_factory=dict)
+
+    def scratch_o(self, s, T, H, D):
+        key = ("o", s, T, H, D)
+        t = self._scratch.get(key)
+        if t is None:
+            t = torch.empty(s, T, H, D, dtype=torch.float32, device=self.query_start_loc.device)
+            self._scratch[key] = t
+        return t
+
+    def scratch_ml(self, s, T, H):
+        key = ("ml", s, T, H)
+        t = self._scratch.get(key)
+        if t is None:
+            t = torch.empty(s, T, H, 2, dtype=torch.float32, device=self.query_start_loc.device)
+            self._scratch[key] = t
+        return t
+
+
+@dataclass
+class ModelCaches:
+    k: list          # per attention layer [blocks, Hkv_local, block_size, hd]
+    v: list
+    conv: list       # per GDN layer [slots, conv_dim_local, W-1] bf16
+    ssm: list        # per GDN layer [slots, Hv_local, dv, dk]
+    block_size: int
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for ts in (self.k, self.v, self.conv, self.ssm)
+                   for t in ts)
+
+
+# ---------------------------------------------------------------------------------------------
+# tensor-parallel helpers
+# ---------------------------------------------------------------------------------------------
+@dataclass
+class TPInfo:
+    rank: int = 0
+    size: int = 1
+    all_reduce: Optional[Callable[[torch.Tensor], torch.Tensor]] = None
+    all_gather_last: Optional[Callable[[torch.Tensor], torch.Tensor]] = None
+
+    def shard(self, n: int) -> tuple[int, int]:
+        assert n % self.size == 0, (n, self.size)
+        per = n // self.size
+        return self.rank * per, per
+
+
+def _cat_sections(w: torch.Tensor, sections: list[int], tp: TPInfo) -> torch.Tensor:
+    """Column-parallel slice of a merged weight made of `sections` along dim 0."""
+    parts, off = [], 0
+    for n in sections:
+        s0, per = tp.shard(n)
+        parts.append(w[off + s0: off + s0 + per])
+        off += n
+    return torch.cat(parts, 0)
+
+
+# ---------------------------------------------------------------------------------------------
+# layers
+# ---------------------------------------------------------------------------------------------
+class GDNMixer:
+    def __init__(self, cfg: ModelConfig, tp: TPInfo, quant: str, gen: torch.Generator, device):
+        self.cfg = cfg
+        self.tp = tp
+        H = cfg.hidden_size
+        self.Hk = cfg.gdn_num_k_heads // tp.size
+        self.Hv = cfg.gdn_num_v_heads // tp.size
+        self.dk, self.dv = cfg.gdn_head_k_dim, cfg.gdn_head_v_dim
+        self.key_dim = self.Hk * self.dk
+        self.value_dim = self.Hv * self.dv
+        self.conv_dim = 2 * self.key_dim + self.value_dim
+        std = cfg.init_std
+        kd, vd, hv = cfg.gdn_key_dim, cfg.gdn_value_dim, cfg.gdn_num_v_heads
+        w_in = torch.randn(cfg.gdn_in_proj_dim, H, generator=gen, device=device) * std
+        w_in = _cat_sections(w_in, [kd, kd, vd, vd, hv, hv], tp)
+        self.in_proj = Linear(w_in, quant, "in_proj")
+        del w_in
+        conv = (torch.rand(cfg.gdn_conv_dim, cfg.gdn_conv_kernel, generator=gen, device=device) - 0.5)
+        self.conv_w = _cat_sections(conv, [kd, kd, vd], tp).to(torch.bfloat16).contiguous()
+        A = torch.rand(hv, generator=gen, device=device) * 15 + 1
+        self.A_log = torch.log(A).float()[tp.shard(hv)[0]: tp.shard(hv)[0] + self.Hv].contiguous()
+        dtb = torch.randn(hv, generator=gen, device=device) * 0.1
+        self.dt_bias = dtb.float()[tp.shard(hv)[0]: tp.shard(hv)[0] + self.Hv].contiguous()
+        self.norm_w = (1 + 0.02 * torch.randn(self.dv, generator=gen, device=device)).to(torch.bfloat16)
+        w_out = torch.randn(H, vd, generator=gen, device=device) * std
+        s0, per = tp.shard(vd)
+        self.out_proj = Linear(w_out[:, s0:s0 + per].contiguous(), quant, "out_proj")
+        del w_out
+        self.quant = quant
+        self.scale = self.dk ** -0.5
+
+    def forward(self, x, meta: StepMeta, conv_state, ssm_state):
+        cfg = self.cfg
+        proj = self.in_proj(x)                                    # [T, in_proj_local]
+        cd, vd = self.conv_dim, self.value_dim
+        xc = proj[:, :cd]
+        z = proj[:, cd:cd + vd]
+        ba = proj[:, cd + vd:]
+        y = K.gdn_conv(xc, self.conv_w, conv_state, meta, self.key_dim, self.dk)
+        K.gdn_conv_state_update(xc, conv_state, meta, meta.commit_len)
+        o = K.gdn_recurrent(y, ba, self.A_log, self.dt_bias, ssm_state, meta, self.Hk, self.scale,
+                            commit_len=meta.commit_len)
+        if self.quant == "bf16":
+            h = self.out_proj(K.gdn_gated_norm(o, z, self.norm_w, cfg.rms_norm_eps, self.dv))
+        else:
+            h = self.out_proj(K.gdn_norm_quant(o, z, self.norm_w, cfg.rms_norm_eps, self.dv))
+        return h
+
+
+class AttentionMixer:
+    def __init__(self, cfg: ModelConfig, tp: TPInfo, quant: str, gen: torch.Generator, device):
+        self.cfg = cfg
+        self.tp = tp
+        H = cfg.hidden_size
+        hd = cfg.head_dim
+        self.hd = hd
+        self.Hq = cfg.num_q_heads // tp.size
+        # kv heads: sharded when divisible, else replicated (one kv head per group of ranks)
+        if cfg.num_kv_heads % tp.size == 0:
+            self.Hkv = cfg.num_kv_heads // tp.size
+            kv_sel = [tp.rank * self.Hkv + i for i in range(self.Hkv)]
+        else:
+            assert tp.size % cfg.num_kv_heads == 0
+            self.Hkv = 1
+            kv_sel = [tp.rank * cfg.num_kv_heads // tp.size]
+        std = cfg.init_std
+        gated = cfg.attn_output_gate
+        qd = cfg.num_q_heads * hd * (2 if gated else 1)
+        w = torch.randn(cfg.qkv_proj_dim, H, generator=gen, device=device) * std
+        s0, per = tp.shard(qd)
+        kvd = cfg.num_kv_heads * hd
+        k_rows = torch.cat([w[qd + h * hd: qd + (h + 1) * hd] for h in kv_sel])
+        v_rows = torch.cat([w[qd + kvd + h * hd: qd + kvd + (h + 1) * hd] for h in kv_sel])
+        self.qkv = Linear(torch.cat([w[s0:s0 + per], k_rows, v_rows]), quant, "qkv")
+        del w
+        self.q_norm = (0.02 * torch.randn(hd, generator=gen, device=device)).to(torch.bfloat16)
+        self.k_norm = (0.02 * torch.randn(hd, generator=gen, device=device)).to(torch.bfloat16)
+        w_o = torch.randn(H, cfg.num_q_heads * hd, generator=gen, device=device) * std
+        s0, per = tp.shard(cfg.num_q_heads * hd)
+        self.o_proj = Linear(w_o[:, s0:s0 + per].contiguous(), quant, "o_proj")
+        del w_o
+        self.quant = quant
+        self.gated = gated
+        self.scale = hd ** -0.5
+        self.cos_sin = None
+
+    def forward(self, x, meta: StepMeta, k_cache, v_cache):
+        cfg = self.cfg
+        hd = self.hd
+        qkv = self.qkv(x)
+        T = qkv.shape[0]
+        q = K.qkv_prologue(qkv, meta.positions, self.q_norm, self.k_norm, self.cos_sin, k_cache,
+                           v_cache, meta.slot_mapping, num_q_heads=self.Hq,
+                           num_kv_heads=self.Hkv, head_dim=hd, rotary_dim=cfg.rotary_dim,
+                           theta=cfg.rope_theta, eps=cfg.rms_norm_eps, gated=self.gated,
+                           block_size=k_cache.shape[2])
+        a = K.paged_attention(q, k_cache, v_cache, meta, self.scale).view(T, -1)
+        if self.gated:
+            gate = qkv[:, hd:]
+            if self.quant == "bf16":
+                return self.o_proj(K.gate_mul(a, gate, hd, 2 * hd))
+            return self.o_proj(K.gate_mul_quant(a, gate, hd, 2 * hd))
+        return self.o_proj(a if self.quant == "bf16" else K.quant_fp8(a))
+
+
+class MLP:
+    def __init__(self, cfg: ModelConfig, tp: TPInfo, quant: str, gen: torch.Generator, device,
+                 inter: Optional[int] = None):
+        H = cfg.hidden_size
+        I = inter or cfg.intermediate_size
+        std = cfg.init_std
+        w = torch.randn(2 * I, H, generator=gen, device=device) * std
+        self.gate_up = Linear(_cat_sections(w, [I, I], tp), quant, "gate_up")
+        del w
+        w = torch.randn(H, I, generator=gen, device=device) * std
+        s0, per = tp.shard(I)
+        self.down = Linear(w[:, s0:s0 + per].contiguous(), quant, "down")
+        del w
+        self.quant = quant
+
+    def forward(self, x):
+        gu = self.gate_up(x)
+        if self.quant == "bf16":
+            from ..ops import reference as ref
+            return self.down(ref.silu_mul(gu) if not gu.is_cuda else _silu_mul_cuda(gu))
+        return self.down(K.silu_mul_quant(gu))
+
+
+def _silu_mul_cuda(gu):
+    q, s = K.silu_mul_quant(gu)
+    return (q.float() * s[:, None]).to(torch.bfloat16)
+
+
+class DecoderLayer:
+    def __init__(self, cfg, idx, tp, quant, gen, device):
+        self.idx = idx
+        self.is_attn = cfg.is_attention_layer(idx)
+        self.ln1 = (0.02 * torch.randn(cfg.hidden_size, generator=gen, device=device)).to(torch.bfloat16)
+        self.ln2 = (0.02 * torch.randn(cfg.hidden_size, generator=gen, device=device)).to(torch.bfloat16)
+        if self.is_attn:
+            self.mixer = AttentionMixer(cfg, tp, quant, gen, device)
+        else:
+            self.mixer = GDNMixer(cfg, tp, quant, gen, device)
+        if cfg.is_moe:
+            from .moe import MoEBlock
+            self.mlp = MoEBlock(cfg, tp, quant, gen, device)
+        else:
+            self.mlp = MLP(cfg, tp, quant, gen, device)
+
+
+class HybridModel:
+    """Random-init (or loaded) hybrid model.  Weights are created per layer on `device` and
+    quantized to MXFP4 at load when quant == 'mxfp4'."""
+
+    def __init__(self, cfg: ModelConfig, quant: str = "mxfp4", device="cpu", seed: int = 0,
+                 tp: Optional[TPInfo] = None, init_device=None):
+        self.cfg = cfg
+        self.quant = quant
+        self.device = torch.device(device)
+        self.tp = tp or TPInfo()
+        init_dev = torch.device(init_device) if init_device is not None else self.device
+        gen = torch.Generator(device=init_dev)
+        gen.manual_seed(seed)
+        H, V = cfg.hidden_size, cfg.vocab_size
+        self.embed = (torch.randn(V, H, generator=gen, device=init_dev) * cfg.init_std).to(torch.bfloat16)
+        self.layers = []
+        for i in range(cfg.num_layers):
+            self.layers.append(DecoderLayer(cfg, i, self.tp, quant, gen, init_dev))
+        self.final_norm = (0.02 * torch.randn(H, generator=gen, device=init_dev)).to(torch.bfloat16)
+        # vocab-parallel lm_head
+        w = torch.randn(V, H, generator=gen, device=init_dev) * cfg.init_std
+        s0, per = self.tp.shard(V)
+        self.vocab_start = s0
+        self.lm_head = Linear(w[s0:s0 + per].contiguous(), quant if quant != "bf16" else "bf16", "lm_head")
+        del w
+        if init_dev != self.device:
+            self.to(self.device)
+        self._init_rope()
+
+    def _init_rope(self):
+        cfg = self.cfg
+        for layer in self.layers:
+            if layer.is_attn:
+                if self.device.type == "cuda":
+                    layer.mixer.cos_sin = rope_cache(cfg.max_position_embeddings, cfg.rotary_dim,
+                                                     cfg.rope_theta, self.device)
+
+    def to(self, device):
+        device = torch.device(device)
+
+        def mv(obj):
+            for k, v in list(vars(obj).items()):
+                if isinstance(v, torch.Tensor):
+                    setattr(obj, k, v.to(device))
+                elif isinstance(v, Linear):
+                    v.to(device)
+        self.embed = self.embed.to(device)
+        self.final_norm = self.final_norm.to(device)
+        self.lm_head.to(device)
+        for layer in self.layers:
+            mv(layer)
+            mv(layer.mixer)
+            mv(layer.mlp)
+            if hasattr(layer.mlp, "to"):
+                layer.mlp.to(device)
+        self.device = device
+        return self
+
+    # ---- caches ----
+    def make_caches(self, num_blocks: int, block_size: int, num_slots: int,
+                    kv_dtype: str = "fp8", ssm_dtype: str = "float32") -> ModelCaches:
+        cfg = self.cfg
+        kdt = {"fp8": torch.float8_e4m3fn, "bf16": torch.bfloat16}[kv_dtype]
+        sdt = {"float32": torch.float32, "bfloat16": torch.bfloat16}[ssm_dtype]
+        ks, vs, convs, ssms = [], [], [], []
+        for layer in self.layers:
+            m = layer.mixer
+            if layer.is_attn:
+                # zero-filled: stale pages never hold NaN bit patterns
+                ks.append(torch.zeros(num_blocks, m.Hkv, block_size, m.hd, dtype=kdt, device=self.device))
+                vs.append(torch.zeros(num_blocks, m.Hkv, block_size, m.hd, dtype=kdt, device=self.device))
+            else:
+                convs.append(torch.zeros(num_slots, m.conv_dim, cfg.gdn_conv_kernel - 1,
+                                         dtype=torch.bfloat16, device=self.device))
+                ssms.append(torch.zeros(num_slots, m.Hv, m.dv, m.dk, dtype=sdt, device=self.device))
+        return ModelCaches(ks, vs, convs, ssms, block_size)
+
+    def cache_bytes_per_block(self, block_size: int, kv_dtype: str = "fp8") -> int:
+        es = 1 if kv_dtype == "fp8" else 2
+        n = 0
+        for layer in self.layers:
+            if layer.is_attn:
+                n += 2 * layer.mixer.Hkv * block_size * layer.mixer.hd * es
+        return n
+
+    def state_bytes_per_slot(self, ssm_dtype: str = "float32") -> int:
+        es = 4 if ssm_dtype == "float32" else 2
+        n = 0
+        for layer in self.layers:
+            if not layer.is_attn:
+                m = layer.mixer
+                n += m.conv_dim * (self.cfg.gdn_conv_kernel - 1) * 2 + m.Hv * m.dv * m.dk * es
+        return n
+
+    # ---- forward ----
+    def _reduce(self, h):
+        if self.tp.size > 1:
+            return self.tp.all_reduce(h)
+        return h
+
+    def forward(self, input_ids: torch.Tensor, meta: StepMeta, caches: ModelCaches,
+                aux_layers: Optional[list] = None, aux_out: Optional[list] = None) -> torch.Tensor:
+        """Returns final-normed hidden states [T, H] bf16.  When `aux_layers` is given, the
+        residual stream after each listed layer is appended to `aux_out` (drafter conditioning)."""
+        cfg = self.cfg
+        eps = cfg.rms_norm_eps
+        x = self.embed[input_ids.long()] if input_ids.is_cuda else self.embed[input_ids.long()]
+        residual = None
+        h = x
+        ai = gi = 0
+        quant = self.quant != "bf16"
+        for li, layer in enumerate(self.layers):
+            if quant:
+                a_in = K.add_rms_quant(h, residual, layer.ln1, eps)
+                residual = a_in[2]
+                a_in = (a_in[0], a_in[1])
+            else:
+                a_in, residual = K.add_rms_norm(h, residual, layer.ln1, eps)
+            if layer.is_attn:
+                h = layer.mixer.forward(a_in, meta, caches.k[ai], caches.v[ai])
+                ai += 1
+            else:
+                h = layer.mixer.forward(a_in, meta, caches.conv[gi], caches.ssm[gi])
+                gi += 1
+            h = self._reduce(h)
+            if quant:
+                q, s, residual = K.add_rms_quant(h, residual, layer.ln2, eps)
+                h = layer.mlp.forward((q, s))
+            else:
+                n, residual = K.add_rms_norm(h, residual, layer.ln2, eps)
+                h = layer.mlp.forward(n)
+            h = self._reduce(h)
+            if aux_layers is not None and li in aux_layers:
+                aux_out.append((h.float() + residual.float()).to(torch.bfloat16))
+        out, _ = K.add_rms_norm(h, residual, self.final_norm, eps, want_residual=False)
+        return out
+
+    def logits(self, hidden: torch.Tensor) -> torch.Tensor:
+        """[n, H] -> [n, V] bf16 (vocab-parallel shards gathered when TP > 1)."""
+        lg = self.lm_head(hidden)
+        if self.tp.size > 1:
+            lg = self.tp.all_gather_last(lg)
+        return lg
+
+    def weight_bytes(self) -> int:
+        n = self.embed.numel() * 2 + self.lm_head.nbytes
+        for layer in self.layers:
+            for obj in (layer.mixer, layer.mlp):
+                for v in vars(obj).values():
+                    if isinstance(v, Linear):
+                        n += v.nbytes
+        return n

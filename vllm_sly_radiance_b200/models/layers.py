@@ -1,0 +1,100 @@
+"""Model building blocks: linears (MXFP4 W4A8, bf16, fp8 baseline), RoPE tables, norms.
+
+A linear consumes either a bf16 activation or a pre-quantized ``(q_e4m3, scale)`` pair produced
+by a fused producer kernel (the reference's tuple input contract,
+``sly/mxfp4/radiance_mxfp4.py:1186-1193``)."""
+from __future__ import annotations
+
+import math
+from typing import Optional, Union
+
+import torch
+
+from ..ops import kernels as K
+from ..quant.mxfp4 import MXFP4Weight
+
+Act = Union[torch.Tensor, tuple]
+
+
+def rope_cache(max_pos: int, rotary_dim: int, theta: float, device) -> torch.Tensor:
+    """[max_pos, rotary_dim] fp32: cos in [:rot/2], sin in [rot/2:], computed in fp64."""
+    inv = 1.0 / (theta ** (torch.arange(0, rotary_dim, 2, dtype=torch.float64) / rotary_dim))
+    ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None]
+    return torch.cat([torch.cos(ang), torch.sin(ang)], 1).float().to(device)
+
+
+class Linear:
+    """y = x W^T with W [N, K] stored as MXFP4 (W4A8 path), bf16, or per-channel fp8 (the
+    cuBLAS baseline build)."""
+
+    def __init__(self, weight: torch.Tensor, quant: str = "mxfp4", name: str = ""):
+        self.name = name
+        self.quant = quant
+        self.N, self.K = weight.shape
+        if quant == "mxfp4":
+            self.w = MXFP4Weight.from_float(weight)
+        elif quant == "bf16":
+            self.w = weight.to(torch.bfloat16).contiguous()
+        elif quant == "fp8":
+            amax = weight.float().abs().amax(1).clamp(min=1e-8)
+            self.w_scale = (amax / 448.0).float()
+            self.w = (weight.float() / self.w_scale[:, None]).clamp(-448, 448).to(
+                torch.float8_e4m3fn).contiguous()
+        else:
+            raise ValueError(quant)
+
+    @staticmethod
+    def from_mxfp4(w: MXFP4Weight, name: str = "") -> "Linear":
+        lin = Linear.__new__(Linear)
+        lin.name, lin.quant, lin.N, lin.K, lin.w = name, "mxfp4", w.N, w.K, w
+        return lin
+
+    def to(self, device) -> "Linear":
+        if self.quant == "mxfp4":
+            self.w = self.w.to(device)
+        else:
+            self.w = self.w.to(device)
+            if self.quant == "fp8":
+                self.w_scale = self.w_scale.to(device)
+        return self
+
+    @property
+    def nbytes(self) -> int:
+        if self.quant == "mxfp4":
+            return self.w.nbytes
+        return self.w.numel() * self.w.element_size()
+
+    def __call__(self, x: Act, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if self.quant == "mxfp4":
+            if isinstance(x, tuple):
+                q, s = x
+            else:
+                q, s = K.quant_fp8(x)
+            return K.mxfp4_gemm(q, s, self.w.packed, self.w.sf, self.w.scales, self.N, out=out)
+        if self.quant == "fp8":
+            if isinstance(x, tuple):
+                q, s = x
+            else:
+                q, s = K.quant_fp8(x)
+            if q.is_cuda:
+                y = torch._scaled_mm(q, self.w.t(), scale_a=s[:, None].float(),
+                                     scale_b=self.w_scale[None, :].float(), out_dtype=torch.bfloat16)
+            else:
+                y = ((q.float() * s[:, None]) @ (self.w.float() * self.w_scale[:, None]).t()).to(
+                    torch.bfloat16)
+            if out is not None:
+                out.copy_(y)
+                return out
+            return y
+        # bf16
+        if isinstance(x, tuple):
+            q, s = x
+            x = (q.float() * s[:, None]).to(torch.bfloat16)
+        if x.is_cuda:
+            y = torch.matmul(x, self.w.t())
+        else:
+            y = (x.float() @ self.w.float().t()).to(torch.bfloat16)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y

@@ -1,0 +1,334 @@
+"""Engine ops.  CUDA tensors run the sm_100a kernels of ``csrc/``; CPU tensors run the PyTorch
+oracle of ``ops/reference.py`` (the CPU model of the tiny config and the fp32 references of the
+kernel tests).  There is no CUDA->PyTorch fallback: a missing kernel library raises."""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from . import reference as ref
+from ._ext import ext
+
+_EMPTY: dict = {}
+
+
+def _empty(device) -> torch.Tensor:
+    t = _EMPTY.get(device)
+    if t is None:
+        t = torch.empty(0, device=device)
+        _EMPTY[device] = t
+    return t
+
+
+_STATUS: dict = {}
+
+
+def status_word(device) -> torch.Tensor:
+    """Per-device int32 error word the kernels write on a bounded-wait timeout (0 = ok)."""
+    t = _STATUS.get(device)
+    if t is None:
+        t = torch.zeros(4, dtype=torch.int32, device=device)
+        _STATUS[device] = t
+    return t
+
+
+def check_status(device, reset: bool = True) -> int:
+    """Host check of the device error word (syncs).  Raises on a recorded kernel timeout."""
+    t = status_word(device)
+    code = int(t[0].item())
+    if code != 0:
+        if reset:
+            t.zero_()
+        raise RuntimeError(f"kernel reported error code {code} (bounded wait timed out)")
+    return code
+
+
+def _none(t, device):
+    return t if t is not None else _empty(device)
+
+
+# ---------------------------------------------------------------------------------------------
+# producers
+# ---------------------------------------------------------------------------------------------
+def add_rms_quant(x: torch.Tensor, residual: Optional[torch.Tensor], weight: torch.Tensor,
+                  eps: float, res_out: Optional[torch.Tensor] = None):
+    """-> (q e4m3 [M,H], scale fp32 [M], residual_out bf16 [M,H])."""
+    if not x.is_cuda:
+        return ref.add_rms_quant(x, residual, weight, eps)
+    M, H = x.shape
+    q = torch.empty(M, H, dtype=torch.float8_e4m3fn, device=x.device)
+    s = torch.empty(M, dtype=torch.float32, device=x.device)
+    if res_out is None:
+        res_out = torch.empty(M, H, dtype=torch.bfloat16, device=x.device)
+    e = _empty(x.device)
+    ext().add_rms_quant(x, _none(residual, x.device), weight, res_out, q, s, e, eps)
+    return q, s, res_out
+
+
+def add_rms_norm(x: torch.Tensor, residual: Optional[torch.Tensor], weight: torch.Tensor,
+                 eps: float, want_residual: bool = True):
+    """-> (normed bf16, residual_out bf16 or None)."""
+    if not x.is_cuda:
+        n, r = ref.add_rms_norm(x, residual, weight, eps)
+        return n, r
+    M, H = x.shape
+    n = torch.empty(M, H, dtype=torch.bfloat16, device=x.device)
+    r = torch.empty(M, H, dtype=torch.bfloat16, device=x.device) if want_residual else None
+    e = _empty(x.device)
+    ext().add_rms_quant(x, _none(residual, x.device), weight, _none(r, x.device), e, e, n, eps)
+    return n, r
+
+
+def silu_mul_quant(gate_up: torch.Tensor):
+    if not gate_up.is_cuda:
+        return ref.silu_mul_quant(gate_up)
+    M, I2 = gate_up.shape
+    q = torch.empty(M, I2 // 2, dtype=torch.float8_e4m3fn, device=gate_up.device)
+    s = torch.empty(M, dtype=torch.float32, device=gate_up.device)
+    ext().silu_mul_quant(gate_up, q, s)
+    return q, s
+
+
+def gdn_norm_quant(o: torch.Tensor, z: torch.Tensor, weight: torch.Tensor, eps: float,
+                   head_dim: int):
+    if not o.is_cuda:
+        return ref.gdn_norm_quant(o, z, weight, eps, head_dim)
+    M, D = o.shape
+    q = torch.empty(M, D, dtype=torch.float8_e4m3fn, device=o.device)
+    s = torch.empty(M, dtype=torch.float32, device=o.device)
+    ext().gdn_norm_quant(o, z, weight, head_dim, eps, q, s, _empty(o.device))
+    return q, s
+
+
+def gdn_gated_norm(o, z, weight, eps, head_dim):
+    if not o.is_cuda:
+        return ref.gdn_gated_norm(o, z, weight, eps, head_dim)
+    M, D = o.shape
+    n = torch.empty(M, D, dtype=torch.bfloat16, device=o.device)
+    e = _empty(o.device)
+    ext().gdn_norm_quant(o, z, weight, head_dim, eps, e, e, n)
+    return n
+
+
+def gate_mul_quant(a: torch.Tensor, gate: torch.Tensor, head_dim: int, gate_head_stride: int):
+    """a [M, H*hd]; gate = a strided view whose head h starts at column h*gate_head_stride."""
+    if not a.is_cuda:
+        M = a.shape[0]
+        H = a.shape[1] // head_dim
+        g = torch.stack([gate[:, h * gate_head_stride:h * gate_head_stride + head_dim]
+                         for h in range(H)], 1).reshape(M, -1)
+        return ref.gate_mul_quant(a, g)
+    M, D = a.shape
+    q = torch.empty(M, D, dtype=torch.float8_e4m3fn, device=a.device)
+    s = torch.empty(M, dtype=torch.float32, device=a.device)
+    ext().gate_mul_quant(a, gate, head_dim, gate_head_stride, q, s, _empty(a.device))
+    return q, s
+
+
+def gate_mul(a, gate, head_dim, gate_head_stride):
+    if not a.is_cuda:
+        M = a.shape[0]
+        H = a.shape[1] // head_dim
+        g = torch.stack([gate[:, h * gate_head_stride:h * gate_head_stride + head_dim]
+                         for h in range(H)], 1).reshape(M, -1)
+        return ref.gate_mul(a, g)
+    M, D = a.shape
+    n = torch.empty(M, D, dtype=torch.bfloat16, device=a.device)
+    e = _empty(a.device)
+    ext().gate_mul_quant(a, gate, head_dim, gate_head_stride, e, e, n)
+    return n
+
+
+def quant_fp8(x: torch.Tensor):
+    if not x.is_cuda:
+        return ref.quant_fp8_rows(x)
+    M, D = x.shape
+    q = torch.empty(M, D, dtype=torch.float8_e4m3fn, device=x.device)
+    s = torch.empty(M, dtype=torch.float32, device=x.device)
+    ext().quant_fp8_rows(x, q, s)
+    return q, s
+
+
+# ---------------------------------------------------------------------------------------------
+# linears
+# ---------------------------------------------------------------------------------------------
+def mxfp4_gemm(q: torch.Tensor, scale: torch.Tensor, packed: torch.Tensor, sf: torch.Tensor,
+               scales_plain: torch.Tensor, N: int, out: Optional[torch.Tensor] = None,
+               splits: int = 0) -> torch.Tensor:
+    if not q.is_cuda:
+        return ref.mxfp4_linear(q, scale, packed, scales_plain)
+    M = q.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=q.device)
+    ext().mxfp4_gemm(q, scale, packed, sf, out, splits, status_word(q.device))
+    return out
+
+
+# ---------------------------------------------------------------------------------------------
+# attention
+# ---------------------------------------------------------------------------------------------
+def qkv_prologue(qkv, positions, q_norm_w, k_norm_w, cos_sin, k_cache, v_cache, slot_mapping, *,
+                 num_q_heads, num_kv_heads, head_dim, rotary_dim, theta, eps, gated, block_size):
+    """-> q [T,Hq,D] bf16 (e4m3-rounded when the cache is fp8); k/v written into the caches."""
+    T = qkv.shape[0]
+    qd = num_q_heads * head_dim * (2 if gated else 1)
+    kd = num_kv_heads * head_dim
+    if not qkv.is_cuda:
+        q, k, v, _ = ref.qkv_prologue(qkv, positions, q_norm_w, k_norm_w,
+                                      num_q_heads=num_q_heads, num_kv_heads=num_kv_heads,
+                                      head_dim=head_dim, rotary_dim=rotary_dim, theta=theta,
+                                      eps=eps, gated=gated)
+        ref.kv_cache_write(k, v, k_cache, v_cache, slot_mapping, block_size)
+        if k_cache.dtype == torch.float8_e4m3fn:
+            q = ref.fp8_e4m3(q.float()).to(torch.bfloat16)
+        return q
+    q = torch.empty(T, num_q_heads, head_dim, dtype=torch.bfloat16, device=qkv.device)
+    ext().qkv_prologue(qkv, head_dim * (2 if gated else 1), qd, qd + kd, positions, q_norm_w,
+                       k_norm_w, cos_sin, rotary_dim, num_q_heads, num_kv_heads, eps, q, k_cache,
+                       v_cache, slot_mapping)
+    return q
+
+
+def paged_attention(q, k_cache, v_cache, meta, scale: float, causal: bool = True,
+                    window: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Varlen paged attention over the batch described by ``meta`` (an AttnMeta)."""
+    if not q.is_cuda:
+        return ref.paged_attention(q, k_cache, v_cache, meta.block_tables, meta.seq_lens,
+                                   meta.query_start_loc, k_cache.shape[2], scale, causal, window)
+    T, Hq, D = q.shape
+    if out is None:
+        out = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=q.device)
+    splits = meta.num_splits
+    if splits > 1:
+        part_o = meta.scratch_o(splits, T, Hq, D)
+        part_ml = meta.scratch_ml(splits, T, Hq)
+    else:
+        part_o = part_ml = _empty(q.device)
+    ext().paged_attention(q, k_cache, v_cache, meta.block_tables, meta.seq_lens,
+                          meta.query_start_loc, meta.tile_seq, meta.tile_row0, scale, causal,
+                          window, splits, part_o, part_ml, out)
+    return out
+
+
+# ---------------------------------------------------------------------------------------------
+# gated delta net
+# ---------------------------------------------------------------------------------------------
+def gdn_conv(x, conv_w, conv_state, meta, qk_dim: int, head_dim: int, eps: float = 1e-6):
+    """x [T, conv_dim] (pre-conv q|k|v) -> y [T, conv_dim] bf16 (SiLU, q/k L2-normed).
+    The conv state is NOT updated here (gdn_conv_state_update does it)."""
+    T, C = x.shape[0], conv_w.shape[0]
+    if not x.is_cuda:
+        y = torch.empty(T, C, dtype=torch.bfloat16)
+        qsl = meta.query_start_loc
+        for b in range(meta.num_seqs):
+            s0, s1 = int(qsl[b]), int(qsl[b + 1])
+            if s1 == s0:
+                continue
+            st = conv_state[int(meta.state_slots[b])] if int(meta.has_initial[b]) else None
+            yy, _ = ref.causal_conv1d(x[s0:s1, :C], conv_w, st)
+            yy = yy.clone()
+            nk = qk_dim // head_dim
+            for hh in range(2 * nk):
+                sl = slice(hh * head_dim, (hh + 1) * head_dim)
+                yy[:, sl] = ref.l2norm(yy[:, sl])
+            y[s0:s1] = yy.to(torch.bfloat16)
+        return y
+    y = torch.empty(T, C, dtype=torch.bfloat16, device=x.device)
+    # the kernel L2-normalises the first `2 * qk_dim` channels (q and k heads)
+    ext().gdn_conv(x, conv_w, conv_state, meta.query_start_loc, meta.state_slots,
+                   meta.has_initial, meta.token_seq, 2 * qk_dim, head_dim, y, eps)
+    return y
+
+
+def gdn_conv_state_update(x, conv_state, meta, commit_len: Optional[torch.Tensor] = None):
+    C = conv_state.shape[1]
+    if not x.is_cuda:
+        qsl = meta.query_start_loc
+        for b in range(meta.num_seqs):
+            s0, s1 = int(qsl[b]), int(qsl[b + 1])
+            n = int(commit_len[b]) if commit_len is not None else s1 - s0
+            slot = int(meta.state_slots[b])
+            st = conv_state[slot].float() if int(meta.has_initial[b]) else \
+                torch.zeros(C, conv_state.shape[2])
+            xx = torch.cat([st.t(), x[s0:s0 + n, :C].float()], 0)
+            conv_state[slot] = xx[-conv_state.shape[2]:].t().to(conv_state.dtype)
+        return
+    ext().gdn_conv_state_update(x, conv_state, meta.query_start_loc, meta.state_slots,
+                                meta.has_initial, _none(commit_len, x.device))
+
+
+def gdn_recurrent(y, ba, A_log, dt_bias, ssm_state, meta, num_k_heads: int, scale: float,
+                  out: Optional[torch.Tensor] = None, commit_len=None, write_out: bool = True):
+    """Delta rule over the batch; ssm_state [S, Hv, dv, dk] updated in place (after the first
+    commit_len[b] tokens when given).  Returns o [T, Hv*dv] bf16."""
+    T = y.shape[0]
+    S_, Hv, DV, DK = ssm_state.shape
+    if out is None:
+        out = torch.empty(T, Hv * DV, dtype=torch.bfloat16, device=y.device)
+    if not y.is_cuda:
+        key_dim = num_k_heads * DK
+        qsl = meta.query_start_loc
+        for b in range(meta.num_seqs):
+            s0, s1 = int(qsl[b]), int(qsl[b + 1])
+            if s1 == s0:
+                continue
+            slot = int(meta.state_slots[b])
+            st = ssm_state[slot].float() if int(meta.has_initial[b]) else torch.zeros(Hv, DV, DK)
+            q = y[s0:s1, :key_dim].float().view(-1, num_k_heads, DK)
+            k = y[s0:s1, key_dim:2 * key_dim].float().view(-1, num_k_heads, DK)
+            v = y[s0:s1, 2 * key_dim:2 * key_dim + Hv * DV].float().view(-1, Hv, DV)
+            g, beta = ref.gdn_gates(ba[s0:s1, Hv:2 * Hv], ba[s0:s1, :Hv], A_log, dt_bias)
+            n = int(commit_len[b]) if commit_len is not None else s1 - s0
+            o, _ = ref.gdn_recurrent(q, k, v, g, beta, st, scale)
+            _, st_c = ref.gdn_recurrent(q[:n], k[:n], v[:n], g[:n], beta[:n], st, scale)
+            ssm_state[slot] = st_c.to(ssm_state.dtype)
+            if write_out:
+                out[s0:s1] = o.reshape(s1 - s0, -1).to(torch.bfloat16)
+        return out
+    ext().gdn_recurrent(y, ba, A_log, dt_bias, ssm_state, meta.query_start_loc, meta.state_slots,
+                        meta.has_initial, _none(commit_len, y.device), num_k_heads, scale, out,
+                        write_out)
+    return out
+
+
+# ---------------------------------------------------------------------------------------------
+# sampling
+# ---------------------------------------------------------------------------------------------
+def argmax(logits: torch.Tensor) -> torch.Tensor:
+    if not logits.is_cuda:
+        return logits.float().argmax(-1)
+    ids = torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device)
+    ext().argmax_rows(logits, ids, _empty(logits.device))
+    return ids
+
+
+def sample_from_topk(vals, ids, temperature, top_k, top_p, min_p, seeds, step: int,
+                     want_probs: bool = False):
+    """vals/ids [B, K] sorted descending -> (token ids [B], probs over the window or None)."""
+    B, K = vals.shape
+    out = torch.empty(B, dtype=torch.int64, device=vals.device)
+    probs = torch.empty(B, K, dtype=torch.float32, device=vals.device) if want_probs else None
+    if not vals.is_cuda:
+        gen = torch.Generator()
+        res = []
+        pr = []
+        for b in range(B):
+            T = float(temperature[b])
+            if T <= 0:
+                res.append(int(ids[b, 0]))
+                pr.append(torch.nn.functional.one_hot(torch.tensor(0), K).float())
+                continue
+            lg = vals[b].float() / T
+            masked = ref.apply_top_k_top_p(lg[None], top_k[b:b + 1], top_p[b:b + 1],
+                                           None if min_p is None else min_p[b:b + 1])[0]
+            p = torch.softmax(masked, -1)
+            gen.manual_seed(int(seeds[b]) * 1000003 + step)
+            res.append(int(ids[b, torch.multinomial(p, 1, generator=gen)]))
+            pr.append(p)
+        out = torch.tensor(res, dtype=torch.int64)
+        return out, (torch.stack(pr) if want_probs else None)
+    ext().sample_from_topk(vals.float().contiguous(), ids.contiguous(), temperature, top_k,
+                           top_p, _none(min_p, vals.device), seeds, step, out,
+                           _empty(vals.device), _none(probs, vals.device))
+    return out, probs
