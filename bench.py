@@ -1,0 +1,271 @@
+"""Headline benchmark: single-stream decode tok/s of the Qwen3.8-27B-shaped GDN hybrid with
+MXFP4 W4A8 weights and an fp8 KV cache, after a 1.5k-token prompt,
+plus prefill tok/s at 1.5k and aggregate tok/s at 8 concurrent streams.
+
+    python bench.py --gpus N --steps K --warmup W          (N > 1: launched by torchrun, TP = N)
+    python bench.py --impl reference ...                     (reference arm)
+
+Timing: W untimed decode steps, then exactly K decode steps bracketed by a barrier and
+torch.cuda.synchronize() on both sides.  `value` is device time (CUDA events around each step's
+GPU work, summed over the K steps, max over ranks); `e2e` is the same K steps timed on the host
+through the public engine API (LLMEngine.step: token ids to the device from pinned memory, sampled
+ids back to the host every step).  Weights are random-init and quantized to MXFP4 at load; prompts
+are uniform-random token ids.  Inputs: a 27B decode step streams ~9 GB of weights, far larger than
+the 126 MB L2, so no explicit L2 flush is needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+BASELINE_DECODE_TOKS = 154.4       # single-stream decode, 1x R9700
+BASELINE_PREFILL_TOKS = 3927.0     # prefill-only at 1,515 tokens
+BASELINE_CONC8_TOKS = 480.0        # aggregate throughput at concurrency 8
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks / throttle reasons during the timed region."""
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu),
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+                 "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+                 "clocks_event_reasons.sw_power_cap", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 7:
+                self.samples.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = sorted(float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit())
+        mx = max((float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()), default=None)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if s[3 + i] == "Active"})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+def dist_setup(n):
+    if n <= 1:
+        return 0, 1, None
+    import datetime
+    import torch.distributed as dist
+    rank = int(os.environ["RANK"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                            device_id=torch.device("cuda", local))
+    return rank, dist.get_world_size(), dist
+
+
+def reference_arm(args):
+    line = {"impl": "reference",
+            "unavailable": "the reference (SlyBase/vllm-sly-radiance) is a ROCm/gfx1201 patch overlay "
+                           "of vLLM shipped as a Docker image: no setup.py/pyproject (pip: 'not "
+                           "installable'), HIP-only kernels, no CUDA path"}
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="native", choices=["native", "reference", "baseline"])
+    ap.add_argument("--model", default="qwen38_27b")
+    ap.add_argument("--prompt-len", type=int, default=1500)
+    ap.add_argument("--conc", type=int, default=8)
+    ap.add_argument("--no-extra", action="store_true", help="skip the prefill / concurrency extras")
+    ap.add_argument("--no-graphs", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return reference_arm(args)
+
+    rank, world, dist = dist_setup(args.gpus)
+    if world == 1:
+        torch.cuda.set_device(0)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    from vllm_sly_radiance_b200.config import EngineConfig
+    from vllm_sly_radiance_b200.engine.llm_engine import LLMEngine
+    from vllm_sly_radiance_b200.engine.request import SamplingParams
+    from vllm_sly_radiance_b200.models.hybrid import TPInfo
+    from vllm_sly_radiance_b200.parallel.comm import make_tp_info
+
+    tp = make_tp_info(rank, world, backend="nccl" if args.impl == "baseline" else "fused") \
+        if world > 1 else TPInfo()
+    max_len = args.prompt_len + args.warmup + args.steps + 64
+    cfg = EngineConfig(model=args.model, tensor_parallel_size=world, max_model_len=max(max_len, 4096),
+                       max_num_seqs=max(args.conc, 1), max_num_batched_tokens=4096,
+                       enable_cuda_graphs=not args.no_graphs, device="cuda",
+                       gemm_backend="cublas" if args.impl == "baseline" else "native",
+                       comm_backend="nccl" if args.impl == "baseline" else "fused")
+    t0 = time.time()
+    eng = LLMEngine(cfg, tp=tp)
+    torch.cuda.synchronize()
+    load_s = time.time() - t0
+    V = eng.model_config.vocab_size
+    g = torch.Generator().manual_seed(1234)
+
+    def rand_prompt(n):
+        return torch.randint(3, V, (n,), generator=g).tolist()
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    greedy = SamplingParams(temperature=0.0, max_tokens=args.warmup + args.steps + 8, ignore_eos=True)
+    # ---- single-stream decode after a 1.5k prompt ----
+    eng.add_request(rand_prompt(args.prompt_len), greedy, request_id="stream0")
+    while eng.requests["stream0"].num_computed_tokens < args.prompt_len:
+        eng.step()                       # prefill (chunked), not timed
+    for _ in range(args.warmup):
+        eng.step()
+    barrier()
+    ev = []
+    stream = torch.cuda.current_stream()
+    with ClockSampler(dev.index) as clk:
+        barrier()
+        torch.cuda.nvtx.range_push("timed")
+        w0 = time.perf_counter()
+        for _ in range(args.steps):
+            s = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            s.record(stream)
+            eng.step()
+            e.record(stream)
+            ev.append((s, e))
+        barrier()
+        wall = time.perf_counter() - w0
+        torch.cuda.nvtx.range_pop()
+    dev_ms = sum(s.elapsed_time(e) for s, e in ev)
+    dev_ms = max_over_ranks(dev_ms)
+    wall = max_over_ranks(wall)
+    value = args.steps / (dev_ms / 1e3)
+    e2e = args.steps / wall
+    eng.abort_request("stream0")
+    kernels_per_step = count_launches(eng) if rank == 0 else None
+
+    extra = {}
+    if not args.no_extra:
+        # ---- prefill-only at the prompt length (fresh request, timed) ----
+        barrier()
+        eng.add_request(rand_prompt(args.prompt_len), SamplingParams(temperature=0, max_tokens=1,
+                                                                      ignore_eos=True), "pf")
+        t1 = time.perf_counter()
+        while eng.has_unfinished_requests():
+            eng.step()
+        barrier()
+        pf = max_over_ranks(time.perf_counter() - t1)
+        extra["prefill_tok_s@%d" % args.prompt_len] = round(args.prompt_len / pf, 1)
+        extra["prefill_vs_baseline"] = round(args.prompt_len / pf / BASELINE_PREFILL_TOKS, 2)
+        # ---- aggregate throughput at concurrency C (1k prompt, 64 output tokens each) ----
+        C = args.conc
+        sp = SamplingParams(temperature=0.7, top_p=0.95, top_k=20, max_tokens=64, ignore_eos=True)
+        for i in range(C):
+            eng.add_request(rand_prompt(1000), sp, f"c{i}")
+        while any(eng.requests[f"c{i}"].num_computed_tokens < 1000 for i in range(C)
+                  if f"c{i}" in eng.requests):
+            eng.step()
+        barrier()
+        t2 = time.perf_counter()
+        ntok = 0
+        while eng.has_unfinished_requests():
+            outs = eng.step()
+            ntok += sum(1 for _ in outs)
+        barrier()
+        dt = max_over_ranks(time.perf_counter() - t2)
+        extra["agg_decode_tok_s@conc%d" % C] = round(ntok / dt, 1)
+        extra["agg_vs_baseline"] = round(ntok / dt / BASELINE_CONC8_TOKS, 2)
+
+    if rank == 0:
+        line = {
+            "metric": "single-stream decode tok/s (Qwen3.8-27B-shaped GDN hybrid, MXFP4 W4A8, fp8 KV, "
+                      "1.5k-token prompt)",
+            "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 3),
+            "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": round(value / BASELINE_DECODE_TOKS, 3), "dtype": "mxfp4-w4a8/bf16",
+            "data": "synthetic: uniform-random prompt token ids, random-init weights quantized to MXFP4 at load",
+            "config": {"model": args.model, "global_batch": 1, "seq_len": args.prompt_len,
+                       "parallelism": f"tp{world}", "kv_cache": "fp8_e4m3",
+                       "l2": "inputs larger than L2 (each decode step streams ~9 GB of weights)"},
+            "e2e": {"value": round(e2e, 2), "unit": "tok/s",
+                    "h2d_bytes_per_step": e2e_h2d_bytes(eng), "d2h_bytes_per_step": 8},
+            "gpu_launches": kernels_per_step * args.steps if kernels_per_step else None,
+            "clocks": clk.summary(),
+            "impl": args.impl,
+            "load_s": round(load_s, 1),
+            "extra": extra,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        eng.runner.graphs.clear()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def e2e_h2d_bytes(eng):
+    """Per decode step the runner copies the packed int32 metadata (token id, position, offsets,
+    lengths, state slot, block table row, attention tile) plus the int64 KV slot from pinned memory."""
+    r = eng.runner
+    L = r.L
+    return int((L.bt - 0) * 0 + (3 + 2 + 3 + 2) * 4 + r.max_blocks * 4 + 8)
+
+
+def count_launches(eng):
+    """Kernels of this library launched by one decode step (from the model structure)."""
+    n = 0
+    for layer in eng.model.layers:
+        n += 1                                  # add_rms_quant (input)
+        if layer.is_attn:
+            n += 1 + 1 + 1 + 1 + 1              # qkv gemm, prologue, attention(+merge), gate quant, o gemm
+        else:
+            n += 1 + 2 + 1 + 1 + 1              # in_proj, conv + state, recurrent, norm quant, out gemm
+        n += 1 + 1 + 1 + 1                      # add_rms_quant, gate_up, silu_mul_quant, down
+    n += 1 + 1 + 1                              # final norm, lm_head gemm, argmax
+    return n
+
+
+if __name__ == "__main__":
+    main()

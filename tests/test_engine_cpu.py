@@ -1,0 +1,112 @@
+"""CPU tests of the model math and engine: GDN recurrent vs chunked oracle, chunked prefill vs
+one-shot prefill, scheduler behaviour, the tiny config's KL(bf16 || MXFP4 W4A8)."""
+import math
+
+import pytest
+import torch
+
+from vllm_sly_radiance_b200.config import EngineConfig, tiny_hybrid
+from vllm_sly_radiance_b200.engine.kv_cache import KVCacheManager
+from vllm_sly_radiance_b200.engine.llm_engine import LLMEngine
+from vllm_sly_radiance_b200.engine.request import Request, SamplingParams
+from vllm_sly_radiance_b200.engine.scheduler import Scheduler
+from vllm_sly_radiance_b200.models.hybrid import HybridModel
+from vllm_sly_radiance_b200.ops import reference as ref
+
+
+def test_gdn_chunked_equals_recurrent():
+    torch.manual_seed(0)
+    L, Hk, Hv, dk, dv = 150, 2, 4, 16, 8
+    q = ref.l2norm(torch.randn(L, Hk, dk).double()).float()
+    k = ref.l2norm(torch.randn(L, Hk, dk).double()).float()
+    v = torch.randn(L, Hv, dv)
+    g = -torch.rand(L, Hv) * 0.1
+    beta = torch.rand(L, Hv)
+    s0 = torch.randn(Hv, dv, dk) * 0.5
+    o1, s1 = ref.gdn_recurrent(q, k, v, g, beta, s0, dk ** -0.5)
+    o2, s2 = ref.gdn_chunked(q, k, v, g, beta, s0, dk ** -0.5)
+    assert torch.allclose(o1, o2, atol=1e-4, rtol=1e-3)
+    assert torch.allclose(s1, s2, atol=1e-4, rtol=1e-3)
+
+
+def _engine(chunk, quant="mxfp4", graphs=False):
+    cfg = EngineConfig(model="tiny_hybrid", device="cpu", max_model_len=1024, max_num_seqs=4,
+                       max_num_batched_tokens=chunk, enable_cuda_graphs=graphs, num_kv_blocks=64,
+                       quantization=quant)
+    return LLMEngine(cfg)
+
+
+def _prefill_logits(eng, prompt):
+    eng.add_request(prompt, SamplingParams(temperature=0, max_tokens=1), "r")
+    while True:
+        sched = eng.scheduler.schedule()
+        res = eng.runner.execute(sched, want_logits=True)
+        eng.scheduler.update(sched, res.sampled)
+        if res.sampled:
+            return res.logits.float()
+
+
+def test_chunked_prefill_matches_single_chunk():
+    prompt = list(range(5, 5 + 200))
+    a = _prefill_logits(_engine(4096), prompt)
+    b = _prefill_logits(_engine(48), prompt)       # 5 chunks, 48 not a page multiple
+    rel = float((a - b).abs().max() / a.abs().max())
+    assert rel < 2e-2, rel
+
+
+def test_decode_matches_recompute():
+    """Greedy decode with cached state/KV produces the tokens a full recompute would."""
+    eng = _engine(4096)
+    prompt = list(range(40, 80))
+    out = eng.generate([prompt], SamplingParams(temperature=0, max_tokens=4, ignore_eos=True))[0]
+    toks = out.outputs[0].token_ids
+    # recompute the last step from scratch with prompt + first 3 generated tokens
+    eng2 = _engine(4096)
+    lg = _prefill_logits(eng2, prompt + toks[:3])
+    assert int(lg.argmax(-1)[0]) == toks[3]
+
+
+def test_kl_quantized_vs_bf16_tiny():
+    """BASELINE config 1 check: KL(bf16 || MXFP4 W4A8 + fp8 KV) on a 128-token prompt."""
+    torch.manual_seed(0)
+    prompt = torch.randint(3, 4096, (128,)).tolist()
+    lq = _prefill_logits(_engine(4096, "mxfp4"), prompt)
+    lb = _prefill_logits(_engine(4096, "bf16"), prompt)
+    p = torch.log_softmax(lb, -1)
+    q = torch.log_softmax(lq, -1)
+    kl = float((p.exp() * (p - q)).sum(-1).mean())
+    assert kl < 0.05, kl
+
+
+def test_scheduler_chunking_and_preemption():
+    kv = KVCacheManager(num_blocks=8, block_size=16, num_slots=4)
+    sch = Scheduler(kv, max_num_seqs=3, max_num_batched_tokens=64, max_model_len=512)
+    reqs = [Request(list(range(60)), SamplingParams(max_tokens=50)) for _ in range(3)]
+    for r in reqs:
+        sch.add(r)
+    out = sch.schedule()
+    assert [s.num_new_tokens for s in out.seqs] == [60, 4]
+    sampled = {s.req.request_id: [7] for s in out.seqs if s.samples}
+    sch.update(out, sampled)
+    assert reqs[0].num_computed_tokens == 60 and len(reqs[0].output_token_ids) == 1
+    # keep decoding until the 7 usable blocks run out -> preemption of the newest request
+    preempted = 0
+    for _ in range(80):
+        out = sch.schedule()
+        if out.is_empty:
+            break
+        preempted += len(out.preempted)
+        sampled = {s.req.request_id: [7] for s in out.seqs if s.samples}
+        sch.update(out, sampled)
+    assert preempted > 0
+    assert all(r.status.finished or r in sch.running or r in sch.waiting for r in reqs)
+
+
+def test_engine_generate_stop_and_abort():
+    eng = _engine(64)
+    rid = eng.add_request(list(range(30)), SamplingParams(temperature=0, max_tokens=100))
+    eng.step()
+    assert eng.abort_request(rid)
+    assert not eng.has_unfinished_requests()
+    outs = eng.generate([list(range(20))], SamplingParams(temperature=0, max_tokens=3))
+    assert len(outs[0].outputs[0].token_ids) == 3 and outs[0].outputs[0].finish_reason == "length"

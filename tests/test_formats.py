@@ -1,0 +1,80 @@
+"""Number formats: E2M1 / UE8M0 / MXFP4, e4m3 per-token, NVFP4 requant, INT4, SF tile layout."""
+import torch
+
+from vllm_sly_radiance_b200.quant import formats as F
+from vllm_sly_radiance_b200.quant.mxfp4 import MXFP4Weight, cat_rows
+
+
+def test_e2m1_roundtrip_and_ties():
+    vals = torch.tensor([0, 0.5, 1, 1.5, 2, 3, 4, 6, -0.5, -6], dtype=torch.float32)
+    assert torch.equal(F.e2m1_decode(F.e2m1_encode(vals)), vals)
+    # ties go to the even code: 0.25->0, 0.75->1.0, 1.25->1.0, 1.75->2.0, 2.5->2, 3.5->4, 5->4
+    ties = torch.tensor([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0])
+    assert F.e2m1_decode(F.e2m1_encode(ties)).tolist() == [0.0, 1.0, 1.0, 2.0, 2.0, 4.0, 4.0]
+    assert F.e2m1_decode(F.e2m1_encode(torch.tensor([100.0, -7.0]))).tolist() == [6.0, -6.0]
+
+
+def test_ue8m0_ocp_rule():
+    # floor(log2 amax) - 2 + 127; zero block -> 0
+    amax = torch.tensor([6.0, 1.0, 0.75, 0.0, 2 ** -130])
+    b = F.ue8m0_ocp(amax)
+    assert b.tolist() == [127, 125, 124, 0, 0]
+
+
+def test_mxfp4_quant_error_and_packing():
+    torch.manual_seed(0)
+    w = torch.randn(64, 256)
+    packed, scales = F.mxfp4_quantize(w)
+    assert packed.shape == (64, 128) and scales.shape == (64, 8)
+    dq = F.mxfp4_dequantize(packed, scales)
+    rel = ((dq - w).norm() / w.norm()).item()
+    assert rel < 0.15, rel
+    # low nibble holds the even index
+    codes = F.unpack_nibbles(packed)
+    assert torch.equal(codes[:, 0], packed[:, 0] & 0xF)
+    assert torch.equal(F.pack_nibbles(codes), packed)
+
+
+def test_sf_tile_layout_roundtrip():
+    s = torch.randint(0, 255, (300, 20), dtype=torch.uint8)
+    t = F.sf_tile_layout(s)
+    assert t.numel() == 384 * 20
+    assert torch.equal(F.sf_tile_layout_inverse(t, 300, 20), s)
+    # byte (n%32)*16 + ((n%128)//32)*4 + kb%4 of atom (n//128, kb//4)
+    n, kb = 130, 9
+    atoms_k = 20 // 4
+    off = ((n // 128) * atoms_k + kb // 4) * 512 + (n % 32) * 16 + ((n % 128) // 32) * 4 + kb % 4
+    assert int(t[off]) == int(s[n, kb])
+
+
+def test_per_token_fp8():
+    x = torch.randn(5, 64) * 10
+    q, s = F.per_token_fp8(x)
+    assert q.dtype == torch.float8_e4m3fn
+    dq = F.per_token_fp8_dequant(q, s)
+    assert ((dq - x.to(torch.bfloat16).float()).abs().max() / x.abs().max()) < 0.07
+    z, sz = F.per_token_fp8(torch.zeros(2, 16))
+    assert torch.all(sz == F.FP8_SCALE_FLOOR)
+
+
+def test_nvfp4_requant_and_int4():
+    torch.manual_seed(1)
+    w = torch.randn(32, 128)
+    p, bs, gs = F.nvfp4_quantize(w)
+    mp, ms = F.nvfp4_to_mxfp4(p, bs, gs)
+    dq = F.mxfp4_dequantize(mp, ms)
+    assert ((dq - w).norm() / w.norm()) < 0.2
+    p4, sc, zp = F.int4_g128_quantize(w)
+    dq4 = F.int4_g128_dequantize(p4, sc, zp)
+    assert ((dq4 - w).norm() / w.norm()) < 0.15
+
+
+def test_mxfp4_weight_slicing():
+    w = torch.randn(256, 512)
+    mw = MXFP4Weight.from_float(w)
+    a = mw.narrow_rows(0, 128)
+    b = mw.narrow_rows(128, 128)
+    cat = cat_rows([a, b])
+    assert torch.equal(cat.packed, mw.packed) and torch.equal(cat.sf, mw.sf)
+    c = mw.narrow_cols(256, 256)
+    assert torch.equal(c.dequantize(), mw.dequantize()[:, 256:])

@@ -1,0 +1,114 @@
+"""Checkpoint loader: a synthetic Qwen3-Next-named safetensors checkpoint (bf16, MXFP4
+compressed-tensors, NVFP4) loads into the same model the canonical weights define."""
+import os
+
+import pytest
+import torch
+from safetensors.torch import save_file
+
+from vllm_sly_radiance_b200.config import tiny_hybrid
+from vllm_sly_radiance_b200.models.hybrid import HybridModel
+from vllm_sly_radiance_b200.models.weights import RandomWeights
+from vllm_sly_radiance_b200.quant import formats as F
+from vllm_sly_radiance_b200.quant.loaders import CheckpointWeights, gdn_in_proj_permutation
+
+
+class Recorder(RandomWeights):
+    """Random provider that remembers what it handed out (the canonical truth)."""
+
+    def __init__(self, cfg):
+        super().__init__(cfg, 0, "cpu")
+        self.lin, self.ten = {}, {}
+
+    def linear(self, name, N, K):
+        w = super().linear(name, N, K).to(torch.bfloat16).float()   # bf16-representable truth
+        self.lin[name] = w.clone()
+        return w
+
+    def tensor(self, name, shape, kind="norm"):
+        t = super().tensor(name, shape, kind)
+        self.ten[name] = t.clone()
+        return t
+
+
+def _write_hf(rec, cfg, path, fmt):
+    sd = {}
+
+    def put_linear(hf, w):
+        if fmt == "bf16":
+            sd[hf + ".weight"] = w.to(torch.bfloat16)
+        elif fmt == "mxfp4":
+            p, s = F.mxfp4_quantize(w)
+            sd[hf + ".weight_packed"] = p
+            sd[hf + ".weight_scale"] = s
+        elif fmt == "nvfp4":
+            p, bs, gs = F.nvfp4_quantize(w)
+            sd[hf + ".weight_packed"] = p
+            sd[hf + ".weight_scale"] = bs
+            sd[hf + ".weight_global_scale"] = (1.0 / gs).reshape(1)
+
+    sd["model.embed_tokens.weight"] = rec.ten["embed"]
+    sd["model.norm.weight"] = rec.ten["final_norm"]
+    put_linear("lm_head", rec.lin["lm_head"])
+    pq, pb = gdn_in_proj_permutation(cfg)
+    kd, vd, hv = cfg.gdn_key_dim, cfg.gdn_value_dim, cfg.gdn_num_v_heads
+    for i in range(cfg.num_layers):
+        L = f"model.layers.{i}."
+        c = f"layers.{i}."
+        sd[L + "input_layernorm.weight"] = rec.ten[c + "ln1"]
+        sd[L + "post_attention_layernorm.weight"] = rec.ten[c + "ln2"]
+        g = rec.lin[c + "gate_up"]
+        I = g.shape[0] // 2
+        put_linear(L + "mlp.gate_proj", g[:I])
+        put_linear(L + "mlp.up_proj", g[I:])
+        put_linear(L + "mlp.down_proj", rec.lin[c + "down"])
+        if cfg.is_attention_layer(i):
+            w = rec.lin[c + "qkv"]
+            qd = cfg.num_q_heads * cfg.head_dim * 2
+            kvd = cfg.num_kv_heads * cfg.head_dim
+            put_linear(L + "self_attn.q_proj", w[:qd])
+            put_linear(L + "self_attn.k_proj", w[qd:qd + kvd])
+            put_linear(L + "self_attn.v_proj", w[qd + kvd:])
+            put_linear(L + "self_attn.o_proj", rec.lin[c + "o_proj"])
+            sd[L + "self_attn.q_norm.weight"] = rec.ten[c + "q_norm"]
+            sd[L + "self_attn.k_norm.weight"] = rec.ten[c + "k_norm"]
+        else:
+            w = rec.lin[c + "in_proj"]
+            n_qkvz = 2 * kd + 2 * vd
+            hf_qkvz = torch.empty_like(w[:n_qkvz])
+            hf_qkvz[pq] = w[:n_qkvz]
+            hf_ba = torch.empty_like(w[n_qkvz:])
+            hf_ba[pb] = w[n_qkvz:]
+            put_linear(L + "linear_attn.in_proj_qkvz", hf_qkvz)
+            sd[L + "linear_attn.in_proj_ba.weight"] = hf_ba.to(torch.bfloat16)   # left unquantized
+            put_linear(L + "linear_attn.out_proj", rec.lin[c + "out_proj"])
+            sd[L + "linear_attn.conv1d.weight"] = rec.ten[c + "conv_w"].unsqueeze(1)
+            sd[L + "linear_attn.A_log"] = rec.ten[c + "A_log"]
+            sd[L + "linear_attn.dt_bias"] = rec.ten[c + "dt_bias"]
+            sd[L + "linear_attn.norm.weight"] = rec.ten[c + "norm_w"]
+    os.makedirs(path, exist_ok=True)
+    keys = sorted(sd)
+    half = len(keys) // 2       # two shards
+    save_file({k: sd[k].contiguous() for k in keys[:half]}, os.path.join(path, "model-00001.safetensors"))
+    save_file({k: sd[k].contiguous() for k in keys[half:]}, os.path.join(path, "model-00002.safetensors"))
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "mxfp4", "nvfp4"])
+def test_load_matches_canonical(tmp_path, fmt):
+    cfg = tiny_hybrid()
+    rec = Recorder(cfg)
+    ref_model = HybridModel(cfg, quant="mxfp4", device="cpu", weights=rec)
+    _write_hf(rec, cfg, str(tmp_path), fmt)
+    W = CheckpointWeights(str(tmp_path), cfg)
+    m = HybridModel(cfg, quant="mxfp4", device="cpu", weights=W)
+    l0, l1 = ref_model.layers[0], m.layers[0]
+    if fmt in ("bf16", "mxfp4"):
+        # MXFP4 from bf16 or from the packed checkpoint: bit-identical codes
+        assert torch.equal(l0.mixer.in_proj.w.packed, l1.mixer.in_proj.w.packed)
+        assert torch.equal(ref_model.layers[3].mixer.qkv.w.packed, m.layers[3].mixer.qkv.w.packed)
+    else:
+        a = l0.mixer.in_proj.w.dequantize()
+        b = l1.mixer.in_proj.w.dequantize()
+        assert ((a - b).norm() / a.norm()) < 0.2
+    assert torch.equal(l0.mixer.conv_w, l1.mixer.conv_w)
+    assert torch.equal(m.embed, ref_model.embed)

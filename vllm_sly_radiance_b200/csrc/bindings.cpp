@@ -1,6 +1,8 @@
 // Python bindings of the sm_100a kernel library.
 #include <torch/extension.h>
 
+#include <vector>
+
 namespace rad {
 void mxfp4_gemm(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
                 torch::Tensor out, int64_t splits_override, torch::Tensor status);
@@ -37,6 +39,14 @@ void sample_from_topk(torch::Tensor vals, torch::Tensor ids, torch::Tensor tempe
                       torch::Tensor top_k, torch::Tensor top_p, torch::Tensor min_p,
                       torch::Tensor seeds, int64_t step, torch::Tensor out,
                       torch::Tensor out_logprob, torch::Tensor probs_out);
+torch::Tensor ipc_handle(torch::Tensor buf);
+int64_t ipc_open(torch::Tensor handle);
+void ipc_close(int64_t ptr);
+int64_t symm_header_bytes();
+void allreduce_oneshot(std::vector<int64_t> peers, int64_t rank, torch::Tensor inp,
+                       int64_t slot_bytes, torch::Tensor out, torch::Tensor residual,
+                       torch::Tensor weight, double eps, torch::Tensor res_out, torch::Tensor q,
+                       torch::Tensor scale, int64_t num_blocks, torch::Tensor status);
 }  // namespace rad
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -52,6 +62,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_recurrent", &rad::gdn_recurrent, "GDN varlen recurrent delta rule");
   m.def("qkv_prologue", &rad::qkv_prologue, "QK RMSNorm + RoPE + paged KV write");
   m.def("paged_attention", &rad::paged_attention, "varlen paged attention (split-KV)");
+  m.def("ipc_handle", &rad::ipc_handle, "CUDA IPC handle of a device buffer");
+  m.def("ipc_open", &rad::ipc_open, "open a peer's IPC handle -> device pointer");
+  m.def("ipc_close", &rad::ipc_close, "close an opened IPC mapping");
+  m.def("symm_header_bytes", &rad::symm_header_bytes, "flag/counter header size of a symmetric buffer");
+  m.def("allreduce_oneshot", &rad::allreduce_oneshot, "one-shot NVLink all-reduce (+ fused add/RMSNorm/quant)");
   m.def("argmax_rows", &rad::argmax_rows, "greedy argmax per row");
   m.def("sample_from_topk", &rad::sample_from_topk, "temperature/top-k/top-p/min-p sampling");
 }

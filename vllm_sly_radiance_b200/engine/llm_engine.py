@@ -1,0 +1,157 @@
+"""LLMEngine: scheduler + KV/state cache manager + model runner (+ speculative decoding).
+
+API (vLLM-compatible subset): ``add_request``, ``abort_request``, ``step`` ->
+``list[RequestOutput]``, ``has_unfinished_requests``.  With tensor parallelism every rank runs
+the same engine on the same request stream (SPMD); rank 0 returns outputs.
+"""
+from __future__ import annotations
+
+import logging
+import time
+from typing import Optional, Union
+
+import torch
+
+from ..config import EngineConfig, ModelConfig
+from ..models.hybrid import HybridModel, TPInfo
+from ..utils.metrics import EngineMetrics
+from .kv_cache import KVCacheManager
+from .model_runner import ModelRunner
+from .request import CompletionOutput, Request, RequestOutput, SamplingParams
+from .scheduler import Scheduler
+from .tokenizer import IncrementalDetokenizer, get_tokenizer
+
+log = logging.getLogger("radiance.engine")
+
+
+class LLMEngine:
+    def __init__(self, config: EngineConfig, model: Optional[HybridModel] = None,
+                 tokenizer=None, tp: Optional[TPInfo] = None, tokenizer_path: Optional[str] = None):
+        self.config = config
+        self.device = torch.device(config.device if (config.device != "cuda" or torch.cuda.is_available()) else "cpu")
+        mcfg: ModelConfig = config.model_config()
+        self.model_config = mcfg
+        self.tp = tp or TPInfo()
+        t0 = time.time()
+        if model is None:
+            quant = config.quantization if config.gemm_backend == "native" else "fp8"
+            if quant == "nvfp4":
+                quant = "mxfp4"
+            model = HybridModel(mcfg, quant=quant, device=self.device, seed=config.seed, tp=self.tp)
+        self.model = model
+        self.load_time = time.time() - t0
+        self.tokenizer = tokenizer or get_tokenizer(tokenizer_path, mcfg.vocab_size)
+        self.eos_token_id = getattr(self.tokenizer, "eos_token_id", None)
+        # ---- cache sizing ----
+        bs = config.block_size
+        num_slots = config.max_num_seqs + 2
+        if config.num_kv_blocks:
+            num_blocks = config.num_kv_blocks
+        elif self.device.type == "cuda":
+            torch.cuda.synchronize()
+            free, total = torch.cuda.mem_get_info(self.device)
+            per_block = max(1, model.cache_bytes_per_block(bs, config.kv_cache_dtype))
+            state = model.state_bytes_per_slot(config.ssm_state_dtype) * num_slots
+            activ = 4 << 30   # activations / graphs headroom
+            budget = int(free - (1 - config.gpu_memory_utilization) * total) - state - activ
+            need = (config.max_model_len + bs - 1) // bs * config.max_num_seqs + 1
+            num_blocks = max(8, min(budget // per_block, need * 4))
+        else:
+            num_blocks = (config.max_model_len + bs - 1) // bs * config.max_num_seqs + 1
+        self.num_blocks = int(num_blocks)
+        self.caches = model.make_caches(self.num_blocks, bs, num_slots, config.kv_cache_dtype,
+                                        config.ssm_state_dtype)
+        self.kv = KVCacheManager(self.num_blocks, bs, num_slots, config.enable_prefix_caching)
+        k = config.num_speculative_tokens if config.speculative_method else 0
+        self.scheduler = Scheduler(self.kv, config.max_num_seqs, config.max_num_batched_tokens,
+                                   config.max_model_len, num_spec_tokens=k)
+        self.runner = ModelRunner(model, self.caches, max_num_seqs=config.max_num_seqs,
+                                  max_num_tokens=config.max_num_batched_tokens,
+                                  max_model_len=config.max_model_len, device=self.device,
+                                  enable_graphs=config.enable_cuda_graphs,
+                                  graph_max_bs=config.cuda_graph_max_bs, num_spec_tokens=k)
+        self.spec = None
+        if config.speculative_method:
+            from ..spec_decode.proposer import build_proposer
+            self.spec = build_proposer(config, self)
+        self.requests: dict[str, Request] = {}
+        self.detok: dict[str, IncrementalDetokenizer] = {}
+        self.metrics = EngineMetrics()
+        self.kv_tokens_capacity = self.num_blocks * bs
+        log.info("engine ready: %d KV blocks (%d tokens), %d state slots, load %.1fs",
+                 self.num_blocks, self.kv_tokens_capacity, num_slots, self.load_time)
+
+    # ------------------------------------------------------------------------------------------
+    def add_request(self, prompt: Union[str, list[int]], params: Optional[SamplingParams] = None,
+                    request_id: Optional[str] = None) -> str:
+        params = params or SamplingParams()
+        ids = self.tokenizer.encode(prompt) if isinstance(prompt, str) else list(prompt)
+        req = Request(ids, params, request_id, eos_token_id=self.eos_token_id)
+        self.scheduler.add(req)
+        self.requests[req.request_id] = req
+        self.detok[req.request_id] = IncrementalDetokenizer(self.tokenizer, params.stop)
+        self.metrics.on_arrival()
+        return req.request_id
+
+    def abort_request(self, request_id: str) -> bool:
+        ok = self.scheduler.abort(request_id)
+        self.requests.pop(request_id, None)
+        self.detok.pop(request_id, None)
+        return ok
+
+    def has_unfinished_requests(self) -> bool:
+        return self.scheduler.has_unfinished()
+
+    # ------------------------------------------------------------------------------------------
+    def step(self) -> list[RequestOutput]:
+        t0 = time.perf_counter()
+        sched = self.scheduler.schedule()
+        if sched.is_empty:
+            return []
+        if self.spec is not None:
+            result = self.spec.execute(sched)
+        else:
+            result = self.runner.execute(sched)
+        finished = self.scheduler.update(sched, result.sampled)
+        self.metrics.on_step(sched, result, time.perf_counter() - t0, self.kv.usage,
+                             len(self.scheduler.running), len(self.scheduler.waiting))
+        outs = []
+        fin_ids = {r.request_id for r in finished}
+        for s in sched.seqs:
+            req = s.req
+            rid = req.request_id
+            if rid not in result.sampled and rid not in fin_ids:
+                continue
+            det = self.detok.get(rid)
+            if det is not None:
+                det.update(req.output_token_ids)
+                if det.stopped and not req.status.finished:
+                    self.scheduler.abort(rid)
+                    from .request import RequestStatus
+                    req.status = RequestStatus.FINISHED_STOPPED
+                    fin_ids.add(rid)
+            done = req.status.finished
+            text = det.text if det else ""
+            outs.append(RequestOutput(
+                request_id=rid, prompt_token_ids=req.prompt_token_ids,
+                outputs=[CompletionOutput(0, text, list(req.output_token_ids),
+                                          req.status.value if done else None)],
+                finished=done,
+                metrics=dict(arrival=req.arrival_time, first_token=req.first_token_time,
+                             finish=req.finish_time, num_preemptions=req.num_preemptions)))
+            if done:
+                self.metrics.on_finish(req)
+                self.requests.pop(rid, None)
+                self.detok.pop(rid, None)
+        return outs
+
+    def generate(self, prompts, params=None) -> list[RequestOutput]:
+        if isinstance(params, SamplingParams) or params is None:
+            params = [params or SamplingParams()] * len(prompts)
+        order = [self.add_request(p, sp) for p, sp in zip(prompts, params)]
+        final = {}
+        while self.has_unfinished_requests():
+            for o in self.step():
+                if o.finished:
+                    final[o.request_id] = o
+        return [final[r] for r in order]

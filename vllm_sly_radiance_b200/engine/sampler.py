@@ -32,10 +32,16 @@ class SamplingTensors:
         k = torch.tensor([r.params.top_k for r in reqs], dtype=torch.int32)
         p = torch.tensor([r.params.top_p for r in reqs], dtype=torch.float32)
         mp = torch.tensor([r.params.min_p for r in reqs], dtype=torch.float32)
-        sd = torch.tensor([r.seed for r in reqs], dtype=torch.int64)
+        # per-row Philox stream: request seed folded with the request's own token position, so a
+        # seeded request reproduces regardless of what else shares its batch
+        sd = torch.tensor([row_seed(r) for r in reqs], dtype=torch.int64)
         greedy = all(r.params.greedy for r in reqs)
         return SamplingTensors(t.to(device), k.to(device), p.to(device), mp.to(device),
                                sd.to(device), greedy, bool((mp > 0).any()))
+
+
+def row_seed(req, offset: int = 0) -> int:
+    return (req.seed * 1000003 + len(req.output_token_ids) + offset) & 0x7FFFFFFFFFFF
 
 
 def apply_penalties(logits: torch.Tensor, reqs) -> torch.Tensor:

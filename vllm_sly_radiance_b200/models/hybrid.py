@@ -26,7 +26,9 @@ import torch
 
 from ..config import ModelConfig
 from ..ops import kernels as K
+from ..quant.mxfp4 import MXFP4Weight
 from .layers import Linear, rope_cache
+from .weights import RandomWeights, cat_rows, slice_cols, slice_rows
 
 
 # ---------------------------------------------------------------------------------------------
@@ -98,21 +100,29 @@ class TPInfo:
         return self.rank * per, per
 
 
-def _cat_sections(w: torch.Tensor, sections: list[int], tp: TPInfo) -> torch.Tensor:
+def _cat_sections(w, sections: list[int], tp: TPInfo):
     """Column-parallel slice of a merged weight made of `sections` along dim 0."""
     parts, off = [], 0
     for n in sections:
         s0, per = tp.shard(n)
-        parts.append(w[off + s0: off + s0 + per])
+        parts.append(slice_rows(w, off + s0, per))
         off += n
-    return torch.cat(parts, 0)
+    return cat_rows(parts) if len(parts) > 1 else parts[0]
+
+
+def make_linear(w, quant: str, name: str) -> Linear:
+    if isinstance(w, MXFP4Weight):
+        if quant != "mxfp4":
+            return Linear(w.dequantize().to(torch.bfloat16), quant, name)
+        return Linear.from_mxfp4(w, name)
+    return Linear(w, quant, name)
 
 
 # ---------------------------------------------------------------------------------------------
 # layers
 # ---------------------------------------------------------------------------------------------
 class GDNMixer:
-    def __init__(self, cfg: ModelConfig, tp: TPInfo, quant: str, gen: torch.Generator, device):
+    def __init__(self, cfg: ModelConfig, tp: TPInfo, quant: str, W, prefix: str):
         self.cfg = cfg
         self.tp = tp
         H = cfg.hidden_size
@@ -122,27 +132,24 @@ class GDNMixer:
         self.key_dim = self.Hk * self.dk
         self.value_dim = self.Hv * self.dv
         self.conv_dim = 2 * self.key_dim + self.value_dim
-        std = cfg.init_std
         kd, vd, hv = cfg.gdn_key_dim, cfg.gdn_value_dim, cfg.gdn_num_v_heads
-        w_in = torch.randn(cfg.gdn_in_proj_dim, H, generator=gen, device=device) * std
-        w_in = _cat_sections(w_in, [kd, kd, vd, vd, hv, hv], tp)
-        self.in_proj = Linear(w_in, quant, "in_proj")
+        w_in = W.linear(prefix + "in_proj", cfg.gdn_in_proj_dim, H)
+        self.in_proj = make_linear(_cat_sections(w_in, [kd, kd, vd, vd, hv, hv], tp), quant, "in_proj")
         del w_in
-        conv = (torch.rand(cfg.gdn_conv_dim, cfg.gdn_conv_kernel, generator=gen, device=device) - 0.5)
+        conv = W.tensor(prefix + "conv_w", (cfg.gdn_conv_dim, cfg.gdn_conv_kernel), "conv")
         self.conv_w = _cat_sections(conv, [kd, kd, vd], tp).to(torch.bfloat16).contiguous()
-        A = torch.rand(hv, generator=gen, device=device) * 15 + 1
-        self.A_log = torch.log(A).float()[tp.shard(hv)[0]: tp.shard(hv)[0] + self.Hv].contiguous()
-        dtb = torch.randn(hv, generator=gen, device=device) * 0.1
-        self.dt_bias = dtb.float()[tp.shard(hv)[0]: tp.shard(hv)[0] + self.Hv].contiguous()
-        self.norm_w = (1 + 0.02 * torch.randn(self.dv, generator=gen, device=device)).to(torch.bfloat16)
-        w_out = torch.randn(H, vd, generator=gen, device=device) * std
+        h0, _ = tp.shard(hv)
+        self.A_log = W.tensor(prefix + "A_log", (hv,), "A_log").float()[h0:h0 + self.Hv].contiguous()
+        self.dt_bias = W.tensor(prefix + "dt_bias", (hv,), "dt_bias").float()[h0:h0 + self.Hv].contiguous()
+        self.norm_w = W.tensor(prefix + "norm_w", (self.dv,), "norm_plain").to(torch.bfloat16)
+        w_out = W.linear(prefix + "out_proj", H, vd)
         s0, per = tp.shard(vd)
-        self.out_proj = Linear(w_out[:, s0:s0 + per].contiguous(), quant, "out_proj")
+        self.out_proj = make_linear(slice_cols(w_out, s0, per), quant, "out_proj")
         del w_out
         self.quant = quant
         self.scale = self.dk ** -0.5
 
-    def forward(self, x, meta: StepMeta, conv_state, ssm_state):
+    def forward(self, x, meta: StepMeta, conv_state, ssm_state, save=None):
         cfg = self.cfg
         proj = self.in_proj(x)                                    # [T, in_proj_local]
         cd, vd = self.conv_dim, self.value_dim
@@ -153,22 +160,32 @@ class GDNMixer:
         K.gdn_conv_state_update(xc, conv_state, meta, meta.commit_len)
         o = K.gdn_recurrent(y, ba, self.A_log, self.dt_bias, ssm_state, meta, self.Hk, self.scale,
                             commit_len=meta.commit_len)
+        if save is not None:        # speculative verify: keep inputs for the commit pass
+            save.append((proj, y))
         if self.quant == "bf16":
             h = self.out_proj(K.gdn_gated_norm(o, z, self.norm_w, cfg.rms_norm_eps, self.dv))
         else:
             h = self.out_proj(K.gdn_norm_quant(o, z, self.norm_w, cfg.rms_norm_eps, self.dv))
         return h
 
+    def commit(self, saved, meta: StepMeta, conv_state, ssm_state, commit_len):
+        """Apply the first commit_len[b] tokens of a verified block to the conv / SSM state."""
+        proj, y = saved
+        cd, vd = self.conv_dim, self.value_dim
+        K.gdn_conv_state_update(proj[:, :cd], conv_state, meta, commit_len)
+        K.gdn_recurrent(y, proj[:, cd + vd:], self.A_log, self.dt_bias, ssm_state, meta, self.Hk,
+                        self.scale, commit_len=commit_len, write_out=False)
+
 
 class AttentionMixer:
-    def __init__(self, cfg: ModelConfig, tp: TPInfo, quant: str, gen: torch.Generator, device):
+    def __init__(self, cfg: ModelConfig, tp: TPInfo, quant: str, W, prefix: str):
         self.cfg = cfg
         self.tp = tp
         H = cfg.hidden_size
         hd = cfg.head_dim
         self.hd = hd
         self.Hq = cfg.num_q_heads // tp.size
-        # kv heads: sharded when divisible, else replicated (one kv head per group of ranks)
+        # kv heads: sharded when divisible, else replicated (each rank keeps its group's head)
         if cfg.num_kv_heads % tp.size == 0:
             self.Hkv = cfg.num_kv_heads // tp.size
             kv_sel = [tp.rank * self.Hkv + i for i in range(self.Hkv)]
@@ -176,21 +193,21 @@ class AttentionMixer:
             assert tp.size % cfg.num_kv_heads == 0
             self.Hkv = 1
             kv_sel = [tp.rank * cfg.num_kv_heads // tp.size]
-        std = cfg.init_std
         gated = cfg.attn_output_gate
         qd = cfg.num_q_heads * hd * (2 if gated else 1)
-        w = torch.randn(cfg.qkv_proj_dim, H, generator=gen, device=device) * std
+        w = W.linear(prefix + "qkv", cfg.qkv_proj_dim, H)
         s0, per = tp.shard(qd)
         kvd = cfg.num_kv_heads * hd
-        k_rows = torch.cat([w[qd + h * hd: qd + (h + 1) * hd] for h in kv_sel])
-        v_rows = torch.cat([w[qd + kvd + h * hd: qd + kvd + (h + 1) * hd] for h in kv_sel])
-        self.qkv = Linear(torch.cat([w[s0:s0 + per], k_rows, v_rows]), quant, "qkv")
-        del w
-        self.q_norm = (0.02 * torch.randn(hd, generator=gen, device=device)).to(torch.bfloat16)
-        self.k_norm = (0.02 * torch.randn(hd, generator=gen, device=device)).to(torch.bfloat16)
-        w_o = torch.randn(H, cfg.num_q_heads * hd, generator=gen, device=device) * std
+        rows = [slice_rows(w, s0, per)]
+        rows += [slice_rows(w, qd + h * hd, hd) for h in kv_sel]
+        rows += [slice_rows(w, qd + kvd + h * hd, hd) for h in kv_sel]
+        self.qkv = make_linear(cat_rows(rows), quant, "qkv")
+        del w, rows
+        self.q_norm = W.tensor(prefix + "q_norm", (hd,), "norm")
+        self.k_norm = W.tensor(prefix + "k_norm", (hd,), "norm")
+        w_o = W.linear(prefix + "o_proj", H, cfg.num_q_heads * hd)
         s0, per = tp.shard(cfg.num_q_heads * hd)
-        self.o_proj = Linear(w_o[:, s0:s0 + per].contiguous(), quant, "o_proj")
+        self.o_proj = make_linear(slice_cols(w_o, s0, per), quant, "o_proj")
         del w_o
         self.quant = quant
         self.gated = gated
@@ -217,48 +234,42 @@ class AttentionMixer:
 
 
 class MLP:
-    def __init__(self, cfg: ModelConfig, tp: TPInfo, quant: str, gen: torch.Generator, device,
+    def __init__(self, cfg: ModelConfig, tp: TPInfo, quant: str, W, prefix: str,
                  inter: Optional[int] = None):
         H = cfg.hidden_size
         I = inter or cfg.intermediate_size
-        std = cfg.init_std
-        w = torch.randn(2 * I, H, generator=gen, device=device) * std
-        self.gate_up = Linear(_cat_sections(w, [I, I], tp), quant, "gate_up")
+        w = W.linear(prefix + "gate_up", 2 * I, H)
+        self.gate_up = make_linear(_cat_sections(w, [I, I], tp), quant, "gate_up")
         del w
-        w = torch.randn(H, I, generator=gen, device=device) * std
+        w = W.linear(prefix + "down", H, I)
         s0, per = tp.shard(I)
-        self.down = Linear(w[:, s0:s0 + per].contiguous(), quant, "down")
+        self.down = make_linear(slice_cols(w, s0, per), quant, "down")
         del w
         self.quant = quant
 
     def forward(self, x):
         gu = self.gate_up(x)
         if self.quant == "bf16":
-            from ..ops import reference as ref
-            return self.down(ref.silu_mul(gu) if not gu.is_cuda else _silu_mul_cuda(gu))
+            return self.down(K.silu_mul(gu))
         return self.down(K.silu_mul_quant(gu))
 
 
-def _silu_mul_cuda(gu):
-    q, s = K.silu_mul_quant(gu)
-    return (q.float() * s[:, None]).to(torch.bfloat16)
-
-
 class DecoderLayer:
-    def __init__(self, cfg, idx, tp, quant, gen, device):
+    def __init__(self, cfg, idx, tp, quant, W):
         self.idx = idx
+        p = f"layers.{idx}."
         self.is_attn = cfg.is_attention_layer(idx)
-        self.ln1 = (0.02 * torch.randn(cfg.hidden_size, generator=gen, device=device)).to(torch.bfloat16)
-        self.ln2 = (0.02 * torch.randn(cfg.hidden_size, generator=gen, device=device)).to(torch.bfloat16)
+        self.ln1 = W.tensor(p + "ln1", (cfg.hidden_size,), "norm")
+        self.ln2 = W.tensor(p + "ln2", (cfg.hidden_size,), "norm")
         if self.is_attn:
-            self.mixer = AttentionMixer(cfg, tp, quant, gen, device)
+            self.mixer = AttentionMixer(cfg, tp, quant, W, p)
         else:
-            self.mixer = GDNMixer(cfg, tp, quant, gen, device)
+            self.mixer = GDNMixer(cfg, tp, quant, W, p)
         if cfg.is_moe:
             from .moe import MoEBlock
-            self.mlp = MoEBlock(cfg, tp, quant, gen, device)
+            self.mlp = MoEBlock(cfg, tp, quant, W, p)
         else:
-            self.mlp = MLP(cfg, tp, quant, gen, device)
+            self.mlp = MLP(cfg, tp, quant, W, p)
 
 
 class HybridModel:
@@ -266,27 +277,24 @@ class HybridModel:
     quantized to MXFP4 at load when quant == 'mxfp4'."""
 
     def __init__(self, cfg: ModelConfig, quant: str = "mxfp4", device="cpu", seed: int = 0,
-                 tp: Optional[TPInfo] = None, init_device=None):
+                 tp: Optional[TPInfo] = None, init_device=None, weights=None):
         self.cfg = cfg
         self.quant = quant
         self.device = torch.device(device)
         self.tp = tp or TPInfo()
         init_dev = torch.device(init_device) if init_device is not None else self.device
-        gen = torch.Generator(device=init_dev)
-        gen.manual_seed(seed)
+        W = weights if weights is not None else RandomWeights(cfg, seed, init_dev)
         H, V = cfg.hidden_size, cfg.vocab_size
-        self.embed = (torch.randn(V, H, generator=gen, device=init_dev) * cfg.init_std).to(torch.bfloat16)
-        self.layers = []
-        for i in range(cfg.num_layers):
-            self.layers.append(DecoderLayer(cfg, i, self.tp, quant, gen, init_dev))
-        self.final_norm = (0.02 * torch.randn(H, generator=gen, device=init_dev)).to(torch.bfloat16)
+        self.embed = W.tensor("embed", (V, H), "embed").to(torch.bfloat16)
+        self.layers = [DecoderLayer(cfg, i, self.tp, quant, W) for i in range(cfg.num_layers)]
+        self.final_norm = W.tensor("final_norm", (H,), "norm")
         # vocab-parallel lm_head
-        w = torch.randn(V, H, generator=gen, device=init_dev) * cfg.init_std
+        w = W.linear("lm_head", V, H) if not cfg.tie_word_embeddings else self.embed.float()
         s0, per = self.tp.shard(V)
         self.vocab_start = s0
-        self.lm_head = Linear(w[s0:s0 + per].contiguous(), quant if quant != "bf16" else "bf16", "lm_head")
+        self.lm_head = make_linear(slice_rows(w, s0, per), quant, "lm_head")
         del w
-        if init_dev != self.device:
+        if init_dev != self.device or getattr(W, "device", self.device) != self.device:
             self.to(self.device)
         self._init_rope()
 

@@ -1,0 +1,80 @@
+"""Weight providers: random init (benchmarks, tests) or checkpoints (``quant/loaders.py``).
+
+The model asks for tensors by canonical name, always in this engine's layout (full, unsharded):
+
+  embed [V,H]  lm_head [V,H]  final_norm [H]
+  layers.{i}.ln1 / ln2 [H]
+  GDN  : in_proj [2kd+2vd+2Hv, H] as [q|k|v|z|b|a],  conv_w [2kd+vd, W],  A_log [Hv],
+         dt_bias [Hv],  norm_w [dv],  out_proj [H, vd]
+  ATTN : qkv [Hq*2hd + 2Hkv*hd, H] as [q0,gate0,q1,gate1,...|k|v],  q_norm/k_norm [hd],
+         o_proj [H, Hq*hd]
+  MLP  : gate_up [2I, H] as [gate|up],  down [H, I]
+  MoE  : router [E, H],  experts.{e}.gate_up / down,  shared.gate_up / down,  shared_gate [1, H]
+
+Linear weights come back either as float tensors (quantized by the model at load) or as
+``MXFP4Weight`` (pre-quantized checkpoints)."""
+from __future__ import annotations
+
+from typing import Optional, Union
+
+import torch
+
+from ..config import ModelConfig
+from ..quant.mxfp4 import MXFP4Weight
+
+WeightT = Union[torch.Tensor, MXFP4Weight]
+
+
+class RandomWeights:
+    """N(0, init_std) linears, small-noise norms, GDN gate parameters in their usual ranges."""
+
+    def __init__(self, cfg: ModelConfig, seed: int, device):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.gen = torch.Generator(device=self.device)
+        self.gen.manual_seed(seed)
+
+    def linear(self, name: str, N: int, K: int) -> WeightT:
+        return torch.randn(N, K, generator=self.gen, device=self.device) * self.cfg.init_std
+
+    def tensor(self, name: str, shape, kind: str = "norm") -> torch.Tensor:
+        g, d = self.gen, self.device
+        if kind == "norm":             # Gemma (1+w) norms
+            return (0.02 * torch.randn(*shape, generator=g, device=d)).to(torch.bfloat16)
+        if kind == "norm_plain":       # plain-weight norm (GDN gated norm)
+            return (1 + 0.02 * torch.randn(*shape, generator=g, device=d)).to(torch.bfloat16)
+        if kind == "conv":
+            return (torch.rand(*shape, generator=g, device=d) - 0.5).to(torch.bfloat16)
+        if kind == "A_log":
+            return torch.log(torch.rand(*shape, generator=g, device=d) * 15 + 1).float()
+        if kind == "dt_bias":
+            return (0.1 * torch.randn(*shape, generator=g, device=d)).float()
+        if kind == "embed":
+            return (torch.randn(*shape, generator=g, device=d) * self.cfg.init_std).to(torch.bfloat16)
+        if kind == "codebook":
+            return (torch.randn(*shape, generator=g, device=d) * 0.1).to(torch.bfloat16)
+        if kind == "linear_bf16":
+            return (torch.randn(*shape, generator=g, device=d) * self.cfg.init_std).to(torch.bfloat16)
+        raise ValueError(kind)
+
+    def has(self, name: str) -> bool:
+        return True
+
+
+def slice_rows(w: WeightT, start: int, length: int) -> WeightT:
+    if isinstance(w, MXFP4Weight):
+        return w.narrow_rows(start, length)
+    return w[start:start + length]
+
+
+def slice_cols(w: WeightT, start: int, length: int) -> WeightT:
+    if isinstance(w, MXFP4Weight):
+        return w.narrow_cols(start, length)
+    return w[:, start:start + length].contiguous()
+
+
+def cat_rows(ws: list) -> WeightT:
+    if isinstance(ws[0], MXFP4Weight):
+        from ..quant.mxfp4 import cat_rows as cr
+        return cr(ws)
+    return torch.cat(ws, 0)

@@ -90,6 +90,16 @@ def silu_mul_quant(gate_up: torch.Tensor):
     return q, s
 
 
+def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
+    """bf16 silu(gate)*up (unquantized reference model path only; the W4A8 hot path uses
+    silu_mul_quant)."""
+    if not gate_up.is_cuda:
+        return ref.silu_mul(gate_up)
+    I = gate_up.shape[1] // 2
+    g = gate_up[:, :I].float()
+    return (g * torch.sigmoid(g) * gate_up[:, I:].float()).to(torch.bfloat16)
+
+
 def gdn_norm_quant(o: torch.Tensor, z: torch.Tensor, weight: torch.Tensor, eps: float,
                    head_dim: int):
     if not o.is_cuda:

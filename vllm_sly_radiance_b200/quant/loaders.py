@@ -1,0 +1,218 @@
+"""Checkpoint loading (safetensors, sharded), mapped onto the engine's canonical weight layout.
+
+Supported per-linear formats (auto-detected from the tensor names next to each weight):
+  * bf16 / fp16 / fp32                 ``{p}.weight``                      -> quantized at load
+  * MXFP4, compressed-tensors          ``{p}.weight_packed`` u8 [N,K/2] + ``{p}.weight_scale`` u8 [N,K/32]
+  * MXFP4, Quark                       ``{p}.weight`` u8 [N,K/2] + ``{p}.weight_scale`` u8 [N,K/32]
+  * NVFP4 (compressed-tensors/modelopt) ``weight_packed`` + e4m3 ``weight_scale`` [N,K/16] +
+                                       ``weight_global_scale`` (divisor) or ``weight_scale_2``
+                                       (multiplier) -> requantized to MXFP4 (``radiance_nvfp4.py``
+                                       'ocp' exponent mode)
+  * INT4 W4A16 g128 (compressed-tensors pack-quantized) ``weight_packed`` i32 [N,K/8] +
+                                       ``weight_scale`` [N,K/g] (+ ``weight_zero_point``)
+                                       -> dequantized, then MXFP4 for the W4A8 path
+
+Qwen3-Next naming (HF) and the layout transforms (reference loader behaviour:
+``sly/mxfp4/radiance_mxfp4.py:1006-1120``, GDN in_proj merge ``radiance_gdnmerge.py:30-35``):
+  * GDN ``in_proj_qkvz`` is grouped per key head ([q_g, k_g, v_g*, z_g*]) and ``in_proj_ba`` per
+    key head ([b_g*, a_g*]); both are permuted into the merged [q|k|v|z|b|a] order.
+  * attention ``q_proj`` (query+gate interleaved per head), ``k_proj``, ``v_proj`` -> ``qkv``.
+  * ``gate_proj`` + ``up_proj`` -> ``gate_up``.
+Shards are read tensor by tensor (peak host memory = one tensor, not one shard;
+``docs/TECHNICAL.md:773-825``).
+"""
+from __future__ import annotations
+
+import glob
+import json
+import os
+from typing import Optional
+
+import torch
+
+from ..config import ModelConfig
+from .formats import (int4_g128_dequantize, mxfp4_quantize, nvfp4_to_mxfp4, unpack_nibbles)
+from .mxfp4 import MXFP4Weight
+
+
+class CheckpointWeights:
+    def __init__(self, path: str, cfg: ModelConfig, device="cpu", prefix: str = "model."):
+        from safetensors import safe_open
+        self.cfg = cfg
+        self.device = torch.device(device)
+        files = sorted(glob.glob(os.path.join(path, "*.safetensors")))
+        if not files:
+            raise FileNotFoundError(f"no .safetensors files under {path}")
+        self.index: dict[str, str] = {}
+        self._open = {}
+        for f in files:
+            h = safe_open(f, framework="pt", device="cpu")
+            self._open[f] = h
+            for k in h.keys():
+                self.index[k] = f
+        self.prefix = prefix if any(k.startswith(prefix) for k in self.index) else ""
+        qc = os.path.join(path, "config.json")
+        self.hf_config = json.load(open(qc)) if os.path.exists(qc) else {}
+
+    # ---- raw access ----
+    def has(self, key: str) -> bool:
+        return key in self.index
+
+    def raw(self, key: str) -> torch.Tensor:
+        return self._open[self.index[key]].get_tensor(key)
+
+    def _hf(self, name: str) -> str:
+        return self.prefix + name
+
+    def _linear_any(self, hf_name: str):
+        """Read one HF linear in whatever format it is stored: float tensor or MXFP4Weight."""
+        p = hf_name
+        if self.has(p + ".weight_packed") or (self.has(p + ".weight") and self.has(p + ".weight_scale")
+                                              and self.raw(p + ".weight").dtype == torch.uint8):
+            packed = self.raw(p + ".weight_packed") if self.has(p + ".weight_packed") else self.raw(p + ".weight")
+            scale = self.raw(p + ".weight_scale")
+            if packed.dtype == torch.int32:                     # int4 pack-quantized (8 per int32)
+                N = packed.shape[0]
+                b = packed.contiguous().view(torch.uint8).view(N, -1)
+                K = b.shape[1] * 2
+                g = K // scale.shape[1]
+                if self.has(p + ".weight_zero_point"):
+                    zp = self.raw(p + ".weight_zero_point")
+                    zp = zp.view(torch.uint8) if zp.dtype == torch.int32 else zp
+                    zp = unpack_nibbles(zp.view(N, -1))[:, :K // g] if zp.dtype == torch.uint8 and zp.shape[1] * 2 == K // g else zp
+                else:
+                    zp = torch.full((N, K // g), 8, dtype=torch.uint8)
+                w = int4_g128_dequantize(b, scale.float(), zp.to(torch.uint8), g)
+                return w
+            if scale.dtype == torch.uint8:                      # MXFP4 (UE8M0 per 32)
+                return MXFP4Weight.from_packed(packed.contiguous(), scale.contiguous())
+            if scale.dtype == torch.float8_e4m3fn:             # NVFP4
+                if self.has(p + ".weight_global_scale"):
+                    gs = 1.0 / self.raw(p + ".weight_global_scale").float()
+                elif self.has(p + ".weight_scale_2"):
+                    gs = self.raw(p + ".weight_scale_2").float()
+                else:
+                    gs = torch.tensor(1.0)
+                mp, ms = nvfp4_to_mxfp4(packed.contiguous(), scale, gs.reshape(()))
+                return MXFP4Weight.from_packed(mp, ms)
+            raise ValueError(f"unsupported quantized format for {p}: scale dtype {scale.dtype}")
+        return self.raw(p + ".weight").float()
+
+    # ---- provider interface ----
+    def linear(self, name: str, N: int, K: int):
+        cfg = self.cfg
+        parts = name.split(".")
+        if name == "lm_head":
+            return self._linear_any("lm_head")
+        i = int(parts[1])
+        leaf = parts[2]
+        L = f"layers.{i}."
+        if leaf == "in_proj":
+            qkvz = self._linear_any(self._hf(L + "linear_attn.in_proj_qkvz"))
+            ba = self._linear_any(self._hf(L + "linear_attn.in_proj_ba"))
+            return _merge_gdn_in_proj(qkvz, ba, cfg)
+        if leaf == "out_proj":
+            return self._linear_any(self._hf(L + "linear_attn.out_proj"))
+        if leaf == "qkv":
+            qs = [self._linear_any(self._hf(L + f"self_attn.{n}_proj")) for n in ("q", "k", "v")]
+            return _cat(qs)
+        if leaf == "o_proj":
+            return self._linear_any(self._hf(L + "self_attn.o_proj"))
+        if leaf == "gate_up":
+            return _cat([self._linear_any(self._hf(L + "mlp.gate_proj")),
+                         self._linear_any(self._hf(L + "mlp.up_proj"))])
+        if leaf == "down":
+            return self._linear_any(self._hf(L + "mlp.down_proj"))
+        if leaf == "experts":
+            e = int(parts[3])
+            kind = parts[4]
+            base = L + f"mlp.experts.{e}."
+            if kind == "gate_up":
+                return _cat([self._linear_any(self._hf(base + "gate_proj")),
+                             self._linear_any(self._hf(base + "up_proj"))])
+            return self._linear_any(self._hf(base + "down_proj"))
+        if leaf == "shared":
+            base = L + "mlp.shared_expert."
+            if parts[3] == "gate_up":
+                return _cat([self._linear_any(self._hf(base + "gate_proj")),
+                             self._linear_any(self._hf(base + "up_proj"))])
+            return self._linear_any(self._hf(base + "down_proj"))
+        raise KeyError(name)
+
+    def tensor(self, name: str, shape, kind: str = "norm") -> torch.Tensor:
+        parts = name.split(".")
+        if name == "embed":
+            return self.raw(self._hf("embed_tokens.weight")).to(torch.bfloat16)
+        if name == "final_norm":
+            return self.raw(self._hf("norm.weight")).to(torch.bfloat16)
+        i = int(parts[1])
+        leaf = parts[2]
+        L = f"layers.{i}."
+        m = {"ln1": "input_layernorm.weight", "ln2": "post_attention_layernorm.weight",
+             "q_norm": "self_attn.q_norm.weight", "k_norm": "self_attn.k_norm.weight",
+             "A_log": "linear_attn.A_log", "dt_bias": "linear_attn.dt_bias",
+             "norm_w": "linear_attn.norm.weight", "router": "mlp.gate.weight",
+             "shared_gate": "mlp.shared_expert_gate.weight"}
+        if leaf == "conv_w":
+            w = self.raw(self._hf(L + "linear_attn.conv1d.weight"))
+            return w.reshape(w.shape[0], -1).to(torch.bfloat16)
+        t = self.raw(self._hf(L + m[leaf]))
+        if leaf in ("A_log", "dt_bias", "router", "shared_gate"):
+            return t.float()
+        return t.to(torch.bfloat16)
+
+
+def _cat(ws):
+    if isinstance(ws[0], MXFP4Weight):
+        from .mxfp4 import cat_rows
+        return cat_rows(ws)
+    return torch.cat(ws, 0)
+
+
+def _rows(w, idx: torch.Tensor):
+    if isinstance(w, MXFP4Weight):
+        return MXFP4Weight.from_packed(w.packed[idx], w.scales[idx])
+    return w[idx]
+
+
+def gdn_in_proj_permutation(cfg: ModelConfig) -> tuple[torch.Tensor, torch.Tensor]:
+    """Row indices taking HF's per-key-head grouped [q_g,k_g,v_g,z_g] (qkvz) and [b_g,a_g] (ba)
+    layouts to the merged canonical [q|k|v|z] and [b|a] orders."""
+    Hk, Hv = cfg.gdn_num_k_heads, cfg.gdn_num_v_heads
+    dk, dv = cfg.gdn_head_k_dim, cfg.gdn_head_v_dim
+    rep = Hv // Hk
+    gsz = 2 * dk + 2 * rep * dv
+    q, k, v, z = [], [], [], []
+    for g in range(Hk):
+        base = g * gsz
+        q += range(base, base + dk)
+        k += range(base + dk, base + 2 * dk)
+        v += range(base + 2 * dk, base + 2 * dk + rep * dv)
+        z += range(base + 2 * dk + rep * dv, base + gsz)
+    qkvz = torch.tensor(q + k + v + z, dtype=torch.long)
+    b, a = [], []
+    for g in range(Hk):
+        b += range(g * 2 * rep, g * 2 * rep + rep)
+        a += range(g * 2 * rep + rep, (g + 1) * 2 * rep)
+    return qkvz, torch.tensor(b + a, dtype=torch.long)
+
+
+def _merge_gdn_in_proj(qkvz, ba, cfg: ModelConfig):
+    pq, pb = gdn_in_proj_permutation(cfg)
+    if isinstance(qkvz, MXFP4Weight) != isinstance(ba, MXFP4Weight):
+        # ba is often left unquantized in MXFP4 checkpoints: quantize it to match
+        if isinstance(qkvz, MXFP4Weight):
+            ba = MXFP4Weight.from_float(ba)
+        else:
+            qkvz = MXFP4Weight.from_float(qkvz)
+    return _cat([_rows(qkvz, pq), _rows(ba, pb)])
+
+
+def load_model(path: str, cfg: Optional[ModelConfig] = None, quant: str = "mxfp4", device="cuda",
+               tp=None):
+    """Build a HybridModel from a checkpoint directory."""
+    from ..config import get_model_config
+    from ..models.hybrid import HybridModel
+    cfg = cfg or get_model_config(path)
+    W = CheckpointWeights(path, cfg)
+    return HybridModel(cfg, quant=quant, device=device, tp=tp, weights=W, init_device="cpu")
