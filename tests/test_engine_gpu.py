@@ -34,8 +34,11 @@ def test_prefill_logits_match_cpu_oracle():
             sched = eng.scheduler.schedule()
         outs[dev] = res.logits.float().cpu()
     a, b = outs["cuda"], outs["cpu"]
-    rel = float((a - b).abs().max() / b.abs().max())
-    assert rel < 5e-2, rel
+    # fp8 activation codes can flip at rounding boundaries between the kernels and the oracle;
+    # compare in norm and by the greedy token
+    rel = float((a - b).norm() / b.norm())
+    assert rel < 3e-2, rel
+    assert int(a.argmax(-1)[0]) == int(b.argmax(-1)[0])
 
 
 def test_greedy_decode_graph_matches_eager():

@@ -35,6 +35,8 @@ __global__ void __launch_bounds__(256) qkv_prologue_kernel(
     const float* __restrict__ cos_sin, int rot, int T, int Hq, int Hkv, float eps,
     __nv_bfloat16* __restrict__ q_out, uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache,
     int cache_fp8, const int64_t* __restrict__ slot_mapping, int block_size) {
+  pdl_wait();     // inputs come from the preceding kernel
+  pdl_trigger();
   constexpr int PER = D / 32;
   const int gw = blockIdx.x * 8 + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -144,7 +146,10 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(
     const int* __restrict__ tile_seq, const int* __restrict__ tile_row0, int Hq, int Hkv,
     int block_size, float scale_log2, int causal, int window, int num_splits,
     __nv_bfloat16* __restrict__ out, float* __restrict__ part_o, float* __restrict__ part_ml,
-    int T) {
+    int T, unsigned* __restrict__ counters) {
+  pdl_wait();     // inputs come from the preceding kernel
+  pdl_trigger();
+  __shared__ bool s_last;
   constexpr int CH = D / 8;               // 16-byte chunks per row (bf16)
   constexpr int NT = BC / 8;              // n-tiles of S per warp (8 keys each)
   constexpr int OT = D / 8;               // n-tiles of O per warp
@@ -359,12 +364,55 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(
       }
     }
   }
+  if (num_splits > 1) {
+    // the last split CTA of this (row tile, kv head) merges all splits' partials
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      s_last = atomicAdd(&counters[tile * Hkv + hk], 1u) == (unsigned)(num_splits - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    constexpr int PER = D / 32;
+    for (int rr = warp; rr < rows_here; rr += 4) {
+      const int r = row0 + rr;
+      const int i = r / G, g = r % G;
+      const size_t gw = (size_t)(s0 + i) * Hq + hk * G + g;
+      float mmax = -INFINITY;
+      for (int sp = 0; sp < num_splits; ++sp) {
+        const float m = __ldcg(part_ml + ((size_t)sp * T * Hq + gw) * 2);
+        const float l = __ldcg(part_ml + ((size_t)sp * T * Hq + gw) * 2 + 1);
+        if (l > 0.f) mmax = fmaxf(mmax, m);
+      }
+      float acc[PER];
+#pragma unroll
+      for (int p = 0; p < PER; ++p) acc[p] = 0.f;
+      float wsum = 0.f;
+      for (int sp = 0; sp < num_splits; ++sp) {
+        const float m = __ldcg(part_ml + ((size_t)sp * T * Hq + gw) * 2);
+        const float l = __ldcg(part_ml + ((size_t)sp * T * Hq + gw) * 2 + 1);
+        if (!(l > 0.f)) continue;
+        const float w = l * exp2f(m - mmax);
+        wsum += w;
+        const float* src = part_o + ((size_t)sp * T * Hq + gw) * D;
+#pragma unroll
+        for (int p = 0; p < PER; ++p) acc[p] += w * __ldcg(src + lane * PER + p);
+      }
+      const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+#pragma unroll
+      for (int p = 0; p < PER; ++p) out[gw * D + lane * PER + p] = __float2bfloat16_rn(acc[p] * inv);
+    }
+    if (threadIdx.x == 0) counters[tile * Hkv + hk] = 0;
+  }
 }
 
 // merge split partials: one warp per (token, head)
 template <int D>
 __global__ void attn_merge_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
                                   int num_splits, int T, int Hq, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();     // inputs come from the preceding kernel
+  pdl_trigger();
   const int gw = blockIdx.x * 8 + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (gw >= T * Hq) return;
@@ -414,12 +462,12 @@ void qkv_prologue(torch::Tensor qkv, int64_t q_head_stride, int64_t k_off, int64
   dim3 grid((warps + 7) / 8);
   auto run = [&](auto dtag) {
     constexpr int Dc = decltype(dtag)::value;
-    attn::qkv_prologue_kernel<Dc><<<grid, 256, 0, stream>>>(
+C10_CUDA_CHECK(launch_pdl((attn::qkv_prologue_kernel<Dc>), dim3(grid), dim3(256), 0, stream, 
         (const __nv_bfloat16*)qkv.data_ptr(), qkv.stride(0), q_head_stride, k_off, v_off,
         positions.data_ptr<int>(), (const __nv_bfloat16*)qn_w.data_ptr(),
         (const __nv_bfloat16*)kn_w.data_ptr(), cos_sin.data_ptr<float>(), rot, T, Hq, Hkv,
         (float)eps, (__nv_bfloat16*)q_out.data_ptr(), (uint8_t*)k_cache.data_ptr(),
-        (uint8_t*)v_cache.data_ptr(), fp8 ? 1 : 0, slot_mapping.data_ptr<int64_t>(), block_size);
+        (uint8_t*)v_cache.data_ptr(), fp8 ? 1 : 0, slot_mapping.data_ptr<int64_t>(), block_size));
   };
   if (D == 256) run(std::integral_constant<int, 256>{});
   else if (D == 128) run(std::integral_constant<int, 128>{});
@@ -434,7 +482,7 @@ void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
                      torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor qsl,
                      torch::Tensor tile_seq, torch::Tensor tile_row0, double scale, bool causal,
                      int64_t window, int64_t num_splits, torch::Tensor part_o,
-                     torch::Tensor part_ml, torch::Tensor out) {
+                     torch::Tensor part_ml, torch::Tensor out, torch::Tensor counters) {
   const int T = q.size(0), Hq = q.size(1), D = q.size(2);
   const int Hkv = k_cache.size(1), block_size = k_cache.size(2);
   const int num_tiles = tile_seq.size(0);
@@ -456,14 +504,15 @@ void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
       C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
       set = true;
     }
-    kern<<<grid, 128, smem, stream>>>(
+C10_CUDA_CHECK(launch_pdl(    kern, dim3(grid), dim3(128), smem, stream, 
         (const __nv_bfloat16*)q.data_ptr(), (const uint8_t*)k_cache.data_ptr(),
         (const uint8_t*)v_cache.data_ptr(), block_tables.data_ptr<int>(), block_tables.stride(0),
         seq_lens.data_ptr<int>(), qsl.data_ptr<int>(), tile_seq.data_ptr<int>(),
         tile_row0.data_ptr<int>(), Hq, Hkv, block_size, scale_log2, causal ? 1 : 0, (int)window,
         (int)num_splits, (__nv_bfloat16*)out.data_ptr(),
         num_splits > 1 ? part_o.data_ptr<float>() : nullptr,
-        num_splits > 1 ? part_ml.data_ptr<float>() : nullptr, T);
+        num_splits > 1 ? part_ml.data_ptr<float>() : nullptr, T,
+        num_splits > 1 ? reinterpret_cast<unsigned*>(counters.data_ptr()) : nullptr));
   };
   if (D == 256) {
     if (fp8) run(std::integral_constant<int, 256>{}, std::true_type{});
@@ -478,19 +527,6 @@ void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
     TORCH_CHECK(false, "paged_attention: head_dim 64/128/256");
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  if (num_splits > 1) {
-    dim3 g2((T * Hq + 7) / 8);
-    auto merge = [&](auto dtag) {
-      constexpr int Dc = decltype(dtag)::value;
-      attn::attn_merge_kernel<Dc><<<g2, 256, 0, stream>>>(part_o.data_ptr<float>(),
-                                                          part_ml.data_ptr<float>(), num_splits, T,
-                                                          Hq, (__nv_bfloat16*)out.data_ptr());
-    };
-    if (D == 256) merge(std::integral_constant<int, 256>{});
-    else if (D == 128) merge(std::integral_constant<int, 128>{});
-    else merge(std::integral_constant<int, 64>{});
-    C10_CUDA_KERNEL_LAUNCH_CHECK();
-  }
 }
 
 }  // namespace rad

@@ -17,7 +17,7 @@ void gate_mul_quant(torch::Tensor a, torch::Tensor gate, int64_t head_dim, int64
 void quant_fp8_rows(torch::Tensor x, torch::Tensor q, torch::Tensor scale);
 void gdn_conv(torch::Tensor x, torch::Tensor w, torch::Tensor conv_state, torch::Tensor qsl,
               torch::Tensor slots, torch::Tensor has_init, torch::Tensor tok_seq, int64_t qk_dim,
-              int64_t head_dim, torch::Tensor y, double eps);
+              int64_t head_dim, torch::Tensor y, double eps, bool update_state);
 void gdn_conv_state_update(torch::Tensor x, torch::Tensor conv_state, torch::Tensor qsl,
                            torch::Tensor slots, torch::Tensor has_init, torch::Tensor commit_len);
 void gdn_recurrent(torch::Tensor y, torch::Tensor ba, torch::Tensor A_log, torch::Tensor dt_bias,
@@ -33,8 +33,9 @@ void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
                      torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor qsl,
                      torch::Tensor tile_seq, torch::Tensor tile_row0, double scale, bool causal,
                      int64_t window, int64_t num_splits, torch::Tensor part_o,
-                     torch::Tensor part_ml, torch::Tensor out);
-void argmax_rows(torch::Tensor x, torch::Tensor out_ids, torch::Tensor out_vals);
+                     torch::Tensor part_ml, torch::Tensor out, torch::Tensor counters);
+void argmax_rows(torch::Tensor x, torch::Tensor out_ids, torch::Tensor out_vals,
+                 torch::Tensor workspace);
 void sample_from_topk(torch::Tensor vals, torch::Tensor ids, torch::Tensor temperature,
                       torch::Tensor top_k, torch::Tensor top_p, torch::Tensor min_p,
                       torch::Tensor seeds, int64_t step, torch::Tensor out,

@@ -52,6 +52,8 @@ __global__ void __launch_bounds__(256) oneshot_kernel(
     const __nv_bfloat16* __restrict__ residual, const __nv_bfloat16* __restrict__ w, float eps,
     __nv_bfloat16* __restrict__ res_out, uint8_t* __restrict__ q, float* __restrict__ scale,
     int* __restrict__ status) {
+  pdl_wait();     // inputs come from the preceding kernel
+  pdl_trigger();
   __shared__ uint32_t s_seq;
   __shared__ float red[8];
   __shared__ int s_ok;
@@ -244,15 +246,15 @@ void allreduce_oneshot(std::vector<int64_t> peers, int64_t rank, torch::Tensor i
   int* st = status.numel() ? status.data_ptr<int>() : nullptr;
   const bool fused = q.defined() && q.numel();
   if (fused)
-    oneshot_kernel<true><<<nb, 256, 0, stream>>>(
+C10_CUDA_CHECK(launch_pdl((oneshot_kernel<true>), dim3(nb), dim3(256), 0, stream, 
         pp, world, rank, (const __nv_bfloat16*)inp.data_ptr(), M, H, slot_bytes, nullptr,
         (const __nv_bfloat16*)residual.data_ptr(), (const __nv_bfloat16*)weight.data_ptr(),
         (float)eps, (__nv_bfloat16*)res_out.data_ptr(), (uint8_t*)q.data_ptr(),
-        scale.data_ptr<float>(), st);
+        scale.data_ptr<float>(), st));
   else
-    oneshot_kernel<false><<<nb, 256, 0, stream>>>(
+C10_CUDA_CHECK(launch_pdl((oneshot_kernel<false>), dim3(nb), dim3(256), 0, stream, 
         pp, world, rank, (const __nv_bfloat16*)inp.data_ptr(), M, H, slot_bytes,
-        (__nv_bfloat16*)out.data_ptr(), nullptr, nullptr, 0.f, nullptr, nullptr, nullptr, st);
+        (__nv_bfloat16*)out.data_ptr(), nullptr, nullptr, 0.f, nullptr, nullptr, nullptr, st));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -332,3 +332,37 @@ DEVI float warp_max(float v) {
 }
 
 }  // namespace rad
+
+// ---------------------------------------------------------------------------------------------
+// programmatic dependent launch (PDL)
+// ---------------------------------------------------------------------------------------------
+namespace rad {
+// Block until the preceding kernel in the stream has completed and its writes are visible.
+DEVI void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allow the next kernel in the stream to start its prologue (it still waits in pdl_wait()).
+DEVI void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+}  // namespace rad
+
+#ifndef __CUDACC_RTC__
+#include <cuda_runtime.h>
+namespace rad {
+// Launch with the programmatic-stream-serialization attribute: the kernel may start while its
+// predecessor drains; every kernel of this library calls pdl_wait() before reading the
+// predecessor's outputs.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+}  // namespace rad
+#endif

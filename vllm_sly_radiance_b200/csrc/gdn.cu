@@ -33,7 +33,9 @@ __global__ void __launch_bounds__(256) conv_kernel(
     const __nv_bfloat16* __restrict__ x, int ldx, const __nv_bfloat16* __restrict__ w,
     const __nv_bfloat16* __restrict__ conv_state, const int* __restrict__ qsl,
     const int* __restrict__ slots, const int* __restrict__ has_init, const int* __restrict__ tok_seq,
-    int C, int qk_dim, __nv_bfloat16* __restrict__ y, int ldy, float eps) {
+    int C, int qk_dim, __nv_bfloat16* __restrict__ y, int ldy, float eps, int update_state) {
+  pdl_wait();     // inputs come from the preceding kernel
+  pdl_trigger();
   constexpr int PER = D / 32;           // channels per lane
   const int t = blockIdx.x;
   const int chunk = blockIdx.y * 8 + threadIdx.x / 32;
@@ -45,6 +47,7 @@ __global__ void __launch_bounds__(256) conv_kernel(
   const int slot = slots[b];
   const bool init = has_init[b] != 0;
   float acc[PER];
+  float xin[W][PER];
 #pragma unroll
   for (int p = 0; p < PER; ++p) acc[p] = 0.f;
 #pragma unroll
@@ -61,7 +64,19 @@ __global__ void __launch_bounds__(256) conv_kernel(
         // state holds the previous W-1 inputs, oldest first: state[W-1+src]
         xv = init ? __bfloat162float(conv_state[((size_t)slot * C + c) * (W - 1) + (W - 1 + src)]) : 0.f;
       }
+      xin[j][p] = xv;
       acc[p] += xv * __bfloat162float(w[(size_t)c * W + j]);
+    }
+  }
+  if (update_state) {
+    // decode (one token per sequence): this warp is the only reader of these state entries, so
+    // it shifts them in place (the separate state-update launch is skipped)
+#pragma unroll
+    for (int p = 0; p < PER; ++p) {
+      const int c = chunk * D + lane * PER + p;
+      __nv_bfloat16* st = const_cast<__nv_bfloat16*>(conv_state) + ((size_t)slot * C + c) * (W - 1);
+#pragma unroll
+      for (int j = 0; j < W - 1; ++j) st[j] = __float2bfloat16_rn(xin[j + 1][p]);
     }
   }
   float ss = 0.f;
@@ -88,11 +103,14 @@ __global__ void conv_state_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
                                   const int* __restrict__ qsl, const int* __restrict__ slots,
                                   const int* __restrict__ has_init,
                                   const int* __restrict__ commit_len, int C) {
+  pdl_wait();     // inputs come from the preceding kernel
+  pdl_trigger();
   const int b = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
   const int s0 = qsl[b];
   const int L = commit_len ? commit_len[b] : (qsl[b + 1] - s0);
+  if (L < 0) return;                    // row not part of this commit pass
   const int slot = slots[b];
   const bool init = has_init[b] != 0;
   __nv_bfloat16* st = conv_state + ((size_t)slot * C + c) * (W - 1);
@@ -124,6 +142,8 @@ __global__ void __launch_bounds__(128) recurrent_kernel(
     const int* __restrict__ commit_len,                  // optional: rows to apply to the stored state
     int Hk, int Hv, int DV, float scale, __nv_bfloat16* __restrict__ out, int ldo,
     int write_out) {
+  pdl_wait();     // inputs come from the preceding kernel
+  pdl_trigger();
   constexpr int PL = DK / 32;          // dk columns per lane
   constexpr int RW = 8;                // rows per warp
   const int b = blockIdx.x;
@@ -133,6 +153,8 @@ __global__ void __launch_bounds__(128) recurrent_kernel(
   const int s0 = qsl[b];
   const int L = qsl[b + 1] - s0;
   const int Lc = commit_len ? commit_len[b] : L;
+  if (Lc < 0) return;                   // row not part of this commit pass
+  const int Lrun = write_out ? L : min(L, Lc);
   const int slot = slots[b];
   const int hk = h / (Hv / Hk);
   const int key_dim = Hk * DK;
@@ -153,7 +175,7 @@ __global__ void __launch_bounds__(128) recurrent_kernel(
       for (int p = 0; p < PL; ++p) S[r][p] = 0.f;
   }
 
-  for (int i = 0; i < L; ++i) {
+  for (int i = 0; i < Lrun; ++i) {
     const size_t t = s0 + i;
     const __nv_bfloat16* yt = y + t * ldy;
     float q[PL], k[PL], v[RW];
@@ -223,7 +245,7 @@ static inline const int* iptr(const torch::Tensor& t) {
 // qsl [B+1], slots [B], has_init [B], tok_seq [T] (sequence index of each token), y [T, C] out
 void gdn_conv(torch::Tensor x, torch::Tensor w, torch::Tensor conv_state, torch::Tensor qsl,
               torch::Tensor slots, torch::Tensor has_init, torch::Tensor tok_seq, int64_t qk_dim,
-              int64_t head_dim, torch::Tensor y, double eps) {
+              int64_t head_dim, torch::Tensor y, double eps, bool update_state) {
   const int T = x.size(0);
   const int C = w.size(0), W = w.size(1);
   if (T == 0) return;
@@ -235,11 +257,11 @@ void gdn_conv(torch::Tensor x, torch::Tensor w, torch::Tensor conv_state, torch:
   dim3 grid(T, (chunks + 7) / 8);
   auto run = [&](auto dtag) {
     constexpr int D = decltype(dtag)::value;
-    gdn::conv_kernel<D, 4><<<grid, 256, 0, stream>>>(
+C10_CUDA_CHECK(launch_pdl((gdn::conv_kernel<D, 4>), dim3(grid), dim3(256), 0, stream, 
         (const __nv_bfloat16*)x.data_ptr(), x.stride(0), (const __nv_bfloat16*)w.data_ptr(),
         (const __nv_bfloat16*)conv_state.data_ptr(), qsl.data_ptr<int>(), slots.data_ptr<int>(),
         has_init.data_ptr<int>(), tok_seq.data_ptr<int>(), C, qk_dim,
-        (__nv_bfloat16*)y.data_ptr(), y.stride(0), (float)eps);
+        (__nv_bfloat16*)y.data_ptr(), y.stride(0), (float)eps, update_state ? 1 : 0));
   };
   if (head_dim == 128) run(std::integral_constant<int, 128>{});
   else if (head_dim == 64) run(std::integral_constant<int, 64>{});
@@ -256,9 +278,9 @@ void gdn_conv_state_update(torch::Tensor x, torch::Tensor conv_state, torch::Ten
   const at::cuda::CUDAGuard guard(x.device());
   auto stream = at::cuda::getCurrentCUDAStream();
   dim3 grid((C + 255) / 256, B);
-  gdn::conv_state_kernel<4><<<grid, 256, 0, stream>>>(
+C10_CUDA_CHECK(launch_pdl((gdn::conv_state_kernel<4>), dim3(grid), dim3(256), 0, stream, 
       (const __nv_bfloat16*)x.data_ptr(), x.stride(0), (__nv_bfloat16*)conv_state.data_ptr(),
-      qsl.data_ptr<int>(), slots.data_ptr<int>(), has_init.data_ptr<int>(), iptr(commit_len), C);
+      qsl.data_ptr<int>(), slots.data_ptr<int>(), has_init.data_ptr<int>(), iptr(commit_len), C));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -277,12 +299,12 @@ void gdn_recurrent(torch::Tensor y, torch::Tensor ba, torch::Tensor A_log, torch
   auto run = [&](auto dtag, auto stag) {
     constexpr int DKc = decltype(dtag)::value;
     using ST = typename decltype(stag)::type;
-    gdn::recurrent_kernel<DKc, ST><<<grid, 128, 0, stream>>>(
+C10_CUDA_CHECK(launch_pdl((gdn::recurrent_kernel<DKc, ST>), dim3(grid), dim3(128), 0, stream, 
         (const __nv_bfloat16*)y.data_ptr(), y.stride(0), (const __nv_bfloat16*)ba.data_ptr(),
         ba.stride(0), A_log.data_ptr<float>(), dt_bias.data_ptr<float>(), (ST*)state.data_ptr(),
         qsl.data_ptr<int>(), slots.data_ptr<int>(), has_init.data_ptr<int>(), iptr(commit_len),
         Hk, Hv, DV, (float)scale, out.defined() && out.numel() ? (__nv_bfloat16*)out.data_ptr() : nullptr,
-        out.defined() && out.numel() ? out.stride(0) : 0, write_out ? 1 : 0);
+        out.defined() && out.numel() ? out.stride(0) : 0, write_out ? 1 : 0));
   };
   struct F32 { using type = float; };
   struct BF16 { using type = __nv_bfloat16; };

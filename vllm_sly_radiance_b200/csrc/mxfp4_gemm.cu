@@ -49,7 +49,11 @@ struct Cfg {
   static constexpr int A_TILE_BYTES = BN * BK;
   // stages start on 1024-byte boundaries (128B-swizzled tiles need it)
   static constexpr int STAGE_BYTES = (W_TILE_BYTES + A_TILE_BYTES + SF_TILE_BYTES + 1023) / 1024 * 1024;
-  static constexpr int STAGES_RAW = (kSmemBudget - 2048) / STAGE_BYTES;
+  // decode tiles (BN <= 64) keep two CTAs per SM so a split-K grid runs in a single wave;
+  // prefill tiles take the whole SM
+  static constexpr int MIN_BLOCKS = BN <= 64 ? 2 : 1;
+  static constexpr int BUDGET = MIN_BLOCKS == 2 ? (228 * 1024 / 2 - 1024 - 3072) : (kSmemBudget - 2048);
+  static constexpr int STAGES_RAW = BUDGET / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   // TMEM columns: accumulator BN + SFA 4 + SFB 8 -> next power of two
   static constexpr int TMEM_NEED = BN + 12;
@@ -74,7 +78,7 @@ __host__ __device__ constexpr uint32_t make_idesc(int bn, int sf_id) {
 }
 
 template <int BN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
     mxfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                       const __grid_constant__ CUtensorMap tmap_a, const uint8_t* __restrict__ sfw,
                       const float* __restrict__ a_scale, __nv_bfloat16* __restrict__ out,
@@ -115,6 +119,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmap_w);
     tma_prefetch_desc(&tmap_a);
   }
+  pdl_trigger();   // the next kernel may start its own prologue
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
     tmem_relinquish();
@@ -146,7 +151,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (elect_one()) {
       const uint64_t w_policy = l2_policy_evict_first();   // weights stream once
       const uint8_t* sf_row = sfw + (size_t)n_tile * (size_t)k_tiles_total * SF_TILE_BYTES;
-      for (int i = 0; i < nk; ++i) {
+      // Weights and scale factors do not depend on the preceding kernel: fill the pipeline with
+      // them while that kernel drains, then wait for it and add the activation tiles.
+      const int pre = nk < C::STAGES ? nk : C::STAGES;
+      for (int i = 0; i < pre; ++i) {
+        uint8_t* st = stage_base + i * C::STAGE_BYTES;
+        const int kt = kt0 + i;
+        mbar_arrive_expect_tx(&full_bar[i], W_TILE_TX + C::A_TILE_BYTES + SF_TILE_BYTES);
+        tma_load_2d_hint(st, &tmap_w, &full_bar[i], kt * BK, n0, w_policy);
+        bulk_load(st + W_TILE_BYTES + C::A_TILE_BYTES, sf_row + (size_t)kt * SF_TILE_BYTES,
+                  SF_TILE_BYTES, &full_bar[i]);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(stage_base + i * C::STAGE_BYTES + W_TILE_BYTES, &tmap_a, &full_bar[i],
+                    (kt0 + i) * BK, m0);
+      for (int i = pre; i < nk; ++i) {
         const int s = i % C::STAGES;
         const uint32_t ph = (i / C::STAGES) & 1;
         if (!mbar_wait(&empty_bar[s], ph ^ 1, status)) { *abort_flag = 1; break; }
@@ -192,6 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;            // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;     // weight row within the tile
     const int n = n0 + row;
+    pdl_wait();                        // a_scale comes from the preceding kernel
     if (!mbar_wait(acc_bar, 0, status)) *abort_flag = 1;
     tc_fence_after();
     const bool have_acc = nk > 0 && !*abort_flag;
@@ -317,23 +338,27 @@ static void launch(const torch::Tensor& a, const torch::Tensor& a_scale, const t
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attrs[1];
+  cudaLaunchAttribute attrs[2];
   attrs[0].id = cudaLaunchAttributeClusterDimension;
   attrs[0].val.clusterDim.x = 1;
   attrs[0].val.clusterDim.y = 1;
   attrs[0].val.clusterDim.z = splits;
+  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tw, ta, (const uint8_t*)sf.data_ptr(),
                                     (const float*)a_scale.data_ptr(),
                                     (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), M, N, K,
                                     per, status));
 }
 
-static int pick_splits(int tiles, int k_tiles) {
-  // fill the 148 SMs: grow the cluster along K while tiles are few and each CTA keeps >= 4 stages
+static int pick_splits(int tiles, int k_tiles, int ctas_per_sm) {
+  // fill the SMs in one wave: grow the cluster along K while the grid fits the resident slots
+  // (148 SMs x CTAs per SM) and each CTA keeps >= 4 k-tiles
+  const int slots = 148 * ctas_per_sm;
   int s = 1;
-  while (s < 8 && tiles * s * 2 <= 2 * 148 && k_tiles / (s * 2) >= 4) s *= 2;
+  while (s < 8 && tiles * s * 2 <= slots && k_tiles / (s * 2) >= 4) s *= 2;
   return s;
 }
 
@@ -367,7 +392,8 @@ void mxfp4_gemm(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch:
   else if (M <= 128) bn = 128;
   else bn = 256;
   const int tiles = ((N + BM - 1) / BM) * ((M + bn - 1) / bn);
-  int splits = splits_override > 0 ? (int)splits_override : pick_splits(tiles, K / BK);
+  int splits = splits_override > 0 ? (int)splits_override
+                                   : pick_splits(tiles, K / BK, bn <= 64 ? 2 : 1);
   switch (bn) {
     case 16: launch<16>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream); break;
     case 32: launch<32>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream); break;

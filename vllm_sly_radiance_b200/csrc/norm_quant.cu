@@ -101,6 +101,8 @@ __global__ void __launch_bounds__(T) add_rms_kernel(
     const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ res_out, int ldro,
     uint8_t* __restrict__ q, int ldq, float* __restrict__ scale, __nv_bfloat16* __restrict__ nout,
     int ldn, int H, float eps) {
+  pdl_wait();     // inputs come from the preceding kernel
+  pdl_trigger();
   __shared__ float red[T / 32];
   const int row = blockIdx.x;
   const int nvec = H / V;
@@ -142,6 +144,8 @@ template <int MAXV>
 __global__ void __launch_bounds__(T) silu_mul_quant_kernel(const __nv_bfloat16* __restrict__ gu,
                                                            int ldg, int I, uint8_t* __restrict__ q,
                                                            int ldq, float* __restrict__ scale) {
+  pdl_wait();     // inputs come from the preceding kernel
+  pdl_trigger();
   __shared__ float red[T / 32];
   const int row = blockIdx.x;
   const int nvec = I / V;
@@ -166,6 +170,8 @@ __global__ void __launch_bounds__(T) gdn_norm_quant_kernel(
     const OT* __restrict__ o, int ldo, const __nv_bfloat16* __restrict__ z, int ldz,
     const __nv_bfloat16* __restrict__ w, int D, int head_dim, float eps, uint8_t* __restrict__ q,
     int ldq, float* __restrict__ scale, __nv_bfloat16* __restrict__ nout, int ldn) {
+  pdl_wait();     // inputs come from the preceding kernel
+  pdl_trigger();
   __shared__ float red[T / 32];
   const int row = blockIdx.x;
   const int nvec = D / V;
@@ -204,6 +210,8 @@ __global__ void __launch_bounds__(T) gate_mul_quant_kernel(
     const __nv_bfloat16* __restrict__ a, int lda, const __nv_bfloat16* __restrict__ gate, int ldg,
     int head_dim, int gate_head_stride, int D, uint8_t* __restrict__ q, int ldq,
     float* __restrict__ scale, __nv_bfloat16* __restrict__ nout, int ldn) {
+  pdl_wait();     // inputs come from the preceding kernel
+  pdl_trigger();
   __shared__ float red[T / 32];
   const int row = blockIdx.x;
   const int nvec = D / V;
@@ -229,6 +237,8 @@ template <int MAXV>
 __global__ void __launch_bounds__(T) quant_rows_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
                                                        int D, uint8_t* __restrict__ q, int ldq,
                                                        float* __restrict__ scale) {
+  pdl_wait();     // inputs come from the preceding kernel
+  pdl_trigger();
   __shared__ float red[T / 32];
   const int row = blockIdx.x;
   const int nvec = D / V;
@@ -275,17 +285,17 @@ void add_rms_quant(torch::Tensor x, torch::Tensor residual, torch::Tensor weight
   const bool quant = q.defined() && q.numel();
   DISPATCH_MAXV(H / V, {
     if (quant)
-      add_rms_kernel<MAXV, true><<<M, T, 0, stream>>>(
+C10_CUDA_CHECK(launch_pdl((add_rms_kernel<MAXV, true>), dim3(M), dim3(T), 0, stream, 
           bf(x), x.stride(0), bf(residual), residual.defined() && residual.numel() ? residual.stride(0) : 0,
           bf(weight), bfm(res_out), res_out.defined() && res_out.numel() ? res_out.stride(0) : 0,
           (uint8_t*)q.data_ptr(), q.stride(0), scale.data_ptr<float>(), bfm(nout),
-          nout.defined() && nout.numel() ? nout.stride(0) : 0, H, (float)eps);
+          nout.defined() && nout.numel() ? nout.stride(0) : 0, H, (float)eps));
     else
-      add_rms_kernel<MAXV, false><<<M, T, 0, stream>>>(
+C10_CUDA_CHECK(launch_pdl((add_rms_kernel<MAXV, false>), dim3(M), dim3(T), 0, stream, 
           bf(x), x.stride(0), bf(residual), residual.defined() && residual.numel() ? residual.stride(0) : 0,
           bf(weight), bfm(res_out), res_out.defined() && res_out.numel() ? res_out.stride(0) : 0,
           nullptr, 0, nullptr, bfm(nout), nout.defined() && nout.numel() ? nout.stride(0) : 0, H,
-          (float)eps);
+          (float)eps));
   });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -298,9 +308,9 @@ void silu_mul_quant(torch::Tensor gate_up, torch::Tensor q, torch::Tensor scale)
   const at::cuda::CUDAGuard guard(gate_up.device());
   auto stream = at::cuda::getCurrentCUDAStream();
   DISPATCH_MAXV(I / V, {
-    silu_mul_quant_kernel<MAXV><<<M, T, 0, stream>>>(bf(gate_up), gate_up.stride(0), I,
+C10_CUDA_CHECK(launch_pdl((silu_mul_quant_kernel<MAXV>), dim3(M), dim3(T), 0, stream, bf(gate_up), gate_up.stride(0), I,
                                                       (uint8_t*)q.data_ptr(), q.stride(0),
-                                                      scale.data_ptr<float>());
+                                                      scale.data_ptr<float>()));
   });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -321,13 +331,13 @@ void gdn_norm_quant(torch::Tensor o, torch::Tensor z, torch::Tensor weight, int6
   const int ldn = nout.defined() && nout.numel() ? nout.stride(0) : 0;
   DISPATCH_MAXV(D / V, {
     if (o.scalar_type() == at::kFloat)
-      gdn_norm_quant_kernel<MAXV, float><<<M, T, 0, stream>>>(
+C10_CUDA_CHECK(launch_pdl((gdn_norm_quant_kernel<MAXV, float>), dim3(M), dim3(T), 0, stream, 
           o.data_ptr<float>(), o.stride(0), bf(z), z.stride(0), bf(weight), D, head_dim, (float)eps,
-          qp, ldq, sp, bfm(nout), ldn);
+          qp, ldq, sp, bfm(nout), ldn));
     else
-      gdn_norm_quant_kernel<MAXV, __nv_bfloat16><<<M, T, 0, stream>>>(
+C10_CUDA_CHECK(launch_pdl((gdn_norm_quant_kernel<MAXV, __nv_bfloat16>), dim3(M), dim3(T), 0, stream, 
           bf(o), o.stride(0), bf(z), z.stride(0), bf(weight), D, head_dim, (float)eps, qp, ldq, sp,
-          bfm(nout), ldn);
+          bfm(nout), ldn));
   });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -346,9 +356,9 @@ void gate_mul_quant(torch::Tensor a, torch::Tensor gate, int64_t head_dim, int64
   const int ldq = qp ? q.stride(0) : 0;
   const int ldn = nout.defined() && nout.numel() ? nout.stride(0) : 0;
   DISPATCH_MAXV(D / V, {
-    gate_mul_quant_kernel<MAXV><<<M, T, 0, stream>>>(bf(a), a.stride(0), bf(gate), gate.stride(0),
+C10_CUDA_CHECK(launch_pdl((gate_mul_quant_kernel<MAXV>), dim3(M), dim3(T), 0, stream, bf(a), a.stride(0), bf(gate), gate.stride(0),
                                                      head_dim, gate_head_stride, D, qp, ldq, sp,
-                                                     bfm(nout), ldn);
+                                                     bfm(nout), ldn));
   });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -361,8 +371,8 @@ void quant_fp8_rows(torch::Tensor x, torch::Tensor q, torch::Tensor scale) {
   const at::cuda::CUDAGuard guard(x.device());
   auto stream = at::cuda::getCurrentCUDAStream();
   DISPATCH_MAXV(D / V, {
-    quant_rows_kernel<MAXV><<<M, T, 0, stream>>>(bf(x), x.stride(0), D, (uint8_t*)q.data_ptr(),
-                                                 q.stride(0), scale.data_ptr<float>());
+C10_CUDA_CHECK(launch_pdl((quant_rows_kernel<MAXV>), dim3(M), dim3(T), 0, stream, bf(x), x.stride(0), D, (uint8_t*)q.data_ptr(),
+                                                 q.stride(0), scale.data_ptr<float>()));
   });
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

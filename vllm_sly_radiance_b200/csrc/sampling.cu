@@ -16,42 +16,64 @@
 namespace rad {
 namespace smp {
 
-template <typename TIn>
-__global__ void __launch_bounds__(1024) argmax_kernel(const TIn* __restrict__ x, int ld, int V,
-                                                      int64_t* __restrict__ out_ids,
-                                                      float* __restrict__ out_vals) {
-  const int row = blockIdx.x;
-  float best = -INFINITY;
-  int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float v = to_f(x[(size_t)row * ld + i]);
-    if (v > best || (v == best && i < bi)) { best = v; bi = i; }
-  }
+// Greedy argmax over long rows, split across CTAs: each CTA reduces one chunk of a row to
+// (value, index); the last CTA of the row (self-resetting arrival counter) reduces the partials.
+// Ties resolve to the lowest index.
+DEVI void argmax_combine(float& best, int& bi, float ov, int oi) {
+  if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+}
+DEVI void block_argmax(float& best, int& bi, float* sv, int* si) {
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffff, best, o);
-    const int oi = __shfl_xor_sync(0xffffffff, bi, o);
-    if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
-  }
-  __shared__ float sv[32];
-  __shared__ int si[32];
+  for (int o = 16; o > 0; o >>= 1)
+    argmax_combine(best, bi, __shfl_xor_sync(0xffffffff, best, o), __shfl_xor_sync(0xffffffff, bi, o));
   const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  __syncthreads();
   if (l == 0) { sv[w] = best; si[w] = bi; }
   __syncthreads();
-  if (w == 0) {
-    const int nw = blockDim.x / 32;
-    best = l < nw ? sv[l] : -INFINITY;
-    bi = l < nw ? si[l] : 0x7fffffff;
+  const int nw = blockDim.x / 32;
+  best = l < nw ? sv[l] : -INFINITY;
+  bi = l < nw ? si[l] : 0x7fffffff;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffff, best, o);
-      const int oi = __shfl_xor_sync(0xffffffff, bi, o);
-      if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
-    }
-    if (l == 0) {
-      out_ids[row] = bi;
-      if (out_vals) out_vals[row] = best;
-    }
+  for (int o = 16; o > 0; o >>= 1)
+    argmax_combine(best, bi, __shfl_xor_sync(0xffffffff, best, o), __shfl_xor_sync(0xffffffff, bi, o));
+}
+
+template <typename TIn>
+__global__ void __launch_bounds__(256) argmax_kernel(const TIn* __restrict__ x, int ld, int V,
+                                                     int chunk, float* __restrict__ pv,
+                                                     int* __restrict__ pi,
+                                                     unsigned* __restrict__ counters,
+                                                     int64_t* __restrict__ out_ids,
+                                                     float* __restrict__ out_vals) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  __shared__ bool last;
+  const int row = blockIdx.y, ch = blockIdx.x, nch = gridDim.x;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  const int i0 = ch * chunk, i1 = min(V, i0 + chunk);
+  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) argmax_combine(best, bi, to_f(x[(size_t)row * ld + i]), i);
+  block_argmax(best, bi, sv, si);
+  if (threadIdx.x == 0) {
+    pv[row * nch + ch] = best;
+    pi[row * nch + ch] = bi;
+    __threadfence();
+    last = atomicAdd(&counters[row], 1u) == (unsigned)(nch - 1);
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  best = -INFINITY;
+  bi = 0x7fffffff;
+  for (int c = threadIdx.x; c < nch; c += blockDim.x)
+    argmax_combine(best, bi, ((volatile float*)pv)[row * nch + c], ((volatile int*)pi)[row * nch + c]);
+  block_argmax(best, bi, sv, si);
+  if (threadIdx.x == 0) {
+    out_ids[row] = bi;
+    if (out_vals) out_vals[row] = best;
+    counters[row] = 0;
   }
 }
 
@@ -62,6 +84,8 @@ __global__ void sample_topk_kernel(const float* __restrict__ vals, const int64_t
                                    const float* __restrict__ min_p, const int64_t* __restrict__ seeds,
                                    int64_t step, int64_t* __restrict__ out, float* __restrict__ out_logprob,
                                    float* __restrict__ probs_out, int B) {
+  pdl_wait();     // inputs come from the preceding kernel
+  pdl_trigger();
   const int row = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (row >= B) return;
@@ -141,19 +165,29 @@ __global__ void sample_topk_kernel(const float* __restrict__ vals, const int64_t
 
 }  // namespace smp
 
-void argmax_rows(torch::Tensor x, torch::Tensor out_ids, torch::Tensor out_vals) {
+// workspace: float[B*64] values, int[B*64] indices, uint32 counters[B] (zero, self-resetting)
+void argmax_rows(torch::Tensor x, torch::Tensor out_ids, torch::Tensor out_vals,
+                 torch::Tensor workspace) {
   const int B = x.size(0), V = x.size(1);
   if (B == 0) return;
   const at::cuda::CUDAGuard guard(x.device());
   auto stream = at::cuda::getCurrentCUDAStream();
   float* vp = out_vals.defined() && out_vals.numel() ? out_vals.data_ptr<float>() : nullptr;
+  const int nch = std::max(1, std::min(64, (V + 4095) / 4096));
+  const int chunk = (V + nch - 1) / nch;
+  TORCH_CHECK(workspace.numel() * 4 >= (int64_t)B * (64 * 2 + 1) * 4, "argmax workspace too small");
+  float* pv = reinterpret_cast<float*>(workspace.data_ptr());
+  int* pi = reinterpret_cast<int*>(pv + B * 64);
+  unsigned* cnt = reinterpret_cast<unsigned*>(pi + B * 64);
+  dim3 grid(nch, B);
   if (x.scalar_type() == at::kFloat)
-    smp::argmax_kernel<float><<<B, 1024, 0, stream>>>(x.data_ptr<float>(), x.stride(0), V,
-                                                      out_ids.data_ptr<int64_t>(), vp);
+    C10_CUDA_CHECK(launch_pdl((smp::argmax_kernel<float>), grid, dim3(256), 0, stream,
+                              x.data_ptr<float>(), (int)x.stride(0), V, chunk, pv, pi, cnt,
+                              out_ids.data_ptr<int64_t>(), vp));
   else
-    smp::argmax_kernel<__nv_bfloat16><<<B, 1024, 0, stream>>>(
-        (const __nv_bfloat16*)x.data_ptr(), x.stride(0), V, out_ids.data_ptr<int64_t>(), vp);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+    C10_CUDA_CHECK(launch_pdl((smp::argmax_kernel<__nv_bfloat16>), grid, dim3(256), 0, stream,
+                              (const __nv_bfloat16*)x.data_ptr(), (int)x.stride(0), V, chunk, pv,
+                              pi, cnt, out_ids.data_ptr<int64_t>(), vp));
 }
 
 void sample_from_topk(torch::Tensor vals, torch::Tensor ids, torch::Tensor temperature,
@@ -164,13 +198,13 @@ void sample_from_topk(torch::Tensor vals, torch::Tensor ids, torch::Tensor tempe
   if (B == 0) return;
   const at::cuda::CUDAGuard guard(vals.device());
   auto stream = at::cuda::getCurrentCUDAStream();
-  smp::sample_topk_kernel<<<(B + 7) / 8, 256, 0, stream>>>(
+C10_CUDA_CHECK(launch_pdl(  smp::sample_topk_kernel, dim3((B + 7) / 8), dim3(256), 0, stream, 
       vals.data_ptr<float>(), ids.data_ptr<int64_t>(), K, temperature.data_ptr<float>(),
       top_k.data_ptr<int>(), top_p.data_ptr<float>(),
       min_p.defined() && min_p.numel() ? min_p.data_ptr<float>() : nullptr, seeds.data_ptr<int64_t>(),
       step, out.data_ptr<int64_t>(),
       out_logprob.defined() && out_logprob.numel() ? out_logprob.data_ptr<float>() : nullptr,
-      probs_out.defined() && probs_out.numel() ? probs_out.data_ptr<float>() : nullptr, B);
+      probs_out.defined() && probs_out.numel() ? probs_out.data_ptr<float>() : nullptr, B));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

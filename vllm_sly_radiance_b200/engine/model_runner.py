@@ -278,8 +278,13 @@ class ModelRunner:
         key = (bucket, greedy)
         g = self.graphs.get(key)
         if g is None:
-            g = self._capture(bucket, greedy, meta, ids)
+            # warm up and capture on an all-padding batch (dummy state slot / KV block 0), so the
+            # capture never advances the real sequences' GDN state; then restore the real batch
+            from .scheduler import SchedulerOutput as _SO
+            dmeta, dids, _, _ = self.prepare(_SO([], 0, [], []), pad_to=bucket, nb_fixed=nb_fixed)
+            g = self._capture(bucket, greedy, dmeta, dids)
             self.graphs[key] = g
+            meta, ids, sample_idx, _ = self.prepare(out, pad_to=bucket, nb_fixed=nb_fixed)
         # sampling params into the static buffers
         B = len(reqs)
         if not greedy:

@@ -156,8 +156,11 @@ class GDNMixer:
         xc = proj[:, :cd]
         z = proj[:, cd:cd + vd]
         ba = proj[:, cd + vd:]
-        y = K.gdn_conv(xc, self.conv_w, conv_state, meta, self.key_dim, self.dk)
-        K.gdn_conv_state_update(xc, conv_state, meta, meta.commit_len)
+        fused_state = meta.commit_len is None and meta.num_tokens == meta.num_seqs
+        y = K.gdn_conv(xc, self.conv_w, conv_state, meta, self.key_dim, self.dk,
+                       update_state=fused_state)
+        if not fused_state:
+            K.gdn_conv_state_update(xc, conv_state, meta, meta.commit_len)
         o = K.gdn_recurrent(y, ba, self.A_log, self.dt_bias, ssm_state, meta, self.Hk, self.scale,
                             commit_len=meta.commit_len)
         if save is not None:        # speculative verify: keep inputs for the commit pass
@@ -370,7 +373,8 @@ class HybridModel:
         return h
 
     def forward(self, input_ids: torch.Tensor, meta: StepMeta, caches: ModelCaches,
-                aux_layers: Optional[list] = None, aux_out: Optional[list] = None) -> torch.Tensor:
+                aux_layers: Optional[list] = None, aux_out: Optional[list] = None,
+                gdn_save: Optional[list] = None) -> torch.Tensor:
         """Returns final-normed hidden states [T, H] bf16.  When `aux_layers` is given, the
         residual stream after each listed layer is appended to `aux_out` (drafter conditioning)."""
         cfg = self.cfg
@@ -391,7 +395,7 @@ class HybridModel:
                 h = layer.mixer.forward(a_in, meta, caches.k[ai], caches.v[ai])
                 ai += 1
             else:
-                h = layer.mixer.forward(a_in, meta, caches.conv[gi], caches.ssm[gi])
+                h = layer.mixer.forward(a_in, meta, caches.conv[gi], caches.ssm[gi], save=gdn_save)
                 gi += 1
             h = self._reduce(h)
             if quant:
@@ -405,6 +409,16 @@ class HybridModel:
                 aux_out.append((h.float() + residual.float()).to(torch.bfloat16))
         out, _ = K.add_rms_norm(h, residual, self.final_norm, eps, want_residual=False)
         return out
+
+    def commit_gdn(self, meta: StepMeta, caches: ModelCaches, saved: list,
+                   commit_len: torch.Tensor):
+        """Speculative verify: apply the accepted prefix (commit_len[b] tokens, -1 = skip row) of
+        each sequence to the GDN conv / SSM state, from the inputs saved during the verify pass."""
+        gi = 0
+        for layer in self.layers:
+            if not layer.is_attn:
+                layer.mixer.commit(saved[gi], meta, caches.conv[gi], caches.ssm[gi], commit_len)
+                gi += 1
 
     def logits(self, hidden: torch.Tensor) -> torch.Tensor:
         """[n, H] -> [n, V] bf16 (vocab-parallel shards gathered when TP > 1)."""

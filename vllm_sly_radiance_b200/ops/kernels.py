@@ -44,6 +44,20 @@ def check_status(device, reset: bool = True) -> int:
     return code
 
 
+_WS: dict = {}
+
+
+def workspace(device, name: str, numel: int) -> torch.Tensor:
+    """Zero-initialised int32 workspace shared by launches of one kernel family (counters in it
+    are self-resetting).  Grown on demand outside CUDA-graph capture."""
+    key = (str(device), name)
+    t = _WS.get(key)
+    if t is None or t.numel() < numel:
+        t = torch.zeros(max(numel, 1 << 16), dtype=torch.int32, device=device)
+        _WS[key] = t
+    return t
+
+
 def _none(t, device):
     return t if t is not None else _empty(device)
 
@@ -217,16 +231,19 @@ def paged_attention(q, k_cache, v_cache, meta, scale: float, causal: bool = True
         part_o = part_ml = _empty(q.device)
     ext().paged_attention(q, k_cache, v_cache, meta.block_tables, meta.seq_lens,
                           meta.query_start_loc, meta.tile_seq, meta.tile_row0, scale, causal,
-                          window, splits, part_o, part_ml, out)
+                          window, splits, part_o, part_ml, out,
+                          workspace(q.device, "attn", meta.tile_seq.shape[0] * k_cache.shape[1]))
     return out
 
 
 # ---------------------------------------------------------------------------------------------
 # gated delta net
 # ---------------------------------------------------------------------------------------------
-def gdn_conv(x, conv_w, conv_state, meta, qk_dim: int, head_dim: int, eps: float = 1e-6):
+def gdn_conv(x, conv_w, conv_state, meta, qk_dim: int, head_dim: int, eps: float = 1e-6,
+             update_state: bool = False):
     """x [T, conv_dim] (pre-conv q|k|v) -> y [T, conv_dim] bf16 (SiLU, q/k L2-normed).
-    The conv state is NOT updated here (gdn_conv_state_update does it)."""
+    update_state (only valid when every sequence feeds exactly one token) also shifts the conv
+    state in place; otherwise gdn_conv_state_update does it in a second launch."""
     T, C = x.shape[0], conv_w.shape[0]
     if not x.is_cuda:
         y = torch.empty(T, C, dtype=torch.bfloat16)
@@ -243,11 +260,13 @@ def gdn_conv(x, conv_w, conv_state, meta, qk_dim: int, head_dim: int, eps: float
                 sl = slice(hh * head_dim, (hh + 1) * head_dim)
                 yy[:, sl] = ref.l2norm(yy[:, sl])
             y[s0:s1] = yy.to(torch.bfloat16)
+        if update_state:
+            gdn_conv_state_update(x, conv_state, meta)
         return y
     y = torch.empty(T, C, dtype=torch.bfloat16, device=x.device)
     # the kernel L2-normalises the first `2 * qk_dim` channels (q and k heads)
     ext().gdn_conv(x, conv_w, conv_state, meta.query_start_loc, meta.state_slots,
-                   meta.has_initial, meta.token_seq, 2 * qk_dim, head_dim, y, eps)
+                   meta.has_initial, meta.token_seq, 2 * qk_dim, head_dim, y, eps, update_state)
     return y
 
 
@@ -258,6 +277,8 @@ def gdn_conv_state_update(x, conv_state, meta, commit_len: Optional[torch.Tensor
         for b in range(meta.num_seqs):
             s0, s1 = int(qsl[b]), int(qsl[b + 1])
             n = int(commit_len[b]) if commit_len is not None else s1 - s0
+            if n < 0:
+                continue
             slot = int(meta.state_slots[b])
             st = conv_state[slot].float() if int(meta.has_initial[b]) else \
                 torch.zeros(C, conv_state.shape[2])
@@ -290,6 +311,8 @@ def gdn_recurrent(y, ba, A_log, dt_bias, ssm_state, meta, num_k_heads: int, scal
             v = y[s0:s1, 2 * key_dim:2 * key_dim + Hv * DV].float().view(-1, Hv, DV)
             g, beta = ref.gdn_gates(ba[s0:s1, Hv:2 * Hv], ba[s0:s1, :Hv], A_log, dt_bias)
             n = int(commit_len[b]) if commit_len is not None else s1 - s0
+            if n < 0:
+                continue
             o, _ = ref.gdn_recurrent(q, k, v, g, beta, st, scale)
             _, st_c = ref.gdn_recurrent(q[:n], k[:n], v[:n], g[:n], beta[:n], st, scale)
             ssm_state[slot] = st_c.to(ssm_state.dtype)
@@ -309,7 +332,8 @@ def argmax(logits: torch.Tensor) -> torch.Tensor:
     if not logits.is_cuda:
         return logits.float().argmax(-1)
     ids = torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device)
-    ext().argmax_rows(logits, ids, _empty(logits.device))
+    ext().argmax_rows(logits, ids, _empty(logits.device), workspace(logits.device, "argmax",
+                                                                     logits.shape[0] * 129))
     return ids
 
 
