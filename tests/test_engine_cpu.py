@@ -110,3 +110,27 @@ def test_engine_generate_stop_and_abort():
     assert not eng.has_unfinished_requests()
     outs = eng.generate([list(range(20))], SamplingParams(temperature=0, max_tokens=3))
     assert len(outs[0].outputs[0].token_ids) == 3 and outs[0].outputs[0].finish_reason == "length"
+
+
+def test_kv4_cache_engine_and_capacity():
+    """4-bit KV cache (int4 + fp16 scale/zero per 16 elements, 16-token pages): the engine runs,
+    logits stay close to the fp8-KV engine, and a page holds more tokens per byte."""
+    from vllm_sly_radiance_b200.models.hybrid import HybridModel
+    from vllm_sly_radiance_b200.config import tiny_hybrid
+    prompt = list(range(5, 105))
+
+    def run(kv):
+        cfg = EngineConfig(model="tiny_hybrid", device="cpu", max_model_len=1024, max_num_seqs=4,
+                           max_num_batched_tokens=48, num_kv_blocks=64, kv_cache_dtype=kv,
+                           quantization="bf16")
+        eng = LLMEngine(cfg)
+        return _prefill_logits(eng, prompt), eng
+    a, e4 = run("int4")
+    b, e8 = run("bf16")
+    assert e4.config.block_size == 16
+    rel = float((a - b).norm() / b.norm())
+    assert rel < 0.1, rel
+    m = e4.model
+    per_tok4 = m.cache_bytes_per_block(16, "int4") / 16
+    per_tok8 = m.cache_bytes_per_block(64, "fp8") / 64
+    assert per_tok4 < per_tok8

@@ -140,6 +140,9 @@ def _attn_meta(q_lens, ctx_lens, block_size, Hq, Hkv, num_splits, dev):
     (256, 24, 4, [8, 8], [500, 1200], 4, True),
     (256, 24, 4, [200, 70], [0, 130], 1, True),
     (64, 4, 2, [33, 1], [0, 90], 1, False),
+    (64, 4, 2, [1, 1, 1, 1], [130, 62, 10, 0], 5, True),
+    (64, 4, 2, [64, 22], [64, 128], 1, True),
+    (64, 4, 2, [1, 1], [200, 70], 3, False),
     (128, 32, 8, [8], [250], 2, True)])
 def test_paged_attention(D, Hq, Hkv, q_lens, ctx_lens, splits, fp8):
     torch.manual_seed(0)
@@ -257,3 +260,27 @@ def test_argmax_and_sampling():
     # probabilities of the kept window sum to one for sampled rows
     for b in (1, 2, 4):
         assert abs(float(probs[b].sum()) - 1.0) < 1e-4
+
+
+@pytest.mark.parametrize("D,Hq,Hkv,splits", [(64, 4, 2, 5), (256, 24, 4, 8)])
+def test_paged_attention_split_repeated(D, Hq, Hkv, splits):
+    """Back-to-back split-KV launches on the same metadata (as in CUDA-graph replays): the
+    in-kernel merge counters reset and no partial of a previous launch leaks into the next."""
+    torch.manual_seed(5)
+    bs = 64
+    q_lens, ctx = [1, 1, 1, 1], [121, 55, 10, 0]
+    meta, nblocks = _attn_meta(q_lens, ctx, bs, Hq, Hkv, splits, DEV)
+    kc = (torch.randn(nblocks, Hkv, bs, D) * 0.5).to(torch.float8_e4m3fn)
+    vc = torch.randn(nblocks, Hkv, bs, D).to(torch.float8_e4m3fn)
+    metac = _Meta()
+    metac.block_tables = meta.block_tables.cpu()
+    metac.seq_lens = meta.seq_lens.cpu()
+    metac.query_start_loc = meta.query_start_loc.cpu()
+    kg, vg = kc.to(DEV), vc.to(DEV)
+    for it in range(4):
+        q = ref.fp8_e4m3(torch.randn(4, Hq, D)).to(torch.bfloat16)
+        want = ref.paged_attention(q, kc, vc, metac.block_tables, metac.seq_lens,
+                                   metac.query_start_loc, bs, D ** -0.5)
+        got = K.paged_attention(q.to(DEV), kg, vg, meta, D ** -0.5)
+        torch.cuda.synchronize()
+        assert rel_err(got, want) < 2e-2, (it, rel_err(got, want))

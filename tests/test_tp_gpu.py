@@ -1,0 +1,95 @@
+"""Tensor parallelism on 2 GPUs (NCCL + the NVLink one-shot all-reduce).  Child processes, NVLS
+off, a short process-group timeout, and every rank runs the same collectives in the same order.
+Skipped when fewer than 2 GPUs are visible."""
+import os
+import socket
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    from vllm_sly_radiance_b200.config import EngineConfig, tiny_hybrid
+    from vllm_sly_radiance_b200.engine.llm_engine import LLMEngine
+    from vllm_sly_radiance_b200.engine.request import SamplingParams
+    from vllm_sly_radiance_b200.models.hybrid import HybridModel
+    from vllm_sly_radiance_b200.ops import kernels as K
+    from vllm_sly_radiance_b200.parallel.comm import make_tp_info
+    out = {}
+    # 1) the NVLink all-reduce (plain and fused) vs NCCL
+    tp = make_tp_info(rank, world, "fused")
+    torch.manual_seed(rank)
+    for M in (1, 8, 64):
+        x = torch.randn(M, 256, device="cuda").to(torch.bfloat16)
+        ref = x.float().clone()
+        dist.all_reduce(ref)
+        got = tp.all_reduce(x.clone())
+        out[f"ar{M}"] = float((got.float() - ref).abs().max())
+        res = torch.randn(M, 256, device="cuda").to(torch.bfloat16)
+        w = (0.1 * torch.randn(256, device="cuda")).to(torch.bfloat16)
+        q, s, r = tp.all_reduce_add_rms_quant(x.clone(), res, w, 1e-6)
+        q2, s2, r2 = K.add_rms_quant(ref.to(torch.bfloat16), res, w, 1e-6)
+        out[f"arq{M}"] = float(((q.float() * s[:, None]) - (q2.float() * s2[:, None])).abs().max())
+    K.check_status(torch.device("cuda", rank))
+    # 2) TP=2 tiny model (fused path) vs single-GPU logits
+    cfg = EngineConfig(model="tiny_hybrid", device="cuda", max_model_len=512, max_num_seqs=2,
+                       max_num_batched_tokens=128, num_kv_blocks=32, enable_cuda_graphs=True)
+    m = HybridModel(tiny_hybrid(), quant="mxfp4", device="cuda", seed=0, tp=tp, init_device="cpu")
+    eng = LLMEngine(cfg, model=m, tp=tp)
+    o = eng.generate([list(range(40, 100))], SamplingParams(temperature=0, max_tokens=6,
+                                                             ignore_eos=True))
+    out["toks"] = o[0].outputs[0].token_ids
+    eng.runner.graphs.clear()
+    tp.fused.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    if rank == 0:
+        q.put(out)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tp2_fused_allreduce_and_model():
+    import torch.multiprocessing as mp
+    from vllm_sly_radiance_b200.config import EngineConfig
+    from vllm_sly_radiance_b200.engine.llm_engine import LLMEngine
+    from vllm_sly_radiance_b200.engine.request import SamplingParams
+    from vllm_sly_radiance_b200.config import tiny_hybrid
+    from vllm_sly_radiance_b200.models.hybrid import HybridModel
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = q.get(timeout=600)
+    for p in ps:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for M in (1, 8, 64):
+        assert res[f"ar{M}"] < 0.05, res
+        assert res[f"arq{M}"] < 0.25, res
+    cfg = EngineConfig(model="tiny_hybrid", device="cuda", max_model_len=512, max_num_seqs=2,
+                       max_num_batched_tokens=128, num_kv_blocks=32)
+    m = HybridModel(tiny_hybrid(), quant="mxfp4", device="cuda", seed=0, init_device="cpu")
+    ref = LLMEngine(cfg, model=m).generate([list(range(40, 100))],
+                                          SamplingParams(temperature=0, max_tokens=6, ignore_eos=True))
+    assert res["toks"][:2] == ref[0].outputs[0].token_ids[:2]

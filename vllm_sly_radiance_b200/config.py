@@ -296,6 +296,9 @@ class EngineConfig:
             raise ValueError(f"kv_cache_dtype {self.kv_cache_dtype!r} not supported")
         if self.acceptance_rule not in ("leviathan", "cactus", "nsd"):
             raise ValueError(f"acceptance_rule {self.acceptance_rule!r} not supported")
+        if self.kv_cache_dtype == "int4":
+            # 4-bit KV pages hold 16 tokens (per-16-element fp16 scale/zero per head)
+            self.block_size = 16
 
     def model_config(self) -> ModelConfig:
         return get_model_config(self.model)

@@ -19,6 +19,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cuda_fp16.h>
+
 #include "common.cuh"
 
 namespace rad {
@@ -34,7 +36,9 @@ __global__ void __launch_bounds__(256) qkv_prologue_kernel(
     const __nv_bfloat16* __restrict__ qn_w, const __nv_bfloat16* __restrict__ kn_w,
     const float* __restrict__ cos_sin, int rot, int T, int Hq, int Hkv, float eps,
     __nv_bfloat16* __restrict__ q_out, uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache,
-    int cache_fp8, const int64_t* __restrict__ slot_mapping, int block_size) {
+    int cache_fmt, const int64_t* __restrict__ slot_mapping, int block_size) {
+  // cache_fmt: 0 bf16, 1 fp8 e4m3, 2 int4 (+ fp16 scale/zero per 16 elements)
+  const int cache_fp8 = cache_fmt == 1;
   pdl_wait();     // inputs come from the preceding kernel
   pdl_trigger();
   constexpr int PER = D / 32;
@@ -79,7 +83,7 @@ __global__ void __launch_bounds__(256) qkv_prologue_kernel(
 #pragma unroll
     for (int p = 0; p < PER; ++p) {
       float v = bf16_round(x[p]);
-      if (cache_fp8) v = e4m3_to_f32(f32_to_e4m3(v));
+      if (cache_fmt == 1) v = e4m3_to_f32(f32_to_e4m3(v));
       dst[lane * PER + p] = __float2bfloat16_rn(v);
     }
   } else {
@@ -87,8 +91,53 @@ __global__ void __launch_bounds__(256) qkv_prologue_kernel(
     const int64_t slot = slot_mapping[t];
     if (slot < 0) return;
     const int64_t blk = slot / block_size, off2 = slot % block_size;
-    const size_t base = (((size_t)blk * Hkv + hk) * block_size + off2) * D;
     const __nv_bfloat16* vsrc = qkv + (size_t)t * ldqkv + v_off + hk * D;
+    if (cache_fmt == 2) {
+      // 4-bit rows: [D/2 nibble bytes][D/16 x (fp16 scale, fp16 zero)]
+      constexpr int RB = D / 2 + D / 4;
+      constexpr int LPG = 16 / PER;                 // lanes per 16-element group
+      const size_t row = (((size_t)blk * Hkv + hk) * block_size + off2) * RB;
+      float vv[PER];
+#pragma unroll
+      for (int p = 0; p < PER; ++p) vv[p] = __bfloat162float(vsrc[lane * PER + p]);
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        float* xs = which == 0 ? x : vv;
+        uint8_t* dst = (which == 0 ? k_cache : v_cache) + row;
+        float lo = 1e30f, hi = -1e30f;
+#pragma unroll
+        for (int p = 0; p < PER; ++p) {
+          const float e = which == 0 ? bf16_round(xs[p]) : xs[p];
+          lo = fminf(lo, e);
+          hi = fmaxf(hi, e);
+        }
+#pragma unroll
+        for (int o = 1; o < LPG; o <<= 1) {
+          lo = fminf(lo, __shfl_xor_sync(0xffffffff, lo, o));
+          hi = fmaxf(hi, __shfl_xor_sync(0xffffffff, hi, o));
+        }
+        float sc = (hi - lo) / 15.f;
+        if (!(sc > 0.f)) sc = 1.f;
+        const __half sc16 = __float2half_rn(sc), lo16 = __float2half_rn(lo);
+        const float scf = __half2float(sc16), lof = __half2float(lo16);
+        uint32_t packed = 0;
+#pragma unroll
+        for (int p = 0; p < PER; ++p) {
+          const float e = which == 0 ? bf16_round(xs[p]) : xs[p];
+          const int qv = min(15, max(0, __float2int_rn((e - lof) / scf)));
+          packed |= (uint32_t)qv << (4 * p);
+        }
+#pragma unroll
+        for (int b = 0; b < PER / 2; ++b) dst[lane * PER / 2 + b] = (uint8_t)(packed >> (8 * b));
+        if ((lane % LPG) == 0) {
+          const int gi = lane / LPG;
+          __half2 m = __halves2half2(sc16, lo16);
+          *reinterpret_cast<__half2*>(dst + D / 2 + gi * 4) = m;
+        }
+      }
+      return;
+    }
+    const size_t base = (((size_t)blk * Hkv + hk) * block_size + off2) * D;
     if (cache_fp8) {
 #pragma unroll
       for (int p = 0; p < PER; ++p) {
@@ -138,7 +187,7 @@ DEVI uint32_t pack_bf16(float a, float b) {
 // swizzled byte offset of (row, 16-byte chunk) in a tile with `chunks` chunks per row
 DEVI uint32_t swz(int row, int chunk, int chunks) { return (uint32_t)(row * chunks + (chunk ^ (row & 7))) * 16u; }
 
-template <int D, bool FP8>
+template <int D, int FMT>
 __global__ void __launch_bounds__(128) paged_attn_kernel(
     const __nv_bfloat16* __restrict__ q, const uint8_t* __restrict__ k_cache,
     const uint8_t* __restrict__ v_cache, const int* __restrict__ block_tables, int bt_stride,
@@ -207,15 +256,20 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(
 
   for (int kt = t_lo; kt < t_hi; ++kt) {
     __syncthreads();
-    // ---- load K/V page kt (fp8 -> bf16 or bf16 copy) ----
-    const int blk = block_tables[(size_t)b * bt_stride + (kt * BC) / block_size];
-    const int in_blk = (kt * BC) % block_size;
-    const size_t base = (((size_t)blk * Hkv + hk) * block_size + in_blk) * D;
-    if constexpr (FP8) {
+    // ---- load K/V tile kt (64 keys; pages of block_size tokens, any size dividing 64 or a
+    //      multiple of 64), converting fp8 / int4 to bf16 in shared memory ----
+    const int key0 = kt * BC;
+    if constexpr (FMT == 1) {
       for (int idx = threadIdx.x; idx < BC * D / 16; idx += 128) {
         const int r = idx / (D / 16), c16 = idx % (D / 16);   // 16 fp8 = two bf16 chunks
-        uint4 kv = *reinterpret_cast<const uint4*>(k_cache + base + (size_t)r * D + c16 * 16);
-        uint4 vv = *reinterpret_cast<const uint4*>(v_cache + base + (size_t)r * D + c16 * 16);
+        const int key = key0 + r;
+        uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+        if (key < L) {
+          const int blk = block_tables[(size_t)b * bt_stride + key / block_size];
+          const size_t base = (((size_t)blk * Hkv + hk) * block_size + key % block_size) * D;
+          kv = *reinterpret_cast<const uint4*>(k_cache + base + c16 * 16);
+          vv = *reinterpret_cast<const uint4*>(v_cache + base + c16 * 16);
+        }
         const uint8_t* kb = reinterpret_cast<const uint8_t*>(&kv);
         const uint8_t* vb = reinterpret_cast<const uint8_t*>(&vv);
         uint32_t kw[8], vw[8];
@@ -229,13 +283,56 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(
         *reinterpret_cast<uint4*>(sV + swz(r, 2 * c16, CH)) = make_uint4(vw[0], vw[1], vw[2], vw[3]);
         *reinterpret_cast<uint4*>(sV + swz(r, 2 * c16 + 1, CH)) = make_uint4(vw[4], vw[5], vw[6], vw[7]);
       }
+    } else if constexpr (FMT == 2) {
+      constexpr int RB = D / 2 + D / 4;
+      for (int idx = threadIdx.x; idx < BC * D / 16; idx += 128) {
+        const int r = idx / (D / 16), g = idx % (D / 16);     // one 16-element group
+        const int key = key0 + r;
+        uint32_t kw[8], vw[8];
+        if (key < L) {
+          const int blk = block_tables[(size_t)b * bt_stride + key / block_size];
+          const size_t row = (((size_t)blk * Hkv + hk) * block_size + key % block_size) * RB;
+#pragma unroll
+          for (int which = 0; which < 2; ++which) {
+            const uint8_t* src = (which == 0 ? k_cache : v_cache) + row;
+            const uint2 nib = *reinterpret_cast<const uint2*>(src + g * 8);
+            const __half2 m = *reinterpret_cast<const __half2*>(src + D / 2 + g * 4);
+            const float sc = __low2float(m), zr = __high2float(m);
+            uint32_t* w = which == 0 ? kw : vw;
+            const uint32_t lo32 = nib.x, hi32 = nib.y;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const uint32_t word = e < 4 ? lo32 : hi32;
+              const int sh = (e % 4) * 8;
+              const float a = (float)((word >> sh) & 0xF) * sc + zr;
+              const float c = (float)((word >> (sh + 4)) & 0xF) * sc + zr;
+              w[e] = pack_bf16(a, c);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) kw[e] = vw[e] = 0u;
+        }
+        *reinterpret_cast<uint4*>(sK + swz(r, 2 * g, CH)) = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+        *reinterpret_cast<uint4*>(sK + swz(r, 2 * g + 1, CH)) = make_uint4(kw[4], kw[5], kw[6], kw[7]);
+        *reinterpret_cast<uint4*>(sV + swz(r, 2 * g, CH)) = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+        *reinterpret_cast<uint4*>(sV + swz(r, 2 * g + 1, CH)) = make_uint4(vw[4], vw[5], vw[6], vw[7]);
+      }
     } else {
       const __nv_bfloat16* kc = reinterpret_cast<const __nv_bfloat16*>(k_cache);
       const __nv_bfloat16* vc = reinterpret_cast<const __nv_bfloat16*>(v_cache);
       for (int idx = threadIdx.x; idx < BC * CH; idx += 128) {
         const int r = idx / CH, c = idx % CH;
-        *reinterpret_cast<uint4*>(sK + swz(r, c, CH)) = *reinterpret_cast<const uint4*>(kc + base + (size_t)r * D + c * 8);
-        *reinterpret_cast<uint4*>(sV + swz(r, c, CH)) = *reinterpret_cast<const uint4*>(vc + base + (size_t)r * D + c * 8);
+        const int key = key0 + r;
+        uint4 kx = make_uint4(0, 0, 0, 0), vx = make_uint4(0, 0, 0, 0);
+        if (key < L) {
+          const int blk = block_tables[(size_t)b * bt_stride + key / block_size];
+          const size_t base = (((size_t)blk * Hkv + hk) * block_size + key % block_size) * D;
+          kx = *reinterpret_cast<const uint4*>(kc + base + c * 8);
+          vx = *reinterpret_cast<const uint4*>(vc + base + c * 8);
+        }
+        *reinterpret_cast<uint4*>(sK + swz(r, c, CH)) = kx;
+        *reinterpret_cast<uint4*>(sV + swz(r, c, CH)) = vx;
       }
     }
     __syncthreads();
@@ -365,10 +462,11 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(
     }
   }
   if (num_splits > 1) {
-    // the last split CTA of this (row tile, kv head) merges all splits' partials
+    // the last split CTA of this (row tile, kv head) merges all splits' partials; every thread
+    // fences its own partial stores before the arrival is counted
+    __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
-      __threadfence();
       s_last = atomicAdd(&counters[tile * Hkv + hk], 1u) == (unsigned)(num_splits - 1);
     }
     __syncthreads();
@@ -453,7 +551,8 @@ void qkv_prologue(torch::Tensor qkv, int64_t q_head_stride, int64_t k_off, int64
   if (T == 0) return;
   const int D = q_out.size(2);
   const int block_size = k_cache.size(2);
-  const bool fp8 = k_cache.scalar_type() == at::kFloat8_e4m3fn;
+  const int fmt = k_cache.scalar_type() == at::kFloat8_e4m3fn ? 1
+                : k_cache.scalar_type() == at::kByte ? 2 : 0;
   TORCH_CHECK(positions.scalar_type() == at::kInt && slot_mapping.scalar_type() == at::kLong, "index dtypes");
   TORCH_CHECK(((rot / 2) % (D / 32)) == 0, "rotary dim / lanes");
   const at::cuda::CUDAGuard guard(qkv.device());
@@ -467,7 +566,7 @@ C10_CUDA_CHECK(launch_pdl((attn::qkv_prologue_kernel<Dc>), dim3(grid), dim3(256)
         positions.data_ptr<int>(), (const __nv_bfloat16*)qn_w.data_ptr(),
         (const __nv_bfloat16*)kn_w.data_ptr(), cos_sin.data_ptr<float>(), rot, T, Hq, Hkv,
         (float)eps, (__nv_bfloat16*)q_out.data_ptr(), (uint8_t*)k_cache.data_ptr(),
-        (uint8_t*)v_cache.data_ptr(), fp8 ? 1 : 0, slot_mapping.data_ptr<int64_t>(), block_size));
+        (uint8_t*)v_cache.data_ptr(), fmt, slot_mapping.data_ptr<int64_t>(), block_size));
   };
   if (D == 256) run(std::integral_constant<int, 256>{});
   else if (D == 128) run(std::integral_constant<int, 128>{});
@@ -487,16 +586,18 @@ void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
   const int Hkv = k_cache.size(1), block_size = k_cache.size(2);
   const int num_tiles = tile_seq.size(0);
   if (T == 0 || num_tiles == 0) return;
-  TORCH_CHECK(block_size % attn::BC == 0, "KV page size must be a multiple of 64");
+  TORCH_CHECK(block_size % attn::BC == 0 || attn::BC % block_size == 0,
+              "KV page size must divide or be a multiple of 64");
   TORCH_CHECK(num_splits >= 1, "num_splits");
-  const bool fp8 = k_cache.scalar_type() == at::kFloat8_e4m3fn;
+  const int fmt = k_cache.scalar_type() == at::kFloat8_e4m3fn ? 1
+                : k_cache.scalar_type() == at::kByte ? 2 : 0;
   const at::cuda::CUDAGuard guard(q.device());
   auto stream = at::cuda::getCurrentCUDAStream();
   const float scale_log2 = (float)(scale * 1.4426950408889634);
   dim3 grid(num_tiles, Hkv, num_splits);
   auto run = [&](auto dtag, auto ftag) {
     constexpr int Dc = decltype(dtag)::value;
-    constexpr bool F8 = decltype(ftag)::value;
+    constexpr int F8 = decltype(ftag)::value;
     const int smem = (attn::BR + 2 * attn::BC) * Dc * 2;
     auto kern = attn::paged_attn_kernel<Dc, F8>;
     static bool set = false;
@@ -514,18 +615,15 @@ C10_CUDA_CHECK(launch_pdl(    kern, dim3(grid), dim3(128), smem, stream,
         num_splits > 1 ? part_ml.data_ptr<float>() : nullptr, T,
         num_splits > 1 ? reinterpret_cast<unsigned*>(counters.data_ptr()) : nullptr));
   };
-  if (D == 256) {
-    if (fp8) run(std::integral_constant<int, 256>{}, std::true_type{});
-    else run(std::integral_constant<int, 256>{}, std::false_type{});
-  } else if (D == 128) {
-    if (fp8) run(std::integral_constant<int, 128>{}, std::true_type{});
-    else run(std::integral_constant<int, 128>{}, std::false_type{});
-  } else if (D == 64) {
-    if (fp8) run(std::integral_constant<int, 64>{}, std::true_type{});
-    else run(std::integral_constant<int, 64>{}, std::false_type{});
-  } else {
-    TORCH_CHECK(false, "paged_attention: head_dim 64/128/256");
-  }
+  auto by_fmt = [&](auto dtag) {
+    if (fmt == 1) run(dtag, std::integral_constant<int, 1>{});
+    else if (fmt == 2) run(dtag, std::integral_constant<int, 2>{});
+    else run(dtag, std::integral_constant<int, 0>{});
+  };
+  if (D == 256) by_fmt(std::integral_constant<int, 256>{});
+  else if (D == 128) by_fmt(std::integral_constant<int, 128>{});
+  else if (D == 64) by_fmt(std::integral_constant<int, 64>{});
+  else TORCH_CHECK(false, "paged_attention: head_dim 64/128/256");
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -16,7 +16,7 @@
 //    buffering keeps a fast rank from overwriting a slot a slow peer still reads.
 //  * Fused epilogue variant: rows are owned whole by one CTA, so the reduced row goes straight
 //    through residual add + RMSNorm(1+w) + per-row e4m3 quant (the producer of the next linear).
-//  * Plain loads/stores to peer memory only (no TMA, no multicast).
+//  * Plain loads and stores to peer memory only; no bulk-copy engine touches a peer address.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>

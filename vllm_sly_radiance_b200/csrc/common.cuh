@@ -345,7 +345,17 @@ DEVI void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "
 
 #ifndef __CUDACC_RTC__
 #include <cuda_runtime.h>
+#include <cstdlib>
+#include <cstring>
 namespace rad {
+// RADIANCE_PDL=0 launches every kernel without programmatic dependencies (A/B switch)
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("RADIANCE_PDL");
+    return !(v && std::strcmp(v, "0") == 0);
+  }();
+  return on;
+}
 // Launch with the programmatic-stream-serialization attribute: the kernel may start while its
 // predecessor drains; every kernel of this library calls pdl_wait() before reading the
 // predecessor's outputs.
@@ -361,7 +371,7 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 }  // namespace rad

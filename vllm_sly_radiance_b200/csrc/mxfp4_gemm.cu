@@ -346,7 +346,7 @@ static void launch(const torch::Tensor& a, const torch::Tensor& a_scale, const t
   attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attrs[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tw, ta, (const uint8_t*)sf.data_ptr(),
                                     (const float*)a_scale.data_ptr(),
                                     (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), M, N, K,

@@ -62,6 +62,7 @@ __global__ void __launch_bounds__(256) argmax_kernel(const TIn* __restrict__ x, 
     __threadfence();
     last = atomicAdd(&counters[row], 1u) == (unsigned)(nch - 1);
   }
+  // (counters are per row at fixed offsets; the last CTA of the row resets its counter)
   __syncthreads();
   if (!last) return;
   __threadfence();
@@ -175,10 +176,12 @@ void argmax_rows(torch::Tensor x, torch::Tensor out_ids, torch::Tensor out_vals,
   float* vp = out_vals.defined() && out_vals.numel() ? out_vals.data_ptr<float>() : nullptr;
   const int nch = std::max(1, std::min(64, (V + 4095) / 4096));
   const int chunk = (V + nch - 1) / nch;
-  TORCH_CHECK(workspace.numel() * 4 >= (int64_t)B * (64 * 2 + 1) * 4, "argmax workspace too small");
-  float* pv = reinterpret_cast<float*>(workspace.data_ptr());
+  // fixed layout independent of B (counters must stay zero between launches of any batch size):
+  // [0, 4096) arrival counters, then values and indices of up to 64 chunks per row
+  TORCH_CHECK(B <= 4096 && workspace.numel() >= 4096 + (int64_t)B * 64 * 2, "argmax workspace too small");
+  unsigned* cnt = reinterpret_cast<unsigned*>(workspace.data_ptr());
+  float* pv = reinterpret_cast<float*>(cnt + 4096);
   int* pi = reinterpret_cast<int*>(pv + B * 64);
-  unsigned* cnt = reinterpret_cast<unsigned*>(pi + B * 64);
   dim3 grid(nch, B);
   if (x.scalar_type() == at::kFloat)
     C10_CUDA_CHECK(launch_pdl((smp::argmax_kernel<float>), grid, dim3(256), 0, stream,

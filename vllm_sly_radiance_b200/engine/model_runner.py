@@ -85,6 +85,7 @@ class ModelRunner:
         self.graph_pool = None
         self.last_timing = {}
         self._scratch: dict = {}
+        self._h2d_event = None
 
     # ------------------------------------------------------------------------------------------
     # metadata
@@ -116,6 +117,10 @@ class ModelRunner:
         bucket of pure decode rows (1 token each).  Returns (meta, input_ids view, sample index,
         per-seq sample counts)."""
         L = self.L
+        # the pinned staging buffers are reused: the previous asynchronous upload must have
+        # finished reading them before they are overwritten
+        if self._h2d_event is not None:
+            self._h2d_event.synchronize()
         h = self.h_meta.numpy()
         hs = self.h_slots.numpy()
         seqs = out.seqs
@@ -201,6 +206,8 @@ class ModelRunner:
         if self.device.type == "cuda":
             self.d_meta[:end].copy_(self.h_meta[:end], non_blocking=True)
             self.d_slots[:T].copy_(self.h_slots[:T], non_blocking=True)
+            self._h2d_event = torch.cuda.Event()
+            self._h2d_event.record()
         else:
             self.d_meta[:end].copy_(self.h_meta[:end])
             self.d_slots[:T].copy_(self.h_slots[:T])

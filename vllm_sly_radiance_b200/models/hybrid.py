@@ -26,6 +26,7 @@ import torch
 
 from ..config import ModelConfig
 from ..ops import kernels as K
+from ..quant.formats import kv4_row_bytes
 from ..quant.mxfp4 import MXFP4Weight
 from .layers import Linear, rope_cache
 from .weights import RandomWeights, cat_rows, slice_cols, slice_rows
@@ -93,6 +94,8 @@ class TPInfo:
     size: int = 1
     all_reduce: Optional[Callable[[torch.Tensor], torch.Tensor]] = None
     all_gather_last: Optional[Callable[[torch.Tensor], torch.Tensor]] = None
+    # fused all-reduce + residual add + RMSNorm + e4m3 quant (NVLink kernel); None = unfused
+    all_reduce_add_rms_quant: Optional[Callable] = None
 
     def shard(self, n: int) -> tuple[int, int]:
         assert n % self.size == 0, (n, self.size)
@@ -334,15 +337,16 @@ class HybridModel:
     def make_caches(self, num_blocks: int, block_size: int, num_slots: int,
                     kv_dtype: str = "fp8", ssm_dtype: str = "float32") -> ModelCaches:
         cfg = self.cfg
-        kdt = {"fp8": torch.float8_e4m3fn, "bf16": torch.bfloat16}[kv_dtype]
+        kdt = {"fp8": torch.float8_e4m3fn, "bf16": torch.bfloat16, "int4": torch.uint8}[kv_dtype]
         sdt = {"float32": torch.float32, "bfloat16": torch.bfloat16}[ssm_dtype]
         ks, vs, convs, ssms = [], [], [], []
         for layer in self.layers:
             m = layer.mixer
             if layer.is_attn:
                 # zero-filled: stale pages never hold NaN bit patterns
-                ks.append(torch.zeros(num_blocks, m.Hkv, block_size, m.hd, dtype=kdt, device=self.device))
-                vs.append(torch.zeros(num_blocks, m.Hkv, block_size, m.hd, dtype=kdt, device=self.device))
+                row = kv4_row_bytes(m.hd) if kv_dtype == "int4" else m.hd
+                ks.append(torch.zeros(num_blocks, m.Hkv, block_size, row, dtype=kdt, device=self.device))
+                vs.append(torch.zeros(num_blocks, m.Hkv, block_size, row, dtype=kdt, device=self.device))
             else:
                 convs.append(torch.zeros(num_slots, m.conv_dim, cfg.gdn_conv_kernel - 1,
                                          dtype=torch.bfloat16, device=self.device))
@@ -350,11 +354,12 @@ class HybridModel:
         return ModelCaches(ks, vs, convs, ssms, block_size)
 
     def cache_bytes_per_block(self, block_size: int, kv_dtype: str = "fp8") -> int:
-        es = 1 if kv_dtype == "fp8" else 2
         n = 0
         for layer in self.layers:
             if layer.is_attn:
-                n += 2 * layer.mixer.Hkv * block_size * layer.mixer.hd * es
+                hd = layer.mixer.hd
+                row = {"fp8": hd, "bf16": 2 * hd, "int4": kv4_row_bytes(hd)}[kv_dtype]
+                n += 2 * layer.mixer.Hkv * block_size * row
         return n
 
     def state_bytes_per_slot(self, ssm_dtype: str = "float32") -> int:
@@ -384,8 +389,13 @@ class HybridModel:
         h = x
         ai = gi = 0
         quant = self.quant != "bf16"
+        fused_ar = self.tp.size > 1 and quant and self.tp.all_reduce_add_rms_quant is not None
+        pending = None          # (q, s) produced by a fused all-reduce epilogue for the next norm
         for li, layer in enumerate(self.layers):
-            if quant:
+            if pending is not None:
+                a_in = pending
+                pending = None
+            elif quant:
                 a_in = K.add_rms_quant(h, residual, layer.ln1, eps)
                 residual = a_in[2]
                 a_in = (a_in[0], a_in[1])
@@ -397,14 +407,24 @@ class HybridModel:
             else:
                 h = layer.mixer.forward(a_in, meta, caches.conv[gi], caches.ssm[gi], save=gdn_save)
                 gi += 1
-            h = self._reduce(h)
-            if quant:
-                q, s, residual = K.add_rms_quant(h, residual, layer.ln2, eps)
+            if fused_ar:
+                q, s, residual = self.tp.all_reduce_add_rms_quant(h, residual, layer.ln2, eps)
                 h = layer.mlp.forward((q, s))
             else:
-                n, residual = K.add_rms_norm(h, residual, layer.ln2, eps)
-                h = layer.mlp.forward(n)
-            h = self._reduce(h)
+                h = self._reduce(h)
+                if quant:
+                    q, s, residual = K.add_rms_quant(h, residual, layer.ln2, eps)
+                    h = layer.mlp.forward((q, s))
+                else:
+                    n, residual = K.add_rms_norm(h, residual, layer.ln2, eps)
+                    h = layer.mlp.forward(n)
+            if fused_ar and li + 1 < len(self.layers) and aux_layers is None:
+                nxt = self.layers[li + 1]
+                q, s, residual = self.tp.all_reduce_add_rms_quant(h, residual, nxt.ln1, eps)
+                pending = (q, s)
+                h = None
+            else:
+                h = self._reduce(h)
             if aux_layers is not None and li in aux_layers:
                 aux_out.append((h.float() + residual.float()).to(torch.bfloat16))
         out, _ = K.add_rms_norm(h, residual, self.final_norm, eps, want_residual=False)

@@ -333,7 +333,7 @@ def argmax(logits: torch.Tensor) -> torch.Tensor:
         return logits.float().argmax(-1)
     ids = torch.empty(logits.shape[0], dtype=torch.int64, device=logits.device)
     ext().argmax_rows(logits, ids, _empty(logits.device), workspace(logits.device, "argmax",
-                                                                     logits.shape[0] * 129))
+                                                                     4096 + logits.shape[0] * 128))
     return ids
 
 

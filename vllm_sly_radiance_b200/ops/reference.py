@@ -14,8 +14,8 @@ from typing import Optional
 import torch
 import torch.nn.functional as F
 
-from ..quant.formats import (FP8_MAX, FP8_SCALE_FLOOR, fp8_e4m3, mxfp4_dequantize,
-                             per_token_fp8)
+from ..quant.formats import (FP8_MAX, FP8_SCALE_FLOOR, fp8_e4m3, kv4_dequantize, kv4_quantize,
+                             mxfp4_dequantize, per_token_fp8)
 
 
 # ---------------------------------------------------------------------------------------------
@@ -145,10 +145,15 @@ def qkv_prologue(qkv: torch.Tensor, positions: torch.Tensor, q_norm_w, k_norm_w,
 # paged KV cache + attention
 # ---------------------------------------------------------------------------------------------
 def kv_cache_write(k, v, k_cache, v_cache, slot_mapping, block_size: int):
-    """k,v [T,Hkv,D]; caches [num_blocks, Hkv, block_size, D] (fp8 e4m3 or bf16)."""
+    """k,v [T,Hkv,D]; caches [num_blocks, Hkv, block_size, D] (fp8 e4m3 or bf16) or 4-bit rows
+    [num_blocks, Hkv, block_size, D/2 + D/4] (uint8)."""
+    keep = slot_mapping >= 0
+    k, v, slot_mapping = k[keep], v[keep], slot_mapping[keep]
     blk = slot_mapping // block_size
     off = slot_mapping % block_size
-    if k_cache.dtype == torch.float8_e4m3fn:
+    if k_cache.dtype == torch.uint8:
+        kq, vq = kv4_quantize(k.to(torch.bfloat16).float()), kv4_quantize(v.float())
+    elif k_cache.dtype == torch.float8_e4m3fn:
         kq, vq = fp8_e4m3(k.float()), fp8_e4m3(v.float())
     else:
         kq, vq = k.to(k_cache.dtype), v.to(v_cache.dtype)
@@ -156,10 +161,12 @@ def kv_cache_write(k, v, k_cache, v_cache, slot_mapping, block_size: int):
     v_cache[blk, :, off] = vq
 
 
-def gather_kv(cache, block_table, length: int, block_size: int):
+def gather_kv(cache, block_table, length: int, block_size: int, head_dim: int = 0):
     nb = (length + block_size - 1) // block_size
     blocks = cache[block_table[:nb].long()]                      # [nb, H, bs, D]
     x = blocks.permute(0, 2, 1, 3).reshape(nb * block_size, cache.shape[1], cache.shape[3])
+    if cache.dtype == torch.uint8:
+        return kv4_dequantize(x[:length], head_dim)
     return x[:length].float()
 
 
@@ -171,6 +178,7 @@ def paged_attention(q, k_cache, v_cache, block_tables, seq_lens, query_start_loc
     T, Hq, D = q.shape
     Hkv = k_cache.shape[1]
     group = Hq // Hkv
+    block_size = k_cache.shape[2]
     out = torch.zeros(T, Hq, D, dtype=torch.float32, device=q.device)
     qf = q.float()
     if k_cache.dtype == torch.float8_e4m3fn:
@@ -182,8 +190,8 @@ def paged_attention(q, k_cache, v_cache, block_tables, seq_lens, query_start_loc
         if ql == 0:
             continue
         L = int(seq_lens[b])
-        K = gather_kv(k_cache, block_tables[b], L, block_size)   # [L,Hkv,D]
-        V = gather_kv(v_cache, block_tables[b], L, block_size)
+        K = gather_kv(k_cache, block_tables[b], L, block_size, D)   # [L,Hkv,D]
+        V = gather_kv(v_cache, block_tables[b], L, block_size, D)
         Kr = K.repeat_interleave(group, dim=1)                    # [L,Hq,D]
         Vr = V.repeat_interleave(group, dim=1)
         qq = qf[s0:s1]                                            # [ql,Hq,D]

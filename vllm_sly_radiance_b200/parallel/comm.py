@@ -33,6 +33,8 @@ def make_tp_info(rank: int, world: int, backend: str = "nccl", group=None) -> TP
             fc = FusedComm.create(rank, world, group)
             if fc is not None:
                 tp.all_reduce = fc.all_reduce
+                tp.all_reduce_add_rms_quant = fc.all_reduce_add_rms_quant
+                tp.fused = fc
         except ImportError:
             pass
     return tp

@@ -63,6 +63,9 @@ class FusedComm:
     def all_reduce_add_rms_quant(self, x, residual, weight, eps):
         """Fused: all-reduce(x) + residual -> residual_out; Gemma RMSNorm + e4m3 quant."""
         M, H = x.shape
+        if not self.fits(x) or M > 256:
+            from ..ops import kernels as K
+            return K.add_rms_quant(self.all_reduce(x), residual, weight, eps)
         q = torch.empty(M, H, dtype=torch.float8_e4m3fn, device=x.device)
         s = torch.empty(M, dtype=torch.float32, device=x.device)
         r = torch.empty_like(x)

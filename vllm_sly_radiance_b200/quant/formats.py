@@ -198,3 +198,38 @@ def sf_tile_layout_inverse(tiled: torch.Tensor, N: int, KB: int) -> torch.Tensor
     KBp = (KB + 3) // 4 * 4
     s = tiled.view(Np // 128, KBp // 4, 32, 4, 4).permute(0, 3, 2, 1, 4).contiguous()
     return s.view(Np, KBp)[:N, :KB]
+
+
+# ---------------------------------------------------------------------------------------------
+# 4-bit KV cache (int4, fp16 scale + zero per 16 elements per head)
+# ---------------------------------------------------------------------------------------------
+KV4_GROUP = 16
+
+
+def kv4_row_bytes(head_dim: int) -> int:
+    """Bytes of one (token, kv-head) row: head_dim/2 nibble bytes + (scale, zero) fp16 pairs."""
+    return head_dim // 2 + (head_dim // KV4_GROUP) * 4
+
+
+def kv4_quantize(x: torch.Tensor) -> torch.Tensor:
+    """x [..., D] -> uint8 rows [..., kv4_row_bytes(D)]: asymmetric 4-bit per 16-element group,
+    zero = group min, scale = (max - min) / 15 (1 when flat), both stored as fp16."""
+    D = x.shape[-1]
+    g = x.float().reshape(*x.shape[:-1], D // KV4_GROUP, KV4_GROUP)
+    lo = g.amin(-1)
+    hi = g.amax(-1)
+    scale = ((hi - lo) / 15.0)
+    scale = torch.where(scale > 0, scale, torch.ones_like(scale)).half()
+    lo16 = lo.half()
+    q = torch.round((g - lo16.float().unsqueeze(-1)) / scale.float().unsqueeze(-1)).clamp(0, 15)
+    q = q.to(torch.uint8).reshape(*x.shape[:-1], D)
+    packed = pack_nibbles(q)
+    meta = torch.stack([scale, lo16], -1).reshape(*x.shape[:-1], -1).contiguous().view(torch.uint8)
+    return torch.cat([packed, meta], -1)
+
+
+def kv4_dequantize(rows: torch.Tensor, D: int) -> torch.Tensor:
+    data = rows[..., :D // 2]
+    meta = rows[..., D // 2:].contiguous().view(torch.float16).reshape(*rows.shape[:-1], D // KV4_GROUP, 2)
+    q = unpack_nibbles(data).float().reshape(*rows.shape[:-1], D // KV4_GROUP, KV4_GROUP)
+    return (q * meta[..., 0:1].float() + meta[..., 1:2].float()).reshape(*rows.shape[:-1], D)
