@@ -284,3 +284,29 @@ def test_paged_attention_split_repeated(D, Hq, Hkv, splits):
         got = K.paged_attention(q.to(DEV), kg, vg, meta, D ** -0.5)
         torch.cuda.synchronize()
         assert rel_err(got, want) < 2e-2, (it, rel_err(got, want))
+
+
+@pytest.mark.parametrize("R_per_expert", [1, 3, 40, 300])
+def test_moe_grouped_gemm(R_per_expert):
+    """Grouped tcgen05 GEMM over stacked expert weights vs per-expert fp32 references."""
+    from vllm_sly_radiance_b200.quant.mxfp4 import MXFP4Weight, cat_rows
+    torch.manual_seed(7)
+    E, N, Kd = 6, 256, 512
+    ws = [MXFP4Weight.from_float(torch.randn(N, Kd) * 0.02) for _ in range(E)]
+    stacked = cat_rows(ws)
+    counts = torch.tensor([R_per_expert, 0, 2 * R_per_expert, 1, R_per_expert, 0])
+    R = int(counts.sum())
+    x = torch.randn(R, Kd).to(torch.bfloat16)
+    q, s = ref.quant_fp8_rows(x)
+    want = torch.empty(R, N)
+    r0 = 0
+    for e in range(E):
+        c = int(counts[e])
+        if c:
+            want[r0:r0 + c] = ref.mxfp4_linear(q[r0:r0 + c], s[r0:r0 + c], ws[e].packed, ws[e].scales).float()
+        r0 += c
+    sg = stacked.to(DEV)
+    got = K.moe_grouped_gemm(q.to(DEV), s.to(DEV), sg, N, counts.to(DEV))
+    torch.cuda.synchronize()
+    K.check_status(got.device)
+    assert rel_err(got, want) < 1e-2, rel_err(got, want)

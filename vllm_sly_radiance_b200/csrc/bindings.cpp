@@ -6,6 +6,9 @@
 namespace rad {
 void mxfp4_gemm(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
                 torch::Tensor out, int64_t splits_override, torch::Tensor status);
+void mxfp4_grouped_gemm(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
+                        torch::Tensor out, torch::Tensor items, int64_t bn, int64_t n_per_group,
+                        torch::Tensor status);
 void add_rms_quant(torch::Tensor x, torch::Tensor residual, torch::Tensor weight,
                    torch::Tensor res_out, torch::Tensor q, torch::Tensor scale, torch::Tensor nout,
                    double eps);
@@ -53,6 +56,7 @@ void allreduce_oneshot(std::vector<int64_t> peers, int64_t rank, torch::Tensor i
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "sm_100a kernels of the radiance B200 serving engine";
   m.def("mxfp4_gemm", &rad::mxfp4_gemm, "MXFP4 W4A8 block-scaled tcgen05 GEMM");
+  m.def("mxfp4_grouped_gemm", &rad::mxfp4_grouped_gemm, "grouped (MoE) MXFP4 W4A8 tcgen05 GEMM");
   m.def("add_rms_quant", &rad::add_rms_quant, "fused residual add + Gemma RMSNorm (+ e4m3 quant)");
   m.def("silu_mul_quant", &rad::silu_mul_quant, "SiLU(gate)*up + e4m3 quant");
   m.def("gdn_norm_quant", &rad::gdn_norm_quant, "GDN gated RMSNorm (+ e4m3 quant)");

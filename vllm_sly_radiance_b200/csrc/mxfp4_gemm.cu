@@ -77,13 +77,24 @@ __host__ __device__ constexpr uint32_t make_idesc(int bn, int sf_id) {
          | ((uint32_t)sf_id << 4);       // B scale-factor id
 }
 
-template <int BN>
+template <int BN, bool GROUPED = false>
 __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
     mxfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                       const __grid_constant__ CUtensorMap tmap_a, const uint8_t* __restrict__ sfw,
                       const float* __restrict__ a_scale, __nv_bfloat16* __restrict__ out,
-                      int ldo, int M, int N, int K, int k_tiles_per_split, int* __restrict__ status) {
+                      int ldo, int M, int N, int K, int k_tiles_per_split, int* __restrict__ status,
+                      const int* __restrict__ items = nullptr, int n_per_group = 0) {
   using C = Cfg<BN>;
+  // Grouped (MoE) mode: blockIdx.y indexes a work table of (expert, first row, rows); the
+  // expert's weights are rows [e * n_per_group, (e + 1) * n_per_group) of the stacked tensor.
+  int g_expert = 0, g_row0 = 0, g_rows = 0;
+  if constexpr (GROUPED) {
+    pdl_wait();
+    g_expert = items[blockIdx.y * 3 + 0];
+    g_row0 = items[blockIdx.y * 3 + 1];
+    g_rows = items[blockIdx.y * 3 + 2];
+    if (g_rows <= 0) return;            // unused slot of the fixed-size work table
+  }
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stage_base = smem;
@@ -95,12 +106,15 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int n_tile = blockIdx.x;
+  const int n_tile = GROUPED ? (g_expert * (n_per_group / BM) + blockIdx.x) : blockIdx.x;
   const int m_tile = blockIdx.y;
   const int split = blockIdx.z;
   const int num_splits = gridDim.z;
-  const int n0 = n_tile * BM;
-  const int m0 = m_tile * BN;
+  const int n0 = n_tile * BM;                       // row of the (stacked) weight tensor
+  const int m0 = GROUPED ? g_row0 : m_tile * BN;
+  const int m_end = GROUPED ? g_row0 + g_rows : M;  // rows of this tile that are stored
+  const int n_out0 = GROUPED ? blockIdx.x * BM : n0;  // output column of weight row n0
+  const int n_lim = GROUPED ? n_per_group : N;
   const int k_tiles_total = K / BK;
   const int kt0 = split * k_tiles_per_split;
   const int kt1 = min(k_tiles_total, kt0 + k_tiles_per_split);
@@ -211,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
     // ---------------- epilogue ----------------
     const int q = warp & 3;            // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;     // weight row within the tile
-    const int n = n0 + row;
+    const int n = n_out0 + row;        // output column
     pdl_wait();                        // a_scale comes from the preceding kernel
     if (!mbar_wait(acc_bar, 0, status)) *abort_flag = 1;
     tc_fence_after();
@@ -222,11 +236,11 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
         uint32_t r[16];
         tmem_ld_32x32b_x16(tmem_acc + ((uint32_t)(q * 32) << 16) + c0, r);
         tmem_ld_wait();
-        if (n < N) {
+        if (n < n_lim) {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             const int m = m0 + c0 + j;
-            if (m < M) {
+            if (m < m_end) {
               const float v = have_acc ? __uint_as_float(r[j]) * a_scale[m] : 0.f;
               out[(size_t)m * ldo + n] = __float2bfloat16_rn(v);
             }
@@ -254,12 +268,12 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
     if (warp >= 2) {
       const int q = warp & 3;
       const int row = q * 32 + lane;
-      const int n = n0 + row;
+      const int n = n_out0 + row;
       const uint32_t my_rank = cluster_ctarank();
       const uint32_t part_addr = smem_u32(stage_base);
       for (int j = my_rank; j < BN; j += num_splits) {
         const int m = m0 + j;
-        if (m >= M || n >= N) continue;
+        if (m >= m_end || n >= n_lim) continue;
         float acc = 0.f;
         for (int r = 0; r < num_splits; ++r) {
           const uint32_t a = mapa_shared(part_addr + (uint32_t)((j * BM + row) * 4), (uint32_t)r);
@@ -350,7 +364,7 @@ static void launch(const torch::Tensor& a, const torch::Tensor& a_scale, const t
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tw, ta, (const uint8_t*)sf.data_ptr(),
                                     (const float*)a_scale.data_ptr(),
                                     (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), M, N, K,
-                                    per, status));
+                                    per, status, (const int*)nullptr, 0));
 }
 
 static int pick_splits(int tiles, int k_tiles, int ctas_per_sm) {
@@ -362,7 +376,54 @@ static int pick_splits(int tiles, int k_tiles, int ctas_per_sm) {
   return s;
 }
 
+template <int BN>
+static void launch_grouped(const torch::Tensor& a, const torch::Tensor& a_scale,
+                           const torch::Tensor& wp, const torch::Tensor& sf, torch::Tensor& out,
+                           const torch::Tensor& items, int max_items, int n_per_group, int K,
+                           int* status, cudaStream_t stream) {
+  using C = Cfg<BN>;
+  const int M = a.size(0);
+  const int Ntot = wp.size(0);
+  CUtensorMap tw = weight_map(wp, Ntot, K);
+  CUtensorMap ta = make_tma_2d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, a.stride(0), BK,
+                               BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  auto kern = mxfp4_gemm_kernel<BN, true>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+    attr_set = true;
+  }
+  dim3 grid(n_per_group / BM, max_items, 1);
+  C10_CUDA_CHECK(launch_pdl(kern, grid, dim3(kThreads), C::SMEM_BYTES, stream, tw, ta,
+                            (const uint8_t*)sf.data_ptr(), (const float*)a_scale.data_ptr(),
+                            (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), M, Ntot, K,
+                            K / BK, status, (const int*)items.data_ptr(), n_per_group));
+}
+
 }  // namespace mxfp4
+
+// Grouped (MoE) W4A8 GEMM.  a: expert-sorted e4m3 rows [R, K]; wp/sf: stacked expert weights
+// [E*n_per_group, K/2]; items [max_items, 3] int32 = (expert, first row, rows), rows <= bn.
+void mxfp4_grouped_gemm(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
+                        torch::Tensor out, torch::Tensor items, int64_t bn, int64_t n_per_group,
+                        torch::Tensor status) {
+  using namespace mxfp4;
+  TORCH_CHECK(a.scalar_type() == at::kFloat8_e4m3fn && out.scalar_type() == at::kBFloat16, "dtypes");
+  const int K = a.size(1);
+  TORCH_CHECK(K % BK == 0 && n_per_group % BM == 0, "grouped gemm: K % 128 and N % 128");
+  const int max_items = items.size(0);
+  if (a.size(0) == 0 || max_items == 0) return;
+  const at::cuda::CUDAGuard guard(a.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  int* st = status.numel() ? status.data_ptr<int>() : nullptr;
+  switch (bn) {
+    case 16: launch_grouped<16>(a, a_scale, wp, sf, out, items, max_items, n_per_group, K, st, stream); break;
+    case 32: launch_grouped<32>(a, a_scale, wp, sf, out, items, max_items, n_per_group, K, st, stream); break;
+    case 64: launch_grouped<64>(a, a_scale, wp, sf, out, items, max_items, n_per_group, K, st, stream); break;
+    case 128: launch_grouped<128>(a, a_scale, wp, sf, out, items, max_items, n_per_group, K, st, stream); break;
+    default: launch_grouped<256>(a, a_scale, wp, sf, out, items, max_items, n_per_group, K, st, stream); break;
+  }
+}
 
 // a: fp8 e4m3 [M, K] (row stride multiple of 16 bytes), a_scale fp32 [M], wp uint8 [N, K/2],
 // sf: tiled scale factors, out: bf16 [M, N] (row stride ldo)

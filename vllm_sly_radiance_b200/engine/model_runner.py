@@ -212,8 +212,11 @@ class ModelRunner:
             self.d_meta[:end].copy_(self.h_meta[:end])
             self.d_slots[:T].copy_(self.h_slots[:T])
         meta = self._views(B, T, ntiles, nb)
-        # graph replays keep the captured split count: size it for the longest context
-        meta.num_splits = self._num_splits(B, ntiles, self.max_blocks * bs if pad_to else max_kv)
+        # decode batches size the split count for the longest context, in graphs (replays keep
+        # the captured count) and eagerly alike, so both paths compute identical numerics
+        all_decode = all(s.is_decode for s in seqs)
+        meta.num_splits = self._num_splits(B, ntiles, self.max_blocks * bs if (pad_to or all_decode)
+                                           else max_kv)
         ids = self.d_meta[L.ids:L.ids + T]
         return meta, ids, sample_idx, sample_cnt
 
@@ -337,7 +340,10 @@ class ModelRunner:
             self.graph_pool = torch.cuda.graph_pool_handle()
         with torch.cuda.graph(graph, pool=self.graph_pool):
             out = run()
-        return dict(graph=graph, out=out, temp=temp, topk=topk, topp=topp, seed=seed, step=step)
+        # every tensor the graph reads must outlive it: a freed input's memory is handed to the
+        # next eager allocation and the replay would read whatever that step wrote there
+        return dict(graph=graph, out=out, temp=temp, topk=topk, topp=topp, seed=seed, step=step,
+                    sidx=sidx, minp=minp, st=st)
 
 
 def _needs_penalties(reqs) -> bool:

@@ -189,6 +189,40 @@ def mxfp4_gemm(q: torch.Tensor, scale: torch.Tensor, packed: torch.Tensor, sf: t
     return out
 
 
+def moe_work_items(counts: torch.Tensor, bn: int, max_items: int) -> torch.Tensor:
+    """(expert, first row, rows) per row tile of the expert-sorted buffer, padded with empty
+    items to a fixed length (device ops only: no host sync, CUDA-graph safe)."""
+    tiles = (counts + bn - 1) // bn
+    starts = torch.cumsum(counts, 0) - counts
+    tcum = torch.cumsum(tiles, 0)
+    i = torch.arange(max_items, device=counts.device)
+    e = torch.searchsorted(tcum, i, right=True).clamp(max=counts.shape[0] - 1)
+    j = i - (tcum[e] - tiles[e])
+    rows = torch.clamp(counts[e] - j * bn, min=0, max=bn)
+    rows = torch.where(i < tcum[-1], rows, torch.zeros_like(rows))
+    return torch.stack([e, starts[e] + j * bn, rows], 1).to(torch.int32).contiguous()
+
+
+def moe_grouped_gemm(q, s, w, n_per_group: int, counts: torch.Tensor) -> torch.Tensor:
+    """Expert-sorted rows (q, s) x stacked expert MXFP4 weights -> [R, n_per_group] bf16."""
+    R = q.shape[0]
+    E = counts.shape[0]
+    avg = max(1, R // max(1, counts.numel()))
+    bn = 16 if avg <= 16 else 32 if avg <= 32 else 64 if avg <= 64 else 128 if avg <= 128 else 256
+    max_items = (R + bn - 1) // bn + E
+    items = moe_work_items(counts, bn, max_items)
+    out = torch.zeros(R, n_per_group, dtype=torch.bfloat16, device=q.device)   # uncovered rows = 0
+    ext().mxfp4_grouped_gemm(q, s, w.packed, w.sf, out, items, bn, n_per_group,
+                             status_word(q.device))
+    return out
+
+
+def moe_grouped_mlp(q, s, counts, w_gate_up, w_down, I: int, H: int) -> torch.Tensor:
+    gu = moe_grouped_gemm(q, s, w_gate_up, 2 * I, counts)
+    a = silu_mul_quant(gu)
+    return moe_grouped_gemm(a[0], a[1], w_down, H, counts)
+
+
 # ---------------------------------------------------------------------------------------------
 # attention
 # ---------------------------------------------------------------------------------------------
