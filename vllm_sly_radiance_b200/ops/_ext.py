@@ -6,6 +6,8 @@ from __future__ import annotations
 
 import importlib
 
+import torch  # noqa: F401  (loads libc10 / libtorch, which the extension links against)
+
 _EXT = None
 _ERR = None
 
