@@ -110,6 +110,10 @@ def main():
     ap.add_argument("--conc", type=int, default=8)
     ap.add_argument("--no-extra", action="store_true", help="skip the prefill / concurrency extras")
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--kernel-profile", default=None,
+                    help="write rank 0's per-kernel device time of one untimed decode step (JSON)")
+    ap.add_argument("--no-profile-launches", action="store_true",
+                    help="count launches from the model structure (for runs under an external profiler)")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)
@@ -164,6 +168,7 @@ def main():
     barrier()
     ev = []
     stream = torch.cuda.current_stream()
+    h2d = d2h = 0
     with ClockSampler(dev.index) as clk:
         barrier()
         torch.cuda.nvtx.range_push("timed")
@@ -175,6 +180,8 @@ def main():
             eng.step()
             e.record(stream)
             ev.append((s, e))
+            h2d += eng.runner.last_io[0]
+            d2h += eng.runner.last_io[1]
         barrier()
         wall = time.perf_counter() - w0
         torch.cuda.nvtx.range_pop()
@@ -183,8 +190,12 @@ def main():
     wall = max_over_ranks(wall)
     value = args.steps / (dev_ms / 1e3)
     e2e = args.steps / wall
+    # launches of this library's kernels per decode step, counted by the profiler on one extra
+    # (untimed) step: every kernel of the library lives in the `rad::` namespace
+    kernels_per_step, launch_method = (count_launches(eng), "model-structure estimate") \
+        if args.no_profile_launches else \
+        profiled_launches(eng, args.kernel_profile if rank == 0 else None)
     eng.abort_request("stream0")
-    kernels_per_step = count_launches(eng) if rank == 0 else None
 
     extra = {}
     if not args.no_extra:
@@ -231,8 +242,9 @@ def main():
                        "parallelism": f"tp{world}", "kv_cache": "fp8_e4m3",
                        "l2": "inputs larger than L2 (each decode step streams ~9 GB of weights)"},
             "e2e": {"value": round(e2e, 2), "unit": "tok/s",
-                    "h2d_bytes_per_step": e2e_h2d_bytes(eng), "d2h_bytes_per_step": 8},
+                    "h2d_bytes_per_step": h2d // args.steps, "d2h_bytes_per_step": d2h // args.steps},
             "gpu_launches": kernels_per_step * args.steps if kernels_per_step else None,
+            "gpu_launches_per_step": kernels_per_step, "gpu_launches_method": launch_method,
             "clocks": clk.summary(),
             "impl": args.impl,
             "load_s": round(load_s, 1),
@@ -245,12 +257,32 @@ def main():
         dist.destroy_process_group()
 
 
-def e2e_h2d_bytes(eng):
-    """Per decode step the runner copies the packed int32 metadata (token id, position, offsets,
-    lengths, state slot, block table row, attention tile) plus the int64 KV slot from pinned memory."""
-    r = eng.runner
-    L = r.L
-    return int((L.bt - 0) * 0 + (3 + 2 + 3 + 2) * 4 + r.max_blocks * 4 + 8)
+def profiled_launches(eng, dump_path=None):
+    """(kernels of this library in one decode step, how counted).  Falls back to counting from
+    the model structure if the profiler is unavailable.  With dump_path, the per-kernel device
+    time of that step (all kernels, not only this library's) is written there as JSON."""
+    try:
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            eng.step()
+            torch.cuda.synchronize()
+        evs = [e for e in prof.events() if e.device_type.name == "CUDA"]
+        n = sum(1 for e in evs if "rad::" in e.name)
+        if dump_path:
+            agg = {}
+            for e in evs:
+                a = agg.setdefault(e.name[:120], [0, 0.0])
+                a[0] += 1
+                a[1] += e.device_time
+            rows = sorted(([k, v[0], round(v[1], 2)] for k, v in agg.items()), key=lambda r: -r[2])
+            with open(dump_path, "w") as f:
+                json.dump({"step_kernel_us": round(sum(r[2] for r in rows), 1),
+                           "kernels": rows}, f, indent=0)
+        if n > 0:
+            return n, "torch.profiler kernel records in namespace rad:: over one decode step"
+    except Exception:
+        pass
+    return count_launches(eng), "model-structure estimate"
 
 
 def count_launches(eng):
@@ -258,12 +290,11 @@ def count_launches(eng):
     n = 0
     for layer in eng.model.layers:
         n += 1                                  # add_rms_quant (input)
-        if layer.is_attn:
-            n += 1 + 1 + 1 + 1 + 1              # qkv gemm, prologue, attention(+merge), gate quant, o gemm
-        else:
-            n += 1 + 2 + 1 + 1 + 1              # in_proj, conv + state, recurrent, norm quant, out gemm
-        n += 1 + 1 + 1 + 1                      # add_rms_quant, gate_up, silu_mul_quant, down
-    n += 1 + 1 + 1                              # final norm, lm_head gemm, argmax
+        n += 5                                  # attention: qkv gemm, prologue, attention, gate quant,
+        #                                         o gemm;  GDN: in_proj, conv(+state), recurrent,
+        #                                         norm quant, out gemm
+        n += 4                                  # add_rms_quant, gate_up, silu_mul_quant, down
+    n += 3                                      # final norm, lm_head gemm, argmax
     return n
 
 

@@ -1,6 +1,7 @@
 """Number formats: E2M1 / UE8M0 / MXFP4, e4m3 per-token, NVFP4 requant, INT4, SF tile layout."""
 import torch
 
+from vllm_sly_radiance_b200.ops import reference as ref
 from vllm_sly_radiance_b200.quant import formats as F
 from vllm_sly_radiance_b200.quant.mxfp4 import MXFP4Weight, cat_rows
 
@@ -78,3 +79,20 @@ def test_mxfp4_weight_slicing():
     assert torch.equal(cat.packed, mw.packed) and torch.equal(cat.sf, mw.sf)
     c = mw.narrow_cols(256, 256)
     assert torch.equal(c.dequantize(), mw.dequantize()[:, 256:])
+
+
+def test_mxfp4_weight_k_tail_padding():
+    """K not a multiple of the 128-wide GEMM tile: the stored weight is zero-padded to whole
+    tiles, the logical K is kept, and a linear over the padded weight equals the unpadded one."""
+    g = torch.Generator().manual_seed(0)
+    w = torch.randn(40, 8704, generator=g) * 0.02
+    full = MXFP4Weight.from_float(w)
+    shard = full.narrow_cols(1088 * 3, 1088)
+    assert shard.K == 1088 and shard.K_padded == 1152
+    assert torch.equal(shard.dequantize(), full.dequantize()[:, 1088 * 3:1088 * 4])
+    assert int(shard.packed[:, 1088 // 2:].sum()) == 0
+    x = torch.randn(3, 1088, generator=g)
+    q, s = ref.quant_fp8_rows(x.to(torch.bfloat16))
+    got = ref.mxfp4_linear(q, s, shard.packed, shard.scales).float()
+    want = ((q.float() @ shard.dequantize().t()) * s[:, None]).to(torch.bfloat16).float()
+    assert torch.equal(got, want)

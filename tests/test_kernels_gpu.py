@@ -31,7 +31,9 @@ def rel_err(a, b):
 @pytest.mark.parametrize("M,N,Kd,splits", [
     (1, 256, 256, 0), (5, 384, 512, 0), (16, 256, 1024, 4), (37, 200, 768, 0),
     (64, 512, 512, 2), (128, 256, 256, 0), (300, 512, 1024, 0), (1, 5120, 8704, 0),
-    (8, 16480, 5120, 0), (520, 640, 2048, 1)])
+    (8, 16480, 5120, 0), (520, 640, 2048, 1),
+    # K tail (a row-parallel shard of 8704 / 8 = 1088 features): zero-padded weight tiles
+    (1, 5120, 1088, 0), (40, 2176, 1088, 0), (3, 384, 1088, 2)])
 def test_mxfp4_gemm(M, N, Kd, splits):
     g = torch.Generator().manual_seed(M * 7 + N)
     w = torch.randn(N, Kd, generator=g) * 0.02

@@ -18,7 +18,27 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, outq):
+    import faulthandler
+    import sys
+    import traceback
+    # a rank that stops making progress prints its Python stack and exits instead of waiting
+    faulthandler.dump_traceback_later(240, exit=True)
+    try:
+        _run(rank, world, port, outq)
+    except BaseException:
+        outq.put(("error", rank, traceback.format_exc()))
+        sys.stderr.write(traceback.format_exc())
+        raise
+
+
+def _log(rank, msg):
+    import sys
+    sys.stderr.write(f"[rank {rank}] {msg}\n")
+    sys.stderr.flush()
+
+
+def _run(rank, world, port, outq):
     import datetime
     import torch.distributed as dist
     os.environ["MASTER_ADDR"] = "127.0.0.1"
@@ -35,6 +55,7 @@ def _worker(rank, world, port, q):
     from vllm_sly_radiance_b200.ops import kernels as K
     from vllm_sly_radiance_b200.parallel.comm import make_tp_info
     out = {}
+    _log(rank, "process group up")
     # 1) the NVLink all-reduce (plain and fused) vs NCCL
     tp = make_tp_info(rank, world, "fused")
     torch.manual_seed(rank)
@@ -50,6 +71,7 @@ def _worker(rank, world, port, q):
         q2, s2, r2 = K.add_rms_quant(ref.to(torch.bfloat16), res, w, 1e-6)
         out[f"arq{M}"] = float(((q.float() * s[:, None]) - (q2.float() * s2[:, None])).abs().max())
     K.check_status(torch.device("cuda", rank))
+    _log(rank, "all-reduce checks done")
     # 2) TP=2 tiny model (fused path) vs single-GPU logits
     cfg = EngineConfig(model="tiny_hybrid", device="cuda", max_model_len=512, max_num_seqs=2,
                        max_num_batched_tokens=128, num_kv_blocks=32, enable_cuda_graphs=True)
@@ -58,12 +80,13 @@ def _worker(rank, world, port, q):
     o = eng.generate([list(range(40, 100))], SamplingParams(temperature=0, max_tokens=6,
                                                              ignore_eos=True))
     out["toks"] = o[0].outputs[0].token_ids
+    _log(rank, f"generate done {out['toks']}")
     eng.runner.graphs.clear()
     tp.fused.close()
     dist.barrier()
     dist.destroy_process_group()
     if rank == 0:
-        q.put(out)
+        outq.put(("ok", rank, out))
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
@@ -80,10 +103,25 @@ def test_tp2_fused_allreduce_and_model():
     ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in ps:
         p.start()
-    res = q.get(timeout=600)
+    import queue
+    import time
+    res = None
+    t0 = time.time()
+    while res is None and time.time() - t0 < 300:
+        try:
+            kind, rank, payload = q.get(timeout=5)
+        except queue.Empty:
+            if any(p.exitcode not in (None, 0) for p in ps):
+                break
+            continue
+        assert kind == "ok", f"rank {rank} failed:\n{payload}"
+        res = payload
     for p in ps:
-        p.join(timeout=120)
-        assert p.exitcode == 0
+        p.join(timeout=60)
+        if p.exitcode is None:
+            p.kill()
+    assert res is not None, [p.exitcode for p in ps]
+    assert all(p.exitcode == 0 for p in ps), [p.exitcode for p in ps]
     for M in (1, 8, 64):
         assert res[f"ar{M}"] < 0.05, res
         assert res[f"arq{M}"] < 0.25, res

@@ -29,7 +29,11 @@ def peaks():
         return 6.65e12, 1.59e15, "fallback"
 
 
-def timeit(fn, iters=50, warmup=5):
+ITERS = 50
+
+
+def timeit(fn, iters=None, warmup=5):
+    iters = iters or ITERS
     for _ in range(warmup):
         fn(0)
     torch.cuda.synchronize()
@@ -69,10 +73,17 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("what", choices=["gemm"])
     ap.add_argument("--m", default="1,8,16,64,256,1024,4096")
+    ap.add_argument("--shape", default="", help="comma list of shape names (default: all)")
+    ap.add_argument("--iters", type=int, default=50)
     a = ap.parse_args()
+    global ITERS
+    ITERS = a.iters
     ms = [int(v) for v in a.m.split(",")]
     shapes = [(16480, 5120, "gdn_in_proj"), (5120, 6144, "out_proj"), (17408, 5120, "gate_up"),
               (5120, 8704, "down"), (14336, 5120, "attn_qkv"), (248320, 5120, "lm_head")]
+    if a.shape:
+        keep = set(a.shape.split(","))
+        shapes = [sh for sh in shapes if sh[2] in keep]
     if a.what == "gemm":
         bench_gemm(ms, shapes)
 

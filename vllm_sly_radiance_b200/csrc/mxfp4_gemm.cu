@@ -334,10 +334,11 @@ static void launch(const torch::Tensor& a, const torch::Tensor& a_scale, const t
                    const torch::Tensor& sf, torch::Tensor& out, int M, int N, int K, int splits,
                    int* status, cudaStream_t stream) {
   using C = Cfg<BN>;
-  CUtensorMap tw = weight_map(wp, N, K);
+  const int Kw = (int)wp.size(1) * 2;          // whole K tiles of stored weight
+  CUtensorMap tw = weight_map(wp, N, Kw);
   CUtensorMap ta = make_tma_2d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, a.stride(0), BK,
                                BN, CU_TENSOR_MAP_SWIZZLE_128B);
-  const int k_tiles = K / BK;
+  const int k_tiles = Kw / BK;
   const int per = (k_tiles + splits - 1) / splits;
   dim3 grid((N + BM - 1) / BM, (M + BN - 1) / BN, splits);
   auto kern = mxfp4_gemm_kernel<BN>;
@@ -363,7 +364,7 @@ static void launch(const torch::Tensor& a, const torch::Tensor& a_scale, const t
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tw, ta, (const uint8_t*)sf.data_ptr(),
                                     (const float*)a_scale.data_ptr(),
-                                    (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), M, N, K,
+                                    (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), M, N, Kw,
                                     per, status, (const int*)nullptr, 0));
 }
 
@@ -434,9 +435,13 @@ void mxfp4_gemm(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch:
   TORCH_CHECK(a.scalar_type() == at::kFloat8_e4m3fn, "activations must be float8_e4m3fn");
   TORCH_CHECK(out.scalar_type() == at::kBFloat16, "output must be bf16");
   TORCH_CHECK(a.dim() == 2 && a.stride(1) == 1 && out.stride(1) == 1 && wp.stride(1) == 1, "row-major");
+  // K: the activation's input features (a multiple of 32); the stored weight is zero-padded to
+  // whole K tiles (Kw), and the activation's missing tail of the last tile is zero-filled by TMA
+  // (out-of-range box elements read as zero)
   const int M = a.size(0), K = a.size(1), N = wp.size(0);
-  TORCH_CHECK(wp.size(1) * 2 == K, "weight K mismatch");
-  TORCH_CHECK(K % BK == 0, "K must be a multiple of 128");
+  const int Kw = (int)wp.size(1) * 2;
+  TORCH_CHECK(K % 32 == 0 && Kw % BK == 0 && Kw >= K && Kw - K < BK,
+              "weight K must be the activation K rounded up to a multiple of 128");
   TORCH_CHECK((a.stride(0) % 16) == 0 && (reinterpret_cast<uintptr_t>(a.data_ptr()) % 16) == 0,
               "activation rows must be 16-byte aligned");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(wp.data_ptr()) % 32) == 0 && (wp.stride(0) % 32) == 0,
@@ -454,7 +459,7 @@ void mxfp4_gemm(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch:
   else bn = 256;
   const int tiles = ((N + BM - 1) / BM) * ((M + bn - 1) / bn);
   int splits = splits_override > 0 ? (int)splits_override
-                                   : pick_splits(tiles, K / BK, bn <= 64 ? 2 : 1);
+                                   : pick_splits(tiles, Kw / BK, bn <= 64 ? 2 : 1);
   switch (bn) {
     case 16: launch<16>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream); break;
     case 32: launch<32>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream); break;

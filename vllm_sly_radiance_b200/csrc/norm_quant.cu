@@ -269,6 +269,16 @@ static inline __nv_bfloat16* bfm(const torch::Tensor& t) {
   return t.defined() && t.numel() ? reinterpret_cast<__nv_bfloat16*>(t.data_ptr()) : nullptr;
 }
 
+// The producers move rows with 16-byte vector loads / stores (8-byte for the e4m3 output): a
+// tensor whose base or row stride breaks that alignment is rejected here instead of faulting.
+static inline void check_vec(const torch::Tensor& t, const char* what, int align = 16) {
+  if (!t.defined() || t.numel() == 0) return;
+  const int64_t es = t.element_size();
+  TORCH_CHECK(t.stride(-1) == 1 && reinterpret_cast<uintptr_t>(t.data_ptr()) % align == 0 &&
+                  (t.dim() < 2 || (t.stride(0) * es) % align == 0),
+              what, ": vector access needs a ", align, "-byte aligned base and row stride");
+}
+
 }  // namespace nq
 
 // x [M,H] bf16; residual (optional, may alias res_out); q fp8 [M,H] / scale [M] (optional);
@@ -279,6 +289,12 @@ void add_rms_quant(torch::Tensor x, torch::Tensor residual, torch::Tensor weight
   using namespace nq;
   const int M = x.size(0), H = x.size(1);
   TORCH_CHECK(H % V == 0 && x.stride(1) == 1, "add_rms_quant: H % 8 and row-major");
+  check_vec(x, "add_rms_quant x");
+  check_vec(weight, "add_rms_quant weight");
+  check_vec(residual, "add_rms_quant residual");
+  check_vec(res_out, "add_rms_quant res_out");
+  check_vec(nout, "add_rms_quant nout");
+  check_vec(q, "add_rms_quant q", 8);
   if (M == 0) return;
   const at::cuda::CUDAGuard guard(x.device());
   auto stream = at::cuda::getCurrentCUDAStream();
@@ -304,6 +320,8 @@ void silu_mul_quant(torch::Tensor gate_up, torch::Tensor q, torch::Tensor scale)
   using namespace nq;
   const int M = gate_up.size(0), I = gate_up.size(1) / 2;
   TORCH_CHECK(I % V == 0 && gate_up.stride(1) == 1, "silu_mul_quant: I % 8");
+  check_vec(gate_up, "silu_mul_quant gate_up");
+  check_vec(q, "silu_mul_quant q", 8);
   if (M == 0) return;
   const at::cuda::CUDAGuard guard(gate_up.device());
   auto stream = at::cuda::getCurrentCUDAStream();
@@ -322,6 +340,11 @@ void gdn_norm_quant(torch::Tensor o, torch::Tensor z, torch::Tensor weight, int6
   TORCH_CHECK(D % V == 0 && head_dim % V == 0 && (head_dim / V) <= 32 &&
                   ((head_dim / V) & (head_dim / V - 1)) == 0,
               "gdn_norm_quant: unsupported head_dim");
+  check_vec(o, "gdn_norm_quant o");
+  check_vec(weight, "gdn_norm_quant weight");
+  check_vec(z, "gdn_norm_quant z");
+  check_vec(q, "gdn_norm_quant q", 8);
+  check_vec(nout, "gdn_norm_quant nout");
   if (M == 0) return;
   const at::cuda::CUDAGuard guard(o.device());
   auto stream = at::cuda::getCurrentCUDAStream();
@@ -347,7 +370,12 @@ void gate_mul_quant(torch::Tensor a, torch::Tensor gate, int64_t head_dim, int64
                     torch::Tensor q, torch::Tensor scale, torch::Tensor nout) {
   using namespace nq;
   const int M = a.size(0), D = a.size(1);
-  TORCH_CHECK(D % V == 0 && head_dim % V == 0, "gate_mul_quant: dims % 8");
+  TORCH_CHECK(D % V == 0 && head_dim % V == 0 && gate_head_stride % V == 0,
+              "gate_mul_quant: dims % 8");
+  check_vec(a, "gate_mul_quant a");
+  check_vec(gate, "gate_mul_quant gate");
+  check_vec(q, "gate_mul_quant q", 8);
+  check_vec(nout, "gate_mul_quant nout");
   if (M == 0) return;
   const at::cuda::CUDAGuard guard(a.device());
   auto stream = at::cuda::getCurrentCUDAStream();
@@ -367,6 +395,8 @@ void quant_fp8_rows(torch::Tensor x, torch::Tensor q, torch::Tensor scale) {
   using namespace nq;
   const int M = x.size(0), D = x.size(1);
   TORCH_CHECK(D % V == 0, "quant_fp8_rows: D % 8");
+  check_vec(x, "quant_fp8_rows x");
+  check_vec(q, "quant_fp8_rows q", 8);
   if (M == 0) return;
   const at::cuda::CUDAGuard guard(x.device());
   auto stream = at::cuda::getCurrentCUDAStream();

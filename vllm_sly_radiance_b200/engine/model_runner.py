@@ -86,6 +86,7 @@ class ModelRunner:
         self.last_timing = {}
         self._scratch: dict = {}
         self._h2d_event = None
+        self.last_io = (0, 0)      # (host->device, device->host) bytes copied by the last step
 
     # ------------------------------------------------------------------------------------------
     # metadata
@@ -203,6 +204,7 @@ class ModelRunner:
             h[L.bt:L.bt + B * nb] = src.reshape(-1)
         # H2D
         end = L.bt + B * nb
+        self._h2d_bytes = end * 4 + T * 8
         if self.device.type == "cuda":
             self.d_meta[:end].copy_(self.h_meta[:end], non_blocking=True)
             self.d_slots[:T].copy_(self.h_slots[:T], non_blocking=True)
@@ -245,6 +247,7 @@ class ModelRunner:
         st = None
         if bucket is not None and not want_logits and not _needs_penalties(reqs):
             toks = self._run_graph(out, bucket)
+            self.last_io = (self._h2d_bytes, 8 * bucket)
             sampled = {}
             for b, s in enumerate(out.seqs):
                 sampled[s.req.request_id] = [int(toks[b])]
@@ -256,7 +259,11 @@ class ModelRunner:
         for s, c in zip(out.seqs, sample_cnt):
             sreqs.extend([s.req] * c)
         sampled = {}
+        h2d = self._h2d_bytes + 8 * len(sample_idx)
+        d2h = 0
         if sreqs:
+            h2d += len(sreqs) * (4 + 4 + 4 + 4 + 8)
+            d2h = 8 * len(sreqs)
             st = SamplingTensors.from_requests(sreqs, self.device)
             lg = apply_penalties(logits, sreqs)
             toks, _, _ = sample(lg, st, 0)
@@ -270,6 +277,7 @@ class ModelRunner:
                 if c:
                     sampled[s.req.request_id] = hv[j:j + c] if c == 1 else hv[j:j + c]
                     j += c
+        self.last_io = (h2d, d2h)
         return StepResult(sampled, logits=logits if want_logits else None,
                           num_tokens=meta.num_tokens)
 
@@ -298,6 +306,7 @@ class ModelRunner:
         # sampling params into the static buffers
         B = len(reqs)
         if not greedy:
+            self._h2d_bytes += B * (4 + 4 + 4 + 8)
             g["temp"][:B].copy_(torch.tensor([r.params.temperature for r in reqs]), non_blocking=True)
             g["topk"][:B].copy_(torch.tensor([r.params.top_k for r in reqs], dtype=torch.int32), non_blocking=True)
             g["topp"][:B].copy_(torch.tensor([r.params.top_p for r in reqs]), non_blocking=True)

@@ -29,7 +29,7 @@ from ..ops import kernels as K
 from ..quant.formats import kv4_row_bytes
 from ..quant.mxfp4 import MXFP4Weight
 from .layers import Linear, rope_cache
-from .weights import RandomWeights, cat_rows, slice_cols, slice_rows
+from .weights import RandomWeights, cat_rows, pad_rows, slice_cols, slice_rows
 
 
 # ---------------------------------------------------------------------------------------------
@@ -137,7 +137,10 @@ class GDNMixer:
         self.conv_dim = 2 * self.key_dim + self.value_dim
         kd, vd, hv = cfg.gdn_key_dim, cfg.gdn_value_dim, cfg.gdn_num_v_heads
         w_in = W.linear(prefix + "in_proj", cfg.gdn_in_proj_dim, H)
-        self.in_proj = make_linear(_cat_sections(w_in, [kd, kd, vd, vd, hv, hv], tp), quant, "in_proj")
+        # [q|k|v|z|b|a] of this rank, padded to a multiple of 8 outputs: the consumers read z with
+        # 16-byte vectors, so the output row stride must stay 16-byte aligned at every TP size
+        self.in_proj = make_linear(pad_rows(_cat_sections(w_in, [kd, kd, vd, vd, hv, hv], tp), 8),
+                                   quant, "in_proj")
         del w_in
         conv = W.tensor(prefix + "conv_w", (cfg.gdn_conv_dim, cfg.gdn_conv_kernel), "conv")
         self.conv_w = _cat_sections(conv, [kd, kd, vd], tp).to(torch.bfloat16).contiguous()
@@ -158,7 +161,7 @@ class GDNMixer:
         cd, vd = self.conv_dim, self.value_dim
         xc = proj[:, :cd]
         z = proj[:, cd:cd + vd]
-        ba = proj[:, cd + vd:]
+        ba = proj[:, cd + vd:cd + vd + 2 * self.Hv]
         fused_state = meta.commit_len is None and meta.num_tokens == meta.num_seqs
         y = K.gdn_conv(xc, self.conv_w, conv_state, meta, self.key_dim, self.dk,
                        update_state=fused_state)
@@ -179,7 +182,7 @@ class GDNMixer:
         proj, y = saved
         cd, vd = self.conv_dim, self.value_dim
         K.gdn_conv_state_update(proj[:, :cd], conv_state, meta, commit_len)
-        K.gdn_recurrent(y, proj[:, cd + vd:], self.A_log, self.dt_bias, ssm_state, meta, self.Hk,
+        K.gdn_recurrent(y, proj[:, cd + vd:cd + vd + 2 * self.Hv], self.A_log, self.dt_bias, ssm_state, meta, self.Hk,
                         self.scale, commit_len=commit_len, write_out=False)
 
 

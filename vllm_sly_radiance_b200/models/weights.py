@@ -73,6 +73,19 @@ def slice_cols(w: WeightT, start: int, length: int) -> WeightT:
     return w[:, start:start + length].contiguous()
 
 
+def pad_rows(w: WeightT, multiple: int) -> WeightT:
+    """Append zero output rows so the row count is a multiple of `multiple` (keeps the row stride
+    of the layer's output 16-byte aligned for the vectorised consumers)."""
+    n = w.N if isinstance(w, MXFP4Weight) else w.shape[0]
+    pad = (-n) % multiple
+    if pad == 0:
+        return w
+    if isinstance(w, MXFP4Weight):
+        z = MXFP4Weight.from_float(torch.zeros(pad, w.K, dtype=torch.float32, device=w.packed.device))
+        return cat_rows([w, z])
+    return torch.cat([w, torch.zeros(pad, w.shape[1], dtype=w.dtype, device=w.device)], 0)
+
+
 def cat_rows(ws: list) -> WeightT:
     if isinstance(ws[0], MXFP4Weight):
         from ..quant.mxfp4 import cat_rows as cr

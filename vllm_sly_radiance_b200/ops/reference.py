@@ -92,7 +92,8 @@ def gate_mul_quant(attn_out, gate):
 def mxfp4_linear(q: torch.Tensor, scale: torch.Tensor, w_packed: torch.Tensor,
                  w_scales: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
     """C[M,N] = a_scale[m] * sum_k e4m3(q[m,k]) * e2m1(w[n,k]) * 2^(ws[n,k/32]-127), fp32 accumulate."""
-    w = mxfp4_dequantize(w_packed, w_scales)                    # [N, K] fp32 exact
+    w = mxfp4_dequantize(w_packed, w_scales)                    # [N, Kp] fp32 exact
+    w = w[:, :q.shape[1]]                                       # zero-padded K tail
     c = (q.float() @ w.t()) * scale.float().unsqueeze(-1)
     if bias is not None:
         c = c + bias.float()
