@@ -128,6 +128,7 @@ def _attn_meta(q_lens, ctx_lens, block_size, Hq, Hkv, num_splits, dev):
     m.query_start_loc = torch.tensor(qsl, dtype=torch.int32, device=dev)
     m.seq_lens = torch.tensor(seq_lens, dtype=torch.int32, device=dev)
     m.block_tables = bt.to(dev)
+    m.num_tokens, m.num_seqs = sum(q_lens), B
     m.tile_seq = torch.tensor(ts, dtype=torch.int32, device=dev)
     m.tile_row0 = torch.tensor(tr, dtype=torch.int32, device=dev)
     m.num_splits = num_splits
@@ -167,6 +168,40 @@ def test_paged_attention(D, Hq, Hkv, q_lens, ctx_lens, splits, fp8):
     got = K.paged_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), meta, scale)
     torch.cuda.synchronize()
     assert rel_err(got, want) < 2e-2, rel_err(got, want)
+
+
+@pytest.mark.parametrize("D,Hq,Hkv,ctx_lens,splits,fmt", [
+    (256, 24, 4, [1500, 100, 0], 17, "fp8"), (256, 24, 4, [4000], 32, "fp8"),
+    (256, 24, 4, [700, 63], 1, "bf16"), (256, 24, 4, [900, 65], 6, "int4"),
+    (128, 32, 2, [300, 1], 3, "fp8"), (64, 4, 2, [130, 62, 10], 5, "int4"),
+    (256, 6, 1, [2048], 8, "fp8")])
+def test_paged_attention_decode_kernel(D, Hq, Hkv, ctx_lens, splits, fmt, monkeypatch):
+    """The decode kernel (one token per sequence, keys split across warps) agrees with the
+    general 64-row tile kernel and with the fp32 oracle, for every cache format."""
+    from vllm_sly_radiance_b200.quant import formats as F
+    torch.manual_seed(5)
+    bs = 16 if fmt == "int4" else 64
+    q_lens = [1] * len(ctx_lens)
+    meta, nblocks = _attn_meta(q_lens, ctx_lens, bs, Hq, Hkv, splits, DEV)
+    k = torch.randn(nblocks, Hkv, bs, D) * 0.5
+    v = torch.randn(nblocks, Hkv, bs, D)
+    q = torch.randn(len(ctx_lens), Hq, D).to(torch.bfloat16)
+    if fmt == "fp8":
+        kc, vc = k.to(torch.float8_e4m3fn), v.to(torch.float8_e4m3fn)
+        q = ref.fp8_e4m3(q.float()).to(torch.bfloat16)
+    elif fmt == "bf16":
+        kc, vc = k.to(torch.bfloat16), v.to(torch.bfloat16)
+    else:
+        kc, vc = F.kv4_quantize(k), F.kv4_quantize(v)
+    scale = D ** -0.5
+    want = ref.paged_attention(q, kc, vc, meta.block_tables.cpu(), meta.seq_lens.cpu(),
+                               meta.query_start_loc.cpu(), bs, scale)
+    got = K.paged_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), meta, scale)
+    monkeypatch.setattr(K, "_ATTN_DECODE", False)
+    general = K.paged_attention(q.to(DEV), kc.to(DEV), vc.to(DEV), meta, scale)
+    torch.cuda.synchronize()
+    assert rel_err(got, want) < 2e-2, rel_err(got, want)
+    assert rel_err(got, general) < 1e-2, rel_err(got, general)
 
 
 def test_qkv_prologue():

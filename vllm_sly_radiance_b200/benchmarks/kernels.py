@@ -2,8 +2,7 @@
 set larger than the 126 MB L2).  Usage:
 
     python -m vllm_sly_radiance_b200.benchmarks.kernels gemm [--m 1,8,64,4096]
-    python -m vllm_sly_radiance_b200.benchmarks.kernels attn
-    python -m vllm_sly_radiance_b200.benchmarks.kernels gdn
+    python -m vllm_sly_radiance_b200.benchmarks.kernels attn [--ctx 1500,4096 --splits 1,17]
 
 Prints one JSON line per case with time, achieved bandwidth / FLOP rate and the fraction of the
 measured peaks in MEASURED_PEAKS.json (fallback 6.65 TB/s, 1.59 PFLOP/s).
@@ -33,11 +32,28 @@ ITERS = 50
 
 
 def timeit(fn, iters=None, warmup=5):
+    """Seconds per call on the device.  The calls are captured into one CUDA graph and replayed,
+    so host launch overhead (which exceeds a short kernel's duration) is not measured; falls
+    back to an eager loop if capture fails."""
     iters = iters or ITERS
-    for _ in range(warmup):
-        fn(0)
+    for i in range(warmup):
+        fn(i)
     torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for i in range(iters):
+                fn(i)
+        g.replay()
+        torch.cuda.synchronize()
+        s.record()
+        g.replay()
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / iters * 1e-3
+    except Exception:
+        torch.cuda.synchronize()
     s.record()
     for i in range(iters):
         fn(i)
@@ -69,9 +85,59 @@ def bench_gemm(ms, shapes):
                               "frac_bf16_peak": round(flops / t / fl, 3), "peaks": src}), flush=True)
 
 
+class _AttnMeta:
+    pass
+
+
+def _attn_meta(ctx_lens, bs, Hq, Hkv, splits, dev):
+    """Decode batch: one query token per sequence, contiguous random page tables."""
+    B = len(ctx_lens)
+    m = _AttnMeta()
+    seq = [c + 1 for c in ctx_lens]
+    nb = max((s + bs - 1) // bs for s in seq)
+    perm = torch.randperm(B * nb, device="cpu").to(torch.int32)
+    m.block_tables = perm.view(B, nb).to(dev)
+    m.seq_lens = torch.tensor(seq, dtype=torch.int32, device=dev)
+    m.query_start_loc = torch.arange(B + 1, dtype=torch.int32, device=dev)
+    m.tile_seq = torch.arange(B, dtype=torch.int32, device=dev)
+    m.tile_row0 = torch.zeros(B, dtype=torch.int32, device=dev)
+    m.num_tokens = m.num_seqs = B
+    m.num_splits = splits
+    m.scratch_o = lambda s_, T, H, D: torch.empty(s_, T, H, D, device=dev)
+    m.scratch_ml = lambda s_, T, H: torch.empty(s_, T, H, 2, device=dev)
+    return m, B * nb
+
+
+def bench_attn(ctxs, splits_list, batch):
+    """Decode attention, Qwen3.8-27B head layout (24 q / 4 kv heads, D=256), fp8 KV cache."""
+    bw, _, src = peaks()
+    Hq, Hkv, D, bs = 24, 4, 256, 64
+    for ctx in ctxs:
+        for sp in splits_list:
+            for dec in (True, False):
+                meta, nblocks = _attn_meta([ctx] * batch, bs, Hq, Hkv, sp, "cuda")
+                kc = (torch.randn(nblocks, Hkv, bs, D, device="cuda") * 0.5).to(torch.float8_e4m3fn)
+                vc = torch.randn(nblocks, Hkv, bs, D, device="cuda").to(torch.float8_e4m3fn)
+                q = torch.randn(batch, Hq, D, device="cuda").to(torch.bfloat16)
+                K._ATTN_DECODE = dec
+
+                def fn(i):
+                    K.paged_attention(q, kc, vc, meta, D ** -0.5)
+                t = timeit(fn)
+                byts = batch * (ctx + 1) * Hkv * D * 2
+                print(json.dumps({"kernel": "paged_attention", "variant": "decode" if dec else "general",
+                                  "batch": batch, "ctx": ctx, "splits": sp,
+                                  "us": round(t * 1e6, 2), "GBps": round(byts / t / 1e9, 1),
+                                  "frac_hbm": round(byts / t / bw, 3), "peaks": src}), flush=True)
+    K._ATTN_DECODE = True
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm"])
+    ap.add_argument("what", choices=["gemm", "attn"])
+    ap.add_argument("--ctx", default="1500,4096,16384")
+    ap.add_argument("--splits", default="1,4,8,17,32")
+    ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--m", default="1,8,16,64,256,1024,4096")
     ap.add_argument("--shape", default="", help="comma list of shape names (default: all)")
     ap.add_argument("--iters", type=int, default=50)
@@ -86,6 +152,9 @@ def main():
         shapes = [sh for sh in shapes if sh[2] in keep]
     if a.what == "gemm":
         bench_gemm(ms, shapes)
+    elif a.what == "attn":
+        bench_attn([int(v) for v in a.ctx.split(",")], [int(v) for v in a.splits.split(",")],
+                   a.batch)
 
 
 if __name__ == "__main__":

@@ -260,18 +260,30 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(
     //      multiple of 64), converting fp8 / int4 to bf16 in shared memory ----
     const int key0 = kt * BC;
     if constexpr (FMT == 1) {
-      for (int idx = threadIdx.x; idx < BC * D / 16; idx += 128) {
-        const int r = idx / (D / 16), c16 = idx % (D / 16);   // 16 fp8 = two bf16 chunks
+      // all of this thread's 16-byte loads of the tile are issued before the first conversion, so
+      // a tile costs about one memory latency instead of one per chunk
+      constexpr int IT = BC * D / 16 / 128;
+      uint4 kraw[IT], vraw[IT];
+#pragma unroll
+      for (int it = 0; it < IT; ++it) {
+        const int idx = threadIdx.x + it * 128;
+        const int r = idx / (D / 16), c16 = idx % (D / 16);
         const int key = key0 + r;
-        uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+        kraw[it] = make_uint4(0, 0, 0, 0);
+        vraw[it] = make_uint4(0, 0, 0, 0);
         if (key < L) {
           const int blk = block_tables[(size_t)b * bt_stride + key / block_size];
           const size_t base = (((size_t)blk * Hkv + hk) * block_size + key % block_size) * D;
-          kv = *reinterpret_cast<const uint4*>(k_cache + base + c16 * 16);
-          vv = *reinterpret_cast<const uint4*>(v_cache + base + c16 * 16);
+          kraw[it] = __ldg(reinterpret_cast<const uint4*>(k_cache + base + c16 * 16));
+          vraw[it] = __ldg(reinterpret_cast<const uint4*>(v_cache + base + c16 * 16));
         }
-        const uint8_t* kb = reinterpret_cast<const uint8_t*>(&kv);
-        const uint8_t* vb = reinterpret_cast<const uint8_t*>(&vv);
+      }
+#pragma unroll
+      for (int it = 0; it < IT; ++it) {
+        const int idx = threadIdx.x + it * 128;
+        const int r = idx / (D / 16), c16 = idx % (D / 16);   // 16 fp8 = two bf16 chunks
+        const uint8_t* kb = reinterpret_cast<const uint8_t*>(&kraw[it]);
+        const uint8_t* vb = reinterpret_cast<const uint8_t*>(&vraw[it]);
         uint32_t kw[8], vw[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
@@ -285,33 +297,46 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(
       }
     } else if constexpr (FMT == 2) {
       constexpr int RB = D / 2 + D / 4;
-      for (int idx = threadIdx.x; idx < BC * D / 16; idx += 128) {
-        const int r = idx / (D / 16), g = idx % (D / 16);     // one 16-element group
+      constexpr int IT = BC * D / 16 / 128;
+      // raw loads of the whole tile first (nibbles + (scale, zero) per 16-element group)
+      uint2 knib[IT], vnib[IT];
+      __half2 kmz[IT], vmz[IT];
+#pragma unroll
+      for (int it = 0; it < IT; ++it) {
+        const int idx = threadIdx.x + it * 128;
+        const int r = idx / (D / 16), g = idx % (D / 16);
         const int key = key0 + r;
-        uint32_t kw[8], vw[8];
+        knib[it] = vnib[it] = make_uint2(0, 0);
+        kmz[it] = vmz[it] = __floats2half2_rn(0.f, 0.f);
         if (key < L) {
           const int blk = block_tables[(size_t)b * bt_stride + key / block_size];
           const size_t row = (((size_t)blk * Hkv + hk) * block_size + key % block_size) * RB;
+          knib[it] = __ldg(reinterpret_cast<const uint2*>(k_cache + row + g * 8));
+          vnib[it] = __ldg(reinterpret_cast<const uint2*>(v_cache + row + g * 8));
+          kmz[it] = *reinterpret_cast<const __half2*>(k_cache + row + D / 2 + g * 4);
+          vmz[it] = *reinterpret_cast<const __half2*>(v_cache + row + D / 2 + g * 4);
+        }
+      }
 #pragma unroll
-          for (int which = 0; which < 2; ++which) {
-            const uint8_t* src = (which == 0 ? k_cache : v_cache) + row;
-            const uint2 nib = *reinterpret_cast<const uint2*>(src + g * 8);
-            const __half2 m = *reinterpret_cast<const __half2*>(src + D / 2 + g * 4);
-            const float sc = __low2float(m), zr = __high2float(m);
-            uint32_t* w = which == 0 ? kw : vw;
-            const uint32_t lo32 = nib.x, hi32 = nib.y;
+      for (int it = 0; it < IT; ++it) {
+        const int idx = threadIdx.x + it * 128;
+        const int r = idx / (D / 16), g = idx % (D / 16);     // one 16-element group
+        uint32_t kw[8], vw[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const uint32_t word = e < 4 ? lo32 : hi32;
-              const int sh = (e % 4) * 8;
-              const float a = (float)((word >> sh) & 0xF) * sc + zr;
-              const float c = (float)((word >> (sh + 4)) & 0xF) * sc + zr;
-              w[e] = pack_bf16(a, c);
-            }
+        for (int which = 0; which < 2; ++which) {
+          const uint2 nib = which == 0 ? knib[it] : vnib[it];
+          const __half2 m = which == 0 ? kmz[it] : vmz[it];
+          const float sc = __low2float(m), zr = __high2float(m);
+          uint32_t* w = which == 0 ? kw : vw;
+          const uint32_t lo32 = nib.x, hi32 = nib.y;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const uint32_t word = e < 4 ? lo32 : hi32;
+            const int sh = (e % 4) * 8;
+            const float a = (float)((word >> sh) & 0xF) * sc + zr;
+            const float c = (float)((word >> (sh + 4)) & 0xF) * sc + zr;
+            w[e] = pack_bf16(a, c);
           }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) kw[e] = vw[e] = 0u;
         }
         *reinterpret_cast<uint4*>(sK + swz(r, 2 * g, CH)) = make_uint4(kw[0], kw[1], kw[2], kw[3]);
         *reinterpret_cast<uint4*>(sK + swz(r, 2 * g + 1, CH)) = make_uint4(kw[4], kw[5], kw[6], kw[7]);
@@ -321,22 +346,39 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(
     } else {
       const __nv_bfloat16* kc = reinterpret_cast<const __nv_bfloat16*>(k_cache);
       const __nv_bfloat16* vc = reinterpret_cast<const __nv_bfloat16*>(v_cache);
-      for (int idx = threadIdx.x; idx < BC * CH; idx += 128) {
-        const int r = idx / CH, c = idx % CH;
-        const int key = key0 + r;
-        uint4 kx = make_uint4(0, 0, 0, 0), vx = make_uint4(0, 0, 0, 0);
-        if (key < L) {
-          const int blk = block_tables[(size_t)b * bt_stride + key / block_size];
-          const size_t base = (((size_t)blk * Hkv + hk) * block_size + key % block_size) * D;
-          kx = *reinterpret_cast<const uint4*>(kc + base + c * 8);
-          vx = *reinterpret_cast<const uint4*>(vc + base + c * 8);
+      // loads issued in batches of up to 8 chunks per thread before the shared-memory stores
+      constexpr int IT = BC * CH / 128;
+      constexpr int BATCH = IT < 8 ? IT : 8;
+#pragma unroll
+      for (int it0 = 0; it0 < IT; it0 += BATCH) {
+        uint4 kx[BATCH], vx[BATCH];
+#pragma unroll
+        for (int u = 0; u < BATCH; ++u) {
+          const int idx = threadIdx.x + (it0 + u) * 128;
+          const int r = idx / CH, c = idx % CH;
+          const int key = key0 + r;
+          kx[u] = make_uint4(0, 0, 0, 0);
+          vx[u] = make_uint4(0, 0, 0, 0);
+          if (key < L) {
+            const int blk = block_tables[(size_t)b * bt_stride + key / block_size];
+            const size_t base = (((size_t)blk * Hkv + hk) * block_size + key % block_size) * D;
+            kx[u] = __ldg(reinterpret_cast<const uint4*>(kc + base + c * 8));
+            vx[u] = __ldg(reinterpret_cast<const uint4*>(vc + base + c * 8));
+          }
         }
-        *reinterpret_cast<uint4*>(sK + swz(r, c, CH)) = kx;
-        *reinterpret_cast<uint4*>(sV + swz(r, c, CH)) = vx;
+#pragma unroll
+        for (int u = 0; u < BATCH; ++u) {
+          const int idx = threadIdx.x + (it0 + u) * 128;
+          const int r = idx / CH, c = idx % CH;
+          *reinterpret_cast<uint4*>(sK + swz(r, c, CH)) = kx[u];
+          *reinterpret_cast<uint4*>(sV + swz(r, c, CH)) = vx[u];
+        }
       }
     }
     __syncthreads();
 
+    // warps whose 16 rows are all padding (decode: G rows per kv head) skip the math
+    if (warp * 16 >= rows_here) continue;
     // ---- S = Q K^T (16 rows x 64 keys per warp) ----
     float s[NT][4];
 #pragma unroll
@@ -473,33 +515,497 @@ __global__ void __launch_bounds__(128) paged_attn_kernel(
     if (!s_last) return;
     __threadfence();
     constexpr int PER = D / 32;
+    // splits past `used` had an empty key range; lane sp handles split sp's (m, l) (num_splits
+    // <= 32 by construction of the host split count)
+    const int used = per > 0 ? min(num_splits, (ntiles + per - 1) / per) : 1;
     for (int rr = warp; rr < rows_here; rr += 4) {
       const int r = row0 + rr;
       const int i = r / G, g = r % G;
       const size_t gw = (size_t)(s0 + i) * Hq + hk * G + g;
-      float mmax = -INFINITY;
-      for (int sp = 0; sp < num_splits; ++sp) {
-        const float m = __ldcg(part_ml + ((size_t)sp * T * Hq + gw) * 2);
-        const float l = __ldcg(part_ml + ((size_t)sp * T * Hq + gw) * 2 + 1);
-        if (l > 0.f) mmax = fmaxf(mmax, m);
+      float m = -INFINITY, l = 0.f;
+      if (lane < used) {
+        m = __ldcg(part_ml + ((size_t)lane * T * Hq + gw) * 2);
+        l = __ldcg(part_ml + ((size_t)lane * T * Hq + gw) * 2 + 1);
       }
+      float mmax = l > 0.f ? m : -INFINITY;
+#pragma unroll
+      for (int o2 = 16; o2 > 0; o2 >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffff, mmax, o2));
+      const float wl = l > 0.f ? l * exp2f(m - mmax) : 0.f;
+      float wsum = wl;
+#pragma unroll
+      for (int o2 = 16; o2 > 0; o2 >>= 1) wsum += __shfl_xor_sync(0xffffffff, wsum, o2);
       float acc[PER];
 #pragma unroll
       for (int p = 0; p < PER; ++p) acc[p] = 0.f;
-      float wsum = 0.f;
-      for (int sp = 0; sp < num_splits; ++sp) {
-        const float m = __ldcg(part_ml + ((size_t)sp * T * Hq + gw) * 2);
-        const float l = __ldcg(part_ml + ((size_t)sp * T * Hq + gw) * 2 + 1);
-        if (!(l > 0.f)) continue;
-        const float w = l * exp2f(m - mmax);
-        wsum += w;
-        const float* src = part_o + ((size_t)sp * T * Hq + gw) * D;
+      for (int sp0 = 0; sp0 < used; sp0 += 4) {
+        float2 v[4][PER / 2];
+        float w4[4];
 #pragma unroll
-        for (int p = 0; p < PER; ++p) acc[p] += w * __ldcg(src + lane * PER + p);
+        for (int u = 0; u < 4; ++u) {
+          const int sp = sp0 + u;
+          w4[u] = __shfl_sync(0xffffffff, wl, sp < used ? sp : 0);
+          if (sp >= used) w4[u] = 0.f;
+          const float2* src = reinterpret_cast<const float2*>(
+              part_o + ((size_t)(sp < used ? sp : 0) * T * Hq + gw) * D + lane * PER);
+#pragma unroll
+          for (int p = 0; p < PER / 2; ++p) v[u][p] = w4[u] > 0.f ? __ldcg(src + p) : make_float2(0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int p = 0; p < PER / 2; ++p) {
+            acc[2 * p + 0] += w4[u] * v[u][p].x;
+            acc[2 * p + 1] += w4[u] * v[u][p].y;
+          }
       }
       const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
 #pragma unroll
       for (int p = 0; p < PER; ++p) out[gw * D + lane * PER + p] = __float2bfloat16_rn(acc[p] * inv);
+    }
+    if (threadIdx.x == 0) counters[tile * Hkv + hk] = 0;
+  }
+}
+
+
+// ------------------------------------------------------------------------------------------------
+// decode attention: at most 16 query rows per (sequence, kv head) -- one token's G query heads,
+// or a short verify window when G * q_len <= 16.  The four warps split each 64-key tile's keys
+// (16 each) instead of its rows, each keeps its own running (max, sum, O), and the CTA merges
+// them in shared memory at the end.  With an fp8 cache, K/V convert to f16 with the hardware
+// e4m3x2 -> f16x2 conversion and the MMAs run in f16 (exact: the query is e4m3-rounded when the
+// cache is fp8, and e4m3 values are exact in f16); other formats use bf16 as the general kernel.
+// ------------------------------------------------------------------------------------------------
+DEVI void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                  uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+DEVI uint32_t pack_f16(float a, float b) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+DEVI uint32_t e4m3x2_to_f16x2(uint16_t v) {
+  __half2_raw h = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)v, __NV_E4M3);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <int D, int FMT>
+__global__ void __launch_bounds__(128) paged_attn_decode_kernel(
+    const __nv_bfloat16* __restrict__ q, const uint8_t* __restrict__ k_cache,
+    const uint8_t* __restrict__ v_cache, const int* __restrict__ block_tables, int bt_stride,
+    const int* __restrict__ seq_lens, const int* __restrict__ qsl,
+    const int* __restrict__ tile_seq, const int* __restrict__ tile_row0, int Hq, int Hkv,
+    int block_size, float scale_log2, int causal, int window, int num_splits,
+    __nv_bfloat16* __restrict__ out, float* __restrict__ part_o, float* __restrict__ part_ml,
+    int T, unsigned* __restrict__ counters) {
+  pdl_wait();     // inputs come from the preceding kernel
+  pdl_trigger();
+  constexpr bool F16 = (FMT == 1);
+  constexpr int QR = 16;                  // query rows per CTA
+  constexpr int CH = D / 8;               // 16-byte chunks per row (16-bit elements)
+  constexpr int OT = D / 8;
+  __shared__ bool s_last;
+  __shared__ float s_ml[4][QR][2];
+  __shared__ float s_fin[QR][2];
+  __shared__ float s_w[QR][33];
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* sQ = smem;                                   // [16][D]
+  uint8_t* sK = smem + QR * D * 2;                      // [64][D]
+  uint8_t* sV = sK + BC * D * 2;                        // [64][D]
+
+  const int tile = blockIdx.x, hk = blockIdx.y, split = blockIdx.z;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int b = tile_seq[tile];
+  const int row0 = tile_row0[tile];
+  const int G = Hq / Hkv;
+  const int s0 = qsl[b];
+  const int ql = qsl[b + 1] - s0;
+  const int L = seq_lens[b];
+  const int R = ql * G;
+  const int rows_here = min(QR, R - row0);
+  const int last_i = (row0 + rows_here - 1) / G;
+  const int first_i = row0 / G;
+  const int kv_end = causal ? (L - ql + last_i + 1) : L;
+  int kv_begin = 0;
+  if (window > 0) kv_begin = max(0, L - ql + first_i - window + 1);
+  const int ntiles_total = (kv_end + BC - 1) / BC;
+  const int tile_begin = kv_begin / BC;
+  const int ntiles = ntiles_total - tile_begin;
+  const int per = (ntiles + num_splits - 1) / num_splits;
+  const int t_lo = tile_begin + split * per;
+  const int t_hi = min(ntiles_total, t_lo + per);
+
+  // fp8 cache: the first tile's loads are issued before the query is staged, so both latencies
+  // overlap
+  constexpr int IT1 = BC * D / 16 / 128;
+  uint4 kraw[IT1], vraw[IT1];
+  auto load_raw = [&](int kt) {
+#pragma unroll
+    for (int it = 0; it < IT1; ++it) {
+      const int idx = threadIdx.x + it * 128;
+      const int r = idx / (D / 16), c16 = idx % (D / 16);
+      const int key = kt * BC + r;
+      kraw[it] = make_uint4(0, 0, 0, 0);
+      vraw[it] = make_uint4(0, 0, 0, 0);
+      if (key < L) {
+        const int blk = block_tables[(size_t)b * bt_stride + key / block_size];
+        const size_t base = (((size_t)blk * Hkv + hk) * block_size + key % block_size) * D;
+        kraw[it] = __ldg(reinterpret_cast<const uint4*>(k_cache + base + c16 * 16));
+        vraw[it] = __ldg(reinterpret_cast<const uint4*>(v_cache + base + c16 * 16));
+      }
+    }
+  };
+  if constexpr (FMT == 1) {
+    if (t_lo < t_hi) load_raw(t_lo);
+  }
+
+  // ---- Q (16 rows; rows past R are zero) ----
+  for (int idx = threadIdx.x; idx < QR * CH; idx += 128) {
+    const int r = idx / CH, c = idx % CH;
+    uint4 val = make_uint4(0, 0, 0, 0);
+    const int rr = row0 + r;
+    if (r < rows_here) {
+      const int i = rr / G, g = rr % G;
+      val = *reinterpret_cast<const uint4*>(q + ((size_t)(s0 + i) * Hq + hk * G + g) * D + c * 8);
+      if constexpr (F16) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&val);
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h[e]);
+          w[e] = pack_f16(f.x, f.y);
+        }
+        val = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+    *reinterpret_cast<uint4*>(sQ + swz(r, c, CH)) = val;
+  }
+
+  float o[OT][4];
+#pragma unroll
+  for (int j = 0; j < OT; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  const int g_ = lane / 4, t4 = lane % 4;
+  const int rA = row0 + g_, rB = rA + 8;
+  const int posA = L - ql + rA / G, posB = L - ql + rB / G;
+  const uint32_t sQa = smem_u32(sQ), sKa = smem_u32(sK), sVa = smem_u32(sV);
+  const int kw0 = warp * 16;              // this warp's keys within the tile
+
+  for (int kt = t_lo; kt < t_hi; ++kt) {
+    __syncthreads();
+    const int key0 = kt * BC;
+    if constexpr (FMT == 1) {
+      constexpr int IT = IT1;
+      if (kt != t_lo) load_raw(kt);
+#pragma unroll
+      for (int it = 0; it < IT; ++it) {
+        const int idx = threadIdx.x + it * 128;
+        const int r = idx / (D / 16), c16 = idx % (D / 16);
+        const uint16_t* kb = reinterpret_cast<const uint16_t*>(&kraw[it]);
+        const uint16_t* vb = reinterpret_cast<const uint16_t*>(&vraw[it]);
+        uint32_t kw[8], vw[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          kw[e] = e4m3x2_to_f16x2(kb[e]);
+          vw[e] = e4m3x2_to_f16x2(vb[e]);
+        }
+        *reinterpret_cast<uint4*>(sK + swz(r, 2 * c16, CH)) = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+        *reinterpret_cast<uint4*>(sK + swz(r, 2 * c16 + 1, CH)) = make_uint4(kw[4], kw[5], kw[6], kw[7]);
+        *reinterpret_cast<uint4*>(sV + swz(r, 2 * c16, CH)) = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+        *reinterpret_cast<uint4*>(sV + swz(r, 2 * c16 + 1, CH)) = make_uint4(vw[4], vw[5], vw[6], vw[7]);
+      }
+    } else if constexpr (FMT == 2) {
+      constexpr int RB = D / 2 + D / 4;
+      constexpr int IT = BC * D / 16 / 128;
+      uint2 knib[IT], vnib[IT];
+      __half2 kmz[IT], vmz[IT];
+#pragma unroll
+      for (int it = 0; it < IT; ++it) {
+        const int idx = threadIdx.x + it * 128;
+        const int r = idx / (D / 16), g = idx % (D / 16);
+        const int key = key0 + r;
+        knib[it] = vnib[it] = make_uint2(0, 0);
+        kmz[it] = vmz[it] = __floats2half2_rn(0.f, 0.f);
+        if (key < L) {
+          const int blk = block_tables[(size_t)b * bt_stride + key / block_size];
+          const size_t row = (((size_t)blk * Hkv + hk) * block_size + key % block_size) * RB;
+          knib[it] = __ldg(reinterpret_cast<const uint2*>(k_cache + row + g * 8));
+          vnib[it] = __ldg(reinterpret_cast<const uint2*>(v_cache + row + g * 8));
+          kmz[it] = *reinterpret_cast<const __half2*>(k_cache + row + D / 2 + g * 4);
+          vmz[it] = *reinterpret_cast<const __half2*>(v_cache + row + D / 2 + g * 4);
+        }
+      }
+#pragma unroll
+      for (int it = 0; it < IT; ++it) {
+        const int idx = threadIdx.x + it * 128;
+        const int r = idx / (D / 16), g = idx % (D / 16);
+        uint32_t kw[8], vw[8];
+#pragma unroll
+        for (int which = 0; which < 2; ++which) {
+          const uint2 nib = which == 0 ? knib[it] : vnib[it];
+          const __half2 m = which == 0 ? kmz[it] : vmz[it];
+          const float sc = __low2float(m), zr = __high2float(m);
+          uint32_t* w = which == 0 ? kw : vw;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const uint32_t word = e < 4 ? nib.x : nib.y;
+            const int sh = (e % 4) * 8;
+            w[e] = pack_bf16((float)((word >> sh) & 0xF) * sc + zr,
+                             (float)((word >> (sh + 4)) & 0xF) * sc + zr);
+          }
+        }
+        *reinterpret_cast<uint4*>(sK + swz(r, 2 * g, CH)) = make_uint4(kw[0], kw[1], kw[2], kw[3]);
+        *reinterpret_cast<uint4*>(sK + swz(r, 2 * g + 1, CH)) = make_uint4(kw[4], kw[5], kw[6], kw[7]);
+        *reinterpret_cast<uint4*>(sV + swz(r, 2 * g, CH)) = make_uint4(vw[0], vw[1], vw[2], vw[3]);
+        *reinterpret_cast<uint4*>(sV + swz(r, 2 * g + 1, CH)) = make_uint4(vw[4], vw[5], vw[6], vw[7]);
+      }
+    } else {
+      const __nv_bfloat16* kc = reinterpret_cast<const __nv_bfloat16*>(k_cache);
+      const __nv_bfloat16* vc = reinterpret_cast<const __nv_bfloat16*>(v_cache);
+      constexpr int IT = BC * CH / 128;
+      constexpr int BATCH = IT < 8 ? IT : 8;
+#pragma unroll
+      for (int it0 = 0; it0 < IT; it0 += BATCH) {
+        uint4 kx[BATCH], vx[BATCH];
+#pragma unroll
+        for (int u = 0; u < BATCH; ++u) {
+          const int idx = threadIdx.x + (it0 + u) * 128;
+          const int r = idx / CH, c = idx % CH;
+          const int key = key0 + r;
+          kx[u] = make_uint4(0, 0, 0, 0);
+          vx[u] = make_uint4(0, 0, 0, 0);
+          if (key < L) {
+            const int blk = block_tables[(size_t)b * bt_stride + key / block_size];
+            const size_t base = (((size_t)blk * Hkv + hk) * block_size + key % block_size) * D;
+            kx[u] = __ldg(reinterpret_cast<const uint4*>(kc + base + c * 8));
+            vx[u] = __ldg(reinterpret_cast<const uint4*>(vc + base + c * 8));
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < BATCH; ++u) {
+          const int idx = threadIdx.x + (it0 + u) * 128;
+          const int r = idx / CH, c = idx % CH;
+          *reinterpret_cast<uint4*>(sK + swz(r, c, CH)) = kx[u];
+          *reinterpret_cast<uint4*>(sV + swz(r, c, CH)) = vx[u];
+        }
+      }
+    }
+    __syncthreads();
+    const int k0 = key0 + kw0;
+    if (k0 >= kv_end) continue;           // this warp's 16 keys are all past the end
+
+    // ---- S = Q K^T: 16 rows x this warp's 16 keys ----
+    float sc[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) sc[j][0] = sc[j][1] = sc[j][2] = sc[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+      ldsm_x4(sQa + swz(lane % 16, kk * 2 + lane / 16, CH), a0, a1, a2, a3);
+      ldsm_x4(sKa + swz(kw0 + (lane % 8) + (lane / 16) * 8, kk * 2 + ((lane / 8) % 2), CH),
+              b0, b1, b2, b3);
+      if constexpr (F16) {
+        mma_f16(sc[0], a0, a1, a2, a3, b0, b1);
+        mma_f16(sc[1], a0, a1, a2, a3, b2, b3);
+      } else {
+        mma_bf16(sc[0], a0, a1, a2, a3, b0, b1);
+        mma_bf16(sc[1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    // ---- masks + online softmax (per warp) ----
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int key = k0 + j * 8 + 2 * t4 + (e & 1);
+        const int pos = (e < 2) ? posA : posB;
+        bool ok = key < L;
+        if (causal) ok = ok && key <= pos;
+        if (window > 0) ok = ok && key > pos - window;
+        const float v = ok ? sc[j][e] * scale_log2 : -INFINITY;
+        sc[j][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffff, mx[h], 1));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffff, mx[h], 2));
+    }
+    float alpha[2], mnew[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mnew[h] = fmaxf(m_run[h], mx[h]);
+      const float mref = mnew[h] == -INFINITY ? 0.f : mnew[h];
+      alpha[h] = exp2f(m_run[h] - mref);
+      m_run[h] = mnew[h];
+    }
+    float rsum[2] = {0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int h = e >> 1;
+        const float mref = mnew[h] == -INFINITY ? 0.f : mnew[h];
+        const float p = exp2f(sc[j][e] - mref);
+        sc[j][e] = p;
+        rsum[h] += p;
+      }
+    }
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      rsum[h] += __shfl_xor_sync(0xffffffff, rsum[h], 1);
+      rsum[h] += __shfl_xor_sync(0xffffffff, rsum[h], 2);
+      l_run[h] = l_run[h] * alpha[h] + rsum[h];
+    }
+#pragma unroll
+    for (int j = 0; j < OT; ++j) {
+      o[j][0] *= alpha[0]; o[j][1] *= alpha[0];
+      o[j][2] *= alpha[1]; o[j][3] *= alpha[1];
+    }
+    // ---- O += P V over this warp's 16 keys ----
+    uint32_t a0, a1, a2, a3;
+    if constexpr (F16) {
+      a0 = pack_f16(sc[0][0], sc[0][1]); a1 = pack_f16(sc[0][2], sc[0][3]);
+      a2 = pack_f16(sc[1][0], sc[1][1]); a3 = pack_f16(sc[1][2], sc[1][3]);
+    } else {
+      a0 = pack_bf16(sc[0][0], sc[0][1]); a1 = pack_bf16(sc[0][2], sc[0][3]);
+      a2 = pack_bf16(sc[1][0], sc[1][1]); a3 = pack_bf16(sc[1][2], sc[1][3]);
+    }
+#pragma unroll
+    for (int jn = 0; jn < OT; jn += 2) {
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(sVa + swz(kw0 + (lane % 8) + ((lane / 8) % 2) * 8, jn + lane / 16, CH), b0, b1, b2, b3);
+      if constexpr (F16) {
+        mma_f16(o[jn], a0, a1, a2, a3, b0, b1);
+        mma_f16(o[jn + 1], a0, a1, a2, a3, b2, b3);
+      } else {
+        mma_bf16(o[jn], a0, a1, a2, a3, b0, b1);
+        mma_bf16(o[jn + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+  }
+
+  // ---- merge the four warps: M = max_w m_w, L = sum_w l_w 2^(m_w - M), O = sum_w o_w 2^(m_w - M)
+  __syncthreads();                        // all warps are done with sK / sV
+  float* sOw = reinterpret_cast<float*>(sK);            // [4][16][D] fp32 (fits sK + sV)
+  if (t4 == 0) {
+    s_ml[warp][g_][0] = m_run[0];
+    s_ml[warp][g_][1] = l_run[0];
+    s_ml[warp][g_ + 8][0] = m_run[1];
+    s_ml[warp][g_ + 8][1] = l_run[1];
+  }
+  __syncthreads();
+  float wself[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = g_ + 8 * h;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w)
+      if (s_ml[w][r][1] > 0.f) M = fmaxf(M, s_ml[w][r][0]);
+    wself[h] = (l_run[h] > 0.f) ? exp2f(m_run[h] - M) : 0.f;
+    if (warp == 0 && t4 == 0) {
+      float Ls = 0.f;
+#pragma unroll
+      for (int w = 0; w < 4; ++w)
+        if (s_ml[w][r][1] > 0.f) Ls += s_ml[w][r][1] * exp2f(s_ml[w][r][0] - M);
+      s_fin[r][0] = M;
+      s_fin[r][1] = Ls;
+    }
+  }
+  float* myO = sOw + (size_t)warp * QR * D;
+#pragma unroll
+  for (int j = 0; j < OT; ++j) {
+    const int col = j * 8 + 2 * t4;
+    *reinterpret_cast<float2*>(myO + g_ * D + col) = make_float2(o[j][0] * wself[0], o[j][1] * wself[0]);
+    *reinterpret_cast<float2*>(myO + (g_ + 8) * D + col) =
+        make_float2(o[j][2] * wself[1], o[j][3] * wself[1]);
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < rows_here * (D / 4); idx += 128) {
+    const int r = idx / (D / 4), c = (idx % (D / 4)) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float4 v = *reinterpret_cast<const float4*>(sOw + ((size_t)w * QR + r) * D + c);
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    const float Ls = s_fin[r][1];
+    const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+    const int rr = row0 + r;
+    const int i = rr / G, g = rr % G;
+    const int tok = s0 + i, head = hk * G + g;
+    if (num_splits == 1) {
+      __nv_bfloat16* dst = out + ((size_t)tok * Hq + head) * D + c;
+      *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
+      *reinterpret_cast<__nv_bfloat162*>(dst + 2) = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
+    } else {
+      *reinterpret_cast<float4*>(part_o + (((size_t)split * T + tok) * Hq + head) * D + c) =
+          make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+      if (c == 0) {
+        float* ml = part_ml + (((size_t)split * T + tok) * Hq + head) * 2;
+        ml[0] = s_fin[r][0];
+        ml[1] = Ls;
+      }
+    }
+  }
+  if (num_splits > 1) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      s_last = atomicAdd(&counters[tile * Hkv + hk], 1u) == (unsigned)(num_splits - 1);
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // splits past `used` had an empty key range (num_splits <= 32 by the host check)
+    const int used = per > 0 ? min(num_splits, (ntiles + per - 1) / per) : 1;
+    // weights per (row, split): warp w handles rows w, w + 4, ...; lane = split
+    for (int r = warp; r < rows_here; r += 4) {
+      const int rr = row0 + r;
+      const size_t gw = (size_t)(s0 + rr / G) * Hq + hk * G + rr % G;
+      float m = -INFINITY, l = 0.f;
+      if (lane < used) {
+        m = __ldcg(part_ml + ((size_t)lane * T * Hq + gw) * 2);
+        l = __ldcg(part_ml + ((size_t)lane * T * Hq + gw) * 2 + 1);
+      }
+      float mmax = l > 0.f ? m : -INFINITY;
+#pragma unroll
+      for (int o2 = 16; o2 > 0; o2 >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffff, mmax, o2));
+      const float wl = l > 0.f ? l * exp2f(m - mmax) : 0.f;
+      float wsum = wl;
+#pragma unroll
+      for (int o2 = 16; o2 > 0; o2 >>= 1) wsum += __shfl_xor_sync(0xffffffff, wsum, o2);
+      s_w[r][lane] = wl;
+      if (lane == 0) s_w[r][32] = wsum;
+    }
+    __syncthreads();
+    // every split's partial of one 4-column group is loaded before any is summed
+    for (int idx = threadIdx.x; idx < rows_here * (D / 4); idx += 128) {
+      const int r = idx / (D / 4), c = (idx % (D / 4)) * 4;
+      const int rr = row0 + r;
+      const size_t gw = (size_t)(s0 + rr / G) * Hq + hk * G + rr % G;
+      float4 v[32];
+#pragma unroll
+      for (int sp = 0; sp < 32; ++sp)
+        if (sp < used) v[sp] = __ldcg(reinterpret_cast<const float4*>(part_o + ((size_t)sp * T * Hq + gw) * D + c));
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int sp = 0; sp < 32; ++sp)
+        if (sp < used) {
+          const float w = s_w[r][sp];
+          acc.x += w * v[sp].x; acc.y += w * v[sp].y; acc.z += w * v[sp].z; acc.w += w * v[sp].w;
+        }
+      const float wsum = s_w[r][32];
+      const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+      __nv_bfloat16* dst = out + gw * D + c;
+      *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
+      *reinterpret_cast<__nv_bfloat162*>(dst + 2) = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
     }
     if (threadIdx.x == 0) counters[tile * Hkv + hk] = 0;
   }
@@ -581,14 +1087,15 @@ void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
                      torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor qsl,
                      torch::Tensor tile_seq, torch::Tensor tile_row0, double scale, bool causal,
                      int64_t window, int64_t num_splits, torch::Tensor part_o,
-                     torch::Tensor part_ml, torch::Tensor out, torch::Tensor counters) {
+                     torch::Tensor part_ml, torch::Tensor out, torch::Tensor counters,
+                     bool decode) {
   const int T = q.size(0), Hq = q.size(1), D = q.size(2);
   const int Hkv = k_cache.size(1), block_size = k_cache.size(2);
   const int num_tiles = tile_seq.size(0);
   if (T == 0 || num_tiles == 0) return;
   TORCH_CHECK(block_size % attn::BC == 0 || attn::BC % block_size == 0,
               "KV page size must divide or be a multiple of 64");
-  TORCH_CHECK(num_splits >= 1, "num_splits");
+  TORCH_CHECK(num_splits >= 1 && num_splits <= 32, "num_splits must be in [1, 32]");
   const int fmt = k_cache.scalar_type() == at::kFloat8_e4m3fn ? 1
                 : k_cache.scalar_type() == at::kByte ? 2 : 0;
   const at::cuda::CUDAGuard guard(q.device());
@@ -598,9 +1105,11 @@ void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
   auto run = [&](auto dtag, auto ftag) {
     constexpr int Dc = decltype(dtag)::value;
     constexpr int F8 = decltype(ftag)::value;
-    const int smem = (attn::BR + 2 * attn::BC) * Dc * 2;
-    auto kern = attn::paged_attn_kernel<Dc, F8>;
-    static bool set = false;
+    // decode: tiles hold at most 16 query rows (the caller guarantees G * q_len <= 16)
+    const int smem = ((decode ? 16 : attn::BR) + 2 * attn::BC) * Dc * 2;
+    auto kern = decode ? attn::paged_attn_decode_kernel<Dc, F8> : attn::paged_attn_kernel<Dc, F8>;
+    static bool set_general = false, set_decode = false;
+    bool& set = decode ? set_decode : set_general;
     if (!set) {
       C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
       set = true;

@@ -36,7 +36,8 @@ void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
                      torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor qsl,
                      torch::Tensor tile_seq, torch::Tensor tile_row0, double scale, bool causal,
                      int64_t window, int64_t num_splits, torch::Tensor part_o,
-                     torch::Tensor part_ml, torch::Tensor out, torch::Tensor counters);
+                     torch::Tensor part_ml, torch::Tensor out, torch::Tensor counters,
+                     bool decode);
 void argmax_rows(torch::Tensor x, torch::Tensor out_ids, torch::Tensor out_vals,
                  torch::Tensor workspace);
 void sample_from_topk(torch::Tensor vals, torch::Tensor ids, torch::Tensor temperature,

@@ -107,10 +107,12 @@ class ModelRunner:
             tile_row0=d[L.tile_r:L.tile_r + ntiles],
             _scratch=self._scratch)
 
-    def _num_splits(self, B: int, ntiles: int, max_kv: int) -> int:
+    def _num_splits(self, B: int, ntiles: int, max_kv: int, decode: bool = False) -> int:
+        """KV splits per (row tile, kv head): fill ~2 CTAs per SM, at least 256 keys per split
+        (one 64-key tile for decode batches, whose per-tile work is small), at most 32."""
         ctas = max(1, ntiles * self.Hkv)
         s = max(1, min(32, 148 * 2 // ctas))
-        s = min(s, max(1, (max_kv + 255) // 256))
+        s = min(s, max(1, (max_kv + (63 if decode else 255)) // (64 if decode else 256)))
         return s
 
     def prepare(self, out: SchedulerOutput, pad_to: Optional[int] = None, nb_fixed: Optional[int] = None):
@@ -217,8 +219,9 @@ class ModelRunner:
         # decode batches size the split count for the longest context, in graphs (replays keep
         # the captured count) and eagerly alike, so both paths compute identical numerics
         all_decode = all(s.is_decode for s in seqs)
+        decode_rows = (pad_to or all_decode) and T == B and self.G <= 16
         meta.num_splits = self._num_splits(B, ntiles, self.max_blocks * bs if (pad_to or all_decode)
-                                           else max_kv)
+                                           else max_kv, decode=bool(decode_rows))
         ids = self.d_meta[L.ids:L.ids + T]
         return meta, ids, sample_idx, sample_cnt
 

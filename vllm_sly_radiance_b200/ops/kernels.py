@@ -5,6 +5,8 @@ from __future__ import annotations
 
 from typing import Optional
 
+import os
+
 import torch
 
 from . import reference as ref
@@ -248,6 +250,9 @@ def qkv_prologue(qkv, positions, q_norm_w, k_norm_w, cos_sin, k_cache, v_cache, 
     return q
 
 
+_ATTN_DECODE = os.environ.get("RADIANCE_ATTN_DECODE", "1") != "0"
+
+
 def paged_attention(q, k_cache, v_cache, meta, scale: float, causal: bool = True,
                     window: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Varlen paged attention over the batch described by ``meta`` (an AttnMeta)."""
@@ -263,10 +268,15 @@ def paged_attention(q, k_cache, v_cache, meta, scale: float, causal: bool = True
         part_ml = meta.scratch_ml(splits, T, Hq)
     else:
         part_o = part_ml = _empty(q.device)
+    # one query token per sequence and at most 16 query heads per kv head: the decode kernel
+    # (keys split across warps) replaces the 64-row tile kernel
+    decode = (meta.num_tokens == meta.num_seqs and Hq // k_cache.shape[1] <= 16
+              and _ATTN_DECODE)
     ext().paged_attention(q, k_cache, v_cache, meta.block_tables, meta.seq_lens,
                           meta.query_start_loc, meta.tile_seq, meta.tile_row0, scale, causal,
                           window, splits, part_o, part_ml, out,
-                          workspace(q.device, "attn", meta.tile_seq.shape[0] * k_cache.shape[1]))
+                          workspace(q.device, "attn", meta.tile_seq.shape[0] * k_cache.shape[1]),
+                          decode)
     return out
 
 
