@@ -112,6 +112,8 @@ def main():
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--kernel-profile", default=None,
                     help="write rank 0's per-kernel device time of one untimed decode step (JSON)")
+    ap.add_argument("--prefill-profile", default=None,
+                    help="write rank 0's per-kernel device time of one untimed prefill (JSON)")
     ap.add_argument("--no-profile-launches", action="store_true",
                     help="count launches from the model structure (for runs under an external profiler)")
     args = ap.parse_args()
@@ -196,6 +198,13 @@ def main():
         if args.no_profile_launches else \
         profiled_launches(eng, args.kernel_profile if rank == 0 else None)
     eng.abort_request("stream0")
+
+    if args.prefill_profile:
+        barrier()
+        eng.add_request(rand_prompt(args.prompt_len), SamplingParams(temperature=0, max_tokens=1,
+                                                                      ignore_eos=True), "pfp")
+        profile_steps(eng, args.prefill_profile if rank == 0 else None,
+                      lambda: eng.has_unfinished_requests())
 
     extra = {}
     if not args.no_extra:
@@ -283,6 +292,27 @@ def profiled_launches(eng, dump_path=None):
     except Exception:
         pass
     return count_launches(eng), "model-structure estimate"
+
+
+def profile_steps(eng, dump_path, more):
+    """Per-kernel device time over engine steps while more() holds (JSON to dump_path)."""
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        while more():
+            eng.step()
+        torch.cuda.synchronize()
+    if not dump_path:
+        return
+    agg = {}
+    for e in prof.events():
+        if e.device_type.name != "CUDA":
+            continue
+        a = agg.setdefault(e.name[:120], [0, 0.0])
+        a[0] += 1
+        a[1] += e.device_time
+    rows = sorted(([k, v[0], round(v[1], 2)] for k, v in agg.items()), key=lambda r: -r[2])
+    with open(dump_path, "w") as f:
+        json.dump({"kernel_us": round(sum(r[2] for r in rows), 1), "kernels": rows}, f, indent=0)
 
 
 def count_launches(eng):

@@ -68,3 +68,46 @@ def test_dflash2_drafter_runs_and_is_lossless_greedy():
     assert eng.spec.stats["draft_tokens"] > 0
     sp2 = SamplingParams(temperature=0.8, top_p=0.95, top_k=20, max_tokens=10, seed=1, ignore_eos=True)
     assert len(eng.generate([prompt], sp2)[0].outputs[0].token_ids) == 10
+
+
+def test_adaptive_width_choice_and_estimates():
+    """High-acceptance requests get long verify windows, low-acceptance ones short windows, and
+    the step-cost model refits from measured (rows, ms) samples."""
+    from vllm_sly_radiance_b200.spec_decode.adaptive import AdaptiveWidth
+    aw = AdaptiveWidth(widths=(1, 3, 5, 7), t0_ms=5.0, t1_ms=0.05)
+    for _ in range(40):
+        aw.observe("good", 7, 7)
+        aw.observe("bad", 7, 0)
+    assert aw.alpha("good") > 0.95 and aw.alpha("bad") < 0.1
+    w = aw.choose(["good", "bad", "new"], [7, 7, 7])
+    assert w[0] == 7 and w[1] == 1 and 1 <= w[2] <= 7
+    # fewer drafts available than the widths: never exceed them
+    assert aw.choose(["good"], [2]) == [1] or aw.choose(["good"], [2])[0] <= 2
+    # expected tokens: geometric sum incl. the bonus token
+    assert abs(AdaptiveWidth.expected_tokens(0.5, 3) - 1.875) < 1e-9
+    # cost refit from exact linear samples
+    for rows in (8, 16, 64, 128):
+        aw.record_step(rows, 3.0 + 0.02 * rows)
+    assert abs(aw.t0_ms - 3.0) < 1e-6 and abs(aw.t1_ms - 0.02) < 1e-6
+    # an expensive per-row cost shortens every window (4 requests: rows 8 at width 1, 32 at 7)
+    aw2 = AdaptiveWidth(t0_ms=1.0, t1_ms=2.0)
+    ids = ["a", "b", "c", "d"]
+    for _ in range(10):
+        for r in ids:
+            aw2.observe(r, 7, 4)
+    assert aw2.choose(ids, [7] * 4) == [1] * 4
+
+
+def test_adaptive_width_engine_runs():
+    """Spec decode with adaptive width through the engine (lookup drafts, CPU)."""
+    from vllm_sly_radiance_b200.config import EngineConfig
+    from vllm_sly_radiance_b200.engine.llm_engine import LLMEngine
+    from vllm_sly_radiance_b200.engine.request import SamplingParams
+    cfg = EngineConfig(model="tiny_hybrid", device="cpu", max_model_len=512, max_num_seqs=2,
+                       max_num_batched_tokens=256, num_kv_blocks=32, enable_cuda_graphs=False,
+                       speculative_method="lookup", num_speculative_tokens=7, adaptive_width=True)
+    eng = LLMEngine(cfg)
+    prompt = [5, 6, 7, 8, 9] * 12
+    out = eng.generate([prompt], SamplingParams(temperature=0, max_tokens=12, ignore_eos=True))
+    assert len(out[0].outputs[0].token_ids) == 12
+    assert eng.spec.adaptive is not None

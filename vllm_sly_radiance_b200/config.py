@@ -273,6 +273,7 @@ class EngineConfig:
     # speculative decoding
     speculative_method: Optional[str] = None   # None | "dflash2" | "lookup"
     num_speculative_tokens: int = 7
+    adaptive_width: bool = False     # per-request verify width from acceptance + step-cost model
     acceptance_rule: str = "leviathan"          # leviathan | cactus | nsd
     forced_acceptance: Optional[str] = None     # benchmarking: "uniform07" forced schedule
     # comm

@@ -15,6 +15,9 @@ Proposers:
                 request's suffix (``sly/radiance_lookup_draft.py``: suffix up to 24 tokens over the
                 whole history, point-mass drafts, lossless).
   * ``dflash2`` the DFlash2 block drafter (``models/dflash2.py``).
+Adaptive verify width (``spec_decode/adaptive.py``, opt-in ``adaptive_width``) truncates each
+request's drafts to the width that maximises expected tokens per unit of step time.
+
   * ``forced``  benchmark mode: drafts from the lookup proposer (or repeats), acceptance forced
                 by a fixed schedule (mean 5.5 of 7) so verify throughput is measurable with random
                 weights.
@@ -30,6 +33,7 @@ import torch
 from ..engine.model_runner import StepResult
 from ..engine.sampler import SamplingTensors, apply_penalties, row_seed, sample
 from ..engine.scheduler import SchedulerOutput
+from .adaptive import AdaptiveWidth
 from .rejection import AcceptRule, ForcedAcceptance, rejection_sample
 
 
@@ -63,7 +67,8 @@ class LookupProposer:
 
 class SpecRunner:
     def __init__(self, engine, method: str, k: int, rule: AcceptRule,
-                 forced: Optional[ForcedAcceptance] = None, drafter=None):
+                 forced: Optional[ForcedAcceptance] = None, drafter=None,
+                 adaptive: Optional[AdaptiveWidth] = None):
         self.engine = engine
         self.runner = engine.runner
         self.model = engine.model
@@ -75,6 +80,7 @@ class SpecRunner:
         self.lookup = LookupProposer(k)
         self.gen = None
         self.stats = dict(steps=0, drafts=0, draft_tokens=0, accepted=0)
+        self.adaptive = adaptive
 
     # ------------------------------------------------------------------------------------------
     def execute(self, sched: SchedulerOutput) -> StepResult:
@@ -86,6 +92,7 @@ class SpecRunner:
             self._propose(sched, res.sampled)
             return res
         r.step_count += 1
+        t_step = time.perf_counter()
         meta, ids, sample_idx, sample_cnt = r.prepare(sched)
         commit = [0 if (s.is_decode and s.draft_tokens) else s.num_new_tokens for s in sched.seqs]
         meta.commit_len = torch.tensor(commit, dtype=torch.int32).to(dev, non_blocking=True)
@@ -142,10 +149,15 @@ class SpecRunner:
                 sampled[s.req.request_id] = [t for t in o[:n + 1]]
                 commit_len[bi] = 1 + n
                 n_acc_all.append(n)
+                if self.adaptive is not None:
+                    self.adaptive.observe(s.req.request_id, k, n)
         # commit the accepted prefixes to the GDN state
         cl = torch.tensor(commit_len, dtype=torch.int32).to(dev, non_blocking=True)
         meta.commit_len = None
         self.model.commit_gdn(meta, r.caches, saved, cl)
+        if self.adaptive is not None and verify:
+            # the step already synchronised on the sampled tokens: wall time ~ device time
+            self.adaptive.record_step(meta.num_tokens, (time.perf_counter() - t_step) * 1e3)
         self.stats["steps"] += 1
         self.stats["drafts"] += len(verify)
         self.stats["draft_tokens"] += sum(len(s.draft_tokens) for s in verify)
@@ -173,6 +185,10 @@ class SpecRunner:
             drafts = [self.lookup.propose_one(r.all_token_ids + t) for r, t in reqs]
             if self.forced is not None:
                 drafts = [(d + [t[-1]] * self.k)[:self.k] for d, (r, t) in zip(drafts, reqs)]
+        if self.adaptive is not None:
+            widths = self.adaptive.choose([r.request_id for r, _ in reqs],
+                                          [min(len(d), self.k) for d in drafts])
+            drafts = [d[:w] for d, w in zip(drafts, widths)]
         for (req, _), d in zip(reqs, drafts):
             req.draft_token_ids = list(d[:self.k])
 
@@ -187,4 +203,5 @@ def build_proposer(config, engine) -> SpecRunner:
         drafter = DFlash2Drafter.for_engine(engine, k)
     elif config.speculative_method not in ("lookup", "forced"):
         raise ValueError(f"unknown speculative method {config.speculative_method!r}")
-    return SpecRunner(engine, config.speculative_method, k, rule, forced, drafter)
+    adaptive = AdaptiveWidth.from_env(k) if config.adaptive_width else None
+    return SpecRunner(engine, config.speculative_method, k, rule, forced, drafter, adaptive)
