@@ -134,3 +134,49 @@ def test_kv4_cache_engine_and_capacity():
     per_tok4 = m.cache_bytes_per_block(16, "int4") / 16
     per_tok8 = m.cache_bytes_per_block(64, "fp8") / 64
     assert per_tok4 < per_tok8
+
+
+def _prefix_engine(prefix, interval=0):
+    cfg = EngineConfig(model="tiny_hybrid", device="cpu", max_model_len=1024, max_num_seqs=4,
+                       max_num_batched_tokens=4096, enable_cuda_graphs=False,
+                       num_kv_blocks=64, block_size=16, enable_prefix_caching=prefix,
+                       prefix_snapshot_slots=4, prefix_snapshot_interval=interval)
+    return LLMEngine(cfg)
+
+
+def _first_step_logits(eng, prompt):
+    """Logits of the first sampled position; also the prompt tokens skipped by the cache."""
+    eng.add_request(prompt, SamplingParams(temperature=0, max_tokens=1), "r2")
+    skipped = None
+    while True:
+        sched = eng.scheduler.schedule()
+        if skipped is None:
+            skipped = sched.seqs[0].req.num_computed_tokens
+        for s in sched.seqs:
+            if s.req.restore_snapshot is not None:
+                eng.model.copy_state(eng.caches, s.req.restore_snapshot, s.req.state_slot)
+                s.req.restore_snapshot = None
+        res = eng.runner.execute(sched, want_logits=True)
+        eng.scheduler.update(sched, res.sampled)
+        if res.sampled:
+            return res.logits.float(), skipped
+
+
+@pytest.mark.parametrize("interval,second_len,skip", [(0, None, 144), (64, 140, 128)])
+def test_prefix_caching_restores_gdn_state(interval, second_len, skip):
+    """A prompt sharing a cached prefix skips those tokens (attention blocks + the GDN state
+    snapshot at a block boundary) and produces the logits of a full recompute: a multi-turn
+    continuation (snapshot at the previous prompt's last boundary) and a shared leading part
+    (snapshots every `interval` tokens)."""
+    base = torch.randint(3, 4096, (150,), generator=torch.Generator().manual_seed(3)).tolist()
+    second = (base + [11, 12, 13, 14, 15]) if second_len is None else \
+        (base[:second_len] + [11, 12, 13, 14, 15])
+    eng = _prefix_engine(True, interval)
+    eng.generate([base], SamplingParams(temperature=0, max_tokens=2, ignore_eos=True))
+    assert eng.kv.snap_by_hash, "no GDN snapshot taken"
+    got, skipped = _first_step_logits(eng, second)
+    assert skipped == skip, skipped
+    want = _prefill_logits(_prefix_engine(False), second)
+    rel = float((got - want).abs().max() / want.abs().max())
+    assert rel < 2e-2, rel
+    assert eng.kv.hits >= 1

@@ -269,6 +269,8 @@ class EngineConfig:
     enable_cuda_graphs: bool = True
     cuda_graph_max_bs: int = 64
     enable_prefix_caching: bool = False
+    prefix_snapshot_slots: int = 16  # GDN state snapshots kept for cached prefixes
+    prefix_snapshot_interval: int = 0  # also snapshot every N prompt tokens (0: last boundary only)
     seed: int = 0
     # speculative decoding
     speculative_method: Optional[str] = None   # None | "dflash2" | "lookup"

@@ -65,11 +65,24 @@ class SlotPool:
 
 class KVCacheManager:
     def __init__(self, num_blocks: int, block_size: int, num_slots: int,
-                 enable_prefix_caching: bool = False):
+                 enable_prefix_caching: bool = False, num_snapshots: int = 0,
+                 snapshot_interval: int = 0):
         self.block_size = block_size
         self.blocks = BlockPool(num_blocks)
         self.slots = SlotPool(num_slots)
         self.enable_prefix_caching = enable_prefix_caching
+        # GDN state snapshots: extra state slots [num_slots, num_slots + num_snapshots) holding the
+        # conv + SSM state of a cached prefix at a block boundary, keyed by that prefix's hash
+        # (the attention KV alone cannot resume a hybrid model: the GDN layers need their state)
+        self.num_slots = num_slots
+        self.num_snapshots = num_snapshots if enable_prefix_caching else 0
+        self.snap_free = deque(range(num_slots, num_slots + self.num_snapshots))
+        self.snap_by_hash: dict[str, int] = {}
+        self.snap_lru: "OrderedDict[int, str]" = OrderedDict()
+        # besides the last boundary of every prompt, snapshot every `snapshot_interval` tokens
+        # (rounded to blocks) so prompts that share only a leading part (a system prompt) hit
+        self.snapshot_interval = (snapshot_interval // block_size * block_size
+                                  if snapshot_interval else 0)
         # prefix cache: hash -> block id (LRU of unreferenced cached blocks)
         self.cached: dict[str, int] = {}
         self.block_hash: dict[int, str] = {}
@@ -128,20 +141,70 @@ class KVCacheManager:
         return out
 
     def match_prefix(self, req: Request) -> int:
-        """Number of prompt tokens whose attention KV is cached (a multiple of block_size).
-        The GDN state at that boundary must also be available (see StateSnapshots)."""
+        """Number of prompt tokens that can be skipped: the longest run of cached attention
+        blocks whose end boundary also has a GDN state snapshot.  Sets `req.restore_snapshot`
+        (the snapshot slot to copy into the request's state slot before its first step)."""
         if not self.enable_prefix_caching:
             return 0
         self.queries += 1
+        hs = self._hashes(req.prompt_token_ids[:-1])
         n = 0
-        for h in self._hashes(req.prompt_token_ids[:-1]):
+        for h in hs:
             if h in self.cached:
                 n += 1
             else:
                 break
-        if n:
+        best = 0
+        for j in range(n, 0, -1):
+            sid = self.snap_by_hash.get(hs[j - 1])
+            if sid is not None:
+                self.snap_lru.move_to_end(sid)
+                req.restore_snapshot = sid
+                best = j
+                break
+        if best:
             self.hits += 1
-        return n * self.block_size
+        return best * self.block_size
+
+    # ---- GDN state snapshots ----
+    def snapshot_boundary(self, req: Request) -> int:
+        """The next token count (> computed) at which a prefill snapshots its GDN state: a
+        multiple of the snapshot interval, or the last block boundary before the prompt's final
+        token (0 = none left)."""
+        if not self.num_snapshots:
+            return 0
+        last = (req.num_prompt_tokens - 1) // self.block_size * self.block_size
+        c = req.num_computed_tokens
+        if self.snapshot_interval:
+            nxt = (c // self.snapshot_interval + 1) * self.snapshot_interval
+            if nxt < last:
+                return nxt
+        return last if last > c else 0
+
+    def is_snapshot_point(self, req: Request, n: int) -> bool:
+        last = (req.num_prompt_tokens - 1) // self.block_size * self.block_size
+        if n <= 0 or n > last:
+            return False
+        return n == last or (self.snapshot_interval and n % self.snapshot_interval == 0)
+
+    def take_snapshot(self, req: Request) -> Optional[int]:
+        """Reserve the snapshot slot for `req`'s prefix up to its current length when that is a
+        snapshot point (None when the prefix already has one, or snapshots are off).  The
+        caller copies the state into it."""
+        B = req.num_computed_tokens
+        if not self.num_snapshots or not self.is_snapshot_point(req, B):
+            return None
+        h = self._hashes(req.prompt_token_ids[:B])[-1]
+        if h in self.snap_by_hash:
+            return None
+        if not self.snap_free:
+            sid, old = self.snap_lru.popitem(last=False)
+            self.snap_by_hash.pop(old, None)
+        else:
+            sid = self.snap_free.popleft()
+        self.snap_by_hash[h] = sid
+        self.snap_lru[sid] = h
+        return sid
 
     def adopt_prefix(self, req: Request, num_tokens: int):
         hs = self._hashes(req.prompt_token_ids[:num_tokens])

@@ -51,7 +51,8 @@ class LLMEngine:
             torch.cuda.synchronize()
             free, total = torch.cuda.mem_get_info(self.device)
             per_block = max(1, model.cache_bytes_per_block(bs, config.kv_cache_dtype))
-            state = model.state_bytes_per_slot(config.ssm_state_dtype) * num_slots
+            n_snap_b = config.prefix_snapshot_slots if config.enable_prefix_caching else 0
+            state = model.state_bytes_per_slot(config.ssm_state_dtype) * (num_slots + n_snap_b)
             activ = 4 << 30   # activations / graphs headroom
             budget = int(free - (1 - config.gpu_memory_utilization) * total) - state - activ
             need = (config.max_model_len + bs - 1) // bs * config.max_num_seqs + 1
@@ -59,9 +60,15 @@ class LLMEngine:
         else:
             num_blocks = (config.max_model_len + bs - 1) // bs * config.max_num_seqs + 1
         self.num_blocks = int(num_blocks)
-        self.caches = model.make_caches(self.num_blocks, bs, num_slots, config.kv_cache_dtype,
-                                        config.ssm_state_dtype)
-        self.kv = KVCacheManager(self.num_blocks, bs, num_slots, config.enable_prefix_caching)
+        n_snap = config.prefix_snapshot_slots if config.enable_prefix_caching else 0
+        if n_snap and config.speculative_method == "dflash2":
+            raise ValueError("prefix caching with the DFlash2 drafter is not supported: a cached "
+                             "prefix would skip the target forward that feeds the drafter context")
+        self.caches = model.make_caches(self.num_blocks, bs, num_slots + n_snap,
+                                        config.kv_cache_dtype, config.ssm_state_dtype)
+        self.kv = KVCacheManager(self.num_blocks, bs, num_slots, config.enable_prefix_caching,
+                                 num_snapshots=n_snap,
+                                 snapshot_interval=config.prefix_snapshot_interval)
         k = config.num_speculative_tokens if config.speculative_method else 0
         self.scheduler = Scheduler(self.kv, config.max_num_seqs, config.max_num_batched_tokens,
                                    config.max_model_len, num_spec_tokens=k)
@@ -108,11 +115,21 @@ class LLMEngine:
         sched = self.scheduler.schedule()
         if sched.is_empty:
             return []
+        for s in sched.seqs:         # prefix-cache hits resume from a GDN state snapshot
+            if s.req.restore_snapshot is not None:
+                self.model.copy_state(self.caches, s.req.restore_snapshot, s.req.state_slot)
+                s.req.restore_snapshot = None
         if self.spec is not None:
             result = self.spec.execute(sched)
         else:
             result = self.runner.execute(sched)
         finished = self.scheduler.update(sched, result.sampled)
+        if self.kv.num_snapshots:
+            for s in sched.seqs:
+                if not s.is_decode and s.req.state_slot is not None:
+                    sid = self.kv.take_snapshot(s.req)
+                    if sid is not None:
+                        self.model.copy_state(self.caches, s.req.state_slot, sid)
         self.metrics.on_step(sched, result, time.perf_counter() - t0, self.kv.usage,
                              len(self.scheduler.running), len(self.scheduler.waiting))
         outs = []

@@ -72,6 +72,7 @@ class Request:
         self.num_computed_tokens = 0
         self.block_ids: list[int] = []
         self.state_slot: Optional[int] = None
+        self.restore_snapshot: Optional[int] = None   # GDN snapshot slot to restore (prefix hit)
         self.arrival_time = arrival_time if arrival_time is not None else time.monotonic()
         self.first_token_time: Optional[float] = None
         self.finish_time: Optional[float] = None

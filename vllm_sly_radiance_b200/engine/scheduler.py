@@ -115,7 +115,7 @@ class Scheduler:
                     k = max(0, budget - 1)
                     n = 1 + k
             else:
-                n = min(remaining, budget)
+                n = self._chunk(req, min(remaining, budget))
                 k = 0
             # make room (preempting from the back if needed)
             while not self.kv.allocate(req, req.num_computed_tokens + n):
@@ -144,7 +144,7 @@ class Scheduler:
                     self.kv.adopt_prefix(req, cached)
                     req.num_computed_tokens = cached
             remaining = req.num_tokens - req.num_computed_tokens
-            n = min(remaining, budget)
+            n = self._chunk(req, min(remaining, budget))
             if not self.kv.allocate(req, req.num_computed_tokens + n):
                 break
             self.waiting.popleft()
@@ -158,6 +158,15 @@ class Scheduler:
         fin = self.finished_ids
         self.finished_ids = []
         return SchedulerOutput(seqs, self.max_tokens - budget, preempted, fin)
+
+    def _chunk(self, req: Request, n: int) -> int:
+        """With GDN state snapshots on, a prefill chunk that would cross the request's snapshot
+        boundary ends exactly there, so the state at that boundary can be copied out."""
+        B = self.kv.snapshot_boundary(req)
+        c = req.num_computed_tokens
+        if B > 0 and c < B < c + n:
+            return B - c
+        return n
 
     def update(self, out: SchedulerOutput, sampled: dict, accepted: Optional[dict] = None) -> list:
         """Advance request state after a step.  `sampled[req_id]` = list of new token ids

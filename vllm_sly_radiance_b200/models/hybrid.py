@@ -356,6 +356,14 @@ class HybridModel:
                 ssms.append(torch.zeros(num_slots, m.Hv, m.dv, m.dk, dtype=sdt, device=self.device))
         return ModelCaches(ks, vs, convs, ssms, block_size)
 
+    @staticmethod
+    def copy_state(caches: ModelCaches, src: int, dst: int):
+        """Copy every GDN layer's conv + SSM state from slot `src` to slot `dst`."""
+        for c in caches.conv:
+            c[dst].copy_(c[src])
+        for t in caches.ssm:
+            t[dst].copy_(t[src])
+
     def cache_bytes_per_block(self, block_size: int, kv_dtype: str = "fp8") -> int:
         n = 0
         for layer in self.layers:
