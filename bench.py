@@ -284,9 +284,11 @@ def profiled_launches(eng, dump_path=None):
                 a[0] += 1
                 a[1] += e.device_time
             rows = sorted(([k, v[0], round(v[1], 2)] for k, v in agg.items()), key=lambda r: -r[2])
+            seq = [[e.name[:60], round(e.device_time, 2)]
+                   for e in sorted(evs, key=lambda e: e.time_range.start)][:120]
             with open(dump_path, "w") as f:
                 json.dump({"step_kernel_us": round(sum(r[2] for r in rows), 1),
-                           "kernels": rows}, f, indent=0)
+                           "kernels": rows, "sequence": seq}, f, indent=0)
         if n > 0:
             return n, "torch.profiler kernel records in namespace rad:: over one decode step"
     except Exception:

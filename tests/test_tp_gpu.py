@@ -72,6 +72,26 @@ def _run(rank, world, port, outq):
         out[f"arq{M}"] = float(((q.float() * s[:, None]) - (q2.float() * s2[:, None])).abs().max())
     K.check_status(torch.device("cuda", rank))
     _log(rank, "all-reduce checks done")
+    # 1b) GEMM-fused all-reduce: the row-parallel GEMM pushes its tiles to every rank
+    from vllm_sly_radiance_b200.quant.mxfp4 import MXFP4Weight
+    g = torch.Generator().manual_seed(100 + rank)
+    for N, Kd in ((256, 512), (5120, 4096)):
+        w = MXFP4Weight.from_float(torch.randn(N, Kd, generator=g) * 0.02).to("cuda")
+        for M in (1, 5, 16):
+            x = torch.randn(M, Kd, generator=g).to(torch.bfloat16).cuda()
+            qa, sa = K.quant_fp8(x)
+            local = K.mxfp4_gemm(qa, sa, w.packed, w.sf, w.scales, N)
+            ref = local.float().clone()
+            dist.all_reduce(ref)
+            got = tp.fused.all_reduce(tp.fused.gemm_push(qa, sa, w))
+            out[f"push{N}_{M}"] = float((got.float() - ref).abs().max() / ref.abs().max())
+            res = torch.randn(M, N, generator=g).to(torch.bfloat16).cuda()
+            wn = (0.1 * torch.randn(N, generator=g)).to(torch.bfloat16).cuda()
+            q1, s1, r1 = tp.fused.all_reduce_add_rms_quant(tp.fused.gemm_push(qa, sa, w), res, wn, 1e-6)
+            q2, s2, r2 = K.add_rms_quant(ref.to(torch.bfloat16), res, wn, 1e-6)
+            out[f"pushq{N}_{M}"] = float(((q1.float() * s1[:, None]) - (q2.float() * s2[:, None])).abs().max())
+    K.check_status(torch.device("cuda", rank))
+    _log(rank, "gemm push checks done")
     # 2) TP=2 tiny model (fused path) vs single-GPU logits
     cfg = EngineConfig(model="tiny_hybrid", device="cuda", max_model_len=512, max_num_seqs=2,
                        max_num_batched_tokens=128, num_kv_blocks=32, enable_cuda_graphs=True)
@@ -125,6 +145,10 @@ def test_tp2_fused_allreduce_and_model():
     for M in (1, 8, 64):
         assert res[f"ar{M}"] < 0.05, res
         assert res[f"arq{M}"] < 0.25, res
+    for N in (256, 5120):
+        for M in (1, 5, 16):
+            assert res[f"push{N}_{M}"] < 1e-2, res
+            assert res[f"pushq{N}_{M}"] < 0.25, res
     cfg = EngineConfig(model="tiny_hybrid", device="cuda", max_model_len=512, max_num_seqs=2,
                        max_num_batched_tokens=128, num_kv_blocks=32)
     m = HybridModel(tiny_hybrid(), quant="mxfp4", device="cuda", seed=0, init_device="cpu")

@@ -38,6 +38,14 @@ void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
                      int64_t window, int64_t num_splits, torch::Tensor part_o,
                      torch::Tensor part_ml, torch::Tensor out, torch::Tensor counters,
                      bool decode);
+int64_t mxfp4_gemm_push(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
+                        std::vector<int64_t> peers, int64_t rank, int64_t half_words,
+                        torch::Tensor status);
+int64_t push_buffer_bytes(int64_t world, int64_t mmax, int64_t H);
+void push_allreduce_recv(std::vector<int64_t> peers, int64_t rank, int64_t M, int64_t H,
+                         int64_t half_words, torch::Tensor out, torch::Tensor residual,
+                         torch::Tensor weight, double eps, torch::Tensor res_out, torch::Tensor q,
+                         torch::Tensor scale, int64_t num_blocks, torch::Tensor status);
 void argmax_rows(torch::Tensor x, torch::Tensor out_ids, torch::Tensor out_vals,
                  torch::Tensor workspace);
 void sample_from_topk(torch::Tensor vals, torch::Tensor ids, torch::Tensor temperature,
@@ -68,6 +76,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_recurrent", &rad::gdn_recurrent, "GDN varlen recurrent delta rule");
   m.def("qkv_prologue", &rad::qkv_prologue, "QK RMSNorm + RoPE + paged KV write");
   m.def("paged_attention", &rad::paged_attention, "varlen paged attention (split-KV)");
+  m.def("mxfp4_gemm_push", &rad::mxfp4_gemm_push,
+        "row-parallel W4A8 GEMM that pushes its tiles into every peer's receive buffer");
+  m.def("push_buffer_bytes", &rad::push_buffer_bytes, "size of a GEMM-push receive buffer");
+  m.def("push_allreduce_recv", &rad::push_allreduce_recv,
+        "receiving half of the GEMM-fused all-reduce (+ add / RMSNorm / e4m3 quant)");
   m.def("ipc_handle", &rad::ipc_handle, "CUDA IPC handle of a device buffer");
   m.def("ipc_open", &rad::ipc_open, "open a peer's IPC handle -> device pointer");
   m.def("ipc_close", &rad::ipc_close, "close an opened IPC mapping");

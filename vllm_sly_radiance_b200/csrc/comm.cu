@@ -6,16 +6,21 @@
 // with the next layer's residual add + Gemma RMSNorm + e4m3 quant ("fp8 residual-stream contract").
 //
 // B200 design:
-//  * Each rank owns one symmetric buffer (cudaMalloc'd, IPC-mapped into every peer).  Layout:
-//    [flags: kMaxBlocks x kMaxRanks u32][counters: kMaxBlocks u32][data: 2 parity slots].
-//  * One-shot all-reduce, per CTA: copy own row chunk into the parity slot, release-store the
-//    sequence number into every peer's flag[cta][me], acquire-poll own flag[cta][p] for all p
-//    (bounded: after the timeout the CTA records kErrPeerTimeout in the status word and returns),
-//    then read the chunk from all peers' slots and reduce in fp32.  Sequence numbers live in
-//    device memory (per-CTA counter), so the kernel replays inside CUDA graphs.  Parity double
-//    buffering keeps a fast rank from overwriting a slot a slow peer still reads.
-//  * Fused epilogue variant: rows are owned whole by one CTA, so the reduced row goes straight
+//  * Each rank owns one symmetric buffer (cudaMalloc'd, IPC-mapped into every peer).  Data moves
+//    by PUSH: a rank stores its rows into its own source slot of every peer's buffer, and each
+//    rank reduces only its local slots, so nothing is ever read across NVLink.
+//  * Flag-in-word ("LL") stores: every 8-byte word carries 4 bytes of payload (two bf16) and the
+//    32-bit sequence number of the call that wrote it.  The reader polls each word until its
+//    sequence matches, so no system-scope fence, flag or counter sits between data and reader:
+//    an 8-byte store is seen whole.  Sequence numbers live in device memory (per-CTA counter for
+//    the one-shot, per-buffer epoch for the GEMM push), so the kernels replay inside CUDA graphs.
+//    Two parity halves keep a fast rank from overwriting words a slow peer has not read yet.
+//    Every poll is bounded: on timeout the CTA records kErrPeerTimeout and returns.
+//  * One-shot all-reduce: CTA c pushes rows [c*rows, ...) to every peer, then reduces the same
+//    rows from the `world` local source slots in fp32.  Fused variant: each reduced row goes
 //    through residual add + RMSNorm(1+w) + per-row e4m3 quant (the producer of the next linear).
+//  * GEMM push: the row-parallel GEMM's epilogue writes its tile as LL words straight into every
+//    peer (mxfp4_gemm.cu); push_recv_kernel is the reducing half.
 //  * Plain loads and stores to peer memory only; no bulk-copy engine touches a peer address.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -29,84 +34,76 @@ namespace rad {
 namespace comm {
 
 constexpr int kMaxRanks = 8;
-constexpr uint64_t kPeerWaitNs = 5ull * 1000ull * 1000ull * 1000ull;   // 5 s per handshake
+constexpr uint64_t kPeerWaitNs = 5ull * 1000ull * 1000ull * 1000ull;   // 5 s per wait
 constexpr int kMaxBlocks = 64;
-constexpr int kHeaderBytes = kMaxBlocks * kMaxRanks * 4 + kMaxBlocks * 4;
-constexpr int kDataOffset = (kHeaderBytes + 255) / 256 * 256;
+constexpr int kDataOffset = 256;                 // after the per-CTA sequence counters
 
 struct PeerPtrs {
   uint8_t* p[kMaxRanks];
 };
 
-DEVI uint32_t* flags_of(uint8_t* base) { return reinterpret_cast<uint32_t*>(base); }
-DEVI uint32_t* counters_of(uint8_t* base) {
-  return reinterpret_cast<uint32_t*>(base + kMaxBlocks * kMaxRanks * 4);
+DEVI uint32_t* counters_of(uint8_t* base) { return reinterpret_cast<uint32_t*>(base); }
+
+// poll 4 LL words (8 bf16, 32 bytes, 16-byte aligned) until all carry `seq`
+DEVI bool ld_ll8(const uint64_t* p, uint32_t seq, float (&f)[8], int* status) {
+  uint32_t a0, f0, a1, f1, a2, f2, a3, f3;
+  uint64_t t0 = 0;
+  for (int it = 0;; ++it) {
+    asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(a0), "=r"(f0), "=r"(a1), "=r"(f1) : "l"(p) : "memory");
+    asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(a2), "=r"(f2), "=r"(a3), "=r"(f3) : "l"(p + 2) : "memory");
+    if (f0 == seq && f1 == seq && f2 == seq && f3 == seq) break;
+    if ((it & 63) == 0) {
+      const uint64_t now = globaltimer_ns();
+      if (it == 0) t0 = now;
+      else if (now - t0 > kPeerWaitNs) {
+        if (status) atomicExch(status, kErrPeerTimeout);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] = 0.f;
+        return false;
+      }
+    }
+  }
+  const uint32_t w[4] = {a0, a1, a2, a3};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&w[i]);
+    const float2 v = __bfloat1622float2(h);
+    f[2 * i] = v.x;
+    f[2 * i + 1] = v.y;
+  }
+  return true;
 }
 
-// rows [M, H] bf16; each CTA owns a contiguous set of rows.  Output either bf16 sum or the fused
-// add + RMSNorm + quant triple.
+// store 8 bf16 (one uint4) as 4 LL words
+DEVI void st_ll8(uint64_t* p, uint4 u, uint32_t seq) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(u.x), "r"(seq),
+               "r"(u.y), "r"(seq) : "memory");
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p + 2), "r"(u.z), "r"(seq),
+               "r"(u.w), "r"(seq) : "memory");
+}
+
+// Sum rows [r0, r1) over `world` LL sources (row r of source p at srcs[p] + r * H / 2 words) in
+// fp32; plain: write the bf16 sum to out; fused: s = bf16(sum) + residual -> res_out, Gemma
+// RMSNorm (1 + w), per-row e4m3 quant.  False if a wait timed out.
 template <bool FUSED>
-__global__ void __launch_bounds__(256) oneshot_kernel(
-    PeerPtrs peers, int world, int rank, const __nv_bfloat16* __restrict__ inp, int M, int H,
-    int64_t slot_bytes, __nv_bfloat16* __restrict__ out,
-    const __nv_bfloat16* __restrict__ residual, const __nv_bfloat16* __restrict__ w, float eps,
-    __nv_bfloat16* __restrict__ res_out, uint8_t* __restrict__ q, float* __restrict__ scale,
-    int* __restrict__ status) {
-  pdl_wait();     // inputs come from the preceding kernel
-  pdl_trigger();
-  __shared__ uint32_t s_seq;
-  __shared__ float red[8];
-  __shared__ int s_ok;
-  const int cta = blockIdx.x;
-  const int rows_per = (M + gridDim.x - 1) / gridDim.x;
-  const int r0 = cta * rows_per;
-  const int r1 = min(M, r0 + rows_per);
-  uint8_t* mine = peers.p[rank];
-  if (threadIdx.x == 0) {
-    uint32_t* ctr = counters_of(mine) + cta;
-    s_seq = *ctr + 1;
-    *ctr = s_seq;
-    s_ok = 1;
-  }
-  __syncthreads();
-  const uint32_t seq = s_seq;
-  const int par = seq & 1;
-  // 1) own rows -> own parity slot
-  __nv_bfloat16* my_slot = reinterpret_cast<__nv_bfloat16*>(mine + kDataOffset + par * slot_bytes);
+DEVI bool reduce_rows(const uint64_t* const* srcs, int world, uint32_t seq, int r0, int r1, int H,
+                      __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ residual,
+                      const __nv_bfloat16* __restrict__ w, float eps,
+                      __nv_bfloat16* __restrict__ res_out, uint8_t* __restrict__ q,
+                      float* __restrict__ scale, float* red, int* status) {
   const int nv = H / 8;
-  for (int r = r0; r < r1; ++r)
-    for (int v = threadIdx.x; v < nv; v += blockDim.x)
-      reinterpret_cast<uint4*>(my_slot + (size_t)r * H)[v] = reinterpret_cast<const uint4*>(inp + (size_t)r * H)[v];
-  __threadfence_system();
-  __syncthreads();
-  // 2) signal every peer, 3) wait for every peer
-  if (threadIdx.x < world) {
-    const int p = threadIdx.x;
-    st_release_sys(flags_of(peers.p[p]) + cta * kMaxRanks + rank, seq);
-  }
-  if (threadIdx.x < world) {
-    const int p = threadIdx.x;
-    if (!wait_flag_geq(flags_of(mine) + cta * kMaxRanks + p, seq, status, kErrPeerTimeout,
-                        kPeerWaitNs))
-      atomicExch(&s_ok, 0);
-  }
-  __syncthreads();
-  if (!s_ok) return;
-  // 4) reduce
+  bool ok = true;
   for (int r = r0; r < r1; ++r) {
     if constexpr (!FUSED) {
       for (int v = threadIdx.x; v < nv; v += blockDim.x) {
         float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
         for (int p = 0; p < world; ++p) {
-          const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(peers.p[p] + kDataOffset + par * slot_bytes);
-          uint4 u = reinterpret_cast<const uint4*>(src + (size_t)r * H)[v];
-          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+          float f[8];
+          ok &= ld_ll8(srcs[p] + (size_t)r * (H / 2) + v * 4, seq, f, status);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            float2 f = __bfloat1622float2(h[i]);
-            acc[2 * i] += f.x;
-            acc[2 * i + 1] += f.y;
-          }
+          for (int i = 0; i < 8; ++i) acc[i] += f[i];
         }
         uint4 o;
         __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
@@ -115,7 +112,6 @@ __global__ void __launch_bounds__(256) oneshot_kernel(
         reinterpret_cast<uint4*>(out + (size_t)r * H)[v] = o;
       }
     } else {
-      // fused: s = bf16(sum) + residual (fp32), res_out = bf16(s), n = bf16(s*rs*(1+w)), quant
       constexpr int MAXV = 5;   // H <= 5 * 256 * 8 = 10240
       float vals[MAXV][8];
       float ss = 0.f;
@@ -126,15 +122,10 @@ __global__ void __launch_bounds__(256) oneshot_kernel(
 #pragma unroll
           for (int j = 0; j < 8; ++j) vals[i][j] = 0.f;
           for (int p = 0; p < world; ++p) {
-            const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(peers.p[p] + kDataOffset + par * slot_bytes);
-            uint4 u = reinterpret_cast<const uint4*>(src + (size_t)r * H)[v];
-            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+            float f[8];
+            ok &= ld_ll8(srcs[p] + (size_t)r * (H / 2) + v * 4, seq, f, status);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              float2 f = __bfloat1622float2(h[k]);
-              vals[i][2 * k] += f.x;
-              vals[i][2 * k + 1] += f.y;
-            }
+            for (int j = 0; j < 8; ++j) vals[i][j] += f[j];
           }
           uint4 ru = reinterpret_cast<const uint4*>(residual + (size_t)r * H)[v];
           const __nv_bfloat162* rh = reinterpret_cast<const __nv_bfloat162*>(&ru);
@@ -200,6 +191,85 @@ __global__ void __launch_bounds__(256) oneshot_kernel(
       if (threadIdx.x == 0) scale[r] = sc;
     }
   }
+  return ok;
+}
+
+// One-shot push all-reduce.  Buffer of each rank: [per-CTA sequence counters][data @ 256: two
+// parity halves of `half_bytes`, each world source slots x M rows x H / 2 LL words].
+template <bool FUSED>
+__global__ void __launch_bounds__(256) oneshot_kernel(
+    PeerPtrs peers, int world, int rank, const __nv_bfloat16* __restrict__ inp, int M, int H,
+    int64_t half_bytes, __nv_bfloat16* __restrict__ out,
+    const __nv_bfloat16* __restrict__ residual, const __nv_bfloat16* __restrict__ w, float eps,
+    __nv_bfloat16* __restrict__ res_out, uint8_t* __restrict__ q, float* __restrict__ scale,
+    int* __restrict__ status) {
+  pdl_wait();     // inputs come from the preceding kernel
+  pdl_trigger();
+  __shared__ uint32_t s_seq;
+  __shared__ float red[8];
+  const int cta = blockIdx.x;
+  const int rows_per = (M + gridDim.x - 1) / gridDim.x;
+  const int r0 = cta * rows_per;
+  const int r1 = min(M, r0 + rows_per);
+  uint8_t* mine = peers.p[rank];
+  if (threadIdx.x == 0) {
+    uint32_t* ctr = counters_of(mine) + cta;
+    s_seq = *ctr + 1;
+    *ctr = s_seq;
+  }
+  __syncthreads();
+  const uint32_t seq = s_seq;
+  const int64_t half = (int64_t)(seq & 1) * half_bytes;
+  const size_t row_words = (size_t)H / 2;
+  // 1) push own rows into this rank's source slot of every peer
+  const int nv = H / 8;
+  for (int r = r0; r < r1; ++r)
+    for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+      const uint4 u = reinterpret_cast<const uint4*>(inp + (size_t)r * H)[v];
+      for (int p = 0; p < world; ++p) {
+        uint64_t* dst = reinterpret_cast<uint64_t*>(peers.p[p] + kDataOffset + half) +
+                        ((size_t)rank * M + r) * row_words + v * 4;
+        st_ll8(dst, u, seq);
+      }
+    }
+  // 2) reduce the local source slots
+  const uint64_t* srcs[kMaxRanks];
+  for (int p = 0; p < world; ++p)
+    srcs[p] = reinterpret_cast<const uint64_t*>(mine + kDataOffset + half) + (size_t)p * M * row_words;
+  reduce_rows<FUSED>(srcs, world, seq, r0, r1, H, out, residual, w, eps, res_out, q, scale, red,
+                     status);
+}
+
+// Reducing half of the GEMM-fused all-reduce: every rank's row-parallel GEMM has pushed its tile
+// rows as LL words into this rank's buffer (PushArgs layout).  The last CTA to finish advances
+// the epoch, which is the sequence source of the next GEMM push on this rank.
+template <bool FUSED>
+__global__ void __launch_bounds__(256) push_recv_kernel(
+    const PushArgs pa, int M, int H, __nv_bfloat16* __restrict__ out,
+    const __nv_bfloat16* __restrict__ residual, const __nv_bfloat16* __restrict__ w, float eps,
+    __nv_bfloat16* __restrict__ res_out, uint8_t* __restrict__ q, float* __restrict__ scale,
+    int* __restrict__ status) {
+  pdl_wait();     // the pushing GEMM precedes this kernel on every rank
+  pdl_trigger();
+  __shared__ float red[8];
+  __shared__ bool s_last;
+  const uint32_t seq = push_seq(pa);
+  const int rows_per = (M + gridDim.x - 1) / gridDim.x;
+  const int r0 = blockIdx.x * rows_per;
+  const int r1 = min(M, r0 + rows_per);
+  const uint64_t* srcs[kMaxRanks];
+  for (int p = 0; p < pa.world; ++p) srcs[p] = push_slot(pa, pa.rank, seq & 1u, p, M);
+  reduce_rows<FUSED>(srcs, pa.world, seq, r0, r1, H, out, residual, w, eps, res_out, q, scale,
+                     red, status);
+  __syncthreads();
+  uint8_t* mine = pa.peer[pa.rank];
+  if (threadIdx.x == 0)
+    s_last = atomicAdd(reinterpret_cast<uint32_t*>(mine + kPushDoneOff), 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (s_last && threadIdx.x == 0) {
+    *reinterpret_cast<uint32_t*>(mine + kPushDoneOff) = 0u;
+    *reinterpret_cast<volatile uint32_t*>(mine + kPushEpochOff) = seq;
+  }
 }
 
 }  // namespace comm
@@ -225,9 +295,10 @@ void ipc_close(int64_t ptr) { C10_CUDA_CHECK(cudaIpcCloseMemHandle((void*)(uintp
 
 int64_t symm_header_bytes() { return comm::kDataOffset; }
 
-// peers: int64 device pointers of every rank's symmetric buffer (own included at `rank`)
+// peers: int64 device pointers of every rank's symmetric buffer (own included at `rank`);
+// half_bytes: capacity of one parity half of the data region
 void allreduce_oneshot(std::vector<int64_t> peers, int64_t rank, torch::Tensor inp,
-                       int64_t slot_bytes, torch::Tensor out, torch::Tensor residual,
+                       int64_t half_bytes, torch::Tensor out, torch::Tensor residual,
                        torch::Tensor weight, double eps, torch::Tensor res_out, torch::Tensor q,
                        torch::Tensor scale, int64_t num_blocks, torch::Tensor status) {
   using namespace comm;
@@ -235,7 +306,7 @@ void allreduce_oneshot(std::vector<int64_t> peers, int64_t rank, torch::Tensor i
   TORCH_CHECK(world >= 1 && world <= kMaxRanks, "world size");
   const int M = inp.size(0), H = inp.size(1);
   TORCH_CHECK(H % 8 == 0 && H <= 10240, "allreduce: H % 8 and H <= 10240");
-  TORCH_CHECK((int64_t)M * H * 2 <= slot_bytes, "allreduce: message exceeds the symmetric slot");
+  TORCH_CHECK((int64_t)world * M * H * 4 <= half_bytes, "allreduce: message exceeds the symmetric buffer");
   if (M == 0) return;
   PeerPtrs pp;
   for (int i = 0; i < kMaxRanks; ++i) pp.p[i] = i < world ? (uint8_t*)(uintptr_t)peers[i] : nullptr;
@@ -247,14 +318,54 @@ void allreduce_oneshot(std::vector<int64_t> peers, int64_t rank, torch::Tensor i
   const bool fused = q.defined() && q.numel();
   if (fused)
 C10_CUDA_CHECK(launch_pdl((oneshot_kernel<true>), dim3(nb), dim3(256), 0, stream, 
-        pp, world, rank, (const __nv_bfloat16*)inp.data_ptr(), M, H, slot_bytes, nullptr,
+        pp, world, rank, (const __nv_bfloat16*)inp.data_ptr(), M, H, half_bytes, nullptr,
         (const __nv_bfloat16*)residual.data_ptr(), (const __nv_bfloat16*)weight.data_ptr(),
         (float)eps, (__nv_bfloat16*)res_out.data_ptr(), (uint8_t*)q.data_ptr(),
         scale.data_ptr<float>(), st));
   else
 C10_CUDA_CHECK(launch_pdl((oneshot_kernel<false>), dim3(nb), dim3(256), 0, stream, 
-        pp, world, rank, (const __nv_bfloat16*)inp.data_ptr(), M, H, slot_bytes,
+        pp, world, rank, (const __nv_bfloat16*)inp.data_ptr(), M, H, half_bytes,
         (__nv_bfloat16*)out.data_ptr(), nullptr, nullptr, 0.f, nullptr, nullptr, nullptr, st));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+int64_t push_buffer_bytes(int64_t world, int64_t mmax, int64_t H) {
+  // header + two parity halves of world x mmax x H/2 LL words (8 bytes)
+  return kPushDataOff + 2 * world * mmax * (H / 2) * 8;
+}
+
+// peers: every rank's push receive buffer (own at `rank`); half_words = words per parity half
+void push_allreduce_recv(std::vector<int64_t> peers, int64_t rank, int64_t M, int64_t H,
+                         int64_t half_words, torch::Tensor out, torch::Tensor residual,
+                         torch::Tensor weight, double eps, torch::Tensor res_out, torch::Tensor q,
+                         torch::Tensor scale, int64_t num_blocks, torch::Tensor status) {
+  using namespace comm;
+  const int world = peers.size();
+  TORCH_CHECK(world >= 1 && world <= kMaxRanks, "world size");
+  TORCH_CHECK(H % 8 == 0 && H <= 10240, "push recv: H % 8 and H <= 10240");
+  TORCH_CHECK((int64_t)world * M * (H / 2) <= half_words, "push recv: message exceeds the buffer");
+  if (M == 0) return;
+  PushArgs pa{};
+  for (int i = 0; i < world; ++i) pa.peer[i] = (uint8_t*)(uintptr_t)peers[i];
+  pa.world = world;
+  pa.rank = (int)rank;
+  pa.half_words = half_words;
+  pa.ld = (int)H;
+  int nb = (int)std::min<int64_t>(num_blocks > 0 ? num_blocks : M, kMaxBlocks);
+  nb = std::max(1, std::min<int>(nb, (int)M));
+  const at::cuda::CUDAGuard guard(out.defined() && out.numel() ? out.device() : res_out.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  int* st = status.numel() ? status.data_ptr<int>() : nullptr;
+  const bool fused = q.defined() && q.numel();
+  if (fused)
+    C10_CUDA_CHECK(launch_pdl((push_recv_kernel<true>), dim3(nb), dim3(256), 0, stream, pa, (int)M,
+        (int)H, nullptr, (const __nv_bfloat16*)residual.data_ptr(),
+        (const __nv_bfloat16*)weight.data_ptr(), (float)eps, (__nv_bfloat16*)res_out.data_ptr(),
+        (uint8_t*)q.data_ptr(), scale.data_ptr<float>(), st));
+  else
+    C10_CUDA_CHECK(launch_pdl((push_recv_kernel<false>), dim3(nb), dim3(256), 0, stream, pa, (int)M,
+        (int)H, (__nv_bfloat16*)out.data_ptr(), nullptr, nullptr, 0.f, nullptr, nullptr, nullptr,
+        st));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -278,6 +278,40 @@ DEVI uint32_t ld_acquire_sys(const uint32_t* p) {
 DEVI void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// ---------------------------------------------------------------------------------------------
+// GEMM -> all-reduce push (tensor parallel, NVLink peer memory).  Every rank owns one receive
+// buffer, mapped into every peer:
+//   [.. epoch u32 @ 64, done u32 @ 68 ..][data @ 256: two parity halves of half_words words]
+//   half: world source slots x M rows x ld/2 flag-in-word ("LL") words: low 32 bits = two bf16,
+//   high 32 bits = the sequence number of the call (epoch + 1) that wrote them
+// A row-parallel GEMM stores each finished output tile as LL words into its own source slot of
+// every peer's buffer; the receiving kernel polls its local words until they carry the current
+// sequence, reduces them, and its last CTA advances the epoch.
+// ---------------------------------------------------------------------------------------------
+struct PushArgs {
+  uint8_t* peer[8];
+  int world;        // 0: no push (plain output)
+  int rank;
+  int64_t half_words;
+  int ld;           // row length (output features)
+};
+constexpr int kPushEpochOff = 64;
+constexpr int kPushDoneOff = 68;
+constexpr int kPushDataOff = 256;
+DEVI uint32_t push_seq(const PushArgs& pa) {
+  return *reinterpret_cast<volatile const uint32_t*>(pa.peer[pa.rank] + kPushEpochOff) + 1u;
+}
+// source slot `src` (M rows x ld/2 words) of parity `par` in rank p's buffer
+DEVI uint64_t* push_slot(const PushArgs& pa, int p, uint32_t par, int src, int M) {
+  return reinterpret_cast<uint64_t*>(pa.peer[p] + kPushDataOff) + (int64_t)par * pa.half_words +
+         (size_t)src * M * (pa.ld / 2);
+}
+DEVI void st_ll_pair(uint64_t* p, float lo, float hi, uint32_t seq) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  const uint32_t d = *reinterpret_cast<uint32_t*>(&h);
+  asm volatile("st.volatile.global.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(d), "r"(seq) : "memory");
+}
+
 // spin until *p >= target (wrap-safe); false + error after `timeout_ns` of wall clock
 DEVI bool wait_flag_geq(const uint32_t* p, uint32_t target, int* err, int code,
                         uint64_t timeout_ns = kWaitNs) {

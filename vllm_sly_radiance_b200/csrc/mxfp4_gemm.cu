@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
                       const __grid_constant__ CUtensorMap tmap_a, const uint8_t* __restrict__ sfw,
                       const float* __restrict__ a_scale, __nv_bfloat16* __restrict__ out,
                       int ldo, int M, int N, int K, int k_tiles_per_split, int* __restrict__ status,
-                      const int* __restrict__ items = nullptr, int n_per_group = 0) {
+                      const int* __restrict__ items, int n_per_group, const PushArgs push) {
   using C = Cfg<BN>;
   // Grouped (MoE) mode: blockIdx.y indexes a work table of (expert, first row, rows); the
   // expert's weights are rows [e * n_per_group, (e + 1) * n_per_group) of the stacked tensor.
@@ -231,19 +231,27 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
     tc_fence_after();
     const bool have_acc = nk > 0 && !*abort_flag;
     if (num_splits == 1) {
+      const uint32_t seq = push.world ? push_seq(push) : 0u;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
         uint32_t r[16];
         tmem_ld_32x32b_x16(tmem_acc + ((uint32_t)(q * 32) << 16) + c0, r);
         tmem_ld_wait();
-        if (n < n_lim) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int m = m0 + c0 + j;
-            if (m < m_end) {
-              const float v = have_acc ? __uint_as_float(r[j]) * a_scale[m] : 0.f;
-              out[(size_t)m * ldo + n] = __float2bfloat16_rn(v);
-            }
+        for (int j = 0; j < 16; ++j) {
+          const int m = m0 + c0 + j;
+          if (m >= m_end) break;                       // uniform across the warp
+          const float v = (have_acc && n < n_lim) ? __uint_as_float(r[j]) * a_scale[m] : 0.f;
+          if (push.world) {
+            // adjacent lanes own adjacent columns: even lanes store the pair as one LL word
+            // straight into this rank's slot of every peer's receive buffer
+            const float vn = __shfl_down_sync(0xffffffffu, v, 1);
+            if ((lane & 1) == 0 && n < n_lim)
+              for (int p = 0; p < push.world; ++p)
+                st_ll_pair(push_slot(push, p, seq & 1u, push.rank, M) + (size_t)m * (push.ld / 2) + n / 2,
+                           v, vn, seq);
+          } else if (n < n_lim) {
+            out[(size_t)m * ldo + n] = __float2bfloat16_rn(v);
           }
         }
       }
@@ -271,17 +279,29 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
       const int n = n_out0 + row;
       const uint32_t my_rank = cluster_ctarank();
       const uint32_t part_addr = smem_u32(stage_base);
+      const uint32_t seq = push.world ? push_seq(push) : 0u;
       for (int j = my_rank; j < BN; j += num_splits) {
         const int m = m0 + j;
-        if (m >= m_end || n >= n_lim) continue;
+        if (m >= m_end) break;                         // uniform across the warp
         float acc = 0.f;
-        for (int r = 0; r < num_splits; ++r) {
-          const uint32_t a = mapa_shared(part_addr + (uint32_t)((j * BM + row) * 4), (uint32_t)r);
-          float v;
-          asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a));
-          acc += v;
+        if (n < n_lim) {
+          for (int r = 0; r < num_splits; ++r) {
+            const uint32_t a = mapa_shared(part_addr + (uint32_t)((j * BM + row) * 4), (uint32_t)r);
+            float v;
+            asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a));
+            acc += v;
+          }
+          acc *= a_scale[m];
         }
-        out[(size_t)m * ldo + n] = __float2bfloat16_rn(acc * a_scale[m]);
+        if (push.world) {
+          const float vn = __shfl_down_sync(0xffffffffu, acc, 1);
+          if ((lane & 1) == 0 && n < n_lim)
+            for (int p = 0; p < push.world; ++p)
+              st_ll_pair(push_slot(push, p, seq & 1u, push.rank, M) + (size_t)m * (push.ld / 2) + n / 2,
+                         acc, vn, seq);
+        } else if (n < n_lim) {
+          out[(size_t)m * ldo + n] = __float2bfloat16_rn(acc);
+        }
       }
     }
     __syncwarp();
@@ -332,7 +352,7 @@ static CUtensorMap weight_map(const torch::Tensor& packed, int64_t N, int64_t K)
 template <int BN>
 static void launch(const torch::Tensor& a, const torch::Tensor& a_scale, const torch::Tensor& wp,
                    const torch::Tensor& sf, torch::Tensor& out, int M, int N, int K, int splits,
-                   int* status, cudaStream_t stream) {
+                   int* status, cudaStream_t stream, const PushArgs& push) {
   using C = Cfg<BN>;
   const int Kw = (int)wp.size(1) * 2;          // whole K tiles of stored weight
   CUtensorMap tw = weight_map(wp, N, Kw);
@@ -364,8 +384,9 @@ static void launch(const torch::Tensor& a, const torch::Tensor& a_scale, const t
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tw, ta, (const uint8_t*)sf.data_ptr(),
                                     (const float*)a_scale.data_ptr(),
-                                    (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), M, N, Kw,
-                                    per, status, (const int*)nullptr, 0));
+                                    push.world ? nullptr : (__nv_bfloat16*)out.data_ptr(),
+                                    push.world ? 0 : (int)out.stride(0), M, N, Kw,
+                                    per, status, (const int*)nullptr, 0, push));
 }
 
 static int pick_splits(int tiles, int k_tiles, int ctas_per_sm) {
@@ -398,7 +419,7 @@ static void launch_grouped(const torch::Tensor& a, const torch::Tensor& a_scale,
   C10_CUDA_CHECK(launch_pdl(kern, grid, dim3(kThreads), C::SMEM_BYTES, stream, tw, ta,
                             (const uint8_t*)sf.data_ptr(), (const float*)a_scale.data_ptr(),
                             (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), M, Ntot, K,
-                            K / BK, status, (const int*)items.data_ptr(), n_per_group));
+                            K / BK, status, (const int*)items.data_ptr(), n_per_group, PushArgs{}));
 }
 
 }  // namespace mxfp4
@@ -427,14 +448,20 @@ void mxfp4_grouped_gemm(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp
 }
 
 // a: fp8 e4m3 [M, K] (row stride multiple of 16 bytes), a_scale fp32 [M], wp uint8 [N, K/2],
-// sf: tiled scale factors, out: bf16 [M, N] (row stride ldo)
-void mxfp4_gemm(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
-                torch::Tensor out, int64_t splits_override, torch::Tensor status) {
+// sf: tiled scale factors, out: bf16 [M, N] (row stride ldo) -- or, with push.world > 0, no
+// output tensor: the tiles go to the peers' receive buffers.  Returns the number of output
+// tiles (= arrivals each peer receives from this rank).
+static int64_t mxfp4_gemm_impl(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp,
+                               torch::Tensor sf, torch::Tensor out, int64_t splits_override,
+                               torch::Tensor status, const PushArgs& push) {
   using namespace mxfp4;
-  TORCH_CHECK(a.is_cuda() && wp.is_cuda() && out.is_cuda(), "mxfp4_gemm: CUDA tensors required");
+  const bool has_out = !push.world;
+  TORCH_CHECK(a.is_cuda() && wp.is_cuda() && (!has_out || out.is_cuda()),
+              "mxfp4_gemm: CUDA tensors required");
   TORCH_CHECK(a.scalar_type() == at::kFloat8_e4m3fn, "activations must be float8_e4m3fn");
-  TORCH_CHECK(out.scalar_type() == at::kBFloat16, "output must be bf16");
-  TORCH_CHECK(a.dim() == 2 && a.stride(1) == 1 && out.stride(1) == 1 && wp.stride(1) == 1, "row-major");
+  TORCH_CHECK(!has_out || out.scalar_type() == at::kBFloat16, "output must be bf16");
+  TORCH_CHECK(a.dim() == 2 && a.stride(1) == 1 && (!has_out || out.stride(1) == 1) &&
+                  wp.stride(1) == 1, "row-major");
   // K: the activation's input features (a multiple of 32); the stored weight is zero-padded to
   // whole K tiles (Kw), and the activation's missing tail of the last tile is zero-filled by TMA
   // (out-of-range box elements read as zero)
@@ -446,8 +473,8 @@ void mxfp4_gemm(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch:
               "activation rows must be 16-byte aligned");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(wp.data_ptr()) % 32) == 0 && (wp.stride(0) % 32) == 0,
               "weight rows must be 32-byte aligned");
-  TORCH_CHECK(out.size(0) >= M && out.size(1) >= N, "output too small");
-  if (M == 0) return;
+  if (!push.world) TORCH_CHECK(out.size(0) >= M && out.size(1) >= N, "output too small");
+  if (M == 0) return 0;
   const at::cuda::CUDAGuard guard(a.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
   int* st = status.numel() ? status.data_ptr<int>() : nullptr;
@@ -461,12 +488,37 @@ void mxfp4_gemm(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch:
   int splits = splits_override > 0 ? (int)splits_override
                                    : pick_splits(tiles, Kw / BK, bn <= 64 ? 2 : 1);
   switch (bn) {
-    case 16: launch<16>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream); break;
-    case 32: launch<32>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream); break;
-    case 64: launch<64>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream); break;
-    case 128: launch<128>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream); break;
-    default: launch<256>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream); break;
+    case 16: launch<16>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream, push); break;
+    case 32: launch<32>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream, push); break;
+    case 64: launch<64>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream, push); break;
+    case 128: launch<128>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream, push); break;
+    default: launch<256>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream, push); break;
   }
+  return (int64_t)tiles;
+}
+
+void mxfp4_gemm(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
+                torch::Tensor out, int64_t splits_override, torch::Tensor status) {
+  mxfp4_gemm_impl(a, a_scale, wp, sf, out, splits_override, status, PushArgs{});
+}
+
+// Row-parallel GEMM fused with the push half of the all-reduce: peers = every rank's receive
+// buffer (own included at `rank`), half_words = words of one parity half; slot row = N outputs.
+int64_t mxfp4_gemm_push(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
+                        std::vector<int64_t> peers, int64_t rank, int64_t half_words,
+                        torch::Tensor status) {
+  const int world = peers.size();
+  TORCH_CHECK(world >= 1 && world <= 8, "push: world size 1..8");
+  TORCH_CHECK(wp.size(0) % 8 == 0, "push: output features must be a multiple of 8");
+  TORCH_CHECK((int64_t)world * a.size(0) * (wp.size(0) / 2) <= half_words,
+              "push: message exceeds the receive buffer");
+  PushArgs pa{};
+  for (int i = 0; i < world; ++i) pa.peer[i] = (uint8_t*)(uintptr_t)peers[i];
+  pa.world = world;
+  pa.rank = (int)rank;
+  pa.half_words = half_words;
+  pa.ld = (int)wp.size(0);
+  return mxfp4_gemm_impl(a, a_scale, wp, sf, torch::Tensor(), 0, status, pa);
 }
 
 }  // namespace rad

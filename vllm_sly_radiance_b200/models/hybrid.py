@@ -306,6 +306,20 @@ class HybridModel:
         if init_dev != self.device or getattr(W, "device", self.device) != self.device:
             self.to(self.device)
         self._init_rope()
+        self._attach_push()
+
+    def _attach_push(self):
+        """TP > 1 with the NVLink communicator: the row-parallel linears (GDN out_proj,
+        attention o_proj, dense MLP down) push their output tiles to every rank from the GEMM
+        epilogue; the model's all-reduce call then only runs the receiving half."""
+        comm = getattr(self.tp, "fused", None)
+        if comm is None or self.quant != "mxfp4" or not getattr(comm, "push_enabled", False):
+            return
+        for layer in self.layers:
+            lin = layer.mixer.out_proj if not layer.is_attn else layer.mixer.o_proj
+            lin.push = comm
+            if isinstance(layer.mlp, MLP):
+                layer.mlp.down.push = comm
 
     def _init_rope(self):
         cfg = self.cfg

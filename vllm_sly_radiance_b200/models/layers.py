@@ -64,12 +64,19 @@ class Linear:
             return self.w.nbytes
         return self.w.numel() * self.w.element_size()
 
+    # row-parallel linears of a TP>1 model get the NVLink communicator here: for decode-sized
+    # batches their GEMM pushes its output tiles to every rank (fused GEMM -> all-reduce)
+    push = None
+
     def __call__(self, x: Act, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if self.quant == "mxfp4":
             if isinstance(x, tuple):
                 q, s = x
             else:
                 q, s = K.quant_fp8(x)
+            if self.push is not None and out is None and q.is_cuda and \
+                    self.push.can_push(q.shape[0], self.N):
+                return self.push.gemm_push(q, s, self.w)
             return K.mxfp4_gemm(q, s, self.w.packed, self.w.sf, self.w.scales, self.N, out=out)
         if self.quant == "fp8":
             if isinstance(x, tuple):

@@ -1,17 +1,37 @@
 """Symmetric peer memory for the NVLink collectives (``csrc/comm.cu``).
 
-Each rank allocates one device buffer (flag/counter header + two parity data slots), exports a
-CUDA IPC handle, and opens every peer's handle (exchange over the process group as a CPU
+Each rank allocates device buffers (sequence header + two parity data halves), exports CUDA
+IPC handles, and opens every peer's handle (exchange over the process group as a CPU
 all_gather_object, like the reference's handle exchange ``radiance_allreduce.py:139-160``).
 Only plain peer loads/stores touch these buffers."""
 from __future__ import annotations
 
+import os
+from dataclasses import dataclass
 from typing import Optional
 
 import torch
 
 from ..ops._ext import ext
 from ..ops.kernels import _empty, status_word
+
+PUSH_MAX_ROWS = 64           # decode / verify batches use the GEMM-fused path
+PUSH_MAX_HIDDEN = 10240
+
+
+@dataclass
+class PushedPartial:
+    """Stand-in for the output of a row-parallel GEMM whose tiles were pushed into every rank's
+    receive buffer (``mxfp4_gemm_push``); the all-reduce call that consumes it only runs the
+    receiving half."""
+    M: int
+    H: int
+    expected: int
+    device: torch.device
+
+    @property
+    def shape(self):
+        return (self.M, self.H)
 
 
 class FusedComm:
@@ -21,21 +41,59 @@ class FusedComm:
         self.slot_bytes = slot_bytes
         hdr = ext().symm_header_bytes()
         self.buf = torch.zeros(hdr + 2 * slot_bytes, dtype=torch.uint8, device="cuda")
-        h = ext().ipc_handle(self.buf)
-        handles = [None] * world
-        dist.all_gather_object(handles, h.numpy().tobytes(), group=group)
-        self.ptrs = []
         self.opened = []
-        for r in range(world):
-            if r == rank:
-                self.ptrs.append(self.buf.data_ptr())
-            else:
-                p = ext().ipc_open(torch.frombuffer(bytearray(handles[r]), dtype=torch.uint8))
-                self.ptrs.append(p)
-                self.opened.append(p)
+        self.ptrs = self._exchange(self.buf, group)
+        # receive buffers of the GEMM-fused all-reduce (row-parallel GEMM pushes its tiles)
+        self.push_enabled = os.environ.get("RADIANCE_GEMM_PUSH", "1") != "0"
+        self.push_ptrs = None
+        if self.push_enabled:
+            nbytes = ext().push_buffer_bytes(world, PUSH_MAX_ROWS, PUSH_MAX_HIDDEN)
+            self.push_half_words = world * PUSH_MAX_ROWS * (PUSH_MAX_HIDDEN // 2)
+            self.push_buf = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+            self.push_ptrs = self._exchange(self.push_buf, group)
         dist.barrier(group=group)
         self.calls = 0
         self.fallbacks = 0
+        self.pushes = 0
+
+    def _exchange(self, buf: torch.Tensor, group) -> list:
+        """IPC-map every rank's `buf`; returns the device pointers, own one at `rank`."""
+        import torch.distributed as dist
+        h = ext().ipc_handle(buf)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, h.numpy().tobytes(), group=group)
+        ptrs = []
+        for r in range(self.world):
+            if r == self.rank:
+                ptrs.append(buf.data_ptr())
+            else:
+                p = ext().ipc_open(torch.frombuffer(bytearray(handles[r]), dtype=torch.uint8))
+                ptrs.append(p)
+                self.opened.append(p)
+        return ptrs
+
+    # ---- GEMM-fused all-reduce ----
+    def can_push(self, M: int, N: int) -> bool:
+        return (self.push_ptrs is not None and 0 < M <= PUSH_MAX_ROWS and N % 8 == 0
+                and N <= PUSH_MAX_HIDDEN)
+
+    def gemm_push(self, q, s, w) -> PushedPartial:
+        """Row-parallel W4A8 GEMM whose output tiles go straight into every rank's receive
+        buffer; the following all-reduce call reduces them."""
+        exp = ext().mxfp4_gemm_push(q, s, w.packed, w.sf, self.push_ptrs, self.rank,
+                                    self.push_half_words, status_word(q.device))
+        self.pushes += 1
+        return PushedPartial(q.shape[0], w.N, int(exp), q.device)
+
+    def _recv(self, x: PushedPartial, out, residual, weight, eps, res_out, q, s):
+        e = _empty(x.device)
+        ext().push_allreduce_recv(self.push_ptrs, self.rank, x.M, x.H, self.push_half_words,
+                                  out if out is not None else e,
+                                  residual if residual is not None else e,
+                                  weight if weight is not None else e, eps,
+                                  res_out if res_out is not None else e,
+                                  q if q is not None else e, s if s is not None else e,
+                                  min(64, x.M), status_word(x.device))
 
     @staticmethod
     def create(rank, world, group) -> Optional["FusedComm"]:
@@ -44,10 +102,16 @@ class FusedComm:
         return FusedComm(rank, world, group)
 
     def fits(self, x: torch.Tensor) -> bool:
+        # every rank's rows land in each buffer as 8-byte words carrying two bf16
         return x.dim() == 2 and x.dtype == torch.bfloat16 and x.shape[1] % 8 == 0 and \
-            x.shape[1] <= 10240 and x.numel() * 2 <= self.slot_bytes and x.is_contiguous()
+            x.shape[1] <= 10240 and self.world * x.numel() * 4 <= self.slot_bytes and \
+            x.is_contiguous()
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        if isinstance(x, PushedPartial):
+            out = torch.empty(x.M, x.H, dtype=torch.bfloat16, device=x.device)
+            self._recv(x, out, None, None, 0.0, None, None, None)
+            return out
         if not self.fits(x) or x.shape[0] > 256:
             import torch.distributed as dist
             self.fallbacks += 1
@@ -63,6 +127,12 @@ class FusedComm:
     def all_reduce_add_rms_quant(self, x, residual, weight, eps):
         """Fused: all-reduce(x) + residual -> residual_out; Gemma RMSNorm + e4m3 quant."""
         M, H = x.shape
+        if isinstance(x, PushedPartial):
+            q = torch.empty(M, H, dtype=torch.float8_e4m3fn, device=x.device)
+            s = torch.empty(M, dtype=torch.float32, device=x.device)
+            r = torch.empty(M, H, dtype=torch.bfloat16, device=x.device)
+            self._recv(x, None, residual, weight, eps, r, q, s)
+            return q, s, r
         if not self.fits(x) or M > 256:
             from ..ops import kernels as K
             return K.add_rms_quant(self.all_reduce(x), residual, weight, eps)
