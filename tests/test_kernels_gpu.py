@@ -204,6 +204,55 @@ def test_paged_attention_decode_kernel(D, Hq, Hkv, ctx_lens, splits, fmt, monkey
     assert rel_err(got, general) < 1e-2, rel_err(got, general)
 
 
+@pytest.mark.parametrize("lens,has_init,sdt", [
+    ([1500], [0], torch.float32), ([64, 1, 200, 7], [1, 1, 0, 1], torch.float32),
+    ([130, 65], [1, 0], torch.bfloat16)])
+def test_gdn_chunked_matches_recurrent(lens, has_init, sdt, monkeypatch):
+    """The 64-token chunk-scan kernel (tensor cores, bf16 operands, fp32 state) against the fp32
+    token-serial oracle and against the token-serial CUDA kernel: outputs and final states."""
+    torch.manual_seed(7)
+    Hk, Hv, D = 4, 12, 128
+    key_dim, vdim = Hk * D, Hv * D
+    T = sum(lens)
+    qk = torch.randn(T, 2 * Hk, D)
+    qk = qk / qk.norm(dim=-1, keepdim=True)
+    v = torch.randn(T, vdim) * 0.5
+    y = torch.cat([qk.reshape(T, -1), v], 1).to(torch.bfloat16)
+    ba = (torch.randn(T, 2 * Hv) * 1.5).to(torch.bfloat16)
+    A_log = torch.log(torch.rand(Hv) * 8 + 0.5)
+    dt_bias = torch.randn(Hv) * 0.3
+    state0 = (torch.randn(len(lens) + 1, Hv, D, D) * 0.05).to(sdt)
+    meta = _Meta()
+    qsl = [0]
+    for l in lens:
+        qsl.append(qsl[-1] + l)
+    meta.query_start_loc = torch.tensor(qsl, dtype=torch.int32, device=DEV)
+    meta.state_slots = torch.arange(1, len(lens) + 1, dtype=torch.int32, device=DEV)
+    meta.has_initial = torch.tensor(has_init, dtype=torch.int32, device=DEV)
+    meta.num_seqs, meta.num_tokens = len(lens), T
+    scale = D ** -0.5
+    st_chunk = state0.to(DEV).clone()
+    got = K.gdn_recurrent(y.to(DEV), ba.to(DEV), A_log.to(DEV), dt_bias.to(DEV), st_chunk, meta,
+                          Hk, scale)
+    monkeypatch.setattr(K, "_GDN_CHUNKED", False)
+    st_serial = state0.to(DEV).clone()
+    serial = K.gdn_recurrent(y.to(DEV), ba.to(DEV), A_log.to(DEV), dt_bias.to(DEV), st_serial,
+                             meta, Hk, scale)
+    torch.cuda.synchronize()
+    yf = y.float()
+    for bi, (s0, s1) in enumerate(zip(qsl[:-1], qsl[1:])):
+        q = yf[s0:s1, :key_dim].view(-1, Hk, D)
+        k = yf[s0:s1, key_dim:2 * key_dim].view(-1, Hk, D)
+        vv = yf[s0:s1, 2 * key_dim:].view(-1, Hv, D)
+        g, beta = ref.gdn_gates(ba[s0:s1, Hv:], ba[s0:s1, :Hv], A_log, dt_bias)
+        s_init = state0[bi + 1].float() if has_init[bi] else torch.zeros(Hv, D, D)
+        o_ref, s_ref = ref.gdn_recurrent(q, k, vv, g, beta, s_init, scale)
+        o_got = got[s0:s1].float().cpu().view(-1, Hv, D)
+        assert rel_err(o_got, o_ref) < 3e-2, (bi, rel_err(o_got, o_ref))
+        assert rel_err(st_chunk[bi + 1].float().cpu(), s_ref) < 3e-2, bi
+        assert rel_err(o_got, serial[s0:s1].float().cpu().view(-1, Hv, D)) < 3e-2, bi
+
+
 def test_qkv_prologue():
     torch.manual_seed(1)
     T, Hq, Hkv, D, rot = 5, 4, 2, 256, 64

@@ -27,6 +27,9 @@ void gdn_recurrent(torch::Tensor y, torch::Tensor ba, torch::Tensor A_log, torch
                    torch::Tensor state, torch::Tensor qsl, torch::Tensor slots,
                    torch::Tensor has_init, torch::Tensor commit_len, int64_t Hk, double scale,
                    torch::Tensor out, bool write_out);
+void gdn_chunked(torch::Tensor y, torch::Tensor ba, torch::Tensor A_log, torch::Tensor dt_bias,
+                 torch::Tensor state, torch::Tensor qsl, torch::Tensor slots,
+                 torch::Tensor has_init, int64_t Hk, double scale, torch::Tensor out);
 void qkv_prologue(torch::Tensor qkv, int64_t q_head_stride, int64_t k_off, int64_t v_off,
                   torch::Tensor positions, torch::Tensor qn_w, torch::Tensor kn_w,
                   torch::Tensor cos_sin, int64_t rot, int64_t Hq, int64_t Hkv, double eps,
@@ -76,6 +79,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_recurrent", &rad::gdn_recurrent, "GDN varlen recurrent delta rule");
   m.def("qkv_prologue", &rad::qkv_prologue, "QK RMSNorm + RoPE + paged KV write");
   m.def("paged_attention", &rad::paged_attention, "varlen paged attention (split-KV)");
+  m.def("gdn_chunked", &rad::gdn_chunked, "chunked (64-token) gated delta rule for prefill");
   m.def("mxfp4_gemm_push", &rad::mxfp4_gemm_push,
         "row-parallel W4A8 GEMM that pushes its tiles into every peer's receive buffer");
   m.def("push_buffer_bytes", &rad::push_buffer_bytes, "size of a GEMM-push receive buffer");

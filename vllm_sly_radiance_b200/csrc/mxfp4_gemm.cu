@@ -77,7 +77,7 @@ __host__ __device__ constexpr uint32_t make_idesc(int bn, int sf_id) {
          | ((uint32_t)sf_id << 4);       // B scale-factor id
 }
 
-template <int BN, bool GROUPED = false>
+template <int BN, bool GROUPED = false, bool PUSH = false>
 __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
     mxfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                       const __grid_constant__ CUtensorMap tmap_a, const uint8_t* __restrict__ sfw,
@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
     tc_fence_after();
     const bool have_acc = nk > 0 && !*abort_flag;
     if (num_splits == 1) {
-      const uint32_t seq = push.world ? push_seq(push) : 0u;
+      const uint32_t seq = PUSH ? push_seq(push) : 0u;
 #pragma unroll 1
       for (int c0 = 0; c0 < BN; c0 += 16) {
         uint32_t r[16];
@@ -242,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
           const int m = m0 + c0 + j;
           if (m >= m_end) break;                       // uniform across the warp
           const float v = (have_acc && n < n_lim) ? __uint_as_float(r[j]) * a_scale[m] : 0.f;
-          if (push.world) {
+          if constexpr (PUSH) {
             // adjacent lanes own adjacent columns: even lanes store the pair as one LL word
             // straight into this rank's slot of every peer's receive buffer
             const float vn = __shfl_down_sync(0xffffffffu, v, 1);
@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
       const int n = n_out0 + row;
       const uint32_t my_rank = cluster_ctarank();
       const uint32_t part_addr = smem_u32(stage_base);
-      const uint32_t seq = push.world ? push_seq(push) : 0u;
+      const uint32_t seq = PUSH ? push_seq(push) : 0u;
       for (int j = my_rank; j < BN; j += num_splits) {
         const int m = m0 + j;
         if (m >= m_end) break;                         // uniform across the warp
@@ -293,7 +293,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
           }
           acc *= a_scale[m];
         }
-        if (push.world) {
+        if constexpr (PUSH) {
           const float vn = __shfl_down_sync(0xffffffffu, acc, 1);
           if ((lane & 1) == 0 && n < n_lim)
             for (int p = 0; p < push.world; ++p)
@@ -361,12 +361,12 @@ static void launch(const torch::Tensor& a, const torch::Tensor& a_scale, const t
   const int k_tiles = Kw / BK;
   const int per = (k_tiles + splits - 1) / splits;
   dim3 grid((N + BM - 1) / BM, (M + BN - 1) / BN, splits);
-  auto kern = mxfp4_gemm_kernel<BN>;
-  static bool attr_set = false;
-  if (!attr_set) {
+  auto kern = push.world ? mxfp4_gemm_kernel<BN, false, true> : mxfp4_gemm_kernel<BN, false, false>;
+  static bool attr_set[2] = {false, false};
+  if (!attr_set[push.world ? 1 : 0]) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-    attr_set = true;
+    attr_set[push.world ? 1 : 0] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;

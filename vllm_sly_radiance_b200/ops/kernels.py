@@ -333,6 +333,9 @@ def gdn_conv_state_update(x, conv_state, meta, commit_len: Optional[torch.Tensor
                                 meta.has_initial, _none(commit_len, x.device))
 
 
+_GDN_CHUNKED = os.environ.get("RADIANCE_GDN_CHUNKED", "1") != "0"
+
+
 def gdn_recurrent(y, ba, A_log, dt_bias, ssm_state, meta, num_k_heads: int, scale: float,
                   out: Optional[torch.Tensor] = None, commit_len=None, write_out: bool = True):
     """Delta rule over the batch; ssm_state [S, Hv, dv, dk] updated in place (after the first
@@ -362,6 +365,12 @@ def gdn_recurrent(y, ba, A_log, dt_bias, ssm_state, meta, num_k_heads: int, scal
             ssm_state[slot] = st_c.to(ssm_state.dtype)
             if write_out:
                 out[s0:s1] = o.reshape(s1 - s0, -1).to(torch.bfloat16)
+        return out
+    if (commit_len is None and write_out and _GDN_CHUNKED and DK == 128 and DV == 128
+            and meta.num_tokens > meta.num_seqs):
+        # prefill rows in the batch: the 64-token chunk scan on the tensor cores
+        ext().gdn_chunked(y, ba, A_log, dt_bias, ssm_state, meta.query_start_loc,
+                          meta.state_slots, meta.has_initial, num_k_heads, scale, out)
         return out
     ext().gdn_recurrent(y, ba, A_log, dt_bias, ssm_state, meta.query_start_loc, meta.state_slots,
                         meta.has_initial, _none(commit_len, y.device), num_k_heads, scale, out,
