@@ -204,10 +204,10 @@ def test_paged_attention_decode_kernel(D, Hq, Hkv, ctx_lens, splits, fmt, monkey
     assert rel_err(got, general) < 1e-2, rel_err(got, general)
 
 
-@pytest.mark.parametrize("lens,has_init,sdt", [
-    ([1500], [0], torch.float32), ([64, 1, 200, 7], [1, 1, 0, 1], torch.float32),
-    ([130, 65], [1, 0], torch.bfloat16)])
-def test_gdn_chunked_matches_recurrent(lens, has_init, sdt, monkeypatch):
+@pytest.mark.parametrize("lens,has_init,sdt,split", [
+    ([1500], [0], torch.float32, 0), ([64, 1, 200, 7], [1, 1, 0, 1], torch.float32, 1),
+    ([130, 65], [1, 0], torch.bfloat16, 2), ([300], [1], torch.float32, 4)])
+def test_gdn_chunked_matches_recurrent(lens, has_init, sdt, split, monkeypatch):
     """The 64-token chunk-scan kernel (tensor cores, bf16 operands, fp32 state) against the fp32
     token-serial oracle and against the token-serial CUDA kernel: outputs and final states."""
     torch.manual_seed(7)
@@ -231,6 +231,7 @@ def test_gdn_chunked_matches_recurrent(lens, has_init, sdt, monkeypatch):
     meta.has_initial = torch.tensor(has_init, dtype=torch.int32, device=DEV)
     meta.num_seqs, meta.num_tokens = len(lens), T
     scale = D ** -0.5
+    monkeypatch.setattr(K, "_GDN_CHUNK_SPLIT", split)
     st_chunk = state0.to(DEV).clone()
     got = K.gdn_recurrent(y.to(DEV), ba.to(DEV), A_log.to(DEV), dt_bias.to(DEV), st_chunk, meta,
                           Hk, scale)

@@ -268,6 +268,7 @@ class EngineConfig:
     num_kv_blocks: Optional[int] = None
     enable_cuda_graphs: bool = True
     cuda_graph_max_bs: int = 64
+    capture_graphs_at_start: bool = True   # capture every decode bucket at engine start
     enable_prefix_caching: bool = False
     prefix_snapshot_slots: int = 16  # GDN state snapshots kept for cached prefixes
     prefix_snapshot_interval: int = 0  # also snapshot every N prompt tokens (0: last boundary only)

@@ -29,7 +29,8 @@ void gdn_recurrent(torch::Tensor y, torch::Tensor ba, torch::Tensor A_log, torch
                    torch::Tensor out, bool write_out);
 void gdn_chunked(torch::Tensor y, torch::Tensor ba, torch::Tensor A_log, torch::Tensor dt_bias,
                  torch::Tensor state, torch::Tensor qsl, torch::Tensor slots,
-                 torch::Tensor has_init, int64_t Hk, double scale, torch::Tensor out);
+                 torch::Tensor has_init, int64_t Hk, double scale, torch::Tensor out,
+                 int64_t split_override);
 void qkv_prologue(torch::Tensor qkv, int64_t q_head_stride, int64_t k_off, int64_t v_off,
                   torch::Tensor positions, torch::Tensor qn_w, torch::Tensor kn_w,
                   torch::Tensor cos_sin, int64_t rot, int64_t Hq, int64_t Hkv, double eps,

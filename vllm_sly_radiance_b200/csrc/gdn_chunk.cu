@@ -95,7 +95,10 @@ DEVI float2 ld_bf16x2(const uint8_t* base, int row, int col, int ch) {
       *reinterpret_cast<const __nv_bfloat162*>(base + swz(row, col >> 3, ch) + (col & 7) * 2));
 }
 
-template <typename ST>
+// NS CTAs share one (sequence, head): CTA z owns value columns [z * 128 / NS, (z + 1) * 128 / NS)
+// of V, RHS, U, O and the matching rows of S; the intra-chunk K K^T / Q K^T terms are computed
+// by each of them (small next to the per-column work), so no data crosses CTAs.
+template <typename ST, int NS>
 __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(
     const __nv_bfloat16* __restrict__ y, int ldy,        // conv output [T, *]: q | k | v
     const __nv_bfloat16* __restrict__ ba, int ldba,      // [T, *]: b at col 0.., a at col Hv..
@@ -124,7 +127,9 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(
   const uint32_t aU = smem_u32(sU), aUs = smem_u32(sUs), aAb = smem_u32(sAb), aP = smem_u32(sP);
   const uint32_t aT = smem_u32(sT), aX = smem_u32(sX);
 
+  constexpr int DVS = D / NS;                       // value columns of this CTA
   const int b = blockIdx.x, h = blockIdx.y;
+  const int voff = blockIdx.z * DVS;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g_ = lane >> 2, t4 = lane & 3;
   const int s0 = qsl[b];
@@ -136,13 +141,17 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(
   const float negA = -__expf(A_log[h]);
   const float dtb = dt_bias[h];
 
-  // ---- state: fp32 in registers, warp w owns rows [16w, 16w + 16) of S [dv][dk] ----
-  float Sr[16][4];
+  // ---- state: fp32 in registers.  Rows [voff, voff + DVS) of S [dv][dk] belong to this CTA:
+  //      warp w owns the 16-row block w / NS and dk columns [(w % NS) * 128 / NS, ...) ----
+  constexpr int SNT = 16 / NS;                       // 8-wide dk tiles per warp
+  const int srow = voff + 16 * (warp / NS);
+  const int scol = (warp % NS) * (D / NS);
+  float Sr[SNT][4];
   ST* gS = state + ((size_t)slot * Hv + h) * D * D;
   const bool init = has_init[b] != 0;
 #pragma unroll
-  for (int n = 0; n < 16; ++n) {
-    const int r0 = 16 * warp + g_, c = n * 8 + 2 * t4;
+  for (int n = 0; n < SNT; ++n) {
+    const int r0 = srow + g_, c = scol + n * 8 + 2 * t4;
     Sr[n][0] = init ? to_f(gS[(size_t)r0 * D + c]) : 0.f;
     Sr[n][1] = init ? to_f(gS[(size_t)r0 * D + c + 1]) : 0.f;
     Sr[n][2] = init ? to_f(gS[(size_t)(r0 + 8) * D + c]) : 0.f;
@@ -249,13 +258,14 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(
     }
 
     // ---- K S^T and Q S^T: RHS = beta (V - e^G K S^T); O = e^G Q S^T (kept in registers) ----
-    float o[8][4];
+    constexpr int ONT = DVS / 16;            // 8-wide value tiles per warp in the [64 x DVS] stages
+    float o[ONT][4];
     {
       const int mt = warp >> 1;
-      const int nb = (warp & 1) * 64;         // 64 value columns
-      float ks[8][4];
+      const int nb = voff + (warp & 1) * (DVS / 2);
+      float ks[ONT][4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
+      for (int j = 0; j < ONT; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e) ks[j][e] = o[j][e] = 0.f;
 #pragma unroll
@@ -264,7 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(
         ldA(aK, 16 * mt, 2 * kk, CHD, lane, fk);
         ldA(aQ, 16 * mt, 2 * kk, CHD, lane, fq);
 #pragma unroll
-        for (int np = 0; np < 4; ++np) {
+        for (int np = 0; np < ONT / 2; ++np) {
           uint32_t bs[4];
           ldB(aS, nb + 16 * np, 2 * kk, CHD, lane, bs);
           mma(ks[2 * np], fk, bs[0], bs[1]);
@@ -274,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(
         }
       }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
+      for (int j = 0; j < ONT; ++j) {
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           const int i = 16 * mt + g_ + 8 * hh;
@@ -306,9 +316,9 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(
     }
     __syncthreads();
 
-    // ---- (I + A) U = RHS, blocked: warp w owns value columns [16w, 16w + 16) ----
-    {
-      const int nc = 2 * warp;                // first 8-column chunk of this warp
+    // ---- (I + A) U = RHS, blocked: warp w owns value columns voff + [16w, 16w + 16) ----
+    if (warp < DVS / 16) {
+      const int nc = (voff >> 3) + 2 * warp;  // first 8-column chunk of this warp
 #pragma unroll
       for (int bi = 0; bi < 4; ++bi) {
         float x[2][4];
@@ -362,13 +372,13 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(
     // ---- O += P U; write the chunk's outputs ----
     {
       const int mt = warp >> 1;
-      const int nb = (warp & 1) * 64;
+      const int nb = voff + (warp & 1) * (DVS / 2);
 #pragma unroll
       for (int kk = 0; kk < C / 16; ++kk) {
         uint32_t fp[4];
         ldA(aP, 16 * mt, 2 * kk, CHC, lane, fp);
 #pragma unroll
-        for (int np = 0; np < 4; ++np) {
+        for (int np = 0; np < ONT / 2; ++np) {
           uint32_t bu[4];
           ldBt(aU, 16 * kk, (nb >> 3) + 2 * np, CHD, lane, bu);
           mma(o[2 * np], fp, bu[0], bu[1]);
@@ -376,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(
         }
       }
 #pragma unroll
-      for (int j = 0; j < 8; ++j)
+      for (int j = 0; j < ONT; ++j)
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           const int i = 16 * mt + g_ + 8 * hh;
@@ -390,19 +400,19 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(
 
     // ---- S <- e^{G_last} S + (e^{G_last - G} U)^T K;  refresh the bf16 copy ----
     {
-      float acc[16][4];
+      float acc[SNT][4];
 #pragma unroll
-      for (int n = 0; n < 16; ++n)
+      for (int n = 0; n < SNT; ++n)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
 #pragma unroll
       for (int kk = 0; kk < C / 16; ++kk) {
         uint32_t fu[4];
-        ldAt(aUs, 16 * kk, 2 * warp, CHD, lane, fu);
+        ldAt(aUs, 16 * kk, srow >> 3, CHD, lane, fu);
 #pragma unroll
-        for (int np = 0; np < 8; ++np) {
+        for (int np = 0; np < SNT / 2; ++np) {
           uint32_t bk[4];
-          ldBt(aK, 16 * kk, 2 * np, CHD, lane, bk);
+          ldBt(aK, 16 * kk, (scol >> 3) + 2 * np, CHD, lane, bk);
           mma(acc[2 * np], fu, bk[0], bk[1]);
           mma(acc[2 * np + 1], fu, bk[2], bk[3]);
         }
@@ -410,8 +420,8 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(
       const float dl = __expf(Glast);
       __syncthreads();          // every warp has finished reading the previous bf16 state
 #pragma unroll
-      for (int n = 0; n < 16; ++n) {
-        const int r0 = 16 * warp + g_, c = n * 8 + 2 * t4;
+      for (int n = 0; n < SNT; ++n) {
+        const int r0 = srow + g_, c = scol + n * 8 + 2 * t4;
 #pragma unroll
         for (int e = 0; e < 4; ++e) Sr[n][e] = dl * Sr[n][e] + acc[n][e];
         st_bf16x2(sS, r0, c, CHD, Sr[n][0], Sr[n][1]);
@@ -422,8 +432,8 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(
 
   // ---- final state ----
 #pragma unroll
-  for (int n = 0; n < 16; ++n) {
-    const int r0 = 16 * warp + g_, c = n * 8 + 2 * t4;
+  for (int n = 0; n < SNT; ++n) {
+    const int r0 = srow + g_, c = scol + n * 8 + 2 * t4;
     gS[(size_t)r0 * D + c] = from_f<ST>(Sr[n][0]);
     gS[(size_t)r0 * D + c + 1] = from_f<ST>(Sr[n][1]);
     gS[(size_t)(r0 + 8) * D + c] = from_f<ST>(Sr[n][2]);
@@ -437,7 +447,8 @@ __global__ void __launch_bounds__(kThreads, 1) chunk_kernel(
 // speculative-commit options.  dk = dv = 128.
 void gdn_chunked(torch::Tensor y, torch::Tensor ba, torch::Tensor A_log, torch::Tensor dt_bias,
                  torch::Tensor state, torch::Tensor qsl, torch::Tensor slots,
-                 torch::Tensor has_init, int64_t Hk, double scale, torch::Tensor out) {
+                 torch::Tensor has_init, int64_t Hk, double scale, torch::Tensor out,
+                 int64_t split_override) {
   const int B = slots.size(0);
   if (B == 0) return;
   const int Hv = state.size(1), DV = state.size(2), DK = state.size(3);
@@ -447,10 +458,16 @@ void gdn_chunked(torch::Tensor y, torch::Tensor ba, torch::Tensor A_log, torch::
   TORCH_CHECK(out.stride(1) == 1 && (out.stride(0) % 2) == 0, "gdn_chunked: out layout");
   const at::cuda::CUDAGuard guard(y.device());
   auto stream = at::cuda::getCurrentCUDAStream();
-  dim3 grid(B, Hv);
-  auto run = [&](auto stag) {
+  // value-column split: enough CTAs to cover the SMs for small batches (1, 2 or 4 per head)
+  int ns = 1;
+  if ((int64_t)B * Hv < 148) ns = 2;     // measured: 4-way costs more than it gains
+  if (split_override > 0) ns = (int)split_override;
+  TORCH_CHECK(ns == 1 || ns == 2 || ns == 4, "gdn_chunked: split 1, 2 or 4");
+  dim3 grid(B, Hv, ns);
+  auto run = [&](auto stag, auto ntag) {
     using ST = typename decltype(stag)::type;
-    auto kern = gdnc::chunk_kernel<ST>;
+    constexpr int NSc = decltype(ntag)::value;
+    auto kern = gdnc::chunk_kernel<ST, NSc>;
     static bool set = false;
     if (!set) {
       C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, gdnc::SMEM));
@@ -465,8 +482,13 @@ void gdn_chunked(torch::Tensor y, torch::Tensor ba, torch::Tensor A_log, torch::
   };
   struct F32 { using type = float; };
   struct BF16 { using type = __nv_bfloat16; };
-  if (state.scalar_type() == at::kFloat) run(F32{});
-  else run(BF16{});
+  auto by_split = [&](auto stag) {
+    if (ns == 1) run(stag, std::integral_constant<int, 1>{});
+    else if (ns == 2) run(stag, std::integral_constant<int, 2>{});
+    else run(stag, std::integral_constant<int, 4>{});
+  };
+  if (state.scalar_type() == at::kFloat) by_split(F32{});
+  else by_split(BF16{});
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -77,6 +77,10 @@ class LLMEngine:
                                   max_model_len=config.max_model_len, device=self.device,
                                   enable_graphs=config.enable_cuda_graphs,
                                   graph_max_bs=config.cuda_graph_max_bs, num_spec_tokens=k)
+        if config.capture_graphs_at_start and self.device.type == "cuda":
+            t1 = time.time()
+            self.runner.capture_all()
+            log.info("captured %d decode graphs in %.1fs", len(self.runner.graphs), time.time() - t1)
         self.spec = None
         if config.speculative_method:
             from ..spec_decode.proposer import build_proposer

@@ -321,6 +321,23 @@ class ModelRunner:
         torch.cuda.current_stream().synchronize()
         return self.h_out[:B].tolist()
 
+    def capture_all(self):
+        """Capture the decode graphs of every bucket (greedy and sampled) up front, on dummy
+        all-padding batches, so no request pays a capture inside its step."""
+        if not self.enable_graphs:
+            return
+        from .scheduler import SchedulerOutput as _SO
+        for bucket in GRAPH_BUCKETS:
+            if bucket > self.graph_max_bs:
+                break
+            for greedy in (True, False):
+                if (bucket, greedy) in self.graphs:
+                    continue
+                dmeta, dids, _, _ = self.prepare(_SO([], 0, [], []), pad_to=bucket,
+                                                 nb_fixed=self.max_blocks)
+                self.graphs[(bucket, greedy)] = self._capture(bucket, greedy, dmeta, dids)
+        torch.cuda.synchronize(self.device)
+
     def _capture(self, bucket, greedy, meta, ids):
         dev = self.device
         sidx = torch.arange(bucket, dtype=torch.long, device=dev)

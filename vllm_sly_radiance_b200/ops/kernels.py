@@ -334,6 +334,7 @@ def gdn_conv_state_update(x, conv_state, meta, commit_len: Optional[torch.Tensor
 
 
 _GDN_CHUNKED = os.environ.get("RADIANCE_GDN_CHUNKED", "1") != "0"
+_GDN_CHUNK_SPLIT = int(os.environ.get("RADIANCE_GDN_CHUNK_SPLIT", "0"))   # 0: by batch size
 
 
 def gdn_recurrent(y, ba, A_log, dt_bias, ssm_state, meta, num_k_heads: int, scale: float,
@@ -370,7 +371,8 @@ def gdn_recurrent(y, ba, A_log, dt_bias, ssm_state, meta, num_k_heads: int, scal
             and meta.num_tokens > meta.num_seqs):
         # prefill rows in the batch: the 64-token chunk scan on the tensor cores
         ext().gdn_chunked(y, ba, A_log, dt_bias, ssm_state, meta.query_start_loc,
-                          meta.state_slots, meta.has_initial, num_k_heads, scale, out)
+                          meta.state_slots, meta.has_initial, num_k_heads, scale, out,
+                          _GDN_CHUNK_SPLIT)
         return out
     ext().gdn_recurrent(y, ba, A_log, dt_bias, ssm_state, meta.query_start_loc, meta.state_slots,
                         meta.has_initial, _none(commit_len, y.device), num_k_heads, scale, out,
