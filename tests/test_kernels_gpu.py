@@ -48,6 +48,35 @@ def test_mxfp4_gemm(M, N, Kd, splits):
     assert rel_err(got, want) < 1e-2, rel_err(got, want)
 
 
+@pytest.mark.parametrize("mode,M,N,Kd,with_res", [
+    (1, 1, 16480, 5120, True), (1, 1, 2176, 1088, False), (1, 1, 5120, 256, True),
+    (2, 1, 5120, 8704, False), (2, 1, 384, 1088, False), (2, 1, 256, 768, False)])
+def test_mxfp4_gemm_fused_producer(mode, M, N, Kd, with_res):
+    """Decode GEMM with the producer inside (add + RMSNorm + e4m3, or SiLU * mul + e4m3)
+    against the stand-alone producer kernel followed by the plain GEMM."""
+    g = torch.Generator().manual_seed(M * 11 + N + mode)
+    wq = MXFP4Weight.from_float(torch.randn(N, Kd, generator=g) * 0.02).to(DEV)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+    if mode == 1:
+        h = torch.randn(M, Kd, generator=g).to(torch.bfloat16).to(DEV)
+        res = torch.randn(M, Kd, generator=g).to(torch.bfloat16).to(DEV) if with_res else None
+        lw = (0.1 * torch.randn(Kd, generator=g)).to(torch.bfloat16).to(DEV)
+        q, s, r = K.add_rms_quant(h, res, lw, 1e-6)
+        want = K.mxfp4_gemm(q, s, wq.packed, wq.sf, wq.scales, N)
+        ro = torch.empty(M, Kd, dtype=torch.bfloat16, device=DEV)
+        K.mxfp4_gemm_act(1, h, res, lw, ro, 1e-6, wq, out)
+        torch.cuda.synchronize()
+        assert torch.equal(ro, r)
+    else:
+        gu = (torch.randn(M, 2 * Kd, generator=g) * 2).to(torch.bfloat16).to(DEV)
+        q, s = K.silu_mul_quant(gu)
+        want = K.mxfp4_gemm(q, s, wq.packed, wq.sf, wq.scales, N)
+        K.mxfp4_gemm_act(2, gu, None, None, None, 0.0, wq, out)
+        torch.cuda.synchronize()
+    K.check_status(out.device)
+    assert rel_err(out, want) < 1e-2, rel_err(out, want)
+
+
 def test_mxfp4_gemm_repeat_no_stale_state():
     """Back-to-back launches without a sync between them (split-K reduction must not leak)."""
     g = torch.Generator().manual_seed(3)

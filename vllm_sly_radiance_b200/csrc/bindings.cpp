@@ -46,6 +46,9 @@ int64_t mxfp4_gemm_push(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp
                         std::vector<int64_t> peers, int64_t rank, int64_t half_words,
                         torch::Tensor status);
 int64_t push_buffer_bytes(int64_t world, int64_t mmax, int64_t H);
+void mxfp4_gemm_act(int64_t mode, torch::Tensor x, torch::Tensor res, torch::Tensor w,
+                    torch::Tensor res_out, double eps, torch::Tensor wp, torch::Tensor sf,
+                    torch::Tensor out, torch::Tensor status);
 void push_allreduce_recv(std::vector<int64_t> peers, int64_t rank, int64_t M, int64_t H,
                          int64_t half_words, torch::Tensor out, torch::Tensor residual,
                          torch::Tensor weight, double eps, torch::Tensor res_out, torch::Tensor q,
@@ -84,6 +87,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mxfp4_gemm_push", &rad::mxfp4_gemm_push,
         "row-parallel W4A8 GEMM that pushes its tiles into every peer's receive buffer");
   m.def("push_buffer_bytes", &rad::push_buffer_bytes, "size of a GEMM-push receive buffer");
+  m.def("mxfp4_gemm_act", &rad::mxfp4_gemm_act,
+        "decode W4A8 GEMM with its producer fused in (1: add + RMSNorm + e4m3, 2: SiLU*mul + e4m3)");
   m.def("push_allreduce_recv", &rad::push_allreduce_recv,
         "receiving half of the GEMM-fused all-reduce (+ add / RMSNorm / e4m3 quant)");
   m.def("ipc_handle", &rad::ipc_handle, "CUDA IPC handle of a device buffer");

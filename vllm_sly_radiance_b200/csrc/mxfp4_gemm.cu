@@ -77,13 +77,88 @@ __host__ __device__ constexpr uint32_t make_idesc(int bn, int sf_id) {
          | ((uint32_t)sf_id << 4);       // B scale-factor id
 }
 
-template <int BN, bool GROUPED = false, bool PUSH = false>
+// Producer fused into the decode GEMM (ACT > 0, BN = 16, single row tile): the four epilogue
+// warps build the e4m3 activation tiles themselves instead of a separate producer kernel.
+//   ACT 1 (norm): s = x (+ res); y = bf16(s * rsqrt(mean(s^2) + eps) * (1 + w)); res_out = bf16(s)
+//   ACT 2 (silu): y = bf16(silu(g) * u) with x = [g | u] (K columns each)
+// then q = e4m3(y / scale), scale = max(amax(y) / 448, 1 / (448 * 512)) per row -- the exact
+// numerics of the stand-alone producers (norm_quant.cu).
+constexpr int kActMaxChunks = 9;       // fused producers: rows of up to 9 * 1024 features
+
+struct ActArgs {
+  const __nv_bfloat16* x;
+  int ldx;
+  const __nv_bfloat16* res;
+  int ldr;
+  const __nv_bfloat16* w;
+  __nv_bfloat16* res_out;
+  int ldro;
+  float eps;
+  int K;
+};
+
+DEVI void act_load8(const __nv_bfloat16* p, float (&f)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+// 8 activation values of row m at feature k (k % 8 == 0): y (bf16-rounded) and, for norm, the
+// residual sum s
+template <int ACT>
+DEVI void act_values(const ActArgs& aa, int m, int k, float rs, float (&y)[8], float (&sv)[8]) {
+  if constexpr (ACT == 1) {
+    act_load8(aa.x + (size_t)m * aa.ldx + k, sv);
+    if (aa.res) {
+      float r[8];
+      act_load8(aa.res + (size_t)m * aa.ldr + k, r);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sv[j] += r[j];
+    }
+    float wv[8];
+    act_load8(aa.w + k, wv);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y[j] = bf16_round(sv[j] * rs * (wv[j] + 1.f));
+  } else {
+    float g[8], u[8];
+    act_load8(aa.x + (size_t)m * aa.ldx + k, g);
+    act_load8(aa.x + (size_t)m * aa.ldx + aa.K + k, u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) y[j] = bf16_round(g[j] / (1.f + __expf(-g[j])) * u[j]);
+  }
+}
+
+// sum over the 128 producer threads (warps 2-5), named barrier 2
+DEVI float prod_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = (threadIdx.x >> 5) - 2;
+  asm volatile("bar.sync 2, 128;" ::: "memory");
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  asm volatile("bar.sync 2, 128;" ::: "memory");
+  return red[0] + red[1] + red[2] + red[3];
+}
+DEVI float prod_max(float v, float* red) {
+  v = warp_max(v);
+  const int w = (threadIdx.x >> 5) - 2;
+  asm volatile("bar.sync 2, 128;" ::: "memory");
+  if ((threadIdx.x & 31) == 0) red[w] = v;
+  asm volatile("bar.sync 2, 128;" ::: "memory");
+  return fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+}
+
+template <int BN, bool GROUPED = false, bool PUSH = false, int ACT = 0>
 __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
     mxfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                       const __grid_constant__ CUtensorMap tmap_a, const uint8_t* __restrict__ sfw,
                       const float* __restrict__ a_scale, __nv_bfloat16* __restrict__ out,
                       int ldo, int M, int N, int K, int k_tiles_per_split, int* __restrict__ status,
-                      const int* __restrict__ items, int n_per_group, const PushArgs push) {
+                      const int* __restrict__ items, int n_per_group, const PushArgs push,
+                      const ActArgs act) {
   using C = Cfg<BN>;
   // Grouped (MoE) mode: blockIdx.y indexes a work table of (expert, first row, rows); the
   // expert's weights are rows [e * n_per_group, (e + 1) * n_per_group) of the stacked tensor.
@@ -120,9 +195,11 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
   const int kt1 = min(k_tiles_total, kt0 + k_tiles_per_split);
   const int nk = kt1 - kt0;
 
+  __shared__ float s_act_scale[ACT ? BN : 1];
+  __shared__ float s_red[4];
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(&full_bar[s], 1);
+      mbar_init(&full_bar[s], ACT ? 2 : 1);   // + the activation producers' arrival
       mbar_init(&empty_bar[s], 1);
     }
     mbar_init(acc_bar, 1);
@@ -131,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmap_w);
-    tma_prefetch_desc(&tmap_a);
+    if (!ACT) tma_prefetch_desc(&tmap_a);
   }
   pdl_trigger();   // the next kernel may start its own prologue
   if (warp == 1) {
@@ -168,27 +245,30 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
       // Weights and scale factors do not depend on the preceding kernel: fill the pipeline with
       // them while that kernel drains, then wait for it and add the activation tiles.
       const int pre = nk < C::STAGES ? nk : C::STAGES;
+      constexpr uint32_t kTx = W_TILE_TX + (ACT ? 0 : C::A_TILE_BYTES) + SF_TILE_BYTES;
       for (int i = 0; i < pre; ++i) {
         uint8_t* st = stage_base + i * C::STAGE_BYTES;
         const int kt = kt0 + i;
-        mbar_arrive_expect_tx(&full_bar[i], W_TILE_TX + C::A_TILE_BYTES + SF_TILE_BYTES);
+        mbar_arrive_expect_tx(&full_bar[i], kTx);
         tma_load_2d_hint(st, &tmap_w, &full_bar[i], kt * BK, n0, w_policy);
         bulk_load(st + W_TILE_BYTES + C::A_TILE_BYTES, sf_row + (size_t)kt * SF_TILE_BYTES,
                   SF_TILE_BYTES, &full_bar[i]);
       }
-      pdl_wait();
-      for (int i = 0; i < pre; ++i)
-        tma_load_2d(stage_base + i * C::STAGE_BYTES + W_TILE_BYTES, &tmap_a, &full_bar[i],
-                    (kt0 + i) * BK, m0);
+      if (!ACT) {
+        pdl_wait();
+        for (int i = 0; i < pre; ++i)
+          tma_load_2d(stage_base + i * C::STAGE_BYTES + W_TILE_BYTES, &tmap_a, &full_bar[i],
+                      (kt0 + i) * BK, m0);
+      }
       for (int i = pre; i < nk; ++i) {
         const int s = i % C::STAGES;
         const uint32_t ph = (i / C::STAGES) & 1;
         if (!mbar_wait(&empty_bar[s], ph ^ 1, status)) { *abort_flag = 1; break; }
         uint8_t* st = stage_base + s * C::STAGE_BYTES;
         const int kt = kt0 + i;
-        mbar_arrive_expect_tx(&full_bar[s], W_TILE_TX + C::A_TILE_BYTES + SF_TILE_BYTES);
+        mbar_arrive_expect_tx(&full_bar[s], kTx);
         tma_load_2d_hint(st, &tmap_w, &full_bar[s], kt * BK, n0, w_policy);
-        tma_load_2d(st + W_TILE_BYTES, &tmap_a, &full_bar[s], kt * BK, m0);
+        if (!ACT) tma_load_2d(st + W_TILE_BYTES, &tmap_a, &full_bar[s], kt * BK, m0);
         bulk_load(st + W_TILE_BYTES + C::A_TILE_BYTES, sf_row + (size_t)kt * SF_TILE_BYTES,
                   SF_TILE_BYTES, &full_bar[s]);
       }
@@ -222,11 +302,105 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
       else mbar_arrive(acc_bar);
     }
   } else {
-    // ---------------- epilogue ----------------
+    // ---------------- activation producers (ACT) + epilogue ----------------
     const int q = warp & 3;            // TMEM lane quarter this warp may access
     const int row = q * 32 + lane;     // weight row within the tile
     const int n = n_out0 + row;        // output column
-    pdl_wait();                        // a_scale comes from the preceding kernel
+    pdl_wait();                        // activations / a_scale come from the preceding kernel
+    if constexpr (ACT != 0) {
+      static_assert(BN == 16, "fused producers run with one 16-row tile");
+      // One activation row (M = 1, host-checked).  Thread pt owns the 8-element chunks
+      // j = pt + 128 * i of the row (K <= kActMaxChunks * 1024).  All of a thread's loads are
+      // issued together; the CTA's own K range is quantised into registers up front, so the
+      // pipeline loop below only stores precomputed bytes into each stage's slot.
+      constexpr int MAXC = kActMaxChunks;
+      const int pt = threadIdx.x - 64;                  // 0..127
+      const int Ka = act.K;
+      const int nch = Ka / 8;
+      const int own0 = kt0 * (BK / 8), own1 = min(kt1 * (BK / 8), nch);
+      float rs = 0.f;
+      if constexpr (ACT == 1) {
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < MAXC; ++i) {
+          const int j = pt + 128 * i;
+          if (j < nch) {
+            float sv[8];
+            act_load8(act.x + j * 8, sv);
+            if (act.res) {
+              float rr[8];
+              act_load8(act.res + j * 8, rr);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) sv[e] += rr[e];
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) ss += sv[e] * sv[e];
+            if (n_tile == 0 && act.res_out && j >= own0 && j < own1) {   // new residual, once
+              uint4 o;
+              __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) oh[e] = __floats2bfloat162_rn(sv[2 * e], sv[2 * e + 1]);
+              *reinterpret_cast<uint4*>(act.res_out + j * 8) = o;
+            }
+          }
+        }
+        rs = rsqrtf(prod_sum(ss, s_red) / (float)Ka + act.eps);
+      }
+      uint32_t ypk[MAXC][4];                            // bf16-rounded y, packed in pairs
+      float amax = 0.f;
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        const int j = pt + 128 * i;
+        if (j < nch) {
+          float y[8], sv[8];
+          act_values<ACT>(act, 0, j * 8, rs, y, sv);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            __nv_bfloat162 hh = __floats2bfloat162_rn(y[2 * e], y[2 * e + 1]);
+            ypk[i][e] = *reinterpret_cast<uint32_t*>(&hh);
+            amax = fmaxf(amax, fmaxf(fabsf(y[2 * e]), fabsf(y[2 * e + 1])));
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) ypk[i][e] = 0u;
+        }
+      }
+      amax = prod_max(amax, s_red);
+      const float scale = fmaxf(amax / 448.f, 1.f / (448.f * 512.f));
+      const float inv = 1.f / scale;
+      if (pt == 0) s_act_scale[0] = scale;
+      uint2 qv[MAXC];
+#pragma unroll
+      for (int i = 0; i < MAXC; ++i) {
+        uint16_t* hh = reinterpret_cast<uint16_t*>(&qv[i]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&ypk[i][e]));
+          hh[e] = f32x2_to_e4m3x2(f.x * inv, f.y * inv);
+        }
+      }
+      // pipeline: stage i holds chunks [kt * 16, kt * 16 + 16) of row 0 (rows 1..15 of the tile
+      // are never read back: their output rows are not stored)
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % C::STAGES;
+        const uint32_t ph = (i / C::STAGES) & 1;
+        if (!mbar_wait(&empty_bar[s], ph ^ 1, status)) { *abort_flag = 1; break; }
+        const int jb = (kt0 + i) * (BK / 8);
+        const int c = (pt - jb) & 127;                  // chunk of this stage owned by pt, if < 16
+        if (c < BK / 8) {
+          const int j = jb + c;
+          uint2 val = make_uint2(0, 0);
+#pragma unroll
+          for (int ii = 0; ii < MAXC; ++ii)
+            if (pt + 128 * ii == j) val = qv[ii];
+          uint8_t* slot = stage_base + s * C::STAGE_BYTES + W_TILE_BYTES;
+          *reinterpret_cast<uint2*>(slot + (c >> 1) * 16 + (c & 1) * 8) = val;   // row 0: no swizzle
+        }
+        fence_proxy_async();                            // generic-proxy writes -> tensor core
+        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (pt == 0) mbar_arrive(&full_bar[s]);
+      }
+    }
     if (!mbar_wait(acc_bar, 0, status)) *abort_flag = 1;
     tc_fence_after();
     const bool have_acc = nk > 0 && !*abort_flag;
@@ -241,7 +415,8 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
         for (int j = 0; j < 16; ++j) {
           const int m = m0 + c0 + j;
           if (m >= m_end) break;                       // uniform across the warp
-          const float v = (have_acc && n < n_lim) ? __uint_as_float(r[j]) * a_scale[m] : 0.f;
+          const float asc = ACT ? s_act_scale[m - m0] : a_scale[m];
+          const float v = (have_acc && n < n_lim) ? __uint_as_float(r[j]) * asc : 0.f;
           if constexpr (PUSH) {
             // adjacent lanes own adjacent columns: even lanes store the pair as one LL word
             // straight into this rank's slot of every peer's receive buffer
@@ -291,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
             asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(a));
             acc += v;
           }
-          acc *= a_scale[m];
+          acc *= ACT ? s_act_scale[m - m0] : a_scale[m];
         }
         if constexpr (PUSH) {
           const float vn = __shfl_down_sync(0xffffffffu, acc, 1);
@@ -352,21 +527,32 @@ static CUtensorMap weight_map(const torch::Tensor& packed, int64_t N, int64_t K)
 template <int BN>
 static void launch(const torch::Tensor& a, const torch::Tensor& a_scale, const torch::Tensor& wp,
                    const torch::Tensor& sf, torch::Tensor& out, int M, int N, int K, int splits,
-                   int* status, cudaStream_t stream, const PushArgs& push) {
+                   int* status, cudaStream_t stream, const PushArgs& push, int act_mode = 0,
+                   const ActArgs& aa = ActArgs{}) {
   using C = Cfg<BN>;
   const int Kw = (int)wp.size(1) * 2;          // whole K tiles of stored weight
   CUtensorMap tw = weight_map(wp, N, Kw);
-  CUtensorMap ta = make_tma_2d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, a.stride(0), BK,
-                               BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  // fused producers build the activation tiles in the kernel: no activation tensor map
+  CUtensorMap ta = act_mode ? tw
+                            : make_tma_2d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M,
+                                          a.stride(0), BK, BN, CU_TENSOR_MAP_SWIZZLE_128B);
   const int k_tiles = Kw / BK;
   const int per = (k_tiles + splits - 1) / splits;
   dim3 grid((N + BM - 1) / BM, (M + BN - 1) / BN, splits);
-  auto kern = push.world ? mxfp4_gemm_kernel<BN, false, true> : mxfp4_gemm_kernel<BN, false, false>;
-  static bool attr_set[2] = {false, false};
-  if (!attr_set[push.world ? 1 : 0]) {
+  using KernT = decltype(&mxfp4_gemm_kernel<BN, false, false, 0>);
+  KernT kern = push.world ? mxfp4_gemm_kernel<BN, false, true, 0> : mxfp4_gemm_kernel<BN, false, false, 0>;
+  int variant = push.world ? 1 : 0;
+  if constexpr (BN == 16) {
+    if (act_mode == 1) { kern = mxfp4_gemm_kernel<BN, false, false, 1>; variant = 2; }
+    if (act_mode == 2) { kern = mxfp4_gemm_kernel<BN, false, false, 2>; variant = 3; }
+  } else {
+    TORCH_CHECK(act_mode == 0, "fused producers need a 16-row tile");
+  }
+  static bool attr_set[4] = {false, false, false, false};
+  if (!attr_set[variant]) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-    attr_set[push.world ? 1 : 0] = true;
+    attr_set[variant] = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
@@ -383,10 +569,10 @@ static void launch(const torch::Tensor& a, const torch::Tensor& a_scale, const t
   cfg.attrs = attrs;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tw, ta, (const uint8_t*)sf.data_ptr(),
-                                    (const float*)a_scale.data_ptr(),
+                                    act_mode ? (const float*)nullptr : (const float*)a_scale.data_ptr(),
                                     push.world ? nullptr : (__nv_bfloat16*)out.data_ptr(),
                                     push.world ? 0 : (int)out.stride(0), M, N, Kw,
-                                    per, status, (const int*)nullptr, 0, push));
+                                    per, status, (const int*)nullptr, 0, push, aa));
 }
 
 static int pick_splits(int tiles, int k_tiles, int ctas_per_sm) {
@@ -419,7 +605,8 @@ static void launch_grouped(const torch::Tensor& a, const torch::Tensor& a_scale,
   C10_CUDA_CHECK(launch_pdl(kern, grid, dim3(kThreads), C::SMEM_BYTES, stream, tw, ta,
                             (const uint8_t*)sf.data_ptr(), (const float*)a_scale.data_ptr(),
                             (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), M, Ntot, K,
-                            K / BK, status, (const int*)items.data_ptr(), n_per_group, PushArgs{}));
+                            K / BK, status, (const int*)items.data_ptr(), n_per_group, PushArgs{},
+                            ActArgs{}));
 }
 
 }  // namespace mxfp4
@@ -500,6 +687,51 @@ static int64_t mxfp4_gemm_impl(torch::Tensor a, torch::Tensor a_scale, torch::Te
 void mxfp4_gemm(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
                 torch::Tensor out, int64_t splits_override, torch::Tensor status) {
   mxfp4_gemm_impl(a, a_scale, wp, sf, out, splits_override, status, PushArgs{});
+}
+
+// Decode GEMM (M <= 16) with its producer fused in: mode 1 = residual add + RMSNorm(1 + w) +
+// e4m3 (x = h, res optional, res_out receives the new residual), mode 2 = SiLU(g) * u + e4m3
+// (x = [g | u]).  out: bf16 [M, N].
+void mxfp4_gemm_act(int64_t mode, torch::Tensor x, torch::Tensor res, torch::Tensor w,
+                    torch::Tensor res_out, double eps, torch::Tensor wp, torch::Tensor sf,
+                    torch::Tensor out, torch::Tensor status) {
+  using namespace mxfp4;
+  TORCH_CHECK(mode == 1 || mode == 2, "mxfp4_gemm_act: mode 1 (norm) or 2 (silu)");
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.stride(1) == 1, "x: bf16 rows");
+  const int M = x.size(0);
+  const int K = mode == 2 ? (int)x.size(1) / 2 : (int)x.size(1);
+  const int N = wp.size(0);
+  const int Kw = (int)wp.size(1) * 2;
+  TORCH_CHECK(M == 1, "mxfp4_gemm_act: one activation row");
+  TORCH_CHECK(K <= kActMaxChunks * 1024, "mxfp4_gemm_act: K <= 9216");
+  TORCH_CHECK(K % 16 == 0 && Kw % BK == 0 && Kw >= K && Kw - K < BK, "mxfp4_gemm_act: K");
+  TORCH_CHECK(x.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(x.data_ptr()) % 16) == 0,
+              "mxfp4_gemm_act: x rows 16-byte aligned");
+  const bool has_res = res.defined() && res.numel();
+  const bool has_ro = res_out.defined() && res_out.numel();
+  if (mode == 1) {
+    TORCH_CHECK(w.numel() >= K, "mxfp4_gemm_act: norm weight");
+    TORCH_CHECK(!has_res || (res.stride(0) % 8 == 0 && res.stride(1) == 1), "res rows");
+    TORCH_CHECK(!has_ro || (res_out.stride(0) % 8 == 0 && res_out.stride(1) == 1), "res_out rows");
+  }
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(1) == 1 && out.size(1) >= N, "out");
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(x.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  int* st = status.numel() ? status.data_ptr<int>() : nullptr;
+  ActArgs aa{};
+  aa.x = (const __nv_bfloat16*)x.data_ptr();
+  aa.ldx = (int)x.stride(0);
+  aa.res = has_res ? (const __nv_bfloat16*)res.data_ptr() : nullptr;
+  aa.ldr = has_res ? (int)res.stride(0) : 0;
+  aa.w = mode == 1 ? (const __nv_bfloat16*)w.data_ptr() : nullptr;
+  aa.res_out = has_ro ? (__nv_bfloat16*)res_out.data_ptr() : nullptr;
+  aa.ldro = has_ro ? (int)res_out.stride(0) : 0;
+  aa.eps = (float)eps;
+  aa.K = K;
+  const int tiles = (N + BM - 1) / BM;
+  const int splits = pick_splits(tiles, Kw / BK, 2);
+  launch<16>(x, x, wp, sf, out, M, N, K, splits, st, stream, PushArgs{}, (int)mode, aa);
 }
 
 // Row-parallel GEMM fused with the push half of the all-reduce: peers = every rank's receive

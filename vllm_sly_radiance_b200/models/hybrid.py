@@ -22,19 +22,23 @@ import math
 from dataclasses import dataclass, field
 from typing import Callable, Optional
 
+import os
+
 import torch
 
 from ..config import ModelConfig
 from ..ops import kernels as K
 from ..quant.formats import kv4_row_bytes
 from ..quant.mxfp4 import MXFP4Weight
-from .layers import Linear, rope_cache
+from .layers import FUSE_MAX_ROWS, Linear, NormAct, SiluAct, rope_cache
 from .weights import RandomWeights, cat_rows, pad_rows, slice_cols, slice_rows
 
 
 # ---------------------------------------------------------------------------------------------
 # per-step metadata
 # ---------------------------------------------------------------------------------------------
+_FUSE_PRODUCERS = os.environ.get("RADIANCE_FUSE_PRODUCERS", "0") == "1"   # measured slower at M = 1
+
 @dataclass
 class StepMeta:
     """Device tensors describing one forward step (built by the model runner)."""
@@ -260,6 +264,8 @@ class MLP:
         gu = self.gate_up(x)
         if self.quant == "bf16":
             return self.down(K.silu_mul(gu))
+        if self.quant == "mxfp4" and gu.is_cuda and gu.shape[0] <= FUSE_MAX_ROWS and _FUSE_PRODUCERS:
+            return self.down(SiluAct(gu))       # SiLU * mul + e4m3 inside the down GEMM
         return self.down(K.silu_mul_quant(gu))
 
 
@@ -415,11 +421,18 @@ class HybridModel:
         ai = gi = 0
         quant = self.quant != "bf16"
         fused_ar = self.tp.size > 1 and quant and self.tp.all_reduce_add_rms_quant is not None
+        # decode-sized steps: residual add + RMSNorm + e4m3 run inside the next GEMM
+        fuse_prod = (self.quant == "mxfp4" and input_ids.is_cuda and _FUSE_PRODUCERS
+                     and input_ids.shape[0] <= FUSE_MAX_ROWS)
         pending = None          # (q, s) produced by a fused all-reduce epilogue for the next norm
         for li, layer in enumerate(self.layers):
             if pending is not None:
                 a_in = pending
                 pending = None
+            elif fuse_prod:
+                res_new = torch.empty_like(h)
+                a_in = NormAct(h, residual, layer.ln1, eps, res_new)
+                residual = res_new
             elif quant:
                 a_in = K.add_rms_quant(h, residual, layer.ln1, eps)
                 residual = a_in[2]
@@ -437,7 +450,11 @@ class HybridModel:
                 h = layer.mlp.forward((q, s))
             else:
                 h = self._reduce(h)
-                if quant:
+                if fuse_prod and isinstance(layer.mlp, MLP):
+                    res_new = torch.empty_like(h)
+                    h = layer.mlp.forward(NormAct(h, residual, layer.ln2, eps, res_new))
+                    residual = res_new
+                elif quant:
                     q, s, residual = K.add_rms_quant(h, residual, layer.ln2, eps)
                     h = layer.mlp.forward((q, s))
                 else:

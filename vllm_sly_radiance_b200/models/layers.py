@@ -13,7 +13,28 @@ import torch
 from ..ops import kernels as K
 from ..quant.mxfp4 import MXFP4Weight
 
-Act = Union[torch.Tensor, tuple]
+Act = Union[torch.Tensor, tuple, "NormAct", "SiluAct"]
+
+
+class NormAct:
+    """Activation given as its producer: residual add + RMSNorm(1 + w) of `h` (+ `res`), quantised
+    to e4m3 inside the decode GEMM.  `res_out` receives the new residual stream."""
+    __slots__ = ("h", "res", "w", "eps", "res_out")
+
+    def __init__(self, h, res, w, eps, res_out):
+        self.h, self.res, self.w, self.eps, self.res_out = h, res, w, eps, res_out
+
+
+class SiluAct:
+    """Activation given as its producer: SiLU(g) * u of `gu` = [g | u], quantised in the GEMM."""
+    __slots__ = ("gu",)
+
+    def __init__(self, gu):
+        self.gu = gu
+
+
+FUSE_MAX_ROWS = 1          # fused producers: single-row decode (the rows are held in registers)
+FUSE_MAX_K = 9216
 
 
 def rope_cache(max_pos: int, rotary_dim: int, theta: float, device) -> torch.Tensor:
@@ -58,6 +79,31 @@ class Linear:
                 self.w_scale = self.w_scale.to(device)
         return self
 
+    def _fused(self, x, out):
+        """The decode GEMM with its producer inside (one launch instead of two)."""
+        if isinstance(x, NormAct):
+            M = x.h.shape[0]
+            ok = (self.quant == "mxfp4" and x.h.is_cuda and M <= FUSE_MAX_ROWS and self.push is None
+                  and self.K <= FUSE_MAX_K)
+            if not ok:
+                q, s_, r = K.add_rms_quant(x.h, x.res, x.w, x.eps)
+                x.res_out.copy_(r)
+                return self((q, s_), out)
+            if out is None:
+                out = torch.empty(M, self.N, dtype=torch.bfloat16, device=x.h.device)
+            K.mxfp4_gemm_act(1, x.h, x.res, x.w, x.res_out, x.eps, self.w, out)
+            return out
+        M = x.gu.shape[0]
+        ok = (self.quant == "mxfp4" and x.gu.is_cuda and M <= FUSE_MAX_ROWS and self.push is None
+              and self.K <= FUSE_MAX_K)
+        if not ok:
+            act = K.silu_mul_quant(x.gu) if self.quant != "bf16" else K.silu_mul(x.gu)
+            return self(act, out)
+        if out is None:
+            out = torch.empty(M, self.N, dtype=torch.bfloat16, device=x.gu.device)
+        K.mxfp4_gemm_act(2, x.gu, None, None, None, 0.0, self.w, out)
+        return out
+
     @property
     def nbytes(self) -> int:
         if self.quant == "mxfp4":
@@ -69,6 +115,8 @@ class Linear:
     push = None
 
     def __call__(self, x: Act, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if isinstance(x, (NormAct, SiluAct)):
+            return self._fused(x, out)
         if self.quant == "mxfp4":
             if isinstance(x, tuple):
                 q, s = x

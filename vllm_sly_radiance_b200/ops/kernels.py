@@ -191,6 +191,16 @@ def mxfp4_gemm(q: torch.Tensor, scale: torch.Tensor, packed: torch.Tensor, sf: t
     return out
 
 
+def mxfp4_gemm_act(mode: int, x, res, w_norm, res_out, eps: float, w, out):
+    """Decode GEMM with the producer fused in (CUDA only): mode 1 = add + RMSNorm + e4m3 of
+    x (+ res), new residual -> res_out; mode 2 = SiLU(g) * u + e4m3 of x = [g | u]."""
+    e = _empty(x.device)
+    ext().mxfp4_gemm_act(mode, x, res if res is not None else e,
+                         w_norm if w_norm is not None else e, res_out if res_out is not None else e,
+                         eps, w.packed, w.sf, out, status_word(x.device))
+    return out
+
+
 def moe_work_items(counts: torch.Tensor, bn: int, max_items: int) -> torch.Tensor:
     """(expert, first row, rows) per row tile of the expert-sorted buffer, padded with empty
     items to a fixed length (device ops only: no host sync, CUDA-graph safe)."""
