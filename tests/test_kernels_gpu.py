@@ -283,6 +283,42 @@ def test_gdn_chunked_matches_recurrent(lens, has_init, sdt, split, monkeypatch):
         assert rel_err(o_got, serial[s0:s1].float().cpu().view(-1, Hv, D)) < 3e-2, bi
 
 
+@pytest.mark.parametrize("B,Hk,Hv,sdt,init", [(1, 4, 12, torch.float32, 1), (5, 2, 6, torch.float32, 1),
+                                              (3, 4, 4, torch.bfloat16, 1), (2, 2, 6, torch.float32, 0)])
+def test_gdn_decode_fused_matches_separate(B, Hk, Hv, sdt, init):
+    """One-launch GDN decode step against conv (+ in-place state shift) followed by the
+    token-serial recurrence: outputs, SSM states and conv states."""
+    torch.manual_seed(11)
+    D = 128
+    key_dim, vdim = Hk * D, Hv * D
+    C = 2 * key_dim + vdim
+    ncol = C + vdim + 2 * Hv + 8
+    x = (torch.randn(B, ncol) * 0.7).to(torch.bfloat16).to(DEV)
+    conv_w = (0.4 * torch.randn(C, 4)).to(torch.bfloat16).to(DEV)
+    conv0 = (0.5 * torch.randn(B + 1, C, 3)).to(torch.bfloat16).to(DEV)
+    ssm0 = (torch.randn(B + 1, Hv, D, D) * 0.05).to(sdt).to(DEV)
+    A_log = torch.log(torch.rand(Hv) * 8 + 0.5).to(DEV)
+    dt_bias = (torch.randn(Hv) * 0.3).to(DEV)
+    meta = _Meta()
+    meta.query_start_loc = torch.arange(B + 1, dtype=torch.int32, device=DEV)
+    meta.state_slots = torch.arange(1, B + 1, dtype=torch.int32, device=DEV)
+    meta.has_initial = torch.full((B,), init, dtype=torch.int32, device=DEV)
+    meta.token_seq = torch.arange(B, dtype=torch.int32, device=DEV)
+    meta.num_seqs = meta.num_tokens = B
+    meta.commit_len = None
+    scale = D ** -0.5
+    ba_off = C + vdim
+    c1, s1 = conv0.clone(), ssm0.clone()
+    got = K.gdn_decode_fused(x, ba_off, conv_w, c1, s1, A_log, dt_bias, meta, Hk, scale)
+    c2, s2 = conv0.clone(), ssm0.clone()
+    y = K.gdn_conv(x[:, :C], conv_w, c2, meta, key_dim, D, update_state=True)
+    want = K.gdn_recurrent(y, x[:, ba_off:ba_off + 2 * Hv], A_log, dt_bias, s2, meta, Hk, scale)
+    torch.cuda.synchronize()
+    assert rel_err(got, want) < 1e-2, rel_err(got, want)
+    assert rel_err(s1.float(), s2.float()) < 1e-2
+    assert torch.equal(c1, c2)
+
+
 def test_qkv_prologue():
     torch.manual_seed(1)
     T, Hq, Hkv, D, rot = 5, 4, 2, 256, 64

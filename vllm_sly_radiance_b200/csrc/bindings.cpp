@@ -27,6 +27,10 @@ void gdn_recurrent(torch::Tensor y, torch::Tensor ba, torch::Tensor A_log, torch
                    torch::Tensor state, torch::Tensor qsl, torch::Tensor slots,
                    torch::Tensor has_init, torch::Tensor commit_len, int64_t Hk, double scale,
                    torch::Tensor out, bool write_out);
+void gdn_decode_fused(torch::Tensor x, int64_t ba_off, torch::Tensor conv_w,
+                      torch::Tensor conv_state, torch::Tensor A_log, torch::Tensor dt_bias,
+                      torch::Tensor state, torch::Tensor slots, torch::Tensor has_init, int64_t Hk,
+                      double scale, double eps, torch::Tensor out);
 void gdn_chunked(torch::Tensor y, torch::Tensor ba, torch::Tensor A_log, torch::Tensor dt_bias,
                  torch::Tensor state, torch::Tensor qsl, torch::Tensor slots,
                  torch::Tensor has_init, int64_t Hk, double scale, torch::Tensor out,
@@ -84,6 +88,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qkv_prologue", &rad::qkv_prologue, "QK RMSNorm + RoPE + paged KV write");
   m.def("paged_attention", &rad::paged_attention, "varlen paged attention (split-KV)");
   m.def("gdn_chunked", &rad::gdn_chunked, "chunked (64-token) gated delta rule for prefill");
+  m.def("gdn_decode_fused", &rad::gdn_decode_fused,
+        "one-token GDN step: conv update + SiLU + q/k L2 norm + gates + delta rule");
   m.def("mxfp4_gemm_push", &rad::mxfp4_gemm_push,
         "row-parallel W4A8 GEMM that pushes its tiles into every peer's receive buffer");
   m.def("push_buffer_bytes", &rad::push_buffer_bytes, "size of a GEMM-push receive buffer");

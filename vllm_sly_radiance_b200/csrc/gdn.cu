@@ -235,6 +235,157 @@ __global__ void __launch_bounds__(128) recurrent_kernel(
   }
 }
 
+
+// ------------------------------------------------------------------------------------------------
+// fused decode step (one token per sequence): conv update + SiLU + q/k L2 norm + gates + delta
+// rule in one launch (the reference's gdn_fused_update / radiance_gdn_decode.hip:140 step).
+// grid (B, Hv), 256 threads; the rep = Hv / Hk value heads that share one q/k head form a thread
+// block cluster: each computes the shared q/k conv itself, and after a cluster barrier (every
+// CTA has read the old q/k conv state) only cluster rank 0 writes the shifted q/k state.  A
+// thread pair owns one row of the [dv, dk] state (64 columns each): one shuffle per reduction.
+// ------------------------------------------------------------------------------------------------
+template <int D, typename ST>
+__global__ void __launch_bounds__(2 * D) decode_fused_kernel(
+    const __nv_bfloat16* __restrict__ x, int ldx,        // in_proj output [B, *]: q|k|v|z|b|a
+    const __nv_bfloat16* __restrict__ conv_w,            // [C, 4]
+    __nv_bfloat16* __restrict__ conv_state,              // [S, C, 3]
+    int ba_off,                                          // column of b (a at ba_off + Hv)
+    const float* __restrict__ A_log, const float* __restrict__ dt_bias,
+    ST* __restrict__ state,                              // [S, Hv, D, D]
+    const int* __restrict__ slots, const int* __restrict__ has_init, int Hk, int Hv, int C,
+    float scale, float eps, __nv_bfloat16* __restrict__ out, int ldo) {
+  pdl_wait();     // inputs come from the preceding kernel
+  pdl_trigger();
+  constexpr int W = 4;
+  constexpr int HC = D / 2;             // state columns per thread
+  __shared__ float sq[D], sk[D], sv[D], sred[2][D / 32];
+  const int b = blockIdx.x, h = blockIdx.y;
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  const int rep = Hv / Hk, hk = h / rep;
+  const int key_dim = Hk * D;
+  const int slot = slots[b];
+  const bool init = has_init[b] != 0;
+  const __nv_bfloat16* xr = x + (size_t)b * ldx;
+  // ---- conv (threads 0..D-1, one channel of q, k and v each) + SiLU + q/k L2 norm ----
+  float in_q[W], in_k[W], in_v[W];
+  __nv_bfloat16 *stq = nullptr, *stk = nullptr, *stv = nullptr;
+  if (t < D) {
+    const int cq = hk * D + t, ck = key_dim + hk * D + t, cv = 2 * key_dim + h * D + t;
+    stq = conv_state + ((size_t)slot * C + cq) * (W - 1);
+    stk = conv_state + ((size_t)slot * C + ck) * (W - 1);
+    stv = conv_state + ((size_t)slot * C + cv) * (W - 1);
+#pragma unroll
+    for (int j = 0; j < W - 1; ++j) {
+      in_q[j] = init ? __bfloat162float(stq[j]) : 0.f;
+      in_k[j] = init ? __bfloat162float(stk[j]) : 0.f;
+      in_v[j] = init ? __bfloat162float(stv[j]) : 0.f;
+    }
+    in_q[W - 1] = __bfloat162float(xr[cq]);
+    in_k[W - 1] = __bfloat162float(xr[ck]);
+    in_v[W - 1] = __bfloat162float(xr[cv]);
+    float aq = 0.f, ak = 0.f, av = 0.f;
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+      aq += in_q[j] * __bfloat162float(conv_w[(size_t)cq * W + j]);
+      ak += in_k[j] * __bfloat162float(conv_w[(size_t)ck * W + j]);
+      av += in_v[j] * __bfloat162float(conv_w[(size_t)cv * W + j]);
+    }
+    aq = aq / (1.f + __expf(-aq));
+    ak = ak / (1.f + __expf(-ak));
+    av = av / (1.f + __expf(-av));
+    const float s2q = warp_sum(aq * aq), s2k = warp_sum(ak * ak);
+    if (lane == 0) { sred[0][warp] = s2q; sred[1][warp] = s2k; }
+    sq[t] = aq;
+    sk[t] = ak;
+    sv[t] = bf16_round(av);             // the conv kernel's bf16 output rounding
+  }
+  __syncthreads();
+  if (t < D) {
+    float s2q = 0.f, s2k = 0.f;
+#pragma unroll
+    for (int w = 0; w < D / 32; ++w) { s2q += sred[0][w]; s2k += sred[1][w]; }
+    sq[t] = bf16_round(sq[t] * rsqrtf(s2q + eps));
+    sk[t] = bf16_round(sk[t] * rsqrtf(s2k + eps));
+    // shift the conv state: v channels belong to this CTA
+#pragma unroll
+    for (int j = 0; j < W - 1; ++j) stv[j] = __float2bfloat16_rn(in_v[j + 1]);
+  }
+  // q/k state: cluster rank 0, after every CTA of the cluster has read the old q/k state
+  cluster_sync();
+  if (t < D && cluster_ctarank() == 0) {
+#pragma unroll
+    for (int j = 0; j < W - 1; ++j) {
+      stq[j] = __float2bfloat16_rn(in_q[j + 1]);
+      stk[j] = __float2bfloat16_rn(in_k[j + 1]);
+    }
+  }
+  // ---- gates ----
+  const float bb = __bfloat162float(xr[ba_off + h]);
+  const float aa = __bfloat162float(xr[ba_off + Hv + h]);
+  const float xs = aa + dt_bias[h];
+  const float sp = xs > 20.f ? xs : log1pf(__expf(xs));
+  const float decay = __expf(-__expf(A_log[h]) * sp);
+  const float beta = 1.f / (1.f + __expf(-bb));
+  // ---- delta rule: thread pair (2r, 2r + 1) owns row r of S, half the columns each ----
+  const int r = t >> 1, c0 = (t & 1) * HC;
+  ST* srow = state + (((size_t)slot * Hv + h) * D + r) * D + c0;
+  float S[HC];
+  if (init) {
+    if constexpr (sizeof(ST) == 4) {
+#pragma unroll
+      for (int c = 0; c < HC; c += 4) {
+        const float4 f = *reinterpret_cast<const float4*>(srow + c);
+        S[c] = f.x; S[c + 1] = f.y; S[c + 2] = f.z; S[c + 3] = f.w;
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < HC; c += 8) {
+        const uint4 u = *reinterpret_cast<const uint4*>(srow + c);
+        const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(hh[e]);
+          S[c + 2 * e] = f.x;
+          S[c + 2 * e + 1] = f.y;
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < HC; ++c) S[c] = 0.f;
+  }
+  float kv = 0.f;
+#pragma unroll
+  for (int c = 0; c < HC; ++c) {
+    S[c] *= decay;
+    kv += S[c] * sk[c0 + c];
+  }
+  kv += __shfl_xor_sync(0xffffffffu, kv, 1);
+  const float dlt = beta * (sv[r] - kv);
+  float o = 0.f;
+#pragma unroll
+  for (int c = 0; c < HC; ++c) {
+    S[c] += dlt * sk[c0 + c];
+    o += S[c] * sq[c0 + c];
+  }
+  o += __shfl_xor_sync(0xffffffffu, o, 1);
+  if ((t & 1) == 0) out[(size_t)b * ldo + h * D + r] = __float2bfloat16_rn(o * scale);
+  if constexpr (sizeof(ST) == 4) {
+#pragma unroll
+    for (int c = 0; c < HC; c += 4)
+      *reinterpret_cast<float4*>(srow + c) = make_float4(S[c], S[c + 1], S[c + 2], S[c + 3]);
+  } else {
+#pragma unroll
+    for (int c = 0; c < HC; c += 8) {
+      uint4 u;
+      __nv_bfloat162* hh = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) hh[e] = __floats2bfloat162_rn(S[c + 2 * e], S[c + 2 * e + 1]);
+      *reinterpret_cast<uint4*>(srow + c) = u;
+    }
+  }
+}
+
 }  // namespace gdn
 
 static inline const int* iptr(const torch::Tensor& t) {
@@ -318,6 +469,53 @@ C10_CUDA_CHECK(launch_pdl((gdn::recurrent_kernel<DKc, ST>), dim3(grid), dim3(128
   } else {
     TORCH_CHECK(false, "gdn_recurrent: dk 64 or 128");
   }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+
+// One-token-per-sequence GDN step fused into one launch (see decode_fused_kernel).  x = in_proj
+// output rows, ba_off = column of the b gates; out = [B, Hv * dv] bf16.
+void gdn_decode_fused(torch::Tensor x, int64_t ba_off, torch::Tensor conv_w,
+                      torch::Tensor conv_state, torch::Tensor A_log, torch::Tensor dt_bias,
+                      torch::Tensor state, torch::Tensor slots, torch::Tensor has_init, int64_t Hk,
+                      double scale, double eps, torch::Tensor out) {
+  const int B = slots.size(0);
+  if (B == 0) return;
+  const int Hv = state.size(1), DV = state.size(2), DK = state.size(3);
+  const int C = conv_w.size(0);
+  TORCH_CHECK(DV == 128 && DK == 128, "gdn_decode_fused: dk = dv = 128");
+  TORCH_CHECK(conv_w.size(1) == 4 && conv_state.size(2) == 3, "gdn_decode_fused: conv width 4");
+  TORCH_CHECK(Hv % Hk == 0 && Hv / Hk <= 8, "gdn_decode_fused: value heads per key head <= 8");
+  TORCH_CHECK(x.size(0) >= B && x.stride(1) == 1, "gdn_decode_fused: one row per sequence");
+  const at::cuda::CUDAGuard guard(x.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto run = [&](auto stag) {
+    using ST = typename decltype(stag)::type;
+    auto kern = gdn::decode_fused_kernel<128, ST>;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(B, Hv);
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attrs[2];
+    attrs[0].id = cudaLaunchAttributeClusterDimension;
+    attrs[0].val.clusterDim.x = 1;
+    attrs[0].val.clusterDim.y = Hv / Hk;
+    attrs[0].val.clusterDim.z = 1;
+    attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attrs;
+    cfg.numAttrs = pdl_enabled() ? 2 : 1;
+    C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, (const __nv_bfloat16*)x.data_ptr(),
+        (int)x.stride(0), (const __nv_bfloat16*)conv_w.data_ptr(),
+        (__nv_bfloat16*)conv_state.data_ptr(), (int)ba_off, A_log.data_ptr<float>(),
+        dt_bias.data_ptr<float>(), (ST*)state.data_ptr(), slots.data_ptr<int>(),
+        has_init.data_ptr<int>(), (int)Hk, Hv, C, (float)scale, (float)eps,
+        (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0)));
+  };
+  struct F32 { using type = float; };
+  struct BF16 { using type = __nv_bfloat16; };
+  if (state.scalar_type() == at::kFloat) run(F32{});
+  else run(BF16{});
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

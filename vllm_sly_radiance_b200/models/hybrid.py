@@ -167,14 +167,20 @@ class GDNMixer:
         z = proj[:, cd:cd + vd]
         ba = proj[:, cd + vd:cd + vd + 2 * self.Hv]
         fused_state = meta.commit_len is None and meta.num_tokens == meta.num_seqs
-        y = K.gdn_conv(xc, self.conv_w, conv_state, meta, self.key_dim, self.dk,
-                       update_state=fused_state)
-        if not fused_state:
-            K.gdn_conv_state_update(xc, conv_state, meta, meta.commit_len)
-        o = K.gdn_recurrent(y, ba, self.A_log, self.dt_bias, ssm_state, meta, self.Hk, self.scale,
-                            commit_len=meta.commit_len)
-        if save is not None:        # speculative verify: keep inputs for the commit pass
-            save.append((proj, y))
+        if (fused_state and save is None and proj.is_cuda and K._GDN_DECODE_FUSED
+                and self.dk == 128 and self.dv == 128 and conv_state.shape[2] == 3):
+            # decode: the whole GDN step (conv, norms, gates, delta rule) in one launch
+            o = K.gdn_decode_fused(proj, cd + vd, self.conv_w, conv_state, ssm_state, self.A_log,
+                                   self.dt_bias, meta, self.Hk, self.scale)
+        else:
+            y = K.gdn_conv(xc, self.conv_w, conv_state, meta, self.key_dim, self.dk,
+                           update_state=fused_state)
+            if not fused_state:
+                K.gdn_conv_state_update(xc, conv_state, meta, meta.commit_len)
+            o = K.gdn_recurrent(y, ba, self.A_log, self.dt_bias, ssm_state, meta, self.Hk,
+                                self.scale, commit_len=meta.commit_len)
+            if save is not None:    # speculative verify: keep inputs for the commit pass
+                save.append((proj, y))
         if self.quant == "bf16":
             h = self.out_proj(K.gdn_gated_norm(o, z, self.norm_w, cfg.rms_norm_eps, self.dv))
         else:

@@ -343,8 +343,21 @@ def gdn_conv_state_update(x, conv_state, meta, commit_len: Optional[torch.Tensor
                                 meta.has_initial, _none(commit_len, x.device))
 
 
+def gdn_decode_fused(proj, ba_off: int, conv_w, conv_state, ssm_state, A_log, dt_bias, meta,
+                     num_k_heads: int, scale: float, eps: float = 1e-6) -> torch.Tensor:
+    """One token per sequence (CUDA): conv update + SiLU + q/k L2 norm + gates + delta rule in
+    one launch.  proj = in_proj output rows; returns o [B, Hv * dv] bf16; states updated."""
+    B = meta.num_seqs
+    _, Hv, DV, _ = ssm_state.shape
+    out = torch.empty(B, Hv * DV, dtype=torch.bfloat16, device=proj.device)
+    ext().gdn_decode_fused(proj, ba_off, conv_w, conv_state, A_log, dt_bias, ssm_state,
+                           meta.state_slots, meta.has_initial, num_k_heads, scale, eps, out)
+    return out
+
+
 _GDN_CHUNKED = os.environ.get("RADIANCE_GDN_CHUNKED", "1") != "0"
 _GDN_CHUNK_SPLIT = int(os.environ.get("RADIANCE_GDN_CHUNK_SPLIT", "0"))   # 0: by batch size
+_GDN_DECODE_FUSED = os.environ.get("RADIANCE_GDN_DECODE_FUSED", "1") != "0"
 
 
 def gdn_recurrent(y, ba, A_log, dt_bias, ssm_state, meta, num_k_heads: int, scale: float,
