@@ -57,6 +57,15 @@ void push_allreduce_recv(std::vector<int64_t> peers, int64_t rank, int64_t M, in
                          int64_t half_words, torch::Tensor out, torch::Tensor residual,
                          torch::Tensor weight, double eps, torch::Tensor res_out, torch::Tensor q,
                          torch::Tensor scale, int64_t num_blocks, torch::Tensor status);
+void rejection_sample_cuda(torch::Tensor draft, torch::Tensor t_ids, torch::Tensor t_probs,
+                           torch::Tensor d_ids, torch::Tensor d_probs, torch::Tensor greedy,
+                           torch::Tensor seq_lens, torch::Tensor forced, torch::Tensor seeds,
+                           int64_t kind, double delta, int64_t fade_start, int64_t fade_end,
+                           double cap_r, double escape, double theta, torch::Tensor out,
+                           torch::Tensor n_acc);
+void lookup_draft_cuda(torch::Tensor hist, torch::Tensor rows, torch::Tensor len, int64_t k,
+                       int64_t max_ngram, int64_t min_ngram, torch::Tensor out,
+                       torch::Tensor n_out);
 void argmax_rows(torch::Tensor x, torch::Tensor out_ids, torch::Tensor out_vals,
                  torch::Tensor workspace);
 void sample_from_topk(torch::Tensor vals, torch::Tensor ids, torch::Tensor temperature,
@@ -87,6 +96,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_recurrent", &rad::gdn_recurrent, "GDN varlen recurrent delta rule");
   m.def("qkv_prologue", &rad::qkv_prologue, "QK RMSNorm + RoPE + paged KV write");
   m.def("paged_attention", &rad::paged_attention, "varlen paged attention (split-KV)");
+  m.def("rejection_sample", &rad::rejection_sample_cuda,
+        "speculative acceptance (Leviathan / Cactus / NSD / greedy / forced), one warp per request");
+  m.def("lookup_draft", &rad::lookup_draft_cuda, "prompt-lookup drafts: longest suffix match");
   m.def("gdn_chunked", &rad::gdn_chunked, "chunked (64-token) gated delta rule for prefill");
   m.def("gdn_decode_fused", &rad::gdn_decode_fused,
         "one-token GDN step: conv update + SiLU + q/k L2 norm + gates + delta rule");

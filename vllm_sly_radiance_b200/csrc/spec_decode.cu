@@ -1,0 +1,264 @@
+// Speculative-decoding kernels: rejection sampling with the reference's acceptance rules, and
+// the prompt-lookup draft scan.
+//
+// Reference behaviour: vLLM's rejection sampler with sly/patch_cactus.py and sly/patch_nsd.py
+// (README.md:452-578), and the lookup drafter sly/radiance_lookup_draft.py:101,129.
+//
+//  * rejection_kernel: one warp per request walks its k drafts in order.  Target distributions
+//    arrive as the sampler's top-W windows (ids + probs, sorted descending, W <= 64: two entries
+//    per lane), draft distributions as candidate windows (or a point mass on the drafted token).
+//      stock (Leviathan): accept d with probability min(1, p(d) / q(d))
+//      Cactus: h = clamp(p + sqrt(2 delta_eff p (1 - p)), 0, 1), capped at 1 - r (1 - p);
+//              escape mixture eps runs the stock test instead (same uniform)
+//      NSD: stock OR target mass strictly above p(d) <= theta
+//      greedy rows: accept iff d == argmax p; on the first mismatch emit argmax p
+//    On rejection a token is drawn from norm(max(0, p - q)) (p itself if that is empty); after
+//    k acceptances a bonus token is drawn from p_k.  Uniforms come from a Philox stream keyed by
+//    the row seed, so a seeded request reproduces its draws.
+//  * lookup_kernel: one CTA per request finds the most recent earlier occurrence of the longest
+//    suffix (max_ngram .. min_ngram tokens) in the request's token history and proposes the k
+//    tokens that followed it.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <curand_kernel.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace rad {
+namespace spec {
+
+constexpr int kWin = 64;      // max window entries (2 per lane)
+
+struct Rule {
+  int kind;                   // 0 leviathan, 1 cactus, 2 nsd
+  float delta;
+  int fade_start, fade_end;
+  float cap_r, escape, theta;
+};
+
+// window entry j of lane: j = lane and lane + 32
+DEVI float win_lookup(const int64_t* ids, const float* pr, int W, int64_t tok, int lane) {
+  float v = 0.f;
+  if (lane < W && ids[lane] == tok) v += pr[lane];
+  if (lane + 32 < W && ids[lane + 32] == tok) v += pr[lane + 32];
+  return warp_sum(v);
+}
+
+// inverse-CDF draw over (unnormalised) weights w0 (entry lane), w1 (entry lane + 32)
+DEVI int64_t win_sample(const int64_t* ids, int W, float w0, float w1, float u, int lane) {
+  const float z = warp_sum(w0 + w1);
+  if (!(z > 0.f)) return ids[0];
+  const float target = fminf(u, 1.f - 1e-7f) * z;
+  // inclusive scan of w0 over lanes, then of w1 over lanes (entries 32..63 follow 0..31)
+  float c0 = w0;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float t = __shfl_up_sync(0xffffffffu, c0, o);
+    if (lane >= o) c0 += t;
+  }
+  const float tot0 = __shfl_sync(0xffffffffu, c0, 31);
+  float c1 = w1;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float t = __shfl_up_sync(0xffffffffu, c1, o);
+    if (lane >= o) c1 += t;
+  }
+  c1 += tot0;
+  // first entry whose cumulative weight exceeds the target (entries with zero weight skipped)
+  const unsigned m0 = __ballot_sync(0xffffffffu, lane < W && w0 > 0.f && c0 > target);
+  if (m0) return ids[__ffs(m0) - 1];
+  const unsigned m1 = __ballot_sync(0xffffffffu, lane + 32 < W && w1 > 0.f && c1 > target);
+  if (m1) return ids[32 + __ffs(m1) - 1];
+  // rounding: the last entry with weight
+  const unsigned l0 = __ballot_sync(0xffffffffu, lane < W && w0 > 0.f);
+  const unsigned l1 = __ballot_sync(0xffffffffu, lane + 32 < W && w1 > 0.f);
+  if (l1) return ids[32 + 31 - __clz(l1)];
+  return ids[31 - __clz(l0)];
+}
+
+__global__ void rejection_kernel(const int64_t* __restrict__ draft, int k,
+                                 const int64_t* __restrict__ t_ids, const float* __restrict__ t_pr,
+                                 int W, const int64_t* __restrict__ d_ids,
+                                 const float* __restrict__ d_pr, int Kd,
+                                 const bool* __restrict__ greedy,
+                                 const int64_t* __restrict__ seq_lens,
+                                 const int64_t* __restrict__ forced,
+                                 const int64_t* __restrict__ seeds, Rule rule, int B,
+                                 int64_t* __restrict__ out, int64_t* __restrict__ n_acc) {
+  pdl_wait();     // windows come from the preceding kernels
+  pdl_trigger();
+  const int b = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (b >= B) return;
+  curandStatePhilox4_32_10_t rng;
+  curand_init((unsigned long long)seeds[b], 0ull, 0ull, &rng);
+  const bool g = greedy[b];
+  float dlt = rule.delta;
+  if (rule.kind == 1 && rule.fade_end != 0) {
+    const float sl = (float)seq_lens[b];
+    if (rule.fade_end <= rule.fade_start) dlt = sl >= rule.fade_start ? 0.f : dlt;
+    else dlt *= fminf(fmaxf((rule.fade_end - sl) / (float)(rule.fade_end - rule.fade_start), 0.f), 1.f);
+  }
+  int64_t* orow = out + (size_t)b * (k + 1);
+  for (int i = lane; i < k + 1; i += 32) orow[i] = -1;
+  __syncwarp();
+  int acc_n = 0;
+  for (int i = 0; i <= k; ++i) {
+    const int64_t* ids = t_ids + ((size_t)b * (k + 1) + i) * W;
+    const float* pr = t_pr + ((size_t)b * (k + 1) + i) * W;
+    // one draw of four uniforms per position (same in every lane: identical Philox state)
+    const float4 u4 = curand_uniform4(&rng);
+    const float u_acc = u4.x, u_res = u4.y, u_esc = u4.z;
+    const float p0 = lane < W ? pr[lane] : 0.f;
+    const float p1 = lane + 32 < W ? pr[lane + 32] : 0.f;
+    if (i == k) {                                   // bonus token
+      const int64_t tok = g ? ids[0] : win_sample(ids, W, p0, p1, u_res, lane);
+      if (lane == 0) orow[i] = tok;
+      break;
+    }
+    const int64_t d = draft[(size_t)b * k + i];
+    bool acc;
+    if (forced) {
+      acc = i < forced[b];
+    } else if (g) {
+      acc = d == ids[0];
+    } else {
+      const float pt = win_lookup(ids, pr, W, d, lane);
+      float qd = 1.f;
+      if (d_ids) {
+        const int64_t* di = d_ids + ((size_t)b * k + i) * Kd;
+        const float* dp = d_pr + ((size_t)b * k + i) * Kd;
+        qd = win_lookup(di, dp, Kd, d, lane);
+      }
+      qd = fmaxf(qd, 1e-20f);
+      const bool stock = u_acc < fminf(pt / qd, 1.f);
+      if (rule.kind == 1) {
+        float h = fminf(fmaxf(pt + sqrtf(fmaxf(2.f * dlt * pt * (1.f - pt), 0.f)), 0.f), 1.f);
+        if (rule.cap_r > 0.f) h = fminf(h, 1.f - rule.cap_r * (1.f - pt));
+        const bool cac = u_acc < fminf(h / qd, 1.f);
+        acc = (rule.escape > 0.f && u_esc < rule.escape) ? stock : cac;
+      } else if (rule.kind == 2) {
+        const float higher = warp_sum((p0 > pt ? p0 : 0.f) + (p1 > pt ? p1 : 0.f));
+        acc = stock || (pt > 0.f && higher <= rule.theta);
+      } else {
+        acc = stock;
+      }
+    }
+    if (acc) {
+      if (lane == 0) orow[i] = d;
+      ++acc_n;
+      continue;
+    }
+    int64_t tok;
+    if (g || forced) {
+      tok = ids[0];
+    } else {
+      // residual max(0, p - q) over the target window
+      float q0 = 0.f, q1 = 0.f;
+      if (d_ids) {
+        const int64_t* di = d_ids + ((size_t)b * k + i) * Kd;
+        const float* dp = d_pr + ((size_t)b * k + i) * Kd;
+        for (int j = 0; j < Kd; ++j) {
+          const int64_t dj = di[j];
+          if (lane < W && ids[lane] == dj) q0 += dp[j];
+          if (lane + 32 < W && ids[lane + 32] == dj) q1 += dp[j];
+        }
+      } else {
+        q0 = (lane < W && ids[lane] == d) ? 1.f : 0.f;
+        q1 = (lane + 32 < W && ids[lane + 32] == d) ? 1.f : 0.f;
+      }
+      float r0 = fmaxf(p0 - q0, 0.f), r1 = fmaxf(p1 - q1, 0.f);
+      if (!(warp_sum(r0 + r1) > 0.f)) { r0 = p0; r1 = p1; }
+      tok = win_sample(ids, W, r0, r1, u_res, lane);
+    }
+    if (lane == 0) orow[i] = tok;
+    break;
+  }
+  if (lane == 0) n_acc[b] = acc_n;
+}
+
+// hist [rows, Lmax] int32 token histories; request b uses row rows[b] of length len[b]; proposes
+// up to k tokens per request into out [B, k] (-1 padded) and the count into n_out [B].
+__global__ void __launch_bounds__(256) lookup_kernel(const int* __restrict__ hist, int Lmax,
+                                                     const int* __restrict__ rows,
+                                                     const int* __restrict__ len, int k,
+                                                     int max_ngram, int min_ngram,
+                                                     int* __restrict__ out, int* __restrict__ n_out) {
+  const int b = blockIdx.x;
+  const int L = len[b];
+  const int* h = hist + (size_t)rows[b] * Lmax;
+  __shared__ int s_best;
+  for (int i = threadIdx.x; i < k; i += blockDim.x) out[(size_t)b * k + i] = -1;
+  int found = -1;
+  for (int n = min(max_ngram, L - 1); n >= min_ngram && found < 0; --n) {
+    // candidate end positions e (exclusive): h[e - n, e) == suffix, e + 1 <= L - 1 so at least
+    // one continuation token exists; keep the most recent (largest e)
+    if (threadIdx.x == 0) s_best = -1;
+    __syncthreads();
+    for (int e = L - 1 - threadIdx.x; e >= n; e -= blockDim.x) {
+      bool match = true;
+      for (int j = 1; j <= n && match; ++j) match = h[e - j] == h[L - j];
+      if (match) atomicMax(&s_best, e);
+    }
+    __syncthreads();
+    found = s_best;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    int cnt = 0;
+    if (found >= 0)
+      for (int i = 0; i < k && found + i < L; ++i) out[(size_t)b * k + cnt++] = h[found + i];
+    n_out[b] = cnt;
+  }
+}
+
+}  // namespace spec
+
+// draft [B,k] int64; t_ids/t_probs [B,k+1,W]; d_ids/d_probs [B,k,Kd] or empty (point mass);
+// greedy [B] bool; seq_lens [B] int64; forced [B] int64 or empty; seeds [B] int64.
+void rejection_sample_cuda(torch::Tensor draft, torch::Tensor t_ids, torch::Tensor t_probs,
+                           torch::Tensor d_ids, torch::Tensor d_probs, torch::Tensor greedy,
+                           torch::Tensor seq_lens, torch::Tensor forced, torch::Tensor seeds,
+                           int64_t kind, double delta, int64_t fade_start, int64_t fade_end,
+                           double cap_r, double escape, double theta, torch::Tensor out,
+                           torch::Tensor n_acc) {
+  const int B = draft.size(0), k = draft.size(1), W = t_ids.size(2);
+  if (B == 0) return;
+  TORCH_CHECK(W <= spec::kWin && t_ids.size(1) == k + 1, "rejection: target window <= 64");
+  const bool has_d = d_ids.defined() && d_ids.numel();
+  const int Kd = has_d ? d_ids.size(2) : 0;
+  TORCH_CHECK(!has_d || Kd <= spec::kWin, "rejection: draft window <= 64");
+  TORCH_CHECK(t_probs.scalar_type() == at::kFloat && greedy.scalar_type() == at::kBool, "dtypes");
+  const at::cuda::CUDAGuard guard(draft.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  spec::Rule rule{(int)kind, (float)delta, (int)fade_start, (int)fade_end, (float)cap_r,
+                  (float)escape, (float)theta};
+  const int warps = 4;
+  C10_CUDA_CHECK(launch_pdl(spec::rejection_kernel, dim3((B + warps - 1) / warps), dim3(32 * warps), 0,
+      stream, draft.data_ptr<int64_t>(), k, t_ids.data_ptr<int64_t>(), t_probs.data_ptr<float>(), W,
+      has_d ? d_ids.data_ptr<int64_t>() : (const int64_t*)nullptr,
+      has_d ? d_probs.data_ptr<float>() : (const float*)nullptr, Kd, greedy.data_ptr<bool>(),
+      seq_lens.data_ptr<int64_t>(),
+      forced.defined() && forced.numel() ? forced.data_ptr<int64_t>() : (const int64_t*)nullptr,
+      seeds.data_ptr<int64_t>(), rule, B, out.data_ptr<int64_t>(), n_acc.data_ptr<int64_t>()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void lookup_draft_cuda(torch::Tensor hist, torch::Tensor rows, torch::Tensor len, int64_t k,
+                       int64_t max_ngram, int64_t min_ngram, torch::Tensor out,
+                       torch::Tensor n_out) {
+  const int B = rows.size(0);
+  if (B == 0) return;
+  TORCH_CHECK(hist.scalar_type() == at::kInt && len.scalar_type() == at::kInt, "int32 histories");
+  const at::cuda::CUDAGuard guard(hist.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  spec::lookup_kernel<<<B, 256, 0, stream>>>(hist.data_ptr<int>(), (int)hist.size(1),
+                                             rows.data_ptr<int>(), len.data_ptr<int>(), (int)k,
+                                             (int)max_ngram,
+                                             (int)min_ngram, out.data_ptr<int>(),
+                                             n_out.data_ptr<int>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace rad

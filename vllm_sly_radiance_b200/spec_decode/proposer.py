@@ -38,12 +38,45 @@ from .rejection import AcceptRule, ForcedAcceptance, rejection_sample
 
 
 class LookupProposer:
-    """n-gram prompt lookup over each request's full token history."""
+    """n-gram prompt lookup over each request's full token history.  On CUDA the scan runs in
+    ``lookup_kernel`` (csrc/spec_decode.cu) over device-resident histories, one row per GDN state
+    slot; only the tokens added since the previous step are uploaded."""
 
-    def __init__(self, k: int, max_ngram: int = 24, min_ngram: int = 2):
+    def __init__(self, k: int, max_ngram: int = 24, min_ngram: int = 2, device=None,
+                 num_rows: int = 0, max_len: int = 0):
         self.k = k
         self.max_ngram = max_ngram
         self.min_ngram = min_ngram
+        self.dev = None
+        if device is not None and torch.device(device).type == "cuda" and num_rows and max_len:
+            self.dev = torch.device(device)
+            self.hist = torch.zeros(num_rows, max_len, dtype=torch.int32, device=self.dev)
+            self.row_owner: dict = {}          # row -> (request_id, tokens uploaded)
+
+    def propose_gpu(self, reqs_tokens: list) -> list[list[int]]:
+        """reqs_tokens: [(request, full token history)]; the request's state slot picks its row."""
+        from ..ops._ext import ext
+        rows, lens = [], []
+        for req, toks in reqs_tokens:
+            row = req.state_slot
+            owner = self.row_owner.get(row)
+            start = owner[1] if owner is not None and owner[0] == req.request_id else 0
+            n = min(len(toks), self.hist.shape[1])
+            if n > start:
+                self.hist[row, start:n].copy_(torch.tensor(toks[start:n], dtype=torch.int32),
+                                              non_blocking=False)
+            self.row_owner[row] = (req.request_id, n)
+            rows.append(row)
+            lens.append(n)
+        B = len(rows)
+        rows_t = torch.tensor(rows, dtype=torch.int32).to(self.dev)
+        lens_t = torch.tensor(lens, dtype=torch.int32).to(self.dev)
+        out = torch.empty(B, self.k, dtype=torch.int32, device=self.dev)
+        n_out = torch.empty(B, dtype=torch.int32, device=self.dev)
+        ext().lookup_draft(self.hist, rows_t, lens_t, self.k, self.max_ngram, self.min_ngram,
+                           out, n_out)
+        o, n = out.cpu().tolist(), n_out.cpu().tolist()
+        return [o[b][:n[b]] for b in range(B)]
 
     def propose_one(self, toks: list[int]) -> list[int]:
         n_tok = len(toks)
@@ -77,7 +110,9 @@ class SpecRunner:
         self.rule = rule
         self.forced = forced
         self.drafter = drafter
-        self.lookup = LookupProposer(k)
+        r = engine.runner
+        self.lookup = LookupProposer(k, device=r.device, num_rows=engine.kv.slots.num_slots,
+                                     max_len=r.max_blocks * r.bs)
         self.gen = None
         self.stats = dict(steps=0, drafts=0, draft_tokens=0, accepted=0)
         self.adaptive = adaptive
@@ -142,8 +177,9 @@ class SpecRunner:
             if self.drafter is not None:
                 d_ids, d_pr = self.drafter.draft_windows([s.req for _, s in group], k, dev)
             forced = self.forced.next(Bk, dev) if self.forced is not None else None
+            seeds = torch.tensor([row_seed(s.req, 7919) for _, s in group], dtype=torch.int64)
             out, n_acc = rejection_sample(draft, t_ids, t_pr, d_ids, d_pr, greedy, self.rule,
-                                          seq_lens, forced=forced)
+                                          seq_lens, forced=forced, seeds=seeds)
             out_h, n_h = out.cpu().tolist(), n_acc.cpu().tolist()
             for (bi, s), o, n in zip(group, out_h, n_h):
                 sampled[s.req.request_id] = [t for t in o[:n + 1]]
@@ -182,7 +218,10 @@ class SpecRunner:
             drafts = self.drafter.propose([r for r, _ in reqs], [t for _, t in reqs])
         else:
             # history as it will be after the scheduler appends the new tokens
-            drafts = [self.lookup.propose_one(r.all_token_ids + t) for r, t in reqs]
+            if self.lookup.dev is not None:
+                drafts = self.lookup.propose_gpu([(r, r.all_token_ids + t) for r, t in reqs])
+            else:
+                drafts = [self.lookup.propose_one(r.all_token_ids + t) for r, t in reqs]
             if self.forced is not None:
                 drafts = [(d + [t[-1]] * self.k)[:self.k] for d, (r, t) in zip(drafts, reqs)]
         if self.adaptive is not None:

@@ -23,6 +23,7 @@ window and the drafter's candidate set — so nothing of vocabulary size is mate
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 from typing import Optional
 
@@ -85,11 +86,50 @@ def _sample_window(ids, probs, u):
     return ids.gather(-1, j).squeeze(-1)
 
 
+_KIND = {"leviathan": 0, "cactus": 1, "nsd": 2}
+_USE_CUDA = os.environ.get("RADIANCE_CUDA_REJECTION", "1") != "0"
+
+
 def rejection_sample(draft: torch.Tensor, t_ids: torch.Tensor, t_probs: torch.Tensor,
                      d_ids: Optional[torch.Tensor], d_probs: Optional[torch.Tensor],
                      greedy: torch.Tensor, rule: AcceptRule, seq_lens: torch.Tensor,
                      gen: Optional[torch.Generator] = None,
-                     forced: Optional[torch.Tensor] = None):
+                     forced: Optional[torch.Tensor] = None,
+                     seeds: Optional[torch.Tensor] = None):
+    """See the module docstring.  CUDA tensors run the one-warp-per-request kernel
+    (``csrc/spec_decode.cu``) with a Philox stream per row keyed by `seeds` [B] (drawn from `gen`
+    or torch's generator when absent); CPU tensors run the reference torch version below."""
+    if draft.is_cuda and _USE_CUDA and t_ids.shape[-1] <= 64 and \
+            (d_ids is None or d_ids.shape[-1] <= 64):
+        from ..ops._ext import ext
+        B, k = draft.shape
+        dev = draft.device
+        if seeds is None:
+            seeds = torch.randint(0, 2 ** 62, (B,), generator=gen,
+                                  device="cpu" if gen is None or gen.device.type == "cpu"
+                                  else dev).to(dev)
+        out = torch.empty(B, k + 1, dtype=torch.long, device=dev)
+        n_acc = torch.empty(B, dtype=torch.long, device=dev)
+        e = torch.empty(0, device=dev)
+        ext().rejection_sample(draft.long().contiguous(), t_ids.long().contiguous(),
+                               t_probs.float().contiguous(),
+                               d_ids.long().contiguous() if d_ids is not None else e.long(),
+                               d_probs.float().contiguous() if d_probs is not None else e,
+                               greedy.bool().contiguous(), seq_lens.to(dev).long().contiguous(),
+                               forced.to(dev).long().contiguous() if forced is not None else e.long(),
+                               seeds.to(dev).long().contiguous(), _KIND[rule.kind], rule.delta,
+                               rule.fade_start, rule.fade_end, rule.cap_r, rule.escape,
+                               rule.theta, out, n_acc)
+        return out, n_acc
+    return _rejection_sample_torch(draft, t_ids, t_probs, d_ids, d_probs, greedy, rule, seq_lens,
+                                   gen, forced)
+
+
+def _rejection_sample_torch(draft: torch.Tensor, t_ids: torch.Tensor, t_probs: torch.Tensor,
+                            d_ids: Optional[torch.Tensor], d_probs: Optional[torch.Tensor],
+                            greedy: torch.Tensor, rule: AcceptRule, seq_lens: torch.Tensor,
+                            gen: Optional[torch.Generator] = None,
+                            forced: Optional[torch.Tensor] = None):
     """Per request b with k drafts:
       draft [B,k] drafted ids; t_ids/t_probs [B,k+1,W] target windows (probs sum to 1, sorted
       descending); d_ids/d_probs [B,k,Kd] draft windows (None -> point mass on the draft token,
