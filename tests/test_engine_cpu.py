@@ -78,6 +78,25 @@ def test_kl_quantized_vs_bf16_tiny():
     assert kl < 0.05, kl
 
 
+def test_int4_model_and_int4_lm_head_close_to_bf16():
+    """W4A16 INT4 linears (and an int4 lm_head on the MXFP4 model) stay close to the bf16 model."""
+    torch.manual_seed(0)
+    prompt = torch.randint(3, 4096, (96,)).tolist()
+    lb = _prefill_logits(_engine(4096, "bf16"), prompt)
+    li = _prefill_logits(_engine(4096, "int4"), prompt)
+    cfg = EngineConfig(model="tiny_hybrid", device="cpu", max_model_len=1024, max_num_seqs=4,
+                       max_num_batched_tokens=4096, enable_cuda_graphs=False, num_kv_blocks=64,
+                       quantization="mxfp4", lm_head_quant="int4")
+    eng = LLMEngine(cfg)
+    assert eng.model.lm_head.quant == "int4"
+    lh = _prefill_logits(eng, prompt)
+    p = torch.log_softmax(lb, -1)
+    for lq in (li, lh):
+        q = torch.log_softmax(lq, -1)
+        kl = float((p.exp() * (p - q)).sum(-1).mean())
+        assert kl < 0.05, kl
+
+
 def test_scheduler_chunking_and_preemption():
     kv = KVCacheManager(num_blocks=8, block_size=16, num_slots=4)
     sch = Scheduler(kv, max_num_seqs=3, max_num_batched_tokens=64, max_model_len=512)

@@ -96,3 +96,46 @@ def test_mxfp4_weight_k_tail_padding():
     got = ref.mxfp4_linear(q, s, shard.packed, shard.scales).float()
     want = ((q.float() @ shard.dequantize().t()) * s[:, None]).to(torch.bfloat16).float()
     assert torch.equal(got, want)
+
+
+def test_int4_weight_roundtrip_and_clip_search():
+    """INT4 g128 container: dequantisation matches the format, the MSE clip search never loses to
+    the plain min/max range, and the host W4A16 linear is x @ dequant(w)^T."""
+    from vllm_sly_radiance_b200.quant.int4 import Int4Weight, w4a16_linear
+    g = torch.Generator().manual_seed(5)
+    w = torch.randn(64, 512, generator=g)
+    w[3, 7] = 9.0                                            # an outlier group
+    plain = Int4Weight.from_float(w)
+    clipped = Int4Weight.from_float(w, clip_search=True)
+    e_plain = float((plain.dequantize() - w).pow(2).sum())
+    e_clip = float((clipped.dequantize() - w).pow(2).sum())
+    assert e_clip <= e_plain + 1e-6 and e_clip / float(w.pow(2).sum()) < 0.02
+    x = torch.randn(5, 512, generator=g).to(torch.bfloat16)
+    y = w4a16_linear(x, clipped)
+    want = (x.float() @ clipped.dequantize().t()).to(torch.bfloat16)
+    assert torch.equal(y, want)
+    assert clipped.nbytes == 64 * 256 + 64 * 4 * 3
+
+
+def test_int4_fragment_tiling_roundtrip():
+    """The tensor-core fragment layout of int4 weights is a pure permutation: nibble i = h + 2c + 4p
+    of lane 4g + t, step s of tile T / block kb is w[16T + 8h + g, 64kb + 16t + 4s + 2c + p]."""
+    from vllm_sly_radiance_b200.quant.formats import unpack_nibbles
+    from vllm_sly_radiance_b200.quant.int4 import Int4Weight, mma_tile, mma_untile
+    w = Int4Weight.from_float(torch.randn(40, 384))
+    wt, sz = mma_tile(w.packed, w.scales, w.zeros)
+    assert wt.shape == (48, 192) and sz.shape == (3, 3, 8, 2)
+    p, s, z = mma_untile(wt, sz, 40, 384)
+    assert torch.equal(p, w.packed) and torch.equal(s, w.scales) and torch.equal(z, w.zeros)
+    q = unpack_nibbles(w.packed)
+    words = wt.view(torch.int32).view(3, 6, 32, 4)
+    g = torch.Generator().manual_seed(0)
+    for _ in range(100):
+        T, kb, lane, st, i = (int(torch.randint(0, n, (1,), generator=g)) for n in (2, 6, 32, 4, 8))
+        h, c, pp = i & 1, (i >> 1) & 1, i >> 2
+        v = (int(words[T, kb, lane, st]) >> (4 * i)) & 15
+        assert v == int(q[16 * T + 8 * h + lane // 4, 64 * kb + 16 * (lane % 4) + 4 * st + 2 * c + pp])
+    # scale/zero words: fp16 pair of rows (g, g + 8), bf16 bits of 128 + zero
+    sw = int(sz[1, 2, 5, 0]) & 0xFFFF
+    assert torch.tensor([sw], dtype=torch.int32).to(torch.int16).view(torch.float16) == w.scales[21, 2]
+    assert ((int(sz[1, 2, 5, 1]) >> 16) & 0xFFFF) - 0x4300 == int(w.zeros[29, 2])

@@ -77,6 +77,25 @@ def test_mxfp4_gemm_fused_producer(mode, M, N, Kd, with_res):
     assert rel_err(out, want) < 1e-2, rel_err(out, want)
 
 
+@pytest.mark.parametrize("M,N,Kd", [(1, 248320 // 8, 5120), (3, 5120, 8704), (8, 1000, 1024),
+                                     (40, 2176, 1024), (2, 96, 128), (12, 1000, 256),
+                                     (5, 17408, 5120)])
+def test_w4a16_linear(M, N, Kd):
+    """INT4 g128 W4A16: the tensor-core GEMV (M <= 8) and the dequantise + GEMM path against the
+    fp32 product with the dequantised weight."""
+    from vllm_sly_radiance_b200.quant.int4 import Int4Weight, w4a16_linear
+    g = torch.Generator().manual_seed(M + N)
+    w = Int4Weight.from_float(torch.randn(N, Kd, generator=g) * 0.02)
+    x = torch.randn(M, Kd, generator=g).to(torch.bfloat16)
+    want = x.float() @ w.dequantize().t()
+    wd = w.to(DEV)
+    assert wd.tiled
+    got = w4a16_linear(x.to(DEV), wd)
+    torch.cuda.synchronize()
+    K.check_status(got.device)
+    assert rel_err(got, want) < 1e-2, rel_err(got, want)
+
+
 def test_mxfp4_gemm_repeat_no_stale_state():
     """Back-to-back launches without a sync between them (split-K reduction must not leak)."""
     g = torch.Generator().manual_seed(3)

@@ -76,3 +76,55 @@ def test_tp2_matches_tp1():
     # bf16 partial sums reduce in a different order across ranks: near-tied argmaxes of a random
     # model may flip after a few steps, so only the first greedy tokens must agree
     assert toks[:2] == ref_toks[:2]
+
+
+def test_tp3_geometry_of_target():
+    """The 27B target widened for TP = 3: GQA 6 and the GDN value/key ratio 3 are kept."""
+    from vllm_sly_radiance_b200.config import qwen38_27b
+    from vllm_sly_radiance_b200.parallel.tp_pad import needs_padding, padded_config
+    c = qwen38_27b(17408)
+    p = padded_config(c, 3)
+    assert (p.num_q_heads, p.num_kv_heads, p.gdn_num_k_heads, p.gdn_num_v_heads) == (36, 6, 18, 54)
+    assert p.intermediate_size == 17472 and p.vocab_size == 248448 and p.real_vocab_size == 248320
+    assert p.logical_vocab_size == 248320
+    for tp in (1, 2, 4, 8):
+        assert not needs_padding(c, tp)
+
+
+@pytest.mark.parametrize("quant", ["bf16", "mxfp4"])
+def test_padded_geometry_is_exact_on_one_rank(quant):
+    """Dummy heads / channels / vocabulary rows compute exact zeros: the model widened for TP = 3
+    but run on one rank gives the unpadded model's logits (up to the bf16 rounding of the
+    row-parallel GEMMs, whose longer K is blocked differently by the host BLAS)."""
+    prompt = list(range(30, 90))
+    ref_lg, _ = _logits(HybridModel(tiny_hybrid(), quant=quant, device="cpu", seed=0), prompt)
+    m = HybridModel(tiny_hybrid(), quant=quant, device="cpu", seed=0, tp_pad=3)
+    assert m.cfg.num_kv_heads == 3 and m.cfg.gdn_num_k_heads == 6 and m.cfg.vocab_size == 4224
+    lg, _ = _logits(m, prompt)
+    assert lg.shape == ref_lg.shape
+    rel = float((lg - ref_lg).norm() / ref_lg.norm())
+    assert rel < 1e-2, rel
+    # the dummy rows and columns themselves are exactly zero
+    gdn = m.layers[0].mixer
+    assert float(gdn.A_log[4:].abs().sum()) == 0.0 and gdn.conv_w.shape[0] == 2 * 6 * 64 + 6 * 64
+
+
+def test_tp3_matches_tp1():
+    """Three gloo ranks over the padded geometry (kv heads 2 -> 3, GDN heads 4 -> 6, vocab 4096
+    -> 4224): the last rank holds every dummy, the gathered logits match one rank."""
+    prompt = list(range(30, 90))
+    ref_lg, ref_toks = _logits(HybridModel(tiny_hybrid(), quant="bf16", device="cpu", seed=0), prompt)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 3, port, prompt, q)) for r in range(3)]
+    for p in procs:
+        p.start()
+    lg, toks = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert lg.shape == ref_lg.shape
+    rel = float((lg - ref_lg).norm() / ref_lg.norm())
+    assert rel < 2e-2, rel
+    assert toks[:2] == ref_toks[:2]

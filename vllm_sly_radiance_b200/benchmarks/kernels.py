@@ -3,6 +3,7 @@ set larger than the 126 MB L2).  Usage:
 
     python -m vllm_sly_radiance_b200.benchmarks.kernels gemm [--m 1,8,64,4096]
     python -m vllm_sly_radiance_b200.benchmarks.kernels attn [--ctx 1500,4096 --splits 1,17]
+    python -m vllm_sly_radiance_b200.benchmarks.kernels w4a16 [--m 1,8 --shape lm_head,62080x5120]
 
 Prints one JSON line per case with time, achieved bandwidth / FLOP rate and the fraction of the
 measured peaks in MEASURED_PEAKS.json (fallback 6.65 TB/s, 1.59 PFLOP/s).
@@ -132,14 +133,45 @@ def bench_attn(ctxs, splits_list, batch):
     K._ATTN_DECODE = True
 
 
+def _int4_random(N, Kd, rows=16384):
+    """A random int4 weight built on the host in row blocks (small device footprint)."""
+    from ..quant.int4 import Int4Weight
+    parts = [Int4Weight.from_float(torch.randn(min(rows, N - r), Kd) * 0.02)
+             for r in range(0, N, rows)]
+    return Int4Weight(torch.cat([p.packed for p in parts]), torch.cat([p.scales for p in parts]),
+                      torch.cat([p.zeros for p in parts]), N, Kd).to("cuda")
+
+
+def bench_w4a16(ms, shapes):
+    """W4A16 int4 (g128) linear, DRAM-cold weight rotation."""
+    from ..quant.int4 import w4a16_linear
+    bw, fl, src = peaks()
+    for (N, Kd, name) in shapes:
+        per = N * Kd // 2 + N * (Kd // 128) * 4
+        nrot = max(2, int(300e6 // per) + 1)
+        ws = [_int4_random(N, Kd) for _ in range(nrot)]
+        torch.cuda.empty_cache()
+        for M in ms:
+            x = torch.randn(M, Kd, device="cuda").to(torch.bfloat16)
+
+            def fn(i):
+                w4a16_linear(x, ws[i % nrot])
+            t = timeit(fn)
+            byts = per + M * Kd * 2 + M * N * 2
+            print(json.dumps({"kernel": "w4a16", "shape": name, "M": M, "N": N, "K": Kd,
+                              "us": round(t * 1e6, 2), "GBps": round(byts / t / 1e9, 1),
+                              "frac_hbm": round(byts / t / bw, 3), "peaks": src}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attn"])
+    ap.add_argument("what", choices=["gemm", "attn", "w4a16"])
     ap.add_argument("--ctx", default="1500,4096,16384")
     ap.add_argument("--splits", default="1,4,8,17,32")
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--m", default="1,8,16,64,256,1024,4096")
-    ap.add_argument("--shape", default="", help="comma list of shape names (default: all)")
+    ap.add_argument("--shape", default="",
+                    help="comma list of shape names or NxK (default: all named shapes)")
     ap.add_argument("--iters", type=int, default=50)
     a = ap.parse_args()
     global ITERS
@@ -148,10 +180,14 @@ def main():
     shapes = [(16480, 5120, "gdn_in_proj"), (5120, 6144, "out_proj"), (17408, 5120, "gate_up"),
               (5120, 8704, "down"), (14336, 5120, "attn_qkv"), (248320, 5120, "lm_head")]
     if a.shape:
-        keep = set(a.shape.split(","))
-        shapes = [sh for sh in shapes if sh[2] in keep]
+        keep = a.shape.split(",")
+        # a name from the table, or an explicit NxK
+        shapes = [sh for sh in shapes if sh[2] in keep] + [
+            (int(k.split("x")[0]), int(k.split("x")[1]), k) for k in keep if "x" in k]
     if a.what == "gemm":
         bench_gemm(ms, shapes)
+    elif a.what == "w4a16":
+        bench_w4a16([m for m in ms if m <= 8] or [1], shapes)
     elif a.what == "attn":
         bench_attn([int(v) for v in a.ctx.split(",")], [int(v) for v in a.splits.split(",")],
                    a.batch)

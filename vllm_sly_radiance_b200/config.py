@@ -53,6 +53,8 @@ class ModelConfig:
     max_position_embeddings: int = 262144
     init_std: float = 0.02
     tie_word_embeddings: bool = False
+    # vocabulary rows beyond this are tensor-parallel padding (0 = no padding)
+    real_vocab_size: int = 0
 
     # ---- derived -------------------------------------------------------------------------
     def is_attention_layer(self, i: int) -> bool:
@@ -93,6 +95,10 @@ class ModelConfig:
         # [q+gate interleaved per head (2*hd each) | k | v]
         qd = self.num_q_heads * self.head_dim * (2 if self.attn_output_gate else 1)
         return qd + 2 * self.num_kv_heads * self.head_dim
+
+    @property
+    def logical_vocab_size(self) -> int:
+        return self.real_vocab_size or self.vocab_size
 
     @property
     def is_moe(self) -> bool:
@@ -259,6 +265,7 @@ class EngineConfig:
     dtype: str = "bfloat16"
     quantization: str = "mxfp4"         # mxfp4 (W4A8) | bf16 | nvfp4 (requantized to mxfp4) | int4
     kv_cache_dtype: str = "fp8"         # fp8 | int4 (4-bit per-16 scale/zero) | bf16
+    lm_head_quant: Optional[str] = None  # None (the model's) | int4 (W4A16 g128) | bf16 | mxfp4
     ssm_state_dtype: str = "float32"    # float32 | bfloat16
     block_size: int = 64                # KV page size in tokens
     max_model_len: int = 65536

@@ -37,7 +37,8 @@ class LLMEngine:
             quant = config.quantization if config.gemm_backend == "native" else "fp8"
             if quant == "nvfp4":
                 quant = "mxfp4"
-            model = HybridModel(mcfg, quant=quant, device=self.device, seed=config.seed, tp=self.tp)
+            model = HybridModel(mcfg, quant=quant, device=self.device, seed=config.seed, tp=self.tp,
+                                lm_head_quant=config.lm_head_quant)
         self.model = model
         self.load_time = time.time() - t0
         self.tokenizer = tokenizer or get_tokenizer(tokenizer_path, mcfg.vocab_size)

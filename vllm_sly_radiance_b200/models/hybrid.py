@@ -181,7 +181,7 @@ class GDNMixer:
                                 self.scale, commit_len=meta.commit_len)
             if save is not None:    # speculative verify: keep inputs for the commit pass
                 save.append((proj, y))
-        if self.quant == "bf16":
+        if self.quant in ("bf16", "int4"):
             h = self.out_proj(K.gdn_gated_norm(o, z, self.norm_w, cfg.rms_norm_eps, self.dv))
         else:
             h = self.out_proj(K.gdn_norm_quant(o, z, self.norm_w, cfg.rms_norm_eps, self.dv))
@@ -246,10 +246,10 @@ class AttentionMixer:
         a = K.paged_attention(q, k_cache, v_cache, meta, self.scale).view(T, -1)
         if self.gated:
             gate = qkv[:, hd:]
-            if self.quant == "bf16":
+            if self.quant in ("bf16", "int4"):
                 return self.o_proj(K.gate_mul(a, gate, hd, 2 * hd))
             return self.o_proj(K.gate_mul_quant(a, gate, hd, 2 * hd))
-        return self.o_proj(a if self.quant == "bf16" else K.quant_fp8(a))
+        return self.o_proj(a if self.quant in ("bf16", "int4") else K.quant_fp8(a))
 
 
 class MLP:
@@ -268,7 +268,7 @@ class MLP:
 
     def forward(self, x):
         gu = self.gate_up(x)
-        if self.quant == "bf16":
+        if self.quant in ("bf16", "int4"):
             return self.down(K.silu_mul(gu))
         if self.quant == "mxfp4" and gu.is_cuda and gu.shape[0] <= FUSE_MAX_ROWS and _FUSE_PRODUCERS:
             return self.down(SiluAct(gu))       # SiLU * mul + e4m3 inside the down GEMM
@@ -298,13 +298,21 @@ class HybridModel:
     quantized to MXFP4 at load when quant == 'mxfp4'."""
 
     def __init__(self, cfg: ModelConfig, quant: str = "mxfp4", device="cpu", seed: int = 0,
-                 tp: Optional[TPInfo] = None, init_device=None, weights=None):
-        self.cfg = cfg
+                 tp: Optional[TPInfo] = None, init_device=None, weights=None,
+                 lm_head_quant: Optional[str] = None, tp_pad: Optional[int] = None):
         self.quant = quant
         self.device = torch.device(device)
         self.tp = tp or TPInfo()
         init_dev = torch.device(init_device) if init_device is not None else self.device
         W = weights if weights is not None else RandomWeights(cfg, seed, init_dev)
+        # a TP degree that does not divide the geometry (TP = 3): zero-weight dummy heads and
+        # channels widen it (``tp_pad`` forces the widening of that degree at any TP size)
+        from ..parallel.tp_pad import PaddedWeights, padded_config
+        pcfg = padded_config(cfg, tp_pad or self.tp.size)
+        if pcfg != cfg:
+            W = PaddedWeights(W, cfg, pcfg)
+            cfg = pcfg
+        self.cfg = cfg
         H, V = cfg.hidden_size, cfg.vocab_size
         self.embed = W.tensor("embed", (V, H), "embed").to(torch.bfloat16)
         self.layers = [DecoderLayer(cfg, i, self.tp, quant, W) for i in range(cfg.num_layers)]
@@ -313,7 +321,9 @@ class HybridModel:
         w = W.linear("lm_head", V, H) if not cfg.tie_word_embeddings else self.embed.float()
         s0, per = self.tp.shard(V)
         self.vocab_start = s0
-        self.lm_head = make_linear(slice_rows(w, s0, per), quant, "lm_head")
+        # lm_head format: the model's by default; "int4" = W4A16 g128 with MSE clip search (the
+        # reference's int4 lm_head: a quarter of the bf16 bytes on the decode critical path)
+        self.lm_head = make_linear(slice_rows(w, s0, per), lm_head_quant or quant, "lm_head")
         del w
         if init_dev != self.device or getattr(W, "device", self.device) != self.device:
             self.to(self.device)
@@ -425,7 +435,7 @@ class HybridModel:
         residual = None
         h = x
         ai = gi = 0
-        quant = self.quant != "bf16"
+        quant = self.quant in ("mxfp4", "fp8")     # e4m3 activations (int4 / bf16: bf16 ones)
         fused_ar = self.tp.size > 1 and quant and self.tp.all_reduce_add_rms_quant is not None
         # decode-sized steps: residual add + RMSNorm + e4m3 run inside the next GEMM
         fuse_prod = (self.quant == "mxfp4" and input_ids.is_cuda and _FUSE_PRODUCERS
@@ -493,6 +503,8 @@ class HybridModel:
         lg = self.lm_head(hidden)
         if self.tp.size > 1:
             lg = self.tp.all_gather_last(lg)
+        if self.cfg.real_vocab_size:
+            lg = lg[..., :self.cfg.real_vocab_size].contiguous()    # drop padding rows
         return lg
 
     def weight_bytes(self) -> int:

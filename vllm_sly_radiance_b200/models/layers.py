@@ -1,4 +1,4 @@
-"""Model building blocks: linears (MXFP4 W4A8, bf16, fp8 baseline), RoPE tables, norms.
+"""Model building blocks: linears (MXFP4 W4A8, INT4 W4A16, bf16, fp8 baseline), RoPE tables, norms.
 
 A linear consumes either a bf16 activation or a pre-quantized ``(q_e4m3, scale)`` pair produced
 by a fused producer kernel (the reference's tuple input contract,
@@ -56,6 +56,9 @@ class Linear:
             self.w = MXFP4Weight.from_float(weight)
         elif quant == "bf16":
             self.w = weight.to(torch.bfloat16).contiguous()
+        elif quant == "int4":
+            from ..quant.int4 import Int4Weight
+            self.w = Int4Weight.from_float(weight, clip_search=True)
         elif quant == "fp8":
             amax = weight.float().abs().amax(1).clamp(min=1e-8)
             self.w_scale = (amax / 448.0).float()
@@ -71,7 +74,7 @@ class Linear:
         return lin
 
     def to(self, device) -> "Linear":
-        if self.quant == "mxfp4":
+        if self.quant in ("mxfp4", "int4"):
             self.w = self.w.to(device)
         else:
             self.w = self.w.to(device)
@@ -106,7 +109,7 @@ class Linear:
 
     @property
     def nbytes(self) -> int:
-        if self.quant == "mxfp4":
+        if self.quant in ("mxfp4", "int4"):
             return self.w.nbytes
         return self.w.numel() * self.w.element_size()
 
@@ -137,6 +140,16 @@ class Linear:
             else:
                 y = ((q.float() * s[:, None]) @ (self.w.float() * self.w_scale[:, None]).t()).to(
                     torch.bfloat16)
+            if out is not None:
+                out.copy_(y)
+                return out
+            return y
+        if self.quant == "int4":
+            from ..quant.int4 import w4a16_linear
+            if isinstance(x, tuple):
+                q, s = x
+                x = (q.float() * s[:, None]).to(torch.bfloat16)
+            y = w4a16_linear(x, self.w)
             if out is not None:
                 out.copy_(y)
                 return out
