@@ -199,3 +199,64 @@ def test_prefix_caching_restores_gdn_state(interval, second_len, skip):
     rel = float((got - want).abs().max() / want.abs().max())
     assert rel < 2e-2, rel
     assert eng.kv.hits >= 1
+
+
+def _offload_engine(host_gb, disk_dir=None, disk_gb=0.0, policy="lru", frac=0.5):
+    cfg = EngineConfig(model="tiny_hybrid", device="cpu", max_model_len=1024, max_num_seqs=2,
+                       max_num_batched_tokens=4096, enable_cuda_graphs=False,
+                       num_kv_blocks=22, block_size=16, enable_prefix_caching=True,
+                       prefix_snapshot_slots=1, kv_offload_gb=host_gb,
+                       kv_offload_disk_dir=disk_dir, kv_offload_disk_gb=disk_gb,
+                       kv_offload_policy=policy, kv_offload_state_fraction=frac)
+    return LLMEngine(cfg)
+
+
+@pytest.mark.parametrize("tier", ["host_lru", "host_arc", "disk"])
+def test_kv_offload_tiers_restore_evicted_prefix(tier, tmp_path):
+    """A prefix whose KV blocks and GDN snapshot were evicted from the GPU cache (a second long
+    prompt takes all 21 blocks and the single snapshot slot) comes back from the host RAM tier
+    (LRU / ARC) or, with a tiny RAM tier, partly from the disk tier: the tokens are skipped and
+    the logits equal a full recompute."""
+    g = torch.Generator().manual_seed(4)
+    a = torch.randint(3, 4096, (150,), generator=g).tolist()
+    b = torch.randint(3, 4096, (320,), generator=g).tolist()
+    if tier == "disk":
+        eng = _offload_engine(0.00025, str(tmp_path / "kv"), 0.01, frac=0.9)
+    else:
+        eng = _offload_engine(0.002, policy=tier.split("_")[1])
+    eng.generate([a], SamplingParams(temperature=0, max_tokens=2, ignore_eos=True))
+    eng.generate([b], SamplingParams(temperature=0, max_tokens=2, ignore_eos=True))
+    st = eng.kv.offload.stats
+    assert st["kv"]["saved"] >= 9 and st["state"]["saved"] >= 1, st
+    if tier == "disk":
+        assert st["kv"]["spilled"] > 0 and st["kv"]["disk_items"] > 0, st
+    second = a + [11, 12, 13, 14, 15]
+    got, skipped = _first_step_logits(eng, second)
+    assert skipped == 144, skipped
+    assert eng.kv.offload_hits == 1
+    st = eng.kv.offload.stats
+    assert st["kv"]["loaded_host"] + st["kv"]["loaded_disk"] >= 9, st
+    if tier == "disk":
+        assert st["kv"]["loaded_disk"] > 0, st
+    want = _prefill_logits(_prefix_engine(False), second)
+    rel = float((got - want).abs().max() / want.abs().max())
+    assert rel < 2e-2, rel
+
+
+def test_arc_policy_prefers_frequent_items():
+    """ARC keeps an item hit twice (T2) over a scan of one-time items that LRU would keep."""
+    from vllm_sly_radiance_b200.engine.kv_offload import ARCPolicy, LRUPolicy
+    for cls, survives in ((ARCPolicy, True), (LRUPolicy, False)):
+        p = cls(4)
+        resident = set()
+        for k in ("hot", "a", "b"):
+            for v in p.insert(k):
+                resident.discard(v)
+            resident.add(k)
+        p.hit("hot")
+        for k in ("s1", "s2", "s3", "s4"):
+            for v in p.insert(k):
+                resident.discard(v)
+            resident.add(k)
+        assert ("hot" in p) == survives, cls
+        assert len(p) <= 4 and resident == {k for k in resident if k in p}

@@ -62,3 +62,30 @@ def test_sampling_runs_and_is_seeded():
     a = eng.generate([list(range(50, 90))], sp)[0].outputs[0].token_ids
     b = eng.generate([list(range(50, 90))], sp)[0].outputs[0].token_ids
     assert len(a) == 10 and a == b
+
+
+def test_kv_offload_host_tier_on_gpu():
+    """Evicted prefix blocks and the GDN snapshot round-trip through pinned host memory (device
+    gather kernel + one copy per item) and the resumed prefill equals a recompute."""
+    from vllm_sly_radiance_b200.engine.request import SamplingParams as SP
+
+    def eng_(offload):
+        cfg = EngineConfig(model="tiny_hybrid", device="cuda", max_model_len=1024, max_num_seqs=2,
+                           max_num_batched_tokens=4096, enable_cuda_graphs=False,
+                           num_kv_blocks=22, block_size=16, enable_prefix_caching=offload,
+                           prefix_snapshot_slots=1, kv_offload_gb=0.002 if offload else 0.0,
+                           quantization="bf16", kv_cache_dtype="bf16")
+        return LLMEngine(cfg)
+    g = torch.Generator().manual_seed(4)
+    a = torch.randint(3, 4096, (150,), generator=g).tolist()
+    b = torch.randint(3, 4096, (320,), generator=g).tolist()
+    eng = eng_(True)
+    assert eng.kv.offload.kv.vec and eng.kv.offload.state.vec     # the kernel path
+    eng.generate([a], SP(temperature=0, max_tokens=2, ignore_eos=True))
+    eng.generate([b], SP(temperature=0, max_tokens=2, ignore_eos=True))
+    out = eng.generate([a + [11, 12, 13]], SP(temperature=0, max_tokens=6, ignore_eos=True))
+    assert eng.kv.offload_hits == 1
+    assert eng.kv.offload.stats["kv"]["loaded_host"] >= 9
+    ref = eng_(False).generate([a + [11, 12, 13]], SP(temperature=0, max_tokens=6,
+                                                       ignore_eos=True))
+    assert out[0].outputs[0].token_ids == ref[0].outputs[0].token_ids

@@ -481,3 +481,33 @@ def test_moe_grouped_gemm(R_per_expert):
     torch.cuda.synchronize()
     K.check_status(got.device)
     assert rel_err(got, want) < 1e-2, rel_err(got, want)
+
+
+def test_segment_copy_gather_scatter_roundtrip():
+    """The offload copy engine: segments of items (block / slot indices) of several cache tensors
+    pack into a contiguous staging buffer exactly, and unpack into other items exactly."""
+    from vllm_sly_radiance_b200.ops._ext import ext
+    g = torch.Generator().manual_seed(9)
+    ts = [torch.randint(0, 255, (12, 2, 16, 64), generator=g, dtype=torch.uint8).to(DEV),
+          torch.randn(12, 3, 40, generator=g).to(torch.bfloat16).to(DEV),
+          torch.randn(12, 4, 8, 8, generator=g).to(DEV)]
+    seg = [t[0].numel() * t.element_size() for t in ts]
+    offs = [0, seg[0], seg[0] + seg[1]]
+    item = sum(seg)
+    table = torch.tensor([[t.data_ptr(), t.stride(0) * t.element_size(), b] for t, b in zip(ts, seg)],
+                         dtype=torch.int64, device=DEV)
+    offs_t = torch.tensor(offs, dtype=torch.int64, device=DEV)
+    idx = torch.tensor([7, 2, 11], dtype=torch.int32, device=DEV)
+    stage = torch.empty(3, item, dtype=torch.uint8, device=DEV)
+    ext().segment_copy(table, offs_t, idx, stage, item, True)
+    for k, i in enumerate([7, 2, 11]):
+        for t, o, b in zip(ts, offs, seg):
+            assert torch.equal(stage[k, o:o + b], t[i].reshape(-1).view(torch.uint8))
+    ref = [t.clone() for t in ts]
+    dst = torch.tensor([1, 5, 9], dtype=torch.int32, device=DEV)
+    ext().segment_copy(table, offs_t, dst, stage, item, False)
+    torch.cuda.synchronize()
+    for t, r in zip(ts, ref):
+        assert torch.equal(t[[1, 5, 9]], r[[7, 2, 11]])
+        keep = [j for j in range(12) if j not in (1, 5, 9)]
+        assert torch.equal(t[keep], r[keep])

@@ -279,6 +279,12 @@ class EngineConfig:
     enable_prefix_caching: bool = False
     prefix_snapshot_slots: int = 16  # GDN state snapshots kept for cached prefixes
     prefix_snapshot_interval: int = 0  # also snapshot every N prompt tokens (0: last boundary only)
+    # offload tiers under the GPU prefix cache (evicted KV blocks and GDN snapshots)
+    kv_offload_gb: float = 0.0          # pinned host RAM tier (0 = off)
+    kv_offload_disk_dir: Optional[str] = None
+    kv_offload_disk_gb: float = 0.0     # disk tier below the RAM tier
+    kv_offload_policy: str = "lru"      # lru | arc
+    kv_offload_state_fraction: float = 0.5   # share of each tier for GDN state snapshots
     seed: int = 0
     # speculative decoding
     speculative_method: Optional[str] = None   # None | "dflash2" | "lookup"

@@ -69,6 +69,8 @@ void lookup_draft_cuda(torch::Tensor hist, torch::Tensor rows, torch::Tensor len
 void w4a16_gemv(torch::Tensor x, torch::Tensor wq, torch::Tensor sz, torch::Tensor out,
                 torch::Tensor status);
 void w4a16_dequant(torch::Tensor wq, torch::Tensor sz, int64_t n0, torch::Tensor out);
+void segment_copy(torch::Tensor table, torch::Tensor offs, torch::Tensor idx, torch::Tensor stage,
+                  int64_t item_bytes, bool gather);
 void argmax_rows(torch::Tensor x, torch::Tensor out_ids, torch::Tensor out_vals,
                  torch::Tensor workspace);
 void sample_from_topk(torch::Tensor vals, torch::Tensor ids, torch::Tensor temperature,
@@ -104,6 +106,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("lookup_draft", &rad::lookup_draft_cuda, "prompt-lookup drafts: longest suffix match");
   m.def("w4a16_gemv", &rad::w4a16_gemv, "int4 (g128) x bf16 linear for up to 8 rows");
   m.def("w4a16_dequant", &rad::w4a16_dequant, "int4 (g128) weight rows -> bf16");
+  m.def("segment_copy", &rad::segment_copy, "cache segments <-> contiguous staging (KV offload)");
   m.def("gdn_chunked", &rad::gdn_chunked, "chunked (64-token) gated delta rule for prefill");
   m.def("gdn_decode_fused", &rad::gdn_decode_fused,
         "one-token GDN step: conv update + SiLU + q/k L2 norm + gates + delta rule");

@@ -8,7 +8,9 @@ with the reference's group sizing, ``sly/patch_kv_groups.py``, and the mamba-sty
   * GDN layers: one fixed-size state slot (conv state + SSM state) per running request
     (slot 0 reserved likewise).
 Optional prefix caching hashes full blocks of prompt tokens; a hit reuses the attention blocks
-and restores the GDN state snapshot taken at that block boundary.
+and restores the GDN state snapshot taken at that block boundary.  With an offload manager
+(``engine/kv_offload.py``) evicted blocks and snapshots move to host RAM / disk tiers and a hit
+may continue into them.
 """
 from __future__ import annotations
 
@@ -89,6 +91,9 @@ class KVCacheManager:
         self.lru: "OrderedDict[int, None]" = OrderedDict()
         self.hits = 0
         self.queries = 0
+        self.offload = None            # OffloadManager (host / disk tiers), set by the engine
+        self.offload_hits = 0
+        self._pending_saves: list = []
 
     # ---- capacity ----
     def blocks_needed(self, req: Request, num_tokens: int) -> int:
@@ -117,8 +122,17 @@ class KVCacheManager:
             h = self.block_hash.pop(b)
             self.cached.pop(h, None)
             self.blocks.free.append(b)
+            if self.offload is not None:
+                self._pending_saves.append((h, b))     # write-back to the host tier
         b = self.blocks.alloc()
         return b
+
+    def flush_offload(self):
+        """Enqueue the pending write-backs of evicted blocks (before anything overwrites them:
+        the caller runs this before the step's forward, on the same stream)."""
+        if self._pending_saves:
+            self.offload.save_blocks(self._pending_saves)
+            self._pending_saves = []
 
     def free(self, req: Request):
         for b in req.block_ids:
@@ -147,6 +161,8 @@ class KVCacheManager:
         if not self.enable_prefix_caching:
             return 0
         self.queries += 1
+        if self.offload is not None:
+            self.flush_offload()          # blocks evicted earlier this step become tier hits
         hs = self._hashes(req.prompt_token_ids[:-1])
         n = 0
         for h in hs:
@@ -154,16 +170,36 @@ class KVCacheManager:
                 n += 1
             else:
                 break
-        best = 0
-        for j in range(n, 0, -1):
+        # the run continues into the offload tiers while they hold the blocks (bounded by the
+        # blocks that can be allocated for the reload)
+        m = n
+        if self.offload is not None:
+            room = self.blocks.num_free + len(self.lru) - self.blocks_needed(req, req.num_tokens)
+            while m < len(hs) and m - n < room and (hs[m] in self.cached
+                                                     or self.offload.has_block(hs[m])):
+                m += 1
+        best, tier = 0, False
+        for j in range(m, 0, -1):
             sid = self.snap_by_hash.get(hs[j - 1])
             if sid is not None:
                 self.snap_lru.move_to_end(sid)
                 req.restore_snapshot = sid
                 best = j
                 break
+            if self.offload is not None and self.num_snapshots and \
+                    self.offload.has_state(hs[j - 1]):
+                # the tier snapshot comes back into a GPU snapshot slot now (on the stream,
+                # before this step's forward) and is restored from there like a resident one
+                h = hs[j - 1]
+                sid = self.offload.restore_state(h, lambda: self._reserve_snapshot(h))
+                req.restore_snapshot = sid
+                best = j
+                tier = True
+                break
         if best:
             self.hits += 1
+            if best > n or tier:
+                self.offload_hits += 1
         return best * self.block_size
 
     # ---- GDN state snapshots ----
@@ -197,9 +233,15 @@ class KVCacheManager:
         h = self._hashes(req.prompt_token_ids[:B])[-1]
         if h in self.snap_by_hash:
             return None
+        return self._reserve_snapshot(h)
+
+    def _reserve_snapshot(self, h: str) -> int:
         if not self.snap_free:
             sid, old = self.snap_lru.popitem(last=False)
             self.snap_by_hash.pop(old, None)
+            if self.offload is not None:
+                # write-back before the new snapshot is copied into the slot
+                self.offload.save_state(old, sid)
         else:
             sid = self.snap_free.popleft()
         self.snap_by_hash[h] = sid
@@ -208,14 +250,32 @@ class KVCacheManager:
 
     def adopt_prefix(self, req: Request, num_tokens: int):
         hs = self._hashes(req.prompt_token_ids[:num_tokens])
-        for h in hs:
-            b = self.cached[h]
+        # pin every GPU-resident block of the run first, so allocating the reloaded ones cannot
+        # evict them
+        got = {}
+        for i, h in enumerate(hs):
+            b = self.cached.get(h)
+            if b is None:
+                continue
             if b in self.lru:
                 self.lru.pop(b)
                 self.blocks.ref[b] = 1
             else:
                 self.blocks.incref(b)
+            got[i] = b
+        loads = []
+        for i, h in enumerate(hs):
+            b = got.get(i)
+            if b is None:
+                # a block from the offload tiers: a fresh GPU block, reloaded and re-registered
+                b = self._alloc_block()
+                self.cached[h] = b
+                self.block_hash[b] = h
+                loads.append((h, b))
             req.block_ids.append(b)
+        if loads:
+            self.flush_offload()          # an evicted block must be saved before it is reused
+            self.offload.load_blocks(loads)
 
     def register_blocks(self, req: Request):
         """After a prefill chunk: publish the full prompt blocks of `req` to the prefix cache."""

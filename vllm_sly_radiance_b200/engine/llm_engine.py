@@ -70,6 +70,12 @@ class LLMEngine:
         self.kv = KVCacheManager(self.num_blocks, bs, num_slots, config.enable_prefix_caching,
                                  num_snapshots=n_snap,
                                  snapshot_interval=config.prefix_snapshot_interval)
+        if config.enable_prefix_caching and (config.kv_offload_gb > 0 or config.kv_offload_disk_dir):
+            from .kv_offload import OffloadManager
+            self.kv.offload = OffloadManager(
+                self.caches, int(config.kv_offload_gb * (1 << 30)), config.kv_offload_disk_dir,
+                int(config.kv_offload_disk_gb * (1 << 30)), config.kv_offload_policy,
+                state_fraction=config.kv_offload_state_fraction)
         k = config.num_speculative_tokens if config.speculative_method else 0
         self.scheduler = Scheduler(self.kv, config.max_num_seqs, config.max_num_batched_tokens,
                                    config.max_model_len, num_spec_tokens=k)
@@ -118,6 +124,8 @@ class LLMEngine:
     def step(self) -> list[RequestOutput]:
         t0 = time.perf_counter()
         sched = self.scheduler.schedule()
+        if self.kv.offload is not None:
+            self.kv.flush_offload()    # write-backs of blocks evicted by this schedule
         if sched.is_empty:
             return []
         for s in sched.seqs:         # prefix-cache hits resume from a GDN state snapshot
