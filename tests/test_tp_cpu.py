@@ -126,5 +126,6 @@ def test_tp3_matches_tp1():
         assert p.exitcode == 0
     assert lg.shape == ref_lg.shape
     rel = float((lg - ref_lg).norm() / ref_lg.norm())
-    assert rel < 2e-2, rel
+    # three bf16 partial sums per row-parallel output, reduced in another order than one rank's
+    assert rel < 3e-2, rel
     assert toks[:2] == ref_toks[:2]

@@ -276,7 +276,7 @@ class MLP:
 
 
 class DecoderLayer:
-    def __init__(self, cfg, idx, tp, quant, W):
+    def __init__(self, cfg, idx, tp, quant, W, ep=None):
         self.idx = idx
         p = f"layers.{idx}."
         self.is_attn = cfg.is_attention_layer(idx)
@@ -288,7 +288,7 @@ class DecoderLayer:
             self.mixer = GDNMixer(cfg, tp, quant, W, p)
         if cfg.is_moe:
             from .moe import MoEBlock
-            self.mlp = MoEBlock(cfg, tp, quant, W, p)
+            self.mlp = MoEBlock(cfg, tp, quant, W, p, ep=ep)
         else:
             self.mlp = MLP(cfg, tp, quant, W, p)
 
@@ -299,7 +299,8 @@ class HybridModel:
 
     def __init__(self, cfg: ModelConfig, quant: str = "mxfp4", device="cpu", seed: int = 0,
                  tp: Optional[TPInfo] = None, init_device=None, weights=None,
-                 lm_head_quant: Optional[str] = None, tp_pad: Optional[int] = None):
+                 lm_head_quant: Optional[str] = None, tp_pad: Optional[int] = None,
+                 ep=None):
         self.quant = quant
         self.device = torch.device(device)
         self.tp = tp or TPInfo()
@@ -315,7 +316,10 @@ class HybridModel:
         self.cfg = cfg
         H, V = cfg.hidden_size, cfg.vocab_size
         self.embed = W.tensor("embed", (V, H), "embed").to(torch.bfloat16)
-        self.layers = [DecoderLayer(cfg, i, self.tp, quant, W) for i in range(cfg.num_layers)]
+        # ep: data-parallel attention with expert-parallel MoE layers (parallel/ep.py)
+        self.ep = ep
+        self.layers = [DecoderLayer(cfg, i, self.tp, quant, W, ep=ep)
+                       for i in range(cfg.num_layers)]
         self.final_norm = W.tensor("final_norm", (H,), "norm")
         # vocab-parallel lm_head
         w = W.linear("lm_head", V, H) if not cfg.tie_word_embeddings else self.embed.float()

@@ -26,7 +26,7 @@ from .layers import Linear
 
 
 class MoEBlock:
-    def __init__(self, cfg: ModelConfig, tp, quant: str, W, prefix: str):
+    def __init__(self, cfg: ModelConfig, tp, quant: str, W, prefix: str, ep=None):
         H = cfg.hidden_size
         E = cfg.num_experts
         I = cfg.moe_intermediate_size
@@ -34,10 +34,12 @@ class MoEBlock:
         self.E, self.H, self.I = E, H, I
         self.top_k = cfg.num_experts_per_tok
         self.quant = quant
-        self.ep = None
-        # experts owned by this rank (expert parallel over the tensor-parallel group)
-        size = tp.size if tp is not None else 1
-        rank = tp.rank if tp is not None else 0
+        # experts owned by this rank: expert parallel over the tensor-parallel group (tokens
+        # replicated, partial sums all-reduced), or over a data-parallel group `ep` (tokens
+        # local to each rank, rows exchanged by the EP transport's dispatch / combine)
+        self.ep = ep.transport if ep is not None else None
+        size = ep.size if ep is not None else (tp.size if tp is not None else 1)
+        rank = ep.rank if ep is not None else (tp.rank if tp is not None else 0)
         assert E % size == 0, (E, size)
         self.e0, self.e_local = rank * (E // size), E // size
         router = W.tensor(prefix + "router", (E, H), "linear_bf16") if hasattr(W, "tensor") else None
@@ -106,6 +108,40 @@ class MoEBlock:
         if self.ep is not None:
             return self.ep.dispatch_combine(self, xb, qs, ids, w)
         return self.local_experts(xb, qs, ids, w)
+
+    def expert_rows(self, q, s, xb, le):
+        """Unweighted outputs of this rank's experts for rows routed to them: row i goes through
+        local expert le[i] (any order; rows of one expert are grouped internally)."""
+        n = le.shape[0]
+        dev = le.device
+        if n == 0:
+            return torch.zeros(0, self.H, dtype=torch.bfloat16, device=dev)
+        order = torch.argsort(le, stable=True)
+        counts = torch.bincount(le, minlength=self.e_local)
+        y = torch.empty(n, self.H, dtype=torch.bfloat16, device=dev)
+        if self.w_gate_up is not None and le.is_cuda:
+            y[order] = K.moe_grouped_mlp(q[order], s[order], counts, self.w_gate_up, self.w_down,
+                                         self.I, self.H)
+            return y
+        starts = torch.cumsum(counts, 0) - counts
+        for e in range(self.e_local):
+            c = int(counts[e])
+            if c == 0:
+                continue
+            idx = order[int(starts[e]):int(starts[e]) + c]
+            if self.w_gate_up is not None:
+                gsl = slice(e * 2 * self.I, (e + 1) * 2 * self.I)
+                dsl = slice(e * self.H, (e + 1) * self.H)
+                gu = K.mxfp4_gemm(q[idx], s[idx], self.w_gate_up.packed[gsl], None,
+                                  self.w_gate_up.scales[gsl], 2 * self.I)
+                a = K.silu_mul_quant(gu)
+                y[idx] = K.mxfp4_gemm(a[0], a[1], self.w_down.packed[dsl], None,
+                                      self.w_down.scales[dsl], self.H)
+            else:
+                gu = xb[idx].float() @ self.dense_gu[e].float().t()
+                a = K.silu_mul(gu.to(torch.bfloat16)).float()
+                y[idx] = (a @ self.dense_dn[e].float().t()).to(torch.bfloat16)
+        return y
 
     def local_experts(self, xb, qs, ids, w):
         """Experts [e0, e0+e_local) applied to every (token, slot) routed to them; the other

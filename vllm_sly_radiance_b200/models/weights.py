@@ -17,6 +17,8 @@ from __future__ import annotations
 
 from typing import Optional, Union
 
+import zlib
+
 import torch
 
 from ..config import ModelConfig
@@ -26,19 +28,27 @@ WeightT = Union[torch.Tensor, MXFP4Weight]
 
 
 class RandomWeights:
-    """N(0, init_std) linears, small-noise norms, GDN gate parameters in their usual ranges."""
+    """N(0, init_std) linears, small-noise norms, GDN gate parameters in their usual ranges.
+
+    Every tensor is drawn from its own generator seeded by (seed, name), so a tensor's values do
+    not depend on which other tensors a rank asks for (an expert-parallel rank draws only its own
+    experts and still holds exactly the single-process model's values for them)."""
 
     def __init__(self, cfg: ModelConfig, seed: int, device):
         self.cfg = cfg
         self.device = torch.device(device)
-        self.gen = torch.Generator(device=self.device)
-        self.gen.manual_seed(seed)
+        self.seed = seed
+
+    def _gen(self, name: str) -> torch.Generator:
+        g = torch.Generator(device=self.device)
+        g.manual_seed((self.seed * 1000003 + zlib.crc32(name.encode())) & 0x7FFFFFFFFFFFFFFF)
+        return g
 
     def linear(self, name: str, N: int, K: int) -> WeightT:
-        return torch.randn(N, K, generator=self.gen, device=self.device) * self.cfg.init_std
+        return torch.randn(N, K, generator=self._gen(name), device=self.device) * self.cfg.init_std
 
     def tensor(self, name: str, shape, kind: str = "norm") -> torch.Tensor:
-        g, d = self.gen, self.device
+        g, d = self._gen(name), self.device
         if kind == "norm":             # Gemma (1+w) norms
             return (0.02 * torch.randn(*shape, generator=g, device=d)).to(torch.bfloat16)
         if kind == "norm_plain":       # plain-weight norm (GDN gated norm)
