@@ -121,3 +121,58 @@ def test_lookup_kernel_matches_numpy():
     # incremental upload: extend histories and propose again
     reqs2 = [(r, h + h[:3]) for r, h in reqs]
     assert lp.propose_gpu(reqs2) == [lp_cpu.propose_one(h) for _, h in reqs2]
+
+
+def test_dflash_walk_kernel_matches_torch():
+    """DFlash2 path walk kernel vs the torch walk: identical drafts and one-hot windows at T = 0;
+    at T > 0 the windows equal softmax(score / T) along the sampled path, and Gumbel-max draws
+    follow those probabilities."""
+    from vllm_sly_radiance_b200.models.dflash2 import selector_walk_torch
+    from vllm_sly_radiance_b200.ops import kernels as K
+    from vllm_sly_radiance_b200.ops._ext import ext
+    from vllm_sly_radiance_b200.ops.kernels import status_word
+    g = torch.Generator().manual_seed(11)
+    B, k, Kc, r, V = 37, 7, 8, 64, 5000
+    unary = (torch.randn(B, k, Kc, generator=g) * 2).to(DEV)
+    # distinct candidates per position (slot frequencies below are token frequencies)
+    cand = (torch.arange(Kc) * (V // Kc) +
+            torch.randint(0, V // Kc, (B, k, Kc), generator=g)).to(DEV)
+    anchors = torch.randint(0, V, (B,), generator=g).to(DEV)
+    hp = torch.randn(B, k, r, generator=g).to(DEV)
+    pred = (torch.randn(V, r, generator=g) * 0.3).to(torch.bfloat16).to(DEV)
+    succ = (torch.randn(V, r, generator=g) * 0.3).to(torch.bfloat16).to(DEV)
+    st = status_word(torch.device(DEV))
+
+    def run(temps, seeds):
+        n = temps.numel()
+        d = torch.empty(n, k, dtype=torch.int64, device=DEV)
+        wp = torch.empty(n, k, Kc, dtype=torch.float32, device=DEV)
+        ext().dflash_walk(unary[:n].contiguous(), cand[:n].contiguous(), anchors[:n].contiguous(),
+                          hp[:n].contiguous(), pred, succ, temps, seeds, d, wp, st)
+        return d, wp
+    t0 = torch.zeros(B, device=DEV)
+    d, wp = run(t0, torch.arange(B, dtype=torch.int64, device=DEV))
+    dt, wt = selector_walk_torch(unary, cand, anchors, hp, pred, succ, t0)
+    assert torch.equal(d, dt) and torch.equal(wp, wt)
+    # T > 0: windows along the kernel's own path equal the torch softmax on that path
+    t1 = torch.full((B,), 0.7, device=DEV)
+    d, wp = run(t1, torch.arange(B, dtype=torch.int64, device=DEV) + 5)
+    prev = anchors.clone()
+    for i in range(k):
+        sc = unary[:, i] + ((pred[prev].float() * hp[:, i]).unsqueeze(1) *
+                            succ[cand[:, i]].float()).sum(-1)
+        want = torch.softmax(sc / 0.7, -1)
+        assert torch.allclose(wp[:, i], want, atol=1e-4), i
+        assert bool((cand[:, i] == d[:, i:i + 1]).any(-1).all())
+        prev = d[:, i]
+    # Gumbel-max frequencies at position 0 of one request repeated under many seeds
+    n = 20000
+    one = lambda x: x[:1].expand(n, *x.shape[1:]).contiguous()
+    dd = torch.empty(n, k, dtype=torch.int64, device=DEV)
+    ww = torch.empty(n, k, Kc, dtype=torch.float32, device=DEV)
+    ext().dflash_walk(one(unary), one(cand), one(anchors), one(hp), pred, succ,
+                      torch.full((n,), 0.7, device=DEV),
+                      torch.arange(n, dtype=torch.int64, device=DEV) * 3 + 1, dd, ww, st)
+    K.check_status(torch.device(DEV))
+    freq = torch.stack([(dd[:, 0] == cand[0, 0, c]).float().mean() for c in range(Kc)])
+    assert float((freq - ww[0, 0]).abs().max()) < 0.02, (freq, ww[0, 0])

@@ -71,6 +71,21 @@ void w4a16_gemv(torch::Tensor x, torch::Tensor wq, torch::Tensor sz, torch::Tens
 void w4a16_dequant(torch::Tensor wq, torch::Tensor sz, int64_t n0, torch::Tensor out);
 void segment_copy(torch::Tensor table, torch::Tensor offs, torch::Tensor idx, torch::Tensor stage,
                   int64_t item_bytes, bool gather);
+int64_t ep_buffer_bytes(int64_t world, int64_t maxr, int64_t H, int64_t K, int64_t maxt);
+std::vector<int64_t> ep_offsets(int64_t world, int64_t maxr, int64_t H, int64_t K, int64_t maxt);
+void ep_dispatch(std::vector<int64_t> peers, int64_t rank, int64_t maxr, int64_t El,
+                 int64_t maxt, torch::Tensor q, torch::Tensor s, torch::Tensor ids,
+                 torch::Tensor status);
+void ep_items(std::vector<int64_t> peers, int64_t rank, int64_t maxr, int64_t H, int64_t K,
+              int64_t El, int64_t maxt, int64_t bn, torch::Tensor items, torch::Tensor status);
+void ep_silu_items(torch::Tensor gu, torch::Tensor items, int64_t bn, torch::Tensor q,
+                   torch::Tensor scale);
+void ep_combine(std::vector<int64_t> peers, int64_t rank, int64_t maxr, int64_t El,
+                int64_t maxt, torch::Tensor y, torch::Tensor w, torch::Tensor out,
+                torch::Tensor status);
+void dflash_walk(torch::Tensor unary, torch::Tensor cand, torch::Tensor anchors, torch::Tensor hp,
+                 torch::Tensor pred, torch::Tensor succ, torch::Tensor temps, torch::Tensor seeds,
+                 torch::Tensor drafts, torch::Tensor winp, torch::Tensor status);
 void argmax_rows(torch::Tensor x, torch::Tensor out_ids, torch::Tensor out_vals,
                  torch::Tensor workspace);
 void sample_from_topk(torch::Tensor vals, torch::Tensor ids, torch::Tensor temperature,
@@ -107,6 +122,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("w4a16_gemv", &rad::w4a16_gemv, "int4 (g128) x bf16 linear for up to 8 rows");
   m.def("w4a16_dequant", &rad::w4a16_dequant, "int4 (g128) weight rows -> bf16");
   m.def("segment_copy", &rad::segment_copy, "cache segments <-> contiguous staging (KV offload)");
+  m.def("ep_buffer_bytes", &rad::ep_buffer_bytes, "expert-parallel peer buffer size");
+  m.def("ep_offsets", &rad::ep_offsets, "expert-parallel buffer offsets (rows, scales, meta, combine)");
+  m.def("ep_dispatch", &rad::ep_dispatch, "MoE rows -> expert owners' receive buffers (NVLink)");
+  m.def("ep_items", &rad::ep_items, "wait for every source; grouped GEMM work table in place");
+  m.def("ep_silu_items", &rad::ep_silu_items, "SiLU*mul + e4m3 for the work table's rows");
+  m.def("ep_combine", &rad::ep_combine, "expert outputs -> sources; weighted sum over top-k");
+  m.def("dflash_walk", &rad::dflash_walk, "DFlash2 candidate path walk (one warp per request)");
   m.def("gdn_chunked", &rad::gdn_chunked, "chunked (64-token) gated delta rule for prefill");
   m.def("gdn_decode_fused", &rad::gdn_decode_fused,
         "one-token GDN step: conv update + SiLU + q/k L2 norm + gates + delta rule");

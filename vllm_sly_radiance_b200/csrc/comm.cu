@@ -26,6 +26,10 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <map>
+#include <mutex>
+#include <string>
+
 #include <vector>
 
 #include "common.cuh"
@@ -275,23 +279,80 @@ __global__ void __launch_bounds__(256) push_recv_kernel(
 }  // namespace comm
 
 // ---- IPC plumbing ----
+// A tensor from the caching allocator usually sits inside a larger cudaMalloc segment, and an IPC
+// handle always names the whole segment: the exported record therefore carries the tensor's
+// offset inside it (found with cuMemGetAddressRange), and the opening side adds that offset to
+// the mapped base.  A segment mapped twice (two buffers in one segment) is opened once and
+// reference-counted.
+namespace {
+using GetRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+GetRangeFn get_range_fn() {
+  static GetRangeFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q);
+    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && p,
+                "cuMemGetAddressRange unavailable");
+    return reinterpret_cast<GetRangeFn>(p);
+  }();
+  return fn;
+}
+struct Mapped {
+  void* base;
+  int refs;
+};
+std::mutex g_ipc_mu;
+std::map<std::string, Mapped> g_ipc_by_handle;      // handle bytes -> mapping
+std::map<int64_t, std::string> g_ipc_by_ptr;        // returned pointer -> handle bytes
+}  // namespace
+
 torch::Tensor ipc_handle(torch::Tensor buf) {
   cudaIpcMemHandle_t h;
   C10_CUDA_CHECK(cudaIpcGetMemHandle(&h, buf.data_ptr()));
-  auto out = torch::empty({(int64_t)sizeof(h)}, torch::kUInt8);
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  TORCH_CHECK(get_range_fn()(&base, &size, (CUdeviceptr)buf.data_ptr()) == CUDA_SUCCESS,
+              "ipc_handle: cuMemGetAddressRange failed");
+  const int64_t off = (int64_t)((uintptr_t)buf.data_ptr() - (uintptr_t)base);
+  auto out = torch::empty({(int64_t)(sizeof(h) + sizeof(off))}, torch::kUInt8);
   memcpy(out.data_ptr(), &h, sizeof(h));
+  memcpy((uint8_t*)out.data_ptr() + sizeof(h), &off, sizeof(off));
   return out;
 }
 
 int64_t ipc_open(torch::Tensor handle) {
   cudaIpcMemHandle_t h;
+  TORCH_CHECK(handle.numel() == (int64_t)(sizeof(h) + sizeof(int64_t)), "ipc_open: record size");
   memcpy(&h, handle.data_ptr(), sizeof(h));
-  void* p = nullptr;
-  C10_CUDA_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
-  return (int64_t)(uintptr_t)p;
+  int64_t off = 0;
+  memcpy(&off, (const uint8_t*)handle.data_ptr() + sizeof(h), sizeof(off));
+  const std::string key(reinterpret_cast<const char*>(&h), sizeof(h));
+  std::lock_guard<std::mutex> lk(g_ipc_mu);
+  auto it = g_ipc_by_handle.find(key);
+  void* base = nullptr;
+  if (it == g_ipc_by_handle.end()) {
+    C10_CUDA_CHECK(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
+    g_ipc_by_handle[key] = Mapped{base, 1};
+  } else {
+    base = it->second.base;
+    it->second.refs += 1;
+  }
+  const int64_t ptr = (int64_t)((uintptr_t)base + off);
+  g_ipc_by_ptr[ptr] = key;
+  return ptr;
 }
 
-void ipc_close(int64_t ptr) { C10_CUDA_CHECK(cudaIpcCloseMemHandle((void*)(uintptr_t)ptr)); }
+void ipc_close(int64_t ptr) {
+  std::lock_guard<std::mutex> lk(g_ipc_mu);
+  auto pit = g_ipc_by_ptr.find(ptr);
+  TORCH_CHECK(pit != g_ipc_by_ptr.end(), "ipc_close: pointer was not opened here");
+  auto it = g_ipc_by_handle.find(pit->second);
+  g_ipc_by_ptr.erase(pit);
+  if (it != g_ipc_by_handle.end() && --it->second.refs == 0) {
+    C10_CUDA_CHECK(cudaIpcCloseMemHandle(it->second.base));
+    g_ipc_by_handle.erase(it);
+  }
+}
 
 int64_t symm_header_bytes() { return comm::kDataOffset; }
 

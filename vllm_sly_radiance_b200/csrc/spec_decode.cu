@@ -18,6 +18,12 @@
 //  * lookup_kernel: one CTA per request finds the most recent earlier occurrence of the longest
 //    suffix (max_ngram .. min_ngram tokens) in the request's token history and proposes the k
 //    tokens that followed it.
+//  * walk_kernel: the DFlash2 candidate path walk (dflash2/speculator.py:16 _selector_walk_kernel
+//    behaviour).  One warp per request, one lane per candidate (Kc <= 32); step i scores the
+//    candidates of draft position i against the token chosen at step i - 1 (the anchor at step
+//    0): unary + sum_r pred[prev, r] * hproj[i, r] * succ[cand, r], then picks the argmax at
+//    T = 0 or the Gumbel-noised argmax of score / T, and records the window probabilities
+//    (softmax(score / T), one-hot at T = 0) that the rejection sampler uses as q.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <curand_kernel.h>
@@ -213,6 +219,94 @@ __global__ void __launch_bounds__(256) lookup_kernel(const int* __restrict__ his
   }
 }
 
+// one warp per request; lanes = candidates
+__global__ void __launch_bounds__(128) walk_kernel(
+    const float* __restrict__ unary, const int64_t* __restrict__ cand,
+    const int64_t* __restrict__ anchors, const float* __restrict__ hp,
+    const __nv_bfloat16* __restrict__ pred, const __nv_bfloat16* __restrict__ succ,
+    const float* __restrict__ temps, const int64_t* __restrict__ seeds, int B, int k, int Kc,
+    int r, int64_t V, int64_t* __restrict__ drafts, float* __restrict__ winp,
+    int* __restrict__ status) {
+  pdl_wait();
+  pdl_trigger();
+  const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (b >= B) return;
+  const float t = temps[b];
+  curandStatePhilox4_32_10_t rng;
+  curand_init((unsigned long long)seeds[b], 0ull, 0ull, &rng);
+  int64_t prev = anchors[b];
+  for (int i = 0; i < k; ++i) {
+    const size_t row = ((size_t)b * k + i) * Kc;
+    const bool live = lane < Kc;
+    int64_t c = live ? cand[row + lane] : 0;
+    if (c < 0 || c >= V) {
+      if (live) atomicExch(status, (int)kErrBounds);
+      c = 0;
+    }
+    if (prev < 0 || prev >= V) {
+      if (lane == 0) atomicExch(status, (int)kErrBounds);
+      prev = 0;
+    }
+    float sc = -INFINITY;
+    if (live) {
+      const __nv_bfloat16* pp = pred + (size_t)prev * r;
+      const __nv_bfloat16* sp = succ + (size_t)c * r;
+      const float* hv = hp + ((size_t)b * k + i) * r;
+      float acc = 0.f;
+      for (int j = 0; j < r; ++j)
+        acc += __bfloat162float(pp[j]) * hv[j] * __bfloat162float(sp[j]);
+      sc = unary[row + lane] + acc;
+    }
+    // greedy choice (first maximum)
+    float best = sc;
+    int bi = live ? lane : 32;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    int ch = bi;
+    float w = live && lane == bi ? 1.f : 0.f;
+    // uniforms for the Gumbel noise: ceil(Kc / 4) draws of four per step; every lane holds the
+    // same Philox state and keeps the uniform of its own candidate
+    float u = 0.5f;
+    for (int d = 0; d < (Kc + 3) / 4; ++d) {
+      const float4 v = curand_uniform4(&rng);
+      if ((lane >> 2) == d) {
+        const int e = lane & 3;
+        u = e == 0 ? v.x : e == 1 ? v.y : e == 2 ? v.z : v.w;
+      }
+    }
+    if (t > 0.f) {
+      const float st = live ? sc / t : -INFINITY;
+      float mx = st;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      const float ex = live ? __expf(st - mx) : 0.f;
+      float sum = ex;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      w = ex / sum;
+      u = fminf(fmaxf(u, 1e-9f), 1.f - 1e-9f);
+      float noisy = live ? st - logf(-logf(u)) : -INFINITY;
+      int ni = live ? lane : 32;
+#pragma unroll
+      for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, noisy, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, ni, o);
+        if (ov > noisy || (ov == noisy && oi < ni)) { noisy = ov; ni = oi; }
+      }
+      ch = ni;
+    }
+    if (live) winp[row + lane] = w;
+    const int64_t tok = __shfl_sync(0xffffffffu, c, ch);
+    if (lane == 0) drafts[(size_t)b * k + i] = tok;
+    prev = tok;
+  }
+}
+
 }  // namespace spec
 
 // draft [B,k] int64; t_ids/t_probs [B,k+1,W]; d_ids/d_probs [B,k,Kd] or empty (point mass);
@@ -261,4 +355,39 @@ void lookup_draft_cuda(torch::Tensor hist, torch::Tensor rows, torch::Tensor len
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+}  // namespace rad
+
+namespace rad {
+// unary f32 [B, k, Kc]; cand i64 [B, k, Kc]; anchors i64 [B]; hp f32 [B, k, r];
+// pred / succ bf16 [V, r]; temps f32 [B]; seeds i64 [B] -> drafts i64 [B, k], winp f32 [B, k, Kc]
+void dflash_walk(torch::Tensor unary, torch::Tensor cand, torch::Tensor anchors, torch::Tensor hp,
+                 torch::Tensor pred, torch::Tensor succ, torch::Tensor temps, torch::Tensor seeds,
+                 torch::Tensor drafts, torch::Tensor winp, torch::Tensor status) {
+  const int B = unary.size(0), k = unary.size(1), Kc = unary.size(2), r = hp.size(2);
+  TORCH_CHECK(Kc >= 1 && Kc <= 32, "dflash_walk: 1..32 candidates");
+  TORCH_CHECK(unary.scalar_type() == at::kFloat && unary.is_contiguous() &&
+                  cand.scalar_type() == at::kLong && cand.is_contiguous() &&
+                  cand.numel() == unary.numel() && anchors.scalar_type() == at::kLong &&
+                  anchors.numel() >= B && hp.scalar_type() == at::kFloat && hp.is_contiguous() &&
+                  hp.size(0) == B && hp.size(1) == k && pred.scalar_type() == at::kBFloat16 &&
+                  succ.scalar_type() == at::kBFloat16 && pred.is_contiguous() &&
+                  succ.is_contiguous() && pred.size(1) == r && succ.size(1) == r &&
+                  pred.size(0) == succ.size(0) && temps.scalar_type() == at::kFloat &&
+                  temps.numel() >= B && seeds.scalar_type() == at::kLong && seeds.numel() >= B &&
+                  drafts.scalar_type() == at::kLong && drafts.numel() >= (int64_t)B * k &&
+                  winp.scalar_type() == at::kFloat && winp.is_contiguous() &&
+                  winp.numel() >= unary.numel(), "dflash_walk: args");
+  if (B == 0) return;
+  const at::cuda::CUDAGuard guard(unary.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  C10_CUDA_CHECK(launch_pdl(spec::walk_kernel, dim3((B + 3) / 4), dim3(128), 0, stream,
+                            unary.data_ptr<float>(), cand.data_ptr<int64_t>(),
+                            anchors.data_ptr<int64_t>(), hp.data_ptr<float>(),
+                            (const __nv_bfloat16*)pred.data_ptr(),
+                            (const __nv_bfloat16*)succ.data_ptr(), temps.data_ptr<float>(),
+                            seeds.data_ptr<int64_t>(), B, k, Kc, r, (int64_t)pred.size(0),
+                            drafts.data_ptr<int64_t>(), winp.data_ptr<float>(),
+                            status.data_ptr<int>()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
 }  // namespace rad

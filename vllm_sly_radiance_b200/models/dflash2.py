@@ -55,6 +55,34 @@ class _DrafterLayer:
         self.mlp_kproj = Linear(rnd(2 * dc.conv_taps * G, H).contiguous(), "bf16", "d_mlp_kproj")
 
 
+def selector_walk_torch(unary, cand, anchors, hp, pred_cb, succ_cb, temps):
+    """Candidate path walk (torch ops): unary [B,k,Kc], cand [B,k,Kc], anchors [B], hp [B,k,r],
+    codebooks [V,r], temps [B] -> drafts [B,k], window probs [B,k,Kc].  Edge scores
+    unary + <pred[prev] * hp, succ[cand]> with prev the token chosen one position earlier (the
+    anchor first); Gumbel-noised argmax of score / T at T > 0, argmax at T = 0."""
+    B, k, Kc = unary.shape
+    dev = unary.device
+    prev_ids = torch.cat([anchors.view(B, 1, 1).expand(B, 1, Kc), cand[:, :-1]], dim=1)
+    pred = pred_cb[prev_ids].float()                                    # [B,k,Kp,r]
+    succ = succ_cb[cand].float()                                        # [B,k,Kc,r]
+    scores = unary.unsqueeze(2) + torch.einsum("bkpr,bkcr->bkpc", pred * hp.unsqueeze(2), succ)
+    temps = temps.view(B, 1)
+    prev = torch.zeros(B, dtype=torch.long, device=dev)
+    drafts, win_p = [], []
+    for i in range(k):
+        s = scores[torch.arange(B, device=dev), i, prev]               # [B, Kc]
+        t = temps.clamp(min=1e-6)
+        probs = torch.softmax(s / t, -1)
+        g = -torch.log(-torch.log(torch.rand(B, Kc, device=dev).clamp(1e-9, 1 - 1e-9)))
+        noisy = torch.where(temps > 0, s / t + g, s)
+        ch = noisy.argmax(-1)
+        greedy_p = F.one_hot(s.argmax(-1), Kc).float()
+        win_p.append(torch.where(temps > 0, probs, greedy_p))
+        drafts.append(cand[torch.arange(B, device=dev), i, ch])
+        prev = ch
+    return torch.stack(drafts, 1), torch.stack(win_p, 1)
+
+
 def grouped_conv(h: torch.Tensor, delta: torch.Tensor, base: torch.Tensor, block: int,
                  G: int, taps: int) -> torch.Tensor:
     """h [T, H] (T = n_blocks * block, block-major); delta [T, taps, G]; base [taps, H].
@@ -226,32 +254,33 @@ class DFlash2Drafter:
         unary, cand = torch.topk(logits, Kc, dim=-1)                    # [B*k, Kc]
         unary, cand = unary.view(B, k, Kc), cand.view(B, k, Kc)
         hp = self.hidden_proj(hd).float().view(B, k, -1)                # [B,k,r]
-        prev_ids = torch.cat([torch.tensor(anchors, device=dev).view(B, 1, 1).expand(B, 1, Kc),
-                              cand[:, :-1]], dim=1)                     # [B,k,Kc(prev)]
-        pred = self.pred_codebook[prev_ids].float()                     # [B,k,Kp,r]
-        succ = self.succ_codebook[cand].float()                         # [B,k,Kc,r]
-        scores = unary.unsqueeze(2) + torch.einsum("bkpr,bkcr->bkpc", pred * hp.unsqueeze(2), succ)
-        # path walk (Gumbel-noised argmax at the request temperature; greedy at T=0)
-        temps = torch.tensor([r.params.temperature for r in reqs], device=dev).view(B, 1)
-        prev = torch.zeros(B, dtype=torch.long, device=dev)
-        drafts, win_p = [], []
-        for i in range(k):
-            s = scores[torch.arange(B, device=dev), i, prev]           # [B, Kc]
-            t = temps.clamp(min=1e-6)
-            probs = torch.softmax(s / t, -1)
-            g = -torch.log(-torch.log(torch.rand(B, Kc, device=dev).clamp(1e-9, 1 - 1e-9)))
-            noisy = torch.where(temps > 0, s / t + g, s)
-            ch = noisy.argmax(-1)
-            greedy_p = F.one_hot(s.argmax(-1), Kc).float()
-            win_p.append(torch.where(temps > 0, probs, greedy_p))
-            drafts.append(cand[torch.arange(B, device=dev), i, ch])
-            prev = ch
-        D = torch.stack(drafts, 1)
-        Wp = torch.stack(win_p, 1)
+        temps = torch.tensor([r.params.temperature for r in reqs], device=dev).view(B)
+        if dev.type == "cuda" and Kc <= 32:
+            D, Wp = self.walk_cuda(unary, cand, anchors, hp, temps, reqs)
+        else:
+            D, Wp = selector_walk_torch(unary, cand, torch.tensor(anchors, device=dev), hp,
+                                        self.pred_codebook, self.succ_codebook, temps)
         out = D.cpu().tolist()
         for b, r in enumerate(reqs):
             self.last[r.request_id] = (cand[b], Wp[b])
         return out
+
+    def walk_cuda(self, unary, cand, anchors, hp, temps, reqs):
+        """The path walk as one kernel (``csrc/spec_decode.cu`` walk_kernel): scores along the
+        chosen path only, Gumbel-max at T > 0, window probabilities for the rejection test."""
+        from ..engine.sampler import row_seed
+        from ..ops._ext import ext
+        from ..ops.kernels import status_word
+        B, k, Kc = unary.shape
+        dev = unary.device
+        drafts = torch.empty(B, k, dtype=torch.int64, device=dev)
+        winp = torch.empty(B, k, Kc, dtype=torch.float32, device=dev)
+        seeds = torch.tensor([row_seed(r, 104729) for r in reqs], dtype=torch.int64).to(dev)
+        anc = torch.as_tensor(anchors, dtype=torch.int64).to(dev)
+        ext().dflash_walk(unary.float().contiguous(), cand.contiguous(), anc, hp.contiguous(),
+                          self.pred_codebook.contiguous(), self.succ_codebook.contiguous(),
+                          temps.float().contiguous(), seeds, drafts, winp, status_word(dev))
+        return drafts, winp
 
     def draft_windows(self, reqs, k, dev):
         ids = torch.stack([self.last[r.request_id][0][:k] for r in reqs])
