@@ -176,3 +176,30 @@ def test_dflash_walk_kernel_matches_torch():
     K.check_status(torch.device(DEV))
     freq = torch.stack([(dd[:, 0] == cand[0, 0, c]).float().mean() for c in range(Kc)])
     assert float((freq - ww[0, 0]).abs().max()) < 0.02, (freq, ww[0, 0])
+
+
+def test_mtp_drafter_engine_gpu():
+    """The MTP drafter through the CUDA engine.  With bf16 weights and a bf16 KV cache the batched
+    verify forward rounds exactly like the one-row decode forward, so greedy speculative output
+    equals plain decoding token for token.  (With e4m3 activations or an fp8 KV cache the verify
+    and decode kernels round differently and a near-tie of this random model may flip; that
+    case only has to run.)"""
+    from vllm_sly_radiance_b200.config import EngineConfig
+    from vllm_sly_radiance_b200.engine.llm_engine import LLMEngine
+    from vllm_sly_radiance_b200.engine.request import SamplingParams
+
+    def eng(spec, quant="bf16", kv="bf16"):
+        return LLMEngine(EngineConfig(model="tiny_hybrid", device="cuda", max_model_len=1024,
+                                      max_num_seqs=4, max_num_batched_tokens=64,
+                                      num_kv_blocks=64, speculative_method=spec,
+                                      num_speculative_tokens=4, enable_cuda_graphs=False,
+                                      quantization=quant, kv_cache_dtype=kv))
+    prompt = list(range(100, 240))
+    sp = SamplingParams(temperature=0, max_tokens=16, ignore_eos=True)
+    base = eng(None).generate([prompt], sp)[0].outputs[0].token_ids
+    e = eng("mtp")
+    assert e.generate([prompt], sp)[0].outputs[0].token_ids == base
+    assert e.spec.stats["draft_tokens"] > 0
+    e8 = eng("mtp", "mxfp4", "fp8")
+    sp2 = SamplingParams(temperature=0.8, top_p=0.95, max_tokens=8, seed=3, ignore_eos=True)
+    assert len(e8.generate([prompt, prompt[:40]], sp2)[1].outputs[0].token_ids) == 8

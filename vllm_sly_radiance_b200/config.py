@@ -287,7 +287,7 @@ class EngineConfig:
     kv_offload_state_fraction: float = 0.5   # share of each tier for GDN state snapshots
     seed: int = 0
     # speculative decoding
-    speculative_method: Optional[str] = None   # None | "dflash2" | "lookup"
+    speculative_method: Optional[str] = None   # None | "dflash2" | "mtp" | "lookup" | "forced"
     num_speculative_tokens: int = 7
     adaptive_width: bool = False     # per-request verify width from acceptance + step-cost model
     acceptance_rule: str = "leviathan"          # leviathan | cactus | nsd

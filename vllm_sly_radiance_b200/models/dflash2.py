@@ -160,7 +160,7 @@ class DFlash2Drafter:
                               rotary_dim=dc.head_dim, theta=dc.rope_theta, eps=dc.rms_norm_eps,
                               gated=False, block_size=self.block_size)
 
-    def observe(self, sched, meta: StepMeta, aux: list, sampled: dict, sample_cnt):
+    def observe(self, sched, meta: StepMeta, aux: list, sampled: dict, sample_cnt, hidden=None):
         """Write context K/V for the tokens the target just committed (prefill chunks and the
         accepted prefix of verified blocks), from the target's aux-layer hidden states."""
         if not aux:

@@ -15,6 +15,7 @@ Proposers:
                 request's suffix (``sly/radiance_lookup_draft.py``: suffix up to 24 tokens over the
                 whole history, point-mass drafts, lossless).
   * ``dflash2`` the DFlash2 block drafter (``models/dflash2.py``).
+  * ``mtp``     the target's multi-token-prediction head chained k times (``models/mtp.py``).
 Adaptive verify width (``spec_decode/adaptive.py``, opt-in ``adaptive_width``) truncates each
 request's drafts to the width that maximises expected tokens per unit of step time.
 
@@ -136,6 +137,12 @@ class SpecRunner:
         hidden = self.model.forward(ids, meta, r.caches, gdn_save=saved,
                                     aux_layers=self.drafter.aux_layers if self.drafter else None,
                                     aux_out=aux)
+        if not sample_idx:
+            # only intermediate prefill chunks this step (their state was written by the
+            # forward itself): nothing to sample, verify or commit
+            if self.drafter is not None:
+                self.drafter.observe(sched, meta, aux, {}, sample_cnt, hidden=hidden)
+            return StepResult({}, num_tokens=meta.num_tokens)
         sidx = torch.tensor(sample_idx, dtype=torch.long).to(dev, non_blocking=True)
         logits = self.model.logits(hidden[sidx])
         rows = []
@@ -201,7 +208,7 @@ class SpecRunner:
         self.engine.metrics.on_spec(len(verify), sum(len(s.draft_tokens) for s in verify),
                                     n_acc_all, self.k)
         if self.drafter is not None:
-            self.drafter.observe(sched, meta, aux, sampled, sample_cnt)
+            self.drafter.observe(sched, meta, aux, sampled, sample_cnt, hidden=hidden)
         self._propose(sched, sampled)
         return StepResult(sampled, num_tokens=meta.num_tokens)
 
@@ -240,6 +247,9 @@ def build_proposer(config, engine) -> SpecRunner:
     if config.speculative_method == "dflash2":
         from ..models.dflash2 import DFlash2Drafter
         drafter = DFlash2Drafter.for_engine(engine, k)
+    elif config.speculative_method == "mtp":
+        from ..models.mtp import MTPDrafter
+        drafter = MTPDrafter.for_engine(engine, k)
     elif config.speculative_method not in ("lookup", "forced"):
         raise ValueError(f"unknown speculative method {config.speculative_method!r}")
     adaptive = AdaptiveWidth.from_env(k) if config.adaptive_width else None
