@@ -302,9 +302,10 @@ def test_gdn_chunked_matches_recurrent(lens, has_init, sdt, split, monkeypatch):
         assert rel_err(o_got, serial[s0:s1].float().cpu().view(-1, Hv, D)) < 3e-2, bi
 
 
+@pytest.mark.parametrize("split", [1, 2, 4])
 @pytest.mark.parametrize("B,Hk,Hv,sdt,init", [(1, 4, 12, torch.float32, 1), (5, 2, 6, torch.float32, 1),
                                               (3, 4, 4, torch.bfloat16, 1), (2, 2, 6, torch.float32, 0)])
-def test_gdn_decode_fused_matches_separate(B, Hk, Hv, sdt, init):
+def test_gdn_decode_fused_matches_separate(B, Hk, Hv, sdt, init, split):
     """One-launch GDN decode step against conv (+ in-place state shift) followed by the
     token-serial recurrence: outputs, SSM states and conv states."""
     torch.manual_seed(11)
@@ -328,7 +329,8 @@ def test_gdn_decode_fused_matches_separate(B, Hk, Hv, sdt, init):
     scale = D ** -0.5
     ba_off = C + vdim
     c1, s1 = conv0.clone(), ssm0.clone()
-    got = K.gdn_decode_fused(x, ba_off, conv_w, c1, s1, A_log, dt_bias, meta, Hk, scale)
+    got = K.gdn_decode_fused(x, ba_off, conv_w, c1, s1, A_log, dt_bias, meta, Hk, scale,
+                             split=split)
     c2, s2 = conv0.clone(), ssm0.clone()
     y = K.gdn_conv(x[:, :C], conv_w, c2, meta, key_dim, D, update_state=True)
     want = K.gdn_recurrent(y, x[:, ba_off:ba_off + 2 * Hv], A_log, dt_bias, s2, meta, Hk, scale)

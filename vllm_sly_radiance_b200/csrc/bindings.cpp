@@ -30,7 +30,8 @@ void gdn_recurrent(torch::Tensor y, torch::Tensor ba, torch::Tensor A_log, torch
 void gdn_decode_fused(torch::Tensor x, int64_t ba_off, torch::Tensor conv_w,
                       torch::Tensor conv_state, torch::Tensor A_log, torch::Tensor dt_bias,
                       torch::Tensor state, torch::Tensor slots, torch::Tensor has_init, int64_t Hk,
-                      double scale, double eps, torch::Tensor out);
+                      double scale, double eps, torch::Tensor out,
+                      int64_t split);
 void gdn_chunked(torch::Tensor y, torch::Tensor ba, torch::Tensor A_log, torch::Tensor dt_bias,
                  torch::Tensor state, torch::Tensor qsl, torch::Tensor slots,
                  torch::Tensor has_init, int64_t Hk, double scale, torch::Tensor out,

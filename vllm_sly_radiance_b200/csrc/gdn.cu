@@ -19,6 +19,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace rad {
@@ -244,7 +246,7 @@ __global__ void __launch_bounds__(128) recurrent_kernel(
 // CTA has read the old q/k conv state) only cluster rank 0 writes the shifted q/k state.  A
 // thread pair owns one row of the [dv, dk] state (64 columns each): one shuffle per reduction.
 // ------------------------------------------------------------------------------------------------
-template <int D, typename ST>
+template <int D, typename ST, int NS>
 __global__ void __launch_bounds__(2 * D) decode_fused_kernel(
     const __nv_bfloat16* __restrict__ x, int ldx,        // in_proj output [B, *]: q|k|v|z|b|a
     const __nv_bfloat16* __restrict__ conv_w,            // [C, 4]
@@ -257,15 +259,46 @@ __global__ void __launch_bounds__(2 * D) decode_fused_kernel(
   pdl_wait();     // inputs come from the preceding kernel
   pdl_trigger();
   constexpr int W = 4;
-  constexpr int HC = D / 2;             // state columns per thread
+  constexpr int TPR = 2 * NS;           // threads per state row
+  constexpr int RPC = D / NS;           // state rows of this CTA (blockIdx.z picks which)
+  constexpr int HC = D / TPR;           // state columns per thread
+  static_assert(RPC * TPR == 2 * D, "2 * D threads cover the CTA's rows");
   __shared__ float sq[D], sk[D], sv[D], sred[2][D / 32];
-  const int b = blockIdx.x, h = blockIdx.y;
+  const int b = blockIdx.x, h = blockIdx.y, z = blockIdx.z;
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int rep = Hv / Hk, hk = h / rep;
   const int key_dim = Hk * D;
   const int slot = slots[b];
   const bool init = has_init[b] != 0;
   const __nv_bfloat16* xr = x + (size_t)b * ldx;
+  // ---- this thread's slice of its state row, loaded first so the load overlaps the conv ----
+  const int r = z * RPC + t / TPR, c0 = (t % TPR) * HC;
+  ST* srow = state + (((size_t)slot * Hv + h) * D + r) * D + c0;
+  float S[HC];
+  if (init) {
+    if constexpr (sizeof(ST) == 4) {
+#pragma unroll
+      for (int c = 0; c < HC; c += 4) {
+        const float4 f = *reinterpret_cast<const float4*>(srow + c);
+        S[c] = f.x; S[c + 1] = f.y; S[c + 2] = f.z; S[c + 3] = f.w;
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < HC; c += 8) {
+        const uint4 u = *reinterpret_cast<const uint4*>(srow + c);
+        const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(hh[e]);
+          S[c + 2 * e] = f.x;
+          S[c + 2 * e + 1] = f.y;
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < HC; ++c) S[c] = 0.f;
+  }
   // ---- conv (threads 0..D-1, one channel of q, k and v each) + SiLU + q/k L2 norm ----
   float in_q[W], in_k[W], in_v[W];
   __nv_bfloat16 *stq = nullptr, *stk = nullptr, *stv = nullptr;
@@ -306,13 +339,15 @@ __global__ void __launch_bounds__(2 * D) decode_fused_kernel(
     for (int w = 0; w < D / 32; ++w) { s2q += sred[0][w]; s2k += sred[1][w]; }
     sq[t] = bf16_round(sq[t] * rsqrtf(s2q + eps));
     sk[t] = bf16_round(sk[t] * rsqrtf(s2k + eps));
-    // shift the conv state: v channels belong to this CTA
+    // shift the conv state: v channel t belongs to the CTA that owns state row t
+    if (t / RPC == z) {
 #pragma unroll
-    for (int j = 0; j < W - 1; ++j) stv[j] = __float2bfloat16_rn(in_v[j + 1]);
+      for (int j = 0; j < W - 1; ++j) stv[j] = __float2bfloat16_rn(in_v[j + 1]);
+    }
   }
   // q/k state: cluster rank 0, after every CTA of the cluster has read the old q/k state
   cluster_sync();
-  if (t < D && cluster_ctarank() == 0) {
+  if (t < D && z == 0 && cluster_ctarank() == 0) {
 #pragma unroll
     for (int j = 0; j < W - 1; ++j) {
       stq[j] = __float2bfloat16_rn(in_q[j + 1]);
@@ -326,41 +361,15 @@ __global__ void __launch_bounds__(2 * D) decode_fused_kernel(
   const float sp = xs > 20.f ? xs : log1pf(__expf(xs));
   const float decay = __expf(-__expf(A_log[h]) * sp);
   const float beta = 1.f / (1.f + __expf(-bb));
-  // ---- delta rule: thread pair (2r, 2r + 1) owns row r of S, half the columns each ----
-  const int r = t >> 1, c0 = (t & 1) * HC;
-  ST* srow = state + (((size_t)slot * Hv + h) * D + r) * D + c0;
-  float S[HC];
-  if (init) {
-    if constexpr (sizeof(ST) == 4) {
-#pragma unroll
-      for (int c = 0; c < HC; c += 4) {
-        const float4 f = *reinterpret_cast<const float4*>(srow + c);
-        S[c] = f.x; S[c + 1] = f.y; S[c + 2] = f.z; S[c + 3] = f.w;
-      }
-    } else {
-#pragma unroll
-      for (int c = 0; c < HC; c += 8) {
-        const uint4 u = *reinterpret_cast<const uint4*>(srow + c);
-        const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = __bfloat1622float2(hh[e]);
-          S[c + 2 * e] = f.x;
-          S[c + 2 * e + 1] = f.y;
-        }
-      }
-    }
-  } else {
-#pragma unroll
-    for (int c = 0; c < HC; ++c) S[c] = 0.f;
-  }
+  // ---- delta rule: TPR consecutive threads own row r of S, HC columns each ----
   float kv = 0.f;
 #pragma unroll
   for (int c = 0; c < HC; ++c) {
     S[c] *= decay;
     kv += S[c] * sk[c0 + c];
   }
-  kv += __shfl_xor_sync(0xffffffffu, kv, 1);
+#pragma unroll
+  for (int o = 1; o < TPR; o <<= 1) kv += __shfl_xor_sync(0xffffffffu, kv, o);
   const float dlt = beta * (sv[r] - kv);
   float o = 0.f;
 #pragma unroll
@@ -368,8 +377,9 @@ __global__ void __launch_bounds__(2 * D) decode_fused_kernel(
     S[c] += dlt * sk[c0 + c];
     o += S[c] * sq[c0 + c];
   }
-  o += __shfl_xor_sync(0xffffffffu, o, 1);
-  if ((t & 1) == 0) out[(size_t)b * ldo + h * D + r] = __float2bfloat16_rn(o * scale);
+#pragma unroll
+  for (int m = 1; m < TPR; m <<= 1) o += __shfl_xor_sync(0xffffffffu, o, m);
+  if (t % TPR == 0) out[(size_t)b * ldo + h * D + r] = __float2bfloat16_rn(o * scale);
   if constexpr (sizeof(ST) == 4) {
 #pragma unroll
     for (int c = 0; c < HC; c += 4)
@@ -478,7 +488,7 @@ C10_CUDA_CHECK(launch_pdl((gdn::recurrent_kernel<DKc, ST>), dim3(grid), dim3(128
 void gdn_decode_fused(torch::Tensor x, int64_t ba_off, torch::Tensor conv_w,
                       torch::Tensor conv_state, torch::Tensor A_log, torch::Tensor dt_bias,
                       torch::Tensor state, torch::Tensor slots, torch::Tensor has_init, int64_t Hk,
-                      double scale, double eps, torch::Tensor out) {
+                      double scale, double eps, torch::Tensor out, int64_t split) {
   const int B = slots.size(0);
   if (B == 0) return;
   const int Hv = state.size(1), DV = state.size(2), DK = state.size(3);
@@ -489,11 +499,25 @@ void gdn_decode_fused(torch::Tensor x, int64_t ba_off, torch::Tensor conv_w,
   TORCH_CHECK(x.size(0) >= B && x.stride(1) == 1, "gdn_decode_fused: one row per sequence");
   const at::cuda::CUDAGuard guard(x.device());
   auto stream = at::cuda::getCurrentCUDAStream();
+  // RADIANCE_GDN_DECODE_SPLIT=2|4 splits each head's state rows over that many CTAs (more CTAs
+  // than Hv at batch 1).  Off by default: on the 27B decode step (48 heads, PDL on) it measured
+  // 220.6 tok/s with 4 CTAs per head against 221.8 with one, since the kernel sits on the step's
+  // dependency chain and not on bandwidth.  Sizes whose grid is small still exercise it in tests.
+  static const int ns_env = [] {
+    const char* v = std::getenv("RADIANCE_GDN_DECODE_SPLIT");
+    return v ? std::atoi(v) : -1;
+  }();
+  // split: 1 | 2 | 4 CTAs per head, 0 = RADIANCE_GDN_DECODE_SPLIT (default 1; its value 0 sizes
+  // the split to the grid)
+  const int req = split == 1 || split == 2 || split == 4 ? (int)split : ns_env;
+  const int ns = req == 1 || req == 2 || req == 4 ? req
+               : req == -1 ? 1 : (B * Hv >= 148 ? 1 : B * Hv * 2 >= 148 ? 2 : 4);
   auto run = [&](auto stag) {
     using ST = typename decltype(stag)::type;
-    auto kern = gdn::decode_fused_kernel<128, ST>;
+    auto kern = ns == 4 ? gdn::decode_fused_kernel<128, ST, 4>
+              : ns == 2 ? gdn::decode_fused_kernel<128, ST, 2> : gdn::decode_fused_kernel<128, ST, 1>;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(B, Hv);
+    cfg.gridDim = dim3(B, Hv, ns);
     cfg.blockDim = dim3(256);
     cfg.stream = stream;
     cudaLaunchAttribute attrs[2];

@@ -344,14 +344,17 @@ def gdn_conv_state_update(x, conv_state, meta, commit_len: Optional[torch.Tensor
 
 
 def gdn_decode_fused(proj, ba_off: int, conv_w, conv_state, ssm_state, A_log, dt_bias, meta,
-                     num_k_heads: int, scale: float, eps: float = 1e-6) -> torch.Tensor:
+                     num_k_heads: int, scale: float, eps: float = 1e-6,
+                     split: int = 0) -> torch.Tensor:
     """One token per sequence (CUDA): conv update + SiLU + q/k L2 norm + gates + delta rule in
-    one launch.  proj = in_proj output rows; returns o [B, Hv * dv] bf16; states updated."""
+    one launch.  proj = in_proj output rows; returns o [B, Hv * dv] bf16; states updated.
+    split: CTAs per head (1, 2, 4; 0 = the library default)."""
     B = meta.num_seqs
     _, Hv, DV, _ = ssm_state.shape
     out = torch.empty(B, Hv * DV, dtype=torch.bfloat16, device=proj.device)
     ext().gdn_decode_fused(proj, ba_off, conv_w, conv_state, A_log, dt_bias, ssm_state,
-                           meta.state_slots, meta.has_initial, num_k_heads, scale, eps, out)
+                           meta.state_slots, meta.has_initial, num_k_heads, scale, eps, out,
+                           split)
     return out
 
 
