@@ -108,6 +108,8 @@ def main():
     ap.add_argument("--model", default="qwen38_27b")
     ap.add_argument("--prompt-len", type=int, default=1500)
     ap.add_argument("--conc", type=int, default=8)
+    ap.add_argument("--prefill-lens", default="",
+                    help="comma list of prompt lengths for prefill-only extras (default: --prompt-len)")
     ap.add_argument("--no-extra", action="store_true", help="skip the prefill / concurrency extras")
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--kernel-profile", default=None,
@@ -132,7 +134,8 @@ def main():
 
     tp = make_tp_info(rank, world, backend="nccl" if args.impl == "baseline" else "fused") \
         if world > 1 else TPInfo()
-    max_len = args.prompt_len + args.warmup + args.steps + 64
+    pf_lens = [int(v) for v in args.prefill_lens.split(",") if v] or [args.prompt_len]
+    max_len = max(args.prompt_len + args.warmup + args.steps + 64, max(pf_lens) + 64)
     cfg = EngineConfig(model=args.model, tensor_parallel_size=world, max_model_len=max(max_len, 4096),
                        max_num_seqs=max(args.conc, 1), max_num_batched_tokens=4096,
                        enable_cuda_graphs=not args.no_graphs, device="cuda",
@@ -208,17 +211,19 @@ def main():
 
     extra = {}
     if not args.no_extra:
-        # ---- prefill-only at the prompt length (fresh request, timed) ----
-        barrier()
-        eng.add_request(rand_prompt(args.prompt_len), SamplingParams(temperature=0, max_tokens=1,
-                                                                      ignore_eos=True), "pf")
-        t1 = time.perf_counter()
-        while eng.has_unfinished_requests():
-            eng.step()
-        barrier()
-        pf = max_over_ranks(time.perf_counter() - t1)
-        extra["prefill_tok_s@%d" % args.prompt_len] = round(args.prompt_len / pf, 1)
-        extra["prefill_vs_baseline"] = round(args.prompt_len / pf / BASELINE_PREFILL_TOKS, 2)
+        # ---- prefill-only at each prompt length (fresh request, timed) ----
+        for L in pf_lens:
+            barrier()
+            eng.add_request(rand_prompt(L), SamplingParams(temperature=0, max_tokens=1,
+                                                           ignore_eos=True), f"pf{L}")
+            t1 = time.perf_counter()
+            while eng.has_unfinished_requests():
+                eng.step()
+            barrier()
+            pf = max_over_ranks(time.perf_counter() - t1)
+            extra["prefill_tok_s@%d" % L] = round(L / pf, 1)
+            if L == args.prompt_len or len(pf_lens) == 1:
+                extra["prefill_vs_baseline"] = round(L / pf / BASELINE_PREFILL_TOKS, 2)
         # ---- aggregate throughput at concurrency C (1k prompt, 64 output tokens each) ----
         C = args.conc
         sp = SamplingParams(temperature=0.7, top_p=0.95, top_k=20, max_tokens=64, ignore_eos=True)
