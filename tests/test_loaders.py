@@ -41,6 +41,11 @@ def _write_hf(rec, cfg, path, fmt):
             p, s = F.mxfp4_quantize(w)
             sd[hf + ".weight_packed"] = p
             sd[hf + ".weight_scale"] = s
+        elif fmt == "int4":       # compressed-tensors pack-quantized, 8 nibbles per int32
+            p, sc, zp = F.int4_g128_quantize(w)
+            sd[hf + ".weight_packed"] = p.contiguous().view(torch.int32)
+            sd[hf + ".weight_scale"] = sc
+            sd[hf + ".weight_zero_point"] = zp
         elif fmt == "nvfp4":
             p, bs, gs = F.nvfp4_quantize(w)
             sd[hf + ".weight_packed"] = p
@@ -112,3 +117,28 @@ def test_load_matches_canonical(tmp_path, fmt):
         assert ((a - b).norm() / a.norm()) < 0.2
     assert torch.equal(l0.mixer.conv_w, l1.mixer.conv_w)
     assert torch.equal(m.embed, ref_model.embed)
+
+
+def test_int4_checkpoint_stays_int4(tmp_path):
+    """An INT4 (W4A16 pack-quantized) checkpoint served with quantization=int4 keeps its codes:
+    the merged / sharded linears hold exactly the stored nibbles, scales and zero points (no
+    dequantise + requantise), and the model runs close to the bf16 model."""
+    from vllm_sly_radiance_b200.quant.int4 import Int4Weight
+    cfg = tiny_hybrid()
+    rec = Recorder(cfg)
+    ref_model = HybridModel(cfg, quant="bf16", device="cpu", weights=rec)
+    _write_hf(rec, cfg, str(tmp_path), "int4")
+    W = CheckpointWeights(str(tmp_path), cfg)
+    W.keep_int4 = True
+    m = HybridModel(cfg, quant="int4", device="cpu", weights=W)
+    down = m.layers[0].mlp.down.w
+    assert isinstance(down, Int4Weight)
+    p, s, z = F.int4_g128_quantize(rec.lin["layers.0.down"])
+    assert torch.equal(down.packed, p) and torch.equal(down.zeros, z)
+    assert torch.equal(down.scales, s)
+    assert isinstance(m.layers[0].mixer.in_proj.w, Int4Weight)
+    assert isinstance(m.layers[3].mixer.qkv.w, Int4Weight)
+    x = (torch.randn(3, cfg.hidden_size) * 0.5).to(torch.bfloat16)
+    a = ref_model.layers[0].mlp.gate_up(x).float()
+    b = m.layers[0].mlp.gate_up(x).float()
+    assert float((a - b).norm() / a.norm()) < 0.15

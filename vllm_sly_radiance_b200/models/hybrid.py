@@ -118,10 +118,15 @@ def _cat_sections(w, sections: list[int], tp: TPInfo):
 
 
 def make_linear(w, quant: str, name: str) -> Linear:
+    from ..quant.int4 import Int4Weight
     if isinstance(w, MXFP4Weight):
         if quant != "mxfp4":
             return Linear(w.dequantize().to(torch.bfloat16), quant, name)
         return Linear.from_mxfp4(w, name)
+    if isinstance(w, Int4Weight):
+        if quant == "int4":
+            return Linear.from_int4(w, name)        # checkpoint codes kept as stored
+        return Linear(w.dequantize(), quant, name)
     return Linear(w, quant, name)
 
 

@@ -73,6 +73,12 @@ class Linear:
         lin.name, lin.quant, lin.N, lin.K, lin.w = name, "mxfp4", w.N, w.K, w
         return lin
 
+    @staticmethod
+    def from_int4(w, name: str = "") -> "Linear":
+        lin = Linear.__new__(Linear)
+        lin.name, lin.quant, lin.N, lin.K, lin.w = name, "int4", w.N, w.K, w
+        return lin
+
     def to(self, device) -> "Linear":
         if self.quant in ("mxfp4", "int4"):
             self.w = self.w.to(device)

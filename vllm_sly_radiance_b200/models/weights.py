@@ -71,14 +71,19 @@ class RandomWeights:
         return True
 
 
+def _is_q(w) -> bool:
+    from ..quant.int4 import Int4Weight
+    return isinstance(w, (MXFP4Weight, Int4Weight))
+
+
 def slice_rows(w: WeightT, start: int, length: int) -> WeightT:
-    if isinstance(w, MXFP4Weight):
+    if _is_q(w):
         return w.narrow_rows(start, length)
     return w[start:start + length]
 
 
 def slice_cols(w: WeightT, start: int, length: int) -> WeightT:
-    if isinstance(w, MXFP4Weight):
+    if _is_q(w):
         return w.narrow_cols(start, length)
     return w[:, start:start + length].contiguous()
 
@@ -86,10 +91,14 @@ def slice_cols(w: WeightT, start: int, length: int) -> WeightT:
 def pad_rows(w: WeightT, multiple: int) -> WeightT:
     """Append zero output rows so the row count is a multiple of `multiple` (keeps the row stride
     of the layer's output 16-byte aligned for the vectorised consumers)."""
-    n = w.N if isinstance(w, MXFP4Weight) else w.shape[0]
+    n = w.N if _is_q(w) else w.shape[0]
     pad = (-n) % multiple
     if pad == 0:
         return w
+    from ..quant.int4 import Int4Weight
+    if isinstance(w, Int4Weight):
+        z = Int4Weight.from_float(torch.zeros(pad, w.K))
+        return cat_rows([w, z])
     if isinstance(w, MXFP4Weight):
         z = MXFP4Weight.from_float(torch.zeros(pad, w.K, dtype=torch.float32, device=w.packed.device))
         return cat_rows([w, z])
@@ -97,7 +106,11 @@ def pad_rows(w: WeightT, multiple: int) -> WeightT:
 
 
 def cat_rows(ws: list) -> WeightT:
+    from ..quant.int4 import Int4Weight
     if isinstance(ws[0], MXFP4Weight):
         from ..quant.mxfp4 import cat_rows as cr
         return cr(ws)
+    if isinstance(ws[0], Int4Weight):
+        from ..quant.int4 import cat_rows as ci
+        return ci(ws)
     return torch.cat(ws, 0)

@@ -132,11 +132,39 @@ class Int4Weight:
         p, s, z = self.canonical()
         return Int4Weight(p.to(device), s.to(device), z.to(device), self.N, self.K)._placed()
 
+    # ---- sharding / merging on the canonical codes (checkpoint weights stay int4) ----
+    def narrow_rows(self, start: int, length: int) -> "Int4Weight":
+        p, s, z = self.canonical()
+        return Int4Weight(p[start:start + length].contiguous(), s[start:start + length].contiguous(),
+                          z[start:start + length].contiguous(), length, self.K)
+
+    def narrow_cols(self, start: int, length: int) -> "Int4Weight":
+        """K slice (row-parallel shard); start / length multiples of the 128-column group."""
+        assert start % GROUP == 0 and length % GROUP == 0 and start + length <= self.K
+        p, s, z = self.canonical()
+        g0, ng = start // GROUP, length // GROUP
+        return Int4Weight(p[:, start // 2:(start + length) // 2].contiguous(),
+                          s[:, g0:g0 + ng].contiguous(), z[:, g0:g0 + ng].contiguous(),
+                          self.N, length)
+
+    def index_rows(self, idx: torch.Tensor) -> "Int4Weight":
+        p, s, z = self.canonical()
+        return Int4Weight(p[idx].contiguous(), s[idx].contiguous(), z[idx].contiguous(),
+                          int(idx.numel()), self.K)
+
     @property
     def nbytes(self) -> int:
         if self.tiled:
             return self.packed.numel() + self.sz.numel() * 4
         return self.packed.numel() + self.scales.numel() * 2 + self.zeros.numel()
+
+
+def cat_rows(ws: list) -> Int4Weight:
+    """Merged linear (qkv, gate_up): concatenate along N."""
+    assert all(w.K == ws[0].K for w in ws)
+    parts = [w.canonical() for w in ws]
+    return Int4Weight(torch.cat([p for p, _, _ in parts]), torch.cat([s for _, s, _ in parts]),
+                      torch.cat([z for _, _, z in parts]), sum(w.N for w in ws), ws[0].K)
 
 
 def w4a16_linear(x: torch.Tensor, w: Int4Weight, row_block: int = 16384) -> torch.Tensor:

@@ -40,6 +40,7 @@ class CheckpointWeights:
         from safetensors import safe_open
         self.cfg = cfg
         self.device = torch.device(device)
+        self.keep_int4 = False         # True: int4 pack-quantized linears load as Int4Weight
         files = sorted(glob.glob(os.path.join(path, "*.safetensors")))
         if not files:
             raise FileNotFoundError(f"no .safetensors files under {path}")
@@ -82,6 +83,11 @@ class CheckpointWeights:
                     zp = unpack_nibbles(zp.view(N, -1))[:, :K // g] if zp.dtype == torch.uint8 and zp.shape[1] * 2 == K // g else zp
                 else:
                     zp = torch.full((N, K // g), 8, dtype=torch.uint8)
+                if self.keep_int4 and g == 128:
+                    # served int4 (W4A16 kernel): keep the codes, scales and zero points as stored
+                    from .int4 import Int4Weight
+                    return Int4Weight(b.contiguous(), scale.half().contiguous(),
+                                      zp.to(torch.uint8).contiguous(), N, K)
                 w = int4_g128_dequantize(b, scale.float(), zp.to(torch.uint8), g)
                 return w
             if scale.dtype == torch.uint8:                      # MXFP4 (UE8M0 per 32)
@@ -163,15 +169,24 @@ class CheckpointWeights:
 
 
 def _cat(ws):
+    from .int4 import Int4Weight
     if isinstance(ws[0], MXFP4Weight):
         from .mxfp4 import cat_rows
         return cat_rows(ws)
+    if isinstance(ws[0], Int4Weight):
+        from .int4 import cat_rows as ci
+        return ci(ws)
+    if any(isinstance(w, Int4Weight) for w in ws):      # mixed (an unquantized part)
+        ws = [w.dequantize() if isinstance(w, Int4Weight) else w for w in ws]
     return torch.cat(ws, 0)
 
 
 def _rows(w, idx: torch.Tensor):
+    from .int4 import Int4Weight
     if isinstance(w, MXFP4Weight):
         return MXFP4Weight.from_packed(w.packed[idx], w.scales[idx])
+    if isinstance(w, Int4Weight):
+        return w.index_rows(idx)
     return w[idx]
 
 
@@ -198,8 +213,13 @@ def gdn_in_proj_permutation(cfg: ModelConfig) -> tuple[torch.Tensor, torch.Tenso
 
 
 def _merge_gdn_in_proj(qkvz, ba, cfg: ModelConfig):
+    from .int4 import Int4Weight
     pq, pb = gdn_in_proj_permutation(cfg)
-    if isinstance(qkvz, MXFP4Weight) != isinstance(ba, MXFP4Weight):
+    if isinstance(qkvz, Int4Weight) and not isinstance(ba, Int4Weight):
+        ba = Int4Weight.from_float(ba.float() if not isinstance(ba, MXFP4Weight)
+                                   else ba.dequantize())
+    if isinstance(qkvz, MXFP4Weight) != isinstance(ba, MXFP4Weight) and \
+            not isinstance(qkvz, Int4Weight):
         # ba is often left unquantized in MXFP4 checkpoints: quantize it to match
         if isinstance(qkvz, MXFP4Weight):
             ba = MXFP4Weight.from_float(ba)
@@ -215,4 +235,5 @@ def load_model(path: str, cfg: Optional[ModelConfig] = None, quant: str = "mxfp4
     from ..models.hybrid import HybridModel
     cfg = cfg or get_model_config(path)
     W = CheckpointWeights(path, cfg)
+    W.keep_int4 = quant == "int4"
     return HybridModel(cfg, quant=quant, device=device, tp=tp, weights=W, init_device="cpu")
