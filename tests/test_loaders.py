@@ -46,6 +46,21 @@ def _write_hf(rec, cfg, path, fmt):
             sd[hf + ".weight_packed"] = p.contiguous().view(torch.int32)
             sd[hf + ".weight_scale"] = sc
             sd[hf + ".weight_zero_point"] = zp
+        elif fmt == "gptq":       # GPTQ v1 / AutoRound layout: K-packed qweight, N-packed qzeros
+            p, sc, zp = F.int4_g128_quantize(w)
+            N, K = w.shape
+            q = F.unpack_nibbles(p).to(torch.int32).t().contiguous()            # [K, N]
+            qw = torch.zeros(K // 8, N, dtype=torch.int32)
+            for i in range(8):
+                qw |= q[i::8] << (4 * i)
+            zq = (zp.to(torch.int32) - 1).t().contiguous()                       # [K/g, N], zero-1
+            qz = torch.zeros(zq.shape[0], (N + 7) // 8, dtype=torch.int32)
+            for i in range(8):
+                col = zq[:, i::8]
+                qz[:, :col.shape[1]] |= (col & 0xF) << (4 * i)
+            sd[hf + ".qweight"] = qw
+            sd[hf + ".scales"] = sc.t().contiguous()
+            sd[hf + ".qzeros"] = qz
         elif fmt == "nvfp4":
             p, bs, gs = F.nvfp4_quantize(w)
             sd[hf + ".weight_packed"] = p
@@ -119,7 +134,8 @@ def test_load_matches_canonical(tmp_path, fmt):
     assert torch.equal(m.embed, ref_model.embed)
 
 
-def test_int4_checkpoint_stays_int4(tmp_path):
+@pytest.mark.parametrize("fmt", ["int4", "gptq"])
+def test_int4_checkpoint_stays_int4(tmp_path, fmt):
     """An INT4 (W4A16 pack-quantized) checkpoint served with quantization=int4 keeps its codes:
     the merged / sharded linears hold exactly the stored nibbles, scales and zero points (no
     dequantise + requantise), and the model runs close to the bf16 model."""
@@ -127,7 +143,7 @@ def test_int4_checkpoint_stays_int4(tmp_path):
     cfg = tiny_hybrid()
     rec = Recorder(cfg)
     ref_model = HybridModel(cfg, quant="bf16", device="cpu", weights=rec)
-    _write_hf(rec, cfg, str(tmp_path), "int4")
+    _write_hf(rec, cfg, str(tmp_path), fmt)
     W = CheckpointWeights(str(tmp_path), cfg)
     W.keep_int4 = True
     m = HybridModel(cfg, quant="int4", device="cpu", weights=W)

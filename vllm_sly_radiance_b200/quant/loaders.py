@@ -10,7 +10,12 @@ Supported per-linear formats (auto-detected from the tensor names next to each w
                                        'ocp' exponent mode)
   * INT4 W4A16 g128 (compressed-tensors pack-quantized) ``weight_packed`` i32 [N,K/8] +
                                        ``weight_scale`` [N,K/g] (+ ``weight_zero_point``)
-                                       -> dequantized, then MXFP4 for the W4A8 path
+                                       -> kept as int4 for ``quantization=int4`` (the W4A16
+                                       kernel), else dequantized (then MXFP4 for W4A8)
+  * INT4 GPTQ / AutoRound layout       ``qweight`` i32 [K/8,N] (8 k per word), ``scales``
+                                       [K/g,N], ``qzeros`` i32 [K/g,N/8] (8 n per word; stored
+                                       zero - 1 unless the config says ``gptq_v2`` /
+                                       ``auto_round`` exact zeros) -> the same int4 path
 
 Qwen3-Next naming (HF) and the layout transforms (reference loader behaviour:
 ``sly/mxfp4/radiance_mxfp4.py:1006-1120``, GDN in_proj merge ``radiance_gdnmerge.py:30-35``):
@@ -41,6 +46,8 @@ class CheckpointWeights:
         self.cfg = cfg
         self.device = torch.device(device)
         self.keep_int4 = False         # True: int4 pack-quantized linears load as Int4Weight
+        # GPTQ v1 stores zero points minus one; gptq_v2 / auto_round store them exactly
+        self.gptq_zero_offset = 1
         files = sorted(glob.glob(os.path.join(path, "*.safetensors")))
         if not files:
             raise FileNotFoundError(f"no .safetensors files under {path}")
@@ -54,6 +61,11 @@ class CheckpointWeights:
         self.prefix = prefix if any(k.startswith(prefix) for k in self.index) else ""
         qc = os.path.join(path, "config.json")
         self.hf_config = json.load(open(qc)) if os.path.exists(qc) else {}
+        qcfg = self.hf_config.get("quantization_config", {}) or {}
+        fmt = str(qcfg.get("checkpoint_format", qcfg.get("packing_format", ""))).lower()
+        if fmt in ("gptq_v2", "auto_round", "auto_round:gptq_v2") or \
+                str(qcfg.get("quant_method", "")).lower() == "auto-round" and "v1" not in fmt:
+            self.gptq_zero_offset = 0
 
     # ---- raw access ----
     def has(self, key: str) -> bool:
@@ -65,9 +77,38 @@ class CheckpointWeights:
     def _hf(self, name: str) -> str:
         return self.prefix + name
 
+    def _gptq_int4(self, p: str):
+        """GPTQ / AutoRound packing -> canonical int4 (packed [N,K/2], scales, zeros)."""
+        from .formats import pack_nibbles
+        qw = self.raw(p + ".qweight").contiguous()          # [K/8, N] int32
+        sc = self.raw(p + ".scales")                          # [K/g, N]
+        K8, N = qw.shape
+        K = K8 * 8
+        shifts = torch.arange(8, dtype=torch.int32) * 4
+        q = ((qw.unsqueeze(1) >> shifts.view(1, 8, 1)) & 0xF).reshape(K, N).t().contiguous()
+        G = sc.shape[0]
+        if self.has(p + ".qzeros"):
+            qz = self.raw(p + ".qzeros").contiguous()         # [K/g, N/8] int32
+            z = ((qz.unsqueeze(2) >> shifts.view(1, 1, 8)) & 0xF).reshape(G, -1)[:, :N]
+            z = (z + self.gptq_zero_offset) & 0xF       # v1 stores (zero - 1) mod 16
+        else:
+            z = torch.full((G, N), 8, dtype=torch.int32)
+        g = K // G
+        packed = pack_nibbles(q.to(torch.uint8))
+        zeros = z.t().contiguous().to(torch.uint8)
+        scales = sc.t().contiguous().half()
+        return packed, scales, zeros, N, K, g
+
     def _linear_any(self, hf_name: str):
-        """Read one HF linear in whatever format it is stored: float tensor or MXFP4Weight."""
+        """Read one HF linear in whatever format it is stored: float tensor, MXFP4Weight or (for
+        ``quantization=int4``) Int4Weight."""
         p = hf_name
+        if self.has(p + ".qweight"):
+            packed, scales, zeros, N, K, g = self._gptq_int4(p)
+            if self.keep_int4 and g == 128:
+                from .int4 import Int4Weight
+                return Int4Weight(packed, scales, zeros, N, K)
+            return int4_g128_dequantize(packed, scales.float(), zeros, g)
         if self.has(p + ".weight_packed") or (self.has(p + ".weight") and self.has(p + ".weight_scale")
                                               and self.raw(p + ".weight").dtype == torch.uint8):
             packed = self.raw(p + ".weight_packed") if self.has(p + ".weight_packed") else self.raw(p + ".weight")
