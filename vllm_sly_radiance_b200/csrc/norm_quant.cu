@@ -101,11 +101,18 @@ __global__ void __launch_bounds__(T) add_rms_kernel(
     const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ res_out, int ldro,
     uint8_t* __restrict__ q, int ldq, float* __restrict__ scale, __nv_bfloat16* __restrict__ nout,
     int ldn, int H, float eps) {
+  const int nvec = H / V;
+  // the norm weight is a model constant: fetched before the dependency wait, off the critical path
+  uint4 wraw[MAXV];
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int v = threadIdx.x + i * T;
+    if (v < nvec) wraw[i] = *reinterpret_cast<const uint4*>(w + v * V);
+  }
   pdl_wait();     // inputs come from the preceding kernel
   pdl_trigger();
   __shared__ float red[T / 32];
   const int row = blockIdx.x;
-  const int nvec = H / V;
   float vals[MAXV][V];
   float ss = 0.f;
 #pragma unroll
@@ -131,7 +138,7 @@ __global__ void __launch_bounds__(T) add_rms_kernel(
     const int v = threadIdx.x + i * T;
     if (v < nvec) {
       float wv[V];
-      load8(w + v * V, wv);
+      load8(reinterpret_cast<const __nv_bfloat16*>(&wraw[i]), wv);
 #pragma unroll
       for (int j = 0; j < V; ++j) vals[i][j] = bf16_round(vals[i][j] * rs * (wv[j] + 1.f));
       if (nout) store8(nout + (size_t)row * ldn + v * V, vals[i]);
@@ -170,19 +177,35 @@ __global__ void __launch_bounds__(T) gdn_norm_quant_kernel(
     const OT* __restrict__ o, int ldo, const __nv_bfloat16* __restrict__ z, int ldz,
     const __nv_bfloat16* __restrict__ w, int D, int head_dim, float eps, uint8_t* __restrict__ q,
     int ldq, float* __restrict__ scale, __nv_bfloat16* __restrict__ nout, int ldn) {
+  const int nvec = D / V;
+  const int lanes_per_head = head_dim / V;     // 16 for head 128 (power of two <= 32)
+  // the norm weight is a model constant: fetched before the dependency wait
+  uint4 wraw[MAXV];
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int v = threadIdx.x + i * T;
+    if (v < nvec) wraw[i] = *reinterpret_cast<const uint4*>(w + (v * V) % head_dim);
+  }
   pdl_wait();     // inputs come from the preceding kernel
   pdl_trigger();
   __shared__ float red[T / 32];
   const int row = blockIdx.x;
-  const int nvec = D / V;
-  const int lanes_per_head = head_dim / V;     // 16 for head 128 (power of two <= 32)
   float vals[MAXV][V];
+  // z comes from an earlier kernel than o: both loads are issued before any reduction
+  uint4 zraw[MAXV];
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int v = threadIdx.x + i * T;
+    if (v < nvec) {
+      load8(o + (size_t)row * ldo + v * V, vals[i]);
+      zraw[i] = *reinterpret_cast<const uint4*>(z + (size_t)row * ldz + v * V);
+    }
+  }
 #pragma unroll
   for (int i = 0; i < MAXV; ++i) {
     const int v = threadIdx.x + i * T;
     float ss = 0.f;
     if (v < nvec) {
-      load8(o + (size_t)row * ldo + v * V, vals[i]);
 #pragma unroll
       for (int j = 0; j < V; ++j) ss += vals[i][j] * vals[i][j];
     }
@@ -191,9 +214,8 @@ __global__ void __launch_bounds__(T) gdn_norm_quant_kernel(
     if (v < nvec) {
       const float rs = rsqrtf(ss / (float)head_dim + eps);
       float wv[V], zv[V];
-      const int c = (v * V) % head_dim;
-      load8(w + c, wv);
-      load8(z + (size_t)row * ldz + v * V, zv);
+      load8(reinterpret_cast<const __nv_bfloat16*>(&wraw[i]), wv);
+      load8(reinterpret_cast<const __nv_bfloat16*>(&zraw[i]), zv);
 #pragma unroll
       for (int j = 0; j < V; ++j) {
         const float nn = bf16_round(vals[i][j] * rs * wv[j]);
