@@ -39,15 +39,22 @@ __global__ void __launch_bounds__(256) qkv_prologue_kernel(
     int cache_fmt, const int64_t* __restrict__ slot_mapping, int block_size) {
   // cache_fmt: 0 bf16, 1 fp8 e4m3, 2 int4 (+ fp16 scale/zero per 16 elements)
   const int cache_fp8 = cache_fmt == 1;
-  pdl_wait();     // inputs come from the preceding kernel
-  pdl_trigger();
   constexpr int PER = D / 32;
   const int gw = blockIdx.x * 8 + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int H = Hq + Hkv;
-  if (gw >= T * H) return;
   const int t = gw / H, h = gw % H;
   const bool isq = h < Hq;
+  // the RMSNorm weight is a model constant: fetched before the dependency wait
+  float nwv[PER];
+  {
+    const __nv_bfloat16* nw = isq ? qn_w : kn_w;
+#pragma unroll
+    for (int p = 0; p < PER; ++p) nwv[p] = __bfloat162float(nw[lane * PER + p]);
+  }
+  pdl_wait();     // inputs come from the preceding kernel
+  pdl_trigger();
+  if (gw >= T * H) return;
   const __nv_bfloat16* src = qkv + (size_t)t * ldqkv + (isq ? h * q_head_stride : k_off + (h - Hq) * D);
   float x[PER];
   float ss = 0.f;
@@ -58,9 +65,8 @@ __global__ void __launch_bounds__(256) qkv_prologue_kernel(
   }
   ss = warp_sum(ss);
   const float rs = rsqrtf(ss / (float)D + eps);
-  const __nv_bfloat16* nw = isq ? qn_w : kn_w;
 #pragma unroll
-  for (int p = 0; p < PER; ++p) x[p] = bf16_round(x[p] * rs * (__bfloat162float(nw[lane * PER + p]) + 1.f));
+  for (int p = 0; p < PER; ++p) x[p] = bf16_round(x[p] * rs * (nwv[p] + 1.f));
   // RoPE (neox): element i < rot/2 pairs with i + rot/2
   const int pos = positions[t];
   const int half = rot / 2;

@@ -256,9 +256,26 @@ __global__ void __launch_bounds__(2 * D) decode_fused_kernel(
     ST* __restrict__ state,                              // [S, Hv, D, D]
     const int* __restrict__ slots, const int* __restrict__ has_init, int Hk, int Hv, int C,
     float scale, float eps, __nv_bfloat16* __restrict__ out, int ldo) {
+  constexpr int W = 4;
+  // model constants (conv taps of this thread's q / k / v channels, the head's gate parameters)
+  // are fetched before the dependency wait, overlapping the predecessor's tail
+  float cwq[W], cwk[W], cwv[W];
+  {
+    const int hk0 = blockIdx.y / (Hv / Hk);
+    const int tt = threadIdx.x;
+    if (tt < D) {
+      const int cq = hk0 * D + tt, ck = Hk * D + hk0 * D + tt, cv = 2 * Hk * D + blockIdx.y * D + tt;
+#pragma unroll
+      for (int j = 0; j < W; ++j) {
+        cwq[j] = __bfloat162float(conv_w[(size_t)cq * W + j]);
+        cwk[j] = __bfloat162float(conv_w[(size_t)ck * W + j]);
+        cwv[j] = __bfloat162float(conv_w[(size_t)cv * W + j]);
+      }
+    }
+  }
+  const float a_log = A_log[blockIdx.y], dtb = dt_bias[blockIdx.y];
   pdl_wait();     // inputs come from the preceding kernel
   pdl_trigger();
-  constexpr int W = 4;
   constexpr int TPR = 2 * NS;           // threads per state row
   constexpr int RPC = D / NS;           // state rows of this CTA (blockIdx.z picks which)
   constexpr int HC = D / TPR;           // state columns per thread
@@ -319,9 +336,9 @@ __global__ void __launch_bounds__(2 * D) decode_fused_kernel(
     float aq = 0.f, ak = 0.f, av = 0.f;
 #pragma unroll
     for (int j = 0; j < W; ++j) {
-      aq += in_q[j] * __bfloat162float(conv_w[(size_t)cq * W + j]);
-      ak += in_k[j] * __bfloat162float(conv_w[(size_t)ck * W + j]);
-      av += in_v[j] * __bfloat162float(conv_w[(size_t)cv * W + j]);
+      aq += in_q[j] * cwq[j];
+      ak += in_k[j] * cwk[j];
+      av += in_v[j] * cwv[j];
     }
     aq = aq / (1.f + __expf(-aq));
     ak = ak / (1.f + __expf(-ak));
@@ -357,9 +374,9 @@ __global__ void __launch_bounds__(2 * D) decode_fused_kernel(
   // ---- gates ----
   const float bb = __bfloat162float(xr[ba_off + h]);
   const float aa = __bfloat162float(xr[ba_off + Hv + h]);
-  const float xs = aa + dt_bias[h];
+  const float xs = aa + dtb;
   const float sp = xs > 20.f ? xs : log1pf(__expf(xs));
-  const float decay = __expf(-__expf(A_log[h]) * sp);
+  const float decay = __expf(-__expf(a_log) * sp);
   const float beta = 1.f / (1.f + __expf(-bb));
   // ---- delta rule: TPR consecutive threads own row r of S, HC columns each ----
   float kv = 0.f;
