@@ -91,10 +91,23 @@ DEVI void st_ll8(uint64_t* p, uint4 u, uint32_t seq) {
 // Sum rows [r0, r1) over `world` LL sources (row r of source p at srcs[p] + r * H / 2 words) in
 // fp32; plain: write the bf16 sum to out; fused: s = bf16(sum) + residual -> res_out, Gemma
 // RMSNorm (1 + w), per-row e4m3 quant.  False if a wait timed out.
+constexpr int kFusedMaxV = 5;   // fused rows: H <= 5 * 256 * 8 = 10240
+
+// the fused path's RMSNorm weight (a model constant), fetched by each kernel before its
+// programmatic-dependency wait so the load overlaps the predecessor's tail
+DEVI void prefetch_norm_weight(const __nv_bfloat16* __restrict__ w, int H, uint4 (&wpre)[kFusedMaxV]) {
+#pragma unroll
+  for (int i = 0; i < kFusedMaxV; ++i) {
+    const int v = threadIdx.x + i * 256;
+    wpre[i] = (w != nullptr && v < H / 8) ? reinterpret_cast<const uint4*>(w)[v]
+                                          : make_uint4(0, 0, 0, 0);
+  }
+}
+
 template <bool FUSED>
 DEVI bool reduce_rows(const uint64_t* const* srcs, int world, uint32_t seq, int r0, int r1, int H,
                       __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ residual,
-                      const __nv_bfloat16* __restrict__ w, float eps,
+                      const uint4 (&wpre)[kFusedMaxV], float eps,
                       __nv_bfloat16* __restrict__ res_out, uint8_t* __restrict__ q,
                       float* __restrict__ scale, float* red, int* status) {
   const int nv = H / 8;
@@ -116,7 +129,7 @@ DEVI bool reduce_rows(const uint64_t* const* srcs, int world, uint32_t seq, int 
         reinterpret_cast<uint4*>(out + (size_t)r * H)[v] = o;
       }
     } else {
-      constexpr int MAXV = 5;   // H <= 5 * 256 * 8 = 10240
+      constexpr int MAXV = kFusedMaxV;
       float vals[MAXV][8];
       float ss = 0.f;
 #pragma unroll
@@ -161,8 +174,7 @@ DEVI bool reduce_rows(const uint64_t* const* srcs, int world, uint32_t seq, int 
       for (int i = 0; i < MAXV; ++i) {
         const int v = threadIdx.x + i * 256;
         if (v < nv) {
-          uint4 wu = reinterpret_cast<const uint4*>(w)[v];
-          const __nv_bfloat162* wh = reinterpret_cast<const __nv_bfloat162*>(&wu);
+          const __nv_bfloat162* wh = reinterpret_cast<const __nv_bfloat162*>(&wpre[i]);
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
             float2 f = __bfloat1622float2(wh[k]);
@@ -207,6 +219,8 @@ __global__ void __launch_bounds__(256) oneshot_kernel(
     const __nv_bfloat16* __restrict__ residual, const __nv_bfloat16* __restrict__ w, float eps,
     __nv_bfloat16* __restrict__ res_out, uint8_t* __restrict__ q, float* __restrict__ scale,
     int* __restrict__ status) {
+  uint4 wpre[kFusedMaxV];
+  if constexpr (FUSED) prefetch_norm_weight(w, H, wpre);
   pdl_wait();     // inputs come from the preceding kernel
   pdl_trigger();
   __shared__ uint32_t s_seq;
@@ -240,8 +254,8 @@ __global__ void __launch_bounds__(256) oneshot_kernel(
   const uint64_t* srcs[kMaxRanks];
   for (int p = 0; p < world; ++p)
     srcs[p] = reinterpret_cast<const uint64_t*>(mine + kDataOffset + half) + (size_t)p * M * row_words;
-  reduce_rows<FUSED>(srcs, world, seq, r0, r1, H, out, residual, w, eps, res_out, q, scale, red,
-                     status);
+  reduce_rows<FUSED>(srcs, world, seq, r0, r1, H, out, residual, wpre, eps, res_out, q, scale,
+                     red, status);
 }
 
 // Reducing half of the GEMM-fused all-reduce: every rank's row-parallel GEMM has pushed its tile
@@ -253,6 +267,8 @@ __global__ void __launch_bounds__(256) push_recv_kernel(
     const __nv_bfloat16* __restrict__ residual, const __nv_bfloat16* __restrict__ w, float eps,
     __nv_bfloat16* __restrict__ res_out, uint8_t* __restrict__ q, float* __restrict__ scale,
     int* __restrict__ status) {
+  uint4 wpre[kFusedMaxV];
+  if constexpr (FUSED) prefetch_norm_weight(w, H, wpre);
   pdl_wait();     // the pushing GEMM precedes this kernel on every rank
   pdl_trigger();
   __shared__ float red[8];
@@ -263,7 +279,7 @@ __global__ void __launch_bounds__(256) push_recv_kernel(
   const int r1 = min(M, r0 + rows_per);
   const uint64_t* srcs[kMaxRanks];
   for (int p = 0; p < pa.world; ++p) srcs[p] = push_slot(pa, pa.rank, seq & 1u, p, M);
-  reduce_rows<FUSED>(srcs, pa.world, seq, r0, r1, H, out, residual, w, eps, res_out, q, scale,
+  reduce_rows<FUSED>(srcs, pa.world, seq, r0, r1, H, out, residual, wpre, eps, res_out, q, scale,
                      red, status);
   __syncthreads();
   uint8_t* mine = pa.peer[pa.rank];
