@@ -222,7 +222,8 @@ def test_paged_attention(D, Hq, Hkv, q_lens, ctx_lens, splits, fp8):
     (256, 24, 4, [1500, 100, 0], 17, "fp8"), (256, 24, 4, [4000], 32, "fp8"),
     (256, 24, 4, [700, 63], 1, "bf16"), (256, 24, 4, [900, 65], 6, "int4"),
     (128, 32, 2, [300, 1], 3, "fp8"), (64, 4, 2, [130, 62, 10], 5, "int4"),
-    (256, 6, 1, [2048], 8, "fp8")])
+    (256, 6, 1, [2048], 8, "fp8"),
+    (256, 24, 4, [16384, 3000], 96, "fp8"), (256, 24, 4, [8192], 128, "bf16")])   # > 32 splits
 def test_paged_attention_decode_kernel(D, Hq, Hkv, ctx_lens, splits, fmt, monkeypatch):
     """The decode kernel (one token per sequence, keys split across warps) agrees with the
     general 64-row tile kernel and with the fp32 oracle, for every cache format."""

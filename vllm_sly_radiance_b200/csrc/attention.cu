@@ -616,7 +616,8 @@ __global__ void __launch_bounds__(128) paged_attn_decode_kernel(
   __shared__ bool s_last;
   __shared__ float s_ml[4][QR][2];
   __shared__ float s_fin[QR][2];
-  __shared__ float s_w[QR][33];
+  constexpr int MAXSP = 128;              // KV splits the in-kernel merge takes
+  __shared__ float s_w[QR][MAXSP + 1];
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* sQ = smem;                                   // [16][D]
   uint8_t* sK = smem + QR * D * 2;                      // [64][D]
@@ -969,45 +970,59 @@ __global__ void __launch_bounds__(128) paged_attn_decode_kernel(
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    // splits past `used` had an empty key range (num_splits <= 32 by the host check)
+    // splits past `used` had an empty key range (num_splits <= MAXSP by the host check)
     const int used = per > 0 ? min(num_splits, (ntiles + per - 1) / per) : 1;
-    // weights per (row, split): warp w handles rows w, w + 4, ...; lane = split
+    // weights per (row, split): warp w handles rows w, w + 4, ...; lane takes splits lane + 32 j
     for (int r = warp; r < rows_here; r += 4) {
       const int rr = row0 + r;
       const size_t gw = (size_t)(s0 + rr / G) * Hq + hk * G + rr % G;
-      float m = -INFINITY, l = 0.f;
-      if (lane < used) {
-        m = __ldcg(part_ml + ((size_t)lane * T * Hq + gw) * 2);
-        l = __ldcg(part_ml + ((size_t)lane * T * Hq + gw) * 2 + 1);
+      float mj[MAXSP / 32], lj[MAXSP / 32];
+      float mmax = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < MAXSP / 32; ++j) {
+        const int sp = lane + 32 * j;
+        mj[j] = -INFINITY;
+        lj[j] = 0.f;
+        if (sp < used) {
+          mj[j] = __ldcg(part_ml + ((size_t)sp * T * Hq + gw) * 2);
+          lj[j] = __ldcg(part_ml + ((size_t)sp * T * Hq + gw) * 2 + 1);
+        }
+        if (lj[j] > 0.f) mmax = fmaxf(mmax, mj[j]);
       }
-      float mmax = l > 0.f ? m : -INFINITY;
 #pragma unroll
       for (int o2 = 16; o2 > 0; o2 >>= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffff, mmax, o2));
-      const float wl = l > 0.f ? l * exp2f(m - mmax) : 0.f;
-      float wsum = wl;
+      float wsum = 0.f;
+#pragma unroll
+      for (int j = 0; j < MAXSP / 32; ++j) {
+        const float wl = lj[j] > 0.f ? lj[j] * exp2f(mj[j] - mmax) : 0.f;
+        wsum += wl;
+        s_w[r][lane + 32 * j] = wl;
+      }
 #pragma unroll
       for (int o2 = 16; o2 > 0; o2 >>= 1) wsum += __shfl_xor_sync(0xffffffff, wsum, o2);
-      s_w[r][lane] = wl;
-      if (lane == 0) s_w[r][32] = wsum;
+      if (lane == 0) s_w[r][MAXSP] = wsum;
     }
     __syncthreads();
-    // every split's partial of one 4-column group is loaded before any is summed
+    // 32 splits' partials of one 4-column group are loaded before any of them is summed
     for (int idx = threadIdx.x; idx < rows_here * (D / 4); idx += 128) {
       const int r = idx / (D / 4), c = (idx % (D / 4)) * 4;
       const int rr = row0 + r;
       const size_t gw = (size_t)(s0 + rr / G) * Hq + hk * G + rr % G;
-      float4 v[32];
-#pragma unroll
-      for (int sp = 0; sp < 32; ++sp)
-        if (sp < used) v[sp] = __ldcg(reinterpret_cast<const float4*>(part_o + ((size_t)sp * T * Hq + gw) * D + c));
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int sp0 = 0; sp0 < used; sp0 += 32) {
+        float4 v[32];
 #pragma unroll
-      for (int sp = 0; sp < 32; ++sp)
-        if (sp < used) {
-          const float w = s_w[r][sp];
-          acc.x += w * v[sp].x; acc.y += w * v[sp].y; acc.z += w * v[sp].z; acc.w += w * v[sp].w;
-        }
-      const float wsum = s_w[r][32];
+        for (int u = 0; u < 32; ++u)
+          if (sp0 + u < used)
+            v[u] = __ldcg(reinterpret_cast<const float4*>(part_o + ((size_t)(sp0 + u) * T * Hq + gw) * D + c));
+#pragma unroll
+        for (int u = 0; u < 32; ++u)
+          if (sp0 + u < used) {
+            const float w = s_w[r][sp0 + u];
+            acc.x += w * v[u].x; acc.y += w * v[u].y; acc.z += w * v[u].z; acc.w += w * v[u].w;
+          }
+      }
+      const float wsum = s_w[r][MAXSP];
       const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
       __nv_bfloat16* dst = out + gw * D + c;
       *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
@@ -1101,7 +1116,8 @@ void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
   if (T == 0 || num_tiles == 0) return;
   TORCH_CHECK(block_size % attn::BC == 0 || attn::BC % block_size == 0,
               "KV page size must divide or be a multiple of 64");
-  TORCH_CHECK(num_splits >= 1 && num_splits <= 32, "num_splits must be in [1, 32]");
+  TORCH_CHECK(num_splits >= 1 && num_splits <= (decode ? 128 : 32),
+              "num_splits must be in [1, 32] (decode kernel: [1, 128])");
   const int fmt = k_cache.scalar_type() == at::kFloat8_e4m3fn ? 1
                 : k_cache.scalar_type() == at::kByte ? 2 : 0;
   const at::cuda::CUDAGuard guard(q.device());

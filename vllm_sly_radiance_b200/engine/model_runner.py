@@ -109,7 +109,9 @@ class ModelRunner:
 
     def _num_splits(self, B: int, ntiles: int, max_kv: int, decode: bool = False) -> int:
         """KV splits per (row tile, kv head): fill ~2 CTAs per SM, at least 256 keys per split
-        (one 64-key tile for decode batches, whose per-tile work is small), at most 32."""
+        (one 64-key tile for decode batches, whose per-tile work is small), at most 32.  The
+        decode kernel merges up to 128 in-kernel, but more than 32 measured no faster at 16k
+        context (41 us at 32 or 64 splits, 58 us at 128) and slower at 1.5k."""
         ctas = max(1, ntiles * self.Hkv)
         s = max(1, min(32, 148 * 2 // ctas))
         s = min(s, max(1, (max_kv + (63 if decode else 255)) // (64 if decode else 256)))

@@ -272,16 +272,17 @@ def paged_attention(q, k_cache, v_cache, meta, scale: float, causal: bool = True
     T, Hq, D = q.shape
     if out is None:
         out = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=q.device)
-    splits = meta.num_splits
+    # one query token per sequence and at most 16 query heads per kv head: the decode kernel
+    # (keys split across warps) replaces the 64-row tile kernel
+    decode = (meta.num_tokens == meta.num_seqs and Hq // k_cache.shape[1] <= 16
+              and _ATTN_DECODE)
+    # the decode kernel merges up to 128 KV splits in-kernel, the tile kernel up to 32
+    splits = meta.num_splits if decode else min(meta.num_splits, 32)
     if splits > 1:
         part_o = meta.scratch_o(splits, T, Hq, D)
         part_ml = meta.scratch_ml(splits, T, Hq)
     else:
         part_o = part_ml = _empty(q.device)
-    # one query token per sequence and at most 16 query heads per kv head: the decode kernel
-    # (keys split across warps) replaces the 64-row tile kernel
-    decode = (meta.num_tokens == meta.num_seqs and Hq // k_cache.shape[1] <= 16
-              and _ATTN_DECODE)
     ext().paged_attention(q, k_cache, v_cache, meta.block_tables, meta.seq_lens,
                           meta.query_start_loc, meta.tile_seq, meta.tile_row0, scale, causal,
                           window, splits, part_o, part_ml, out,
