@@ -25,7 +25,7 @@ import time
 
 import torch
 
-BASELINE_DECODE_TOKS = 154.4       # single-stream decode, 1x R9700
+BASELINE_DECODE_TOKS = 154.4       # reference's published single-stream decode, 1x R9700
 BASELINE_PREFILL_TOKS = 3927.0     # prefill-only at 1,515 tokens
 BASELINE_CONC8_TOKS = 480.0        # aggregate throughput at concurrency 8
 

@@ -1,6 +1,6 @@
 """Speculative decoding: draft proposers and the verify / accept / commit step.
 
-Step with speculation (reference: vLLM V2 runner + DFlash2 speculator):
+Step with speculation (reference: vLLM V2 runner + DFlash2 speculator, dflash2/speculator.py):
   1. every decoding request feeds [last token, d_1..d_k] (its drafts from the previous step),
   2. one target forward over all rows; the GDN layers run the block without touching their state
      and keep their inputs (the reference writes one state snapshot per candidate instead, which
