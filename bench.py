@@ -1,6 +1,8 @@
 """Headline benchmark: single-stream decode tok/s of the Qwen3.8-27B-shaped GDN hybrid with
-MXFP4 W4A8 weights and an fp8 KV cache, after a 1.5k-token prompt,
-plus prefill tok/s at 1.5k and aggregate tok/s at 8 concurrent streams.
+MXFP4 W4A8 weights and an fp8 KV cache, after a 1.5k-token prompt, sampled with the config's
+T=0.7 / top_p=0.95 / top_k=20; extras: a 512-token decode, greedy decode,
+prefill tok/s (device-timed) and aggregate tok/s at 1/2/4/8/16 concurrent streams (1k prompt,
+256 output tokens each), and at TP > 1 the first position's logits against a TP1 engine.
 
     python bench.py --gpus N --steps K --warmup W          (N > 1: launched by torchrun, TP = N)
     python bench.py --impl reference ...                     (reference arm)
@@ -107,7 +109,14 @@ def main():
     ap.add_argument("--impl", default="native", choices=["native", "reference", "baseline"])
     ap.add_argument("--model", default="qwen38_27b")
     ap.add_argument("--prompt-len", type=int, default=1500)
-    ap.add_argument("--conc", type=int, default=8)
+    ap.add_argument("--conc", default="1,2,4,8,16",
+                    help="comma list of concurrency levels for the aggregate extras")
+    ap.add_argument("--conc-prompt", type=int, default=1000)
+    ap.add_argument("--conc-out", type=int, default=256)
+    ap.add_argument("--long-decode", type=int, default=512,
+                    help="tokens of the extra single-stream decode run (0 = skip)")
+    ap.add_argument("--no-tp-check", action="store_true",
+                    help="TP > 1: skip the logits comparison against a TP1 engine")
     ap.add_argument("--prefill-lens", default="",
                     help="comma list of prompt lengths for prefill-only extras (default: --prompt-len)")
     ap.add_argument("--no-extra", action="store_true", help="skip the prefill / concurrency extras")
@@ -135,9 +144,11 @@ def main():
     tp = make_tp_info(rank, world, backend="nccl" if args.impl == "baseline" else "fused") \
         if world > 1 else TPInfo()
     pf_lens = [int(v) for v in args.prefill_lens.split(",") if v] or [args.prompt_len]
-    max_len = max(args.prompt_len + args.warmup + args.steps + 64, max(pf_lens) + 64)
+    concs = [int(v) for v in args.conc.split(",") if v]
+    max_len = max(args.prompt_len + args.warmup + max(args.steps, args.long_decode) + 64,
+                  max(pf_lens) + 64, args.conc_prompt + args.conc_out + 8)
     cfg = EngineConfig(model=args.model, tensor_parallel_size=world, max_model_len=max(max_len, 4096),
-                       max_num_seqs=max(args.conc, 1), max_num_batched_tokens=4096,
+                       max_num_seqs=max(concs + [1]), max_num_batched_tokens=4096,
                        enable_cuda_graphs=not args.no_graphs, device="cuda",
                        gemm_backend="cublas" if args.impl == "baseline" else "native",
                        comm_backend="nccl" if args.impl == "baseline" else "fused")
@@ -163,34 +174,43 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    greedy = SamplingParams(temperature=0.0, max_tokens=args.warmup + args.steps + 8, ignore_eos=True)
+    def timed_steps(n, until=None):
+        """n engine steps (or until `until()` is false), each bracketed by CUDA events on the
+        launching stream; -> (device ms summed, host wall s, tokens returned, h2d, d2h)."""
+        stream = torch.cuda.current_stream()
+        ev, ntok, h2d, d2h = [], 0, 0, 0
+        barrier()
+        w0 = time.perf_counter()
+        i = 0
+        while (until() if until is not None else i < n):
+            s_ = torch.cuda.Event(enable_timing=True)
+            e_ = torch.cuda.Event(enable_timing=True)
+            s_.record(stream)
+            outs = eng.step()
+            e_.record(stream)
+            ev.append((s_, e_))
+            ntok += sum(1 for _ in outs)
+            h2d += eng.runner.last_io[0]
+            d2h += eng.runner.last_io[1]
+            i += 1
+        barrier()
+        wall = time.perf_counter() - w0
+        return sum(a.elapsed_time(b) for a, b in ev), wall, ntok, h2d, d2h, i
+
+    # config 2 sampling (T 0.7, top_p 0.95, top_k 20): the headline decode samples like the
+    # reference's BetterBench runs
+    sampled = SamplingParams(temperature=0.7, top_p=0.95, top_k=20, seed=7,
+                             max_tokens=args.warmup + args.steps + 8, ignore_eos=True)
     # ---- single-stream decode after a 1.5k prompt ----
-    eng.add_request(rand_prompt(args.prompt_len), greedy, request_id="stream0")
+    eng.add_request(rand_prompt(args.prompt_len), sampled, request_id="stream0")
     while eng.requests["stream0"].num_computed_tokens < args.prompt_len:
         eng.step()                       # prefill (chunked), not timed
     for _ in range(args.warmup):
         eng.step()
-    barrier()
-    ev = []
-    stream = torch.cuda.current_stream()
-    h2d = d2h = 0
     with ClockSampler(dev.index) as clk:
-        barrier()
         torch.cuda.nvtx.range_push("timed")
-        w0 = time.perf_counter()
-        for _ in range(args.steps):
-            s = torch.cuda.Event(enable_timing=True)
-            e = torch.cuda.Event(enable_timing=True)
-            s.record(stream)
-            eng.step()
-            e.record(stream)
-            ev.append((s, e))
-            h2d += eng.runner.last_io[0]
-            d2h += eng.runner.last_io[1]
-        barrier()
-        wall = time.perf_counter() - w0
+        dev_ms, wall, _, h2d, d2h, _ = timed_steps(args.steps)
         torch.cuda.nvtx.range_pop()
-    dev_ms = sum(s.elapsed_time(e) for s, e in ev)
     dev_ms = max_over_ranks(dev_ms)
     wall = max_over_ranks(wall)
     value = args.steps / (dev_ms / 1e3)
@@ -211,42 +231,64 @@ def main():
 
     extra = {}
     if not args.no_extra:
-        # ---- prefill-only at each prompt length (fresh request, timed) ----
+        # ---- greedy single-stream decode (same prompt length) ----
+        greedy = SamplingParams(temperature=0.0, max_tokens=args.warmup + args.steps + 8,
+                                ignore_eos=True)
+        eng.add_request(rand_prompt(args.prompt_len), greedy, request_id="g0")
+        while eng.requests["g0"].num_computed_tokens < args.prompt_len:
+            eng.step()
+        for _ in range(args.warmup):
+            eng.step()
+        gms, _, _, _, _, _ = timed_steps(args.steps)
+        extra["greedy_decode_tok_s"] = round(args.steps / (max_over_ranks(gms) / 1e3), 2)
+        eng.abort_request("g0")
+        # ---- the config's 512-token sampled decode ----
+        if args.long_decode:
+            sp = SamplingParams(temperature=0.7, top_p=0.95, top_k=20, seed=11,
+                                max_tokens=args.long_decode, ignore_eos=True)
+            eng.add_request(rand_prompt(args.prompt_len), sp, request_id="l0")
+            while eng.requests["l0"].num_computed_tokens < args.prompt_len:
+                eng.step()
+            lms, lwall, ntok, _, _, n = timed_steps(0, until=eng.has_unfinished_requests)
+            extra["decode_tok_s@%dtok" % args.long_decode] = round(n / (max_over_ranks(lms) / 1e3), 2)
+        # ---- prefill-only at each prompt length (fresh request, device-timed) ----
         for L in pf_lens:
-            barrier()
             eng.add_request(rand_prompt(L), SamplingParams(temperature=0, max_tokens=1,
                                                            ignore_eos=True), f"pf{L}")
-            t1 = time.perf_counter()
-            while eng.has_unfinished_requests():
-                eng.step()
-            barrier()
-            pf = max_over_ranks(time.perf_counter() - t1)
-            extra["prefill_tok_s@%d" % L] = round(L / pf, 1)
+            pms, pwall, _, _, _, _ = timed_steps(0, until=eng.has_unfinished_requests)
+            pms = max_over_ranks(pms)
+            extra["prefill_tok_s@%d" % L] = round(L / (pms / 1e3), 1)
+            extra["prefill_e2e_tok_s@%d" % L] = round(L / max_over_ranks(pwall), 1)
             if L == args.prompt_len or len(pf_lens) == 1:
-                extra["prefill_vs_baseline"] = round(L / pf / BASELINE_PREFILL_TOKS, 2)
-        # ---- aggregate throughput at concurrency C (1k prompt, 64 output tokens each) ----
-        C = args.conc
-        sp = SamplingParams(temperature=0.7, top_p=0.95, top_k=20, max_tokens=64, ignore_eos=True)
-        for i in range(C):
-            eng.add_request(rand_prompt(1000), sp, f"c{i}")
-        while any(eng.requests[f"c{i}"].num_computed_tokens < 1000 for i in range(C)
-                  if f"c{i}" in eng.requests):
-            eng.step()
-        barrier()
-        t2 = time.perf_counter()
-        ntok = 0
-        while eng.has_unfinished_requests():
-            outs = eng.step()
-            ntok += sum(1 for _ in outs)
-        barrier()
-        dt = max_over_ranks(time.perf_counter() - t2)
-        extra["agg_decode_tok_s@conc%d" % C] = round(ntok / dt, 1)
-        extra["agg_vs_baseline"] = round(ntok / dt / BASELINE_CONC8_TOKS, 2)
+                extra["prefill_vs_baseline"] = round(L / (pms / 1e3) / BASELINE_PREFILL_TOKS, 2)
+        # ---- aggregate throughput at each concurrency (1k prompt, 256 output tokens each) ----
+        for C in concs:
+            sp = SamplingParams(temperature=0.7, top_p=0.95, top_k=20, max_tokens=args.conc_out,
+                                ignore_eos=True)
+            ids = [f"c{C}_{i}" for i in range(C)]
+            for rid in ids:
+                eng.add_request(rand_prompt(args.conc_prompt), sp, rid)
+            # the prompts' prefill is not in the decode aggregate
+            while any(eng.requests[r].num_computed_tokens < args.conc_prompt for r in ids
+                      if r in eng.requests):
+                eng.step()
+            cms, cwall, ntok, _, _, _ = timed_steps(0, until=eng.has_unfinished_requests)
+            extra["agg_decode_tok_s@conc%d" % C] = round(ntok / (max_over_ranks(cms) / 1e3), 1)
+            extra["agg_e2e_tok_s@conc%d" % C] = round(ntok / max_over_ranks(cwall), 1)
+            if C == 8:
+                extra["agg_vs_baseline"] = round(ntok / (max_over_ranks(cms) / 1e3) /
+                                                 BASELINE_CONC8_TOKS, 2)
+    tp_check = None
+    if world > 1 and not args.no_extra and not args.no_tp_check:
+        tp_lg = prompt_logits(eng, tp_check_prompt(eng))
+        eng.runner.graphs.clear()
+        eng = None                      # rank 0 builds a TP1 engine in its place
+        tp_check = tp_agreement(tp_lg, cfg, rank, dist)
 
     if rank == 0:
         line = {
             "metric": "single-stream decode tok/s (Qwen3.8-27B-shaped GDN hybrid, MXFP4 W4A8, fp8 KV, "
-                      "1.5k-token prompt)",
+                      "1.5k-token prompt, sampled T=0.7 top_p=0.95 top_k=20)",
             "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 3),
             "higher_is_better": True, "scaling": "strong",
@@ -254,6 +296,7 @@ def main():
             "data": "synthetic: uniform-random prompt token ids, random-init weights quantized to MXFP4 at load",
             "config": {"model": args.model, "global_batch": 1, "seq_len": args.prompt_len,
                        "parallelism": f"tp{world}", "kv_cache": "fp8_e4m3",
+                       "sampling": {"temperature": 0.7, "top_p": 0.95, "top_k": 20},
                        "l2": "inputs larger than L2 (each decode step streams ~9 GB of weights)"},
             "e2e": {"value": round(e2e, 2), "unit": "tok/s",
                     "h2d_bytes_per_step": h2d // args.steps, "d2h_bytes_per_step": d2h // args.steps},
@@ -264,11 +307,60 @@ def main():
             "load_s": round(load_s, 1),
             "extra": extra,
         }
+        if tp_check is not None:
+            line["tp_check"] = tp_check
         print(json.dumps(line), flush=True)
     if dist is not None:
-        eng.runner.graphs.clear()
+        if eng is not None:
+            eng.runner.graphs.clear()
         dist.barrier()
         dist.destroy_process_group()
+
+
+def tp_check_prompt(eng):
+    g = torch.Generator().manual_seed(99)
+    return torch.randint(3, eng.model_config.vocab_size, (512,), generator=g).tolist()
+
+
+def prompt_logits(e, prompt):
+    """Logits of the last prompt position (one full prefill through the engine)."""
+    from vllm_sly_radiance_b200.engine.request import SamplingParams
+    e.add_request(prompt, SamplingParams(temperature=0, max_tokens=1), "tpchk")
+    while True:
+        sched = e.scheduler.schedule()
+        res = e.runner.execute(sched, want_logits=True)
+        e.scheduler.update(sched, res.sampled)
+        if res.sampled:
+            return res.logits[-1].float().cpu()
+
+
+def tp_agreement(tp_lg, cfg, rank, dist):
+    """TP correctness at this N: the TP engine's last-prompt-position logits against a TP1 engine
+    that rank 0 builds from the same seed (after the TP engine is released)."""
+    import dataclasses
+    import gc
+    from vllm_sly_radiance_b200.engine.llm_engine import LLMEngine
+    dist.barrier()
+    out = None
+    if rank == 0:
+        gc.collect()
+        torch.cuda.empty_cache()
+        c1 = dataclasses.replace(cfg, tensor_parallel_size=1, num_kv_blocks=64, max_num_seqs=1,
+                                 enable_cuda_graphs=False, capture_graphs_at_start=False)
+        e1 = LLMEngine(c1)
+        ref_lg = prompt_logits(e1, tp_check_prompt(e1))
+        del e1
+        d = (tp_lg - ref_lg).abs()
+        out = {"vs": "tp1 engine, same seed, 512-token prompt, last position",
+               "max_abs_diff": round(float(d.max()), 4),
+               "rel_max_diff": round(float(d.max() / ref_lg.abs().max()), 5),
+               "top1_equal": bool(int(tp_lg.argmax()) == int(ref_lg.argmax())),
+               "top20_overlap": len(set(tp_lg.topk(20).indices.tolist()) &
+                                    set(ref_lg.topk(20).indices.tolist()))}
+        gc.collect()
+        torch.cuda.empty_cache()
+    dist.barrier()
+    return out
 
 
 def profiled_launches(eng, dump_path=None):

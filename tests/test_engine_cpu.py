@@ -174,7 +174,7 @@ def _first_step_logits(eng, prompt):
         for s in sched.seqs:
             if s.req.restore_snapshot is not None:
                 eng.model.copy_state(eng.caches, s.req.restore_snapshot, s.req.state_slot)
-                s.req.restore_snapshot = None
+                eng.kv.release_restore(s.req)
         res = eng.runner.execute(sched, want_logits=True)
         eng.scheduler.update(sched, res.sampled)
         if res.sampled:
@@ -260,3 +260,100 @@ def test_arc_policy_prefers_frequent_items():
             resident.add(k)
         assert ("hot" in p) == survives, cls
         assert len(p) <= 4 and resident == {k for k in resident if k in p}
+
+
+def _snap_manager(num_blocks=64):
+    return KVCacheManager(num_blocks, 16, 4, enable_prefix_caching=True, num_snapshots=1)
+
+
+def _cache_prefix(kv, tokens):
+    """Publish `tokens`' full blocks and a GDN snapshot at its last block boundary (what a
+    finished prefill leaves behind)."""
+    r = Request(tokens, SamplingParams(temperature=0, max_tokens=1))
+    assert kv.allocate(r, len(tokens))
+    r.num_computed_tokens = (len(tokens) - 1) // 16 * 16
+    sid = kv.take_snapshot(r)
+    assert sid is not None
+    r.num_computed_tokens = len(tokens)
+    kv.register_blocks(r)
+    kv.free(r)
+    return sid
+
+
+def test_pending_snapshot_restore_is_pinned():
+    """A waiting request whose admission failed after a prefix hit keeps its snapshot slot: other
+    prefills that reserve snapshots meanwhile cannot recycle it (one snapshot slot)."""
+    kv = _snap_manager()
+    a = list(range(100, 150))
+    sid = _cache_prefix(kv, a)
+    b = Request(a + [7, 8, 9], SamplingParams(temperature=0, max_tokens=1))
+    assert kv.match_prefix(b) == 48 and b.restore_snapshot == sid
+    kv.adopt_prefix(b, 48)
+    # another prompt reaches its snapshot point while b still waits: no slot may be taken
+    c = Request(list(range(300, 340)), SamplingParams(temperature=0, max_tokens=1))
+    assert kv.allocate(c, 40)
+    c.num_computed_tokens = 32
+    assert kv.take_snapshot(c) is None
+    assert kv.snap_lru[sid] == kv._hashes(a[:48])[-1]      # b's snapshot untouched
+    # the restore copy is issued: the slot becomes reusable
+    kv.release_restore(b)
+    assert kv.take_snapshot(c) == sid
+
+
+def test_aborted_restore_unpins_snapshot():
+    kv = _snap_manager()
+    a = list(range(100, 150))
+    sid = _cache_prefix(kv, a)
+    b = Request(a + [7], SamplingParams(temperature=0, max_tokens=1))
+    assert kv.match_prefix(b) == 48
+    kv.adopt_prefix(b, 48)
+    assert kv.snap_pins == {sid: 1}
+    kv.free(b)                               # abort / preemption path
+    assert kv.snap_pins == {} and b.restore_snapshot is None
+
+
+class _FakeTier:
+    """Offload stand-in: holds one GDN snapshot (hash `h`) and any KV blocks."""
+
+    def __init__(self, h):
+        self.h = h
+        self.restored = 0
+
+    def has_block(self, h):
+        return False
+
+    def has_state(self, h):
+        return h == self.h
+
+    def restore_state(self, h, reserve):
+        sid = reserve()
+        assert sid is not None
+        self.restored += 1
+        return sid
+
+    def save_state(self, h, sid):
+        pass
+
+
+def test_tier_restore_skips_when_every_snapshot_slot_is_pinned():
+    """A tier snapshot is only brought back when a snapshot slot can be reserved without
+    recycling one that a pending restore pins (two requests in the same schedule)."""
+    kv = _snap_manager()
+    a = list(range(100, 150))
+    sid = _cache_prefix(kv, a)
+    b = Request(a + [1], SamplingParams(temperature=0, max_tokens=1))
+    assert kv.match_prefix(b) == 48                # pins the only slot
+    other = list(range(500, 550))
+    r = Request(other, SamplingParams(temperature=0, max_tokens=1))
+    assert kv.allocate(r, 50)
+    r.num_computed_tokens = 50
+    kv.register_blocks(r)
+    kv.free(r)
+    tier = _FakeTier(kv._hashes(other[:48])[-1])
+    kv.offload = tier
+    kv.flush_offload = lambda: None
+    c = Request(other + [2], SamplingParams(temperature=0, max_tokens=1))
+    assert kv.match_prefix(c) == 0 and tier.restored == 0 and c.restore_snapshot is None
+    assert kv.snap_lru[sid] == kv._hashes(a[:48])[-1]
+    kv.release_restore(b)
+    assert kv.match_prefix(c) == 48 and tier.restored == 1 and c.restore_snapshot == sid

@@ -77,6 +77,55 @@ def test_mxfp4_gemm_fused_producer(mode, M, N, Kd, with_res):
     assert rel_err(out, want) < 1e-2, rel_err(out, want)
 
 
+@pytest.mark.parametrize("M,N,Kd", [(1, 256, 256), (1, 5120, 6144), (3, 16480, 5120),
+                                     (16, 5120, 8704), (1, 5120, 1088), (8, 2176, 1088),
+                                     (1, 248320, 5120), (5, 200, 768), (2, 96, 128)])
+def test_mxfp4_gemv(M, N, Kd):
+    """Persistent stream-K decode GEMM against the fp32 product: tiles whose K range spans
+    several CTAs are reduced in-kernel; two launches in a row check the counter resets."""
+    g = torch.Generator().manual_seed(M * 13 + N + Kd)
+    wq = MXFP4Weight.from_float(torch.randn(N, Kd, generator=g) * 0.02)
+    wg = wq.to(DEV)
+    for rep in range(2):
+        x = torch.randn(M, Kd, generator=g)
+        q, s = ref.quant_fp8_rows(x.to(torch.bfloat16))
+        want = ref.mxfp4_linear(q, s, wq.packed, wq.scales)
+        got = K.mxfp4_gemv(q.to(DEV), s.to(DEV), wg)
+        torch.cuda.synchronize()
+        K.check_status(got.device)
+        assert rel_err(got, want) < 1e-2, (rep, rel_err(got, want))
+
+
+@pytest.mark.parametrize("mode,M,N,Kd,with_res", [
+    (1, 1, 5120, 6144, True), (1, 4, 5120, 8704, True), (1, 1, 2048, 1088, False),
+    (2, 1, 17408, 5120, False), (2, 3, 4352, 5120, False), (2, 16, 768, 256, False)])
+def test_mxfp4_gemv_finisher(mode, M, N, Kd, with_res):
+    """The finisher of the last tile (residual add + RMSNorm + e4m3, or SiLU * mul + e4m3) equals
+    the stand-alone producer applied to the GEMM output."""
+    g = torch.Generator().manual_seed(M * 5 + N + mode)
+    wq = MXFP4Weight.from_float(torch.randn(N, Kd, generator=g) * 0.02).to(DEV)
+    x = torch.randn(M, Kd, generator=g).to(torch.bfloat16).to(DEV)
+    q, s = K.quant_fp8(x)
+    for rep in range(2):
+        if mode == 1:
+            res = torch.randn(M, N, generator=g).to(torch.bfloat16).to(DEV) if with_res else None
+            lw = (0.1 * torch.randn(N, generator=g)).to(torch.bfloat16).to(DEV)
+            ro = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
+            out, fq, fs = K.mxfp4_gemv(q, s, wq, None, K.FIN_NORM, res, lw, ro, 1e-6)
+            wq_, ws_, wr = K.add_rms_quant(out, res, lw, 1e-6)
+            torch.cuda.synchronize()
+            assert torch.equal(ro, wr)
+        else:
+            out, fq, fs = K.mxfp4_gemv(q, s, wq, None, K.FIN_SILU)
+            wq_, ws_ = K.silu_mul_quant(out)
+            torch.cuda.synchronize()
+        K.check_status(out.device)
+        torch.testing.assert_close(fs, ws_, rtol=1e-5, atol=0)
+        assert fp8_close(fq, fs, wq_, ws_)
+        want = K.mxfp4_gemm(q, s, wq.packed, wq.sf, wq.scales, N)
+        assert rel_err(out, want) < 1e-2
+
+
 @pytest.mark.parametrize("M,N,Kd", [(1, 248320 // 8, 5120), (3, 5120, 8704), (8, 1000, 1024),
                                      (40, 2176, 1024), (2, 96, 128), (12, 1000, 256),
                                      (5, 17408, 5120)])
@@ -253,6 +302,29 @@ def test_paged_attention_decode_kernel(D, Hq, Hkv, ctx_lens, splits, fmt, monkey
     assert rel_err(got, general) < 1e-2, rel_err(got, general)
 
 
+@pytest.mark.parametrize("Hq,Hkv,ctx_lens,splits", [(24, 4, [1500], 8), (24, 4, [300, 2000, 64], 1),
+                                                   (6, 1, [700, 4000], 5)])
+def test_paged_attention_decode_gated(Hq, Hkv, ctx_lens, splits):
+    """Decode attention with the o_proj producer inside (sigmoid gate + per-token e4m3 by the last
+    kv-head CTA of each token) against attention followed by gate_mul_quant, twice in a row."""
+    torch.manual_seed(9)
+    D, bs = 256, 64
+    q_lens = [1] * len(ctx_lens)
+    meta, nblocks = _attn_meta(q_lens, ctx_lens, bs, Hq, Hkv, splits, DEV)
+    kc = (torch.randn(nblocks, Hkv, bs, D) * 0.5).to(torch.float8_e4m3fn).to(DEV)
+    vc = torch.randn(nblocks, Hkv, bs, D).to(torch.float8_e4m3fn).to(DEV)
+    T = len(ctx_lens)
+    for rep in range(2):
+        q = ref.fp8_e4m3(torch.randn(T, Hq, D)).to(torch.bfloat16).to(DEV)
+        qkv = torch.randn(T, Hq * 2 * D + 64).to(torch.bfloat16).to(DEV)
+        gq, gs = K.paged_attention_gated(q, kc, vc, meta, D ** -0.5, qkv[:, D:], 2 * D)
+        a = K.paged_attention(q, kc, vc, meta, D ** -0.5).view(T, -1)
+        wq, ws_ = K.gate_mul_quant(a, qkv[:, D:], D, 2 * D)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(gs, ws_, rtol=1e-6, atol=0)
+        assert torch.equal(gq.view(torch.uint8), wq.view(torch.uint8)), rep
+
+
 @pytest.mark.parametrize("lens,has_init,sdt,split", [
     ([1500], [0], torch.float32, 0), ([64, 1, 200, 7], [1, 1, 0, 1], torch.float32, 1),
     ([130, 65], [1, 0], torch.bfloat16, 2), ([300], [1], torch.float32, 4)])
@@ -339,6 +411,45 @@ def test_gdn_decode_fused_matches_separate(B, Hk, Hv, sdt, init, split):
     assert rel_err(got, want) < 1e-2, rel_err(got, want)
     assert rel_err(s1.float(), s2.float()) < 1e-2
     assert torch.equal(c1, c2)
+
+
+@pytest.mark.parametrize("B,Hk,Hv,sdt", [(1, 16, 48, torch.float32), (4, 4, 12, torch.float32),
+                                         (3, 4, 4, torch.bfloat16)])
+def test_gdn_decode_fused_quant(B, Hk, Hv, sdt):
+    """The decode step with the out_proj producer inside (per-head gated RMSNorm in the head's
+    CTA, per-row e4m3 by the last head CTA) against the step followed by gdn_norm_quant; two
+    launches in a row (the per-row counters reset)."""
+    torch.manual_seed(12)
+    D = 128
+    key_dim, vdim = Hk * D, Hv * D
+    C = 2 * key_dim + vdim
+    ncol = C + vdim + 2 * Hv + 8
+    conv_w = (0.4 * torch.randn(C, 4)).to(torch.bfloat16).to(DEV)
+    A_log = torch.log(torch.rand(Hv) * 8 + 0.5).to(DEV)
+    dt_bias = (torch.randn(Hv) * 0.3).to(DEV)
+    norm_w = (1 + 0.1 * torch.randn(D)).to(torch.bfloat16).to(DEV)
+    meta = _Meta()
+    meta.query_start_loc = torch.arange(B + 1, dtype=torch.int32, device=DEV)
+    meta.state_slots = torch.arange(1, B + 1, dtype=torch.int32, device=DEV)
+    meta.has_initial = torch.ones(B, dtype=torch.int32, device=DEV)
+    meta.token_seq = torch.arange(B, dtype=torch.int32, device=DEV)
+    meta.num_seqs = meta.num_tokens = B
+    meta.commit_len = None
+    scale = D ** -0.5
+    ba_off = C + vdim
+    conv0 = (0.5 * torch.randn(B + 1, C, 3)).to(torch.bfloat16).to(DEV)
+    ssm0 = (torch.randn(B + 1, Hv, D, D) * 0.05).to(sdt).to(DEV)
+    c1, s1, c2, s2 = conv0.clone(), ssm0.clone(), conv0.clone(), ssm0.clone()
+    for rep in range(2):
+        x = (torch.randn(B, ncol) * 0.7).to(torch.bfloat16).to(DEV)
+        q, qs = K.gdn_decode_fused_quant(x, ba_off, C, conv_w, c1, s1, A_log, dt_bias, meta, Hk,
+                                         scale, norm_w, 1e-6)
+        o = K.gdn_decode_fused(x, ba_off, conv_w, c2, s2, A_log, dt_bias, meta, Hk, scale, split=1)
+        wq, wqs = K.gdn_norm_quant(o, x[:, C:C + vdim], norm_w, 1e-6, D)
+        torch.cuda.synchronize()
+        assert torch.equal(c1, c2) and torch.equal(s1, s2), rep
+        torch.testing.assert_close(qs, wqs, rtol=1e-5, atol=0)
+        assert fp8_close(q, qs, wq, wqs), rep
 
 
 def test_qkv_prologue():
@@ -434,6 +545,64 @@ def test_argmax_and_sampling():
     # probabilities of the kept window sum to one for sampled rows
     for b in (1, 2, 4):
         assert abs(float(probs[b].sum()) - 1.0) < 1e-4
+
+
+@pytest.mark.parametrize("B,V,dtype", [(1, 248320, torch.bfloat16), (5, 248320, torch.float32),
+                                      (3, 4096, torch.bfloat16), (2, 5000, torch.float32)])
+def test_topk_window_matches_sorted_prefix(B, V, dtype):
+    """The top-64 window kernel equals the first 64 entries of a stable descending sort (ties
+    at equal values keep the lowest column), on two launches in a row (counters reset)."""
+    for rep in range(2):
+        g = torch.Generator().manual_seed(B * 31 + V + rep)
+        x = torch.randn(B, V, generator=g).to(dtype)       # bf16 rows hold many ties
+        vals, ids = K.topk_window(x.to(DEV))
+        torch.cuda.synchronize()
+        nv, ni = torch.sort(-x.float(), dim=-1, stable=True)
+        assert torch.equal(vals.cpu(), -nv[:, :64])
+        assert torch.equal(ids.cpu(), ni[:, :64])
+
+
+def test_topk_fused_draw_equals_window_draw():
+    """The draw fused into the window kernel is the per-row window draw of sample_from_topk."""
+    torch.manual_seed(5)
+    B = 6
+    x = torch.randn(B, 248320).to(torch.bfloat16).to(DEV)
+    temp = torch.tensor([0.0, 0.7, 1.0, 0.7, 0.7, 1.3], device=DEV)
+    topk = torch.tensor([20, 20, 64, 1, 64, 5], dtype=torch.int32, device=DEV)
+    topp = torch.tensor([0.95, 0.95, 1.0, 0.9, 0.5, 0.8], device=DEV)
+    minp = torch.tensor([0.0, 0.0, 0.05, 0.0, 0.0, 0.0], device=DEV)
+    seeds = torch.arange(B, dtype=torch.int64, device=DEV) * 7
+    for step in (0, 3):
+        toks, probs, ids = K.topk_sample(x, temp, topk, topp, minp, seeds, step, want_probs=True)
+        vals, ids2 = K.topk_window(x)
+        want, wprobs = K.sample_from_topk(vals, ids2, temp, topk, topp, minp, seeds, step,
+                                          want_probs=True)
+        torch.cuda.synchronize()
+        assert torch.equal(ids.cpu(), ids2.cpu())
+        assert torch.equal(toks.cpu(), want.cpu())
+        assert torch.allclose(probs.cpu(), wprobs.cpu(), atol=1e-6)
+    assert int(toks[0]) == int(x[0].float().argmax())
+
+
+def test_full_vocab_sampling_distribution():
+    """top_k disabled: rows are drawn over the whole vocabulary (sorted row + the same draw);
+    the empirical distribution matches softmax, mass beyond the top 64 included."""
+    from vllm_sly_radiance_b200.engine.sampler import SamplingTensors, sample
+    V, N = 4096, 8000
+    g = torch.Generator().manual_seed(1)
+    row = torch.randn(V, generator=g) * 0.2
+    st = SamplingTensors(torch.ones(N, device=DEV), torch.zeros(N, dtype=torch.int32, device=DEV),
+                         torch.ones(N, device=DEV), torch.zeros(N, device=DEV),
+                         torch.arange(N, dtype=torch.int64, device=DEV) * 13 + 1, False, False, True)
+    toks, _, _ = sample(row[None].expand(N, V).contiguous().to(DEV), st, 0)
+    emp = torch.bincount(toks.cpu(), minlength=V).double() / N
+    want = torch.softmax(row.double(), 0)
+    order = torch.argsort(row, descending=True)
+    assert abs(float(emp[order[64:]].sum()) - float(want[order[64:]].sum())) < 0.03
+    # coarse bins of 64 ranks: per-bin mass within sampling noise
+    eb = emp[order].view(64, 64).sum(1)
+    wb = want[order].view(64, 64).sum(1)
+    assert float((eb - wb).abs().max()) < 0.02
 
 
 @pytest.mark.parametrize("D,Hq,Hkv,splits", [(64, 4, 2, 5), (256, 24, 4, 8)])

@@ -6,7 +6,9 @@ set larger than the 126 MB L2).  Usage:
     python -m vllm_sly_radiance_b200.benchmarks.kernels w4a16 [--m 1,8 --shape lm_head,62080x5120]
 
 Prints one JSON line per case with time, achieved bandwidth / FLOP rate and the fraction of the
-measured peaks in MEASURED_PEAKS.json (fallback 6.65 TB/s, 1.59 PFLOP/s).
+measured peaks in MEASURED_PEAKS.json (fallback 6.65 TB/s, 1.59 PFLOP/s).  The W4A8 GEMMs run
+tcgen05.mma.kind::mxf8f6f4 (e2m1 x e4m3 with UE8M0 block scales), which issues at the fp8 tensor
+rate -- twice the bf16 rate -- so their compute fraction divides by 2x the measured bf16 GEMM.
 Reference analogue: sly/mxfp4/bench_{decode,prefill}_cells.py (DRAM-cold weight rotation)."""
 from __future__ import annotations
 
@@ -65,6 +67,7 @@ def timeit(fn, iters=None, warmup=5):
 
 def bench_gemm(ms, shapes):
     bw, fl, src = peaks()
+    fp8_peak = 2 * fl          # kind::mxf8f6f4 issues at the fp8 rate
     for (N, Kd, name) in shapes:
         nrot = max(2, int(300e6 // (N * Kd // 2)) + 1)       # > 2x L2 of weights
         ws = [MXFP4Weight.from_float(torch.randn(N, Kd, device="cuda") * 0.02) for _ in range(nrot)]
@@ -72,18 +75,22 @@ def bench_gemm(ms, shapes):
             x = torch.randn(M, Kd, device="cuda").to(torch.bfloat16)
             q, s = K.quant_fp8(x)
             out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
-
-            def fn(i):
-                w = ws[i % nrot]
-                K.mxfp4_gemm(q, s, w.packed, w.sf, w.scales, N, out=out)
-            t = timeit(fn)
-            byts = N * Kd // 2 + N * Kd // 32 + M * Kd + M * N * 2
-            flops = 2.0 * M * N * Kd
-            print(json.dumps({"kernel": "mxfp4_gemm", "shape": name, "M": M, "N": N, "K": Kd,
-                              "us": round(t * 1e6, 2), "GBps": round(byts / t / 1e9, 1),
-                              "TFLOPs": round(flops / t / 1e12, 1),
-                              "frac_hbm": round(byts / t / bw, 3),
-                              "frac_bf16_peak": round(flops / t / fl, 3), "peaks": src}), flush=True)
+            variants = [("mxfp4_gemm", lambda w: K.mxfp4_gemm(q, s, w.packed, w.sf, w.scales, N,
+                                                               out=out))]
+            if M <= K.GEMV_MAX_ROWS:
+                variants.append(("mxfp4_gemv", lambda w: K.mxfp4_gemv(q, s, w, out)))
+            for kname, call in variants:
+                def fn(i, call=call):
+                    call(ws[i % nrot])
+                t = timeit(fn)
+                byts = N * Kd // 2 + N * Kd // 32 + M * Kd + M * N * 2
+                flops = 2.0 * M * N * Kd
+                print(json.dumps({"kernel": kname, "shape": name, "M": M, "N": N, "K": Kd,
+                                  "us": round(t * 1e6, 2), "GBps": round(byts / t / 1e9, 1),
+                                  "TFLOPs": round(flops / t / 1e12, 1),
+                                  "frac_hbm": round(byts / t / bw, 3),
+                                  "frac_fp8_tensor_peak": round(flops / t / fp8_peak, 3),
+                                  "peaks": src + " (fp8 tensor = 2x measured bf16)"}), flush=True)
 
 
 class _AttnMeta:

@@ -17,13 +17,18 @@
 // vocabulary size fits).  Calls outside those limits are rejected with an error message; nothing
 // is launched.
 //
-// Set-up: the first call on each device, with that device current, resolves the scratch address
-// with cudaGetSymbolAddress and caches it for that device.  Make that first call before any
-// stream capture begins.
+// Set-up: the first call in each CUDA context (the runtime's primary context of a device, or a
+// context the caller created with the driver API), with that context current, resolves the
+// scratch address with cudaGetSymbolAddress and caches it for that context: a device address is
+// only valid in the context it was resolved in.  Make that first call before any stream capture
+// begins.  The C declaration and the limits are in radiance_noalloc.h; the file is built both
+// into the torch extension and, alone, into libradiance_noalloc.so, which links only the CUDA
+// runtime.
 //
 // Concurrency: the scratch is one per device, so calls that overlap on the same device (two host
 // threads, or two streams whose launches run at the same time) race on it and may return wrong
 // tokens.  Serialise calls per device, e.g. by issuing them all on one stream.
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
@@ -32,12 +37,14 @@
 
 #include <mutex>
 
+#include "radiance_noalloc.h"
+
 namespace rad {
 namespace noalloc {
 
-constexpr int kNoAllocMaxRows = 1024;
-constexpr int kNoAllocMaxChunks = 64;
-constexpr int kMaxDevices = 64;
+constexpr int kNoAllocMaxRows = RADIANCE_NOALLOC_MAX_ROWS;
+constexpr int kNoAllocMaxChunks = RADIANCE_NOALLOC_MAX_CHUNKS;
+constexpr int kMaxContexts = RADIANCE_NOALLOC_MAX_CONTEXTS;
 constexpr int kThreads = 256;
 
 struct ArgmaxScratch {
@@ -108,8 +115,27 @@ __global__ void __launch_bounds__(kThreads) argmax_static_kernel(
   }
 }
 
+// scratch address per CUDA context (fixed table: the set-up allocates nothing, host or device)
 std::mutex g_setup_mu;
-ArgmaxScratch* g_scratch_ptr[kMaxDevices] = {};
+CUcontext g_ctx[kMaxContexts] = {};
+ArgmaxScratch* g_ctx_scratch[kMaxContexts] = {};
+int g_num_ctx = 0;
+
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+
+// the current context through the runtime's driver entry-point query (no link to libcuda)
+cudaError_t current_context(CUcontext* ctx) {
+  static CtxGetCurrentFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q);
+    if (e != cudaSuccess) return e;
+    if (q != cudaDriverEntryPointSuccess || !p) return cudaErrorNotSupported;
+    fn = reinterpret_cast<CtxGetCurrentFn>(p);
+  }
+  return fn(ctx) == CUDA_SUCCESS ? cudaSuccess : cudaErrorContextIsDestroyed;
+}
 
 int fail(char* err, int err_len, int code, const char* msg) {
   if (err && err_len > 0) snprintf(err, (size_t)err_len, "%s", msg);
@@ -119,9 +145,9 @@ int fail(char* err, int err_len, int code, const char* msg) {
 }  // namespace noalloc
 }  // namespace rad
 
-// Returns 0 on success.  On failure returns a nonzero code (a cudaError_t value for CUDA
-// failures, -1 for a rejected argument) and writes a message into err[0:err_len) when err is
-// non-null.
+// Declared in radiance_noalloc.h.  Returns 0 on success.  On failure returns a nonzero code (a
+// cudaError_t value for CUDA failures, -1 for a rejected argument) and writes a message into
+// err[0:err_len) when err is non-null.
 //   logits   : device pointer, rows x vocab, row stride ld elements; dtype 0 = bf16, 1 = fp32
 //   out_ids  : device int64 [rows]; out_vals: device fp32 [rows] or null
 //   stream   : cudaStream_t to launch on (null = legacy default stream)
@@ -141,8 +167,8 @@ extern "C" int radiance_argmax_rows_noalloc(const void* logits, int dtype, int r
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(err, err_len, (int)e, cudaGetErrorString(e));
-  if (dev < 0 || dev >= kMaxDevices)
-    return fail(err, err_len, -1, "radiance_argmax_rows_noalloc: device ordinal above 63");
+  // cudaGetDevice / cudaPointerGetAttributes make the primary context current when none is
+  CUcontext ctx = nullptr;
   cudaPointerAttributes attr;
   e = cudaPointerGetAttributes(&attr, logits);
   if (e != cudaSuccess) return fail(err, err_len, (int)e, cudaGetErrorString(e));
@@ -150,16 +176,27 @@ extern "C" int radiance_argmax_rows_noalloc(const void* logits, int dtype, int r
     return fail(err, err_len, -1,
                 "radiance_argmax_rows_noalloc: logits must be device memory of the current device");
 
+  e = current_context(&ctx);
+  if (e != cudaSuccess || !ctx)
+    return fail(err, err_len, e != cudaSuccess ? (int)e : -1,
+                "radiance_argmax_rows_noalloc: no current CUDA context");
+
   ArgmaxScratch* scratch = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_setup_mu);
-    if (!g_scratch_ptr[dev]) {
+    for (int c = 0; c < g_num_ctx; ++c)
+      if (g_ctx[c] == ctx) scratch = g_ctx_scratch[c];
+    if (!scratch) {
+      if (g_num_ctx == kMaxContexts)
+        return fail(err, err_len, -1, "radiance_argmax_rows_noalloc: more than 64 CUDA contexts");
       void* p = nullptr;
       e = cudaGetSymbolAddress(&p, g_argmax_scratch);
       if (e != cudaSuccess) return fail(err, err_len, (int)e, cudaGetErrorString(e));
-      g_scratch_ptr[dev] = static_cast<ArgmaxScratch*>(p);
+      scratch = static_cast<ArgmaxScratch*>(p);
+      g_ctx[g_num_ctx] = ctx;
+      g_ctx_scratch[g_num_ctx] = scratch;
+      ++g_num_ctx;
     }
-    scratch = g_scratch_ptr[dev];
   }
 
   // about 4096 logits per CTA, at most kNoAllocMaxChunks CTAs per row

@@ -598,7 +598,21 @@ DEVI uint32_t e4m3x2_to_f16x2(uint16_t v) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-template <int D, int FMT>
+// The o_proj producer fused into decode attention (GQ): once the Hkv CTAs that write a token's
+// heads are done (self-resetting per-token counter), the last one applies the sigmoid output
+// gate to the token's row -- y = bf16(o / (1 + e^-gate)), the numerics of gate_mul_quant -- and
+// quantises it to e4m3 with the per-token scale.  One token per tile (pure decode).
+struct AttnGateArgs {
+  const __nv_bfloat16* gate;    // gate of head h, column c: gate[tok * ldg + h * ghs + c]
+  int ldg;
+  int ghs;
+  unsigned* tok_cnt;            // [T] arrival counters (zero, self-resetting)
+  uint8_t* q;                   // [T, Hq * D] e4m3
+  int ldq;
+  float* q_scale;               // [T]
+};
+
+template <int D, int FMT, bool GQ = false>
 __global__ void __launch_bounds__(128) paged_attn_decode_kernel(
     const __nv_bfloat16* __restrict__ q, const uint8_t* __restrict__ k_cache,
     const uint8_t* __restrict__ v_cache, const int* __restrict__ block_tables, int bt_stride,
@@ -606,7 +620,7 @@ __global__ void __launch_bounds__(128) paged_attn_decode_kernel(
     const int* __restrict__ tile_seq, const int* __restrict__ tile_row0, int Hq, int Hkv,
     int block_size, float scale_log2, int causal, int window, int num_splits,
     __nv_bfloat16* __restrict__ out, float* __restrict__ part_o, float* __restrict__ part_ml,
-    int T, unsigned* __restrict__ counters) {
+    int T, unsigned* __restrict__ counters, const AttnGateArgs ga) {
   pdl_wait();     // inputs come from the preceding kernel
   pdl_trigger();
   constexpr bool F16 = (FMT == 1);
@@ -1030,6 +1044,54 @@ __global__ void __launch_bounds__(128) paged_attn_decode_kernel(
     }
     if (threadIdx.x == 0) counters[tile * Hkv + hk] = 0;
   }
+  if constexpr (GQ) {
+    // this CTA wrote the G heads of kv head hk for token s0 (one token per tile)
+    const int tok = s0;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      s_last = atomicAdd(&ga.tok_cnt[tok], 1u) == (unsigned)(Hkv - 1);
+      if (s_last) ga.tok_cnt[tok] = 0u;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    // the token's whole row (Hq heads): gate, amax, e4m3
+    float* buf = reinterpret_cast<float*>(smem);          // Hq * D floats (fits the K/V tiles)
+    const int H = Hq * D;
+    float am = 0.f;
+    for (int v = threadIdx.x; v < H / 8; v += 128) {
+      const int e = v * 8, h = e / D, c = e % D;
+      const uint4 ou = __ldcg(reinterpret_cast<const uint4*>(out + (size_t)tok * H + e));
+      const uint4 gu = *reinterpret_cast<const uint4*>(ga.gate + (size_t)tok * ga.ldg +
+                                                       (size_t)h * ga.ghs + c);
+      const __nv_bfloat162* oh = reinterpret_cast<const __nv_bfloat162*>(&ou);
+      const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&gu);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 of = __bfloat1622float2(oh[j]), gf = __bfloat1622float2(gh[j]);
+        const float y0 = bf16_round(of.x / (1.f + __expf(-gf.x)));
+        const float y1 = bf16_round(of.y / (1.f + __expf(-gf.y)));
+        buf[e + 2 * j] = y0;
+        buf[e + 2 * j + 1] = y1;
+        am = fmaxf(am, fmaxf(fabsf(y0), fabsf(y1)));
+      }
+    }
+    am = warp_max(am);
+    if (lane == 0) s_fin[warp][0] = am;
+    __syncthreads();
+    am = fmaxf(fmaxf(s_fin[0][0], s_fin[1][0]), fmaxf(s_fin[2][0], s_fin[3][0]));
+    const float qs = fmaxf(am / 448.f, 1.f / (448.f * 512.f));
+    const float inv = 1.f / qs;
+    for (int v = threadIdx.x; v < H / 8; v += 128) {
+      uint2 qq;
+      uint16_t* q16 = reinterpret_cast<uint16_t*>(&qq);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) q16[j] = f32x2_to_e4m3x2(buf[v * 8 + 2 * j] * inv, buf[v * 8 + 2 * j + 1] * inv);
+      *reinterpret_cast<uint2*>(ga.q + (size_t)tok * ga.ldq + v * 8) = qq;
+    }
+    if (threadIdx.x == 0) ga.q_scale[tok] = qs;
+  }
 }
 
 // merge split partials: one warp per (token, head)
@@ -1103,13 +1165,17 @@ C10_CUDA_CHECK(launch_pdl((attn::qkv_prologue_kernel<Dc>), dim3(grid), dim3(256)
 }
 
 // q [T, Hq, D] bf16; caches [blocks, Hkv, block_size(=64k), D]; tile_seq/tile_row0 [num_tiles];
-// part_o [splits, T, Hq, D] fp32 and part_ml [splits, T, Hq, 2] (used when num_splits > 1)
+// part_o [splits, T, Hq, D] fp32 and part_ml [splits, T, Hq, 2] (used when num_splits > 1).
+// With gq defined (decode kernel, one token per tile): the o_proj producer runs in the same
+// launch -- gate [T, *] bf16 (head h at column h * gate_head_stride), gate_cnt int32 [T] zero
+// counters, gq e4m3 [T, Hq * D] and gq_scale [T] receive the gated, quantised rows.
 void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                      torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor qsl,
                      torch::Tensor tile_seq, torch::Tensor tile_row0, double scale, bool causal,
                      int64_t window, int64_t num_splits, torch::Tensor part_o,
                      torch::Tensor part_ml, torch::Tensor out, torch::Tensor counters,
-                     bool decode) {
+                     bool decode, torch::Tensor gate, int64_t gate_head_stride,
+                     torch::Tensor gate_cnt, torch::Tensor gq, torch::Tensor gq_scale) {
   const int T = q.size(0), Hq = q.size(1), D = q.size(2);
   const int Hkv = k_cache.size(1), block_size = k_cache.size(2);
   const int num_tiles = tile_seq.size(0);
@@ -1120,6 +1186,26 @@ void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
               "num_splits must be in [1, 32] (decode kernel: [1, 128])");
   const int fmt = k_cache.scalar_type() == at::kFloat8_e4m3fn ? 1
                 : k_cache.scalar_type() == at::kByte ? 2 : 0;
+  const bool gated = gq.defined() && gq.numel();
+  attn::AttnGateArgs ga{};
+  if (gated) {
+    TORCH_CHECK(decode, "paged_attention: the fused gate needs the decode kernel");
+    TORCH_CHECK(out.is_contiguous() && (int64_t)Hq * D * 4 <= (16 + 2 * attn::BC) * D * 2,
+                "paged_attention: fused gate row");
+    TORCH_CHECK(gate.scalar_type() == at::kBFloat16 && gate.stride(1) == 1 && gate.stride(0) % 8 == 0 &&
+                    gate_head_stride % 8 == 0 &&
+                    (reinterpret_cast<uintptr_t>(gate.data_ptr()) % 16) == 0, "paged_attention: gate");
+    TORCH_CHECK(gq.scalar_type() == at::kFloat8_e4m3fn && gq.stride(1) == 1 && gq.stride(0) % 8 == 0 &&
+                    gq.size(1) >= Hq * D, "paged_attention: gq");
+    TORCH_CHECK(gate_cnt.numel() >= T && gq_scale.numel() >= T, "paged_attention: gate counters");
+    ga.gate = (const __nv_bfloat16*)gate.data_ptr();
+    ga.ldg = (int)gate.stride(0);
+    ga.ghs = (int)gate_head_stride;
+    ga.tok_cnt = reinterpret_cast<unsigned*>(gate_cnt.data_ptr<int>());
+    ga.q = (uint8_t*)gq.data_ptr();
+    ga.ldq = (int)gq.stride(0);
+    ga.q_scale = gq_scale.data_ptr<float>();
+  }
   const at::cuda::CUDAGuard guard(q.device());
   auto stream = at::cuda::getCurrentCUDAStream();
   const float scale_log2 = (float)(scale * 1.4426950408889634);
@@ -1129,22 +1215,38 @@ void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
     constexpr int F8 = decltype(ftag)::value;
     // decode: tiles hold at most 16 query rows (the caller guarantees G * q_len <= 16)
     const int smem = ((decode ? 16 : attn::BR) + 2 * attn::BC) * Dc * 2;
-    auto kern = decode ? attn::paged_attn_decode_kernel<Dc, F8> : attn::paged_attn_kernel<Dc, F8>;
-    static bool set_general = false, set_decode = false;
-    bool& set = decode ? set_decode : set_general;
-    if (!set) {
-      C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      set = true;
+    const __nv_bfloat16* qp = (const __nv_bfloat16*)q.data_ptr();
+    const uint8_t* kp = (const uint8_t*)k_cache.data_ptr();
+    const uint8_t* vp = (const uint8_t*)v_cache.data_ptr();
+    float* po = num_splits > 1 ? part_o.data_ptr<float>() : nullptr;
+    float* pm = num_splits > 1 ? part_ml.data_ptr<float>() : nullptr;
+    unsigned* cn = num_splits > 1 ? reinterpret_cast<unsigned*>(counters.data_ptr()) : nullptr;
+    if (decode) {
+      auto kern = gated ? attn::paged_attn_decode_kernel<Dc, F8, true>
+                        : attn::paged_attn_decode_kernel<Dc, F8, false>;
+      static bool set[2] = {false, false};
+      if (!set[gated]) {
+        C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        set[gated] = true;
+      }
+      C10_CUDA_CHECK(launch_pdl(kern, dim3(grid), dim3(128), smem, stream, qp, kp, vp,
+          block_tables.data_ptr<int>(), block_tables.stride(0), seq_lens.data_ptr<int>(),
+          qsl.data_ptr<int>(), tile_seq.data_ptr<int>(), tile_row0.data_ptr<int>(), Hq, Hkv,
+          block_size, scale_log2, causal ? 1 : 0, (int)window, (int)num_splits,
+          (__nv_bfloat16*)out.data_ptr(), po, pm, T, cn, ga));
+    } else {
+      auto kern = attn::paged_attn_kernel<Dc, F8>;
+      static bool set = false;
+      if (!set) {
+        C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        set = true;
+      }
+      C10_CUDA_CHECK(launch_pdl(kern, dim3(grid), dim3(128), smem, stream, qp, kp, vp,
+          block_tables.data_ptr<int>(), block_tables.stride(0), seq_lens.data_ptr<int>(),
+          qsl.data_ptr<int>(), tile_seq.data_ptr<int>(), tile_row0.data_ptr<int>(), Hq, Hkv,
+          block_size, scale_log2, causal ? 1 : 0, (int)window, (int)num_splits,
+          (__nv_bfloat16*)out.data_ptr(), po, pm, T, cn));
     }
-C10_CUDA_CHECK(launch_pdl(    kern, dim3(grid), dim3(128), smem, stream, 
-        (const __nv_bfloat16*)q.data_ptr(), (const uint8_t*)k_cache.data_ptr(),
-        (const uint8_t*)v_cache.data_ptr(), block_tables.data_ptr<int>(), block_tables.stride(0),
-        seq_lens.data_ptr<int>(), qsl.data_ptr<int>(), tile_seq.data_ptr<int>(),
-        tile_row0.data_ptr<int>(), Hq, Hkv, block_size, scale_log2, causal ? 1 : 0, (int)window,
-        (int)num_splits, (__nv_bfloat16*)out.data_ptr(),
-        num_splits > 1 ? part_o.data_ptr<float>() : nullptr,
-        num_splits > 1 ? part_ml.data_ptr<float>() : nullptr, T,
-        num_splits > 1 ? reinterpret_cast<unsigned*>(counters.data_ptr()) : nullptr));
   };
   auto by_fmt = [&](auto dtag) {
     if (fmt == 1) run(dtag, std::integral_constant<int, 1>{});

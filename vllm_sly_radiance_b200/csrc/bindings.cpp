@@ -30,8 +30,9 @@ void gdn_recurrent(torch::Tensor y, torch::Tensor ba, torch::Tensor A_log, torch
 void gdn_decode_fused(torch::Tensor x, int64_t ba_off, torch::Tensor conv_w,
                       torch::Tensor conv_state, torch::Tensor A_log, torch::Tensor dt_bias,
                       torch::Tensor state, torch::Tensor slots, torch::Tensor has_init, int64_t Hk,
-                      double scale, double eps, torch::Tensor out,
-                      int64_t split);
+                      double scale, double eps, torch::Tensor out, int64_t split, int64_t z_off,
+                      torch::Tensor norm_w, double norm_eps, torch::Tensor nout, torch::Tensor ws,
+                      torch::Tensor q, torch::Tensor q_scale);
 void gdn_chunked(torch::Tensor y, torch::Tensor ba, torch::Tensor A_log, torch::Tensor dt_bias,
                  torch::Tensor state, torch::Tensor qsl, torch::Tensor slots,
                  torch::Tensor has_init, int64_t Hk, double scale, torch::Tensor out,
@@ -46,11 +47,19 @@ void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
                      torch::Tensor tile_seq, torch::Tensor tile_row0, double scale, bool causal,
                      int64_t window, int64_t num_splits, torch::Tensor part_o,
                      torch::Tensor part_ml, torch::Tensor out, torch::Tensor counters,
-                     bool decode);
+                     bool decode, torch::Tensor gate, int64_t gate_head_stride,
+                     torch::Tensor gate_cnt, torch::Tensor gq, torch::Tensor gq_scale);
 int64_t mxfp4_gemm_push(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
                         std::vector<int64_t> peers, int64_t rank, int64_t half_words,
                         torch::Tensor status);
 int64_t push_buffer_bytes(int64_t world, int64_t mmax, int64_t H);
+void mxfp4_gemv(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
+                torch::Tensor out, torch::Tensor ws, int64_t ctas_per_sm, int64_t fin_mode,
+                torch::Tensor res, torch::Tensor w, torch::Tensor res_out, torch::Tensor q,
+                torch::Tensor scale, double eps, torch::Tensor status);
+int64_t mxfp4_gemv_push(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
+                        torch::Tensor ws, int64_t ctas_per_sm, std::vector<int64_t> peers,
+                        int64_t rank, int64_t half_words, torch::Tensor status);
 void mxfp4_gemm_act(int64_t mode, torch::Tensor x, torch::Tensor res, torch::Tensor w,
                     torch::Tensor res_out, double eps, torch::Tensor wp, torch::Tensor sf,
                     torch::Tensor out, torch::Tensor status);
@@ -89,6 +98,10 @@ void dflash_walk(torch::Tensor unary, torch::Tensor cand, torch::Tensor anchors,
                  torch::Tensor drafts, torch::Tensor winp, torch::Tensor status);
 void argmax_rows(torch::Tensor x, torch::Tensor out_ids, torch::Tensor out_vals,
                  torch::Tensor workspace);
+void topk_window(torch::Tensor x, torch::Tensor out_vals, torch::Tensor out_ids,
+                 torch::Tensor workspace, torch::Tensor temperature, torch::Tensor top_k,
+                 torch::Tensor top_p, torch::Tensor min_p, torch::Tensor seeds, int64_t step,
+                 torch::Tensor out_tok, torch::Tensor probs_out);
 void sample_from_topk(torch::Tensor vals, torch::Tensor ids, torch::Tensor temperature,
                       torch::Tensor top_k, torch::Tensor top_p, torch::Tensor min_p,
                       torch::Tensor seeds, int64_t step, torch::Tensor out,
@@ -136,6 +149,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mxfp4_gemm_push", &rad::mxfp4_gemm_push,
         "row-parallel W4A8 GEMM that pushes its tiles into every peer's receive buffer");
   m.def("push_buffer_bytes", &rad::push_buffer_bytes, "size of a GEMM-push receive buffer");
+  m.def("mxfp4_gemv", &rad::mxfp4_gemv,
+        "persistent stream-K decode W4A8 GEMM (<= 16 rows) with an optional fused row finisher");
+  m.def("mxfp4_gemv_push", &rad::mxfp4_gemv_push,
+        "persistent decode W4A8 GEMM pushing its tiles into every rank's receive buffer");
   m.def("mxfp4_gemm_act", &rad::mxfp4_gemm_act,
         "decode W4A8 GEMM with its producer fused in (1: add + RMSNorm + e4m3, 2: SiLU*mul + e4m3)");
   m.def("push_allreduce_recv", &rad::push_allreduce_recv,
@@ -147,4 +164,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("allreduce_oneshot", &rad::allreduce_oneshot, "one-shot NVLink all-reduce (+ fused add/RMSNorm/quant)");
   m.def("argmax_rows", &rad::argmax_rows, "greedy argmax per row");
   m.def("sample_from_topk", &rad::sample_from_topk, "temperature/top-k/top-p/min-p sampling");
+  m.def("topk_window", &rad::topk_window, "top-64 window of each row (+ optional fused draw)");
 }

@@ -52,6 +52,7 @@ DEVI uint32_t* counters_of(uint8_t* base) { return reinterpret_cast<uint32_t*>(b
 DEVI bool ld_ll8(const uint64_t* p, uint32_t seq, float (&f)[8], int* status) {
   uint32_t a0, f0, a1, f1, a2, f2, a3, f3;
   uint64_t t0 = 0;
+  const uint64_t limit = wait_limit_ns(status, 3, kPeerWaitNs);
   for (int it = 0;; ++it) {
     asm volatile("ld.volatile.global.v4.u32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(a0), "=r"(f0), "=r"(a1), "=r"(f1) : "l"(p) : "memory");
@@ -61,7 +62,7 @@ DEVI bool ld_ll8(const uint64_t* p, uint32_t seq, float (&f)[8], int* status) {
     if ((it & 63) == 0) {
       const uint64_t now = globaltimer_ns();
       if (it == 0) t0 = now;
-      else if (now - t0 > kPeerWaitNs) {
+      else if (now - t0 > limit) {
         if (status) atomicExch(status, kErrPeerTimeout);
 #pragma unroll
         for (int i = 0; i < 8; ++i) f[i] = 0.f;

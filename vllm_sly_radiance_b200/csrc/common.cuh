@@ -1,8 +1,12 @@
 // Shared device helpers for the sm_100a kernels: mbarriers, TMA, tcgen05 (TMEM alloc, MMA,
 // commit, loads), cluster/DSMEM access, fp8/fp4 conversions, bounded waits with an error word.
 //
-// Every spin-wait in this library is bounded: after `kSpinLimit` polls it records an error code
+// Every spin-wait in this library is bounded: after its time limit it records an error code
 // into the caller's status word (if any) and gives up, so a kernel never hangs a GPU.
+//
+// Status word (int32[4], one per device): [0] error code (0 = ok), [1] reserved, [2] mbarrier
+// wait limit in microseconds, [3] peer-flag wait limit in microseconds.  A limit of 0 selects the
+// compile-time default; the host sets them at run time (ops.kernels.set_wait_limits).
 #pragma once
 
 #include <cuda.h>
@@ -15,7 +19,6 @@
 
 namespace rad {
 
-constexpr uint32_t kSpinLimit = 1u << 26;   // poll budget of the flag waits
 constexpr uint64_t kWaitNs = 200ull * 1000ull * 1000ull;   // 200 ms wall-clock bound per mbarrier wait
 
 // error codes written to status words
@@ -74,15 +77,23 @@ DEVI uint64_t globaltimer_ns() {
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
   return t;
 }
-// Bounded wait (200 ms of wall clock).  Returns false (and flags *err) on timeout.
+// Wait limit of status-word slot `slot` (2: mbarrier, 3: peer flags), default when unset.
+DEVI uint64_t wait_limit_ns(const int* status, int slot, uint64_t dflt) {
+  if (status == nullptr) return dflt;
+  const int us = reinterpret_cast<const volatile int*>(status)[slot];
+  return us > 0 ? (uint64_t)us * 1000ull : dflt;
+}
+
+// Bounded wait (200 ms of wall clock by default).  Returns false (and flags *err) on timeout.
 DEVI bool mbar_wait(uint64_t* bar, uint32_t phase, int* err) {
   if (mbar_try_wait(bar, phase)) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = wait_limit_ns(err, 2, kWaitNs);
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 32; ++i)
       if (mbar_try_wait(bar, phase)) return true;
-    if (globaltimer_ns() - t0 > kWaitNs) break;
+    if (globaltimer_ns() - t0 > limit) break;
   }
   if (err) atomicExch(err, (int)kErrMbarTimeout);
   return false;
@@ -317,11 +328,12 @@ DEVI bool wait_flag_geq(const uint32_t* p, uint32_t target, int* err, int code,
                         uint64_t timeout_ns = kWaitNs) {
   if ((int32_t)(ld_acquire_sys(p) - target) >= 0) return true;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = wait_limit_ns(err, 3, timeout_ns);
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 64; ++i)
       if ((int32_t)(ld_acquire_sys(p) - target) >= 0) return true;
-    if (globaltimer_ns() - t0 > timeout_ns) break;
+    if (globaltimer_ns() - t0 > limit) break;
   }
   if (err) atomicExch(err, code);
   return false;

@@ -246,7 +246,24 @@ __global__ void __launch_bounds__(128) recurrent_kernel(
 // CTA has read the old q/k conv state) only cluster rank 0 writes the shifted q/k state.  A
 // thread pair owns one row of the [dv, dk] state (64 columns each): one shuffle per reduction.
 // ------------------------------------------------------------------------------------------------
-template <int D, typename ST, int NS>
+// The out_proj producer fused into the decode step (FQ): the CTA of head h applies the gated
+// RMSNorm to its own 128 outputs -- n = bf16(bf16(o * rsqrt(mean_head(o^2) + eps) * w) * silu(z))
+// with o = bf16(scale * S q), the numerics of gdn_norm_quant -- writes them with the head's amax,
+// and the last head CTA of the row (self-resetting per-row counter) quantises the whole row to
+// e4m3 with its per-token scale.
+struct GdnQuantArgs {
+  int z_off;                       // column of z in the in_proj output row
+  const __nv_bfloat16* norm_w;     // [D]
+  float norm_eps;
+  __nv_bfloat16* nout;             // [B, Hv * D] normed row (bf16 scratch)
+  float* head_amax;                // [B, Hv]
+  unsigned* row_cnt;               // [B] arrival counters (zero, self-resetting)
+  uint8_t* q;                      // [B, Hv * D] e4m3
+  int ldq;
+  float* q_scale;                  // [B]
+};
+
+template <int D, typename ST, int NS, bool FQ = false>
 __global__ void __launch_bounds__(2 * D) decode_fused_kernel(
     const __nv_bfloat16* __restrict__ x, int ldx,        // in_proj output [B, *]: q|k|v|z|b|a
     const __nv_bfloat16* __restrict__ conv_w,            // [C, 4]
@@ -255,7 +272,7 @@ __global__ void __launch_bounds__(2 * D) decode_fused_kernel(
     const float* __restrict__ A_log, const float* __restrict__ dt_bias,
     ST* __restrict__ state,                              // [S, Hv, D, D]
     const int* __restrict__ slots, const int* __restrict__ has_init, int Hk, int Hv, int C,
-    float scale, float eps, __nv_bfloat16* __restrict__ out, int ldo) {
+    float scale, float eps, __nv_bfloat16* __restrict__ out, int ldo, const GdnQuantArgs fq) {
   constexpr int W = 4;
   // model constants (conv taps of this thread's q / k / v channels, the head's gate parameters)
   // are fetched before the dependency wait, overlapping the predecessor's tail
@@ -274,6 +291,11 @@ __global__ void __launch_bounds__(2 * D) decode_fused_kernel(
     }
   }
   const float a_log = A_log[blockIdx.y], dtb = dt_bias[blockIdx.y];
+  float nw = 0.f;
+  if constexpr (FQ) {
+    static_assert(NS == 1, "the fused norm needs the head's outputs in one CTA");
+    if (threadIdx.x < D) nw = __bfloat162float(fq.norm_w[threadIdx.x]);
+  }
   pdl_wait();     // inputs come from the preceding kernel
   pdl_trigger();
   constexpr int TPR = 2 * NS;           // threads per state row
@@ -396,7 +418,11 @@ __global__ void __launch_bounds__(2 * D) decode_fused_kernel(
   }
 #pragma unroll
   for (int m = 1; m < TPR; m <<= 1) o += __shfl_xor_sync(0xffffffffu, o, m);
-  if (t % TPR == 0) out[(size_t)b * ldo + h * D + r] = __float2bfloat16_rn(o * scale);
+  if constexpr (!FQ) {
+    if (t % TPR == 0) out[(size_t)b * ldo + h * D + r] = __float2bfloat16_rn(o * scale);
+  } else {
+    if (t % TPR == 0) sv[r] = bf16_round(o * scale);      // v is consumed: reuse its buffer
+  }
   if constexpr (sizeof(ST) == 4) {
 #pragma unroll
     for (int c = 0; c < HC; c += 4)
@@ -409,6 +435,63 @@ __global__ void __launch_bounds__(2 * D) decode_fused_kernel(
 #pragma unroll
       for (int e = 0; e < 4; ++e) hh[e] = __floats2bfloat162_rn(S[c + 2 * e], S[c + 2 * e + 1]);
       *reinterpret_cast<uint4*>(srow + c) = u;
+    }
+  }
+  if constexpr (FQ) {
+    __shared__ bool s_last;
+    __syncthreads();
+    // gated RMSNorm of the head (threads 0..D-1 own one output each)
+    float n = 0.f;
+    if (t < D) {
+      const float ov = sv[t];
+      const float ss = warp_sum(ov * ov);
+      if (lane == 0) sred[0][warp] = ss;
+    }
+    __syncthreads();
+    if (t < D) {
+      float ss = 0.f;
+#pragma unroll
+      for (int w = 0; w < D / 32; ++w) ss += sred[0][w];
+      const float rs = rsqrtf(ss / (float)D + fq.norm_eps);
+      const float zz = __bfloat162float(xr[fq.z_off + h * D + t]);
+      const float nn = bf16_round(sv[t] * rs * nw);
+      n = bf16_round(nn * (zz / (1.f + __expf(-zz))));
+      fq.nout[(size_t)b * Hv * D + h * D + t] = __float2bfloat16_rn(n);
+      const float am = warp_max(fabsf(n));
+      if (lane == 0) sred[1][warp] = am;
+    }
+    __syncthreads();
+    if (t == 0) {
+      float am = 0.f;
+#pragma unroll
+      for (int w = 0; w < D / 32; ++w) am = fmaxf(am, sred[1][w]);
+      fq.head_amax[(size_t)b * Hv + h] = am;
+      __threadfence();
+      s_last = atomicAdd(&fq.row_cnt[b], 1u) == (unsigned)(Hv - 1);
+      if (s_last) fq.row_cnt[b] = 0u;
+    }
+    __syncthreads();
+    if (s_last) {   // every head of row b is normed: quantise the row
+      __threadfence();
+      float am = 0.f;
+      for (int i = lane; i < Hv; i += 32) am = fmaxf(am, __ldcg(fq.head_amax + (size_t)b * Hv + i));
+      am = warp_max(am);
+      const float qs = fmaxf(am / 448.f, 1.f / (448.f * 512.f));
+      const float inv = 1.f / qs;
+      const int H = Hv * D;
+      for (int v = t; v < H / 8; v += 2 * D) {
+        const uint4 u = __ldcg(reinterpret_cast<const uint4*>(fq.nout + (size_t)b * H + v * 8));
+        const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&u);
+        uint2 qq;
+        uint16_t* q16 = reinterpret_cast<uint16_t*>(&qq);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(hh[e]);
+          q16[e] = f32x2_to_e4m3x2(f.x * inv, f.y * inv);
+        }
+        *reinterpret_cast<uint2*>(fq.q + (size_t)b * fq.ldq + v * 8) = qq;
+      }
+      if (t == 0) fq.q_scale[b] = qs;
     }
   }
 }
@@ -502,10 +585,15 @@ C10_CUDA_CHECK(launch_pdl((gdn::recurrent_kernel<DKc, ST>), dim3(grid), dim3(128
 
 // One-token-per-sequence GDN step fused into one launch (see decode_fused_kernel).  x = in_proj
 // output rows, ba_off = column of the b gates; out = [B, Hv * dv] bf16.
+// With q defined (fused norm + quant): z_off = column of z in x, norm_w [128] (gated RMSNorm
+// weight), norm_eps, nout bf16 [B, Hv * 128] scratch, ws int32 workspace (>= B * (1 + Hv)
+// elements, zero: per-row counters then head amax slots), q e4m3 [B, Hv * 128], q_scale [B].
 void gdn_decode_fused(torch::Tensor x, int64_t ba_off, torch::Tensor conv_w,
                       torch::Tensor conv_state, torch::Tensor A_log, torch::Tensor dt_bias,
                       torch::Tensor state, torch::Tensor slots, torch::Tensor has_init, int64_t Hk,
-                      double scale, double eps, torch::Tensor out, int64_t split) {
+                      double scale, double eps, torch::Tensor out, int64_t split, int64_t z_off,
+                      torch::Tensor norm_w, double norm_eps, torch::Tensor nout, torch::Tensor ws,
+                      torch::Tensor q, torch::Tensor q_scale) {
   const int B = slots.size(0);
   if (B == 0) return;
   const int Hv = state.size(1), DV = state.size(2), DK = state.size(3);
@@ -526,12 +614,34 @@ void gdn_decode_fused(torch::Tensor x, int64_t ba_off, torch::Tensor conv_w,
   }();
   // split: 1 | 2 | 4 CTAs per head, 0 = RADIANCE_GDN_DECODE_SPLIT (default 1; its value 0 sizes
   // the split to the grid)
+  const bool fused_q = q.defined() && q.numel();
   const int req = split == 1 || split == 2 || split == 4 ? (int)split : ns_env;
-  const int ns = req == 1 || req == 2 || req == 4 ? req
+  const int ns = fused_q ? 1
+               : req == 1 || req == 2 || req == 4 ? req
                : req == -1 ? 1 : (B * Hv >= 148 ? 1 : B * Hv * 2 >= 148 ? 2 : 4);
+  gdn::GdnQuantArgs fq{};
+  if (fused_q) {
+    TORCH_CHECK(q.scalar_type() == at::kFloat8_e4m3fn && q.size(0) >= B && q.size(1) >= Hv * 128 &&
+                    q.stride(1) == 1 && q.stride(0) % 8 == 0, "gdn_decode_fused: q");
+    TORCH_CHECK(nout.scalar_type() == at::kBFloat16 && nout.is_contiguous() &&
+                    nout.numel() >= (int64_t)B * Hv * 128, "gdn_decode_fused: nout");
+    TORCH_CHECK(ws.scalar_type() == at::kInt && ws.numel() >= (int64_t)B * (1 + Hv), "gdn ws");
+    TORCH_CHECK(norm_w.scalar_type() == at::kBFloat16 && norm_w.numel() >= 128, "norm weight");
+    TORCH_CHECK(q_scale.scalar_type() == at::kFloat && q_scale.numel() >= B, "q_scale");
+    fq.z_off = (int)z_off;
+    fq.norm_w = (const __nv_bfloat16*)norm_w.data_ptr();
+    fq.norm_eps = (float)norm_eps;
+    fq.nout = (__nv_bfloat16*)nout.data_ptr();
+    fq.row_cnt = reinterpret_cast<unsigned*>(ws.data_ptr<int>());
+    fq.head_amax = reinterpret_cast<float*>(ws.data_ptr<int>() + B);
+    fq.q = (uint8_t*)q.data_ptr();
+    fq.ldq = (int)q.stride(0);
+    fq.q_scale = q_scale.data_ptr<float>();
+  }
   auto run = [&](auto stag) {
     using ST = typename decltype(stag)::type;
-    auto kern = ns == 4 ? gdn::decode_fused_kernel<128, ST, 4>
+    auto kern = fused_q ? gdn::decode_fused_kernel<128, ST, 1, true>
+              : ns == 4 ? gdn::decode_fused_kernel<128, ST, 4>
               : ns == 2 ? gdn::decode_fused_kernel<128, ST, 2> : gdn::decode_fused_kernel<128, ST, 1>;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(B, Hv, ns);
@@ -551,7 +661,7 @@ void gdn_decode_fused(torch::Tensor x, int64_t ba_off, torch::Tensor conv_w,
         (__nv_bfloat16*)conv_state.data_ptr(), (int)ba_off, A_log.data_ptr<float>(),
         dt_bias.data_ptr<float>(), (ST*)state.data_ptr(), slots.data_ptr<int>(),
         has_init.data_ptr<int>(), (int)Hk, Hv, C, (float)scale, (float)eps,
-        (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0)));
+        fused_q ? nullptr : (__nv_bfloat16*)out.data_ptr(), fused_q ? 0 : (int)out.stride(0), fq));
   };
   struct F32 { using type = float; };
   struct BF16 { using type = __nv_bfloat16; };

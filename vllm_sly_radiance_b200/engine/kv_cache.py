@@ -81,6 +81,9 @@ class KVCacheManager:
         self.snap_free = deque(range(num_slots, num_slots + self.num_snapshots))
         self.snap_by_hash: dict[str, int] = {}
         self.snap_lru: "OrderedDict[int, str]" = OrderedDict()
+        # snapshot slots a waiting request will restore from: never recycled until the restore
+        # copy is issued (or the request leaves), whatever else reserves snapshots meanwhile
+        self.snap_pins: dict[int, int] = {}
         # besides the last boundary of every prompt, snapshot every `snapshot_interval` tokens
         # (rounded to blocks) so prompts that share only a leading part (a system prompt) hit
         self.snapshot_interval = (snapshot_interval // block_size * block_size
@@ -135,6 +138,7 @@ class KVCacheManager:
             self._pending_saves = []
 
     def free(self, req: Request):
+        self.release_restore(req)
         for b in req.block_ids:
             if self.blocks.release(b) and b in self.block_hash:
                 # keep cached content around for reuse until evicted
@@ -183,16 +187,16 @@ class KVCacheManager:
             sid = self.snap_by_hash.get(hs[j - 1])
             if sid is not None:
                 self.snap_lru.move_to_end(sid)
-                req.restore_snapshot = sid
+                self._pin_restore(req, sid)
                 best = j
                 break
             if self.offload is not None and self.num_snapshots and \
-                    self.offload.has_state(hs[j - 1]):
+                    self.offload.has_state(hs[j - 1]) and self._can_reserve_snapshot():
                 # the tier snapshot comes back into a GPU snapshot slot now (on the stream,
                 # before this step's forward) and is restored from there like a resident one
                 h = hs[j - 1]
                 sid = self.offload.restore_state(h, lambda: self._reserve_snapshot(h))
-                req.restore_snapshot = sid
+                self._pin_restore(req, sid)
                 best = j
                 tier = True
                 break
@@ -235,15 +239,39 @@ class KVCacheManager:
             return None
         return self._reserve_snapshot(h)
 
-    def _reserve_snapshot(self, h: str) -> int:
-        if not self.snap_free:
-            sid, old = self.snap_lru.popitem(last=False)
+    def _pin_restore(self, req: Request, sid: int):
+        req.restore_snapshot = sid
+        self.snap_pins[sid] = self.snap_pins.get(sid, 0) + 1
+
+    def release_restore(self, req: Request):
+        """The request's pending snapshot restore is done (copy issued) or abandoned: unpin."""
+        sid = req.restore_snapshot
+        if sid is None:
+            return
+        req.restore_snapshot = None
+        c = self.snap_pins.get(sid, 0) - 1
+        if c > 0:
+            self.snap_pins[sid] = c
+        else:
+            self.snap_pins.pop(sid, None)
+
+    def _can_reserve_snapshot(self) -> bool:
+        return bool(self.snap_free) or any(sid not in self.snap_pins for sid in self.snap_lru)
+
+    def _reserve_snapshot(self, h: str) -> Optional[int]:
+        """A snapshot slot for prefix hash h: a free one, else the least recently used one that
+        no pending restore pins (None when every slot is pinned)."""
+        if self.snap_free:
+            sid = self.snap_free.popleft()
+        else:
+            sid = next((s for s in self.snap_lru if s not in self.snap_pins), None)
+            if sid is None:
+                return None
+            old = self.snap_lru.pop(sid)
             self.snap_by_hash.pop(old, None)
             if self.offload is not None:
                 # write-back before the new snapshot is copied into the slot
                 self.offload.save_state(old, sid)
-        else:
-            sid = self.snap_free.popleft()
         self.snap_by_hash[h] = sid
         self.snap_lru[sid] = h
         return sid

@@ -24,6 +24,11 @@ from .tokenizer import IncrementalDetokenizer, get_tokenizer
 log = logging.getLogger("radiance.engine")
 
 
+class EngineStepError(RuntimeError):
+    """A step could not complete (e.g. a collective failed because a peer rank left); every open
+    request was aborted."""
+
+
 class LLMEngine:
     def __init__(self, config: EngineConfig, model: Optional[HybridModel] = None,
                  tokenizer=None, tp: Optional[TPInfo] = None, tokenizer_path: Optional[str] = None):
@@ -95,6 +100,7 @@ class LLMEngine:
         self.requests: dict[str, Request] = {}
         self.detok: dict[str, IncrementalDetokenizer] = {}
         self.metrics = EngineMetrics()
+        self.faults = 0
         self.kv_tokens_capacity = self.num_blocks * bs
         log.info("engine ready: %d KV blocks (%d tokens), %d state slots, load %.1fs",
                  self.num_blocks, self.kv_tokens_capacity, num_slots, self.load_time)
@@ -131,11 +137,21 @@ class LLMEngine:
         for s in sched.seqs:         # prefix-cache hits resume from a GDN state snapshot
             if s.req.restore_snapshot is not None:
                 self.model.copy_state(self.caches, s.req.restore_snapshot, s.req.state_slot)
-                s.req.restore_snapshot = None
-        if self.spec is not None:
-            result = self.spec.execute(sched)
-        else:
-            result = self.runner.execute(sched)
+                self.kv.release_restore(s.req)     # the copy is on the stream: slot reusable
+        try:
+            if self.spec is not None:
+                result = self.spec.execute(sched)
+            else:
+                result = self.runner.execute(sched)
+            code = self.runner.read_status()
+        except Exception as e:
+            # a failed collective (a peer rank that left or timed out) or any other step error:
+            # the step's outputs are lost, so no open request can continue
+            n = self._abort_all()
+            log.error("step failed (%r): %d open requests failed", e, n)
+            raise EngineStepError(f"engine step failed: {e!r}") from e
+        if code:
+            self._fail_open_requests(code)
         finished = self.scheduler.update(sched, result.sampled)
         if self.kv.num_snapshots:
             for s in sched.seqs:
@@ -174,6 +190,23 @@ class LLMEngine:
                 self.requests.pop(rid, None)
                 self.detok.pop(rid, None)
         return outs
+
+    def _fail_open_requests(self, code: int):
+        """A kernel of this step recorded an error (a bounded wait expired or a bad index was
+        refused): its outputs are not valid.  Every open request is aborted and the step raises;
+        the OpenAI server turns this into an error for each client and reports itself unhealthy."""
+        from ..ops.kernels import KernelFaultError, reset_status
+        reset_status(self.device)
+        n = self._abort_all()
+        log.error("kernel fault (status %d): %d open requests failed", code, n)
+        self.faults += 1
+        raise KernelFaultError(code)
+
+    def _abort_all(self) -> int:
+        ids = list(self.requests)
+        for rid in ids:
+            self.abort_request(rid)
+        return len(ids)
 
     def generate(self, prompts, params=None) -> list[RequestOutput]:
         if isinstance(params, SamplingParams) or params is None:

@@ -19,7 +19,7 @@ import torch
 
 from ..models.hybrid import HybridModel, ModelCaches, StepMeta
 from .request import Request
-from .sampler import SamplingTensors, apply_penalties, row_seed, sample
+from .sampler import SamplingTensors, apply_penalties, needs_full_vocab, row_seed, sample
 from .scheduler import SchedulerOutput
 
 GRAPH_BUCKETS = [1, 2, 4, 8, 16, 32, 48, 64, 96, 128]
@@ -77,6 +77,9 @@ class ModelRunner:
         self.d_meta = torch.zeros(self.L.size, dtype=torch.int32, device=self.device)
         self.d_slots = torch.full((self.max_tokens,), -1, dtype=torch.int64, device=self.device)
         self.h_out = torch.zeros(self.max_tokens, dtype=torch.int64, pin_memory=pin)
+        # the device status word's error code rides back with the sampled ids (same sync)
+        self.h_status = torch.zeros(1, dtype=torch.int32, pin_memory=pin)
+        self._status_staged = False
         self.step_count = 0
         self.num_spec_tokens = num_spec_tokens
         self.enable_graphs = enable_graphs and self.device.type == "cuda"
@@ -275,6 +278,7 @@ class ModelRunner:
             self.h_out[:len(sreqs)].copy_(toks, non_blocking=True) if self.device.type == "cuda" \
                 else self.h_out[:len(sreqs)].copy_(toks)
             if self.device.type == "cuda":
+                self._stage_status()
                 torch.cuda.current_stream().synchronize()
             hv = self.h_out[:len(sreqs)].tolist()
             j = 0
@@ -285,6 +289,23 @@ class ModelRunner:
         self.last_io = (h2d, d2h)
         return StepResult(sampled, logits=logits if want_logits else None,
                           num_tokens=meta.num_tokens)
+
+    def _stage_status(self):
+        """Queue the copy of the device error code next to the step's output copy."""
+        from ..ops import kernels as K
+        self.h_status.copy_(K.status_word(self.device)[:1], non_blocking=True)
+        self._status_staged = True
+
+    def read_status(self) -> int:
+        """Error code the step's kernels recorded (0 = ok).  Free when the step already synced
+        its output copy; otherwise one 4-byte copy and a stream sync."""
+        if self.device.type != "cuda":
+            return 0
+        if not self._status_staged:
+            self._stage_status()
+            torch.cuda.current_stream().synchronize()
+        self._status_staged = False
+        return int(self.h_status[0])
 
     # ------------------------------------------------------------------------------------------
     # CUDA graphs (pure decode batches)
@@ -298,28 +319,31 @@ class ModelRunner:
         meta, ids, sample_idx, _ = self.prepare(out, pad_to=bucket, nb_fixed=nb_fixed)
         reqs = [s.req for s in out.seqs]
         greedy = all(r.params.greedy for r in reqs)
-        key = (bucket, greedy)
+        mode = "greedy" if greedy else ("full" if needs_full_vocab(reqs) else "window")
+        key = (bucket, mode)
         g = self.graphs.get(key)
         if g is None:
             # warm up and capture on an all-padding batch (dummy state slot / KV block 0), so the
             # capture never advances the real sequences' GDN state; then restore the real batch
             from .scheduler import SchedulerOutput as _SO
             dmeta, dids, _, _ = self.prepare(_SO([], 0, [], []), pad_to=bucket, nb_fixed=nb_fixed)
-            g = self._capture(bucket, greedy, dmeta, dids)
+            g = self._capture(bucket, mode, dmeta, dids)
             self.graphs[key] = g
             meta, ids, sample_idx, _ = self.prepare(out, pad_to=bucket, nb_fixed=nb_fixed)
         # sampling params into the static buffers
         B = len(reqs)
         if not greedy:
-            self._h2d_bytes += B * (4 + 4 + 4 + 8)
+            self._h2d_bytes += B * (4 + 4 + 4 + 4 + 8)
             g["temp"][:B].copy_(torch.tensor([r.params.temperature for r in reqs]), non_blocking=True)
             g["topk"][:B].copy_(torch.tensor([r.params.top_k for r in reqs], dtype=torch.int32), non_blocking=True)
             g["topp"][:B].copy_(torch.tensor([r.params.top_p for r in reqs]), non_blocking=True)
+            g["minp"][:B].copy_(torch.tensor([r.params.min_p for r in reqs]), non_blocking=True)
             # the captured sampler reads a per-row Philox seed; fold the step in on the host
             g["seed"][:B].copy_(torch.tensor([row_seed(r) for r in reqs], dtype=torch.int64),
                                 non_blocking=True)
         g["graph"].replay()
         self.h_out[:bucket].copy_(g["out"], non_blocking=True)
+        self._stage_status()
         torch.cuda.current_stream().synchronize()
         return self.h_out[:B].tolist()
 
@@ -332,24 +356,28 @@ class ModelRunner:
         for bucket in GRAPH_BUCKETS:
             if bucket > self.graph_max_bs:
                 break
-            for greedy in (True, False):
-                if (bucket, greedy) in self.graphs:
+            # the full-vocabulary mode (top_k disabled) is captured when a batch first needs it
+            for mode in ("greedy", "window"):
+                if (bucket, mode) in self.graphs:
                     continue
                 dmeta, dids, _, _ = self.prepare(_SO([], 0, [], []), pad_to=bucket,
                                                  nb_fixed=self.max_blocks)
-                self.graphs[(bucket, greedy)] = self._capture(bucket, greedy, dmeta, dids)
+                self.graphs[(bucket, mode)] = self._capture(bucket, mode, dmeta, dids)
         torch.cuda.synchronize(self.device)
 
-    def _capture(self, bucket, greedy, meta, ids):
+    def _capture(self, bucket, mode, meta, ids):
+        """mode: 'greedy' (argmax), 'window' (top-64 window draw, every top_k in 1..64) or
+        'full' (full-vocabulary draw).  Sampled graphs always apply min_p (0 = off)."""
         dev = self.device
+        greedy = mode == "greedy"
         sidx = torch.arange(bucket, dtype=torch.long, device=dev)
         temp = torch.zeros(bucket, dtype=torch.float32, device=dev)
-        topk = torch.zeros(bucket, dtype=torch.int32, device=dev)
+        topk = torch.full((bucket,), 1 if mode == "window" else 0, dtype=torch.int32, device=dev)
         topp = torch.ones(bucket, dtype=torch.float32, device=dev)
         minp = torch.zeros(bucket, dtype=torch.float32, device=dev)
         seed = torch.zeros(bucket, dtype=torch.int64, device=dev)
         step = torch.zeros(1, dtype=torch.int64, device=dev)
-        st = SamplingTensors(temp, topk, topp, minp, seed, greedy, False)
+        st = SamplingTensors(temp, topk, topp, minp, seed, greedy, True, mode == "full")
 
         def run():
             lg = self._forward_logits(ids, meta, sidx)

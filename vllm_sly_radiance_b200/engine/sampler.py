@@ -1,8 +1,11 @@
 """Sampling: greedy, temperature / top-k / top-p / min-p, penalties.
 
-Rows are sampled from a top-64 window of the logits (the reference's composite top-k/top-p,
-``radiance_topk.py:1-59``: exact whenever the nucleus fits in the window, which holds for the
-production settings top_k=20, top_p=0.95).  Greedy-only batches use the argmax kernel."""
+Routing follows the reference's composite top-k/top-p sampler (``radiance_topk.py:1-59``): a batch
+whose every sampled row has 0 < top_k <= 64 (known on the host) draws from a top-64 window of the
+logits, found and sampled in one CUDA launch -- exact, because each row's top-k set lies inside the
+window.  A batch with any sampled row whose top_k is disabled (<= 0) or above 64 takes the
+full-vocabulary path: the rows are sorted and drawn over the whole vocabulary, so top-p / min-p cut
+the true distribution.  Greedy-only batches use the argmax kernel."""
 from __future__ import annotations
 
 from dataclasses import dataclass
@@ -24,6 +27,7 @@ class SamplingTensors:
     seeds: torch.Tensor         # [B] i64
     all_greedy: bool
     any_min_p: bool
+    full_vocab: bool = False    # some sampled row has top_k disabled or above the window
 
     @staticmethod
     def from_requests(reqs, device, pin: bool = False) -> "SamplingTensors":
@@ -37,7 +41,14 @@ class SamplingTensors:
         sd = torch.tensor([row_seed(r) for r in reqs], dtype=torch.int64)
         greedy = all(r.params.greedy for r in reqs)
         return SamplingTensors(t.to(device), k.to(device), p.to(device), mp.to(device),
-                               sd.to(device), greedy, bool((mp > 0).any()))
+                               sd.to(device), greedy, bool((mp > 0).any()),
+                               needs_full_vocab(reqs))
+
+
+def needs_full_vocab(reqs) -> bool:
+    """True when a sampled row's top-k set does not fit the top-64 window."""
+    return any(not r.params.greedy and (r.params.top_k <= 0 or r.params.top_k > WINDOW)
+               for r in reqs)
 
 
 def row_seed(req, offset: int = 0) -> int:
@@ -71,10 +82,15 @@ def sample(logits: torch.Tensor, st: SamplingTensors, step: int, want_probs: boo
     """-> (token ids [B] int64, window probs [B, WINDOW] or None, window ids or None)."""
     if st.all_greedy and not want_probs:
         return K.argmax(logits), None, None
-    V = logits.shape[1]
-    w = min(WINDOW, V)
-    vals, ids = torch.topk(logits.float(), w, dim=-1)
-    toks, probs = K.sample_from_topk(vals, ids, st.temperature, st.top_k, st.top_p,
-                                     st.min_p if st.any_min_p else None, st.seeds, step,
-                                     want_probs=want_probs)
+    min_p = st.min_p if st.any_min_p else None
+    if st.full_vocab and not want_probs:
+        # exact over the whole vocabulary: sorted rows, drawn by the same per-row kernel
+        vals, ids = torch.sort(logits.float(), dim=-1, descending=True)
+        toks, _ = K.sample_from_topk(vals, ids, st.temperature, st.top_k, st.top_p, min_p,
+                                     st.seeds, step)
+        return toks, None, None
+    # window path (speculative verify always reads the window: its rejection test works on the
+    # top-64 candidates of each position)
+    toks, probs, ids = K.topk_sample(logits, st.temperature, st.top_k, st.top_p, min_p, st.seeds,
+                                     step, want_probs=want_probs)
     return toks, probs, ids

@@ -37,6 +37,7 @@ class EngineLoop:
         self.broadcaster = broadcaster
         self.running = True
         self.error: Optional[str] = None
+        self.kernel_fault = False
         self.thread = threading.Thread(target=self._loop, daemon=True)
         self.thread.start()
 
@@ -78,6 +79,9 @@ class EngineLoop:
                 outs = eng.step()
             except Exception as e:      # engine failure: fail every open request, keep serving
                 self.error = repr(e)
+                from ..ops.kernels import KernelFaultError
+                if isinstance(e, KernelFaultError):
+                    self.kernel_fault = True     # device state is suspect: report unhealthy
                 with self.lock:
                     ids = list(self.outq)
                 for rid in ids:
@@ -136,6 +140,8 @@ def build_app(engine, served_model_name: str = "model", reasoning_parser: Option
     async def health():
         if loop_runner.error and not loop_runner.thread.is_alive():
             return PlainTextResponse("engine dead", status_code=503)
+        if loop_runner.kernel_fault:
+            return PlainTextResponse("kernel fault: " + loop_runner.error, status_code=503)
         return PlainTextResponse("")
 
     @app.get("/version")

@@ -164,7 +164,9 @@ class GDNMixer:
         self.quant = quant
         self.scale = self.dk ** -0.5
 
-    def forward(self, x, meta: StepMeta, conv_state, ssm_state, save=None):
+    def forward(self, x, meta: StepMeta, conv_state, ssm_state, save=None, fin=None):
+        """fin = (residual, norm weight, eps): the out_proj GEMM also runs the post-mixer
+        residual add + RMSNorm + e4m3 and returns (q, scale, new residual) instead of h."""
         cfg = self.cfg
         proj = self.in_proj(x)                                    # [T, in_proj_local]
         cd, vd = self.conv_dim, self.value_dim
@@ -174,6 +176,15 @@ class GDNMixer:
         fused_state = meta.commit_len is None and meta.num_tokens == meta.num_seqs
         if (fused_state and save is None and proj.is_cuda and K._GDN_DECODE_FUSED
                 and self.dk == 128 and self.dv == 128 and conv_state.shape[2] == 3):
+            if self.quant == "mxfp4" and K._GDN_DECODE_FUSED_QUANT:
+                # decode: the whole GDN step and the out_proj producer (gated norm + e4m3) in
+                # one launch
+                act = K.gdn_decode_fused_quant(proj, cd + vd, cd, self.conv_w, conv_state,
+                                               ssm_state, self.A_log, self.dt_bias, meta, self.Hk,
+                                               self.scale, self.norm_w, cfg.rms_norm_eps)
+                if fin is not None and self.out_proj.can_finish(act):
+                    return self.out_proj.call_finish(act, K.FIN_NORM, *fin)
+                return self.out_proj(act)
             # decode: the whole GDN step (conv, norms, gates, delta rule) in one launch
             o = K.gdn_decode_fused(proj, cd + vd, self.conv_w, conv_state, ssm_state, self.A_log,
                                    self.dt_bias, meta, self.Hk, self.scale)
@@ -189,7 +200,10 @@ class GDNMixer:
         if self.quant in ("bf16", "int4"):
             h = self.out_proj(K.gdn_gated_norm(o, z, self.norm_w, cfg.rms_norm_eps, self.dv))
         else:
-            h = self.out_proj(K.gdn_norm_quant(o, z, self.norm_w, cfg.rms_norm_eps, self.dv))
+            act = K.gdn_norm_quant(o, z, self.norm_w, cfg.rms_norm_eps, self.dv)
+            if fin is not None and self.out_proj.can_finish(act):
+                return self.out_proj.call_finish(act, K.FIN_NORM, *fin)
+            h = self.out_proj(act)
         return h
 
     def commit(self, saved, meta: StepMeta, conv_state, ssm_state, commit_len):
@@ -238,7 +252,8 @@ class AttentionMixer:
         self.scale = hd ** -0.5
         self.cos_sin = None
 
-    def forward(self, x, meta: StepMeta, k_cache, v_cache):
+    def forward(self, x, meta: StepMeta, k_cache, v_cache, fin=None):
+        """fin: as GDNMixer.forward (o_proj runs the post-mixer norm as its finisher)."""
         cfg = self.cfg
         hd = self.hd
         qkv = self.qkv(x)
@@ -248,13 +263,21 @@ class AttentionMixer:
                            num_kv_heads=self.Hkv, head_dim=hd, rotary_dim=cfg.rotary_dim,
                            theta=cfg.rope_theta, eps=cfg.rms_norm_eps, gated=self.gated,
                            block_size=k_cache.shape[2])
+        if (self.gated and self.quant == "mxfp4" and
+                K.attention_decode_gated_ok(q, k_cache, meta)):
+            # decode: the sigmoid gate and the e4m3 quantisation run inside the attention launch
+            act = K.paged_attention_gated(q, k_cache, v_cache, meta, self.scale, qkv[:, hd:],
+                                          2 * hd)
+            if fin is not None and self.o_proj.can_finish(act):
+                return self.o_proj.call_finish(act, K.FIN_NORM, *fin)
+            return self.o_proj(act)
         a = K.paged_attention(q, k_cache, v_cache, meta, self.scale).view(T, -1)
-        if self.gated:
-            gate = qkv[:, hd:]
-            if self.quant in ("bf16", "int4"):
-                return self.o_proj(K.gate_mul(a, gate, hd, 2 * hd))
-            return self.o_proj(K.gate_mul_quant(a, gate, hd, 2 * hd))
-        return self.o_proj(a if self.quant in ("bf16", "int4") else K.quant_fp8(a))
+        if self.quant in ("bf16", "int4"):
+            return self.o_proj(K.gate_mul(a, qkv[:, hd:], hd, 2 * hd) if self.gated else a)
+        act = K.gate_mul_quant(a, qkv[:, hd:], hd, 2 * hd) if self.gated else K.quant_fp8(a)
+        if fin is not None and self.o_proj.can_finish(act):
+            return self.o_proj.call_finish(act, K.FIN_NORM, *fin)
+        return self.o_proj(act)
 
 
 class MLP:
@@ -271,7 +294,15 @@ class MLP:
         del w
         self.quant = quant
 
-    def forward(self, x):
+    def forward(self, x, fin=None):
+        """fin = (residual, next norm weight, eps): the down GEMM also produces the next layer's
+        input (q, scale, new residual).  Decode-sized W4A8 inputs run SiLU * mul + e4m3 as the
+        gate_up GEMM's finisher."""
+        if self.gate_up.can_finish(x):
+            act = self.gate_up.call_finish(x, K.FIN_SILU)
+            if fin is not None and self.down.can_finish(act):
+                return self.down.call_finish(act, K.FIN_NORM, *fin)
+            return self.down(act)
         gu = self.gate_up(x)
         if self.quant in ("bf16", "int4"):
             return self.down(K.silu_mul(gu))
@@ -450,7 +481,12 @@ class HybridModel:
         fuse_prod = (self.quant == "mxfp4" and input_ids.is_cuda and _FUSE_PRODUCERS
                      and input_ids.shape[0] <= FUSE_MAX_ROWS)
         pending = None          # (q, s) produced by a fused all-reduce epilogue for the next norm
+        # decode-sized W4A8 steps at TP1: the post-mixer and next-layer norms run as finishers of
+        # the out_proj / o_proj and down GEMMs (no producer launches between the linears)
+        fin_norm = (self.quant == "mxfp4" and input_ids.is_cuda and self.tp.size == 1
+                    and not fuse_prod and input_ids.shape[0] <= K.GEMV_MAX_ROWS)
         for li, layer in enumerate(self.layers):
+            nxt = self.layers[li + 1] if li + 1 < len(self.layers) else None
             if pending is not None:
                 a_in = pending
                 pending = None
@@ -464,13 +500,21 @@ class HybridModel:
                 a_in = (a_in[0], a_in[1])
             else:
                 a_in, residual = K.add_rms_norm(h, residual, layer.ln1, eps)
+            mfin = (residual, layer.ln2, eps) if fin_norm else None
             if layer.is_attn:
-                h = layer.mixer.forward(a_in, meta, caches.k[ai], caches.v[ai])
+                h = layer.mixer.forward(a_in, meta, caches.k[ai], caches.v[ai], fin=mfin)
                 ai += 1
             else:
-                h = layer.mixer.forward(a_in, meta, caches.conv[gi], caches.ssm[gi], save=gdn_save)
+                h = layer.mixer.forward(a_in, meta, caches.conv[gi], caches.ssm[gi], save=gdn_save,
+                                        fin=mfin)
                 gi += 1
-            if fused_ar:
+            dense = isinstance(layer.mlp, MLP)
+            if isinstance(h, tuple):        # the out GEMM's finisher: (q, s, new residual)
+                q, s, residual = h
+                # the down GEMM's finisher adds the MLP output to this (new) residual
+                dfin = (residual, nxt.ln1, eps) if fin_norm and nxt is not None and dense else None
+                h = layer.mlp.forward((q, s), fin=dfin) if dense else layer.mlp.forward((q, s))
+            elif fused_ar:
                 q, s, residual = self.tp.all_reduce_add_rms_quant(h, residual, layer.ln2, eps)
                 h = layer.mlp.forward((q, s))
             else:
@@ -485,8 +529,14 @@ class HybridModel:
                 else:
                     n, residual = K.add_rms_norm(h, residual, layer.ln2, eps)
                     h = layer.mlp.forward(n)
-            if fused_ar and li + 1 < len(self.layers) and aux_layers is None:
-                nxt = self.layers[li + 1]
+            if isinstance(h, tuple):        # the down GEMM's finisher: the next layer's input
+                q, s, residual = h
+                pending = (q, s)
+                h = None
+                if aux_layers is not None and li in aux_layers:
+                    aux_out.append(residual)          # bf16(h + residual), as computed below
+                continue
+            if fused_ar and nxt is not None and aux_layers is None:
                 q, s, residual = self.tp.all_reduce_add_rms_quant(h, residual, nxt.ln1, eps)
                 pending = (q, s)
                 h = None

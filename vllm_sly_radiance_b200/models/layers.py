@@ -36,6 +36,13 @@ class SiluAct:
 FUSE_MAX_ROWS = 1          # fused producers: single-row decode (the rows are held in registers)
 FUSE_MAX_K = 9216
 
+import os as _os
+
+# decode batches (<= 16 rows) run the persistent stream-K GEMM; its finisher produces the next
+# linear's e4m3 rows in the same launch (RADIANCE_GEMV=0 / RADIANCE_FINISH=0 switch them off)
+GEMV_ON = _os.environ.get("RADIANCE_GEMV", "1") != "0"
+FINISH_ON = _os.environ.get("RADIANCE_FINISH", "1") != "0"
+
 
 def rope_cache(max_pos: int, rotary_dim: int, theta: float, device) -> torch.Tensor:
     """[max_pos, rotary_dim] fp32: cos in [:rot/2], sin in [rot/2:], computed in fp64."""
@@ -123,6 +130,29 @@ class Linear:
     # batches their GEMM pushes its output tiles to every rank (fused GEMM -> all-reduce)
     push = None
 
+    def can_finish(self, x) -> bool:
+        """A decode-sized (e4m3, scale) input this MXFP4 linear can run with a fused finisher."""
+        return (FINISH_ON and GEMV_ON and self.quant == "mxfp4" and isinstance(x, tuple)
+                and x[0].is_cuda and x[0].shape[0] <= K.GEMV_MAX_ROWS and self.push is None)
+
+    def call_finish(self, x, mode: int, res=None, norm_w=None, eps: float = 0.0):
+        """y = x W^T followed, in the same launch, by the producer of the next linear:
+        FIN_NORM -> (q, scale, new residual = bf16(y + res)) of RMSNorm(1 + norm_w);
+        FIN_SILU -> (q, scale) of SiLU(g) * u with y = [g | u].  CPU / ineligible inputs run the
+        same ops unfused."""
+        if not self.can_finish(x):
+            y = self(x)
+            if mode == K.FIN_NORM:
+                return K.add_rms_quant(y, res, norm_w, eps)
+            return K.silu_mul_quant(y)
+        q, s = x
+        if mode == K.FIN_NORM:
+            res_new = torch.empty(q.shape[0], self.N, dtype=torch.bfloat16, device=q.device)
+            _, fq, fs = K.mxfp4_gemv(q, s, self.w, None, K.FIN_NORM, res, norm_w, res_new, eps)
+            return fq, fs, res_new
+        _, fq, fs = K.mxfp4_gemv(q, s, self.w, None, K.FIN_SILU)
+        return fq, fs
+
     def __call__(self, x: Act, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         if isinstance(x, (NormAct, SiluAct)):
             return self._fused(x, out)
@@ -134,6 +164,8 @@ class Linear:
             if self.push is not None and out is None and q.is_cuda and \
                     self.push.can_push(q.shape[0], self.N):
                 return self.push.gemm_push(q, s, self.w)
+            if GEMV_ON and q.is_cuda and q.shape[0] <= K.GEMV_MAX_ROWS:
+                return K.mxfp4_gemv(q, s, self.w, out)
             return K.mxfp4_gemm(q, s, self.w.packed, self.w.sf, self.w.scales, self.N, out=out)
         if self.quant == "fp8":
             if isinstance(x, tuple):

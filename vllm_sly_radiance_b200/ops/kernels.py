@@ -25,9 +25,26 @@ def _empty(device) -> torch.Tensor:
 
 _STATUS: dict = {}
 
+# error codes of the device status word (csrc/common.cuh StatusCode)
+STATUS_NAMES = {1: "mbarrier wait timed out", 2: "peer wait timed out",
+                3: "index out of bounds", 4: "tensor-memory allocation failed"}
+
+
+class KernelFaultError(RuntimeError):
+    """A kernel recorded an error in the device status word (a bounded wait that expired, or a
+    bad index it refused to use).  The kernel returned normally; its outputs are not valid."""
+
+    def __init__(self, code: int):
+        self.code = code
+        super().__init__(f"kernel reported error {code}: {STATUS_NAMES.get(code, 'unknown')}")
+
 
 def status_word(device) -> torch.Tensor:
-    """Per-device int32 error word the kernels write on a bounded-wait timeout (0 = ok)."""
+    """Per-device int32[4] status word: [0] error code the kernels write (0 = ok), [2] / [3] the
+    mbarrier / peer-flag wait limits in microseconds (0 = the compiled-in 200 ms / 5 s)."""
+    device = torch.device(device)
+    if device.type == "cuda" and device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
     t = _STATUS.get(device)
     if t is None:
         t = torch.zeros(4, dtype=torch.int32, device=device)
@@ -35,14 +52,27 @@ def status_word(device) -> torch.Tensor:
     return t
 
 
+def set_wait_limits(device, mbar_us: int = 0, peer_us: int = 0):
+    """Time limits of the kernels' bounded waits on `device` (0 = default).  Ordered on the
+    current stream, so kernels launched after it see the new limits."""
+    t = status_word(device)
+    t[2] = int(mbar_us)
+    t[3] = int(peer_us)
+
+
+def reset_status(device):
+    status_word(device)[:2].zero_()
+
+
 def check_status(device, reset: bool = True) -> int:
-    """Host check of the device error word (syncs).  Raises on a recorded kernel timeout."""
+    """Host check of the device error word (syncs).  Raises KernelFaultError on a recorded
+    error; the wait limits are kept."""
     t = status_word(device)
     code = int(t[0].item())
     if code != 0:
         if reset:
-            t.zero_()
-        raise RuntimeError(f"kernel reported error code {code} (bounded wait timed out)")
+            reset_status(device)
+        raise KernelFaultError(code)
     return code
 
 
@@ -191,6 +221,45 @@ def mxfp4_gemm(q: torch.Tensor, scale: torch.Tensor, packed: torch.Tensor, sf: t
     return out
 
 
+# persistent stream-K decode GEMM: one CTA per SM by default (RADIANCE_GEMV_CTAS_PER_SM)
+GEMV_MAX_ROWS = 16
+_GEMV_CPS = int(os.environ.get("RADIANCE_GEMV_CTAS_PER_SM", "1"))
+FIN_NONE, FIN_NORM, FIN_SILU = 0, 1, 2
+
+
+def _gemv_ws(device):
+    return workspace(device, "gemv", 8192 + 2 * 160 * max(1, _GEMV_CPS) * 16 * 128)
+
+
+def mxfp4_gemv(q, scale, w, out=None, fin: int = FIN_NONE, res=None, norm_w=None, res_out=None,
+               eps: float = 1e-6):
+    """Decode W4A8 GEMM (1..16 rows, CUDA) -> out [M, N] bf16; with fin = FIN_NORM / FIN_SILU
+    the CTA that completes the last tile also produces the next linear's (e4m3, scale) rows:
+    residual add + RMSNorm(1 + w) (new residual into res_out) or SiLU(g) * u.  Returns out, or
+    (out, q, scale) with a finisher."""
+    M = q.shape[0]
+    dev = q.device
+    if out is None:
+        out = torch.empty(M, w.N, dtype=torch.bfloat16, device=dev)
+    e = _empty(dev)
+    if fin == FIN_NONE:
+        ext().mxfp4_gemv(q, scale, w.packed, w.sf, out, _gemv_ws(dev), _GEMV_CPS, 0, e, e, e, e, e,
+                         0.0, status_word(dev))
+        return out
+    H = w.N if fin == FIN_NORM else w.N // 2
+    fq = torch.empty(M, H, dtype=torch.float8_e4m3fn, device=dev)
+    fs = torch.empty(M, dtype=torch.float32, device=dev)
+    ext().mxfp4_gemv(q, scale, w.packed, w.sf, out, _gemv_ws(dev), _GEMV_CPS, fin,
+                     _none(res, dev), _none(norm_w, dev), _none(res_out, dev), fq, fs, eps,
+                     status_word(dev))
+    return out, fq, fs
+
+
+def mxfp4_gemv_push(q, scale, w, peers, rank: int, half_words: int) -> int:
+    return ext().mxfp4_gemv_push(q, scale, w.packed, w.sf, _gemv_ws(q.device), _GEMV_CPS, peers,
+                                 rank, half_words, status_word(q.device))
+
+
 def mxfp4_gemm_act(mode: int, x, res, w_norm, res_out, eps: float, w, out):
     """Decode GEMM with the producer fused in (CUDA only): mode 1 = add + RMSNorm + e4m3 of
     x (+ res), new residual -> res_out; mode 2 = SiLU(g) * u + e4m3 of x = [g | u]."""
@@ -263,6 +332,45 @@ def qkv_prologue(qkv, positions, q_norm_w, k_norm_w, cos_sin, k_cache, v_cache, 
 _ATTN_DECODE = os.environ.get("RADIANCE_ATTN_DECODE", "1") != "0"
 
 
+def attention_decode_gated_ok(q, k_cache, meta) -> bool:
+    """The decode kernel can run the o_proj producer (sigmoid gate + e4m3) itself."""
+    T, Hq, D = q.shape
+    return (q.is_cuda and _ATTN_DECODE and _ATTN_GATE_FUSED and meta.num_tokens == meta.num_seqs
+            and Hq // k_cache.shape[1] <= 16 and Hq * D * 4 <= 144 * D * 2)
+
+
+def paged_attention_gated(q, k_cache, v_cache, meta, scale: float, gate, gate_head_stride: int):
+    """Decode attention (one query token per sequence) with the o_proj producer in the same
+    launch: y = bf16(o * sigmoid(gate)) of each token row, quantised to (e4m3, scale)."""
+    T, Hq, D = q.shape
+    dev = q.device
+    out = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=dev)
+    gq = torch.empty(T, Hq * D, dtype=torch.float8_e4m3fn, device=dev)
+    gs = torch.empty(T, dtype=torch.float32, device=dev)
+    _paged_attention_launch(q, k_cache, v_cache, meta, scale, True, 0, out, True,
+                            (gate, gate_head_stride, workspace(dev, "attn_gate", max(4096, T)),
+                             gq, gs))
+    return gq, gs
+
+
+def _paged_attention_launch(q, k_cache, v_cache, meta, scale, causal, window, out, decode,
+                            gated=None):
+    T, Hq, D = q.shape
+    splits = meta.num_splits if decode else min(meta.num_splits, 32)
+    if splits > 1:
+        part_o = meta.scratch_o(splits, T, Hq, D)
+        part_ml = meta.scratch_ml(splits, T, Hq)
+    else:
+        part_o = part_ml = _empty(q.device)
+    e = _empty(q.device)
+    g, ghs, cnt, gq, gs = gated if gated is not None else (e, 0, e, e, e)
+    ext().paged_attention(q, k_cache, v_cache, meta.block_tables, meta.seq_lens,
+                          meta.query_start_loc, meta.tile_seq, meta.tile_row0, scale, causal,
+                          window, splits, part_o, part_ml, out,
+                          workspace(q.device, "attn", meta.tile_seq.shape[0] * k_cache.shape[1]),
+                          decode, g, ghs, cnt, gq, gs)
+
+
 def paged_attention(q, k_cache, v_cache, meta, scale: float, causal: bool = True,
                     window: int = 0, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Varlen paged attention over the batch described by ``meta`` (an AttnMeta)."""
@@ -277,17 +385,7 @@ def paged_attention(q, k_cache, v_cache, meta, scale: float, causal: bool = True
     decode = (meta.num_tokens == meta.num_seqs and Hq // k_cache.shape[1] <= 16
               and _ATTN_DECODE)
     # the decode kernel merges up to 128 KV splits in-kernel, the tile kernel up to 32
-    splits = meta.num_splits if decode else min(meta.num_splits, 32)
-    if splits > 1:
-        part_o = meta.scratch_o(splits, T, Hq, D)
-        part_ml = meta.scratch_ml(splits, T, Hq)
-    else:
-        part_o = part_ml = _empty(q.device)
-    ext().paged_attention(q, k_cache, v_cache, meta.block_tables, meta.seq_lens,
-                          meta.query_start_loc, meta.tile_seq, meta.tile_row0, scale, causal,
-                          window, splits, part_o, part_ml, out,
-                          workspace(q.device, "attn", meta.tile_seq.shape[0] * k_cache.shape[1]),
-                          decode)
+    _paged_attention_launch(q, k_cache, v_cache, meta, scale, causal, window, out, decode)
     return out
 
 
@@ -353,15 +451,37 @@ def gdn_decode_fused(proj, ba_off: int, conv_w, conv_state, ssm_state, A_log, dt
     B = meta.num_seqs
     _, Hv, DV, _ = ssm_state.shape
     out = torch.empty(B, Hv * DV, dtype=torch.bfloat16, device=proj.device)
+    e = _empty(proj.device)
     ext().gdn_decode_fused(proj, ba_off, conv_w, conv_state, A_log, dt_bias, ssm_state,
                            meta.state_slots, meta.has_initial, num_k_heads, scale, eps, out,
-                           split)
+                           split, 0, e, 0.0, e, e, e, e)
     return out
+
+
+def gdn_decode_fused_quant(proj, ba_off: int, z_off: int, conv_w, conv_state, ssm_state, A_log,
+                           dt_bias, meta, num_k_heads: int, scale: float, norm_w, norm_eps: float,
+                           eps: float = 1e-6):
+    """gdn_decode_fused with the out_proj producer in the same launch: the gated RMSNorm of each
+    head (z at column z_off of proj) and the per-token e4m3 quantisation -> (q, scale)."""
+    B = meta.num_seqs
+    _, Hv, DV, _ = ssm_state.shape
+    dev = proj.device
+    nout = torch.empty(B, Hv * DV, dtype=torch.bfloat16, device=dev)
+    q = torch.empty(B, Hv * DV, dtype=torch.float8_e4m3fn, device=dev)
+    qs = torch.empty(B, dtype=torch.float32, device=dev)
+    ws = workspace(dev, "gdn_fq", max(4096, B * (1 + Hv)))
+    ext().gdn_decode_fused(proj, ba_off, conv_w, conv_state, A_log, dt_bias, ssm_state,
+                           meta.state_slots, meta.has_initial, num_k_heads, scale, eps,
+                           _empty(dev), 1, z_off, norm_w, norm_eps, nout, ws, q, qs)
+    return q, qs
 
 
 _GDN_CHUNKED = os.environ.get("RADIANCE_GDN_CHUNKED", "1") != "0"
 _GDN_CHUNK_SPLIT = int(os.environ.get("RADIANCE_GDN_CHUNK_SPLIT", "0"))   # 0: by batch size
 _GDN_DECODE_FUSED = os.environ.get("RADIANCE_GDN_DECODE_FUSED", "1") != "0"
+_ATTN_GATE_FUSED = os.environ.get("RADIANCE_ATTN_GATE_FUSED", "1") != "0"
+# the out_proj producer (gated norm + e4m3) inside the fused decode step
+_GDN_DECODE_FUSED_QUANT = os.environ.get("RADIANCE_GDN_DECODE_FUSED_QUANT", "1") != "0"
 
 
 def gdn_recurrent(y, ba, A_log, dt_bias, ssm_state, meta, num_k_heads: int, scale: float,
@@ -421,30 +541,80 @@ def argmax(logits: torch.Tensor) -> torch.Tensor:
 
 def sample_from_topk(vals, ids, temperature, top_k, top_p, min_p, seeds, step: int,
                      want_probs: bool = False):
-    """vals/ids [B, K] sorted descending -> (token ids [B], probs over the window or None)."""
+    """vals/ids [B, K] sorted descending -> (token ids [B], probs over the window or None).
+    K may be the whole vocabulary (a sorted row): the full-vocabulary sampling path."""
     B, K = vals.shape
     out = torch.empty(B, dtype=torch.int64, device=vals.device)
     probs = torch.empty(B, K, dtype=torch.float32, device=vals.device) if want_probs else None
     if not vals.is_cuda:
-        gen = torch.Generator()
-        res = []
-        pr = []
-        for b in range(B):
-            T = float(temperature[b])
-            if T <= 0:
-                res.append(int(ids[b, 0]))
-                pr.append(torch.nn.functional.one_hot(torch.tensor(0), K).float())
-                continue
-            lg = vals[b].float() / T
-            masked = ref.apply_top_k_top_p(lg[None], top_k[b:b + 1], top_p[b:b + 1],
-                                           None if min_p is None else min_p[b:b + 1])[0]
-            p = torch.softmax(masked, -1)
-            gen.manual_seed(int(seeds[b]) * 1000003 + step)
-            res.append(int(ids[b, torch.multinomial(p, 1, generator=gen)]))
-            pr.append(p)
-        out = torch.tensor(res, dtype=torch.int64)
-        return out, (torch.stack(pr) if want_probs else None)
+        return _sample_rows_cpu(vals, ids, temperature, top_k, top_p, min_p, seeds, step,
+                                want_probs)
     ext().sample_from_topk(vals.float().contiguous(), ids.contiguous(), temperature, top_k,
                            top_p, _none(min_p, vals.device), seeds, step, out,
                            _empty(vals.device), _none(probs, vals.device))
     return out, probs
+
+
+def _sample_rows_cpu(vals, ids, temperature, top_k, top_p, min_p, seeds, step, want_probs):
+    B, K = vals.shape
+    gen = torch.Generator()
+    res = []
+    pr = []
+    for b in range(B):
+        T = float(temperature[b])
+        if T <= 0:
+            res.append(int(ids[b, 0]))
+            pr.append(torch.nn.functional.one_hot(torch.tensor(0), K).float())
+            continue
+        lg = vals[b].float() / T
+        masked = ref.apply_top_k_top_p(lg[None], top_k[b:b + 1], top_p[b:b + 1],
+                                       None if min_p is None else min_p[b:b + 1])[0]
+        p = torch.softmax(masked, -1)
+        gen.manual_seed(int(seeds[b]) * 1000003 + step)
+        res.append(int(ids[b, torch.multinomial(p, 1, generator=gen)]))
+        pr.append(p)
+    out = torch.tensor(res, dtype=torch.int64)
+    return out, (torch.stack(pr) if want_probs else None)
+
+
+TOPK_WINDOW = 64
+
+
+def topk_window(logits: torch.Tensor):
+    """Top-64 window of each row: (values [B, 64] fp32 descending, ids [B, 64] int64).  Ties
+    resolve to the lowest column."""
+    B, V = logits.shape
+    if not logits.is_cuda:
+        vals, ids = torch.topk(logits.float(), min(TOPK_WINDOW, V), dim=-1)
+        return vals, ids
+    vals = torch.empty(B, TOPK_WINDOW, dtype=torch.float32, device=logits.device)
+    ids = torch.empty(B, TOPK_WINDOW, dtype=torch.int64, device=logits.device)
+    e = _empty(logits.device)
+    ext().topk_window(logits, vals, ids, _topk_ws(logits), e, e, e, e, e, 0, e, e)
+    return vals, ids
+
+
+def _topk_ws(logits):
+    B, V = logits.shape
+    nch = (V + 4095) // 4096
+    return workspace(logits.device, "topk", 4096 + B * nch * TOPK_WINDOW * 2)
+
+
+def topk_sample(logits, temperature, top_k, top_p, min_p, seeds, step: int,
+                want_probs: bool = False):
+    """One launch: the top-64 window of each row and the row's draw from it (temperature, top-k
+    <= 64, top-p, min-p; Philox stream per (seed, step)).  -> (tokens [B], window probs or None,
+    window ids [B, 64])."""
+    B, V = logits.shape
+    if not logits.is_cuda:
+        vals, ids = topk_window(logits)
+        toks, probs = sample_from_topk(vals, ids, temperature, top_k, top_p, min_p, seeds, step,
+                                       want_probs)
+        return toks, probs, ids
+    dev = logits.device
+    ids = torch.empty(B, TOPK_WINDOW, dtype=torch.int64, device=dev)
+    toks = torch.empty(B, dtype=torch.int64, device=dev)
+    probs = torch.empty(B, TOPK_WINDOW, dtype=torch.float32, device=dev) if want_probs else None
+    ext().topk_window(logits, _empty(dev), ids, _topk_ws(logits), temperature, top_k, top_p,
+                      _none(min_p, dev), seeds, step, toks, _none(probs, dev))
+    return toks, probs, ids

@@ -80,8 +80,13 @@ class FusedComm:
     def gemm_push(self, q, s, w) -> PushedPartial:
         """Row-parallel W4A8 GEMM whose output tiles go straight into every rank's receive
         buffer; the following all-reduce call reduces them."""
-        exp = ext().mxfp4_gemm_push(q, s, w.packed, w.sf, self.push_ptrs, self.rank,
-                                    self.push_half_words, status_word(q.device))
+        from ..models.layers import GEMV_ON
+        from ..ops import kernels as K
+        if GEMV_ON and q.shape[0] <= K.GEMV_MAX_ROWS:
+            exp = K.mxfp4_gemv_push(q, s, w, self.push_ptrs, self.rank, self.push_half_words)
+        else:
+            exp = ext().mxfp4_gemm_push(q, s, w.packed, w.sf, self.push_ptrs, self.rank,
+                                        self.push_half_words, status_word(q.device))
         self.pushes += 1
         return PushedPartial(q.shape[0], w.N, int(exp), q.device)
 
