@@ -357,3 +357,25 @@ def test_tier_restore_skips_when_every_snapshot_slot_is_pinned():
     assert kv.snap_lru[sid] == kv._hashes(a[:48])[-1]
     kv.release_restore(b)
     assert kv.match_prefix(c) == 48 and tier.restored == 1 and c.restore_snapshot == sid
+
+
+def test_step_trace_summaries():
+    """RADIANCE_STEP_TRACE=N: a summary every N steps with the per-phase medians."""
+    eng = _engine(4096)
+    from vllm_sly_radiance_b200.utils.step_trace import StepTrace
+    eng.trace = StepTrace(every=3, device="cpu")
+    eng.generate([list(range(10, 40))], SamplingParams(temperature=0, max_tokens=7, ignore_eos=True))
+    assert len(eng.trace.summaries) == 2
+    s = eng.trace.summaries[0]
+    assert s["steps"] == 3 and s["execute"] > 0 and "interval" in s
+
+
+def test_workspace_growth_keeps_old_buffers_alive():
+    """An outgrown kernel workspace stays allocated: CUDA graphs captured with it still address
+    its counters."""
+    from vllm_sly_radiance_b200.ops import kernels as K
+    a = K.workspace("cpu", "test_grow", 10)
+    b = K.workspace("cpu", "test_grow", 1 << 17)
+    assert b.numel() >= 1 << 17 and b.data_ptr() != a.data_ptr()
+    assert any(t is a for t in K._WS_RETIRED)
+    assert K.workspace("cpu", "test_grow", 5) is b

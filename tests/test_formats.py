@@ -139,3 +139,19 @@ def test_int4_fragment_tiling_roundtrip():
     sw = int(sz[1, 2, 5, 0]) & 0xFFFF
     assert torch.tensor([sw], dtype=torch.int32).to(torch.int16).view(torch.float16) == w.scales[21, 2]
     assert ((int(sz[1, 2, 5, 1]) >> 16) & 0xFFFF) - 0x4300 == int(w.zeros[29, 2])
+
+
+def test_quant_embedding_roundtrip():
+    """int8 (per-row) and int4 (g128) embedding tables: the lookup dequantises to within half a
+    quantisation step of the bf16 table (reference: radiance_embed_int8.py:47-114)."""
+    from vllm_sly_radiance_b200.quant.embed import QuantEmbedding
+    g = torch.Generator().manual_seed(0)
+    w = (torch.randn(300, 256, generator=g) * 0.05).to(torch.bfloat16)
+    ids = torch.tensor([0, 5, 299, 5, 17])
+    for bits, tol in ((8, 1 / 127), (4, 1 / 7)):
+        qe = QuantEmbedding.from_float(w, bits)
+        got = qe[ids].float()
+        want = w[ids].float()
+        step = want.abs().amax(1, keepdim=True) * tol
+        assert ((got - want).abs() <= 0.51 * step + 4e-3 * want.abs()).all(), bits
+    assert QuantEmbedding.from_float(w, 4).nbytes < w.numel() * 2 // 3

@@ -96,12 +96,14 @@ def test_mxfp4_gemv(M, N, Kd):
         assert rel_err(got, want) < 1e-2, (rep, rel_err(got, want))
 
 
+@pytest.mark.parametrize("impl", ["cluster", "gemv"])
 @pytest.mark.parametrize("mode,M,N,Kd,with_res", [
     (1, 1, 5120, 6144, True), (1, 4, 5120, 8704, True), (1, 1, 2048, 1088, False),
     (2, 1, 17408, 5120, False), (2, 3, 4352, 5120, False), (2, 16, 768, 256, False)])
-def test_mxfp4_gemv_finisher(mode, M, N, Kd, with_res):
-    """The finisher of the last tile (residual add + RMSNorm + e4m3, or SiLU * mul + e4m3) equals
-    the stand-alone producer applied to the GEMM output."""
+def test_mxfp4_gemv_finisher(mode, M, N, Kd, with_res, impl):
+    """The finisher run by the last CTA (residual add + RMSNorm + e4m3, or SiLU * mul + e4m3), in
+    the split-K cluster decode GEMM and in the persistent stream-K one, equals the stand-alone
+    producer applied to the GEMM output."""
     g = torch.Generator().manual_seed(M * 5 + N + mode)
     wq = MXFP4Weight.from_float(torch.randn(N, Kd, generator=g) * 0.02).to(DEV)
     x = torch.randn(M, Kd, generator=g).to(torch.bfloat16).to(DEV)
@@ -111,12 +113,18 @@ def test_mxfp4_gemv_finisher(mode, M, N, Kd, with_res):
             res = torch.randn(M, N, generator=g).to(torch.bfloat16).to(DEV) if with_res else None
             lw = (0.1 * torch.randn(N, generator=g)).to(torch.bfloat16).to(DEV)
             ro = torch.empty(M, N, dtype=torch.bfloat16, device=DEV)
-            out, fq, fs = K.mxfp4_gemv(q, s, wq, None, K.FIN_NORM, res, lw, ro, 1e-6)
+            if impl == "gemv":
+                out, fq, fs = K.mxfp4_gemv(q, s, wq, None, K.FIN_NORM, res, lw, ro, 1e-6)
+            else:
+                out, fq, fs = K.mxfp4_gemm_finish(q, s, wq, K.FIN_NORM, res, lw, ro, 1e-6)
             wq_, ws_, wr = K.add_rms_quant(out, res, lw, 1e-6)
             torch.cuda.synchronize()
             assert torch.equal(ro, wr)
         else:
-            out, fq, fs = K.mxfp4_gemv(q, s, wq, None, K.FIN_SILU)
+            if impl == "gemv":
+                out, fq, fs = K.mxfp4_gemv(q, s, wq, None, K.FIN_SILU)
+            else:
+                out, fq, fs = K.mxfp4_gemm_finish(q, s, wq, K.FIN_SILU)
             wq_, ws_ = K.silu_mul_quant(out)
             torch.cuda.synchronize()
         K.check_status(out.device)
@@ -683,3 +691,17 @@ def test_segment_copy_gather_scatter_roundtrip():
         assert torch.equal(t[[1, 5, 9]], r[[7, 2, 11]])
         keep = [j for j in range(12) if j not in (1, 5, 9)]
         assert torch.equal(t[keep], r[keep])
+
+
+@pytest.mark.parametrize("bits", [8, 4])
+def test_embed_gather_quantised(bits):
+    """int8 / int4-g128 embedding lookup kernel equals the PyTorch dequantisation of the rows."""
+    from vllm_sly_radiance_b200.quant.embed import QuantEmbedding
+    g = torch.Generator().manual_seed(bits)
+    w = (torch.randn(1000, 5120, generator=g) * 0.03).to(torch.bfloat16)
+    qe = QuantEmbedding.from_float(w, bits)
+    ids = torch.tensor([3, 999, 0, 3, 512, 77], dtype=torch.int64)
+    want = qe.dequantize_rows(ids)
+    got = qe.to(DEV)[ids.to(DEV)]
+    torch.cuda.synchronize()
+    assert torch.equal(got.cpu(), want)

@@ -153,3 +153,18 @@ def test_mtp_chunked_prefill_bookkeeping():
     (ids_b, p_b), _ = first_state(256)
     assert torch.equal(ids_a[0], ids_b[0])          # first draft step: same top window
     assert torch.equal(ids_a, ids_b)
+
+
+def test_dflash2_prefill_window_skip_is_lossless(monkeypatch):
+    """Prompt rows farther than window + margin from the prompt's end get no drafter context K/V
+    (the drafter only attends inside its sliding window): rows are skipped, and greedy output stays
+    identical to plain decoding (reference: sly/radiance_dflash_skip.py)."""
+    monkeypatch.setenv("RADIANCE_DFLASH_PREFILL_WINDOW_SKIP_MARGIN", "16")
+    prompt = list(range(50, 350))
+    sp = SamplingParams(temperature=0, max_tokens=8, ignore_eos=True)
+    base = _engine().generate([prompt], sp)[0].outputs[0].token_ids
+    eng = _engine("dflash2")
+    assert eng.spec.drafter._prefill_skip_span() < len(prompt)
+    out = eng.generate([prompt], sp)[0].outputs[0].token_ids
+    assert out == base
+    assert eng.spec.drafter.skipped_rows > 0

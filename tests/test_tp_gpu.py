@@ -92,6 +92,38 @@ def _run(rank, world, port, outq):
             out[f"pushq{N}_{M}"] = float(((q1.float() * s1[:, None]) - (q2.float() * s2[:, None])).abs().max())
     K.check_status(torch.device("cuda", rank))
     _log(rank, "gemm push checks done")
+    # 1c) prefill-sized two-shot all-reduce (reduce-scatter + all-gather pushes), plain, fused with
+    # residual add + RMSNorm + e4m3, and with the reduce-scatter issued by the GEMM epilogue
+    for M in (300, 1031, 4096):
+        x = torch.randn(M, 5120, generator=g).to(torch.bfloat16).cuda()
+        ref = x.float().clone()
+        dist.all_reduce(ref)
+        got = tp.all_reduce(x.clone())
+        out[f"ts{M}"] = float((got.float() - ref).abs().max() / ref.abs().max())
+        res = torch.randn(M, 5120, generator=g).to(torch.bfloat16).cuda()
+        wn = (0.1 * torch.randn(5120, generator=g)).to(torch.bfloat16).cuda()
+        q1, s1, r1 = tp.all_reduce_add_rms_quant(x.clone(), res, wn, 1e-6)
+        q2, s2, r2 = K.add_rms_quant(ref.to(torch.bfloat16), res, wn, 1e-6)
+        out[f"tsq{M}"] = float(((q1.float() * s1[:, None]) - (q2.float() * s2[:, None])).abs().max())
+    w = MXFP4Weight.from_float(torch.randn(5120, 2048, generator=g) * 0.02).to("cuda")
+    for M in (300, 2048):
+        xa = torch.randn(M, 2048, generator=g).to(torch.bfloat16).cuda()
+        qa, sa = K.quant_fp8(xa)
+        local = K.mxfp4_gemm(qa, sa, w.packed, w.sf, w.scales, 5120)
+        ref = local.float().clone()
+        dist.all_reduce(ref)
+        for rep in range(2):
+            pp = tp.fused.gemm_push(qa, sa, w)
+            assert pp.kind == "rs"
+            got = tp.fused.all_reduce(pp)
+            out[f"rs{M}_{rep}"] = float((got.float() - ref).abs().max() / ref.abs().max())
+        res = torch.randn(M, 5120, generator=g).to(torch.bfloat16).cuda()
+        wn = (0.1 * torch.randn(5120, generator=g)).to(torch.bfloat16).cuda()
+        q1, s1, r1 = tp.fused.all_reduce_add_rms_quant(tp.fused.gemm_push(qa, sa, w), res, wn, 1e-6)
+        q2, s2, r2 = K.add_rms_quant(ref.to(torch.bfloat16), res, wn, 1e-6)
+        out[f"rsq{M}"] = float(((q1.float() * s1[:, None]) - (q2.float() * s2[:, None])).abs().max())
+    K.check_status(torch.device("cuda", rank))
+    _log(rank, "two-shot checks done")
     # 2) TP=2 tiny model (fused path) vs single-GPU logits
     cfg = EngineConfig(model="tiny_hybrid", device="cuda", max_model_len=512, max_num_seqs=2,
                        max_num_batched_tokens=128, num_kv_blocks=32, enable_cuda_graphs=True)
@@ -102,6 +134,17 @@ def _run(rank, world, port, outq):
     out["toks"] = o[0].outputs[0].token_ids
     _log(rank, f"generate done {out['toks']}")
     eng.runner.graphs.clear()
+    # 3) bf16 weights: the whole greedy sequence must match TP1 (a 300-token prompt also takes
+    # the two-shot all-reduce in prefill)
+    mb = HybridModel(tiny_hybrid(), quant="bf16", device="cuda", seed=0, tp=tp, init_device="cpu")
+    cfgb = EngineConfig(model="tiny_hybrid", device="cuda", max_model_len=1024, max_num_seqs=2,
+                        max_num_batched_tokens=512, num_kv_blocks=64, enable_cuda_graphs=True,
+                        quantization="bf16")
+    engb = LLMEngine(cfgb, model=mb, tp=tp)
+    ob = engb.generate([list(range(7, 307))], SamplingParams(temperature=0, max_tokens=16,
+                                                              ignore_eos=True))
+    out["toks_bf16"] = ob[0].outputs[0].token_ids
+    engb.runner.graphs.clear()
     tp.fused.close()
     dist.barrier()
     dist.destroy_process_group()
@@ -149,9 +192,23 @@ def test_tp2_fused_allreduce_and_model():
         for M in (1, 5, 16):
             assert res[f"push{N}_{M}"] < 1e-2, res
             assert res[f"pushq{N}_{M}"] < 0.25, res
+    for M in (300, 1031, 4096):
+        assert res[f"ts{M}"] < 1e-2, res
+        assert res[f"tsq{M}"] < 0.25, res
+    for M in (300, 2048):
+        assert res[f"rs{M}_0"] < 1e-2 and res[f"rs{M}_1"] < 1e-2, res
+        assert res[f"rsq{M}"] < 0.25, res
     cfg = EngineConfig(model="tiny_hybrid", device="cuda", max_model_len=512, max_num_seqs=2,
                        max_num_batched_tokens=128, num_kv_blocks=32)
     m = HybridModel(tiny_hybrid(), quant="mxfp4", device="cuda", seed=0, init_device="cpu")
     ref = LLMEngine(cfg, model=m).generate([list(range(40, 100))],
                                           SamplingParams(temperature=0, max_tokens=6, ignore_eos=True))
     assert res["toks"][:2] == ref[0].outputs[0].token_ids[:2]
+    cfgb = EngineConfig(model="tiny_hybrid", device="cuda", max_model_len=1024, max_num_seqs=2,
+                        max_num_batched_tokens=512, num_kv_blocks=64, quantization="bf16")
+    mb = HybridModel(tiny_hybrid(), quant="bf16", device="cuda", seed=0, init_device="cpu")
+    refb = LLMEngine(cfgb, model=mb).generate([list(range(7, 307))],
+                                              SamplingParams(temperature=0, max_tokens=16,
+                                                             ignore_eos=True))
+    assert res["toks_bf16"] == refb[0].outputs[0].token_ids, (res["toks_bf16"],
+                                                              refb[0].outputs[0].token_ids)

@@ -266,6 +266,7 @@ class EngineConfig:
     quantization: str = "mxfp4"         # mxfp4 (W4A8) | bf16 | nvfp4 (requantized to mxfp4) | int4
     kv_cache_dtype: str = "fp8"         # fp8 | int4 (4-bit per-16 scale/zero) | bf16
     lm_head_quant: Optional[str] = None  # None (the model's) | int4 (W4A16 g128) | bf16 | mxfp4
+    embed_quant: Optional[str] = None    # None (bf16) | int8 (per-row scale) | int4 (g128 scales)
     ssm_state_dtype: str = "float32"    # float32 | bfloat16
     block_size: int = 64                # KV page size in tokens
     max_model_len: int = 65536

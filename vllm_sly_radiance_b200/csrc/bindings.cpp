@@ -60,6 +60,22 @@ void mxfp4_gemv(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch:
 int64_t mxfp4_gemv_push(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
                         torch::Tensor ws, int64_t ctas_per_sm, std::vector<int64_t> peers,
                         int64_t rank, int64_t half_words, torch::Tensor status);
+int64_t mxfp4_gemm_rs(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
+                      std::vector<int64_t> peers, int64_t rank, int64_t per, torch::Tensor status);
+int64_t ts_header_bytes();
+int64_t ts_buffer_bytes(int64_t mmax, int64_t H);
+int64_t ts_rows_per_rank(int64_t M, int64_t world);
+void ts_allreduce(std::vector<int64_t> peers, int64_t rank, int64_t M, int64_t H,
+                  int64_t buf_bytes, torch::Tensor x, bool pushed, int64_t expected,
+                  torch::Tensor out, torch::Tensor residual, torch::Tensor weight, double eps,
+                  torch::Tensor res_out, torch::Tensor q, torch::Tensor scale,
+                  torch::Tensor status);
+void embed_gather(torch::Tensor codes, torch::Tensor scales, torch::Tensor ids, int64_t bits,
+                  torch::Tensor out);
+void mxfp4_gemm_fin(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
+                    torch::Tensor out, int64_t fin_mode, torch::Tensor res, torch::Tensor w,
+                    torch::Tensor res_out, torch::Tensor q, torch::Tensor scale, double eps,
+                    torch::Tensor ws, torch::Tensor status);
 void mxfp4_gemm_act(int64_t mode, torch::Tensor x, torch::Tensor res, torch::Tensor w,
                     torch::Tensor res_out, double eps, torch::Tensor wp, torch::Tensor sf,
                     torch::Tensor out, torch::Tensor status);
@@ -153,6 +169,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "persistent stream-K decode W4A8 GEMM (<= 16 rows) with an optional fused row finisher");
   m.def("mxfp4_gemv_push", &rad::mxfp4_gemv_push,
         "persistent decode W4A8 GEMM pushing its tiles into every rank's receive buffer");
+  m.def("mxfp4_gemm_rs", &rad::mxfp4_gemm_rs,
+        "row-parallel W4A8 GEMM pushing its rows into their owners' two-shot slots");
+  m.def("ts_header_bytes", &rad::ts_header_bytes, "two-shot all-reduce buffer header bytes");
+  m.def("ts_buffer_bytes", &rad::ts_buffer_bytes, "two-shot all-reduce buffer bytes");
+  m.def("ts_rows_per_rank", &rad::ts_rows_per_rank, "rows owned per rank by the two-shot all-reduce");
+  m.def("ts_allreduce", &rad::ts_allreduce,
+        "two-shot NVLink all-reduce (+ residual add + RMSNorm + e4m3) for prefill-sized messages");
+  m.def("embed_gather", &rad::embed_gather, "int8 / int4-g128 embedding lookup into bf16 rows");
+  m.def("mxfp4_gemm_fin", &rad::mxfp4_gemm_fin,
+        "decode W4A8 GEMM whose last CTA also runs the next linear's producer over the rows");
   m.def("mxfp4_gemm_act", &rad::mxfp4_gemm_act,
         "decode W4A8 GEMM with its producer fused in (1: add + RMSNorm + e4m3, 2: SiLU*mul + e4m3)");
   m.def("push_allreduce_recv", &rad::push_allreduce_recv,

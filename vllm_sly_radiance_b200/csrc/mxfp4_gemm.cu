@@ -31,6 +31,7 @@
 #include <unordered_map>
 
 #include "common.cuh"
+#include "finish.cuh"
 #include "tma_host.h"
 
 namespace rad {
@@ -151,14 +152,36 @@ DEVI float prod_max(float v, float* red) {
   return fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
 }
 
-template <int BN, bool GROUPED = false, bool PUSH = false, int ACT = 0>
+// RS: reduce-scatter push for the prefill two-shot all-reduce (comm_ts.cu): output row m goes to
+// its owner's source slot (push.peer[o], o = m / per with per = push.half_words, row length
+// push.ld) as bf16 pairs; once the CTA's stores are fenced it adds 1 to every owner's arrival
+// counter of this rank.
+constexpr int kTsHeader = 8192;   // comm_ts.cu buffer header bytes
+
+DEVI void rs_store(const PushArgs& pa, int m, int n, float lo, float hi) {
+  const int per = (int)pa.half_words;
+  const int o = m / per;
+  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(pa.peer[o] + kTsHeader) +
+                       ((size_t)pa.rank * per + (m - o * per)) * pa.ld + n;
+  *reinterpret_cast<__nv_bfloat162*>(dst) = __floats2bfloat162_rn(lo, hi);
+}
+
+// FIN (decode, BN = 16): the CTA that arrives last on a self-resetting counter, after every CTA
+// has written its output rows, runs the next linear's producer over the whole rows (finish.cuh):
+// residual add + RMSNorm(1 + w) + e4m3, or SiLU * mul + e4m3.
+struct FinCtl {
+  unsigned* done;   // arrival counter (zero, self-resetting)
+  FinArgs args;
+};
+
+template <int BN, bool GROUPED = false, bool PUSH = false, int ACT = 0, bool RS = false, int FIN = 0>
 __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
     mxfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                       const __grid_constant__ CUtensorMap tmap_a, const uint8_t* __restrict__ sfw,
                       const float* __restrict__ a_scale, __nv_bfloat16* __restrict__ out,
                       int ldo, int M, int N, int K, int k_tiles_per_split, int* __restrict__ status,
                       const int* __restrict__ items, int n_per_group, const PushArgs push,
-                      const ActArgs act) {
+                      const ActArgs act, const FinCtl fin) {
   using C = Cfg<BN>;
   // Grouped (MoE) mode: blockIdx.y indexes a work table of (expert, first row, rows); the
   // expert's weights are rows [e * n_per_group, (e + 1) * n_per_group) of the stacked tensor.
@@ -425,6 +448,9 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
               for (int p = 0; p < push.world; ++p)
                 st_ll_pair(push_slot(push, p, seq & 1u, push.rank, M) + (size_t)m * (push.ld / 2) + n / 2,
                            v, vn, seq);
+          } else if constexpr (RS) {
+            const float vn = __shfl_down_sync(0xffffffffu, v, 1);
+            if ((lane & 1) == 0 && n < n_lim) rs_store(push, m, n, v, vn);
           } else if (n < n_lim) {
             out[(size_t)m * ldo + n] = __float2bfloat16_rn(v);
           }
@@ -474,6 +500,9 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
             for (int p = 0; p < push.world; ++p)
               st_ll_pair(push_slot(push, p, seq & 1u, push.rank, M) + (size_t)m * (push.ld / 2) + n / 2,
                          acc, vn, seq);
+        } else if constexpr (RS) {
+          const float vn = __shfl_down_sync(0xffffffffu, acc, 1);
+          if ((lane & 1) == 0 && n < n_lim) rs_store(push, m, n, acc, vn);
         } else if (n < n_lim) {
           out[(size_t)m * ldo + n] = __float2bfloat16_rn(acc);
         }
@@ -488,6 +517,33 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+  if constexpr (FIN != 0) {
+    __shared__ bool s_fin;
+    __shared__ float s_fred[kThreads / 32];
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned total = gridDim.x * gridDim.y * gridDim.z;
+      s_fin = atomicAdd(fin.done, 1u) == total - 1u;
+      if (s_fin) *fin.done = 0u;
+    }
+    __syncthreads();
+    if (s_fin) {     // every CTA's rows are written: finish them with all six warps
+      __threadfence();
+      float* buf = reinterpret_cast<float*>(stage_base);
+      for (int m = 0; m < M; ++m) finish_row<kThreads, FIN>(fin.args, out, ldo, N, m, buf, s_fred);
+    }
+  }
+  if constexpr (RS) {
+    // this CTA's rows are stored in their owners' slots: one arrival at every owner
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0)
+      for (int o = 0; o < push.world; ++o)
+        asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(
+                         reinterpret_cast<uint32_t*>(push.peer[o]) + push.rank),
+                     "r"(1u) : "memory");
   }
 }
 
@@ -528,7 +584,8 @@ template <int BN>
 static void launch(const torch::Tensor& a, const torch::Tensor& a_scale, const torch::Tensor& wp,
                    const torch::Tensor& sf, torch::Tensor& out, int M, int N, int K, int splits,
                    int* status, cudaStream_t stream, const PushArgs& push, int act_mode = 0,
-                   const ActArgs& aa = ActArgs{}) {
+                   const ActArgs& aa = ActArgs{}, bool rs = false, int fin_mode = 0,
+                   const FinCtl& fc = FinCtl{}) {
   using C = Cfg<BN>;
   const int Kw = (int)wp.size(1) * 2;          // whole K tiles of stored weight
   CUtensorMap tw = weight_map(wp, N, Kw);
@@ -542,13 +599,14 @@ static void launch(const torch::Tensor& a, const torch::Tensor& a_scale, const t
   using KernT = decltype(&mxfp4_gemm_kernel<BN, false, false, 0>);
   KernT kern = push.world ? mxfp4_gemm_kernel<BN, false, true, 0> : mxfp4_gemm_kernel<BN, false, false, 0>;
   int variant = push.world ? 1 : 0;
+  if (rs) { kern = mxfp4_gemm_kernel<BN, false, false, 0, true>; variant = 4; }
   if constexpr (BN == 16) {
     if (act_mode == 1) { kern = mxfp4_gemm_kernel<BN, false, false, 1>; variant = 2; }
     if (act_mode == 2) { kern = mxfp4_gemm_kernel<BN, false, false, 2>; variant = 3; }
   } else {
     TORCH_CHECK(act_mode == 0, "fused producers need a 16-row tile");
   }
-  static bool attr_set[4] = {false, false, false, false};
+  static bool attr_set[5] = {false, false, false, false, false};
   if (!attr_set[variant]) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
@@ -568,11 +626,12 @@ static void launch(const torch::Tensor& a, const torch::Tensor& a_scale, const t
   attrs[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attrs;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  const bool no_out = push.world || rs;
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tw, ta, (const uint8_t*)sf.data_ptr(),
                                     act_mode ? (const float*)nullptr : (const float*)a_scale.data_ptr(),
-                                    push.world ? nullptr : (__nv_bfloat16*)out.data_ptr(),
-                                    push.world ? 0 : (int)out.stride(0), M, N, Kw,
-                                    per, status, (const int*)nullptr, 0, push, aa));
+                                    no_out ? nullptr : (__nv_bfloat16*)out.data_ptr(),
+                                    no_out ? 0 : (int)out.stride(0), M, N, Kw,
+                                    per, status, (const int*)nullptr, 0, push, aa, fc));
 }
 
 static int pick_splits(int tiles, int k_tiles, int ctas_per_sm) {
@@ -606,7 +665,7 @@ static void launch_grouped(const torch::Tensor& a, const torch::Tensor& a_scale,
                             (const uint8_t*)sf.data_ptr(), (const float*)a_scale.data_ptr(),
                             (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), M, Ntot, K,
                             K / BK, status, (const int*)items.data_ptr(), n_per_group, PushArgs{},
-                            ActArgs{}));
+                            ActArgs{}, FinCtl{}));
 }
 
 }  // namespace mxfp4
@@ -640,9 +699,9 @@ void mxfp4_grouped_gemm(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp
 // tiles (= arrivals each peer receives from this rank).
 static int64_t mxfp4_gemm_impl(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp,
                                torch::Tensor sf, torch::Tensor out, int64_t splits_override,
-                               torch::Tensor status, const PushArgs& push) {
+                               torch::Tensor status, const PushArgs& push, bool rs = false) {
   using namespace mxfp4;
-  const bool has_out = !push.world;
+  const bool has_out = !push.world && !rs;
   TORCH_CHECK(a.is_cuda() && wp.is_cuda() && (!has_out || out.is_cuda()),
               "mxfp4_gemm: CUDA tensors required");
   TORCH_CHECK(a.scalar_type() == at::kFloat8_e4m3fn, "activations must be float8_e4m3fn");
@@ -660,7 +719,7 @@ static int64_t mxfp4_gemm_impl(torch::Tensor a, torch::Tensor a_scale, torch::Te
               "activation rows must be 16-byte aligned");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(wp.data_ptr()) % 32) == 0 && (wp.stride(0) % 32) == 0,
               "weight rows must be 32-byte aligned");
-  if (!push.world) TORCH_CHECK(out.size(0) >= M && out.size(1) >= N, "output too small");
+  if (has_out) TORCH_CHECK(out.size(0) >= M && out.size(1) >= N, "output too small");
   if (M == 0) return 0;
   const at::cuda::CUDAGuard guard(a.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
@@ -674,6 +733,16 @@ static int64_t mxfp4_gemm_impl(torch::Tensor a, torch::Tensor a_scale, torch::Te
   const int tiles = ((N + BM - 1) / BM) * ((M + bn - 1) / bn);
   int splits = splits_override > 0 ? (int)splits_override
                                    : pick_splits(tiles, Kw / BK, bn <= 64 ? 2 : 1);
+  if (rs) {
+    // every CTA adds one arrival at every owner: the count the owner waits for
+    switch (bn) {
+      case 64: launch<64>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream, push, 0, ActArgs{}, true); break;
+      case 128: launch<128>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream, push, 0, ActArgs{}, true); break;
+      case 256: launch<256>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream, push, 0, ActArgs{}, true); break;
+      default: TORCH_CHECK(false, "mxfp4_gemm_rs: more than 32 rows");
+    }
+    return (int64_t)tiles * splits;
+  }
   switch (bn) {
     case 16: launch<16>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream, push); break;
     case 32: launch<32>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream, push); break;
@@ -687,6 +756,60 @@ static int64_t mxfp4_gemm_impl(torch::Tensor a, torch::Tensor a_scale, torch::Te
 void mxfp4_gemm(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
                 torch::Tensor out, int64_t splits_override, torch::Tensor status) {
   mxfp4_gemm_impl(a, a_scale, wp, sf, out, splits_override, status, PushArgs{});
+}
+
+// Decode GEMM (M <= 16) followed, in the same launch, by the next linear's producer over its
+// output rows: fin_mode 1 = residual add + RMSNorm(1 + w) + e4m3 (res optional, res_out optional,
+// q [M, N]), 2 = SiLU(g) * u + e4m3 with out = [g | u] (q [M, N / 2]).  ws: int32 [>= 1] zero
+// arrival counter (self-resetting).
+void mxfp4_gemm_fin(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
+                    torch::Tensor out, int64_t fin_mode, torch::Tensor res, torch::Tensor w,
+                    torch::Tensor res_out, torch::Tensor q, torch::Tensor scale, double eps,
+                    torch::Tensor ws, torch::Tensor status) {
+  using namespace mxfp4;
+  TORCH_CHECK(fin_mode == kFinNorm || fin_mode == kFinSilu, "mxfp4_gemm_fin: mode 1 or 2");
+  TORCH_CHECK(a.scalar_type() == at::kFloat8_e4m3fn && a.dim() == 2 && a.stride(1) == 1 &&
+                  (a.stride(0) % 16) == 0 && (reinterpret_cast<uintptr_t>(a.data_ptr()) % 16) == 0,
+              "mxfp4_gemm_fin: e4m3 activation rows, 16-byte aligned");
+  const int M = a.size(0), K = a.size(1), N = wp.size(0);
+  const int Kw = (int)wp.size(1) * 2;
+  TORCH_CHECK(M >= 1 && M <= 16, "mxfp4_gemm_fin: 1..16 rows");
+  TORCH_CHECK(K % 32 == 0 && Kw % BK == 0 && Kw >= K && Kw - K < BK, "mxfp4_gemm_fin: K");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(wp.data_ptr()) % 32) == 0 && (wp.stride(0) % 32) == 0,
+              "mxfp4_gemm_fin: weight rows 32-byte aligned");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(1) == 1 && out.size(0) >= M &&
+                  out.size(1) >= N && out.stride(0) % 8 == 0 &&
+                  (reinterpret_cast<uintptr_t>(out.data_ptr()) % 16) == 0, "mxfp4_gemm_fin: out");
+  const int H = fin_mode == kFinNorm ? N : N / 2;
+  TORCH_CHECK(N % 16 == 0 && H * 4 <= Cfg<16>::STAGES * Cfg<16>::STAGE_BYTES, "finisher row length");
+  TORCH_CHECK(q.scalar_type() == at::kFloat8_e4m3fn && q.stride(1) == 1 && q.size(0) >= M &&
+                  q.size(1) >= H && q.stride(0) % 8 == 0, "mxfp4_gemm_fin: q");
+  TORCH_CHECK(scale.scalar_type() == at::kFloat && scale.numel() >= M, "mxfp4_gemm_fin: scale");
+  TORCH_CHECK(ws.scalar_type() == at::kInt && ws.numel() >= 1, "mxfp4_gemm_fin: ws");
+  FinCtl fc{};
+  fc.done = reinterpret_cast<unsigned*>(ws.data_ptr<int>());
+  fc.args.q = (uint8_t*)q.data_ptr();
+  fc.args.ldq = (int)q.stride(0);
+  fc.args.scale = scale.data_ptr<float>();
+  fc.args.eps = (float)eps;
+  if (fin_mode == kFinNorm) {
+    TORCH_CHECK(w.defined() && w.numel() >= N && w.scalar_type() == at::kBFloat16, "norm weight");
+    fc.args.w = (const __nv_bfloat16*)w.data_ptr();
+    const bool hr = res.defined() && res.numel(), ho = res_out.defined() && res_out.numel();
+    TORCH_CHECK(!hr || (res.stride(1) == 1 && res.stride(0) % 8 == 0), "res rows");
+    TORCH_CHECK(!ho || (res_out.stride(1) == 1 && res_out.stride(0) % 8 == 0), "res_out rows");
+    fc.args.res = hr ? (const __nv_bfloat16*)res.data_ptr() : nullptr;
+    fc.args.ldr = hr ? (int)res.stride(0) : 0;
+    fc.args.res_out = ho ? (__nv_bfloat16*)res_out.data_ptr() : nullptr;
+    fc.args.ldro = ho ? (int)res_out.stride(0) : 0;
+  }
+  const at::cuda::CUDAGuard guard(a.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  int* st = status.numel() ? status.data_ptr<int>() : nullptr;
+  const int tiles = (N + BM - 1) / BM;
+  const int splits = pick_splits(tiles, Kw / BK, 2);
+  launch<16>(a, a_scale, wp, sf, out, M, N, K, splits, st, stream, PushArgs{}, 0, ActArgs{}, false,
+             (int)fin_mode, fc);
 }
 
 // Decode GEMM (M <= 16) with its producer fused in: mode 1 = residual add + RMSNorm(1 + w) +
@@ -732,6 +855,25 @@ void mxfp4_gemm_act(int64_t mode, torch::Tensor x, torch::Tensor res, torch::Ten
   const int tiles = (N + BM - 1) / BM;
   const int splits = pick_splits(tiles, Kw / BK, 2);
   launch<16>(x, x, wp, sf, out, M, N, K, splits, st, stream, PushArgs{}, (int)mode, aa);
+}
+
+// Row-parallel GEMM fused with the reduce-scatter half of the prefill two-shot all-reduce
+// (comm_ts.cu): output row m is stored into its owner's slot of this rank in the owner's buffer
+// (peers = every rank's two-shot buffer, per = rows per owner).  Returns the CTA count, which is
+// the arrival count each owner waits for.
+int64_t mxfp4_gemm_rs(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
+                      std::vector<int64_t> peers, int64_t rank, int64_t per, torch::Tensor status) {
+  const int world = peers.size();
+  TORCH_CHECK(world >= 1 && world <= 8, "rs: world size 1..8");
+  TORCH_CHECK(wp.size(0) % 8 == 0, "rs: output features must be a multiple of 8");
+  TORCH_CHECK(per * world >= a.size(0) && per % 8 == 0, "rs: rows per owner");
+  PushArgs pa{};
+  for (int i = 0; i < world; ++i) pa.peer[i] = (uint8_t*)(uintptr_t)peers[i];
+  pa.world = world;
+  pa.rank = (int)rank;
+  pa.half_words = per;
+  pa.ld = (int)wp.size(0);
+  return mxfp4_gemm_impl(a, a_scale, wp, sf, torch::Tensor(), 0, status, PushArgs{pa}, true);
 }
 
 // Row-parallel GEMM fused with the push half of the all-reduce: peers = every rank's receive

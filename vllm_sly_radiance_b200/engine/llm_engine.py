@@ -43,7 +43,8 @@ class LLMEngine:
             if quant == "nvfp4":
                 quant = "mxfp4"
             model = HybridModel(mcfg, quant=quant, device=self.device, seed=config.seed, tp=self.tp,
-                                lm_head_quant=config.lm_head_quant)
+                                lm_head_quant=config.lm_head_quant,
+                                embed_quant=config.embed_quant)
         self.model = model
         self.load_time = time.time() - t0
         self.tokenizer = tokenizer or get_tokenizer(tokenizer_path, mcfg.vocab_size)
@@ -51,8 +52,17 @@ class LLMEngine:
         # ---- cache sizing ----
         bs = config.block_size
         num_slots = config.max_num_seqs + 2
+        pin = None
+        if not config.num_kv_blocks and self.device.type == "cuda":
+            # a pool size measured on this device by `calibrate-kv`, when one exists
+            from ..entrypoints.hw import lookup_pin
+            pin = lookup_pin(torch.cuda.get_device_name(self.device), config.model,
+                             config.tensor_parallel_size, config.max_num_seqs,
+                             config.max_num_batched_tokens)
         if config.num_kv_blocks:
             num_blocks = config.num_kv_blocks
+        elif pin:
+            num_blocks = pin
         elif self.device.type == "cuda":
             torch.cuda.synchronize()
             free, total = torch.cuda.mem_get_info(self.device)
@@ -100,6 +110,8 @@ class LLMEngine:
         self.requests: dict[str, Request] = {}
         self.detok: dict[str, IncrementalDetokenizer] = {}
         self.metrics = EngineMetrics()
+        from ..utils.step_trace import StepTrace
+        self.trace = StepTrace(device=self.device)     # RADIANCE_STEP_TRACE=N
         self.faults = 0
         self.kv_tokens_capacity = self.num_blocks * bs
         log.info("engine ready: %d KV blocks (%d tokens), %d state slots, load %.1fs",
@@ -129,7 +141,9 @@ class LLMEngine:
     # ------------------------------------------------------------------------------------------
     def step(self) -> list[RequestOutput]:
         t0 = time.perf_counter()
+        tr = self.trace.begin()
         sched = self.scheduler.schedule()
+        self.trace.mark(tr, "t_sched")
         if self.kv.offload is not None:
             self.kv.flush_offload()    # write-backs of blocks evicted by this schedule
         if sched.is_empty:
@@ -152,6 +166,7 @@ class LLMEngine:
             raise EngineStepError(f"engine step failed: {e!r}") from e
         if code:
             self._fail_open_requests(code)
+        self.trace.mark(tr, "t_exec")
         finished = self.scheduler.update(sched, result.sampled)
         if self.kv.num_snapshots:
             for s in sched.seqs:
@@ -189,6 +204,7 @@ class LLMEngine:
                 self.metrics.on_finish(req)
                 self.requests.pop(rid, None)
                 self.detok.pop(rid, None)
+        self.trace.end(tr, result.num_tokens)
         return outs
 
     def _fail_open_requests(self, code: int):

@@ -37,6 +37,16 @@ def _parser():
             s.add_argument(flag, dest=f.name, action=argparse.BooleanOptionalAction, default=None)
         else:
             s.add_argument(flag, dest=f.name, default=None)
+    d = sub.add_parser("gpus", help="detect usable GPUs, pick the TP size, show the KV pin")
+    d.add_argument("--model", default="qwen38_27b")
+    d.add_argument("--min-gpu-mib", type=int, default=8192)
+    c = sub.add_parser("calibrate-kv", help="measure the largest KV pool that survives a "
+                                            "chunk-sized prefill + decode and save it")
+    c.add_argument("--model", default="qwen38_27b")
+    c.add_argument("--max-num-seqs", type=int, default=8)
+    c.add_argument("--max-num-batched-tokens", type=int, default=4096)
+    c.add_argument("--max-model-len", type=int, default=65536)
+    c.add_argument("--dry-run", action="store_true")
     g = sub.add_parser("generate", help="one-shot offline generation")
     g.add_argument("--model", default="tiny_hybrid")
     g.add_argument("--prompt", default="Hello")
@@ -112,6 +122,25 @@ def generate(ns):
     print(out[0].outputs[0].text)
 
 
+def gpus(ns):
+    import json
+    from ..config import get_model_config
+    from .hw import detect_gpus
+    print(json.dumps(detect_gpus(get_model_config(ns.model), min_mib=ns.min_gpu_mib), indent=1))
+
+
+def calibrate(ns):
+    from .hw import calibrate_kv, search_blocks
+    cfg = EngineConfig(model=ns.model, max_num_seqs=ns.max_num_seqs,
+                       max_num_batched_tokens=ns.max_num_batched_tokens,
+                       max_model_len=ns.max_model_len)
+    if ns.dry_run:
+        print(f"would search num_kv_blocks for {cfg.model} at max_num_seqs={cfg.max_num_seqs}, "
+              f"chunk={cfg.max_num_batched_tokens}: engine start + one chunk prefill + decode per try")
+        return
+    print(f"num_kv_blocks = {calibrate_kv(cfg)}")
+
+
 def main(argv=None):
     logging.basicConfig(level=logging.INFO, format="[radiance] %(message)s")
     ns = _parser().parse_args(argv)
@@ -119,6 +148,10 @@ def main(argv=None):
         serve(ns)
     elif ns.cmd == "generate":
         generate(ns)
+    elif ns.cmd == "gpus":
+        gpus(ns)
+    elif ns.cmd == "calibrate-kv":
+        calibrate(ns)
 
 
 if __name__ == "__main__":

@@ -23,6 +23,8 @@ from __future__ import annotations
 import math
 from typing import Optional
 
+import os
+
 import torch
 import torch.nn.functional as F
 
@@ -133,6 +135,15 @@ class DFlash2Drafter:
             if self.device.type == "cuda" else None
         self.last = {}          # request id -> (candidate ids [k,Kc], draft probs [k,Kc])
         self.kv = None          # engine KV manager (set by for_engine)
+        # prefill window skip (RADIANCE_DFLASH_PREFILL_WINDOW_SKIP, on by default): every drafter
+        # layer attends through the sliding window only, so prompt rows more than window + margin
+        # before the prompt's end get no fc / context K/V.  margin >= 2 KV blocks keeps the block
+        # holding the last skipped position wholly below the first block a draft can touch.
+        # Reference: sly/radiance_dflash_skip.py:1-60 (there per step: whole chunks are skipped).
+        self.window_skip = os.environ.get("RADIANCE_DFLASH_PREFILL_WINDOW_SKIP", "1") == "1"
+        self.skip_margin = max(int(os.environ.get("RADIANCE_DFLASH_PREFILL_WINDOW_SKIP_MARGIN",
+                                                  "512")), 2 * block_size)
+        self.skipped_rows = 0
 
     @staticmethod
     def for_engine(engine, k: int) -> "DFlash2Drafter":
@@ -147,6 +158,13 @@ class DFlash2Drafter:
                            engine.num_blocks)
         d.kv = engine.kv
         return d
+
+    def _prefill_skip_span(self) -> int:
+        """Prompt rows closer than this to the prompt's end keep their context K/V (0 = the
+        skip is off)."""
+        if not self.window_skip or not self.dc.window:
+            return 0
+        return self.dc.window + self.skip_margin
 
     # ------------------------------------------------------------------------------------------
     def _kv_write(self, li, h_norm, positions, slot_mapping):
@@ -167,14 +185,20 @@ class DFlash2Drafter:
             return
         rows, pos, slots = [], [], []
         qsl = meta.query_start_loc.cpu().tolist()
-        slot_h = meta.slot_mapping.cpu().tolist()
         pos_h = meta.positions.cpu().tolist()
+        skip_below = self._prefill_skip_span()
         for bi, s in enumerate(sched.seqs):
             n = s.num_new_tokens
             if s.is_decode and s.draft_tokens:
                 toks = sampled.get(s.req.request_id, [])
                 n = max(1, len(toks))          # the fed token + accepted drafts
+            # prefill window skip: prompt positions the sliding-window drafter will never attend
+            # to (more than window + margin before the prompt's end) need no context K/V
+            lo = s.req.num_prompt_tokens - skip_below if (skip_below and not s.is_decode) else None
             for t in range(qsl[bi], qsl[bi] + min(n, qsl[bi + 1] - qsl[bi])):
+                if lo is not None and pos_h[t] < lo:
+                    self.skipped_rows += 1
+                    continue
                 rows.append(t)
         if not rows:
             return

@@ -336,7 +336,7 @@ class HybridModel:
     def __init__(self, cfg: ModelConfig, quant: str = "mxfp4", device="cpu", seed: int = 0,
                  tp: Optional[TPInfo] = None, init_device=None, weights=None,
                  lm_head_quant: Optional[str] = None, tp_pad: Optional[int] = None,
-                 ep=None):
+                 ep=None, embed_quant: Optional[str] = None):
         self.quant = quant
         self.device = torch.device(device)
         self.tp = tp or TPInfo()
@@ -352,6 +352,8 @@ class HybridModel:
         self.cfg = cfg
         H, V = cfg.hidden_size, cfg.vocab_size
         self.embed = W.tensor("embed", (V, H), "embed").to(torch.bfloat16)
+        # embedding table format: bf16, or int8 / int4 codes dequantised by the lookup kernel
+        self.embed_quant = embed_quant
         # ep: data-parallel attention with expert-parallel MoE layers (parallel/ep.py)
         self.ep = ep
         self.layers = [DecoderLayer(cfg, i, self.tp, quant, W, ep=ep)
@@ -365,6 +367,11 @@ class HybridModel:
         # reference's int4 lm_head: a quarter of the bf16 bytes on the decode critical path)
         self.lm_head = make_linear(slice_rows(w, s0, per), lm_head_quant or quant, "lm_head")
         del w
+        if embed_quant in ("int8", "int4"):
+            from ..quant.embed import QuantEmbedding
+            self.embed = QuantEmbedding.from_float(self.embed, 8 if embed_quant == "int8" else 4)
+        elif embed_quant not in (None, "bf16"):
+            raise ValueError(f"embed_quant: int8, int4 or bf16, got {embed_quant}")
         if init_dev != self.device or getattr(W, "device", self.device) != self.device:
             self.to(self.device)
         self._init_rope()
@@ -471,7 +478,7 @@ class HybridModel:
         residual stream after each listed layer is appended to `aux_out` (drafter conditioning)."""
         cfg = self.cfg
         eps = cfg.rms_norm_eps
-        x = self.embed[input_ids.long()] if input_ids.is_cuda else self.embed[input_ids.long()]
+        x = self.embed[input_ids.long()]
         residual = None
         h = x
         ai = gi = 0
@@ -567,7 +574,8 @@ class HybridModel:
         return lg
 
     def weight_bytes(self) -> int:
-        n = self.embed.numel() * 2 + self.lm_head.nbytes
+        n = (self.embed.nbytes if hasattr(self.embed, "nbytes") and not isinstance(self.embed, torch.Tensor)
+             else self.embed.numel() * 2) + self.lm_head.nbytes
         for layer in self.layers:
             for obj in (layer.mixer, layer.mlp):
                 for v in vars(obj).values():

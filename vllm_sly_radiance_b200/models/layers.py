@@ -38,9 +38,11 @@ FUSE_MAX_K = 9216
 
 import os as _os
 
-# decode batches (<= 16 rows) run the persistent stream-K GEMM; its finisher produces the next
-# linear's e4m3 rows in the same launch (RADIANCE_GEMV=0 / RADIANCE_FINISH=0 switch them off)
-GEMV_ON = _os.environ.get("RADIANCE_GEMV", "1") != "0"
+# decode batches (<= 16 rows): the GEMM's last CTA produces the next linear's e4m3 rows in the
+# same launch (RADIANCE_FINISH=0 switches it off).  RADIANCE_GEMV=1 selects the persistent
+# stream-K decode GEMM (one CTA per SM) instead of the split-K cluster GEMM: it measured slower
+# (fewer weight bytes in flight per SM), so it is opt-in.
+GEMV_ON = _os.environ.get("RADIANCE_GEMV", "0") == "1"
 FINISH_ON = _os.environ.get("RADIANCE_FINISH", "1") != "0"
 
 
@@ -132,8 +134,8 @@ class Linear:
 
     def can_finish(self, x) -> bool:
         """A decode-sized (e4m3, scale) input this MXFP4 linear can run with a fused finisher."""
-        return (FINISH_ON and GEMV_ON and self.quant == "mxfp4" and isinstance(x, tuple)
-                and x[0].is_cuda and x[0].shape[0] <= K.GEMV_MAX_ROWS and self.push is None)
+        return (FINISH_ON and self.quant == "mxfp4" and isinstance(x, tuple)
+                and x[0].is_cuda and 0 < x[0].shape[0] <= K.GEMV_MAX_ROWS and self.push is None)
 
     def call_finish(self, x, mode: int, res=None, norm_w=None, eps: float = 0.0):
         """y = x W^T followed, in the same launch, by the producer of the next linear:
@@ -148,9 +150,15 @@ class Linear:
         q, s = x
         if mode == K.FIN_NORM:
             res_new = torch.empty(q.shape[0], self.N, dtype=torch.bfloat16, device=q.device)
-            _, fq, fs = K.mxfp4_gemv(q, s, self.w, None, K.FIN_NORM, res, norm_w, res_new, eps)
+            if GEMV_ON:
+                _, fq, fs = K.mxfp4_gemv(q, s, self.w, None, K.FIN_NORM, res, norm_w, res_new, eps)
+            else:
+                _, fq, fs = K.mxfp4_gemm_finish(q, s, self.w, K.FIN_NORM, res, norm_w, res_new, eps)
             return fq, fs, res_new
-        _, fq, fs = K.mxfp4_gemv(q, s, self.w, None, K.FIN_SILU)
+        if GEMV_ON:
+            _, fq, fs = K.mxfp4_gemv(q, s, self.w, None, K.FIN_SILU)
+        else:
+            _, fq, fs = K.mxfp4_gemm_finish(q, s, self.w, K.FIN_SILU)
         return fq, fs
 
     def __call__(self, x: Act, out: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -164,7 +172,7 @@ class Linear:
             if self.push is not None and out is None and q.is_cuda and \
                     self.push.can_push(q.shape[0], self.N):
                 return self.push.gemm_push(q, s, self.w)
-            if GEMV_ON and q.is_cuda and q.shape[0] <= K.GEMV_MAX_ROWS:
+            if GEMV_ON and q.is_cuda and 0 < q.shape[0] <= K.GEMV_MAX_ROWS:
                 return K.mxfp4_gemv(q, s, self.w, out)
             return K.mxfp4_gemm(q, s, self.w.packed, self.w.sf, self.w.scales, self.N, out=out)
         if self.quant == "fp8":

@@ -77,15 +77,24 @@ def check_status(device, reset: bool = True) -> int:
 
 
 _WS: dict = {}
+_WS_RETIRED: list = []
 
 
 def workspace(device, name: str, numel: int) -> torch.Tensor:
     """Zero-initialised int32 workspace shared by launches of one kernel family (counters in it
-    are self-resetting).  Grown on demand outside CUDA-graph capture."""
+    are self-resetting).  Grown on demand outside CUDA-graph capture.  A workspace that is
+    outgrown is kept alive, never freed: CUDA graphs captured earlier still address it, and its
+    counters must not land in memory the allocator has handed to another tensor."""
+    device = torch.device(device)
+    if device.type == "cuda" and device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
     key = (str(device), name)
     t = _WS.get(key)
     if t is None or t.numel() < numel:
-        t = torch.zeros(max(numel, 1 << 16), dtype=torch.int32, device=device)
+        if t is not None:
+            _WS_RETIRED.append(t)
+        n = max(numel, 1 << 16, 2 * t.numel() if t is not None else 0)
+        t = torch.zeros(n, dtype=torch.int32, device=device)
         _WS[key] = t
     return t
 
@@ -252,6 +261,23 @@ def mxfp4_gemv(q, scale, w, out=None, fin: int = FIN_NONE, res=None, norm_w=None
     ext().mxfp4_gemv(q, scale, w.packed, w.sf, out, _gemv_ws(dev), _GEMV_CPS, fin,
                      _none(res, dev), _none(norm_w, dev), _none(res_out, dev), fq, fs, eps,
                      status_word(dev))
+    return out, fq, fs
+
+
+def mxfp4_gemm_finish(q, scale, w, fin: int, res=None, norm_w=None, res_out=None,
+                      eps: float = 1e-6):
+    """Decode W4A8 GEMM (1..16 rows, CUDA) whose last CTA also produces the next linear's
+    (e4m3, scale) rows -- FIN_NORM: residual add + RMSNorm(1 + w), new residual into res_out;
+    FIN_SILU: SiLU(g) * u of the output [g | u].  -> (out, q, scale)."""
+    M = q.shape[0]
+    dev = q.device
+    out = torch.empty(M, w.N, dtype=torch.bfloat16, device=dev)
+    H = w.N if fin == FIN_NORM else w.N // 2
+    fq = torch.empty(M, H, dtype=torch.float8_e4m3fn, device=dev)
+    fs = torch.empty(M, dtype=torch.float32, device=dev)
+    ext().mxfp4_gemm_fin(q, scale, w.packed, w.sf, out, fin, _none(res, dev), _none(norm_w, dev),
+                         _none(res_out, dev), fq, fs, eps, workspace(dev, "gemm_fin", 1),
+                         status_word(dev))
     return out, fq, fs
 
 

@@ -21,21 +21,29 @@ PUSH_MAX_HIDDEN = 10240
 
 @dataclass
 class PushedPartial:
-    """Stand-in for the output of a row-parallel GEMM whose tiles were pushed into every rank's
-    receive buffer (``mxfp4_gemm_push``); the all-reduce call that consumes it only runs the
-    receiving half."""
+    """Stand-in for the output of a row-parallel GEMM whose tiles were pushed from its epilogue:
+    into every rank's receive buffer (kind "ll", decode: ``mxfp4_gemm_push``) or into the owners'
+    reduce-scatter slots of the two-shot all-reduce (kind "rs", prefill: ``mxfp4_gemm_rs``).  The
+    all-reduce call that consumes it only runs the remaining half."""
     M: int
     H: int
     expected: int
     device: torch.device
+    kind: str = "ll"
 
     @property
     def shape(self):
         return (self.M, self.H)
 
 
+TS_MIN_ROWS = 257           # prefill-sized all-reduces: two-shot NVLink (comm_ts.cu)
+TS_MAX_ROWS = 4096          # the scheduler's chunk (max_num_batched_tokens) bounds a prefill step
+TS_MAX_HIDDEN = 8192
+
+
 class FusedComm:
-    def __init__(self, rank: int, world: int, group, slot_bytes: int = 32 << 20):
+    def __init__(self, rank: int, world: int, group, slot_bytes: int = 32 << 20,
+                 ts_rows: int = TS_MAX_ROWS, ts_hidden: int = TS_MAX_HIDDEN):
         import torch.distributed as dist
         self.rank, self.world = rank, world
         self.slot_bytes = slot_bytes
@@ -51,6 +59,15 @@ class FusedComm:
             self.push_half_words = world * PUSH_MAX_ROWS * (PUSH_MAX_HIDDEN // 2)
             self.push_buf = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
             self.push_ptrs = self._exchange(self.push_buf, group)
+        # two-shot all-reduce (reduce-scatter + all-gather pushes) for prefill chunks; the
+        # row-parallel GEMM pushes its rows to their owners from its epilogue
+        self.ts_enabled = os.environ.get("RADIANCE_TS", "1") != "0"
+        self.ts_ptrs = None
+        if self.ts_enabled:
+            self.ts_bytes = ext().ts_buffer_bytes(ts_rows, ts_hidden)
+            self.ts_buf = torch.zeros(self.ts_bytes, dtype=torch.uint8, device="cuda")
+            self.ts_ptrs = self._exchange(self.ts_buf, group)
+        self.ts_calls = 0
         dist.barrier(group=group)
         self.calls = 0
         self.fallbacks = 0
@@ -73,13 +90,27 @@ class FusedComm:
         return ptrs
 
     # ---- GEMM-fused all-reduce ----
+    def ts_fits(self, M: int, H: int) -> bool:
+        return (self.ts_ptrs is not None and H % 8 == 0 and H <= 10240
+                and ext().ts_buffer_bytes(M, H) <= self.ts_bytes)
+
     def can_push(self, M: int, N: int) -> bool:
+        if M > PUSH_MAX_ROWS:
+            return M >= TS_MIN_ROWS and self.ts_fits(M, N)
         return (self.push_ptrs is not None and 0 < M <= PUSH_MAX_ROWS and N % 8 == 0
                 and N <= PUSH_MAX_HIDDEN)
 
     def gemm_push(self, q, s, w) -> PushedPartial:
         """Row-parallel W4A8 GEMM whose output tiles go straight into every rank's receive
-        buffer; the following all-reduce call reduces them."""
+        buffer (decode) or into the owners' reduce-scatter slots (prefill); the following
+        all-reduce call runs the rest."""
+        M = q.shape[0]
+        if M > PUSH_MAX_ROWS:
+            per = ext().ts_rows_per_rank(M, self.world)
+            exp = ext().mxfp4_gemm_rs(q, s, w.packed, w.sf, self.ts_ptrs, self.rank, per,
+                                      status_word(q.device))
+            self.pushes += 1
+            return PushedPartial(M, w.N, int(exp), q.device, "rs")
         from ..models.layers import GEMV_ON
         from ..ops import kernels as K
         if GEMV_ON and q.shape[0] <= K.GEMV_MAX_ROWS:
@@ -112,10 +143,31 @@ class FusedComm:
             x.shape[1] <= 10240 and self.world * x.numel() * 4 <= self.slot_bytes and \
             x.is_contiguous()
 
+    def _ts(self, x, M, H, out, residual, weight, eps, res_out, q, s):
+        """Two-shot all-reduce of x (a bf16 partial, or a PushedPartial of kind "rs")."""
+        e = _empty(out.device if out is not None else q.device)
+        pushed = isinstance(x, PushedPartial)
+        self.ts_calls += 1
+        ext().ts_allreduce(self.ts_ptrs, self.rank, M, H, self.ts_bytes, e if pushed else x,
+                           pushed, x.expected if pushed else 0,
+                           out if out is not None else e, residual if residual is not None else e,
+                           weight if weight is not None else e, eps,
+                           res_out if res_out is not None else e, q if q is not None else e,
+                           s if s is not None else e,
+                           status_word(out.device if out is not None else q.device))
+
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         if isinstance(x, PushedPartial):
             out = torch.empty(x.M, x.H, dtype=torch.bfloat16, device=x.device)
-            self._recv(x, out, None, None, 0.0, None, None, None)
+            if x.kind == "rs":
+                self._ts(x, x.M, x.H, out, None, None, 0.0, None, None, None)
+            else:
+                self._recv(x, out, None, None, 0.0, None, None, None)
+            return out
+        if (x.dim() == 2 and x.shape[0] >= TS_MIN_ROWS and x.dtype == torch.bfloat16
+                and x.is_contiguous() and self.ts_fits(x.shape[0], x.shape[1])):
+            out = torch.empty_like(x)
+            self._ts(x, x.shape[0], x.shape[1], out, None, None, 0.0, None, None, None)
             return out
         if not self.fits(x) or x.shape[0] > 256:
             import torch.distributed as dist
@@ -136,7 +188,17 @@ class FusedComm:
             q = torch.empty(M, H, dtype=torch.float8_e4m3fn, device=x.device)
             s = torch.empty(M, dtype=torch.float32, device=x.device)
             r = torch.empty(M, H, dtype=torch.bfloat16, device=x.device)
-            self._recv(x, None, residual, weight, eps, r, q, s)
+            if x.kind == "rs":
+                self._ts(x, M, H, None, residual, weight, eps, r, q, s)
+            else:
+                self._recv(x, None, residual, weight, eps, r, q, s)
+            return q, s, r
+        if (M >= TS_MIN_ROWS and x.dtype == torch.bfloat16 and x.is_contiguous()
+                and self.ts_fits(M, H)):
+            q = torch.empty(M, H, dtype=torch.float8_e4m3fn, device=x.device)
+            s = torch.empty(M, dtype=torch.float32, device=x.device)
+            r = torch.empty_like(x)
+            self._ts(x, M, H, None, residual, weight, eps, r, q, s)
             return q, s, r
         if not self.fits(x) or M > 256:
             from ..ops import kernels as K
