@@ -117,6 +117,11 @@ def main():
                     help="tokens of the extra single-stream decode run (0 = skip)")
     ap.add_argument("--no-tp-check", action="store_true",
                     help="TP > 1: skip the logits comparison against a TP1 engine")
+    ap.add_argument("--workload", default="decode", choices=["decode", "long", "moe", "spec"],
+                    help="decode: the headline (config 2); long: config 4 (int4 KV, 128k / 256k "
+                         "depth); moe: config 5 (EP MoE hybrid, batch-64 decode, 8k prefill)")
+    ap.add_argument("--long-depths", default="131072,262144")
+    ap.add_argument("--long-kv", default="int4", choices=["int4", "fp8"])
     ap.add_argument("--prefill-lens", default="",
                     help="comma list of prompt lengths for prefill-only extras (default: --prompt-len)")
     ap.add_argument("--no-extra", action="store_true", help="skip the prefill / concurrency extras")
@@ -134,6 +139,12 @@ def main():
     rank, world, dist = dist_setup(args.gpus)
     if world == 1:
         torch.cuda.set_device(0)
+    if args.workload == "long":
+        return long_context(args, rank, world, dist)
+    if args.workload == "moe":
+        return moe_workload(args, rank, world, dist)
+    if args.workload == "spec":
+        return spec_workload(args, rank, world, dist)
     dev = torch.device("cuda", torch.cuda.current_device())
     from vllm_sly_radiance_b200.config import EngineConfig
     from vllm_sly_radiance_b200.engine.llm_engine import LLMEngine
@@ -313,6 +324,211 @@ def main():
     if dist is not None:
         if eng is not None:
             eng.runner.graphs.clear()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _device_steps(eng, dist, until):
+    """Engine steps while until() holds, each bracketed by CUDA events -> (device s, steps)."""
+    ev = []
+    stream = torch.cuda.current_stream()
+    while until():
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        eng.step()
+        b.record(stream)
+        ev.append((a, b))
+    torch.cuda.synchronize()
+    return sum(x.elapsed_time(y) for x, y in ev) / 1e3, len(ev)
+
+
+def _max_ranks(x, dist, dev):
+    if dist is None:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def long_context(args, rank, world, dist):
+    """Config 4: the 27B hybrid with the 4-bit KV cache (int4 + fp16 scale/zero per 16 elements),
+    TP = N with kv heads replicated when N exceeds them, all-reduces fused into o_proj / down.
+    Prefill of random tokens in 4096 chunks up to each depth, then --steps decode steps there
+    (device time, max over ranks); the KV pool's token capacity per GPU for int4 and fp8."""
+    from vllm_sly_radiance_b200.config import EngineConfig
+    from vllm_sly_radiance_b200.engine.llm_engine import LLMEngine
+    from vllm_sly_radiance_b200.engine.request import SamplingParams
+    from vllm_sly_radiance_b200.models.hybrid import TPInfo
+    from vllm_sly_radiance_b200.parallel.comm import make_tp_info
+    dev = torch.device("cuda", torch.cuda.current_device())
+    depths = [int(v) for v in args.long_depths.split(",") if v]
+    tp = make_tp_info(rank, world, backend="fused") if world > 1 else TPInfo()
+    cfg = EngineConfig(model=args.model, tensor_parallel_size=world,
+                       max_model_len=max(depths) + args.steps + 64, max_num_seqs=1,
+                       max_num_batched_tokens=4096, kv_cache_dtype=args.long_kv, device="cuda")
+    eng = LLMEngine(cfg, tp=tp)
+    m = eng.model
+    per_tok = {f: m.cache_bytes_per_block(cfg.block_size, f) / cfg.block_size for f in ("int4", "fp8")}
+    pool_bytes = eng.num_blocks * m.cache_bytes_per_block(cfg.block_size, args.long_kv)
+    g = torch.Generator().manual_seed(7)
+    V = eng.model_config.vocab_size
+    out = {"kv_pool_bytes_per_gpu": pool_bytes,
+           "kv_pool_tokens_per_gpu": {f: int(pool_bytes // per_tok[f]) for f in per_tok},
+           "kv_bytes_per_token_per_gpu": {f: round(per_tok[f], 1) for f in per_tok}}
+    prev = 0
+    prompt = torch.randint(3, V, (max(depths),), generator=g).tolist()
+    sp = SamplingParams(temperature=0.7, top_p=0.95, top_k=20, seed=3,
+                        max_tokens=len(depths) * (args.steps + 8) + 8, ignore_eos=True)
+    for d in depths:
+        # prefill up to depth d (a fresh request each depth; chunked, device-timed)
+        eng.add_request(prompt[:d], SamplingParams(temperature=0, max_tokens=args.steps + 1,
+                                                   ignore_eos=True), f"L{d}")
+        req = eng.requests[f"L{d}"]
+        if dist is not None:
+            dist.barrier()
+        pf_s, _ = _device_steps(eng, dist, lambda: req.num_computed_tokens < d)
+        pf_s = _max_ranks(pf_s, dist, dev)
+        out[f"prefill_tok_s@{d}"] = round(d / pf_s, 1)
+        for _ in range(args.warmup):
+            eng.step()
+        n = [0]
+        dec_s, nsteps = _device_steps(eng, dist, lambda: (n.__setitem__(0, n[0] + 1) or n[0]) <= args.steps)
+        dec_s = _max_ranks(dec_s, dist, dev)
+        out[f"decode_tok_s@{d}"] = round(nsteps / dec_s, 2)
+        out[f"decode_ms_per_step@{d}"] = round(dec_s / nsteps * 1e3, 3)
+        eng.abort_request(f"L{d}")
+    if rank == 0:
+        print(json.dumps({"metric": "config 4: long-context decode / prefill with the "
+                                    f"{args.long_kv} KV cache", "n_gpus": world,
+                          "parallelism": f"tp{world}", "model": args.model, "steps": args.steps,
+                          "warmup": args.warmup, "data": "synthetic: uniform-random prompt token ids, "
+                          "random-init MXFP4 weights", **out}), flush=True)
+    if dist is not None:
+        eng.runner.graphs.clear()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def spec_workload(args, rank, world, dist):
+    """Config 3: config 2 plus DFlash2 speculative decoding (5-layer block drafter, k = 7, context
+    from 5 target layers), verify over 8 positions + rejection sampling.  Random weights accept
+    nothing, so the acceptance length follows the forced schedule (cycle with mean 5.5 of 7).
+    Single stream and concurrency 8 (1.5k prompts, --long-decode output tokens each); tokens per
+    second count every emitted token (accepted drafts + bonus), device time over the decode steps,
+    max over ranks."""
+    from vllm_sly_radiance_b200.config import EngineConfig
+    from vllm_sly_radiance_b200.engine.llm_engine import LLMEngine
+    from vllm_sly_radiance_b200.engine.request import SamplingParams
+    from vllm_sly_radiance_b200.models.hybrid import TPInfo
+    from vllm_sly_radiance_b200.parallel.comm import make_tp_info
+    dev = torch.device("cuda", torch.cuda.current_device())
+    tp = make_tp_info(rank, world, backend="fused") if world > 1 else TPInfo()
+    out_tokens = args.long_decode or 256
+    cfg = EngineConfig(model=args.model, tensor_parallel_size=world,
+                       max_model_len=args.prompt_len + out_tokens + 64, max_num_seqs=8,
+                       max_num_batched_tokens=4096, device="cuda", speculative_method="dflash2",
+                       num_speculative_tokens=7, forced_acceptance="uniform07")
+    eng = LLMEngine(cfg, tp=tp)
+    V = eng.model_config.vocab_size
+    g = torch.Generator().manual_seed(5)
+    res = {}
+    for C in (1, 8):
+        sp = SamplingParams(temperature=0.7, top_p=0.95, top_k=20, max_tokens=out_tokens,
+                            ignore_eos=True)
+        ids = [f"s{C}_{i}" for i in range(C)]
+        for rid in ids:
+            eng.add_request(torch.randint(3, V, (args.prompt_len,), generator=g).tolist(), sp, rid)
+        while any(eng.requests[r].num_computed_tokens < args.prompt_len for r in ids if r in eng.requests):
+            eng.step()
+        st0 = dict(eng.spec.stats)
+        emitted0 = {r: len(eng.requests[r].output_token_ids) for r in ids if r in eng.requests}
+        if dist is not None:
+            dist.barrier()
+        stream = torch.cuda.current_stream()
+        ev, ntok = [], 0
+        w0 = time.perf_counter()
+        while eng.has_unfinished_requests():
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            outs = eng.step()
+            b.record(stream)
+            ev.append((a, b))
+        torch.cuda.synchronize()
+        wall = _max_ranks(time.perf_counter() - w0, dist, dev)
+        dev_s = _max_ranks(sum(x.elapsed_time(y) for x, y in ev) / 1e3, dist, dev)
+        ntok = C * out_tokens - sum(emitted0.values())
+        st = {k: eng.spec.stats[k] - st0.get(k, 0) for k in eng.spec.stats}
+        res[f"conc{C}"] = {"tok_s": round(ntok / dev_s, 1), "e2e_tok_s": round(ntok / wall, 1),
+                           "steps": len(ev), "ms_per_step": round(dev_s / len(ev) * 1e3, 3),
+                           "tokens_per_step_per_seq": round(ntok / len(ev) / C, 2),
+                           "accepted_per_draft": round(st["accepted"] / max(1, st["drafts"]), 2)}
+    if rank == 0:
+        print(json.dumps({"metric": "config 3: DFlash2 k=7 speculative decode, forced acceptance "
+                                    "(mean 5.5 of 7), tok/s", "n_gpus": world,
+                          "parallelism": f"tp{world}", "model": args.model, "prompt": args.prompt_len,
+                          "output_tokens": out_tokens, "vs_baseline_conc1":
+                              round(res["conc1"]["tok_s"] / BASELINE_DECODE_TOKS, 2),
+                          "data": "synthetic prompts, random-init weights (target MXFP4 W4A8, drafter "
+                                  "random init); acceptance forced by the schedule", **res}), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def moe_workload(args, rank, world, dist):
+    """Config 5: the MoE hybrid (40 layers, hidden 2048, 256 experts top-8 + shared expert) with
+    expert parallelism over N ranks and data-parallel attention: each rank serves its share of a
+    64-request decode batch (and one 8k-token prefill), MoE rows dispatched to the experts' owners
+    and combined back over NVLink (P2P transport) inside every MoE layer."""
+    from vllm_sly_radiance_b200.config import EngineConfig, moe_hybrid
+    from vllm_sly_radiance_b200.engine.llm_engine import LLMEngine
+    from vllm_sly_radiance_b200.engine.request import SamplingParams
+    from vllm_sly_radiance_b200.models.hybrid import HybridModel
+    from vllm_sly_radiance_b200.parallel.ep import make_ep_group
+    dev = torch.device("cuda", torch.cuda.current_device())
+    ep = make_ep_group(rank, world, "p2p") if world > 1 else None
+    batch = 64
+    per_rank = max(1, batch // world)
+    cfg = EngineConfig(model="moe_hybrid", max_model_len=12288, max_num_seqs=per_rank,
+                       max_num_batched_tokens=4096, device="cuda", enable_cuda_graphs=False)
+    m = HybridModel(moe_hybrid(), quant="mxfp4", device=dev, seed=0, ep=ep)
+    eng = LLMEngine(cfg, model=m)
+    V = m.cfg.vocab_size
+    g = torch.Generator().manual_seed(100 + rank)
+    sp = SamplingParams(temperature=0.7, top_p=0.95, top_k=20, max_tokens=args.warmup + args.steps + 4,
+                        ignore_eos=True)
+    for i in range(per_rank):
+        eng.add_request(torch.randint(3, V, (256,), generator=g).tolist(), sp, f"d{i}")
+    while any(r.num_computed_tokens < 256 for r in eng.requests.values()):
+        eng.step()
+    for _ in range(args.warmup):
+        eng.step()
+    if dist is not None:
+        dist.barrier()
+    n = [0]
+    dec_s, nsteps = _device_steps(eng, dist, lambda: (n.__setitem__(0, n[0] + 1) or n[0]) <= args.steps)
+    dec_s = _max_ranks(dec_s, dist, dev)
+    for rid in list(eng.requests):
+        eng.abort_request(rid)
+    eng.add_request(torch.randint(3, V, (8192,), generator=g).tolist(),
+                    SamplingParams(temperature=0, max_tokens=1, ignore_eos=True), "pf")
+    if dist is not None:
+        dist.barrier()
+    pf_s, _ = _device_steps(eng, dist, eng.has_unfinished_requests)
+    pf_s = _max_ranks(pf_s, dist, dev)
+    if rank == 0:
+        print(json.dumps({"metric": "config 5: EP MoE hybrid, batch-64 decode and 8k prefill",
+                          "n_gpus": world, "parallelism": f"ep{world}+dp-attention",
+                          "model": "moe_hybrid", "steps": args.steps, "warmup": args.warmup,
+                          "decode_tok_s": round(per_rank * world * nsteps / dec_s, 1),
+                          "decode_ms_per_step": round(dec_s / nsteps * 1e3, 3),
+                          "prefill_8k_tok_s": round(8192 * world / pf_s, 1),
+                          "transport": "p2p" if world > 1 else "local",
+                          "data": "synthetic: uniform-random prompts, random-init MXFP4 experts"}),
+              flush=True)
+    if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
 

@@ -310,6 +310,32 @@ def test_paged_attention_decode_kernel(D, Hq, Hkv, ctx_lens, splits, fmt, monkey
     assert rel_err(got, general) < 1e-2, rel_err(got, general)
 
 
+@pytest.mark.parametrize("q_lens,ctx_lens", [([256], [0]), ([300, 77], [1000, 40]),
+                                            ([130], [5000]), ([1024], [3000])])
+def test_fmha_prefill_tcgen05(q_lens, ctx_lens, monkeypatch):
+    """Causal chunked-prefill attention on tcgen05 (e4m3 QK and P V legs, TMEM accumulators,
+    TMA-fed fp8 pages) against the fp32 oracle and the mma.sync tile kernel, GQA 6, head 256."""
+    torch.manual_seed(21)
+    D, Hq, Hkv, bs = 256, 24, 4, 64
+    meta, nblocks = _attn_meta(q_lens, ctx_lens, bs, Hq, Hkv, 1, DEV)
+    k = (torch.randn(nblocks, Hkv, bs, D) * 0.5).to(torch.float8_e4m3fn)
+    v = torch.randn(nblocks, Hkv, bs, D).to(torch.float8_e4m3fn)
+    T = sum(q_lens)
+    q = ref.fp8_e4m3(torch.randn(T, Hq, D)).to(torch.bfloat16)
+    scale = D ** -0.5
+    want = ref.paged_attention(q, k, v, meta.block_tables.cpu(), meta.seq_lens.cpu(),
+                               meta.query_start_loc.cpu(), bs, scale)
+    monkeypatch.setattr(K, "_FMHA", True)
+    got = K.paged_attention(q.to(DEV), k.to(DEV), v.to(DEV), meta, scale)
+    monkeypatch.setattr(K, "_FMHA", False)
+    tile = K.paged_attention(q.to(DEV), k.to(DEV), v.to(DEV), meta, scale)
+    torch.cuda.synchronize()
+    K.check_status(got.device)
+    assert rel_err(tile, want) < 2e-2
+    # P and V on the e4m3 leg: a few percent of the row maximum
+    assert rel_err(got, want) < 5e-2, rel_err(got, want)
+
+
 @pytest.mark.parametrize("Hq,Hkv,ctx_lens,splits", [(24, 4, [1500], 8), (24, 4, [300, 2000, 64], 1),
                                                    (6, 1, [700, 4000], 5)])
 def test_paged_attention_decode_gated(Hq, Hkv, ctx_lens, splits):

@@ -76,6 +76,10 @@ void mxfp4_gemm_fin(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, to
                     torch::Tensor out, int64_t fin_mode, torch::Tensor res, torch::Tensor w,
                     torch::Tensor res_out, torch::Tensor q, torch::Tensor scale, double eps,
                     torch::Tensor ws, torch::Tensor status);
+void fmha_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                  torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor qsl,
+                  torch::Tensor tile_seq, torch::Tensor tile_row0, double scale, torch::Tensor out,
+                  torch::Tensor status);
 void mxfp4_gemm_act(int64_t mode, torch::Tensor x, torch::Tensor res, torch::Tensor w,
                     torch::Tensor res_out, double eps, torch::Tensor wp, torch::Tensor sf,
                     torch::Tensor out, torch::Tensor status);
@@ -179,6 +183,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_gather", &rad::embed_gather, "int8 / int4-g128 embedding lookup into bf16 rows");
   m.def("mxfp4_gemm_fin", &rad::mxfp4_gemm_fin,
         "decode W4A8 GEMM whose last CTA also runs the next linear's producer over the rows");
+  m.def("fmha_prefill", &rad::fmha_prefill,
+        "causal prefill attention on tcgen05 (e4m3 QK and PV, TMEM accumulators, paged fp8 KV)");
   m.def("mxfp4_gemm_act", &rad::mxfp4_gemm_act,
         "decode W4A8 GEMM with its producer fused in (1: add + RMSNorm + e4m3, 2: SiLU*mul + e4m3)");
   m.def("push_allreduce_recv", &rad::push_allreduce_recv,

@@ -1,0 +1,420 @@
+// Chunked-prefill attention on 5th-generation tensor cores: paged fp8 (e4m3) KV cache, head
+// dim 256, grouped-query heads packed into the query rows, causal.
+//
+// Reference behaviour: the libr4d prefill kernel r4d_attn_prefill_h256_gqa6 with its fp8 QK and
+// PV legs, double-buffered K/V staging and heaviest-q-block-first dispatch
+// (sly/r4d/r4d_extras_rx10.patch:393-510 O_QK8 / O_PV8 / O_DB / O_HVF, radiance_r4d_hybrid_attn.py:378).
+//
+// B200 design (one CTA per 128 query rows of one kv head):
+//  * Rows are (token, q head of the group) pairs, the packing the other attention kernels use, so
+//    the six heads of a group share every K/V tile.  Q is gathered once, rounded to e4m3 (it is
+//    e4m3-valued already when the cache is fp8) and stored as two 128-byte-swizzled halves.
+//  * S = Q K^T: tcgen05.mma.kind::f8f6f4 (e4m3 x e4m3, fp32 accumulate), M = 128 rows, N = 128
+//    keys, eight K = 32 steps, into one of two TMEM S buffers, so the next tile's S is computed
+//    while the softmax of this one runs.
+//  * Softmax: four warps, one row per thread (the TMEM lane), online max / sum in the exp2
+//    domain; P = 256 * exp2(s - m) as e4m3 into shared memory (the scale keeps small
+//    probabilities out of the subnormal range; O is divided by 256 l at the end).  O is rescaled
+//    in TMEM only when a warp's running maximum moved.
+//  * O += P V: tcgen05.mma.kind::f8f6f4 with V as an MN-major operand straight from the paged
+//    cache layout (keys x dims), M = 128, N = 256, O (256 fp32 columns) stays in TMEM for the
+//    whole key range.
+//  * K and V pages arrive by TMA (two 64-key pages x two 128-byte halves per 128-key tile) into a
+//    two-stage ring; all waits are bounded (status word).
+//  * Causal tiles are scheduled heaviest first: CTA x takes row tile (last - x).
+// Warp roles (192 threads): warps 0-3 softmax + epilogue, warp 4 TMA producer, warp 5 MMA issuer.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "common.cuh"
+#include "tma_host.h"
+
+namespace rad {
+namespace fmha {
+
+constexpr int D = 256;
+constexpr int BM = 128;                 // query rows per CTA
+constexpr int BN = 128;                 // keys per tile
+constexpr int PAGE = 64;                // KV page rows (TMA box)
+constexpr int HALF = BM * 128;          // one 128-byte column half of a 128-row tile: 16 KB
+constexpr int Q_BYTES = 2 * HALF;
+constexpr int KV_BYTES = 2 * HALF;
+constexpr int P_BYTES = BM * BN;
+constexpr int STAGES = 2;
+constexpr int kThreads = 192;
+constexpr int SMEM_BYTES = 1024 + Q_BYTES + STAGES * 2 * KV_BYTES + P_BYTES + 1024;
+constexpr uint32_t O_COL = 0, S_COL = 256;      // TMEM: O [0, 256), S buffers [256, 384), [384, 512)
+
+// kind::f8f6f4 instruction descriptor: e4m3 x e4m3 -> fp32, M = 128
+__host__ __device__ constexpr uint32_t idesc_f8(int n, bool b_mn_major) {
+  return (1u << 4)                              // D format F32
+         | (0u << 7) | (0u << 10)               // A, B format E4M3
+         | ((b_mn_major ? 1u : 0u) << 16)       // B major-ness
+         | ((uint32_t)(n >> 3) << 17)
+         | ((uint32_t)(BM >> 4) << 24);
+}
+
+// MN-major 128-byte-swizzled operand: rows of 128 bytes along MN, 8-row atoms along K 1024 bytes
+// apart (SBO), 128-byte MN blocks `lbo` bytes apart (LBO)
+DEVI uint64_t sdesc_sw128_mn(uint32_t saddr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFF) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+DEVI void tmem_ld_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+DEVI void tmem_st_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+      "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+struct Bars {
+  uint64_t q_full;
+  uint64_t k_full[STAGES], v_full[STAGES], kv_empty[STAGES];
+  uint64_t s_full[2], s_empty[2];
+  uint64_t p_full, pv_done;
+  uint32_t tmem_slot;
+  int abort;
+};
+
+__global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
+    const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
+    const __nv_bfloat16* __restrict__ q, const int* __restrict__ block_tables, int bt_stride,
+    const int* __restrict__ seq_lens, const int* __restrict__ qsl, const int* __restrict__ tile_seq,
+    const int* __restrict__ tile_row0, int num_tiles, int Hq, int Hkv, float scale_log2,
+    __nv_bfloat16* __restrict__ out, int* __restrict__ status) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sKV = sQ + Q_BYTES;                       // stage s: K at s * 2 * KV_BYTES, V after it
+  uint8_t* sP = sKV + STAGES * 2 * KV_BYTES;
+  Bars* bar = reinterpret_cast<Bars*>(sP + P_BYTES);
+
+  pdl_wait();     // q (prologue) and the cache writes precede this kernel
+  pdl_trigger();
+  // heaviest first: the last row tile of a sequence has the longest causal key range
+  const int tile = num_tiles - 1 - blockIdx.x;
+  const int hk = blockIdx.y;
+  const int row0 = tile_row0[tile];
+  if (row0 % BM != 0) return;          // the metadata lists 64-row tiles: take every other one
+  const int b = tile_seq[tile];
+  const int G = Hq / Hkv;
+  const int s0 = qsl[b];
+  const int ql = qsl[b + 1] - s0;
+  const int L = seq_lens[b];
+  const int R = ql * G;
+  const int rows_here = min(BM, R - row0);
+  const int last_i = (row0 + rows_here - 1) / G;
+  const int kv_end = L - ql + last_i + 1;            // causal: keys up to the last row's position
+  const int nt = (kv_end + BN - 1) / BN;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar->q_full, 128);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&bar->k_full[s], 1);
+      mbar_init(&bar->v_full[s], 1);
+      mbar_init(&bar->kv_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&bar->s_full[s], 1);
+      mbar_init(&bar->s_empty[s], 128);
+    }
+    mbar_init(&bar->p_full, 128);
+    mbar_init(&bar->pv_done, 1);
+    bar->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 4 && lane == 0) {
+    tma_prefetch_desc(&tmap_k);
+    tma_prefetch_desc(&tmap_v);
+  }
+  if (warp == 5) {
+    tmem_alloc(&bar->tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar->tmem_slot;
+
+  if (warp == 4) {
+    // ---------------- TMA producer: K and V pages of each 128-key tile ----------------
+    if (elect_one()) {
+      const int* bt = block_tables + (size_t)b * bt_stride;
+      for (int j = 0; j < nt; ++j) {
+        const int s = j % STAGES;
+        if (j >= STAGES && !mbar_wait(&bar->kv_empty[s], ((j / STAGES) - 1) & 1, status)) {
+          bar->abort = 1;
+          break;
+        }
+        const int key0 = j * BN;
+        const int pg0 = bt[key0 / PAGE];
+        const int pg1 = key0 + PAGE < kv_end ? bt[key0 / PAGE + 1] : pg0;   // past the range: any
+        uint8_t* sk = sKV + s * 2 * KV_BYTES;                             // valid (finite) page
+        uint8_t* sv = sk + KV_BYTES;
+        mbar_arrive_expect_tx(&bar->k_full[s], KV_BYTES);
+        mbar_arrive_expect_tx(&bar->v_full[s], KV_BYTES);
+        const int pgs[2] = {pg0, pg1};
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          const int row = (pgs[p] * Hkv + hk) * PAGE;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            tma_load_2d(sk + h * HALF + p * PAGE * 128, &tmap_k, &bar->k_full[s], h * 128, row);
+            tma_load_2d(sv + h * HALF + p * PAGE * 128, &tmap_v, &bar->v_full[s], h * 128, row);
+          }
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ---------------- MMA issuer ----------------
+    if (elect_one()) {
+      bool ok = mbar_wait(&bar->q_full, 0, status);
+      tc_fence_after();
+      const uint32_t qa = smem_u32(sQ);
+      const uint32_t idesc_s = idesc_f8(BN, false);
+      const uint32_t idesc_o = idesc_f8(D, true);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j % STAGES, sb = j & 1;
+        if (!mbar_wait(&bar->k_full[s], (j / STAGES) & 1, status)) return false;
+        if (j >= 2 && !mbar_wait(&bar->s_empty[sb], ((j >> 1) - 1) & 1, status)) return false;
+        tc_fence_after();
+        const uint32_t ka = smem_u32(sKV + s * 2 * KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / 32; ++kk) {
+          const uint32_t off = (kk / 4) * HALF + (kk % 4) * 32;
+          mma_f8(tmem + S_COL + sb * BN, sdesc_sw128(qa + off), sdesc_sw128(ka + off), idesc_s,
+                 kk > 0 ? 1u : 0u);
+        }
+        mma_commit(&bar->s_full[sb]);
+        return true;
+      };
+      if (ok && nt > 0) ok = issue_s(0);
+      for (int j = 0; j < nt && ok; ++j) {
+        if (j + 1 < nt && !issue_s(j + 1)) { ok = false; break; }
+        const int s = j % STAGES;
+        if (!mbar_wait(&bar->p_full, j & 1, status) ||
+            !mbar_wait(&bar->v_full[s], (j / STAGES) & 1, status)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t pa = smem_u32(sP);
+        const uint32_t va = smem_u32(sKV + s * 2 * KV_BYTES + KV_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BN / 32; ++kk)
+          mma_f8(tmem + O_COL, sdesc_sw128(pa + kk * 32), sdesc_sw128_mn(va + kk * 32 * 128, HALF),
+                 idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&bar->pv_done);
+        mma_commit(&bar->kv_empty[s]);
+      }
+      if (!ok) bar->abort = 1;
+    }
+  } else {
+    // ---------------- softmax + epilogue (warp w owns TMEM lanes 32w..32w+31 = rows) ----------
+    const int r = threadIdx.x;                         // row within the tile
+    const int rr = row0 + r;
+    const bool valid = rr < R;
+    const int i = valid ? rr / G : 0;
+    const int head = hk * G + (valid ? rr % G : 0);
+    const int pos = L - ql + i;
+    // Q row -> e4m3, two swizzled 128-byte halves
+    {
+      const __nv_bfloat16* src = q + ((size_t)(s0 + i) * Hq + head) * D;
+#pragma unroll 4
+      for (int c = 0; c < D / 16; ++c) {
+        uint4 w = make_uint4(0, 0, 0, 0);
+        if (valid) {
+          const uint4 u0 = reinterpret_cast<const uint4*>(src)[2 * c];
+          const uint4 u1 = reinterpret_cast<const uint4*>(src)[2 * c + 1];
+          const __nv_bfloat162* h0 = reinterpret_cast<const __nv_bfloat162*>(&u0);
+          const __nv_bfloat162* h1 = reinterpret_cast<const __nv_bfloat162*>(&u1);
+          uint16_t pk[8];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 a = __bfloat1622float2(h0[e]), bb = __bfloat1622float2(h1[e]);
+            pk[e] = f32x2_to_e4m3x2(a.x, a.y);
+            pk[4 + e] = f32x2_to_e4m3x2(bb.x, bb.y);
+          }
+          w = *reinterpret_cast<uint4*>(pk);
+        }
+        const int h = c / 8, ch = c % 8;
+        *reinterpret_cast<uint4*>(sQ + h * HALF + r * 128 + ((ch ^ (r & 7)) * 16)) = w;
+      }
+    }
+    fence_proxy_async();
+    mbar_arrive(&bar->q_full);
+
+    float m_run = -INFINITY, l_run = 0.f;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    bool ok = true;
+    for (int j = 0; j < nt; ++j) {
+      const int sb = j & 1;
+      if (!mbar_wait(&bar->s_full[sb], (j >> 1) & 1, status)) { ok = false; break; }
+      tc_fence_after();
+      float sv[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t u[32];
+        tmem_ld_x32(tmem + lane_base + S_COL + sb * BN + c * 32, u);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int key = j * BN + c * 32 + e;
+          sv[c * 32 + e] = (valid && key <= pos && key < L) ? __uint_as_float(u[e]) * scale_log2 : -INFINITY;
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&bar->s_empty[sb]);               // S buffer free for tile j + 2
+      float mx = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < BN; ++e) mx = fmaxf(mx, sv[e]);
+      const float m_new = fmaxf(m_run, mx);
+      const float mref = m_new == -INFINITY ? 0.f : m_new;
+      const float alpha = exp2f(m_run - mref);       // m_run = -inf -> 0 (O is still zero)
+      float psum = 0.f;
+#pragma unroll
+      for (int e = 0; e < BN; ++e) {
+        const float p = exp2f(sv[e] - mref);
+        sv[e] = p;
+        psum += p;
+      }
+      l_run = l_run * alpha + psum;
+      m_run = m_new;
+      // P / O of the previous tile are free once its PV MMAs are done
+      if (j > 0) {
+        if (!mbar_wait(&bar->pv_done, (j - 1) & 1, status)) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, alpha < 1.f)) {
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t u[32];
+            tmem_ld_x32(tmem + lane_base + O_COL + c * 32, u);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
+            tmem_st_x32(tmem + lane_base + O_COL + c * 32, u);
+          }
+          tmem_st_wait();
+        }
+      }
+      // P * 256 -> e4m3, row r of the swizzled P tile
+#pragma unroll
+      for (int c = 0; c < BN / 16; ++c) {
+        uint16_t pk[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          pk[e] = f32x2_to_e4m3x2(sv[c * 16 + 2 * e] * 256.f, sv[c * 16 + 2 * e + 1] * 256.f);
+        *reinterpret_cast<uint4*>(sP + r * 128 + ((c ^ (r & 7)) * 16)) = *reinterpret_cast<uint4*>(pk);
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      mbar_arrive(&bar->p_full);
+    }
+    // ---- epilogue: O / (256 l) -> bf16 ----
+    if (ok && nt > 0) ok = mbar_wait(&bar->pv_done, (nt - 1) & 1, status);
+    tc_fence_after();
+    const float inv = (ok && l_run > 0.f) ? 1.f / (256.f * l_run) : 0.f;
+    __nv_bfloat16* dst = out + ((size_t)(s0 + i) * Hq + head) * D;
+    for (int c = 0; c < D / 32; ++c) {
+      uint32_t u[32];
+      tmem_ld_x32(tmem + lane_base + O_COL + c * 32, u);
+      tmem_ld_wait();
+      if (valid) {
+        uint32_t w[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const __nv_bfloat162 hh = __floats2bfloat162_rn(__uint_as_float(u[2 * e]) * inv,
+                                                          __uint_as_float(u[2 * e + 1]) * inv);
+          w[e] = *reinterpret_cast<const uint32_t*>(&hh);
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          reinterpret_cast<uint4*>(dst + c * 32)[e] = make_uint4(w[4 * e], w[4 * e + 1], w[4 * e + 2], w[4 * e + 3]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace fmha
+
+static std::mutex g_fmha_mu;
+static std::unordered_map<uintptr_t, CUtensorMap> g_fmha_maps;
+
+static CUtensorMap cache_map(const torch::Tensor& cache) {
+  std::lock_guard<std::mutex> lk(g_fmha_mu);
+  const uintptr_t key = reinterpret_cast<uintptr_t>(cache.data_ptr()) ^ ((uintptr_t)cache.size(0) << 48);
+  auto it = g_fmha_maps.find(key);
+  if (it != g_fmha_maps.end()) return it->second;
+  const int64_t rows = cache.size(0) * cache.size(1) * cache.size(2);
+  CUtensorMap m = make_tma_2d(cache.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, fmha::D, rows,
+                              fmha::D, 128, fmha::PAGE, CU_TENSOR_MAP_SWIZZLE_128B);
+  g_fmha_maps.emplace(key, m);
+  return m;
+}
+
+// Causal prefill attention over an e4m3 paged cache [blocks, Hkv, 64, 256]: q [T, Hq, 256] bf16
+// (e4m3-valued), tiles listed in 64-row steps as for paged_attention (the kernel takes the
+// 128-row-aligned ones), out [T, Hq, 256] bf16.
+void fmha_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
+                  torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor qsl,
+                  torch::Tensor tile_seq, torch::Tensor tile_row0, double scale, torch::Tensor out,
+                  torch::Tensor status) {
+  using namespace fmha;
+  const int T = q.size(0), Hq = q.size(1);
+  const int Hkv = k_cache.size(1);
+  const int num_tiles = tile_seq.size(0);
+  if (T == 0 || num_tiles == 0) return;
+  TORCH_CHECK(q.size(2) == D && q.is_contiguous() && q.scalar_type() == at::kBFloat16, "fmha: q");
+  TORCH_CHECK(k_cache.scalar_type() == at::kFloat8_e4m3fn && v_cache.scalar_type() == at::kFloat8_e4m3fn &&
+                  k_cache.size(2) == PAGE && k_cache.size(3) == D && k_cache.is_contiguous() &&
+                  v_cache.is_contiguous(), "fmha: e4m3 cache [blocks, Hkv, 64, 256]");
+  TORCH_CHECK(Hq % Hkv == 0, "fmha: grouped heads");
+  TORCH_CHECK(out.is_contiguous() && out.scalar_type() == at::kBFloat16, "fmha: out");
+  const at::cuda::CUDAGuard guard(q.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  CUtensorMap tk = cache_map(k_cache), tv = cache_map(v_cache);
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(fmha_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        SMEM_BYTES));
+    attr = true;
+  }
+  int* st = status.numel() ? status.data_ptr<int>() : nullptr;
+  C10_CUDA_CHECK(launch_pdl(fmha_prefill_kernel, dim3(num_tiles, Hkv), dim3(kThreads), SMEM_BYTES,
+                            stream, tk, tv, (const __nv_bfloat16*)q.data_ptr(),
+                            block_tables.data_ptr<int>(), (int)block_tables.stride(0),
+                            seq_lens.data_ptr<int>(), qsl.data_ptr<int>(), tile_seq.data_ptr<int>(),
+                            tile_row0.data_ptr<int>(), num_tiles, Hq, Hkv,
+                            (float)(scale * 1.4426950408889634), (__nv_bfloat16*)out.data_ptr(), st));
+}
+
+}  // namespace rad

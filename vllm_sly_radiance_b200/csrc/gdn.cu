@@ -586,8 +586,9 @@ C10_CUDA_CHECK(launch_pdl((gdn::recurrent_kernel<DKc, ST>), dim3(grid), dim3(128
 // One-token-per-sequence GDN step fused into one launch (see decode_fused_kernel).  x = in_proj
 // output rows, ba_off = column of the b gates; out = [B, Hv * dv] bf16.
 // With q defined (fused norm + quant): z_off = column of z in x, norm_w [128] (gated RMSNorm
-// weight), norm_eps, nout bf16 [B, Hv * 128] scratch, ws int32 workspace (>= B * (1 + Hv)
-// elements, zero: per-row counters then head amax slots), q e4m3 [B, Hv * 128], q_scale [B].
+// weight), norm_eps, nout bf16 [B, Hv * 128] scratch, ws int32 workspace (>= 4096 + B * Hv
+// elements: per-row counters at [0, 4096), zero, self-resetting; then the head amax slots),
+// q e4m3 [B, Hv * 128], q_scale [B].
 void gdn_decode_fused(torch::Tensor x, int64_t ba_off, torch::Tensor conv_w,
                       torch::Tensor conv_state, torch::Tensor A_log, torch::Tensor dt_bias,
                       torch::Tensor state, torch::Tensor slots, torch::Tensor has_init, int64_t Hk,
@@ -625,7 +626,10 @@ void gdn_decode_fused(torch::Tensor x, int64_t ba_off, torch::Tensor conv_w,
                     q.stride(1) == 1 && q.stride(0) % 8 == 0, "gdn_decode_fused: q");
     TORCH_CHECK(nout.scalar_type() == at::kBFloat16 && nout.is_contiguous() &&
                     nout.numel() >= (int64_t)B * Hv * 128, "gdn_decode_fused: nout");
-    TORCH_CHECK(ws.scalar_type() == at::kInt && ws.numel() >= (int64_t)B * (1 + Hv), "gdn ws");
+    // fixed layout whatever B is: counters [0, 4096) (must stay zero between calls), then the
+    // head amax slots (written each call)
+    TORCH_CHECK(B <= 4096 && ws.scalar_type() == at::kInt && ws.numel() >= 4096 + (int64_t)B * Hv,
+                "gdn ws");
     TORCH_CHECK(norm_w.scalar_type() == at::kBFloat16 && norm_w.numel() >= 128, "norm weight");
     TORCH_CHECK(q_scale.scalar_type() == at::kFloat && q_scale.numel() >= B, "q_scale");
     fq.z_off = (int)z_off;
@@ -633,7 +637,7 @@ void gdn_decode_fused(torch::Tensor x, int64_t ba_off, torch::Tensor conv_w,
     fq.norm_eps = (float)norm_eps;
     fq.nout = (__nv_bfloat16*)nout.data_ptr();
     fq.row_cnt = reinterpret_cast<unsigned*>(ws.data_ptr<int>());
-    fq.head_amax = reinterpret_cast<float*>(ws.data_ptr<int>() + B);
+    fq.head_amax = reinterpret_cast<float*>(ws.data_ptr<int>() + 4096);
     fq.q = (uint8_t*)q.data_ptr();
     fq.ldq = (int)q.stride(0);
     fq.q_scale = q_scale.data_ptr<float>();

@@ -603,10 +603,12 @@ static void launch(const torch::Tensor& a, const torch::Tensor& a_scale, const t
   if constexpr (BN == 16) {
     if (act_mode == 1) { kern = mxfp4_gemm_kernel<BN, false, false, 1>; variant = 2; }
     if (act_mode == 2) { kern = mxfp4_gemm_kernel<BN, false, false, 2>; variant = 3; }
+    if (fin_mode == kFinNorm) { kern = mxfp4_gemm_kernel<BN, false, false, 0, false, kFinNorm>; variant = 5; }
+    if (fin_mode == kFinSilu) { kern = mxfp4_gemm_kernel<BN, false, false, 0, false, kFinSilu>; variant = 6; }
   } else {
-    TORCH_CHECK(act_mode == 0, "fused producers need a 16-row tile");
+    TORCH_CHECK(act_mode == 0 && fin_mode == 0, "fused producers / finishers need a 16-row tile");
   }
-  static bool attr_set[5] = {false, false, false, false, false};
+  static bool attr_set[7] = {false, false, false, false, false, false, false};
   if (!attr_set[variant]) {
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));

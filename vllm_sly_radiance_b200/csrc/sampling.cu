@@ -209,17 +209,21 @@ struct TkSmem {
   uint32_t keys[TK_CHUNK];
   int idx[TK_CHUNK];                 // merge stage: column of each candidate
   int hist[TK_WARPS][256];
+  int tot[256];
   uint32_t sel_key[TK];
   int sel_idx[TK];
   float win_val[TK];
   int wtot[2][TK_WARPS];
-  int sh_bin, sh_k;
+  int sh_bin, sh_k, sh_cnt;
+  uint32_t sh_thr;
   bool last;
 };
 
-// K-th largest of keys[0, n) (n >= K): returns the key and how many elements equal to it belong
-// to the top K
-DEVI void radix_kth(TkSmem& s, int n, int K, uint32_t& thr, int& need_eq) {
+// The top K of keys[0, n) (n >= K) as a digit prefix: every key whose masked value is above
+// `prefix` is selected, and the first `need_eq` keys (in index order) whose masked value equals
+// it.  8-bit digits from the top; the passes stop as soon as the threshold bin holds exactly the
+// keys still needed (then all of them are selected).
+DEVI void radix_kth(TkSmem& s, int n, int K, uint32_t& prefix_out, uint32_t& mask_out, int& need_eq) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   uint32_t prefix = 0, mask = 0;
   int k = K;
@@ -240,18 +244,21 @@ DEVI void radix_kth(TkSmem& s, int n, int K, uint32_t& thr, int& need_eq) {
       }
     }
     __syncthreads();
+    {   // per-bin totals: one bin per thread
+      int v = 0;
+#pragma unroll
+      for (int w = 0; w < TK_WARPS; ++w) v += s.hist[w][tid];
+      s.tot[tid] = v;
+    }
+    __syncthreads();
     if (warp == 0) {
       // lane l owns the bins 255 - 8l ... 248 - 8l (descending order)
       int c[8];
       int tot = 0;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const int b = 255 - (8 * lane + j);
-        int v = 0;
-#pragma unroll
-        for (int w = 0; w < TK_WARPS; ++w) v += s.hist[w][b];
-        c[j] = v;
-        tot += v;
+        c[j] = s.tot[255 - (8 * lane + j)];
+        tot += c[j];
       }
       int incl = tot;
 #pragma unroll
@@ -267,6 +274,7 @@ DEVI void radix_kth(TkSmem& s, int n, int K, uint32_t& thr, int& need_eq) {
           if (cum + c[j] >= k) {
             s.sh_bin = 255 - (8 * lane + j);
             s.sh_k = k - cum;
+            s.sh_cnt = c[j];
             break;
           }
           cum += c[j];
@@ -277,14 +285,17 @@ DEVI void radix_kth(TkSmem& s, int n, int K, uint32_t& thr, int& need_eq) {
     prefix |= (uint32_t)s.sh_bin << shift;
     mask |= 255u << shift;
     k = s.sh_k;
+    if (s.sh_cnt == k) break;       // the whole bin is selected: the prefix decides
   }
-  thr = prefix;
+  prefix_out = prefix;
+  mask_out = mask;
   need_eq = k;
 }
 
-// The K selected entries in index order: every key > thr, then the first need_eq keys == thr.
+// The K selected entries in index order: every key with (key & mask) > prefix, then the first
+// need_eq keys with (key & mask) == prefix.
 template <typename F>
-DEVI void collect_topk(TkSmem& s, int n, int K, uint32_t thr, int need_eq, F col) {
+DEVI void collect_topk(TkSmem& s, int n, int K, uint32_t prefix, uint32_t mask, int need_eq, F col) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_gt = K - need_eq;
   int base_gt = 0, base_eq = 0;
@@ -292,8 +303,9 @@ DEVI void collect_topk(TkSmem& s, int n, int K, uint32_t thr, int need_eq, F col
   for (int i0 = 0; i0 < n; i0 += TK_THREADS) {
     const int i = i0 + tid;
     const uint32_t u = i < n ? s.keys[i] : 0u;
-    const bool gt = i < n && u > thr;
-    const bool eq = i < n && u == thr;
+    const uint32_t um = u & mask;
+    const bool gt = i < n && um > prefix;
+    const bool eq = i < n && um == prefix;
     const unsigned mg = __ballot_sync(0xffffffffu, gt), me = __ballot_sync(0xffffffffu, eq);
     if (lane == 0) {
       s.wtot[0][warp] = __popc(mg);
@@ -314,6 +326,7 @@ DEVI void collect_topk(TkSmem& s, int n, int K, uint32_t thr, int need_eq, F col
     base_gt += tg;
     base_eq += te;
     __syncthreads();
+    if (base_gt >= n_gt && base_eq >= need_eq) break;     // uniform: every slot is filled
   }
 }
 
@@ -349,10 +362,10 @@ __global__ void __launch_bounds__(TK_THREADS) topk_window_kernel(
   const TIn* xr = x + (size_t)row * ld + c0;
   for (int i = threadIdx.x; i < n; i += TK_THREADS) s.keys[i] = f2key(to_f(xr[i]));
   __syncthreads();
-  uint32_t thr;
+  uint32_t pre, msk;
   int need;
-  radix_kth(s, n, TK, thr, need);
-  collect_topk(s, n, TK, thr, need, [&](int i) { return c0 + i; });
+  radix_kth(s, n, TK, pre, msk, need);
+  collect_topk(s, n, TK, pre, msk, need, [&](int i) { return c0 + i; });
   const size_t off = ((size_t)row * nch + ch) * TK;
   rank_sort(s, TK, pk + off, pi + off);
   __threadfence();
@@ -361,17 +374,44 @@ __global__ void __launch_bounds__(TK_THREADS) topk_window_kernel(
   __syncthreads();
   if (!s.last) return;
   __threadfence();
-  // merge: the chunks' candidate lists are in column order, so ties keep the lowest columns
+  // merge.  Chunk c holds 64 keys >= its 64th key t_c, so the row's top 64 are all >= T* = max
+  // t_c: only list entries >= T* are candidates (usually a few more than 64).  The lists are in
+  // column order, so ties keep the lowest columns.
   const int nc = nch * TK;
   const uint32_t* rk = pk + (size_t)row * nc;
   const int* ri = pi + (size_t)row * nc;
-  for (int i = threadIdx.x; i < nc; i += TK_THREADS) {
-    s.keys[i] = __ldcg(rk + i);
-    s.idx[i] = __ldcg(ri + i);
+  if (threadIdx.x < 32) {
+    uint32_t t = 0;
+    for (int c = threadIdx.x; c < nch; c += 32) t = max(t, __ldcg(rk + (size_t)c * TK + TK - 1));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t = max(t, __shfl_xor_sync(0xffffffffu, t, o));
+    if (threadIdx.x == 0) { s.sh_thr = t; s.sh_cnt = 0; }
   }
   __syncthreads();
-  radix_kth(s, nc, TK, thr, need);
-  collect_topk(s, nc, TK, thr, need, [&](int i) { return s.idx[i]; });
+  const uint32_t tstar = s.sh_thr;
+  for (int i0 = 0; i0 < nc; i0 += TK_THREADS) {     // ordered compaction of the candidates
+    const int i = i0 + threadIdx.x;
+    const uint32_t u = i < nc ? __ldcg(rk + i) : 0u;
+    const bool keep = i < nc && u >= tstar;
+    const unsigned m = __ballot_sync(0xffffffffu, keep);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) s.wtot[0][warp] = __popc(m);
+    __syncthreads();
+    int pos = s.sh_cnt, tot = 0;
+#pragma unroll
+    for (int w = 0; w < TK_WARPS; ++w) {
+      if (w < warp) pos += s.wtot[0][w];
+      tot += s.wtot[0][w];
+    }
+    pos += __popc(m & ((1u << lane) - 1u));
+    if (keep) { s.keys[pos] = u; s.idx[pos] = __ldcg(ri + i); }
+    __syncthreads();
+    if (threadIdx.x == 0) s.sh_cnt += tot;
+    __syncthreads();
+  }
+  const int ncand = s.sh_cnt;
+  radix_kth(s, ncand, TK, pre, msk, need);
+  collect_topk(s, ncand, TK, pre, msk, need, [&](int i) { return s.idx[i]; });
   rank_sort(s, TK, s.keys, s.idx);
   __syncthreads();
   if (threadIdx.x < TK) {

@@ -356,6 +356,8 @@ def qkv_prologue(qkv, positions, q_norm_w, k_norm_w, cos_sin, k_cache, v_cache, 
 
 
 _ATTN_DECODE = os.environ.get("RADIANCE_ATTN_DECODE", "1") != "0"
+# chunked prefill over the fp8 cache on the tcgen05 attention kernel (csrc/fmha.cu)
+_FMHA = os.environ.get("RADIANCE_FMHA", "1") != "0"
 
 
 def attention_decode_gated_ok(q, k_cache, meta) -> bool:
@@ -410,6 +412,13 @@ def paged_attention(q, k_cache, v_cache, meta, scale: float, causal: bool = True
     # (keys split across warps) replaces the 64-row tile kernel
     decode = (meta.num_tokens == meta.num_seqs and Hq // k_cache.shape[1] <= 16
               and _ATTN_DECODE)
+    if (not decode and _FMHA and causal and window == 0 and meta.num_splits == 1 and D == 256
+            and k_cache.dtype == torch.float8_e4m3fn and k_cache.shape[2] == 64):
+        # prefill on tcgen05 (e4m3 QK / PV legs, TMEM accumulators, TMA-fed pages)
+        ext().fmha_prefill(q, k_cache, v_cache, meta.block_tables, meta.seq_lens,
+                           meta.query_start_loc, meta.tile_seq, meta.tile_row0, scale, out,
+                           status_word(q.device))
+        return out
     # the decode kernel merges up to 128 KV splits in-kernel, the tile kernel up to 32
     _paged_attention_launch(q, k_cache, v_cache, meta, scale, causal, window, out, decode)
     return out
@@ -495,7 +504,7 @@ def gdn_decode_fused_quant(proj, ba_off: int, z_off: int, conv_w, conv_state, ss
     nout = torch.empty(B, Hv * DV, dtype=torch.bfloat16, device=dev)
     q = torch.empty(B, Hv * DV, dtype=torch.float8_e4m3fn, device=dev)
     qs = torch.empty(B, dtype=torch.float32, device=dev)
-    ws = workspace(dev, "gdn_fq", max(4096, B * (1 + Hv)))
+    ws = workspace(dev, "gdn_fq", 4096 + B * Hv)
     ext().gdn_decode_fused(proj, ba_off, conv_w, conv_state, A_log, dt_bias, ssm_state,
                            meta.state_slots, meta.has_initial, num_k_heads, scale, eps,
                            _empty(dev), 1, z_off, norm_w, norm_eps, nout, ws, q, qs)
@@ -505,7 +514,9 @@ def gdn_decode_fused_quant(proj, ba_off: int, z_off: int, conv_w, conv_state, ss
 _GDN_CHUNKED = os.environ.get("RADIANCE_GDN_CHUNKED", "1") != "0"
 _GDN_CHUNK_SPLIT = int(os.environ.get("RADIANCE_GDN_CHUNK_SPLIT", "0"))   # 0: by batch size
 _GDN_DECODE_FUSED = os.environ.get("RADIANCE_GDN_DECODE_FUSED", "1") != "0"
-_ATTN_GATE_FUSED = os.environ.get("RADIANCE_ATTN_GATE_FUSED", "1") != "0"
+# the o_proj producer inside decode attention: opt-in, it measured slower than attention followed
+# by gate_mul_quant (the gate runs after two levels of last-CTA serialisation: splits, kv heads)
+_ATTN_GATE_FUSED = os.environ.get("RADIANCE_ATTN_GATE_FUSED", "0") == "1"
 # the out_proj producer (gated norm + e4m3) inside the fused decode step
 _GDN_DECODE_FUSED_QUANT = os.environ.get("RADIANCE_GDN_DECODE_FUSED_QUANT", "1") != "0"
 
