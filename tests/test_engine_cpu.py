@@ -78,6 +78,45 @@ def test_kl_quantized_vs_bf16_tiny():
     assert kl < 0.05, kl
 
 
+def test_mxfp6_mxfp8_models_close_to_bf16():
+    """The wider MX element types run the same engine path.  e2m3 and e4m3 both carry three
+    mantissa bits (against e2m1's one), so both land well below MXFP4's KL to the bf16 model; the
+    remaining gap is the e4m3 activations and KV they share."""
+    torch.manual_seed(0)
+    prompt = torch.randint(3, 4096, (96,)).tolist()
+    lb = torch.log_softmax(_prefill_logits(_engine(4096, "bf16"), prompt), -1)
+    kls = {}
+    for quant in ("mxfp4", "mxfp6", "mxfp8"):
+        eng = _engine(4096, quant)
+        fmts = {lin.w.fmt for lin in _linears(eng.model)}
+        assert fmts == {{"mxfp4": "e2m1", "mxfp6": "e2m3", "mxfp8": "e4m3"}[quant]}, fmts
+        lq = torch.log_softmax(_prefill_logits(eng, prompt), -1)
+        kls[quant] = float((lb.exp() * (lb - lq)).sum(-1).mean())
+    assert kls["mxfp4"] < 0.05 and max(kls["mxfp6"], kls["mxfp8"]) < kls["mxfp4"] / 3, kls
+
+
+def _linears(model):
+    from vllm_sly_radiance_b200.models.layers import Linear
+    out, seen = [], set()
+
+    def walk(o, depth=0):
+        if id(o) in seen or depth > 4:
+            return
+        seen.add(id(o))
+        if isinstance(o, Linear):
+            if o.quant == "mxfp4":
+                out.append(o)
+            return
+        if isinstance(o, (list, tuple)):
+            for v in o:
+                walk(v, depth + 1)
+        elif hasattr(o, "__dict__"):
+            for v in vars(o).values():
+                walk(v, depth + 1)
+    walk(model)
+    return out
+
+
 def test_int4_model_and_int4_lm_head_close_to_bf16():
     """W4A16 INT4 linears (and an int4 lm_head on the MXFP4 model) stay close to the bf16 model."""
     torch.manual_seed(0)

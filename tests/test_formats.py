@@ -1,4 +1,5 @@
 """Number formats: E2M1 / UE8M0 / MXFP4, e4m3 per-token, NVFP4 requant, INT4, SF tile layout."""
+import pytest
 import torch
 
 from vllm_sly_radiance_b200.ops import reference as ref
@@ -155,3 +156,85 @@ def test_quant_embedding_roundtrip():
         step = want.abs().amax(1, keepdim=True) * tol
         assert ((got - want).abs() <= 0.51 * step + 4e-3 * want.abs()).all(), bits
     assert QuantEmbedding.from_float(w, 4).nbytes < w.numel() * 2 // 3
+
+
+# ---- MXFP6 (e2m3) / MXFP8 (e4m3) weights ----------------------------------------------------
+def test_e2m3_grid_and_rounding():
+    # every code decodes to the OCP E2M3 value (bias 1, subnormals k/8) and encodes back
+    codes = torch.arange(64, dtype=torch.uint8)
+    vals = F.e2m3_decode(codes)
+    for c in range(64):
+        sgn = -1.0 if c & 32 else 1.0
+        e, m = (c >> 3) & 3, c & 7
+        want = m / 8 if e == 0 else (1 + m / 8) * 2.0 ** (e - 1)
+        assert float(vals[c]) == sgn * want, c
+    nz = codes[(codes != 32)]                    # -0 encodes as +0
+    assert torch.equal(F.e2m3_encode(F.e2m3_decode(nz)), nz)
+    # saturation and ties to even code: 7.75 -> 7.5, 0.0625 (between 0 and 1/8) -> 0
+    x = torch.tensor([100.0, -100.0, 7.75, 0.0625, 0.1875, 1.0625])
+    got = F.e2m3_decode(F.e2m3_encode(x)).tolist()
+    assert got == [7.5, -7.5, 7.5, 0.0, 0.25, 1.0]
+
+
+def test_pack_6bit_layout():
+    # four codes per three bytes, code i at bits [6i, 6i + 6) of the little-endian 24-bit word
+    codes = torch.tensor([[1, 2, 3, 63]], dtype=torch.uint8)
+    word = 1 | (2 << 6) | (3 << 12) | (63 << 18)
+    assert F.pack_6bit(codes).tolist() == [[word & 255, (word >> 8) & 255, word >> 16]]
+    c = torch.randint(0, 64, (5, 64), dtype=torch.uint8)
+    assert torch.equal(F.unpack_6bit(F.pack_6bit(c)), c)
+
+
+@pytest.mark.parametrize("fmt,bits,tol", [("e2m1", 4, 0.15), ("e2m3", 6, 0.05), ("e4m3", 8, 0.04)])
+def test_mx_formats_quantize(fmt, bits, tol):
+    g = torch.Generator().manual_seed(1)
+    w = torch.randn(48, 320, generator=g)
+    p, s = F.mx_quantize(w, fmt)
+    assert p.shape == (48, 320 * bits // 8) and s.shape == (48, 10)
+    dq = F.mx_dequantize(p, s, fmt)
+    assert ((dq - w).norm() / w.norm()).item() < tol
+    # the block maximum never saturates: amax / 2^(floor(log2 amax) - emax) < 2^(emax + 1)
+    blk = w.view(48, 10, 32).abs().amax(-1)
+    scale = F.ue8m0_to_float(s)
+    limit = {"e2m1": 6.0, "e2m3": 7.5, "e4m3": 448.0}[fmt]
+    assert bool(((blk / scale) < 2 * limit).all())
+
+
+@pytest.mark.parametrize("fmt", ["e2m3", "e4m3"])
+def test_mx_weight_container(fmt):
+    from vllm_sly_radiance_b200.quant.mxfp4 import cat_rows
+    g = torch.Generator().manual_seed(2)
+    w = torch.randn(40, 8704, generator=g) * 0.02
+    full = MXFP4Weight.from_float(w, fmt)
+    assert full.fmt == fmt and full.K_padded == 8704
+    shard = full.narrow_cols(1088 * 3, 1088)
+    assert shard.fmt == fmt and shard.K == 1088 and shard.K_padded == 1152
+    assert torch.equal(shard.dequantize(), full.dequantize()[:, 1088 * 3:1088 * 4])
+    rows = full.narrow_rows(8, 16)
+    assert torch.equal(rows.dequantize(), full.dequantize()[8:24])
+    both = cat_rows([rows, full.narrow_rows(0, 8)])
+    assert both.fmt == fmt and both.N == 24
+    padded = shard.pad_cols(1152 + 32)
+    assert torch.equal(padded.dequantize()[:, :1088], shard.dequantize())
+    assert float(padded.dequantize()[:, 1088:].abs().sum()) == 0.0
+    x = torch.randn(3, 1088, generator=g)
+    q, s = ref.quant_fp8_rows(x.to(torch.bfloat16))
+    got = ref.mxfp4_linear(q, s, shard.packed, shard.scales, fmt=fmt).float()
+    want = ((q.float() @ shard.dequantize().t()) * s[:, None]).to(torch.bfloat16).float()
+    assert torch.equal(got, want)
+
+
+def test_mx_cast_weights_keeps_mxfp4_values():
+    """An MXFP4 linear served as MXFP8 is exact (e2m1 x 2^s is representable in e4m3 x 2^s')."""
+    from vllm_sly_radiance_b200.models.weights import MXCastWeights
+
+    class Src:
+        cfg = None
+
+        def linear(self, name, N, K):
+            return MXFP4Weight.from_float(torch.randn(N, K, generator=torch.Generator().manual_seed(3)))
+    src = Src()
+    w8 = MXCastWeights(src, "e4m3").linear("x", 16, 256)
+    assert w8.fmt == "e4m3"
+    assert torch.equal(w8.dequantize(), src.linear("x", 16, 256).dequantize())
+    assert MXCastWeights(src, "e4m3", skip=("x",)).linear("x", 16, 256).fmt == "e2m1"

@@ -48,6 +48,68 @@ def test_mxfp4_gemm(M, N, Kd, splits):
     assert rel_err(got, want) < 1e-2, rel_err(got, want)
 
 
+@pytest.mark.parametrize("fmt", ["e2m3", "e4m3"])
+@pytest.mark.parametrize("M,N,Kd,splits", [
+    (1, 256, 256, 0), (5, 384, 512, 0), (16, 256, 1024, 4), (37, 200, 768, 0),
+    (128, 256, 256, 0), (300, 512, 1024, 0), (1, 5120, 8704, 0), (3, 384, 1088, 2),
+    (40, 2176, 1088, 0)])
+def test_mx_gemm_formats(fmt, M, N, Kd, splits):
+    """MXFP6 (e2m3, TMA 16U6) and MXFP8 (e4m3) weights through the same block-scaled kernel."""
+    g = torch.Generator().manual_seed(M * 7 + N + len(fmt))
+    w = torch.randn(N, Kd, generator=g) * 0.02
+    x = torch.randn(M, Kd, generator=g)
+    wq = MXFP4Weight.from_float(w, fmt)
+    q, s = ref.quant_fp8_rows(x.to(torch.bfloat16))
+    want = ref.mxfp4_linear(q, s, wq.packed, wq.scales, fmt=fmt)
+    wg = wq.to(DEV)
+    got = K.mxfp4_gemm(q.to(DEV), s.to(DEV), wg.packed, wg.sf, wg.scales, N, splits=splits)
+    torch.cuda.synchronize()
+    K.check_status(got.device)
+    assert rel_err(got, want) < 1e-2, rel_err(got, want)
+
+
+@pytest.mark.parametrize("fmt", ["e2m3", "e4m3"])
+def test_mx_formats_fused_and_grouped(fmt):
+    """The decode producer-fused GEMM, the finisher GEMM and the grouped (MoE) GEMM accept the
+    wider element types too."""
+    from vllm_sly_radiance_b200.quant.mxfp4 import cat_rows
+    g = torch.Generator().manual_seed(21)
+    N, Kd = 2176, 1088
+    wq = MXFP4Weight.from_float(torch.randn(N, Kd, generator=g) * 0.02, fmt).to(DEV)
+    h = torch.randn(1, Kd, generator=g).to(torch.bfloat16).to(DEV)
+    lw = (0.1 * torch.randn(Kd, generator=g)).to(torch.bfloat16).to(DEV)
+    q, s, r = K.add_rms_quant(h, None, lw, 1e-6)
+    want = ref.mxfp4_linear(q.cpu(), s.cpu(), wq.packed.cpu(), wq.scales.cpu(), fmt=fmt)
+    out = torch.empty(1, N, dtype=torch.bfloat16, device=DEV)
+    K.mxfp4_gemm_act(1, h, None, lw, None, 1e-6, wq, out)
+    torch.cuda.synchronize()
+    K.check_status(out.device)
+    assert rel_err(out, want) < 1e-2, rel_err(out, want)
+    # finisher: SiLU * mul + e4m3 of the GEMM's own output rows
+    got, fq, fs = K.mxfp4_gemm_finish(q, s, wq, K.FIN_SILU)
+    torch.cuda.synchronize()
+    assert rel_err(got, want) < 1e-2
+    wq2, ws2 = K.silu_mul_quant(got)
+    assert fp8_close(fq, fs, wq2, ws2)
+    # grouped
+    E, Ng, Kg = 4, 256, 512
+    ws = [MXFP4Weight.from_float(torch.randn(Ng, Kg, generator=g) * 0.02, fmt) for _ in range(E)]
+    counts = torch.tensor([3, 0, 40, 1])
+    x = torch.randn(int(counts.sum()), Kg, generator=g).to(torch.bfloat16)
+    q, s = ref.quant_fp8_rows(x)
+    want, r0 = torch.empty(x.shape[0], Ng), 0
+    for e in range(E):
+        c = int(counts[e])
+        if c:
+            want[r0:r0 + c] = ref.mxfp4_linear(q[r0:r0 + c], s[r0:r0 + c], ws[e].packed,
+                                               ws[e].scales, fmt=fmt).float()
+        r0 += c
+    got = K.moe_grouped_gemm(q.to(DEV), s.to(DEV), cat_rows(ws).to(DEV), Ng, counts.to(DEV))
+    torch.cuda.synchronize()
+    K.check_status(got.device)
+    assert rel_err(got, want) < 1e-2, rel_err(got, want)
+
+
 @pytest.mark.parametrize("mode,M,N,Kd,with_res", [
     (1, 1, 16480, 5120, True), (1, 1, 2176, 1088, False), (1, 1, 5120, 256, True),
     (2, 1, 5120, 8704, False), (2, 1, 384, 1088, False), (2, 1, 256, 768, False)])

@@ -41,6 +41,10 @@ def _write_hf(rec, cfg, path, fmt):
             p, s = F.mxfp4_quantize(w)
             sd[hf + ".weight_packed"] = p
             sd[hf + ".weight_scale"] = s
+        elif fmt == "mxfp6":
+            p, s = F.mx_quantize(w, "e2m3")
+            sd[hf + ".weight_packed"] = p
+            sd[hf + ".weight_scale"] = s
         elif fmt == "int4":       # compressed-tensors pack-quantized, 8 nibbles per int32
             p, sc, zp = F.int4_g128_quantize(w)
             sd[hf + ".weight_packed"] = p.contiguous().view(torch.int32)
@@ -134,6 +138,21 @@ def test_load_matches_canonical(tmp_path, fmt):
     assert torch.equal(m.embed, ref_model.embed)
 
 
+def test_mxfp6_checkpoint_model(tmp_path):
+    """A whole MXFP6 checkpoint (merged GDN in_proj with its float ba part, qkv, gate_up) loads
+    into the codes an mxfp6 model quantises from the same weights."""
+    cfg = tiny_hybrid()
+    rec = Recorder(cfg)
+    ref_model = HybridModel(cfg, quant="mxfp6", device="cpu", weights=rec)
+    _write_hf(rec, cfg, str(tmp_path), "mxfp6")
+    m = HybridModel(cfg, quant="mxfp6", device="cpu", weights=CheckpointWeights(str(tmp_path), cfg))
+    for a, b in ((ref_model.layers[0].mixer.in_proj, m.layers[0].mixer.in_proj),
+                 (ref_model.layers[3].mixer.qkv, m.layers[3].mixer.qkv),
+                 (ref_model.layers[1].mlp.gate_up, m.layers[1].mlp.gate_up)):
+        assert a.w.fmt == b.w.fmt == "e2m3"
+        assert torch.equal(a.w.packed, b.w.packed)
+
+
 @pytest.mark.parametrize("fmt", ["int4", "gptq"])
 def test_int4_checkpoint_stays_int4(tmp_path, fmt):
     """An INT4 (W4A16 pack-quantized) checkpoint served with quantization=int4 keeps its codes:
@@ -158,3 +177,87 @@ def test_int4_checkpoint_stays_int4(tmp_path, fmt):
     a = ref_model.layers[0].mlp.gate_up(x).float()
     b = m.layers[0].mlp.gate_up(x).float()
     assert float((a - b).norm() / a.norm()) < 0.15
+
+
+# ---- single-linear checkpoints of the other stored formats ----------------------------------
+def _one_linear(tmp_path, tensors, qcfg=None, table=None):
+    import json
+    from vllm_sly_radiance_b200.quant.loaders import CheckpointWeights
+    save_file({k: v.contiguous() for k, v in tensors.items()}, os.path.join(tmp_path, "m.safetensors"))
+    if qcfg is not None:
+        json.dump({"quantization_config": qcfg}, open(os.path.join(tmp_path, "config.json"), "w"))
+    if table is not None:
+        torch.save(table, os.path.join(tmp_path, "bcq_tables.pt"))
+    return CheckpointWeights(str(tmp_path), tiny_hybrid())
+
+
+def _bcq_case(N=64, K=256, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    table = torch.rand(256, 8, generator=g) * 6
+    table[:, 0] = 0
+    table = table.to(torch.float8_e4m3fn).float()                  # e4m3-exact magnitudes
+    packed = torch.randint(0, 256, (N, K // 2), generator=g, dtype=torch.uint8)
+    ids = torch.randint(0, 256, (N, K // 32), generator=g, dtype=torch.uint8)
+    row_exp = torch.randint(115, 125, (N,), generator=g, dtype=torch.uint8)
+    return table, packed, ids, row_exp
+
+
+def test_mxfp6_checkpoint_loads_as_stored(tmp_path):
+    w = torch.randn(64, 256) * 0.05
+    p, s = F.mx_quantize(w, "e2m3")
+    W = _one_linear(tmp_path, {"x.weight_packed": p, "x.weight_scale": s})
+    got = W._linear_any("x")
+    assert got.fmt == "e2m3" and torch.equal(got.packed, p) and got.K == 256
+    assert torch.equal(got.dequantize(), F.mx_dequantize(p, s, "e2m3"))
+
+
+def test_mxfp8_checkpoint_loads_as_stored(tmp_path):
+    w = torch.randn(32, 128) * 0.05
+    p, s = F.mx_quantize(w, "e4m3")
+    W = _one_linear(tmp_path, {"x.weight": p.view(torch.float8_e4m3fn), "x.weight_scale": s})
+    got = W._linear_any("x")
+    assert got.fmt == "e4m3" and torch.equal(got.packed, p)
+
+
+def test_bcq4_checkpoint_is_exact_in_mxfp8(tmp_path):
+    """BCQ4: sign * table[id][mag] * 2^(row_exp - 127) -> MXFP8 with no rounding."""
+    from vllm_sly_radiance_b200.quant.loaders import bcq_dequantize
+    table, packed, ids, row_exp = _bcq_case()
+    W = _one_linear(tmp_path, {"x.weight_packed": packed, "x.weight_scale": ids,
+                               "x.weight_row_exp": row_exp}, table=table)
+    got = W._linear_any("x")
+    want = bcq_dequantize(packed, ids, row_exp, table)
+    assert got.fmt == "e4m3"
+    assert torch.equal(got.dequantize(), want)
+    # independent decode of one element: row 3, column 37 (odd -> high nibble of byte 18)
+    nib = int(packed[3, 18]) >> 4
+    v = float(table[int(ids[3, 1]), nib & 7]) * 2.0 ** (int(row_exp[3]) - 127)
+    assert float(want[3, 37]) == (-v if nib >= 8 else v)
+
+
+def test_bcq4_hadamard_checkpoint_is_derotated(tmp_path):
+    """Hadamard-128 BCQ4 (stored W' = W R): the loaded weight W' R^T serves y = x W^T, the same
+    product the reference forms as (x R) W'^T with the rotation applied to activations."""
+    from vllm_sly_radiance_b200.quant.loaders import bcq_dequantize, hadamard_rotation
+    R = hadamard_rotation(128)
+    assert torch.allclose(R @ R.t(), torch.eye(128), atol=1e-5)
+    table, packed, ids, row_exp = _bcq_case(seed=1)
+    W = _one_linear(tmp_path, {"x.weight_packed": packed, "x.weight_scale": ids,
+                               "x.weight_row_exp": row_exp}, qcfg={"hadamard": 128}, table=table)
+    got = W._linear_any("x")
+    wr = bcq_dequantize(packed, ids, row_exp, table)                  # W' (rotated)
+    x = torch.randn(5, 256)
+    want = (x.view(5, 2, 128) @ R).view(5, 256) @ wr.t()
+    y = x @ got.dequantize().t()
+    assert float((y - want).norm() / want.norm()) < 0.03
+
+
+def test_fp8_block_checkpoint_dequantizes(tmp_path):
+    g = torch.Generator().manual_seed(4)
+    q = (torch.randn(256, 384, generator=g) * 50).clamp(-448, 448).to(torch.float8_e4m3fn)
+    si = torch.rand(2, 3, generator=g) + 0.01
+    W = _one_linear(tmp_path, {"x.weight": q, "x.weight_scale_inv": si},
+                    qcfg={"weight_block_size": [128, 128]})
+    got = W._linear_any("x")
+    assert torch.equal(got[130:, 260:], q.float()[130:, 260:] * si[1, 2])
+    assert torch.equal(got[:128, :128], q.float()[:128, :128] * si[0, 0])

@@ -170,9 +170,131 @@ def bench_w4a16(ms, shapes):
                               "frac_hbm": round(byts / t / bw, 3), "peaks": src}), flush=True)
 
 
+def bench_gemm_finish(ms, shapes):
+    """Decode GEMM whose last CTA runs the next linear's producer (finisher) against the GEMM
+    followed by the stand-alone producer kernel."""
+    bw, _, src = peaks()
+    for (N, Kd, name) in shapes:
+        nrot = max(2, int(300e6 // (N * Kd // 2)) + 1)
+        ws = [MXFP4Weight.from_float(torch.randn(N, Kd, device="cuda") * 0.02) for _ in range(nrot)]
+        mode = K.FIN_SILU if name.startswith("gate_up") else K.FIN_NORM
+        for M in ms:
+            x = torch.randn(M, Kd, device="cuda").to(torch.bfloat16)
+            q, s = K.quant_fp8(x)
+            res = torch.randn(M, N, device="cuda").to(torch.bfloat16)
+            lw = torch.zeros(N, device="cuda", dtype=torch.bfloat16)
+            ro = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+
+            def fused(i):
+                w = ws[i % nrot]
+                if mode == K.FIN_NORM:
+                    K.mxfp4_gemm_finish(q, s, w, mode, res, lw, ro, 1e-6)
+                else:
+                    K.mxfp4_gemm_finish(q, s, w, mode)
+
+            def separate(i):
+                w = ws[i % nrot]
+                y = K.mxfp4_gemm(q, s, w.packed, w.sf, w.scales, N)
+                if mode == K.FIN_NORM:
+                    K.add_rms_quant(y, res, lw, 1e-6)
+                else:
+                    K.silu_mul_quant(y)
+            for kname, fn in (("gemm+finisher", fused), ("gemm, producer", separate)):
+                t = timeit(fn)
+                byts = N * Kd // 2 + N * Kd // 32
+                print(json.dumps({"kernel": kname, "shape": name, "M": M, "us": round(t * 1e6, 2),
+                                  "frac_hbm": round(byts / t / bw, 3), "peaks": src}), flush=True)
+
+
+def bench_fmha(q_len, ctxs):
+    """Causal prefill attention (27B layout: 24 q / 4 kv heads, D = 256, fp8 pages of 64): the
+    tcgen05 kernel and the mma.sync tile kernel, TFLOP/s of the causal work."""
+    _, fl, src = peaks()
+    Hq, Hkv, D, bs = 24, 4, 256, 64
+    for ctx in ctxs:
+        L = ctx + q_len
+        nb = (L + bs - 1) // bs
+        m = _AttnMeta()
+        m.block_tables = torch.randperm(nb, dtype=torch.int32).view(1, nb).cuda()
+        m.seq_lens = torch.tensor([L], dtype=torch.int32, device="cuda")
+        m.query_start_loc = torch.tensor([0, q_len], dtype=torch.int32, device="cuda")
+        R = q_len * (Hq // Hkv)
+        m.tile_seq = torch.zeros((R + 63) // 64, dtype=torch.int32, device="cuda")
+        m.tile_row0 = torch.arange(0, R, 64, dtype=torch.int32, device="cuda")
+        m.num_tokens, m.num_seqs, m.num_splits = q_len, 1, 1
+        m.scratch_o = lambda s_, T, H, D_: torch.empty(s_, T, H, D_, device="cuda")
+        m.scratch_ml = lambda s_, T, H: torch.empty(s_, T, H, 2, device="cuda")
+        kc = (torch.randn(nb, Hkv, bs, D, device="cuda") * 0.5).to(torch.float8_e4m3fn)
+        vc = torch.randn(nb, Hkv, bs, D, device="cuda").to(torch.float8_e4m3fn)
+        q = torch.randn(q_len, Hq, D, device="cuda").to(torch.float8_e4m3fn).to(torch.bfloat16)
+        # causal work: each query row sees ctx + its position + 1 keys
+        flops = 4.0 * Hq * D * (q_len * ctx + q_len * (q_len + 1) / 2)
+        for name, on in (("fmha_tcgen05", True), ("paged_attn_mma_sync", False)):
+            K._FMHA = on
+
+            def fn(i):
+                K.paged_attention(q, kc, vc, m, D ** -0.5)
+            t = timeit(fn, iters=10)
+            print(json.dumps({"kernel": name, "q_len": q_len, "ctx": ctx, "us": round(t * 1e6, 1),
+                              "TFLOPs": round(flops / t / 1e12, 1),
+                              "frac_fp8_tensor_peak": round(flops / t / (2 * fl), 3),
+                              "peaks": src + " (fp8 tensor = 2x measured bf16)"}), flush=True)
+        K._FMHA = True
+
+
+def bench_gdn_decode(batches):
+    """One-token GDN decode step of the 27B layout (16 k / 48 v heads, dk = dv = 128, fp32 state):
+    conv update + norms + gates + delta rule (+ gated norm + e4m3 for the fused-quant variant);
+    the state (64 KB per head) is read and written once."""
+    bw, _, src = peaks()
+    Hk, Hv, D = 16, 48, 128
+    key_dim, vdim = Hk * D, Hv * D
+    C = 2 * key_dim + vdim
+    for B in batches:
+        nrot = 8
+        states = [torch.randn(B + 1, Hv, D, D, device="cuda") * 0.05 for _ in range(nrot)]
+        conv = torch.randn(B + 1, C, 3, device="cuda").to(torch.bfloat16)
+        x = torch.randn(B, C + vdim + 2 * Hv + 8, device="cuda").to(torch.bfloat16)
+        conv_w = torch.randn(C, 4, device="cuda").to(torch.bfloat16)
+        A_log = torch.zeros(Hv, device="cuda")
+        dt = torch.zeros(Hv, device="cuda")
+        nw = torch.ones(D, device="cuda", dtype=torch.bfloat16)
+        m = _AttnMeta()
+        m.state_slots = torch.arange(1, B + 1, dtype=torch.int32, device="cuda")
+        m.has_initial = torch.ones(B, dtype=torch.int32, device="cuda")
+        m.num_seqs = m.num_tokens = B
+        byts = B * Hv * D * D * 4 * 2
+        for name in ("gdn_decode_fused", "gdn_decode_fused_quant"):
+            def fn(i, name=name):
+                st = states[i % nrot]
+                if name == "gdn_decode_fused":
+                    K.gdn_decode_fused(x, C + vdim, conv_w, conv, st, A_log, dt, m, Hk, D ** -0.5, split=1)
+                else:
+                    K.gdn_decode_fused_quant(x, C + vdim, C, conv_w, conv, st, A_log, dt, m, Hk,
+                                             D ** -0.5, nw, 1e-6)
+            t = timeit(fn)
+            print(json.dumps({"kernel": name, "B": B, "us": round(t * 1e6, 2),
+                              "state_GBps": round(byts / t / 1e9, 1),
+                              "frac_hbm": round(byts / t / bw, 3), "peaks": src}), flush=True)
+
+
+def bench_topk(batches):
+    for B in batches:
+        x = torch.randn(B, 248320, device="cuda").to(torch.bfloat16)
+        temp = torch.full((B,), 0.7, device="cuda")
+        tk = torch.full((B,), 20, dtype=torch.int32, device="cuda")
+        tp = torch.full((B,), 0.95, device="cuda")
+        sd = torch.arange(B, dtype=torch.int64, device="cuda")
+        t = timeit(lambda i: K.topk_sample(x, temp, tk, tp, None, sd, i))
+        t2 = timeit(lambda i: torch.topk(x.float(), 64, dim=-1))
+        print(json.dumps({"kernel": "topk_window+draw", "B": B, "us": round(t * 1e6, 2),
+                          "torch_topk_us": round(t2 * 1e6, 2)}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attn", "w4a16"])
+    ap.add_argument("what", choices=["gemm", "attn", "w4a16", "gemm_fin", "fmha", "topk", "gdn"])
+    ap.add_argument("--q-len", type=int, default=2048)
     ap.add_argument("--ctx", default="1500,4096,16384")
     ap.add_argument("--splits", default="1,4,8,17,32")
     ap.add_argument("--batch", type=int, default=1)
@@ -198,6 +320,15 @@ def main():
     elif a.what == "attn":
         bench_attn([int(v) for v in a.ctx.split(",")], [int(v) for v in a.splits.split(",")],
                    a.batch)
+    elif a.what == "gemm_fin":
+        bench_gemm_finish([m for m in ms if m <= 16] or [1],
+                          [sh for sh in shapes if sh[2] in ("out_proj", "gate_up", "down")] or shapes)
+    elif a.what == "fmha":
+        bench_fmha(a.q_len, [int(v) for v in a.ctx.split(",")])
+    elif a.what == "topk":
+        bench_topk([int(v) for v in a.m.split(",")])
+    elif a.what == "gdn":
+        bench_gdn_decode([int(v) for v in a.m.split(",")])
 
 
 if __name__ == "__main__":

@@ -263,7 +263,8 @@ class EngineConfig:
     tensor_parallel_size: int = 1
     expert_parallel: bool = False
     dtype: str = "bfloat16"
-    quantization: str = "mxfp4"         # mxfp4 (W4A8) | bf16 | nvfp4 (requantized to mxfp4) | int4
+    quantization: str = "mxfp4"         # mxfp4 (W4A8) | mxfp6 (W6A8) | mxfp8 (W8A8) | bf16 |
+    #                                     nvfp4 (requantized to mxfp4) | int4
     kv_cache_dtype: str = "fp8"         # fp8 | int4 (4-bit per-16 scale/zero) | bf16
     lm_head_quant: Optional[str] = None  # None (the model's) | int4 (W4A16 g128) | bf16 | mxfp4
     embed_quant: Optional[str] = None    # None (bf16) | int8 (per-row scale) | int4 (g128 scales)

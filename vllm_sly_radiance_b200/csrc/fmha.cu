@@ -27,6 +27,9 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <array>
+#include <map>
+
 #include <mutex>
 #include <unordered_map>
 
@@ -367,11 +370,14 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
 }  // namespace fmha
 
 static std::mutex g_fmha_mu;
-static std::unordered_map<uintptr_t, CUtensorMap> g_fmha_maps;
+// keyed by the cache's address and every dimension: a cache freed and another allocated at the
+// same address with another shape (an engine rebuilt with other TP or pool sizes) gets its own map
+static std::map<std::array<int64_t, 5>, CUtensorMap> g_fmha_maps;
 
 static CUtensorMap cache_map(const torch::Tensor& cache) {
   std::lock_guard<std::mutex> lk(g_fmha_mu);
-  const uintptr_t key = reinterpret_cast<uintptr_t>(cache.data_ptr()) ^ ((uintptr_t)cache.size(0) << 48);
+  const std::array<int64_t, 5> key{(int64_t)reinterpret_cast<uintptr_t>(cache.data_ptr()),
+                                   cache.size(0), cache.size(1), cache.size(2), cache.size(3)};
   auto it = g_fmha_maps.find(key);
   if (it != g_fmha_maps.end()) return it->second;
   const int64_t rows = cache.size(0) * cache.size(1) * cache.size(2);

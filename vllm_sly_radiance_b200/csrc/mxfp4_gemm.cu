@@ -1,6 +1,10 @@
-// MXFP4 W4A8 linear on 5th-generation tensor cores (sm_100a).
+// MX-format W4A8 / W6A8 / W8A8 linear on 5th-generation tensor cores (sm_100a).
 //
-//   C[m, n] = a_scale[m] * sum_k e4m3(A[m, k]) * e2m1(W[n, k]) * 2^(ws[n, k/32] - 127)
+//   C[m, n] = a_scale[m] * sum_k e4m3(A[m, k]) * w(W[n, k]) * 2^(ws[n, k/32] - 127)
+//
+// w is the weight element type, picked per call from the stored row width: e2m1 (MXFP4, K/2
+// bytes a row), e2m3 (MXFP6, 3K/4 bytes) or e4m3 (MXFP8, K bytes).  All three are native to
+// kind::mxf8f6f4; only the TMA map type, the transaction bytes and the MMA's A-format field change.
 //
 // Reference behaviour: the W4A8 GEMM family of sly/mxfp4/radiance_mxfp4_fp8.hip (:132 per-block,
 // :327 folded, :666 A-tiled prefill, :983 split-K decode).  The B200 design is different:
@@ -40,7 +44,15 @@ namespace mxfp4 {
 constexpr int BM = 128;          // weight rows per tile (MMA M)
 constexpr int BK = 128;          // K elements per pipeline stage (4 MMAs of K = 32)
 constexpr int W_TILE_BYTES = BM * BK;          // padded e2m1: 1 byte per element in smem
-constexpr int W_TILE_TX = BM * BK / 2;         // TMA transaction bytes (packed source)
+// weight element types: code 0 = e2m1 (16U4_ALIGN16B), 1 = e2m3 (16U6_ALIGN16B), 2 = e4m3 (UINT8).
+// TMA transaction bytes are the packed source bytes; the shared-memory tile is one byte per
+// element for all three (16 codes in a 16-byte group, the form the f8f6f4 MMA reads).
+__host__ __device__ constexpr uint32_t w_tile_tx(int wfmt) {
+  return wfmt == 0 ? BM * BK / 2 : wfmt == 1 ? BM * BK * 3 / 4 : BM * BK;
+}
+__host__ __device__ constexpr uint32_t w_mma_format(int wfmt) {
+  return wfmt == 0 ? 5u : wfmt == 1 ? 3u : 0u;          // E2M1 / E2M3 / E4M3
+}
 constexpr int SF_TILE_BYTES = 512;
 constexpr int kThreads = 192;
 constexpr int kSmemBudget = 227 * 1024;
@@ -67,9 +79,9 @@ struct Cfg {
   static_assert(BN * BM * 4 <= STAGES * STAGE_BYTES, "split-K partial tile must fit in stage smem");
 };
 
-__host__ __device__ constexpr uint32_t make_idesc(int bn, int sf_id) {
+__host__ __device__ constexpr uint32_t make_idesc(int bn, int sf_id, int wfmt = 0) {
   return (0u << 4)                       // b_sf_id set below
-         | (5u << 7)                     // A format: E2M1
+         | (w_mma_format(wfmt) << 7)     // A format: the weight element type
          | (0u << 10)                    // B format: E4M3
          | ((uint32_t)(bn >> 3) << 17)   // N >> 3
          | (1u << 23)                    // scale format UE8M0
@@ -179,7 +191,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
     mxfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
                       const __grid_constant__ CUtensorMap tmap_a, const uint8_t* __restrict__ sfw,
                       const float* __restrict__ a_scale, __nv_bfloat16* __restrict__ out,
-                      int ldo, int M, int N, int K, int k_tiles_per_split, int* __restrict__ status,
+                      int ldo, int M, int N, int K, int wfmt, int k_tiles_per_split, int* __restrict__ status,
                       const int* __restrict__ items, int n_per_group, const PushArgs push,
                       const ActArgs act, const FinCtl fin) {
   using C = Cfg<BN>;
@@ -268,7 +280,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
       // Weights and scale factors do not depend on the preceding kernel: fill the pipeline with
       // them while that kernel drains, then wait for it and add the activation tiles.
       const int pre = nk < C::STAGES ? nk : C::STAGES;
-      constexpr uint32_t kTx = W_TILE_TX + (ACT ? 0 : C::A_TILE_BYTES) + SF_TILE_BYTES;
+      const uint32_t kTx = w_tile_tx(wfmt) + (ACT ? 0 : C::A_TILE_BYTES) + SF_TILE_BYTES;
       for (int i = 0; i < pre; ++i) {
         uint8_t* st = stage_base + i * C::STAGE_BYTES;
         const int kt = kt0 + i;
@@ -315,7 +327,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
         for (int kb = 0; kb < BK / 32; ++kb) {
           const uint64_t adesc = sdesc_sw128(w_addr + kb * 32);
           const uint64_t bdesc = sdesc_sw128(a_addr + kb * 32);
-          const uint32_t idesc = make_idesc(BN, kb);
+          const uint32_t idesc = make_idesc(BN, kb, wfmt);
           mma_mxf8f6f4(tmem_acc, adesc, bdesc, idesc, tmem_sfa | ((uint32_t)kb << 30),
                        tmem_sfb | ((uint32_t)kb << 30), (i > 0 || kb > 0) ? 1u : 0u);
         }
@@ -554,8 +566,10 @@ struct MapKey {
   uintptr_t ptr;
   int64_t rows, cols, stride;
   int box_rows;
+  int wfmt;
   bool operator==(const MapKey& o) const {
-    return ptr == o.ptr && rows == o.rows && cols == o.cols && stride == o.stride && box_rows == o.box_rows;
+    return ptr == o.ptr && rows == o.rows && cols == o.cols && stride == o.stride &&
+           box_rows == o.box_rows && wfmt == o.wfmt;
   }
 };
 struct MapKeyHash {
@@ -568,12 +582,31 @@ struct MapKeyHash {
 static std::mutex g_map_mu;
 static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_wmaps;
 
-static CUtensorMap weight_map(const torch::Tensor& packed, int64_t N, int64_t K) {
-  MapKey key{(uintptr_t)packed.data_ptr(), N, K, packed.stride(0), BM};
+// Weight element type and whole-tile K from the stored row width (bytes) and the activation's K:
+// the three packings give distinct widths for the same K tiles, so the width names the type.
+struct WFmt {
+  int code;
+  int Kw;
+};
+static WFmt weight_fmt(int64_t row_bytes, int K) {
+  const int64_t Kp = (int64_t)(K + BK - 1) / BK * BK;
+  if (row_bytes * 2 == Kp) return {0, (int)Kp};
+  if (row_bytes * 4 == Kp * 3) return {1, (int)Kp};
+  if (row_bytes == Kp) return {2, (int)Kp};
+  TORCH_CHECK(false, "MX weight: a row of ", row_bytes, " bytes is not K = ", Kp,
+              " (activation K rounded up to 128) as e2m1, e2m3 or e4m3");
+  return {0, 0};
+}
+
+static CUtensorMap weight_map(const torch::Tensor& packed, int64_t N, int64_t K, int wfmt = 0) {
+  MapKey key{(uintptr_t)packed.data_ptr(), N, K, packed.stride(0), BM, wfmt};
   std::lock_guard<std::mutex> g(g_map_mu);
   auto it = g_wmaps.find(key);
   if (it != g_wmaps.end()) return it->second;
-  CUtensorMap m = make_tma_2d(packed.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B,
+  const CUtensorMapDataType dt = wfmt == 0 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B
+                                 : wfmt == 1 ? CU_TENSOR_MAP_DATA_TYPE_16U6_ALIGN16B
+                                             : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  CUtensorMap m = make_tma_2d(packed.data_ptr(), dt,
                               /*inner elems*/ K, /*rows*/ N, /*row stride bytes*/ packed.stride(0),
                               /*box inner*/ BK, /*box rows*/ BM, CU_TENSOR_MAP_SWIZZLE_128B);
   g_wmaps.emplace(key, m);
@@ -587,8 +620,9 @@ static void launch(const torch::Tensor& a, const torch::Tensor& a_scale, const t
                    const ActArgs& aa = ActArgs{}, bool rs = false, int fin_mode = 0,
                    const FinCtl& fc = FinCtl{}) {
   using C = Cfg<BN>;
-  const int Kw = (int)wp.size(1) * 2;          // whole K tiles of stored weight
-  CUtensorMap tw = weight_map(wp, N, Kw);
+  const WFmt wf = weight_fmt(wp.size(1), K);   // whole K tiles of stored weight
+  const int Kw = wf.Kw;
+  CUtensorMap tw = weight_map(wp, N, Kw, wf.code);
   // fused producers build the activation tiles in the kernel: no activation tensor map
   CUtensorMap ta = act_mode ? tw
                             : make_tma_2d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M,
@@ -632,7 +666,7 @@ static void launch(const torch::Tensor& a, const torch::Tensor& a_scale, const t
   C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tw, ta, (const uint8_t*)sf.data_ptr(),
                                     act_mode ? (const float*)nullptr : (const float*)a_scale.data_ptr(),
                                     no_out ? nullptr : (__nv_bfloat16*)out.data_ptr(),
-                                    no_out ? 0 : (int)out.stride(0), M, N, Kw,
+                                    no_out ? 0 : (int)out.stride(0), M, N, Kw, wf.code,
                                     per, status, (const int*)nullptr, 0, push, aa, fc));
 }
 
@@ -653,7 +687,8 @@ static void launch_grouped(const torch::Tensor& a, const torch::Tensor& a_scale,
   using C = Cfg<BN>;
   const int M = a.size(0);
   const int Ntot = wp.size(0);
-  CUtensorMap tw = weight_map(wp, Ntot, K);
+  const WFmt wf = weight_fmt(wp.size(1), K);
+  CUtensorMap tw = weight_map(wp, Ntot, K, wf.code);
   CUtensorMap ta = make_tma_2d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, a.stride(0), BK,
                                BN, CU_TENSOR_MAP_SWIZZLE_128B);
   auto kern = mxfp4_gemm_kernel<BN, true>;
@@ -666,14 +701,14 @@ static void launch_grouped(const torch::Tensor& a, const torch::Tensor& a_scale,
   C10_CUDA_CHECK(launch_pdl(kern, grid, dim3(kThreads), C::SMEM_BYTES, stream, tw, ta,
                             (const uint8_t*)sf.data_ptr(), (const float*)a_scale.data_ptr(),
                             (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0), M, Ntot, K,
-                            K / BK, status, (const int*)items.data_ptr(), n_per_group, PushArgs{},
+                            wf.code, K / BK, status, (const int*)items.data_ptr(), n_per_group, PushArgs{},
                             ActArgs{}, FinCtl{}));
 }
 
 }  // namespace mxfp4
 
-// Grouped (MoE) W4A8 GEMM.  a: expert-sorted e4m3 rows [R, K]; wp/sf: stacked expert weights
-// [E*n_per_group, K/2]; items [max_items, 3] int32 = (expert, first row, rows), rows <= bn.
+// Grouped (MoE) MX GEMM.  a: expert-sorted e4m3 rows [R, K]; wp/sf: stacked expert weights
+// [E*n_per_group, K * bits / 8]; items [max_items, 3] int32 = (expert, first row, rows), rows <= bn.
 void mxfp4_grouped_gemm(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, torch::Tensor sf,
                         torch::Tensor out, torch::Tensor items, int64_t bn, int64_t n_per_group,
                         torch::Tensor status) {
@@ -695,7 +730,8 @@ void mxfp4_grouped_gemm(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp
   }
 }
 
-// a: fp8 e4m3 [M, K] (row stride multiple of 16 bytes), a_scale fp32 [M], wp uint8 [N, K/2],
+// a: fp8 e4m3 [M, K] (row stride multiple of 16 bytes), a_scale fp32 [M], wp uint8 [N, Kw * bits
+// / 8] (e2m1 4, e2m3 6, e4m3 8 bits an element; Kw = K rounded up to 128),
 // sf: tiled scale factors, out: bf16 [M, N] (row stride ldo) -- or, with push.world > 0, no
 // output tensor: the tiles go to the peers' receive buffers.  Returns the number of output
 // tiles (= arrivals each peer receives from this rank).
@@ -714,9 +750,8 @@ static int64_t mxfp4_gemm_impl(torch::Tensor a, torch::Tensor a_scale, torch::Te
   // whole K tiles (Kw), and the activation's missing tail of the last tile is zero-filled by TMA
   // (out-of-range box elements read as zero)
   const int M = a.size(0), K = a.size(1), N = wp.size(0);
-  const int Kw = (int)wp.size(1) * 2;
-  TORCH_CHECK(K % 32 == 0 && Kw % BK == 0 && Kw >= K && Kw - K < BK,
-              "weight K must be the activation K rounded up to a multiple of 128");
+  const int Kw = weight_fmt(wp.size(1), K).Kw;
+  TORCH_CHECK(K % 32 == 0, "activation K must be a multiple of 32");
   TORCH_CHECK((a.stride(0) % 16) == 0 && (reinterpret_cast<uintptr_t>(a.data_ptr()) % 16) == 0,
               "activation rows must be 16-byte aligned");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(wp.data_ptr()) % 32) == 0 && (wp.stride(0) % 32) == 0,
@@ -774,9 +809,9 @@ void mxfp4_gemm_fin(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, to
                   (a.stride(0) % 16) == 0 && (reinterpret_cast<uintptr_t>(a.data_ptr()) % 16) == 0,
               "mxfp4_gemm_fin: e4m3 activation rows, 16-byte aligned");
   const int M = a.size(0), K = a.size(1), N = wp.size(0);
-  const int Kw = (int)wp.size(1) * 2;
+  const int Kw = weight_fmt(wp.size(1), K).Kw;
   TORCH_CHECK(M >= 1 && M <= 16, "mxfp4_gemm_fin: 1..16 rows");
-  TORCH_CHECK(K % 32 == 0 && Kw % BK == 0 && Kw >= K && Kw - K < BK, "mxfp4_gemm_fin: K");
+  TORCH_CHECK(K % 32 == 0, "mxfp4_gemm_fin: K");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(wp.data_ptr()) % 32) == 0 && (wp.stride(0) % 32) == 0,
               "mxfp4_gemm_fin: weight rows 32-byte aligned");
   TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.stride(1) == 1 && out.size(0) >= M &&
@@ -826,10 +861,10 @@ void mxfp4_gemm_act(int64_t mode, torch::Tensor x, torch::Tensor res, torch::Ten
   const int M = x.size(0);
   const int K = mode == 2 ? (int)x.size(1) / 2 : (int)x.size(1);
   const int N = wp.size(0);
-  const int Kw = (int)wp.size(1) * 2;
+  const int Kw = weight_fmt(wp.size(1), K).Kw;
   TORCH_CHECK(M == 1, "mxfp4_gemm_act: one activation row");
   TORCH_CHECK(K <= kActMaxChunks * 1024, "mxfp4_gemm_act: K <= 9216");
-  TORCH_CHECK(K % 16 == 0 && Kw % BK == 0 && Kw >= K && Kw - K < BK, "mxfp4_gemm_act: K");
+  TORCH_CHECK(K % 16 == 0, "mxfp4_gemm_act: K");
   TORCH_CHECK(x.stride(0) % 8 == 0 && (reinterpret_cast<uintptr_t>(x.data_ptr()) % 16) == 0,
               "mxfp4_gemm_act: x rows 16-byte aligned");
   const bool has_res = res.defined() && res.numel();

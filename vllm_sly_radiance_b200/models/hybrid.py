@@ -337,6 +337,12 @@ class HybridModel:
                  tp: Optional[TPInfo] = None, init_device=None, weights=None,
                  lm_head_quant: Optional[str] = None, tp_pad: Optional[int] = None,
                  ep=None, embed_quant: Optional[str] = None):
+        # MXFP6 / MXFP8 run the MXFP4 code path with another element type in the weights: every
+        # linear arrives from the weight source already in that type
+        from .weights import MX_QUANTS, MXCastWeights
+        self.mx_fmt = MX_QUANTS.get(quant)
+        if quant in ("mxfp6", "mxfp8"):
+            quant = "mxfp4"
         self.quant = quant
         self.device = torch.device(device)
         self.tp = tp or TPInfo()
@@ -349,6 +355,8 @@ class HybridModel:
         if pcfg != cfg:
             W = PaddedWeights(W, cfg, pcfg)
             cfg = pcfg
+        if self.mx_fmt not in (None, "e2m1"):
+            W = MXCastWeights(W, self.mx_fmt, skip=("lm_head",) if lm_head_quant else ())
         self.cfg = cfg
         H, V = cfg.hidden_size, cfg.vocab_size
         self.embed = W.tensor("embed", (V, H), "embed").to(torch.bfloat16)
@@ -361,6 +369,8 @@ class HybridModel:
         self.final_norm = W.tensor("final_norm", (H,), "norm")
         # vocab-parallel lm_head
         w = W.linear("lm_head", V, H) if not cfg.tie_word_embeddings else self.embed.float()
+        if self.mx_fmt not in (None, "e2m1") and not lm_head_quant and isinstance(w, torch.Tensor):
+            w = MXFP4Weight.from_float(w.float(), self.mx_fmt)
         s0, per = self.tp.shard(V)
         self.vocab_start = s0
         # lm_head format: the model's by default; "int4" = W4A16 g128 with MSE clip search (the

@@ -38,12 +38,14 @@ FUSE_MAX_K = 9216
 
 import os as _os
 
-# decode batches (<= 16 rows): the GEMM's last CTA produces the next linear's e4m3 rows in the
-# same launch (RADIANCE_FINISH=0 switches it off).  RADIANCE_GEMV=1 selects the persistent
-# stream-K decode GEMM (one CTA per SM) instead of the split-K cluster GEMM: it measured slower
-# (fewer weight bytes in flight per SM), so it is opt-in.
+# decode batches (<= 16 rows): RADIANCE_FINISH=1 lets the GEMM's last CTA produce the next
+# linear's e4m3 rows in the same launch.  Opt-in: on the 27B decode step it measured 198 against
+# 227 tok/s, since one CTA finishing a whole row (5-9 us) sits serially at each GEMM's tail where
+# the stand-alone producer overlapped under programmatic dependent launch.  RADIANCE_GEMV=1
+# selects the persistent stream-K decode GEMM (one CTA per SM) instead of the split-K cluster
+# GEMM: it measured slower (fewer weight bytes in flight per SM), so it is opt-in too.
 GEMV_ON = _os.environ.get("RADIANCE_GEMV", "0") == "1"
-FINISH_ON = _os.environ.get("RADIANCE_FINISH", "1") != "0"
+FINISH_ON = _os.environ.get("RADIANCE_FINISH", "0") == "1"
 
 
 def rope_cache(max_pos: int, rotary_dim: int, theta: float, device) -> torch.Tensor:
@@ -54,15 +56,18 @@ def rope_cache(max_pos: int, rotary_dim: int, theta: float, device) -> torch.Ten
 
 
 class Linear:
-    """y = x W^T with W [N, K] stored as MXFP4 (W4A8 path), bf16, or per-channel fp8 (the
-    cuBLAS baseline build)."""
+    """y = x W^T with W [N, K] stored as an MX block-scaled type (MXFP4 / MXFP6 / MXFP8 weights
+    with e4m3 activations), bf16, or per-channel fp8 (the cuBLAS baseline build)."""
 
     def __init__(self, weight: torch.Tensor, quant: str = "mxfp4", name: str = ""):
         self.name = name
         self.quant = quant
         self.N, self.K = weight.shape
-        if quant == "mxfp4":
-            self.w = MXFP4Weight.from_float(weight)
+        if quant in ("mxfp4", "mxfp6", "mxfp8"):
+            # one code path for the three block-scaled element types (e2m1 / e2m3 / e4m3)
+            self.w = MXFP4Weight.from_float(weight, {"mxfp4": "e2m1", "mxfp6": "e2m3",
+                                                     "mxfp8": "e4m3"}[quant])
+            self.quant = "mxfp4"
         elif quant == "bf16":
             self.w = weight.to(torch.bfloat16).contiguous()
         elif quant == "int4":
@@ -150,12 +155,12 @@ class Linear:
         q, s = x
         if mode == K.FIN_NORM:
             res_new = torch.empty(q.shape[0], self.N, dtype=torch.bfloat16, device=q.device)
-            if GEMV_ON:
+            if GEMV_ON and self.w.fmt == "e2m1":
                 _, fq, fs = K.mxfp4_gemv(q, s, self.w, None, K.FIN_NORM, res, norm_w, res_new, eps)
             else:
                 _, fq, fs = K.mxfp4_gemm_finish(q, s, self.w, K.FIN_NORM, res, norm_w, res_new, eps)
             return fq, fs, res_new
-        if GEMV_ON:
+        if GEMV_ON and self.w.fmt == "e2m1":
             _, fq, fs = K.mxfp4_gemv(q, s, self.w, None, K.FIN_SILU)
         else:
             _, fq, fs = K.mxfp4_gemm_finish(q, s, self.w, K.FIN_SILU)
@@ -172,9 +177,10 @@ class Linear:
             if self.push is not None and out is None and q.is_cuda and \
                     self.push.can_push(q.shape[0], self.N):
                 return self.push.gemm_push(q, s, self.w)
-            if GEMV_ON and q.is_cuda and 0 < q.shape[0] <= K.GEMV_MAX_ROWS:
+            if GEMV_ON and self.w.fmt == "e2m1" and q.is_cuda and 0 < q.shape[0] <= K.GEMV_MAX_ROWS:
                 return K.mxfp4_gemv(q, s, self.w, out)
-            return K.mxfp4_gemm(q, s, self.w.packed, self.w.sf, self.w.scales, self.N, out=out)
+            return K.mxfp4_gemm(q, s, self.w.packed, self.w.sf, self.w.scales, self.N, out=out,
+                                fmt=self.w.fmt)
         if self.quant == "fp8":
             if isinstance(x, tuple):
                 q, s = x

@@ -133,10 +133,10 @@ class MoEBlock:
                 gsl = slice(e * 2 * self.I, (e + 1) * 2 * self.I)
                 dsl = slice(e * self.H, (e + 1) * self.H)
                 gu = K.mxfp4_gemm(q[idx], s[idx], self.w_gate_up.packed[gsl], None,
-                                  self.w_gate_up.scales[gsl], 2 * self.I)
+                                  self.w_gate_up.scales[gsl], 2 * self.I, fmt=self.w_gate_up.fmt)
                 a = K.silu_mul_quant(gu)
                 y[idx] = K.mxfp4_gemm(a[0], a[1], self.w_down.packed[dsl], None,
-                                      self.w_down.scales[dsl], self.H)
+                                      self.w_down.scales[dsl], self.H, fmt=self.w_down.fmt)
             else:
                 gu = xb[idx].float() @ self.dense_gu[e].float().t()
                 a = K.silu_mul(gu.to(torch.bfloat16)).float()
@@ -185,10 +185,10 @@ class MoEBlock:
                 gsl = slice(e * 2 * self.I, (e + 1) * 2 * self.I)
                 dsl = slice(e * self.H, (e + 1) * self.H)
                 gu = K.mxfp4_gemm(qq, ss, self.w_gate_up.packed[gsl], None,
-                                  self.w_gate_up.scales[gsl], 2 * self.I)
+                                  self.w_gate_up.scales[gsl], 2 * self.I, fmt=self.w_gate_up.fmt)
                 a = K.silu_mul_quant(gu)
                 y[r0:r0 + c] = K.mxfp4_gemm(a[0], a[1], self.w_down.packed[dsl], None,
-                                            self.w_down.scales[dsl], self.H).float()
+                                            self.w_down.scales[dsl], self.H, fmt=self.w_down.fmt).float()
             else:
                 gu = rows.float() @ self.dense_gu[e].float().t()
                 a = K.silu_mul(gu.to(torch.bfloat16)).float()

@@ -71,6 +71,37 @@ class RandomWeights:
         return True
 
 
+# quantization names of the block-scaled (tcgen05 kind::mxf8f6f4) weight formats
+MX_QUANTS = {"mxfp4": "e2m1", "mxfp6": "e2m3", "mxfp8": "e4m3"}
+
+
+class MXCastWeights:
+    """Weight source that returns every linear in one MX element type: float linears are
+    quantised to it, MX linears of another type are re-quantised (an MXFP4 checkpoint served as
+    MXFP8 keeps its values: e2m1 x 2^s is exact in e4m3 x 2^s').  ``skip`` names linears left as
+    they are (an lm_head with its own format)."""
+
+    def __init__(self, inner, fmt: str, skip=()):
+        self.inner, self.fmt, self.skip = inner, fmt, set(skip)
+        self.cfg = inner.cfg
+        self.device = getattr(inner, "device", None)
+
+    def linear(self, name: str, N: int, K: int) -> WeightT:
+        w = self.inner.linear(name, N, K)
+        if name in self.skip or K % 32:
+            return w
+        if isinstance(w, MXFP4Weight):
+            if w.fmt == self.fmt:
+                return w
+            w = w.dequantize()
+        elif not isinstance(w, torch.Tensor):
+            return w                                   # other packed formats (int4) as stored
+        return MXFP4Weight.from_float(w.float(), self.fmt)
+
+    def __getattr__(self, item):
+        return getattr(self.inner, item)
+
+
 def _is_q(w) -> bool:
     from ..quant.int4 import Int4Weight
     return isinstance(w, (MXFP4Weight, Int4Weight))
@@ -100,7 +131,7 @@ def pad_rows(w: WeightT, multiple: int) -> WeightT:
         z = Int4Weight.from_float(torch.zeros(pad, w.K))
         return cat_rows([w, z])
     if isinstance(w, MXFP4Weight):
-        z = MXFP4Weight.from_float(torch.zeros(pad, w.K, dtype=torch.float32, device=w.packed.device))
+        z = MXFP4Weight.zeros(pad, w.K, w.fmt, w.packed.device)
         return cat_rows([w, z])
     return torch.cat([w, torch.zeros(pad, w.shape[1], dtype=w.dtype, device=w.device)], 0)
 

@@ -220,9 +220,11 @@ def quant_fp8(x: torch.Tensor):
 # ---------------------------------------------------------------------------------------------
 def mxfp4_gemm(q: torch.Tensor, scale: torch.Tensor, packed: torch.Tensor, sf: torch.Tensor,
                scales_plain: torch.Tensor, N: int, out: Optional[torch.Tensor] = None,
-               splits: int = 0) -> torch.Tensor:
+               splits: int = 0, fmt: str = "e2m1") -> torch.Tensor:
+    """Block-scaled W(4|6|8)A8 GEMM; the CUDA kernel reads the weight type from the packed row
+    width, fmt names it for the CPU path."""
     if not q.is_cuda:
-        return ref.mxfp4_linear(q, scale, packed, scales_plain)
+        return ref.mxfp4_linear(q, scale, packed, scales_plain, fmt=fmt)
     M = q.shape[0]
     if out is None:
         out = torch.empty(M, N, dtype=torch.bfloat16, device=q.device)

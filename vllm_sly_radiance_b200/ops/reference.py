@@ -15,7 +15,7 @@ import torch
 import torch.nn.functional as F
 
 from ..quant.formats import (FP8_MAX, FP8_SCALE_FLOOR, fp8_e4m3, kv4_dequantize, kv4_quantize,
-                             mxfp4_dequantize, per_token_fp8)
+                             mx_dequantize, per_token_fp8)
 
 
 # ---------------------------------------------------------------------------------------------
@@ -90,9 +90,11 @@ def gate_mul_quant(attn_out, gate):
 # linears
 # ---------------------------------------------------------------------------------------------
 def mxfp4_linear(q: torch.Tensor, scale: torch.Tensor, w_packed: torch.Tensor,
-                 w_scales: torch.Tensor, bias: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """C[M,N] = a_scale[m] * sum_k e4m3(q[m,k]) * e2m1(w[n,k]) * 2^(ws[n,k/32]-127), fp32 accumulate."""
-    w = mxfp4_dequantize(w_packed, w_scales)                    # [N, Kp] fp32 exact
+                 w_scales: torch.Tensor, bias: Optional[torch.Tensor] = None,
+                 fmt: str = "e2m1") -> torch.Tensor:
+    """C[M,N] = a_scale[m] * sum_k e4m3(q[m,k]) * w(w[n,k]) * 2^(ws[n,k/32]-127), fp32
+    accumulate; w = e2m1 (MXFP4), e2m3 (MXFP6) or e4m3 (MXFP8) codes."""
+    w = mx_dequantize(w_packed, w_scales, fmt)                  # [N, Kp] fp32 exact
     w = w[:, :q.shape[1]]                                       # zero-padded K tail
     c = (q.float() @ w.t()) * scale.float().unsqueeze(-1)
     if bias is not None:

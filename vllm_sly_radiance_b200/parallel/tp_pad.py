@@ -79,9 +79,7 @@ def padded_config(cfg: ModelConfig, tp: int) -> ModelConfig:
 
 def _zero_rows(like: WeightT, n: int, K: int) -> WeightT:
     if isinstance(like, MXFP4Weight):
-        dev = like.packed.device
-        return MXFP4Weight.from_packed(torch.zeros(n, K // 2, dtype=torch.uint8, device=dev),
-                                       torch.full((n, K // 32), 127, dtype=torch.uint8, device=dev))
+        return MXFP4Weight.zeros(n, K, like.fmt, like.packed.device)
     return torch.zeros(n, K, dtype=like.dtype, device=like.device)
 
 
@@ -101,16 +99,7 @@ def _pad_cols(w: WeightT, K_new: int) -> WeightT:
     """Zero input features appended (dummy heads / channels of a row-parallel linear).  The MXFP4
     scale of a zero block is 2^0 (any finite scale gives zero; 0xFF would be NaN)."""
     if isinstance(w, MXFP4Weight):
-        K = w.K
-        if K_new == K:
-            return w
-        assert (K_new - K) % 32 == 0
-        dev = w.packed.device
-        pk = torch.cat([w.packed[:, :K // 2],
-                        torch.zeros(w.N, (K_new - K) // 2, dtype=torch.uint8, device=dev)], 1)
-        sc = torch.cat([w.scales[:, :K // 32],
-                        torch.full((w.N, (K_new - K) // 32), 127, dtype=torch.uint8, device=dev)], 1)
-        return MXFP4Weight.from_packed(pk, sc, K_new)
+        return w.pad_cols(K_new)
     if K_new == w.shape[1]:
         return w
     return torch.cat([w, torch.zeros(w.shape[0], K_new - w.shape[1], dtype=w.dtype,

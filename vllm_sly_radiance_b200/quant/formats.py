@@ -94,6 +94,103 @@ def mxfp4_dequantize(packed: torch.Tensor, scales: torch.Tensor) -> torch.Tensor
 
 
 # ---------------------------------------------------------------------------------------------
+# MXFP6 (E2M3) and MXFP8 (E4M3) weights: the other element types of tcgen05 kind::mxf8f6f4
+# ---------------------------------------------------------------------------------------------
+# E2M3: sign bit 5, 2 exponent bits (bias 1), 3 mantissa bits; magnitudes k/8 for k < 8, then
+# (8 + m)/8 * 2^(e-1): 1 .. 7.5.  OCP shared scale: floor(log2 amax) - 2 (emax 2), as E2M1.
+E2M3_VALUES = torch.tensor([i / 8 for i in range(8)] + [(8 + m) / 8 * 2.0 ** (e - 1)
+                                                        for e in (1, 2, 3) for m in range(8)])
+
+
+def e2m3_encode(x: torch.Tensor) -> torch.Tensor:
+    """float -> 6-bit code (uint8 0..63), round to nearest on the E2M3 grid (ties to the even
+    code), saturating at 7.5."""
+    a = x.abs().float().clamp(max=7.5)
+    mags = E2M3_VALUES.to(x.device)
+    mids = (mags[:-1] + mags[1:]) / 2
+    lower = torch.bucketize(a, mids, right=False)
+    tie = (a.unsqueeze(-1) == mids).any(-1)
+    idx = torch.where(tie & (lower % 2 == 1), lower + 1, lower).clamp(max=31).to(torch.uint8)
+    sign = (x < 0) & (idx > 0)
+    return idx | (sign.to(torch.uint8) << 5)
+
+
+def e2m3_decode(code: torch.Tensor) -> torch.Tensor:
+    c = code.long()
+    mag = E2M3_VALUES.to(code.device)[c & 31]
+    return torch.where((c & 32) != 0, -mag, mag)
+
+
+def pack_6bit(codes: torch.Tensor) -> torch.Tensor:
+    """[..., K] 6-bit codes (K % 4 == 0) -> [..., 3K/4] bytes: four codes per three bytes, code i
+    of a group at bits [6i, 6i + 6) of the little-endian 24-bit word (the reference's MXFP6
+    checkpoint packing, and 16 codes per 12 bytes as TMA's 16U6 type reads them)."""
+    c = codes.to(torch.int32).view(*codes.shape[:-1], -1, 4)
+    w = c[..., 0] | (c[..., 1] << 6) | (c[..., 2] << 12) | (c[..., 3] << 18)
+    b = torch.stack([w & 255, (w >> 8) & 255, (w >> 16) & 255], -1)
+    return b.to(torch.uint8).view(*codes.shape[:-1], -1)
+
+
+def unpack_6bit(packed: torch.Tensor) -> torch.Tensor:
+    t = packed.to(torch.int32).view(*packed.shape[:-1], -1, 3)
+    w = t[..., 0] | (t[..., 1] << 8) | (t[..., 2] << 16)
+    return torch.stack([(w >> (6 * i)) & 63 for i in range(4)], -1).view(
+        *packed.shape[:-1], -1).to(torch.uint8)
+
+
+def ue8m0_for(amax: torch.Tensor, emax: int) -> torch.Tensor:
+    """OCP shared-scale byte: floor(log2 amax) - emax of the element type, biased by 127."""
+    a = amax.double()
+    _, e = torch.frexp(a)
+    s = (e.long() - 1 - emax + 127).clamp(0, 254)
+    return torch.where(a == 0, torch.zeros_like(s), s).to(torch.uint8)
+
+
+def ue8m0_ceil(amax: torch.Tensor, vmax: float) -> torch.Tensor:
+    """Smallest power-of-two scale with amax / scale <= vmax (no element saturates), biased."""
+    x = amax.double() / vmax
+    m, e = torch.frexp(x)                       # x = m * 2^e, m in [0.5, 1)
+    s = (e.long() - (m == 0.5).long() + 127).clamp(0, 254)
+    return torch.where(amax == 0, torch.zeros_like(s), s).to(torch.uint8)
+
+
+def mx_quantize(w: torch.Tensor, fmt: str):
+    """w [N, K] -> (packed, UE8M0 scales [N, K/32]) for fmt e2m1 (MXFP4, [N, K/2]), e2m3 (MXFP6,
+    [N, 3K/4]) or e4m3 (MXFP8, [N, K] bytes).  e2m1 / e2m3 take the OCP scale floor(log2 amax) -
+    emax (the block maximum may round down to the largest code); e4m3 takes the smallest scale
+    that does not saturate, since the OCP rule would clip up to 12 % off a block's largest
+    values there (amax / scale reaches 511 against a largest code of 448)."""
+    if fmt == "e2m1":
+        return mxfp4_quantize(w)
+    N, K = w.shape
+    assert K % MX_BLOCK == 0, K
+    wb = w.float().view(N, K // MX_BLOCK, MX_BLOCK)
+    amax = wb.abs().amax(-1)
+    sb = ue8m0_for(amax, 2) if fmt == "e2m3" else ue8m0_ceil(amax, 448.0)
+    x = (wb / ue8m0_to_float(sb).unsqueeze(-1)).view(N, K)
+    if fmt == "e2m3":
+        return pack_6bit(e2m3_encode(x)), sb
+    if fmt == "e4m3":
+        return fp8_e4m3(x).view(torch.uint8), sb
+    raise ValueError(fmt)
+
+
+def mx_dequantize(packed: torch.Tensor, scales: torch.Tensor, fmt: str) -> torch.Tensor:
+    if fmt == "e2m1":
+        return mxfp4_dequantize(packed, scales)
+    N = packed.shape[0]
+    if fmt == "e2m3":
+        vals = e2m3_decode(unpack_6bit(packed))
+    else:
+        vals = packed.view(torch.float8_e4m3fn).float()
+    K = vals.shape[1]
+    return (vals.view(N, K // MX_BLOCK, MX_BLOCK) * ue8m0_to_float(scales).unsqueeze(-1)).view(N, K)
+
+
+MX_BITS = {"e2m1": 4, "e2m3": 6, "e4m3": 8}
+
+
+# ---------------------------------------------------------------------------------------------
 # fp8 e4m3 per-token activations
 # ---------------------------------------------------------------------------------------------
 def fp8_e4m3(x: torch.Tensor) -> torch.Tensor:

@@ -4,6 +4,19 @@ Supported per-linear formats (auto-detected from the tensor names next to each w
   * bf16 / fp16 / fp32                 ``{p}.weight``                      -> quantized at load
   * MXFP4, compressed-tensors          ``{p}.weight_packed`` u8 [N,K/2] + ``{p}.weight_scale`` u8 [N,K/32]
   * MXFP4, Quark                       ``{p}.weight`` u8 [N,K/2] + ``{p}.weight_scale`` u8 [N,K/32]
+  * MXFP6 (E2M3)                      ``weight_packed`` u8 [N,3K/4] (four 6-bit codes per three
+                                       bytes, code i at bits 6i of the little-endian 24-bit word)
+                                       + ``weight_scale`` u8 [N,K/32] -> MXFP6 as stored
+  * BCQ4 (block-clustered tables)      ``weight_packed`` u8 [N,K/2] + ``weight_scale`` u8 table ids
+                                       [N,K/32] + ``weight_row_exp`` u8 [N], with a [256, 8] table
+                                       file (``bcq_tables.pt``): w = sign * T[id][mag] *
+                                       2^(row_exp - 127) -> MXFP8 exactly (each table entry is an
+                                       e4m3 value, the row exponent is the block scale); with a
+                                       Hadamard-128 checkpoint (weights stored as W R) the rotation
+                                       is undone at load (W = W' R^T) and W requantised to MXFP8
+  * fp8 block W8A8                     ``weight`` e4m3 [N,K] + ``weight_scale_inv`` fp32
+                                       [N/128,K/128] -> dequantised (served as MXFP8 with
+                                       ``quantization=mxfp8``)
   * NVFP4 (compressed-tensors/modelopt) ``weight_packed`` + e4m3 ``weight_scale`` [N,K/16] +
                                        ``weight_global_scale`` (divisor) or ``weight_scale_2``
                                        (multiplier) -> requantized to MXFP4 (``radiance_nvfp4.py``
@@ -36,8 +49,44 @@ from typing import Optional
 import torch
 
 from ..config import ModelConfig
-from .formats import (int4_g128_dequantize, mxfp4_quantize, nvfp4_to_mxfp4, unpack_nibbles)
+from .formats import (MX_BITS, int4_g128_dequantize, mxfp4_quantize, nvfp4_to_mxfp4,
+                      unpack_nibbles)
 from .mxfp4 import MXFP4Weight
+
+
+def hadamard_rotation(n: int = 128) -> torch.Tensor:
+    """R = H_n diag(s) / sqrt(n): Sylvester Hadamard matrix with column signs s drawn as
+    ``torch.rand(n) < 0.5 -> -1`` from a seed-0 generator -- the rotation the reference's
+    Hadamard-128 checkpoints were written with (``sly/mxfp4/radiance_mxfp4.py:254-272``).
+    Orthogonal: R R^T = I."""
+    g = torch.Generator().manual_seed(0)
+    sgn = torch.where(torch.rand(n, generator=g, dtype=torch.float32) < 0.5, -1.0, 1.0)
+    H = torch.ones(1, 1)
+    while H.shape[0] < n:
+        H = torch.cat([torch.cat([H, H], 1), torch.cat([H, -H], 1)])
+    return H * (sgn / n ** 0.5)
+
+
+def bcq_dequantize(packed: torch.Tensor, ids: torch.Tensor, row_exp: torch.Tensor,
+                   table: torch.Tensor) -> torch.Tensor:
+    """BCQ4 -> fp32 [N, K]: w = sign * T[id[n, k/32]][code & 7] * 2^(row_exp[n] - 127), code =
+    nibble (low nibble = even k), sign = code bit 3 (``ci/check_bcq_all_paths.py:52-58``)."""
+    nib = unpack_nibbles(packed).long()
+    t = ids.long().repeat_interleave(32, 1)
+    mag = table.float()[t, nib & 7]
+    return torch.where(nib >= 8, -mag, mag) * torch.exp2(row_exp.float() - 127.0)[:, None]
+
+
+def bcq_to_mxfp8(packed: torch.Tensor, ids: torch.Tensor, row_exp: torch.Tensor,
+                 table: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """BCQ4 -> MXFP8 (e4m3 codes [N, K], UE8M0 scales [N, K/32]) with no rounding: each element
+    is a table entry (e4m3-exact) and the block scale is the row's exponent."""
+    nib = unpack_nibbles(packed).long()
+    t = ids.long().repeat_interleave(32, 1)
+    tb = table.float().to(torch.float8_e4m3fn).view(torch.uint8)
+    code = tb[t, nib & 7] | ((nib >= 8) & (tb[t, nib & 7] != 0)).to(torch.uint8) << 7
+    scales = row_exp.to(torch.uint8)[:, None].expand(-1, ids.shape[1]).contiguous()
+    return code.contiguous(), scales
 
 
 class CheckpointWeights:
@@ -62,6 +111,20 @@ class CheckpointWeights:
         qc = os.path.join(path, "config.json")
         self.hf_config = json.load(open(qc)) if os.path.exists(qc) else {}
         qcfg = self.hf_config.get("quantization_config", {}) or {}
+        # BCQ4 tables ([256, 8] e4m3-exact magnitudes) and the Hadamard-128 flag
+        self.bcq_table = None
+        for tf in ("bcq_tables.pt", "mcb_tables.pt"):
+            if os.path.exists(os.path.join(path, tf)):
+                t = torch.load(os.path.join(path, tf), map_location="cpu").float()
+                if tuple(t.shape) != (256, 8) or bool((t < 0).any()) or not torch.equal(
+                        t.to(torch.float8_e4m3fn).float(), t):
+                    raise ValueError(f"{tf}: want [256, 8] e4m3-exact magnitudes")
+                self.bcq_table = t
+                break
+        self.hadamard = int(qcfg.get("hadamard", qcfg.get("radiance_hadamard", 0)) or 0)
+        if self.hadamard not in (0, 128):
+            raise ValueError(f"hadamard block {self.hadamard}: 0 or 128")
+        self.fp8_block = tuple(qcfg.get("weight_block_size", (128, 128)) or (128, 128))
         fmt = str(qcfg.get("checkpoint_format", qcfg.get("packing_format", ""))).lower()
         if fmt in ("gptq_v2", "auto_round", "auto_round:gptq_v2") or \
                 str(qcfg.get("quant_method", "")).lower() == "auto-round" and "v1" not in fmt:
@@ -131,8 +194,24 @@ class CheckpointWeights:
                                       zp.to(torch.uint8).contiguous(), N, K)
                 w = int4_g128_dequantize(b, scale.float(), zp.to(torch.uint8), g)
                 return w
-            if scale.dtype == torch.uint8:                      # MXFP4 (UE8M0 per 32)
-                return MXFP4Weight.from_packed(packed.contiguous(), scale.contiguous())
+            if scale.dtype == torch.uint8 and self.has(p + ".weight_row_exp"):    # BCQ4
+                if self.bcq_table is None:
+                    raise ValueError(f"{p}: BCQ4 weights need bcq_tables.pt next to the checkpoint")
+                row_exp = self.raw(p + ".weight_row_exp").view(-1)
+                if self.hadamard:
+                    w = bcq_dequantize(packed, scale, row_exp, self.bcq_table)
+                    N, K = w.shape
+                    R = hadamard_rotation(self.hadamard)
+                    w = (w.view(N, K // self.hadamard, self.hadamard) @ R.t()).view(N, K)
+                    return MXFP4Weight.from_float(w, "e4m3")
+                code, sc = bcq_to_mxfp8(packed, scale, row_exp, self.bcq_table)
+                return MXFP4Weight.from_packed(code, sc, fmt="e4m3")
+            if scale.dtype == torch.uint8:                      # MXFP4 / MXFP6 (UE8M0 per 32)
+                K = scale.shape[1] * 32
+                fmt = {K // 2: "e2m1", 3 * K // 4: "e2m3", K: "e4m3"}.get(packed.shape[1])
+                if fmt is None:
+                    raise ValueError(f"{p}: packed width {packed.shape[1]} is no MX type of K={K}")
+                return MXFP4Weight.from_packed(packed.contiguous(), scale.contiguous(), fmt=fmt)
             if scale.dtype == torch.float8_e4m3fn:             # NVFP4
                 if self.has(p + ".weight_global_scale"):
                     gs = 1.0 / self.raw(p + ".weight_global_scale").float()
@@ -143,7 +222,20 @@ class CheckpointWeights:
                 mp, ms = nvfp4_to_mxfp4(packed.contiguous(), scale, gs.reshape(()))
                 return MXFP4Weight.from_packed(mp, ms)
             raise ValueError(f"unsupported quantized format for {p}: scale dtype {scale.dtype}")
-        return self.raw(p + ".weight").float()
+        w = self.raw(p + ".weight")
+        if w.dtype == torch.float8_e4m3fn and self.has(p + ".weight_scale") and \
+                self.raw(p + ".weight_scale").dtype == torch.uint8:
+            # MXFP8: e4m3 elements with UE8M0 per-32 scales, served as stored
+            return MXFP4Weight.from_packed(w.view(torch.uint8).contiguous(),
+                                           self.raw(p + ".weight_scale").contiguous(), fmt="e4m3")
+        if w.dtype == torch.float8_e4m3fn and self.has(p + ".weight_scale_inv"):
+            # fp8 block W8A8: one fp32 scale per (bn x bk) block
+            si = self.raw(p + ".weight_scale_inv").float()
+            bn, bk = self.fp8_block
+            N, K = w.shape
+            s = si.repeat_interleave(bn, 0)[:N].repeat_interleave(bk, 1)[:, :K]
+            return w.float() * s
+        return w.float()
 
     # ---- provider interface ----
     def linear(self, name: str, N: int, K: int):
@@ -211,8 +303,13 @@ class CheckpointWeights:
 
 def _cat(ws):
     from .int4 import Int4Weight
-    if isinstance(ws[0], MXFP4Weight):
+    if any(isinstance(w, MXFP4Weight) for w in ws):
         from .mxfp4 import cat_rows
+        # parts stored in different MX types (or one left in float) meet in the widest type
+        fmt = max((w.fmt for w in ws if isinstance(w, MXFP4Weight)), key=lambda f: MX_BITS[f])
+        ws = [w if isinstance(w, MXFP4Weight) and w.fmt == fmt else
+              MXFP4Weight.from_float(w.dequantize() if isinstance(w, MXFP4Weight) else w.float(), fmt)
+              for w in ws]
         return cat_rows(ws)
     if isinstance(ws[0], Int4Weight):
         from .int4 import cat_rows as ci
@@ -225,7 +322,7 @@ def _cat(ws):
 def _rows(w, idx: torch.Tensor):
     from .int4 import Int4Weight
     if isinstance(w, MXFP4Weight):
-        return MXFP4Weight.from_packed(w.packed[idx], w.scales[idx])
+        return MXFP4Weight.from_packed(w.packed[idx], w.scales[idx], w.K, w.fmt)
     if isinstance(w, Int4Weight):
         return w.index_rows(idx)
     return w[idx]
@@ -263,9 +360,9 @@ def _merge_gdn_in_proj(qkvz, ba, cfg: ModelConfig):
             not isinstance(qkvz, Int4Weight):
         # ba is often left unquantized in MXFP4 checkpoints: quantize it to match
         if isinstance(qkvz, MXFP4Weight):
-            ba = MXFP4Weight.from_float(ba)
+            ba = MXFP4Weight.from_float(ba, qkvz.fmt)
         else:
-            qkvz = MXFP4Weight.from_float(qkvz)
+            qkvz = MXFP4Weight.from_float(qkvz, ba.fmt)
     return _cat([_rows(qkvz, pq), _rows(ba, pb)])
 
 
