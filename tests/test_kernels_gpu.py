@@ -421,12 +421,18 @@ def test_paged_attention_decode_gated(Hq, Hkv, ctx_lens, splits):
         assert torch.equal(gq.view(torch.uint8), wq.view(torch.uint8)), rep
 
 
+@pytest.mark.parametrize("two_phase", [False, True])
 @pytest.mark.parametrize("lens,has_init,sdt,split", [
     ([1500], [0], torch.float32, 0), ([64, 1, 200, 7], [1, 1, 0, 1], torch.float32, 1),
-    ([130, 65], [1, 0], torch.bfloat16, 2), ([300], [1], torch.float32, 4)])
-def test_gdn_chunked_matches_recurrent(lens, has_init, sdt, split, monkeypatch):
-    """The 64-token chunk-scan kernel (tensor cores, bf16 operands, fp32 state) against the fp32
-    token-serial oracle and against the token-serial CUDA kernel: outputs and final states."""
+    ([130, 65], [1, 0], torch.bfloat16, 2), ([300], [1], torch.float32, 4),
+    ([4096], [1], torch.float32, 8), ([63, 129, 640], [0, 1, 1], torch.bfloat16, 0)])
+def test_gdn_chunked_matches_recurrent(lens, has_init, sdt, split, two_phase, monkeypatch):
+    """The 64-token chunk-scan kernels (tensor cores, bf16 operands, fp32 state; one kernel, or
+    the chunk-parallel solve followed by the state scan) against the fp32 token-serial oracle and
+    against the token-serial CUDA kernel: outputs and final states."""
+    if (split == 8 and not two_phase) or (split == 1 and two_phase):
+        pytest.skip("split not offered by this form")
+    monkeypatch.setattr(K, "_GDN_TWO_PHASE", two_phase)
     torch.manual_seed(7)
     Hk, Hv, D = 4, 12, 128
     key_dim, vdim = Hk * D, Hv * D

@@ -4,6 +4,7 @@ set larger than the 126 MB L2).  Usage:
     python -m vllm_sly_radiance_b200.benchmarks.kernels gemm [--m 1,8,64,4096]
     python -m vllm_sly_radiance_b200.benchmarks.kernels attn [--ctx 1500,4096 --splits 1,17]
     python -m vllm_sly_radiance_b200.benchmarks.kernels w4a16 [--m 1,8 --shape lm_head,62080x5120]
+    python -m vllm_sly_radiance_b200.benchmarks.kernels gdn_prefill [--ctx 1500,4096]
 
 Prints one JSON line per case with time, achieved bandwidth / FLOP rate and the fraction of the
 measured peaks in MEASURED_PEAKS.json (fallback 6.65 TB/s, 1.59 PFLOP/s).  The W4A8 GEMMs run
@@ -278,6 +279,38 @@ def bench_gdn_decode(batches):
                               "frac_hbm": round(byts / t / bw, 3), "peaks": src}), flush=True)
 
 
+def bench_gdn_prefill(lens, head_counts):
+    """Prefill chunk scan of one GDN layer (dk = dv = 128, fp32 state, one sequence): the
+    one-kernel form against the two-phase form (chunk-parallel solve + state scan), at the
+    per-rank head counts of TP 1 / 2 / 4 / 8 (48 / 24 / 12 / 6 value heads, ratio 3)."""
+    for Hv in head_counts:
+        Hk = max(1, Hv // 3)
+        D = 128
+        for L in lens:
+            y = (torch.randn(L, 2 * Hk * D + Hv * D, device="cuda") * 0.1).to(torch.bfloat16)
+            ba = torch.randn(L, 2 * Hv, device="cuda").to(torch.bfloat16)
+            A_log = torch.zeros(Hv, device="cuda")
+            dt = torch.zeros(Hv, device="cuda")
+            st = torch.zeros(2, Hv, D, D, device="cuda")
+            m = _AttnMeta()
+            m.query_start_loc = torch.tensor([0, L], dtype=torch.int32, device="cuda")
+            m.state_slots = torch.tensor([1], dtype=torch.int32, device="cuda")
+            m.has_initial = torch.zeros(1, dtype=torch.int32, device="cuda")
+            m.num_seqs, m.num_tokens = 1, L
+            m.commit_len = None
+            out = {}
+            for form in (False, True):
+                K._GDN_TWO_PHASE = form
+                out[form] = timeit(lambda i: K.gdn_recurrent(y, ba, A_log, dt, st, m, Hk, D ** -0.5))
+            K._GDN_TWO_PHASE = True
+            flops = 2 * L * Hv * D * D * 6          # ~6 [token x D x D] products per token
+            print(json.dumps({"kernel": "gdn_chunk_prefill", "L": L, "Hv": Hv,
+                              "one_kernel_us": round(out[False] * 1e6, 1),
+                              "two_phase_us": round(out[True] * 1e6, 1),
+                              "speedup": round(out[False] / out[True], 2),
+                              "two_phase_tflops": round(flops / out[True] / 1e12, 1)}), flush=True)
+
+
 def bench_topk(batches):
     for B in batches:
         x = torch.randn(B, 248320, device="cuda").to(torch.bfloat16)
@@ -293,7 +326,8 @@ def bench_topk(batches):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attn", "w4a16", "gemm_fin", "fmha", "topk", "gdn"])
+    ap.add_argument("what", choices=["gemm", "attn", "w4a16", "gemm_fin", "fmha", "topk", "gdn",
+                                          "gdn_prefill"])
     ap.add_argument("--q-len", type=int, default=2048)
     ap.add_argument("--ctx", default="1500,4096,16384")
     ap.add_argument("--splits", default="1,4,8,17,32")
@@ -329,6 +363,8 @@ def main():
         bench_topk([int(v) for v in a.m.split(",")])
     elif a.what == "gdn":
         bench_gdn_decode([int(v) for v in a.m.split(",")])
+    elif a.what == "gdn_prefill":
+        bench_gdn_prefill([int(v) for v in a.ctx.split(",")], [48, 24, 12, 6])
 
 
 if __name__ == "__main__":

@@ -37,6 +37,11 @@ void gdn_chunked(torch::Tensor y, torch::Tensor ba, torch::Tensor A_log, torch::
                  torch::Tensor state, torch::Tensor qsl, torch::Tensor slots,
                  torch::Tensor has_init, int64_t Hk, double scale, torch::Tensor out,
                  int64_t split_override);
+int64_t gdn_chunked2_ws_bytes(int64_t T, int64_t B, int64_t Hv);
+void gdn_chunked2(torch::Tensor y, torch::Tensor ba, torch::Tensor A_log, torch::Tensor dt_bias,
+                  torch::Tensor state, torch::Tensor qsl, torch::Tensor slots,
+                  torch::Tensor has_init, int64_t Hk, double scale, torch::Tensor out,
+                  torch::Tensor ws, int64_t split_override);
 void qkv_prologue(torch::Tensor qkv, int64_t q_head_stride, int64_t k_off, int64_t v_off,
                   torch::Tensor positions, torch::Tensor qn_w, torch::Tensor kn_w,
                   torch::Tensor cos_sin, int64_t rot, int64_t Hq, int64_t Hkv, double eps,
@@ -164,6 +169,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_combine", &rad::ep_combine, "expert outputs -> sources; weighted sum over top-k");
   m.def("dflash_walk", &rad::dflash_walk, "DFlash2 candidate path walk (one warp per request)");
   m.def("gdn_chunked", &rad::gdn_chunked, "chunked (64-token) gated delta rule for prefill");
+  m.def("gdn_chunked2_ws_bytes", &rad::gdn_chunked2_ws_bytes, "two-phase chunk scan workspace");
+  m.def("gdn_chunked2", &rad::gdn_chunked2,
+        "two-phase chunked gated delta rule: chunk-parallel solve, then the state scan");
   m.def("gdn_decode_fused", &rad::gdn_decode_fused,
         "one-token GDN step: conv update + SiLU + q/k L2 norm + gates + delta rule");
   m.def("mxfp4_gemm_push", &rad::mxfp4_gemm_push,

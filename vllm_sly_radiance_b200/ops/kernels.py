@@ -515,6 +515,7 @@ def gdn_decode_fused_quant(proj, ba_off: int, z_off: int, conv_w, conv_state, ss
 
 _GDN_CHUNKED = os.environ.get("RADIANCE_GDN_CHUNKED", "1") != "0"
 _GDN_CHUNK_SPLIT = int(os.environ.get("RADIANCE_GDN_CHUNK_SPLIT", "0"))   # 0: by batch size
+_GDN_TWO_PHASE = os.environ.get("RADIANCE_GDN_TWO_PHASE", "1") != "0"
 _GDN_DECODE_FUSED = os.environ.get("RADIANCE_GDN_DECODE_FUSED", "1") != "0"
 # the o_proj producer inside decode attention: opt-in, it measured slower than attention followed
 # by gate_mul_quant (the gate runs after two levels of last-CTA serialisation: splits, kv heads)
@@ -555,10 +556,19 @@ def gdn_recurrent(y, ba, A_log, dt_bias, ssm_state, meta, num_k_heads: int, scal
         return out
     if (commit_len is None and write_out and _GDN_CHUNKED and DK == 128 and DV == 128
             and meta.num_tokens > meta.num_seqs):
-        # prefill rows in the batch: the 64-token chunk scan on the tensor cores
-        ext().gdn_chunked(y, ba, A_log, dt_bias, ssm_state, meta.query_start_loc,
-                          meta.state_slots, meta.has_initial, num_k_heads, scale, out,
-                          _GDN_CHUNK_SPLIT)
+        # prefill rows in the batch: the 64-token chunk scan on the tensor cores -- by default in
+        # two phases (every chunk's triangular solve in parallel, then the state scan split over
+        # value columns)
+        if _GDN_TWO_PHASE:
+            T, B = y.shape[0], meta.state_slots.shape[0]
+            ws = workspace(y.device, "gdn2", ext().gdn_chunked2_ws_bytes(T, B, Hv) // 4 + 4)
+            ext().gdn_chunked2(y, ba, A_log, dt_bias, ssm_state, meta.query_start_loc,
+                               meta.state_slots, meta.has_initial, num_k_heads, scale, out, ws,
+                               _GDN_CHUNK_SPLIT if _GDN_CHUNK_SPLIT in (2, 4, 8) else 0)
+        else:
+            ext().gdn_chunked(y, ba, A_log, dt_bias, ssm_state, meta.query_start_loc,
+                              meta.state_slots, meta.has_initial, num_k_heads, scale, out,
+                              _GDN_CHUNK_SPLIT)
         return out
     ext().gdn_recurrent(y, ba, A_log, dt_bias, ssm_state, meta.query_start_loc, meta.state_slots,
                         meta.has_initial, _none(commit_len, y.device), num_k_heads, scale, out,
