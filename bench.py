@@ -292,9 +292,10 @@ def main():
     tp_check = None
     if world > 1 and not args.no_extra and not args.no_tp_check:
         tp_lg = prompt_logits(eng, tp_check_prompt(eng))
+        tp_h0 = prompt_logits(eng, tp_check_prompt(eng, 98), layer0=True, rid="tpchk0")[1]
         eng.runner.graphs.clear()
         eng = None                      # rank 0 builds a TP1 engine in its place
-        tp_check = tp_agreement(tp_lg, cfg, rank, dist)
+        tp_check = tp_agreement(tp_lg, tp_h0, cfg, rank, dist)
 
     if rank == 0:
         line = {
@@ -533,26 +534,45 @@ def moe_workload(args, rank, world, dist):
         dist.destroy_process_group()
 
 
-def tp_check_prompt(eng):
-    g = torch.Generator().manual_seed(99)
+def tp_check_prompt(eng, seed=99):
+    g = torch.Generator().manual_seed(seed)
     return torch.randint(3, eng.model_config.vocab_size, (512,), generator=g).tolist()
 
 
-def prompt_logits(e, prompt):
-    """Logits of the last prompt position (one full prefill through the engine)."""
+def prompt_logits(e, prompt, layer0=False, rid="tpchk"):
+    """Logits of the last prompt position (one full prefill through the engine).  layer0: also
+    the residual stream after the first layer (the model's aux-layer output), -> (logits, h0)."""
     from vllm_sly_radiance_b200.engine.request import SamplingParams
-    e.add_request(prompt, SamplingParams(temperature=0, max_tokens=1), "tpchk")
-    while True:
-        sched = e.scheduler.schedule()
-        res = e.runner.execute(sched, want_logits=True)
-        e.scheduler.update(sched, res.sampled)
-        if res.sampled:
-            return res.logits[-1].float().cpu()
+    caps = []
+    orig = e.model.forward
+    if layer0:
+        def fwd(input_ids, meta, caches, aux_layers=None, aux_out=None, gdn_save=None):
+            st = []
+            r = orig(input_ids, meta, caches, aux_layers=[0], aux_out=st, gdn_save=gdn_save)
+            caps.append(st[0].float().cpu())
+            return r
+        e.model.forward = fwd
+    e.add_request(prompt, SamplingParams(temperature=0, max_tokens=1), rid)
+    try:
+        while True:
+            sched = e.scheduler.schedule()
+            res = e.runner.execute(sched, want_logits=True)
+            e.scheduler.update(sched, res.sampled)
+            if res.sampled:
+                lg = res.logits[-1].float().cpu()
+                return (lg, torch.cat(caps)) if layer0 else lg
+    finally:
+        e.model.forward = orig
 
 
-def tp_agreement(tp_lg, cfg, rank, dist):
-    """TP correctness at this N: the TP engine's last-prompt-position logits against a TP1 engine
-    that rank 0 builds from the same seed (after the TP engine is released)."""
+def tp_agreement(tp_lg, tp_h0, cfg, rank, dist):
+    """TP correctness at this N: the TP engine's last-prompt-position logits and its residual
+    stream after the first layer against a TP1 engine that rank 0 builds from the same seed
+    (after the TP engine is released).  With W4A8 the row-parallel linears quantise each rank's
+    shard of a token with that shard's own e4m3 scale, so one layer differs by a few percent
+    from TP1 (layer0_rel); a random-weight 64-layer stack then amplifies any such difference
+    (with bf16 weights: 0.6 % after layer 0, 12 % after layer 64), so the logits are reported,
+    not asserted."""
     import dataclasses
     import gc
     from vllm_sly_radiance_b200.engine.llm_engine import LLMEngine
@@ -565,9 +585,11 @@ def tp_agreement(tp_lg, cfg, rank, dist):
                                  enable_cuda_graphs=False, capture_graphs_at_start=False)
         e1 = LLMEngine(c1)
         ref_lg = prompt_logits(e1, tp_check_prompt(e1))
+        ref_h0 = prompt_logits(e1, tp_check_prompt(e1, 98), layer0=True, rid="tpchk0")[1]
         del e1
         d = (tp_lg - ref_lg).abs()
         out = {"vs": "tp1 engine, same seed, 512-token prompt, last position",
+               "layer0_rel": round(float((tp_h0 - ref_h0).norm() / ref_h0.norm()), 5),
                "max_abs_diff": round(float(d.max()), 4),
                "rel_max_diff": round(float(d.max() / ref_lg.abs().max()), 5),
                "top1_equal": bool(int(tp_lg.argmax()) == int(ref_lg.argmax())),

@@ -203,3 +203,19 @@ def test_mtp_drafter_engine_gpu():
     e8 = eng("mtp", "mxfp4", "fp8")
     sp2 = SamplingParams(temperature=0.8, top_p=0.95, max_tokens=8, seed=3, ignore_eos=True)
     assert len(e8.generate([prompt, prompt[:40]], sp2)[1].outputs[0].token_ids) == 8
+
+
+@pytest.mark.parametrize("T,H,G,taps,block", [(8, 256, 16, 4, 8), (40, 5120, 320, 4, 8),
+                                               (21, 512, 32, 3, 7)])
+def test_dflash_grouped_conv_kernel(T, H, G, taps, block):
+    """The drafter's block-causal grouped conv kernel against its torch form (fp32 oracle)."""
+    from vllm_sly_radiance_b200.models.dflash2 import grouped_conv
+    g = torch.Generator().manual_seed(T + H)
+    h = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    co = torch.randn(T, 2 * taps * G, generator=g).to(torch.bfloat16)
+    delta = co.view(T, 2, taps, G)[:, 1]
+    base = (torch.randn(taps, H, generator=g) * 0.1).to(torch.bfloat16)
+    want = grouped_conv(h, delta, base, block, G, taps).float()
+    got = grouped_conv(h.cuda(), co.cuda().view(T, 2, taps, G)[:, 1], base.cuda(), block, G,
+                       taps).float().cpu()
+    assert torch.allclose(got, want, atol=2e-2, rtol=1e-2), float((got - want).abs().max())

@@ -118,6 +118,8 @@ void ep_silu_items(torch::Tensor gu, torch::Tensor items, int64_t bn, torch::Ten
 void ep_combine(std::vector<int64_t> peers, int64_t rank, int64_t maxr, int64_t El,
                 int64_t maxt, torch::Tensor y, torch::Tensor w, torch::Tensor out,
                 torch::Tensor status);
+void dflash_conv(torch::Tensor h, torch::Tensor delta, torch::Tensor base, int64_t G,
+                 int64_t block, torch::Tensor out);
 void dflash_walk(torch::Tensor unary, torch::Tensor cand, torch::Tensor anchors, torch::Tensor hp,
                  torch::Tensor pred, torch::Tensor succ, torch::Tensor temps, torch::Tensor seeds,
                  torch::Tensor drafts, torch::Tensor winp, torch::Tensor status);
@@ -168,6 +170,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_silu_items", &rad::ep_silu_items, "SiLU*mul + e4m3 for the work table's rows");
   m.def("ep_combine", &rad::ep_combine, "expert outputs -> sources; weighted sum over top-k");
   m.def("dflash_walk", &rad::dflash_walk, "DFlash2 candidate path walk (one warp per request)");
+  m.def("dflash_conv", &rad::dflash_conv, "DFlash2 block-causal grouped depthwise conv");
   m.def("gdn_chunked", &rad::gdn_chunked, "chunked (64-token) gated delta rule for prefill");
   m.def("gdn_chunked2_ws_bytes", &rad::gdn_chunked2_ws_bytes, "two-phase chunk scan workspace");
   m.def("gdn_chunked2", &rad::gdn_chunked2,

@@ -307,6 +307,45 @@ __global__ void __launch_bounds__(128) walk_kernel(
   }
 }
 
+
+// DFlash2 grouped depthwise convolution over block positions (the drafter's DFlashGroupedConv):
+//   out[t, c] = sum_{tap <= min(pos(t), taps - 1)} (base[tap, c] + delta[t, tap, c / gs]) h[t - tap, c]
+// with pos(t) = t % block (blocks are independent).  One CTA per row, 8 channels per thread,
+// fp32 arithmetic, bf16 in and out.
+__global__ void __launch_bounds__(128) dflash_conv_kernel(
+    const __nv_bfloat16* __restrict__ h, int ldh, const __nv_bfloat16* __restrict__ delta,
+    int ldd, const __nv_bfloat16* __restrict__ base, int H, int G, int taps, int block,
+    __nv_bfloat16* __restrict__ out, int ldo) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x;
+  const int pos = t % block;
+  const int gs = H / G;
+  const int nt = min(pos + 1, taps);
+  for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
+    const int c = v * 8;
+    const int g = c / gs;                   // gs % 8 == 0: the 8 channels share a group
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int tap = 0; tap < nt; ++tap) {
+      const float d = __bfloat162float(delta[(size_t)t * ldd + tap * G + g]);
+      const uint4 hu = *reinterpret_cast<const uint4*>(h + (size_t)(t - tap) * ldh + c);
+      const uint4 bu = *reinterpret_cast<const uint4*>(base + (size_t)tap * H + c);
+      const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&hu);
+      const __nv_bfloat162* bb = reinterpret_cast<const __nv_bfloat162*>(&bu);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float2 hf = __bfloat1622float2(hh[i]), bf = __bfloat1622float2(bb[i]);
+        acc[2 * i] += (bf.x + d) * hf.x;
+        acc[2 * i + 1] += (bf.y + d) * hf.y;
+      }
+    }
+    uint4 o;
+    __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) oh[i] = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+    *reinterpret_cast<uint4*>(out + (size_t)t * ldo + c) = o;
+  }
+}
 }  // namespace spec
 
 // draft [B,k] int64; t_ids/t_probs [B,k+1,W]; d_ids/d_probs [B,k,Kd] or empty (point mass);
@@ -388,6 +427,34 @@ void dflash_walk(torch::Tensor unary, torch::Tensor cand, torch::Tensor anchors,
                             seeds.data_ptr<int64_t>(), B, k, Kc, r, (int64_t)pred.size(0),
                             drafts.data_ptr<int64_t>(), winp.data_ptr<float>(),
                             status.data_ptr<int>()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+// h [T, H] bf16 (rows 16-byte aligned); delta: bf16 view [T, taps, G] with row stride ldd and
+// unit group stride; base bf16 [taps, H]; out [T, H] bf16.
+void dflash_conv(torch::Tensor h, torch::Tensor delta, torch::Tensor base, int64_t G,
+                 int64_t block, torch::Tensor out) {
+  const int T = h.size(0), H = h.size(1), taps = base.size(0);
+  TORCH_CHECK(h.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16 &&
+                  base.scalar_type() == at::kBFloat16 && delta.scalar_type() == at::kBFloat16,
+              "dflash_conv: bf16 tensors");
+  TORCH_CHECK(h.stride(1) == 1 && h.stride(0) % 8 == 0 && out.stride(1) == 1 &&
+                  out.stride(0) % 8 == 0 && base.is_contiguous() && base.size(1) == H,
+              "dflash_conv: row layouts");
+  TORCH_CHECK(H % 8 == 0 && G >= 1 && H % G == 0 && (H / G) % 8 == 0, "dflash_conv: groups");
+  TORCH_CHECK(delta.dim() == 3 && delta.size(0) == T && delta.size(1) == taps &&
+                  delta.size(2) == G && delta.stride(2) == 1 && delta.stride(1) == G,
+              "dflash_conv: delta [T, taps, G]");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(h.data_ptr()) % 16) == 0 &&
+                  (reinterpret_cast<uintptr_t>(out.data_ptr()) % 16) == 0 &&
+                  (reinterpret_cast<uintptr_t>(base.data_ptr()) % 16) == 0, "dflash_conv: alignment");
+  if (T == 0) return;
+  const at::cuda::CUDAGuard guard(h.device());
+  auto stream = at::cuda::getCurrentCUDAStream();
+  C10_CUDA_CHECK(launch_pdl(spec::dflash_conv_kernel, dim3(T), dim3(128), 0, stream,
+                            (const __nv_bfloat16*)h.data_ptr(), (int)h.stride(0),
+                            (const __nv_bfloat16*)delta.data_ptr(), (int)delta.stride(0),
+                            (const __nv_bfloat16*)base.data_ptr(), H, (int)G, taps, (int)block,
+                            (__nv_bfloat16*)out.data_ptr(), (int)out.stride(0)));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 }  // namespace rad

@@ -88,7 +88,13 @@ def selector_walk_torch(unary, cand, anchors, hp, pred_cb, succ_cb, temps):
 def grouped_conv(h: torch.Tensor, delta: torch.Tensor, base: torch.Tensor, block: int,
                  G: int, taps: int) -> torch.Tensor:
     """h [T, H] (T = n_blocks * block, block-major); delta [T, taps, G]; base [taps, H].
-    out[t] = sum_{tap <= pos(t)} (base[tap] + delta[t, tap, group]) * h[t - tap]."""
+    out[t] = sum_{tap <= pos(t)} (base[tap] + delta[t, tap, group]) * h[t - tap].  CUDA rows run
+    as one kernel (``csrc/spec_decode.cu`` dflash_conv_kernel); this torch form is its oracle."""
+    if h.is_cuda:
+        from ..ops._ext import ext
+        out = torch.empty(h.shape, dtype=torch.bfloat16, device=h.device)
+        ext().dflash_conv(h.contiguous(), delta, base.contiguous(), G, block, out)
+        return out
     T, H = h.shape
     gs = H // G
     hb = h.float().view(T, G, gs)
@@ -273,9 +279,14 @@ class DFlash2Drafter:
             h = grouped_conv(m, co[:, 1], lay.mlp_base[1], blk, lay.G, dc.conv_taps)
         hf, _ = K.add_rms_norm(h, res, self.final_norm, dc.rms_norm_eps, want_residual=False)
         hd = hf.view(B, blk, -1)[:, 1:].reshape(B * k, -1)             # draft positions
-        logits = self.target.logits(hd).float()                        # shared lm_head
+        logits = self.target.logits(hd)                                 # shared lm_head
         Kc = dc.top_k_candidates
-        unary, cand = torch.topk(logits, Kc, dim=-1)                    # [B*k, Kc]
+        if logits.is_cuda and Kc <= K.TOPK_WINDOW:
+            # the sampler's top-64 window kernel (sorted, ties to the lowest id) over the vocab
+            unary, cand = K.topk_window(logits)
+            unary, cand = unary[:, :Kc].contiguous(), cand[:, :Kc].contiguous()
+        else:
+            unary, cand = torch.topk(logits.float(), Kc, dim=-1)        # [B*k, Kc]
         unary, cand = unary.view(B, k, Kc), cand.view(B, k, Kc)
         hp = self.hidden_proj(hd).float().view(B, k, -1)                # [B,k,r]
         temps = torch.tensor([r.params.temperature for r in reqs], device=dev).view(B)
