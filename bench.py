@@ -492,8 +492,10 @@ def moe_workload(args, rank, world, dist):
     ep = make_ep_group(rank, world, "p2p") if world > 1 else None
     batch = 64
     per_rank = max(1, batch // world)
+    # one rank: the local grouped-expert path has fixed shapes and no host sync, so decode steps
+    # replay as CUDA graphs; the EP exchange synchronises with the peers on the host and runs eagerly
     cfg = EngineConfig(model="moe_hybrid", max_model_len=12288, max_num_seqs=per_rank,
-                       max_num_batched_tokens=4096, device="cuda", enable_cuda_graphs=False)
+                       max_num_batched_tokens=4096, device="cuda", enable_cuda_graphs=world == 1)
     m = HybridModel(moe_hybrid(), quant="mxfp4", device=dev, seed=0, ep=ep)
     eng = LLMEngine(cfg, model=m)
     V = m.cfg.vocab_size

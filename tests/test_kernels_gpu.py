@@ -48,6 +48,28 @@ def test_mxfp4_gemm(M, N, Kd, splits):
     assert rel_err(got, want) < 1e-2, rel_err(got, want)
 
 
+@pytest.mark.parametrize("M,N,Kd,fmt", [
+    (512, 256, 256, "e2m1"), (1031, 640, 1088, "e2m1"), (4096, 5120, 1088, "e2m1"),
+    (777, 2176, 5120, "e2m1"), (2048, 384, 512, "e4m3"), (600, 1000, 768, "e2m3")])
+def test_mxfp4_gemm_cta_pair(M, N, Kd, fmt):
+    """Prefill GEMM on CTA pairs (tcgen05 cta_group::2, persistent, M >= 512) against the fp32
+    product and against the one-CTA kernel (forced by an explicit split count)."""
+    g = torch.Generator().manual_seed(M + N + Kd)
+    w = torch.randn(N, Kd, generator=g) * 0.02
+    x = torch.randn(M, Kd, generator=g)
+    wq = MXFP4Weight.from_float(w, fmt)
+    q, s = ref.quant_fp8_rows(x.to(torch.bfloat16))
+    want = ref.mxfp4_linear(q, s, wq.packed, wq.scales, fmt=fmt)
+    wg = wq.to(DEV)
+    for rep in range(2):
+        got = K.mxfp4_gemm(q.to(DEV), s.to(DEV), wg.packed, wg.sf, wg.scales, N)
+        one = K.mxfp4_gemm(q.to(DEV), s.to(DEV), wg.packed, wg.sf, wg.scales, N, splits=1)
+        torch.cuda.synchronize()
+        K.check_status(got.device)
+        assert rel_err(got, want) < 1e-2, (rep, rel_err(got, want))
+        assert rel_err(got, one) < 5e-3, (rep, rel_err(got, one))
+
+
 @pytest.mark.parametrize("fmt", ["e2m3", "e4m3"])
 @pytest.mark.parametrize("M,N,Kd,splits", [
     (1, 256, 256, 0), (5, 384, 512, 0), (16, 256, 1024, 4), (37, 200, 768, 0),

@@ -560,6 +560,277 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
 }
 
 // ---------------------------------------------------------------------------------------------
+// Prefill tiles on CTA pairs (tcgen05 cta_group::2).  A 2-CTA cluster owns a 256 x 256 output
+// tile: each CTA stages its 128 weight rows and its 128 of the 256 tokens, and the pair's leader
+// issues one M = 256, N = 256 block-scaled MMA per 32 K.  Against one CTA per 128 x 256 tile this
+// halves the activation bytes each SM moves through shared memory per MMA -- the limit of the
+// fp8-rate MMA with both operands in shared memory.  The kernel is persistent (one pair per two
+// SMs, tiles strided by the pair count, weight tiles fastest so concurrent pairs share the
+// activation tile in L2); the producers keep prefetching the next tile's stages while the
+// epilogue drains the accumulator.  No load is multicast: each CTA's TMA fills its own shared
+// memory and signals the leader's barrier (.cta_group::2 form).
+// ---------------------------------------------------------------------------------------------
+constexpr int P_BN = 256;                                  // tokens per pair tile (MMA N)
+constexpr int P_HALF = 128;                                // tokens staged per CTA
+constexpr int P_W_BYTES = BM * BK;                         // expanded weight tile (16 KB)
+constexpr int P_A_BYTES = P_HALF * BK;                     // this CTA's activation half (16 KB)
+constexpr int P_STAGE = (P_W_BYTES + P_A_BYTES + SF_TILE_BYTES + 1023) / 1024 * 1024;
+constexpr int P_STAGES = (kSmemBudget - 2048) / P_STAGE;
+constexpr int P_SMEM = 1024 + P_STAGES * P_STAGE + 1024;
+constexpr int P_TMEM_COLS = 512;                           // accumulator 256 + SFA + SFB
+constexpr int P_SFA_COL = 256;
+constexpr int P_SFB_COL = 288;                             // 32 columns of UE8M0 1.0
+static_assert(P_STAGES >= 4, "pair pipeline depth");
+
+struct PairBars {
+  uint64_t full[P_STAGES];      // leader: both CTAs' bytes of a stage landed
+  uint64_t empty[P_STAGES];     // each CTA: the pair's MMAs have read its stage
+  uint64_t acc_full;            // each CTA: the tile's accumulator is complete
+  uint64_t acc_empty;           // leader: both epilogues drained the accumulator
+  uint32_t tmem;
+  int abort;
+};
+
+__host__ __device__ constexpr uint32_t make_idesc_pair(int sf_id, int wfmt) {
+  return (w_mma_format(wfmt) << 7)             // A format: the weight element type
+         | (0u << 10)                          // B format: E4M3
+         | ((uint32_t)(P_BN >> 3) << 17)       // N >> 3
+         | (1u << 23)                          // scale format UE8M0
+         | ((uint32_t)(256 >> 4) << 24)        // M >> 4 (the pair's 256 rows)
+         | ((uint32_t)sf_id << 29) | ((uint32_t)sf_id << 4);
+}
+
+DEVI void tma_load_2d_pair(void* smem_dst, const void* desc, uint32_t mbar, int c0, int c1,
+                           uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
+      "l"(desc), "r"(mbar), "r"(c0), "r"(c1), "l"(policy)
+      : "memory");
+}
+DEVI void mma_mxf8f6f4_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                            uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+// arrive on the mbarrier at a cluster address once the pair's prior tcgen05 ops are done
+DEVI void commit_pair(uint32_t mbar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   mbar)
+               : "memory");
+}
+DEVI void tmem_cp_pair_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
+               : "memory");
+}
+DEVI void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+DEVI void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+DEVI void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+DEVI void mbar_arrive_cluster(uint32_t mbar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(mbar) : "memory");
+}
+
+// Warp roles as in the one-CTA kernel: warp 0 = TMA producer (both CTAs), warp 1 = TMEM
+// allocator (both CTAs) and MMA issuer (leader only), warps 2..5 = epilogue (both CTAs, each its
+// own 128 weight rows x 256 tokens of the accumulator).
+template <bool RS>
+__global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(
+    const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_a,
+    const __grid_constant__ CUtensorMap tmap_sf, const float* __restrict__ a_scale,
+    __nv_bfloat16* __restrict__ out, int ldo, int M, int N, int Kw, int wfmt,
+    int* __restrict__ status, const PushArgs push) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  PairBars* bars = reinterpret_cast<PairBars*>(smem + P_STAGES * P_STAGE);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();             // 0 = leader (issues the MMAs)
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int n_tiles = (N + P_BN - 1) / P_BN;
+  const int num_tiles = n_tiles * ((M + P_BN - 1) / P_BN);
+  const int k_tiles = Kw / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(&bars->full[s], 1);
+      mbar_init(&bars->empty[s], 1);
+    }
+    mbar_init(&bars->acc_full, 1);
+    mbar_init(&bars->acc_empty, 2);
+    bars->abort = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_w);
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_sf);
+  }
+  pdl_trigger();
+  if (warp == 1) {
+    tmem_alloc_pair(&bars->tmem, P_TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_acc = bars->tmem;
+  const uint32_t tmem_sfa = tmem_acc + P_SFA_COL;
+  const uint32_t tmem_sfb = tmem_acc + P_SFB_COL;
+  if (warp >= 2) {              // activation scale factors: UE8M0 1.0 everywhere
+    const int q = warp & 3;
+    uint32_t ones[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ones[i] = 0x7F7F7F7Fu;
+#pragma unroll
+    for (int c = 0; c < 32; c += 8) tmem_st_32x32b_x8(tmem_sfb + ((uint32_t)(q * 32) << 16) + c, ones);
+    tmem_st_wait();
+  }
+  tc_fence_before();
+  __syncthreads();
+  __syncwarp();
+  cluster_sync();               // both CTAs: barriers initialised, TMEM allocated and filled
+  tc_fence_after();
+
+  if (warp == 0) {
+    // ---------------- TMA producer (both CTAs) ----------------
+    if (elect_one()) {
+      const uint64_t w_policy = l2_policy_evict_first();
+      const uint64_t a_policy = l2_policy_evict_last();
+      const uint32_t tx = 2u * (w_tile_tx(wfmt) + P_A_BYTES + SF_TILE_BYTES);
+      pdl_wait();
+      uint32_t it = 0;
+      for (int t = pair; t < num_tiles && !*(volatile int*)&bars->abort; t += npairs) {
+        const int n0 = (t % n_tiles) * P_BN + (int)rank * BM;
+        const int m0 = (t / n_tiles) * P_BN + (int)rank * P_HALF;
+        for (int kt = 0; kt < k_tiles; ++kt, ++it) {
+          const int s = it % P_STAGES;
+          const uint32_t ph = (it / P_STAGES) & 1;
+          if (!mbar_wait(&bars->empty[s], ph ^ 1, status)) { bars->abort = 1; break; }
+          uint8_t* st = smem + s * P_STAGE;
+          const uint32_t full = mapa_shared(smem_u32(&bars->full[s]), 0);
+          if (rank == 0) mbar_arrive_expect_tx(&bars->full[s], tx);
+          tma_load_2d_pair(st, &tmap_w, full, kt * BK, n0, w_policy);
+          tma_load_2d_pair(st + P_W_BYTES, &tmap_a, full, kt * BK, m0, a_policy);
+          tma_load_2d_pair(st + P_W_BYTES + P_A_BYTES, &tmap_sf, full, 0, (n0 / BM) * k_tiles + kt,
+                           w_policy);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (leader) ----------------
+    if (rank == 0 && elect_one()) {
+      const uint32_t empty_peer0 = mapa_shared(smem_u32(&bars->empty[0]), 1);
+      const uint32_t accf_peer = mapa_shared(smem_u32(&bars->acc_full), 1);
+      uint32_t it = 0, tc = 0;
+      bool ok = true;
+      for (int t = pair; t < num_tiles && ok; t += npairs, ++tc) {
+        if (!mbar_wait(&bars->acc_empty, (tc & 1) ^ 1, status)) { ok = false; break; }
+        tc_fence_after();
+        for (int kt = 0; kt < k_tiles; ++kt, ++it) {
+          const int s = it % P_STAGES;
+          const uint32_t ph = (it / P_STAGES) & 1;
+          if (!mbar_wait(&bars->full[s], ph, status)) { ok = false; break; }
+          tc_fence_after();
+          uint8_t* st = smem + s * P_STAGE;
+          const uint32_t w_addr = smem_u32(st);
+          const uint32_t a_addr = smem_u32(st + P_W_BYTES);
+          tmem_cp_pair_32x128b_warpx4(tmem_sfa, sdesc_plain(smem_u32(st + P_W_BYTES + P_A_BYTES), 0, 128));
+#pragma unroll
+          for (int kb = 0; kb < BK / 32; ++kb)
+            mma_mxf8f6f4_pair(tmem_acc, sdesc_sw128(w_addr + kb * 32), sdesc_sw128(a_addr + kb * 32),
+                              make_idesc_pair(kb, wfmt), tmem_sfa | ((uint32_t)kb << 30),
+                              tmem_sfb | ((uint32_t)kb << 30), (kt > 0 || kb > 0) ? 1u : 0u);
+          commit_pair(smem_u32(&bars->empty[s]));
+          commit_pair(empty_peer0 + (uint32_t)(s * sizeof(uint64_t)));
+        }
+        if (!ok) break;
+        commit_pair(smem_u32(&bars->acc_full));
+        commit_pair(accf_peer);
+      }
+      if (!ok) bars->abort = 1;
+    }
+  } else {
+    // ---------------- epilogue (both CTAs) ----------------
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const uint32_t acc_empty = mapa_shared(smem_u32(&bars->acc_empty), 0);
+    const uint32_t lane_base = tmem_acc + ((uint32_t)(q * 32) << 16);
+    pdl_wait();
+    uint32_t tc = 0;
+    for (int t = pair; t < num_tiles; t += npairs, ++tc) {
+      const bool got = mbar_wait(&bars->acc_full, tc & 1, status);
+      if (!got) bars->abort = 1;
+      tc_fence_after();
+      const int n = (t % n_tiles) * P_BN + (int)rank * BM + row;
+      const int mt0 = (t / n_tiles) * P_BN;
+      auto store16 = [&](const uint32_t (&r)[16], int c) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int m = mt0 + c * 16 + j;
+          if (m >= M) break;                               // uniform across the warp
+          const float v = got ? __uint_as_float(r[j]) * a_scale[m] : 0.f;
+          if constexpr (RS) {
+            const float vn = __shfl_down_sync(0xffffffffu, v, 1);
+            if ((lane & 1) == 0 && n < N) rs_store(push, m, n, v, vn);
+          } else if (n < N) {
+            out[(size_t)m * ldo + n] = __float2bfloat16_rn(v);
+          }
+        }
+      };
+      uint32_t ra[16], rb[16];
+      tmem_ld_32x32b_x16(lane_base, ra);
+      tmem_ld_wait();
+#pragma unroll 1
+      for (int c = 0; c < P_BN / 16; c += 2) {
+        tmem_ld_32x32b_x16(lane_base + (uint32_t)((c + 1) * 16), rb);
+        store16(ra, c);
+        tmem_ld_wait();
+        if (c + 2 < P_BN / 16) tmem_ld_32x32b_x16(lane_base + (uint32_t)((c + 2) * 16), ra);
+        store16(rb, c + 1);
+        tmem_ld_wait();
+      }
+      // the accumulator is free for the pair's next tile once all four warps have read it
+      tc_fence_before();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 64) mbar_arrive_cluster(acc_empty);
+      if (*(volatile int*)&bars->abort) break;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  __syncwarp();
+  cluster_sync();               // the pair's MMAs, copies and remote arrivals are all done
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_acc, P_TMEM_COLS);
+  }
+  if constexpr (RS) {
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0)
+      for (int o = 0; o < push.world; ++o)
+        asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(
+                         reinterpret_cast<uint32_t*>(push.peer[o]) + push.rank),
+                     "r"(1u) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------
 struct MapKey {
@@ -670,6 +941,74 @@ static void launch(const torch::Tensor& a, const torch::Tensor& a_scale, const t
                                     per, status, (const int*)nullptr, 0, push, aa, fc));
 }
 
+// scale-factor tiles as TMA rows: 512 bytes (128 x u32) per (128-row tile, k tile)
+static CUtensorMap sf_map(const torch::Tensor& sf, int64_t rows) {
+  MapKey key{(uintptr_t)sf.data_ptr(), rows, 128, 512, 1, -1};
+  std::lock_guard<std::mutex> g(g_map_mu);
+  auto it = g_wmaps.find(key);
+  if (it != g_wmaps.end()) return it->second;
+  CUtensorMap m = make_tma_2d(sf.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT32, 128, rows, 512, 128, 1,
+                              CU_TENSOR_MAP_SWIZZLE_NONE);
+  g_wmaps.emplace(key, m);
+  return m;
+}
+
+static bool pair_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("RADIANCE_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+constexpr int kPairMinRows = 512;      // prefill chunks; shorter batches keep the one-CTA tiles
+
+// Persistent CTA-pair GEMM (prefill).  Returns the CTA count (the RS arrival count).
+template <bool RS>
+static int launch_pair(const torch::Tensor& a, const torch::Tensor& a_scale, const torch::Tensor& wp,
+                       const torch::Tensor& sf, torch::Tensor& out, int M, int N, int K,
+                       int* status, cudaStream_t stream, const PushArgs& push) {
+  const WFmt wf = weight_fmt(wp.size(1), K);
+  const int Kw = wf.Kw;
+  const int k_tiles = Kw / BK;
+  TORCH_CHECK(sf.numel() >= (int64_t)((N + BM - 1) / BM) * k_tiles * SF_TILE_BYTES,
+              "mxfp4_gemm: scale-factor tiles");
+  CUtensorMap tw = weight_map(wp, N, Kw, wf.code);
+  CUtensorMap ta = make_tma_2d(a.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, K, M, a.stride(0), BK,
+                               P_HALF, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap ts = sf_map(sf, (int64_t)((N + BM - 1) / BM) * k_tiles);
+  static int sms = [] {
+    int dev = 0, v = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    return v;
+  }();
+  const int tiles = ((N + P_BN - 1) / P_BN) * ((M + P_BN - 1) / P_BN);
+  const int pairs = std::max(1, std::min(tiles, sms / 2));
+  auto kern = gemm_pair_kernel<RS>;
+  static bool attr = false;
+  if (!attr) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM));
+    attr = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = P_SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  attrs[0].id = cudaLaunchAttributeClusterDimension;
+  attrs[0].val.clusterDim.x = 2;
+  attrs[0].val.clusterDim.y = 1;
+  attrs[0].val.clusterDim.z = 1;
+  attrs[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attrs;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  C10_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, tw, ta, ts, (const float*)a_scale.data_ptr(),
+                                    RS ? nullptr : (__nv_bfloat16*)out.data_ptr(),
+                                    RS ? 0 : (int)out.stride(0), M, N, Kw, wf.code, status, push));
+  return 2 * pairs;
+}
+
 static int pick_splits(int tiles, int k_tiles, int ctas_per_sm) {
   // fill the SMs in one wave: grow the cluster along K while the grid fits the resident slots
   // (148 SMs x CTAs per SM) and each CTA keeps >= 4 k-tiles
@@ -770,6 +1109,12 @@ static int64_t mxfp4_gemm_impl(torch::Tensor a, torch::Tensor a_scale, torch::Te
   const int tiles = ((N + BM - 1) / BM) * ((M + bn - 1) / bn);
   int splits = splits_override > 0 ? (int)splits_override
                                    : pick_splits(tiles, Kw / BK, bn <= 64 ? 2 : 1);
+  if (bn == 256 && M >= kPairMinRows && splits_override <= 0 && pair_enabled()) {
+    // prefill: persistent CTA-pair tiles (every CTA adds one arrival at every owner for RS)
+    if (rs) return launch_pair<true>(a, a_scale, wp, sf, out, M, N, K, st, stream, push);
+    launch_pair<false>(a, a_scale, wp, sf, out, M, N, K, st, stream, push);
+    return (int64_t)tiles;
+  }
   if (rs) {
     // every CTA adds one arrival at every owner: the count the owner waits for
     switch (bn) {

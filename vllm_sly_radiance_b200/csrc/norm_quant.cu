@@ -281,6 +281,7 @@ __global__ void __launch_bounds__(T) quant_rows_kernel(const __nv_bfloat16* __re
     else if (_nv <= 3 * T) { constexpr int MAXV = 3; __VA_ARGS__; } \
     else if (_nv <= 5 * T) { constexpr int MAXV = 5; __VA_ARGS__; } \
     else if (_nv <= 9 * T) { constexpr int MAXV = 9; __VA_ARGS__; } \
+    else if (_nv <= 13 * T) { constexpr int MAXV = 13; __VA_ARGS__; } \
     else TORCH_CHECK(false, "row too long for producer kernel");   \
   } while (0)
 

@@ -114,8 +114,13 @@ class ModelRunner:
         """KV splits per (row tile, kv head): fill ~2 CTAs per SM, at least 256 keys per split
         (one 64-key tile for decode batches, whose per-tile work is small), at most 32.  The
         decode kernel merges up to 128 in-kernel, but more than 32 measured no faster at 16k
-        context (41 us at 32 or 64 splits, 58 us at 128) and slower at 1.5k."""
+        context (41 us at 32 or 64 splits, 58 us at 128) and slower at 1.5k.  Sized for 128k keys
+        or more (long-context engines), a decode split streams its keys one tile at a time for
+        long enough that the loads in flight, not the merge, bound it: there the splits fill ~3
+        CTAs per SM, up to 128."""
         ctas = max(1, ntiles * self.Hkv)
+        if decode and max_kv >= 131072:
+            return max(1, min(128, 148 * 3 // ctas, (max_kv + 1023) // 1024))
         s = max(1, min(32, 148 * 2 // ctas))
         s = min(s, max(1, (max_kv + (63 if decode else 255)) // (64 if decode else 256)))
         return s
