@@ -118,3 +118,19 @@ def test_peer_rank_leaving_fails_the_step():
         if p.is_alive():
             p.kill()
     assert res == ("raised", False, 0), res
+
+
+def test_workspace_canary_catches_an_overrun(monkeypatch):
+    """Debug mode: a write past a workspace's end lands in its canary tail and the check names
+    the workspace; untouched canaries pass."""
+    from vllm_sly_radiance_b200.ops import kernels as K
+    monkeypatch.setattr(K, "_CANARY", True)
+    monkeypatch.setattr(K, "_CANARIES", [])
+    monkeypatch.setattr(K, "_WS", {})
+    ws = K.workspace("cpu", "probe", 100)
+    K.check_canaries()
+    name, base, n = K._CANARIES[0]
+    assert name == "probe" and ws.numel() == n and base.numel() == n + K.CANARY_WORDS
+    base[n + 3] = 7                      # an "overrun" by a kernel writing past ws
+    with pytest.raises(RuntimeError, match="workspace 'probe' overrun: canary word 3"):
+        K.check_canaries()

@@ -14,6 +14,7 @@ import torch
 
 from ..config import EngineConfig, ModelConfig
 from ..models.hybrid import HybridModel, TPInfo
+from ..ops import kernels as K
 from ..utils.metrics import EngineMetrics
 from .kv_cache import KVCacheManager
 from .model_runner import ModelRunner
@@ -158,6 +159,8 @@ class LLMEngine:
             else:
                 result = self.runner.execute(sched)
             code = self.runner.read_status()
+            if K._CANARY:
+                K.check_canaries()          # debug mode: no kernel wrote past its workspace
         except Exception as e:
             # a failed collective (a peer rank that left or timed out) or any other step error:
             # the step's outputs are lost, so no open request can continue

@@ -29,6 +29,8 @@ def _parser():
     s.add_argument("--tool-call-parser", default=None)
     s.add_argument("--enable-auto-tool-choice", action="store_true")
     s.add_argument("--speculative-method", default=None)
+    s.add_argument("--data-parallel-size", type=int, default=1,
+                   help="independent engine replicas, one GPU each, behind this server")
     for f in dataclasses.fields(EngineConfig):
         flag = "--" + f.name.replace("_", "-")
         if flag in ("--speculative-method",):
@@ -105,6 +107,9 @@ def serve(ns):
         if rank != 0:
             follower_loop(engine, bcast)
             return
+    elif getattr(ns, "data_parallel_size", 1) > 1:
+        from .dp import DataParallelEngine
+        engine = DataParallelEngine(cfg, ns.data_parallel_size, tokenizer_path=ns.tokenizer)
     else:
         engine = LLMEngine(cfg, tokenizer_path=ns.tokenizer)
     import uvicorn

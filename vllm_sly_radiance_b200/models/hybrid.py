@@ -38,6 +38,8 @@ from .weights import RandomWeights, cat_rows, pad_rows, slice_cols, slice_rows
 # per-step metadata
 # ---------------------------------------------------------------------------------------------
 _FUSE_PRODUCERS = os.environ.get("RADIANCE_FUSE_PRODUCERS", "0") == "1"   # measured slower at M = 1
+# NVTX ranges per decoder layer (and the final norm) for timeline profilers
+_NVTX = os.environ.get("RADIANCE_NVTX", "0") == "1"
 
 @dataclass
 class StepMeta:
@@ -503,6 +505,10 @@ class HybridModel:
         fin_norm = (self.quant == "mxfp4" and input_ids.is_cuda and self.tp.size == 1
                     and not fuse_prod and input_ids.shape[0] <= K.GEMV_MAX_ROWS)
         for li, layer in enumerate(self.layers):
+            if _NVTX:
+                if li:
+                    torch.cuda.nvtx.range_pop()
+                torch.cuda.nvtx.range_push(f"layer {li} {'attn' if layer.is_attn else 'gdn'}")
             nxt = self.layers[li + 1] if li + 1 < len(self.layers) else None
             if pending is not None:
                 a_in = pending
@@ -561,6 +567,8 @@ class HybridModel:
                 h = self._reduce(h)
             if aux_layers is not None and li in aux_layers:
                 aux_out.append((h.float() + residual.float()).to(torch.bfloat16))
+        if _NVTX and self.layers:
+            torch.cuda.nvtx.range_pop()
         out, _ = K.add_rms_norm(h, residual, self.final_norm, eps, want_residual=False)
         return out
 

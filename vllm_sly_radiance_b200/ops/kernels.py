@@ -78,6 +78,12 @@ def check_status(device, reset: bool = True) -> int:
 
 _WS: dict = {}
 _WS_RETIRED: list = []
+# Debug mode (RADIANCE_CANARY=1): every workspace carries a tail of canary words that no kernel
+# may write; the engine checks them after each step (check_canaries) and names an overrun.
+_CANARY = os.environ.get("RADIANCE_CANARY", "0") == "1"
+CANARY_WORDS = 1024
+CANARY_VALUE = 0x5A5A5A5A
+_CANARIES: list = []
 
 
 def workspace(device, name: str, numel: int) -> torch.Tensor:
@@ -94,9 +100,25 @@ def workspace(device, name: str, numel: int) -> torch.Tensor:
         if t is not None:
             _WS_RETIRED.append(t)
         n = max(numel, 1 << 16, 2 * t.numel() if t is not None else 0)
-        t = torch.zeros(n, dtype=torch.int32, device=device)
+        if _CANARY:
+            base = torch.zeros(n + CANARY_WORDS, dtype=torch.int32, device=device)
+            base[n:] = CANARY_VALUE
+            _CANARIES.append((name, base, n))
+            t = base[:n]
+        else:
+            t = torch.zeros(n, dtype=torch.int32, device=device)
         _WS[key] = t
     return t
+
+
+def check_canaries() -> None:
+    """Debug mode: raise if any workspace's canary tail was written (syncs)."""
+    for name, base, n in _CANARIES:
+        tail = base[n:]
+        if not bool((tail == CANARY_VALUE).all()):
+            first = int((tail != CANARY_VALUE).nonzero()[0])
+            raise RuntimeError(f"workspace '{name}' overrun: canary word {first} past its "
+                               f"{n} words was written")
 
 
 def _none(t, device):
