@@ -103,3 +103,27 @@ def test_expert_parallel_dispatch_combine_matches_single_rank(quant):
         rel = float((lg - ref_lg).norm() / ref_lg.norm())
         assert rel < 2e-2, (rank, rel)
         assert toks[:2] == ref_toks[:2], (rank, toks, ref_toks)
+
+
+def test_ep_transport_splits_a_large_step_into_rounds():
+    """Tokens beyond the NVLink transport's per-call capacity run as several rounds of at most
+    `maxt` tokens, in order; every rank runs the same round count (world 1 here)."""
+    from vllm_sly_radiance_b200.parallel.ep_p2p import P2PTransport
+    tr = P2PTransport(0, 1, maxt=4)
+    tr.begin_step(10)
+    assert tr.rounds == 3
+    seen = []
+
+    def fake_call(blk, q, s, ids, w):
+        seen.append(q.shape[0])
+        return q.float().clone()
+    tr._call = fake_call
+
+    class Blk:
+        w_gate_up = object()
+    q = torch.arange(10, dtype=torch.float32).view(10, 1)
+    out = tr.dispatch_combine(Blk(), None, (q, torch.ones(10)), torch.zeros(10, 2, dtype=torch.long),
+                              torch.ones(10, 2))
+    assert seen == [4, 4, 2] and torch.equal(out, q)
+    tr.begin_step(3)
+    assert tr.rounds == 1

@@ -96,6 +96,14 @@ DEVI void tmem_st_x32(uint32_t taddr, const uint32_t (&r)[32]) {
       : "memory");
 }
 
+// 2^x on the multi-function unit (PTX ex2.approx.ftz: relative error ~2^-22, -inf -> +0); the
+// probabilities it feeds are rounded to e4m3 next, so its error is far below theirs
+DEVI float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 struct Bars {
   uint64_t q_full;
   uint64_t k_full[STAGES], v_full[STAGES], kv_empty[STAGES];
@@ -287,24 +295,30 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const int key = j * BN + c * 32 + e;
-          sv[c * 32 + e] = (valid && key <= pos && key < L) ? __uint_as_float(u[e]) * scale_log2 : -INFINITY;
+          sv[c * 32 + e] = (valid && key <= pos && key < L) ? __uint_as_float(u[e]) : -INFINITY;
         }
       }
       tc_fence_before();
       mbar_arrive(&bar->s_empty[sb]);               // S buffer free for tile j + 2
-      float mx = -INFINITY;
+      // one warp per scheduler here: eight independent chains instead of one 128-long chain
+      float mx8[8];
 #pragma unroll
-      for (int e = 0; e < BN; ++e) mx = fmaxf(mx, sv[e]);
-      const float m_new = fmaxf(m_run, mx);
+      for (int e = 0; e < 8; ++e) mx8[e] = sv[e];
+#pragma unroll
+      for (int e = 8; e < BN; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], sv[e]);
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      const float m_new = fmaxf(m_run, mx * scale_log2);   // scale > 0: max commutes with it
       const float mref = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = exp2f(m_run - mref);       // m_run = -inf -> 0 (O is still zero)
-      float psum = 0.f;
+      const float alpha = ex2_approx(m_run - mref);  // m_run = -inf -> 0 (O is still zero)
+      float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int e = 0; e < BN; ++e) {
-        const float p = exp2f(sv[e] - mref);
+        const float p = ex2_approx(fmaf(sv[e], scale_log2, -mref));   // masked: ex2(-inf) = 0
         sv[e] = p;
-        psum += p;
+        ps8[e & 7] += p;
       }
+      const float psum = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
       l_run = l_run * alpha + psum;
       m_run = m_new;
       // P / O of the previous tile are free once its PV MMAs are done

@@ -490,6 +490,8 @@ class HybridModel:
         residual stream after each listed layer is appended to `aux_out` (drafter conditioning)."""
         cfg = self.cfg
         eps = cfg.rms_norm_eps
+        if self.ep is not None and hasattr(self.ep.transport, "begin_step"):
+            self.ep.transport.begin_step(int(input_ids.shape[0]))   # EP rounds for this step
         x = self.embed[input_ids.long()]
         residual = None
         h = x

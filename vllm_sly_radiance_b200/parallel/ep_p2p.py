@@ -20,6 +20,7 @@ class P2PTransport:
     def __init__(self, rank: int, world: int, group=None, maxt: int = 256, bn: int = 16):
         self.rank, self.world, self.group = rank, world, group
         self.maxt, self.bn = maxt, bn
+        self.rounds = 1          # transport rounds per MoE call this step (begin_step)
         self.buf = None
         self.calls = 0
         self.opened = []
@@ -54,13 +55,38 @@ class P2PTransport:
         if self.world > 1:
             dist.barrier(group=self.group)
 
+    def begin_step(self, T: int) -> None:
+        """Per forward step, before the first MoE layer: every rank learns the largest token count
+        of the group (one small collective), so all ranks run the same number of transport
+        rounds of at most ``maxt`` tokens each (a prefill chunk larger than the capacity runs as
+        several rounds; ranks with fewer tokens send empty slices)."""
+        if self.world <= 1:
+            self.rounds = max(1, -(-T // self.maxt))
+            return
+        import torch.distributed as dist
+        t = torch.tensor([T], dtype=torch.int64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.group)
+        self.rounds = max(1, -(-int(t.item()) // self.maxt))
+
     def dispatch_combine(self, blk, xb, qs, ids, w):
         q, s = qs
         if q is None or blk.w_gate_up is None:
             raise RuntimeError("the NVLink EP transport needs W4A8 (mxfp4) experts")
         T, K = ids.shape
+        if self.rounds > 1:
+            if T > self.rounds * self.maxt:
+                raise RuntimeError(f"{T} tokens exceed {self.rounds} rounds of {self.maxt}")
+            outs = []
+            for r in range(self.rounds):
+                a, b = min(T, r * self.maxt), min(T, (r + 1) * self.maxt)
+                outs.append(self._call(blk, q[a:b], s[a:b], ids[a:b], w[a:b]))
+            return torch.cat(outs, 0)
         if T > self.maxt:
             raise RuntimeError(f"{T} tokens exceed the EP transport capacity {self.maxt} per call")
+        return self._call(blk, q, s, ids, w)
+
+    def _call(self, blk, q, s, ids, w):
+        T, K = ids.shape
         dev = q.device
         if self.buf is None:
             self._setup(blk.H, K, blk.e_local, dev)
