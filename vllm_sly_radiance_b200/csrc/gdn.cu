@@ -296,8 +296,6 @@ __global__ void __launch_bounds__(2 * D) decode_fused_kernel(
     static_assert(NS == 1, "the fused norm needs the head's outputs in one CTA");
     if (threadIdx.x < D) nw = __bfloat162float(fq.norm_w[threadIdx.x]);
   }
-  pdl_wait();     // inputs come from the preceding kernel
-  pdl_trigger();
   constexpr int TPR = 2 * NS;           // threads per state row
   constexpr int RPC = D / NS;           // state rows of this CTA (blockIdx.z picks which)
   constexpr int HC = D / TPR;           // state columns per thread
@@ -341,8 +339,8 @@ __global__ void __launch_bounds__(2 * D) decode_fused_kernel(
   // ---- conv (threads 0..D-1, one channel of q, k and v each) + SiLU + q/k L2 norm ----
   float in_q[W], in_k[W], in_v[W];
   __nv_bfloat16 *stq = nullptr, *stk = nullptr, *stv = nullptr;
+  const int cq = hk * D + t, ck = key_dim + hk * D + t, cv = 2 * key_dim + h * D + t;
   if (t < D) {
-    const int cq = hk * D + t, ck = key_dim + hk * D + t, cv = 2 * key_dim + h * D + t;
     stq = conv_state + ((size_t)slot * C + cq) * (W - 1);
     stk = conv_state + ((size_t)slot * C + ck) * (W - 1);
     stv = conv_state + ((size_t)slot * C + cv) * (W - 1);
@@ -352,6 +350,13 @@ __global__ void __launch_bounds__(2 * D) decode_fused_kernel(
       in_k[j] = init ? __bfloat162float(stk[j]) : 0.f;
       in_v[j] = init ? __bfloat162float(stv[j]) : 0.f;
     }
+  }
+  // The recurrent and conv states (read above) were last written by this layer's kernel one
+  // step earlier, and the slot tables come with the step's metadata: only the in_proj row below
+  // depends on the kernel before this one, so the state loads overlap that kernel's tail.
+  pdl_wait();
+  pdl_trigger();
+  if (t < D) {
     in_q[W - 1] = __bfloat162float(xr[cq]);
     in_k[W - 1] = __bfloat162float(xr[ck]);
     in_v[W - 1] = __bfloat162float(xr[cv]);

@@ -159,7 +159,10 @@ class MoEBlock:
             order = torch.argsort(key, stable=True)
             st = flat_t[order]
             sw = torch.where(own[order], flat_w[order], torch.zeros_like(flat_w))
-            counts = torch.bincount(key, minlength=self.e_local + 1)[:self.e_local]
+            # scatter-add, not bincount: bincount reads its maximum back to the host, which a
+            # CUDA-graph capture of the decode step cannot contain
+            counts = torch.zeros(self.e_local + 1, dtype=torch.long, device=dev).scatter_add_(
+                0, key, torch.ones_like(key))[:self.e_local]
             q, s = qs
             y = K.moe_grouped_mlp(q[st], s[st], counts, self.w_gate_up, self.w_down, self.I, self.H)
             out = torch.zeros(T, self.H, dtype=torch.float32, device=dev)
