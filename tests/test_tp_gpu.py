@@ -24,6 +24,7 @@ def _worker(rank, world, port, outq):
     import traceback
     # a rank that stops making progress prints its Python stack and exits instead of waiting
     faulthandler.dump_traceback_later(240, exit=True)
+    os.environ["RADIANCE_TS"] = "1"      # the two-shot prefill all-reduce is opt-in: test it
     try:
         _run(rank, world, port, outq)
     except BaseException:

@@ -570,23 +570,28 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
 // epilogue drains the accumulator.  No load is multicast: each CTA's TMA fills its own shared
 // memory and signals the leader's barrier (.cta_group::2 form).
 // ---------------------------------------------------------------------------------------------
-constexpr int P_BN = 256;                                  // tokens per pair tile (MMA N)
-constexpr int P_HALF = 128;                                // tokens staged per CTA
+constexpr int P_WROWS = 2 * BM;                            // weight rows per pair tile (MMA M)
+constexpr int P_BN = 224;                                  // tokens per pair tile (MMA N)
+constexpr int P_HALF = P_BN / 2;                           // tokens staged per CTA
 constexpr int P_W_BYTES = BM * BK;                         // expanded weight tile (16 KB)
-constexpr int P_A_BYTES = P_HALF * BK;                     // this CTA's activation half (16 KB)
+constexpr int P_A_BYTES = P_HALF * BK;                     // this CTA's activation half
 constexpr int P_STAGE = (P_W_BYTES + P_A_BYTES + SF_TILE_BYTES + 1023) / 1024 * 1024;
 constexpr int P_STAGES = (kSmemBudget - 2048) / P_STAGE;
 constexpr int P_SMEM = 1024 + P_STAGES * P_STAGE + 1024;
-constexpr int P_TMEM_COLS = 512;                           // accumulator 256 + SFA + SFB
-constexpr int P_SFA_COL = 256;
-constexpr int P_SFB_COL = 288;                             // 32 columns of UE8M0 1.0
+// TMEM: two accumulators (the epilogue drains one while the MMAs fill the other), then the
+// weight scale factors and 32 columns of UE8M0 1.0 for the activations
+constexpr int P_TMEM_COLS = 512;
+constexpr int P_SFA_COL = 2 * P_BN;
+constexpr int P_SFB_COL = P_SFA_COL + 8;
+static_assert(P_SFB_COL + 32 <= P_TMEM_COLS, "TMEM columns");
+static_assert(P_HALF % 8 == 0, "activation half tile in whole 8-row swizzle atoms");
 static_assert(P_STAGES >= 4, "pair pipeline depth");
 
 struct PairBars {
   uint64_t full[P_STAGES];      // leader: both CTAs' bytes of a stage landed
   uint64_t empty[P_STAGES];     // each CTA: the pair's MMAs have read its stage
-  uint64_t acc_full;            // each CTA: the tile's accumulator is complete
-  uint64_t acc_empty;           // leader: both epilogues drained the accumulator
+  uint64_t acc_full[2];         // each CTA: accumulator b of the tile is complete
+  uint64_t acc_empty[2];        // leader: both epilogues drained accumulator b
   uint32_t tmem;
   int abort;
 };
@@ -596,7 +601,7 @@ __host__ __device__ constexpr uint32_t make_idesc_pair(int sf_id, int wfmt) {
          | (0u << 10)                          // B format: E4M3
          | ((uint32_t)(P_BN >> 3) << 17)       // N >> 3
          | (1u << 23)                          // scale format UE8M0
-         | ((uint32_t)(256 >> 4) << 24)        // M >> 4 (the pair's 256 rows)
+         | ((uint32_t)(P_WROWS >> 4) << 24)    // M >> 4 (the pair's 256 rows)
          | ((uint32_t)sf_id << 29) | ((uint32_t)sf_id << 4);
 }
 
@@ -660,7 +665,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const uint32_t rank = cluster_ctarank();             // 0 = leader (issues the MMAs)
   const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
-  const int n_tiles = (N + P_BN - 1) / P_BN;
+  const int n_tiles = (N + P_WROWS - 1) / P_WROWS;
   const int num_tiles = n_tiles * ((M + P_BN - 1) / P_BN);
   const int k_tiles = Kw / BK;
 
@@ -669,8 +674,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(
       mbar_init(&bars->full[s], 1);
       mbar_init(&bars->empty[s], 1);
     }
-    mbar_init(&bars->acc_full, 1);
-    mbar_init(&bars->acc_empty, 2);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bars->acc_full[b], 1);
+      mbar_init(&bars->acc_empty[b], 2);
+    }
     bars->abort = 0;
     fence_mbar_init();
   }
@@ -714,7 +721,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(
       pdl_wait();
       uint32_t it = 0;
       for (int t = pair; t < num_tiles && !*(volatile int*)&bars->abort; t += npairs) {
-        const int n0 = (t % n_tiles) * P_BN + (int)rank * BM;
+        const int n0 = (t % n_tiles) * P_WROWS + (int)rank * BM;
         const int m0 = (t / n_tiles) * P_BN + (int)rank * P_HALF;
         for (int kt = 0; kt < k_tiles; ++kt, ++it) {
           const int s = it % P_STAGES;
@@ -734,11 +741,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(
     // ---------------- MMA issuer (leader) ----------------
     if (rank == 0 && elect_one()) {
       const uint32_t empty_peer0 = mapa_shared(smem_u32(&bars->empty[0]), 1);
-      const uint32_t accf_peer = mapa_shared(smem_u32(&bars->acc_full), 1);
+      const uint32_t accf_peer0 = mapa_shared(smem_u32(&bars->acc_full[0]), 1);
       uint32_t it = 0, tc = 0;
       bool ok = true;
       for (int t = pair; t < num_tiles && ok; t += npairs, ++tc) {
-        if (!mbar_wait(&bars->acc_empty, (tc & 1) ^ 1, status)) { ok = false; break; }
+        const int ab = tc & 1;                        // accumulator of this tile
+        if (!mbar_wait(&bars->acc_empty[ab], ((tc >> 1) & 1) ^ 1, status)) { ok = false; break; }
         tc_fence_after();
         for (int kt = 0; kt < k_tiles; ++kt, ++it) {
           const int s = it % P_STAGES;
@@ -751,15 +759,16 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(
           tmem_cp_pair_32x128b_warpx4(tmem_sfa, sdesc_plain(smem_u32(st + P_W_BYTES + P_A_BYTES), 0, 128));
 #pragma unroll
           for (int kb = 0; kb < BK / 32; ++kb)
-            mma_mxf8f6f4_pair(tmem_acc, sdesc_sw128(w_addr + kb * 32), sdesc_sw128(a_addr + kb * 32),
+            mma_mxf8f6f4_pair(tmem_acc + (uint32_t)(ab * P_BN), sdesc_sw128(w_addr + kb * 32),
+                              sdesc_sw128(a_addr + kb * 32),
                               make_idesc_pair(kb, wfmt), tmem_sfa | ((uint32_t)kb << 30),
                               tmem_sfb | ((uint32_t)kb << 30), (kt > 0 || kb > 0) ? 1u : 0u);
           commit_pair(smem_u32(&bars->empty[s]));
           commit_pair(empty_peer0 + (uint32_t)(s * sizeof(uint64_t)));
         }
         if (!ok) break;
-        commit_pair(smem_u32(&bars->acc_full));
-        commit_pair(accf_peer);
+        commit_pair(smem_u32(&bars->acc_full[ab]));
+        commit_pair(accf_peer0 + (uint32_t)(ab * sizeof(uint64_t)));
       }
       if (!ok) bars->abort = 1;
     }
@@ -767,15 +776,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(
     // ---------------- epilogue (both CTAs) ----------------
     const int q = warp & 3;
     const int row = q * 32 + lane;
-    const uint32_t acc_empty = mapa_shared(smem_u32(&bars->acc_empty), 0);
-    const uint32_t lane_base = tmem_acc + ((uint32_t)(q * 32) << 16);
+    const uint32_t acc_empty0 = mapa_shared(smem_u32(&bars->acc_empty[0]), 0);
+    const uint32_t lane_base0 = tmem_acc + ((uint32_t)(q * 32) << 16);
     pdl_wait();
     uint32_t tc = 0;
     for (int t = pair; t < num_tiles; t += npairs, ++tc) {
-      const bool got = mbar_wait(&bars->acc_full, tc & 1, status);
+      const int ab = tc & 1;
+      const uint32_t lane_base = lane_base0 + (uint32_t)(ab * P_BN);
+      const bool got = mbar_wait(&bars->acc_full[ab], (tc >> 1) & 1, status);
       if (!got) bars->abort = 1;
       tc_fence_after();
-      const int n = (t % n_tiles) * P_BN + (int)rank * BM + row;
+      const int n = (t % n_tiles) * P_WROWS + (int)rank * BM + row;
       const int mt0 = (t / n_tiles) * P_BN;
       auto store16 = [&](const uint32_t (&r)[16], int c) {
 #pragma unroll
@@ -806,7 +817,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(
       // the accumulator is free for the pair's next tile once all four warps have read it
       tc_fence_before();
       asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (threadIdx.x == 64) mbar_arrive_cluster(acc_empty);
+      if (threadIdx.x == 64) mbar_arrive_cluster(acc_empty0 + (uint32_t)(ab * sizeof(uint64_t)));
       if (*(volatile int*)&bars->abort) break;
     }
   }
@@ -981,7 +992,7 @@ static int launch_pair(const torch::Tensor& a, const torch::Tensor& a_scale, con
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
     return v;
   }();
-  const int tiles = ((N + P_BN - 1) / P_BN) * ((M + P_BN - 1) / P_BN);
+  const int tiles = ((N + P_WROWS - 1) / P_WROWS) * ((M + P_BN - 1) / P_BN);
   const int pairs = std::max(1, std::min(tiles, sms / 2));
   auto kern = gemm_pair_kernel<RS>;
   static bool attr = false;
