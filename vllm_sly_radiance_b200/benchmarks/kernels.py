@@ -117,25 +117,37 @@ def _attn_meta(ctx_lens, bs, Hq, Hkv, splits, dev):
     return m, B * nb
 
 
-def bench_attn(ctxs, splits_list, batch):
-    """Decode attention, Qwen3.8-27B head layout (24 q / 4 kv heads, D=256), fp8 KV cache."""
+def _kv4_random(nblocks, Hkv, bs, D):
+    """A random int4 (KV4) cache: 4-bit codes, then an fp16 (scale, zero) pair per 16 elements."""
+    t = torch.randint(0, 256, (nblocks, Hkv, bs, D // 2 + D // 4), dtype=torch.uint8, device="cuda")
+    sz = torch.tensor([0.05, -0.4], dtype=torch.float16, device="cuda").view(torch.uint8)
+    t[..., D // 2:] = sz.repeat(D // 16)
+    return t
+
+
+def bench_attn(ctxs, splits_list, batch, kv: str = "fp8"):
+    """Decode attention, Qwen3.8-27B head layout (24 q / 4 kv heads, D=256), fp8 or int4 KV."""
     bw, _, src = peaks()
     Hq, Hkv, D, bs = 24, 4, 256, 64
+    row_bytes = D if kv == "fp8" else D // 2 + D // 4
     for ctx in ctxs:
         for sp in splits_list:
             for dec in (True, False):
                 meta, nblocks = _attn_meta([ctx] * batch, bs, Hq, Hkv, sp, "cuda")
-                kc = (torch.randn(nblocks, Hkv, bs, D, device="cuda") * 0.5).to(torch.float8_e4m3fn)
-                vc = torch.randn(nblocks, Hkv, bs, D, device="cuda").to(torch.float8_e4m3fn)
+                if kv == "fp8":
+                    kc = (torch.randn(nblocks, Hkv, bs, D, device="cuda") * 0.5).to(torch.float8_e4m3fn)
+                    vc = torch.randn(nblocks, Hkv, bs, D, device="cuda").to(torch.float8_e4m3fn)
+                else:
+                    kc, vc = _kv4_random(nblocks, Hkv, bs, D), _kv4_random(nblocks, Hkv, bs, D)
                 q = torch.randn(batch, Hq, D, device="cuda").to(torch.bfloat16)
                 K._ATTN_DECODE = dec
 
                 def fn(i):
                     K.paged_attention(q, kc, vc, meta, D ** -0.5)
                 t = timeit(fn)
-                byts = batch * (ctx + 1) * Hkv * D * 2
+                byts = batch * (ctx + 1) * Hkv * row_bytes * 2
                 print(json.dumps({"kernel": "paged_attention", "variant": "decode" if dec else "general",
-                                  "batch": batch, "ctx": ctx, "splits": sp,
+                                  "kv": kv, "batch": batch, "ctx": ctx, "splits": sp,
                                   "us": round(t * 1e6, 2), "GBps": round(byts / t / 1e9, 1),
                                   "frac_hbm": round(byts / t / bw, 3), "peaks": src}), flush=True)
     K._ATTN_DECODE = True
@@ -332,6 +344,7 @@ def main():
     ap.add_argument("--ctx", default="1500,4096,16384")
     ap.add_argument("--splits", default="1,4,8,17,32")
     ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--kv", default="fp8", choices=["fp8", "int4"])
     ap.add_argument("--m", default="1,8,16,64,256,1024,4096")
     ap.add_argument("--shape", default="",
                     help="comma list of shape names or NxK (default: all named shapes)")
@@ -353,7 +366,7 @@ def main():
         bench_w4a16([m for m in ms if m <= 8] or [1], shapes)
     elif a.what == "attn":
         bench_attn([int(v) for v in a.ctx.split(",")], [int(v) for v in a.splits.split(",")],
-                   a.batch)
+                   a.batch, a.kv)
     elif a.what == "gemm_fin":
         bench_gemm_finish([m for m in ms if m <= 16] or [1],
                           [sh for sh in shapes if sh[2] in ("out_proj", "gate_up", "down")] or shapes)

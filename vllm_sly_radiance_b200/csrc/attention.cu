@@ -682,6 +682,34 @@ __global__ void __launch_bounds__(128) paged_attn_decode_kernel(
   if constexpr (FMT == 1) {
     if (t_lo < t_hi) load_raw(t_lo);
   }
+  // int4 cache (4-bit codes + fp16 scale / zero per 16 elements): same one-tile-ahead prefetch
+  constexpr int RB4 = D / 2 + D / 4;
+  constexpr int IT4 = BC * D / 16 / 128;
+  uint2 knib[FMT == 2 ? IT4 : 1], vnib[FMT == 2 ? IT4 : 1];
+  __half2 kmz[FMT == 2 ? IT4 : 1], vmz[FMT == 2 ? IT4 : 1];
+  auto load_nib = [&](int kt) {
+    if constexpr (FMT == 2) {
+#pragma unroll
+      for (int it = 0; it < IT4; ++it) {
+        const int idx = threadIdx.x + it * 128;
+        const int r = idx / (D / 16), g = idx % (D / 16);
+        const int key = kt * BC + r;
+        knib[it] = vnib[it] = make_uint2(0, 0);
+        kmz[it] = vmz[it] = __floats2half2_rn(0.f, 0.f);
+        if (key < L) {
+          const int blk = block_tables[(size_t)b * bt_stride + key / block_size];
+          const size_t row = (((size_t)blk * Hkv + hk) * block_size + key % block_size) * RB4;
+          knib[it] = __ldg(reinterpret_cast<const uint2*>(k_cache + row + g * 8));
+          vnib[it] = __ldg(reinterpret_cast<const uint2*>(v_cache + row + g * 8));
+          kmz[it] = *reinterpret_cast<const __half2*>(k_cache + row + D / 2 + g * 4);
+          vmz[it] = *reinterpret_cast<const __half2*>(v_cache + row + D / 2 + g * 4);
+        }
+      }
+    }
+  };
+  if constexpr (FMT == 2) {
+    if (t_lo < t_hi) load_nib(t_lo);
+  }
 
   // ---- Q (16 rows; rows past R are zero) ----
   for (int idx = threadIdx.x; idx < QR * CH; idx += 128) {
@@ -720,7 +748,6 @@ __global__ void __launch_bounds__(128) paged_attn_decode_kernel(
     const int key0 = kt * BC;
     if constexpr (FMT == 1) {
       constexpr int IT = IT1;
-      if (kt != t_lo) load_raw(kt);
 #pragma unroll
       for (int it = 0; it < IT; ++it) {
         const int idx = threadIdx.x + it * 128;
@@ -738,27 +765,10 @@ __global__ void __launch_bounds__(128) paged_attn_decode_kernel(
         *reinterpret_cast<uint4*>(sV + swz(r, 2 * c16, CH)) = make_uint4(vw[0], vw[1], vw[2], vw[3]);
         *reinterpret_cast<uint4*>(sV + swz(r, 2 * c16 + 1, CH)) = make_uint4(vw[4], vw[5], vw[6], vw[7]);
       }
+      // the next tile's bytes travel while this tile's products run (one tile in flight ahead)
+      if (kt + 1 < t_hi) load_raw(kt + 1);
     } else if constexpr (FMT == 2) {
-      constexpr int RB = D / 2 + D / 4;
-      constexpr int IT = BC * D / 16 / 128;
-      uint2 knib[IT], vnib[IT];
-      __half2 kmz[IT], vmz[IT];
-#pragma unroll
-      for (int it = 0; it < IT; ++it) {
-        const int idx = threadIdx.x + it * 128;
-        const int r = idx / (D / 16), g = idx % (D / 16);
-        const int key = key0 + r;
-        knib[it] = vnib[it] = make_uint2(0, 0);
-        kmz[it] = vmz[it] = __floats2half2_rn(0.f, 0.f);
-        if (key < L) {
-          const int blk = block_tables[(size_t)b * bt_stride + key / block_size];
-          const size_t row = (((size_t)blk * Hkv + hk) * block_size + key % block_size) * RB;
-          knib[it] = __ldg(reinterpret_cast<const uint2*>(k_cache + row + g * 8));
-          vnib[it] = __ldg(reinterpret_cast<const uint2*>(v_cache + row + g * 8));
-          kmz[it] = *reinterpret_cast<const __half2*>(k_cache + row + D / 2 + g * 4);
-          vmz[it] = *reinterpret_cast<const __half2*>(v_cache + row + D / 2 + g * 4);
-        }
-      }
+      constexpr int IT = IT4;
 #pragma unroll
       for (int it = 0; it < IT; ++it) {
         const int idx = threadIdx.x + it * 128;
@@ -783,6 +793,7 @@ __global__ void __launch_bounds__(128) paged_attn_decode_kernel(
         *reinterpret_cast<uint4*>(sV + swz(r, 2 * g, CH)) = make_uint4(vw[0], vw[1], vw[2], vw[3]);
         *reinterpret_cast<uint4*>(sV + swz(r, 2 * g + 1, CH)) = make_uint4(vw[4], vw[5], vw[6], vw[7]);
       }
+      if (kt + 1 < t_hi) load_nib(kt + 1);
     } else {
       const __nv_bfloat16* kc = reinterpret_cast<const __nv_bfloat16*>(k_cache);
       const __nv_bfloat16* vc = reinterpret_cast<const __nv_bfloat16*>(v_cache);
