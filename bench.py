@@ -508,6 +508,8 @@ def moe_workload(args, rank, world, dist):
         eng.step()
     for _ in range(args.warmup):
         eng.step()
+    if args.kernel_profile and rank == 0 and world == 1:
+        profiled_launches(eng, args.kernel_profile)       # one (untimed) decode step's kernels
     if dist is not None:
         dist.barrier()
     n = [0]
