@@ -394,16 +394,23 @@ def test_paged_attention_decode_kernel(D, Hq, Hkv, ctx_lens, splits, fmt, monkey
     assert rel_err(got, general) < 1e-2, rel_err(got, general)
 
 
+@pytest.mark.parametrize("kv", ["fp8", "int4"])
 @pytest.mark.parametrize("q_lens,ctx_lens", [([256], [0]), ([300, 77], [1000, 40]),
                                             ([130], [5000]), ([1024], [3000])])
-def test_fmha_prefill_tcgen05(q_lens, ctx_lens, monkeypatch):
+def test_fmha_prefill_tcgen05(q_lens, ctx_lens, kv, monkeypatch):
     """Causal chunked-prefill attention on tcgen05 (e4m3 QK and P V legs, TMEM accumulators,
-    TMA-fed fp8 pages) against the fp32 oracle and the mma.sync tile kernel, GQA 6, head 256."""
+    TMA-fed fp8 pages) against the fp32 oracle and the mma.sync tile kernel, GQA 6, head 256.
+    A 4-bit cache reaches the kernel through its pages dequantised into e4m3 copies."""
+    from vllm_sly_radiance_b200.quant.formats import kv4_quantize
     torch.manual_seed(21)
     D, Hq, Hkv, bs = 256, 24, 4, 64
     meta, nblocks = _attn_meta(q_lens, ctx_lens, bs, Hq, Hkv, 1, DEV)
-    k = (torch.randn(nblocks, Hkv, bs, D) * 0.5).to(torch.float8_e4m3fn)
-    v = torch.randn(nblocks, Hkv, bs, D).to(torch.float8_e4m3fn)
+    if kv == "fp8":
+        k = (torch.randn(nblocks, Hkv, bs, D) * 0.5).to(torch.float8_e4m3fn)
+        v = torch.randn(nblocks, Hkv, bs, D).to(torch.float8_e4m3fn)
+    else:
+        k = kv4_quantize(torch.randn(nblocks, Hkv, bs, D) * 0.5)
+        v = kv4_quantize(torch.randn(nblocks, Hkv, bs, D))
     T = sum(q_lens)
     q = ref.fp8_e4m3(torch.randn(T, Hq, D)).to(torch.bfloat16)
     scale = D ** -0.5
@@ -416,8 +423,9 @@ def test_fmha_prefill_tcgen05(q_lens, ctx_lens, monkeypatch):
     torch.cuda.synchronize()
     K.check_status(got.device)
     assert rel_err(tile, want) < 2e-2
-    # P and V on the e4m3 leg: a few percent of the row maximum
-    assert rel_err(got, want) < 5e-2, rel_err(got, want)
+    # P and V on the e4m3 leg: a few percent of the row maximum (the 4-bit cache's dequantised
+    # K / V take one more e4m3 rounding)
+    assert rel_err(got, want) < (5e-2 if kv == "fp8" else 7e-2), rel_err(got, want)
 
 
 @pytest.mark.parametrize("Hq,Hkv,ctx_lens,splits", [(24, 4, [1500], 8), (24, 4, [300, 2000, 64], 1),
@@ -601,9 +609,12 @@ def test_qkv_prologue():
     assert torch.equal(vcg.cpu().float(), vc.float())
 
 
-def test_gdn_conv_and_recurrent():
+@pytest.mark.parametrize("Dh", [64, 128])
+def test_gdn_conv_and_recurrent(Dh):
+    """Varlen conv (head 64: per-token kernel; head 128: the token-tiled prefill kernel, whose
+    8-token tiles here straddle sequence boundaries) and the recurrent rule against the oracle."""
     torch.manual_seed(2)
-    Hk, Hv, Dh, W = 2, 4, 64, 4
+    Hk, Hv, W = 2, 4, 4
     key_dim, vdim = Hk * Dh, Hv * Dh
     C = 2 * key_dim + vdim
     q_lens = [1, 5, 70]

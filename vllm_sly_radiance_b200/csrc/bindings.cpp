@@ -81,6 +81,9 @@ void mxfp4_gemm_fin(torch::Tensor a, torch::Tensor a_scale, torch::Tensor wp, to
                     torch::Tensor out, int64_t fin_mode, torch::Tensor res, torch::Tensor w,
                     torch::Tensor res_out, torch::Tensor q, torch::Tensor scale, double eps,
                     torch::Tensor ws, torch::Tensor status);
+void kv4_to_e4m3_pages(torch::Tensor k4, torch::Tensor v4, torch::Tensor block_tables,
+                       torch::Tensor seq_lens, torch::Tensor k8, torch::Tensor v8,
+                       torch::Tensor bt_out);
 void fmha_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                   torch::Tensor block_tables, torch::Tensor seq_lens, torch::Tensor qsl,
                   torch::Tensor tile_seq, torch::Tensor tile_row0, double scale, torch::Tensor out,
@@ -194,6 +197,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed_gather", &rad::embed_gather, "int8 / int4-g128 embedding lookup into bf16 rows");
   m.def("mxfp4_gemm_fin", &rad::mxfp4_gemm_fin,
         "decode W4A8 GEMM whose last CTA also runs the next linear's producer over the rows");
+  m.def("kv4_to_e4m3_pages", &rad::kv4_to_e4m3_pages,
+        "dequantise the 4-bit KV pages a prefill chunk reaches into compact e4m3 pages");
   m.def("fmha_prefill", &rad::fmha_prefill,
         "causal prefill attention on tcgen05 (e4m3 QK and PV, TMEM accumulators, paged fp8 KV)");
   m.def("mxfp4_gemm_act", &rad::mxfp4_gemm_act,

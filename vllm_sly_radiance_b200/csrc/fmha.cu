@@ -381,6 +381,52 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
   }
 }
 
+
+// ---------------------------------------------------------------------------------------------
+// int4 (KV4) pages -> e4m3 pages for the prefill kernel.  A 4-bit cache row is D/2 code bytes
+// (low nibble = even element) and one fp16 (scale, zero) pair per 16 elements: v = code * scale
+// + zero.  Before a prefill chunk attends over such a cache, every page its sequences reach is
+// dequantised once into a compact e4m3 copy (pages renumbered per sequence), and the tcgen05
+// kernel runs on that copy.  The copy costs one read of the 4-bit pages and one e4m3 write per
+// chunk and layer -- small next to the chunk's attention over the same keys.
+// grid (table width, sequences, kv heads); thread t converts 16-element groups of one page.
+// ---------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) kv4_to_e4m3_pages_kernel(
+    const uint8_t* __restrict__ k4, const uint8_t* __restrict__ v4,
+    const int* __restrict__ block_tables, int bt_stride, const int* __restrict__ seq_lens,
+    int Hkv, uint8_t* __restrict__ k8, uint8_t* __restrict__ v8, int* __restrict__ bt_out) {
+  pdl_wait();     // the chunk's keys were written by the preceding prologue
+  pdl_trigger();
+  constexpr int RB = D / 2 + D / 4;              // 4-bit row bytes (codes + fp16 pairs)
+  constexpr int G = D / 16;                      // 16-element groups per row
+  const int p = blockIdx.x, b = blockIdx.y, hk = blockIdx.z;
+  const int pages = (seq_lens[b] + PAGE - 1) / PAGE;
+  if (p >= pages) return;
+  int dst = p;
+  for (int i = 0; i < b; ++i) dst += (seq_lens[i] + PAGE - 1) / PAGE;
+  const int src = block_tables[(size_t)b * bt_stride + p];
+  if (hk == 0 && threadIdx.x == 0) bt_out[(size_t)b * bt_stride + p] = dst;
+  const size_t s_off = ((size_t)src * Hkv + hk) * PAGE * RB;
+  const size_t d_off = ((size_t)dst * Hkv + hk) * PAGE * D;
+  for (int idx = threadIdx.x; idx < 2 * PAGE * G; idx += blockDim.x) {
+    const int which = idx / (PAGE * G), rem = idx % (PAGE * G);
+    const int r = rem / G, g = rem % G;
+    const uint8_t* row = (which ? v4 : k4) + s_off + (size_t)r * RB;
+    const uint2 codes = *reinterpret_cast<const uint2*>(row + g * 8);
+    const __half2 sz = *reinterpret_cast<const __half2*>(row + D / 2 + g * 4);
+    const float sc = __low2float(sz), zr = __high2float(sz);
+    uint16_t o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const uint32_t word = e < 4 ? codes.x : codes.y;
+      const int sh = (e % 4) * 8;
+      o[e] = f32x2_to_e4m3x2((float)((word >> sh) & 0xF) * sc + zr,
+                             (float)((word >> (sh + 4)) & 0xF) * sc + zr);
+    }
+    *reinterpret_cast<uint4*>((which ? v8 : k8) + d_off + (size_t)r * D + g * 16) =
+        *reinterpret_cast<const uint4*>(o);
+  }
+}
 }  // namespace fmha
 
 static std::mutex g_fmha_mu;
@@ -435,6 +481,32 @@ void fmha_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                             seq_lens.data_ptr<int>(), qsl.data_ptr<int>(), tile_seq.data_ptr<int>(),
                             tile_row0.data_ptr<int>(), num_tiles, Hq, Hkv,
                             (float)(scale * 1.4426950408889634), (__nv_bfloat16*)out.data_ptr(), st));
+}
+
+// int4 caches [blocks, Hkv, 64, D/2 + D/4] -> compact e4m3 pages k8 / v8 [>= sum of pages, Hkv,
+// 64, D] for the sequences of the batch, with their renumbered block table in bt_out (same shape
+// as block_tables).
+void kv4_to_e4m3_pages(torch::Tensor k4, torch::Tensor v4, torch::Tensor block_tables,
+                       torch::Tensor seq_lens, torch::Tensor k8, torch::Tensor v8,
+                       torch::Tensor bt_out) {
+  using namespace fmha;
+  const int B = block_tables.size(0), nb = block_tables.size(1), Hkv = k4.size(1);
+  TORCH_CHECK(k4.scalar_type() == at::kByte && v4.scalar_type() == at::kByte && k4.dim() == 4 &&
+                  k4.size(2) == PAGE && k4.size(3) == D / 2 + D / 4 && k4.is_contiguous() &&
+                  v4.is_contiguous(), "kv4_to_e4m3_pages: 4-bit cache [blocks, Hkv, 64, 192]");
+  TORCH_CHECK(k8.scalar_type() == at::kFloat8_e4m3fn && v8.scalar_type() == at::kFloat8_e4m3fn &&
+                  k8.size(1) == Hkv && k8.size(2) == PAGE && k8.size(3) == D && k8.is_contiguous() &&
+                  v8.is_contiguous() && k8.size(0) >= (int64_t)B * nb, "kv4_to_e4m3_pages: e4m3 pages");
+  TORCH_CHECK(bt_out.sizes() == block_tables.sizes() && bt_out.stride(0) == block_tables.stride(0) &&
+                  bt_out.scalar_type() == at::kInt, "kv4_to_e4m3_pages: block table");
+  if (B == 0 || nb == 0) return;
+  const at::cuda::CUDAGuard guard(k4.device());
+  C10_CUDA_CHECK(launch_pdl(kv4_to_e4m3_pages_kernel, dim3(nb, B, Hkv), dim3(256), 0,
+                            at::cuda::getCurrentCUDAStream(), (const uint8_t*)k4.data_ptr(),
+                            (const uint8_t*)v4.data_ptr(), block_tables.data_ptr<int>(),
+                            (int)block_tables.stride(0), seq_lens.data_ptr<int>(), Hkv,
+                            (uint8_t*)k8.data_ptr(), (uint8_t*)v8.data_ptr(),
+                            bt_out.data_ptr<int>()));
 }
 
 }  // namespace rad

@@ -98,6 +98,97 @@ __global__ void __launch_bounds__(256) conv_kernel(
     y[(size_t)t * ldy + chunk * D + lane * PER + p] = __float2bfloat16_rn(acc[p]);
 }
 
+// Prefill conv, token-tiled: a warp owns one D-channel chunk of TT consecutive tokens; lane l
+// keeps 4 channels.  The TT + W - 1 input rows the tile reads are loaded once (8-byte vectors)
+// and slide through the W taps, instead of every output re-reading its W inputs; taps are fetched
+// before the dependency wait.  Rows of another sequence (varlen batches) come from the sequence's
+// saved conv state, as in conv_kernel.
+template <int D, int W, int TT>
+__global__ void __launch_bounds__(256) conv_tile_kernel(
+    const __nv_bfloat16* __restrict__ x, int ldx, const __nv_bfloat16* __restrict__ w,
+    const __nv_bfloat16* __restrict__ conv_state, const int* __restrict__ qsl,
+    const int* __restrict__ slots, const int* __restrict__ has_init, const int* __restrict__ tok_seq,
+    int T, int C, int qk_dim, __nv_bfloat16* __restrict__ y, int ldy, float eps) {
+  static_assert(D == 128 && W == 4, "4 channels per lane, 4 taps");
+  const int chunk = blockIdx.y * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int c0 = chunk * D + lane * 4;
+  const bool live = chunk * D < C;
+  float wt[4][W];                       // [channel][tap]
+  if (live) {
+    const uint4 wa = *reinterpret_cast<const uint4*>(w + (size_t)c0 * W);
+    const uint4 wb = *reinterpret_cast<const uint4*>(w + (size_t)c0 * W + 8);
+    const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&wa);
+    const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&wb);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 fa = __bfloat1622float2(ha[e]), fb = __bfloat1622float2(hb[e]);
+      wt[e / 2][(e % 2) * 2] = fa.x;
+      wt[e / 2][(e % 2) * 2 + 1] = fa.y;
+      wt[2 + e / 2][(e % 2) * 2] = fb.x;
+      wt[2 + e / 2][(e % 2) * 2 + 1] = fb.y;
+    }
+  }
+  pdl_wait();     // the in_proj output comes from the preceding kernel
+  pdl_trigger();
+  if (!live) return;
+  const int t0 = blockIdx.x * TT;
+  // rows t0 - (W - 1) .. t0 + TT - 1 (clamped; a clamped row is never used as a same-sequence input)
+  float xr[TT + W - 1][4];
+#pragma unroll
+  for (int j = 0; j < TT + W - 1; ++j) {
+    const int r = min(max(t0 - (W - 1) + j, 0), T - 1);
+    const uint2 u = *reinterpret_cast<const uint2*>(x + (size_t)r * ldx + c0);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    const float2 a = __bfloat1622float2(h[0]), b2 = __bfloat1622float2(h[1]);
+    xr[j][0] = a.x; xr[j][1] = a.y; xr[j][2] = b2.x; xr[j][3] = b2.y;
+  }
+  const bool qk = chunk * D < qk_dim;
+#pragma unroll
+  for (int k = 0; k < TT; ++k) {
+    const int t = t0 + k;
+    if (t >= T) break;                  // uniform across the warp
+    const int b = tok_seq[t];
+    const int i = t - qsl[b];           // position within the sequence's tokens of this step
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < W; ++j) {
+      const int src = i + j - (W - 1);
+      float v[4];
+      if (src >= 0) {
+#pragma unroll
+        for (int p = 0; p < 4; ++p) v[p] = xr[k + j][p];
+      } else {
+        const bool init = has_init[b] != 0;
+        const int slot = slots[b];
+#pragma unroll
+        for (int p = 0; p < 4; ++p)
+          v[p] = init ? __bfloat162float(conv_state[((size_t)slot * C + c0 + p) * (W - 1) + (W - 1 + src)])
+                      : 0.f;
+      }
+#pragma unroll
+      for (int p = 0; p < 4; ++p) acc[p] += v[p] * wt[p][j];
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      acc[p] = acc[p] / (1.f + __expf(-acc[p]));
+      ss += acc[p] * acc[p];
+    }
+    if (qk) {
+      ss = warp_sum(ss);
+      const float r = rsqrtf(ss + eps);
+#pragma unroll
+      for (int p = 0; p < 4; ++p) acc[p] *= r;
+    }
+    uint2 o;
+    __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+    oh[0] = __floats2bfloat162_rn(acc[0], acc[1]);
+    oh[1] = __floats2bfloat162_rn(acc[2], acc[3]);
+    *reinterpret_cast<uint2*>(y + (size_t)t * ldy + c0) = o;
+  }
+}
+
 // new state for each sequence = the last W-1 inputs of concat(old_state, x_seq[:n_commit])
 template <int W>
 __global__ void conv_state_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
@@ -520,6 +611,21 @@ void gdn_conv(torch::Tensor x, torch::Tensor w, torch::Tensor conv_state, torch:
   const at::cuda::CUDAGuard guard(x.device());
   auto stream = at::cuda::getCurrentCUDAStream();
   const int chunks = C / head_dim;
+  if (!update_state && head_dim == 128 && T > 1 && (x.stride(0) % 4) == 0 &&
+      (y.stride(0) % 4) == 0 && (reinterpret_cast<uintptr_t>(x.data_ptr()) % 8) == 0 &&
+      (reinterpret_cast<uintptr_t>(y.data_ptr()) % 8) == 0 &&
+      (reinterpret_cast<uintptr_t>(w.data_ptr()) % 16) == 0) {
+    // prefill: token tiles of 8 (each input row loaded once per tile)
+    constexpr int TT = 8;
+    C10_CUDA_CHECK(launch_pdl((gdn::conv_tile_kernel<128, 4, TT>), dim3((T + TT - 1) / TT, (chunks + 7) / 8),
+        dim3(256), 0, stream, (const __nv_bfloat16*)x.data_ptr(), (int)x.stride(0),
+        (const __nv_bfloat16*)w.data_ptr(), (const __nv_bfloat16*)conv_state.data_ptr(),
+        qsl.data_ptr<int>(), slots.data_ptr<int>(), has_init.data_ptr<int>(),
+        tok_seq.data_ptr<int>(), T, C, (int)qk_dim, (__nv_bfloat16*)y.data_ptr(), (int)y.stride(0),
+        (float)eps));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   dim3 grid(T, (chunks + 7) / 8);
   auto run = [&](auto dtag) {
     constexpr int D = decltype(dtag)::value;
