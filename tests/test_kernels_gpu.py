@@ -630,6 +630,7 @@ def test_gdn_conv_and_recurrent(Dh):
     dt_bias = torch.randn(Hv) * 0.1
     m = _Meta()
     m.num_seqs = 3
+    m.num_tokens = T
     m.query_start_loc = torch.tensor(qsl, dtype=torch.int32)
     m.state_slots = torch.tensor(slots, dtype=torch.int32)
     m.has_initial = torch.tensor(has_init, dtype=torch.int32)
@@ -638,6 +639,7 @@ def test_gdn_conv_and_recurrent(Dh):
     for k_ in ("query_start_loc", "state_slots", "has_initial", "token_seq"):
         setattr(mg, k_, getattr(m, k_).to(DEV))
     mg.num_seqs = 3
+    mg.num_tokens = T
     y_w = K.gdn_conv(x[:, :C], conv_w, conv_state, m, key_dim, Dh)
     y_g = K.gdn_conv(x.to(DEV)[:, :C], conv_w.to(DEV), conv_state.to(DEV), mg, key_dim, Dh)
     torch.cuda.synchronize()
@@ -650,7 +652,8 @@ def test_gdn_conv_and_recurrent(Dh):
                           Dh ** -0.5)
     torch.cuda.synchronize()
     assert rel_err(o_g, o_w) < 2e-2
-    assert rel_err(ssm_g, ssm_w) < 1e-3
+    # head 128 takes the chunked (tensor-core) scan: bf16 operands, a few 1e-3 of the state
+    assert rel_err(ssm_g, ssm_w) < (1e-3 if Dh == 64 else 3e-2)
     cs_w = conv_state.clone()
     K.gdn_conv_state_update(x[:, :C], cs_w, m)
     cs_g = conv_state.clone().to(DEV)
