@@ -22,7 +22,8 @@
 //  * K and V pages arrive by TMA (two 64-key pages x two 128-byte halves per 128-key tile) into a
 //    two-stage ring; all waits are bounded (status word).
 //  * Causal tiles are scheduled heaviest first: CTA x takes row tile (last - x).
-// Warp roles (192 threads): warps 0-3 softmax + epilogue, warp 4 TMA producer, warp 5 MMA issuer.
+// Warp roles (320 threads): warps 0-7 softmax + epilogue (two threads per query row), warp 8 TMA
+// producer, warp 9 MMA issuer.
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -48,8 +49,10 @@ constexpr int Q_BYTES = 2 * HALF;
 constexpr int KV_BYTES = 2 * HALF;
 constexpr int P_BYTES = BM * BN;
 constexpr int STAGES = 2;
-constexpr int kThreads = 192;
-constexpr int SMEM_BYTES = 1024 + Q_BYTES + STAGES * 2 * KV_BYTES + P_BYTES + 1024;
+constexpr int kSoftThreads = 256;      // softmax / epilogue warps 0-7
+constexpr int kTmaWarp = 8, kMmaWarp = 9;
+constexpr int kThreads = kSoftThreads + 64;
+constexpr int SMEM_BYTES = 1024 + Q_BYTES + STAGES * 2 * KV_BYTES + P_BYTES + 4096;   // + barriers
 constexpr uint32_t O_COL = 0, S_COL = 256;      // TMEM: O [0, 256), S buffers [256, 384), [384, 512)
 
 // kind::f8f6f4 instruction descriptor: e4m3 x e4m3 -> fp32, M = 128
@@ -109,9 +112,12 @@ struct Bars {
   uint64_t k_full[STAGES], v_full[STAGES], kv_empty[STAGES];
   uint64_t s_full[2], s_empty[2];
   uint64_t p_full, pv_done;
+  float row_max[2][2][BM];      // [S buffer][half][row]: the halves' partial row maxima
+  float row_sum[2][BM];         // [half][row]: the halves' final sums
   uint32_t tmem_slot;
   int abort;
 };
+static_assert(sizeof(Bars) <= 4096, "barrier block");
 
 __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
     const __grid_constant__ CUtensorMap tmap_k, const __grid_constant__ CUtensorMap tmap_v,
@@ -146,7 +152,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
-    mbar_init(&bar->q_full, 128);
+    mbar_init(&bar->q_full, kSoftThreads);
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&bar->k_full[s], 1);
       mbar_init(&bar->v_full[s], 1);
@@ -154,18 +160,18 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&bar->s_full[s], 1);
-      mbar_init(&bar->s_empty[s], 128);
+      mbar_init(&bar->s_empty[s], kSoftThreads);
     }
-    mbar_init(&bar->p_full, 128);
+    mbar_init(&bar->p_full, kSoftThreads);
     mbar_init(&bar->pv_done, 1);
     bar->abort = 0;
     fence_mbar_init();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == kTmaWarp && lane == 0) {
     tma_prefetch_desc(&tmap_k);
     tma_prefetch_desc(&tmap_v);
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tmem_alloc(&bar->tmem_slot, 512);
     tmem_relinquish();
   }
@@ -174,7 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
   tc_fence_after();
   const uint32_t tmem = bar->tmem_slot;
 
-  if (warp == 4) {
+  if (warp == kTmaWarp) {
     // ---------------- TMA producer: K and V pages of each 128-key tile ----------------
     if (elect_one()) {
       const int* bt = block_tables + (size_t)b * bt_stride;
@@ -203,7 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
         }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
     if (elect_one()) {
       bool ok = mbar_wait(&bar->q_full, 0, status);
@@ -245,18 +251,22 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
       if (!ok) bar->abort = 1;
     }
   } else {
-    // ---------------- softmax + epilogue (warp w owns TMEM lanes 32w..32w+31 = rows) ----------
-    const int r = threadIdx.x;                         // row within the tile
+    // ---------------- softmax + epilogue: two threads per query row ----------------
+    // warp w owns TMEM lanes 32 (w % 4) .. + 31 (the rows); half hf = w / 4 takes key columns
+    // [64 hf, 64 hf + 64) of each S tile and O columns [128 hf, 128 hf + 128).  The halves swap
+    // their row maxima through shared memory once per tile; each keeps its own running sum.
+    const int hf = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;              // row within the tile
     const int rr = row0 + r;
     const bool valid = rr < R;
     const int i = valid ? rr / G : 0;
     const int head = hk * G + (valid ? rr % G : 0);
     const int pos = L - ql + i;
-    // Q row -> e4m3, two swizzled 128-byte halves
+    // Q row -> e4m3, this half's 128-byte half of the two swizzled halves
     {
       const __nv_bfloat16* src = q + ((size_t)(s0 + i) * Hq + head) * D;
 #pragma unroll 4
-      for (int c = 0; c < D / 16; ++c) {
+      for (int c = hf * 8; c < hf * 8 + 8; ++c) {
         uint4 w = make_uint4(0, 0, 0, 0);
         if (valid) {
           const uint4 u0 = reinterpret_cast<const uint4*>(src)[2 * c];
@@ -279,41 +289,52 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
     fence_proxy_async();
     mbar_arrive(&bar->q_full);
 
-    float m_run = -INFINITY, l_run = 0.f;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    constexpr int HC = BN / 2;                         // key columns per half
+    float m_run = -INFINITY, l_run = 0.f;              // l_run: this half's share of the sum
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    // Every softmax thread runs all nt iterations and reaches each named barrier: a failed wait
+    // only turns the rest of the work off (ok is warp-uniform), so no barrier is left short.
     bool ok = true;
     for (int j = 0; j < nt; ++j) {
       const int sb = j & 1;
-      if (!mbar_wait(&bar->s_full[sb], (j >> 1) & 1, status)) { ok = false; break; }
-      tc_fence_after();
-      float sv[BN];
+      if (ok) ok = mbar_wait(&bar->s_full[sb], (j >> 1) & 1, status);
+      ok = __all_sync(0xffffffffu, ok);
+      float sv[HC];
+      if (ok) {
+        tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t u[32];
-        tmem_ld_x32(tmem + lane_base + S_COL + sb * BN + c * 32, u);
-        tmem_ld_wait();
+        for (int c = 0; c < HC / 32; ++c) {
+          uint32_t u[32];
+          tmem_ld_x32(tmem + lane_base + S_COL + sb * BN + hf * HC + c * 32, u);
+          tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int key = j * BN + c * 32 + e;
-          sv[c * 32 + e] = (valid && key <= pos && key < L) ? __uint_as_float(u[e]) : -INFINITY;
+          for (int e = 0; e < 32; ++e) {
+            const int key = j * BN + hf * HC + c * 32 + e;
+            sv[c * 32 + e] = (valid && key <= pos && key < L) ? __uint_as_float(u[e]) : -INFINITY;
+          }
         }
+        tc_fence_before();
+        mbar_arrive(&bar->s_empty[sb]);             // S buffer free for tile j + 2
+      } else {
+#pragma unroll
+        for (int e = 0; e < HC; ++e) sv[e] = -INFINITY;
       }
-      tc_fence_before();
-      mbar_arrive(&bar->s_empty[sb]);               // S buffer free for tile j + 2
-      // one warp per scheduler here: eight independent chains instead of one 128-long chain
       float mx8[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) mx8[e] = sv[e];
 #pragma unroll
-      for (int e = 8; e < BN; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], sv[e]);
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      for (int e = 8; e < HC; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], sv[e]);
+      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      bar->row_max[sb][hf][r] = mx;
+      asm volatile("bar.sync 1, %0;" ::"n"(kSoftThreads) : "memory");
+      mx = fmaxf(mx, bar->row_max[sb][hf ^ 1][r]);
       const float m_new = fmaxf(m_run, mx * scale_log2);   // scale > 0: max commutes with it
       const float mref = m_new == -INFINITY ? 0.f : m_new;
       const float alpha = ex2_approx(m_run - mref);  // m_run = -inf -> 0 (O is still zero)
       float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int e = 0; e < BN; ++e) {
+      for (int e = 0; e < HC; ++e) {
         const float p = ex2_approx(fmaf(sv[e], scale_log2, -mref));   // masked: ex2(-inf) = 0
         sv[e] = p;
         ps8[e & 7] += p;
@@ -322,42 +343,49 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
       l_run = l_run * alpha + psum;
       m_run = m_new;
       // P / O of the previous tile are free once its PV MMAs are done
-      if (j > 0) {
-        if (!mbar_wait(&bar->pv_done, (j - 1) & 1, status)) { ok = false; break; }
+      if (ok && j > 0) ok = mbar_wait(&bar->pv_done, (j - 1) & 1, status);
+      ok = __all_sync(0xffffffffu, ok);
+      if (ok && j > 0) {
         tc_fence_after();
         if (__any_sync(0xffffffffu, alpha < 1.f)) {
-          for (int c = 0; c < D / 32; ++c) {
+          for (int c = 0; c < D / 64; ++c) {
             uint32_t u[32];
-            tmem_ld_x32(tmem + lane_base + O_COL + c * 32, u);
+            const uint32_t col = O_COL + hf * (D / 2) + c * 32;
+            tmem_ld_x32(tmem + lane_base + col, u);
             tmem_ld_wait();
 #pragma unroll
             for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
-            tmem_st_x32(tmem + lane_base + O_COL + c * 32, u);
+            tmem_st_x32(tmem + lane_base + col, u);
           }
           tmem_st_wait();
         }
       }
-      // P * 256 -> e4m3, row r of the swizzled P tile
+      if (!ok) continue;                             // no barrier below: safe to skip
+      // P * 256 -> e4m3, this half's 64 columns of row r of the swizzled P tile
 #pragma unroll
-      for (int c = 0; c < BN / 16; ++c) {
+      for (int c = 0; c < HC / 16; ++c) {
         uint16_t pk[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e)
           pk[e] = f32x2_to_e4m3x2(sv[c * 16 + 2 * e] * 256.f, sv[c * 16 + 2 * e + 1] * 256.f);
-        *reinterpret_cast<uint4*>(sP + r * 128 + ((c ^ (r & 7)) * 16)) = *reinterpret_cast<uint4*>(pk);
+        const int cc = hf * (HC / 16) + c;
+        *reinterpret_cast<uint4*>(sP + r * 128 + ((cc ^ (r & 7)) * 16)) = *reinterpret_cast<uint4*>(pk);
       }
       fence_proxy_async();
       tc_fence_before();
       mbar_arrive(&bar->p_full);
     }
-    // ---- epilogue: O / (256 l) -> bf16 ----
+    // ---- epilogue: O / (256 l) -> bf16, l = the two halves' sums ----
+    bar->row_sum[hf][r] = l_run;
+    asm volatile("bar.sync 1, %0;" ::"n"(kSoftThreads) : "memory");
+    const float l_tot = l_run + bar->row_sum[hf ^ 1][r];
     if (ok && nt > 0) ok = mbar_wait(&bar->pv_done, (nt - 1) & 1, status);
     tc_fence_after();
-    const float inv = (ok && l_run > 0.f) ? 1.f / (256.f * l_run) : 0.f;
-    __nv_bfloat16* dst = out + ((size_t)(s0 + i) * Hq + head) * D;
-    for (int c = 0; c < D / 32; ++c) {
+    const float inv = (ok && l_tot > 0.f) ? 1.f / (256.f * l_tot) : 0.f;
+    __nv_bfloat16* dst = out + ((size_t)(s0 + i) * Hq + head) * D + hf * (D / 2);
+    for (int c = 0; c < D / 64; ++c) {
       uint32_t u[32];
-      tmem_ld_x32(tmem + lane_base + O_COL + c * 32, u);
+      tmem_ld_x32(tmem + lane_base + O_COL + hf * (D / 2) + c * 32, u);
       tmem_ld_wait();
       if (valid) {
         uint32_t w[16];
@@ -375,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
