@@ -394,16 +394,18 @@ def test_paged_attention_decode_kernel(D, Hq, Hkv, ctx_lens, splits, fmt, monkey
     assert rel_err(got, general) < 1e-2, rel_err(got, general)
 
 
-@pytest.mark.parametrize("kv", ["fp8", "int4"])
+@pytest.mark.parametrize("kv", ["fp8", "int4", "int4_p64"])
 @pytest.mark.parametrize("q_lens,ctx_lens", [([256], [0]), ([300, 77], [1000, 40]),
                                             ([130], [5000]), ([1024], [3000])])
 def test_fmha_prefill_tcgen05(q_lens, ctx_lens, kv, monkeypatch):
     """Causal chunked-prefill attention on tcgen05 (e4m3 QK and P V legs, TMEM accumulators,
     TMA-fed fp8 pages) against the fp32 oracle and the mma.sync tile kernel, GQA 6, head 256.
-    A 4-bit cache reaches the kernel through its pages dequantised into e4m3 copies."""
+    A 4-bit cache (the engine's 16-token pages, or 64-token ones) reaches the kernel through its
+    keys dequantised into 64-key e4m3 pages."""
     from vllm_sly_radiance_b200.quant.formats import kv4_quantize
     torch.manual_seed(21)
-    D, Hq, Hkv, bs = 256, 24, 4, 64
+    D, Hq, Hkv = 256, 24, 4
+    bs = 16 if kv == "int4" else 64
     meta, nblocks = _attn_meta(q_lens, ctx_lens, bs, Hq, Hkv, 1, DEV)
     if kv == "fp8":
         k = (torch.randn(nblocks, Hkv, bs, D) * 0.5).to(torch.float8_e4m3fn)

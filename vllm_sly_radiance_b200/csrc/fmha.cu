@@ -413,33 +413,38 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
 // ---------------------------------------------------------------------------------------------
 // int4 (KV4) pages -> e4m3 pages for the prefill kernel.  A 4-bit cache row is D/2 code bytes
 // (low nibble = even element) and one fp16 (scale, zero) pair per 16 elements: v = code * scale
-// + zero.  Before a prefill chunk attends over such a cache, every page its sequences reach is
-// dequantised once into a compact e4m3 copy (pages renumbered per sequence), and the tcgen05
-// kernel runs on that copy.  The copy costs one read of the 4-bit pages and one e4m3 write per
-// chunk and layer -- small next to the chunk's attention over the same keys.
-// grid (table width, sequences, kv heads); thread t converts 16-element groups of one page.
+// + zero.  Before a prefill chunk attends over such a cache, every key its sequences reach is
+// dequantised once into a compact e4m3 copy in 64-key pages (the TMA box of the prefill kernel;
+// the 4-bit cache may use smaller pages), pages renumbered per sequence, and the tcgen05 kernel
+// runs on that copy.  The copy costs one read of the 4-bit rows and one e4m3 write per chunk and
+// layer -- small next to the chunk's attention over the same keys.
+// grid (64-key pages of the table, sequences, kv heads); a thread converts 16-element groups.
 // ---------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) kv4_to_e4m3_pages_kernel(
     const uint8_t* __restrict__ k4, const uint8_t* __restrict__ v4,
-    const int* __restrict__ block_tables, int bt_stride, const int* __restrict__ seq_lens,
-    int Hkv, uint8_t* __restrict__ k8, uint8_t* __restrict__ v8, int* __restrict__ bt_out) {
+    const int* __restrict__ block_tables, int bt_stride, int nb, int block_size,
+    const int* __restrict__ seq_lens, int Hkv, uint8_t* __restrict__ k8, uint8_t* __restrict__ v8,
+    int* __restrict__ bt_out, int bt_out_stride) {
   pdl_wait();     // the chunk's keys were written by the preceding prologue
   pdl_trigger();
   constexpr int RB = D / 2 + D / 4;              // 4-bit row bytes (codes + fp16 pairs)
   constexpr int G = D / 16;                      // 16-element groups per row
   const int p = blockIdx.x, b = blockIdx.y, hk = blockIdx.z;
-  const int pages = (seq_lens[b] + PAGE - 1) / PAGE;
-  if (p >= pages) return;
+  const int len = seq_lens[b], pages = (len + PAGE - 1) / PAGE;
+  if (p >= pages || p * PAGE >= nb * block_size) return;
   int dst = p;
   for (int i = 0; i < b; ++i) dst += (seq_lens[i] + PAGE - 1) / PAGE;
-  const int src = block_tables[(size_t)b * bt_stride + p];
-  if (hk == 0 && threadIdx.x == 0) bt_out[(size_t)b * bt_stride + p] = dst;
-  const size_t s_off = ((size_t)src * Hkv + hk) * PAGE * RB;
+  if (hk == 0 && threadIdx.x == 0) bt_out[(size_t)b * bt_out_stride + p] = dst;
   const size_t d_off = ((size_t)dst * Hkv + hk) * PAGE * D;
+  const int last_key = min(len, nb * block_size) - 1;
   for (int idx = threadIdx.x; idx < 2 * PAGE * G; idx += blockDim.x) {
     const int which = idx / (PAGE * G), rem = idx % (PAGE * G);
     const int r = rem / G, g = rem % G;
-    const uint8_t* row = (which ? v4 : k4) + s_off + (size_t)r * RB;
+    // rows past the sequence repeat its last key (masked; their table slots may be unset)
+    const int key = min(p * PAGE + r, last_key);
+    const int blk = block_tables[(size_t)b * bt_stride + key / block_size];
+    const uint8_t* row = (which ? v4 : k4) +
+                         (((size_t)blk * Hkv + hk) * block_size + key % block_size) * RB;
     const uint2 codes = *reinterpret_cast<const uint2*>(row + g * 8);
     const __half2 sz = *reinterpret_cast<const __half2*>(row + D / 2 + g * 4);
     const float sc = __low2float(sz), zr = __high2float(sz);
@@ -455,6 +460,7 @@ __global__ void __launch_bounds__(256) kv4_to_e4m3_pages_kernel(
         *reinterpret_cast<const uint4*>(o);
   }
 }
+
 }  // namespace fmha
 
 static std::mutex g_fmha_mu;
@@ -511,30 +517,35 @@ void fmha_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache,
                             (float)(scale * 1.4426950408889634), (__nv_bfloat16*)out.data_ptr(), st));
 }
 
-// int4 caches [blocks, Hkv, 64, D/2 + D/4] -> compact e4m3 pages k8 / v8 [>= sum of pages, Hkv,
-// 64, D] for the sequences of the batch, with their renumbered block table in bt_out (same shape
-// as block_tables).
+// int4 caches [blocks, Hkv, block_size, D/2 + D/4] -> compact e4m3 pages k8 / v8 [>= sum of
+// 64-key pages, Hkv, 64, D] for the sequences of the batch, with their 64-key block table in
+// bt_out [B, ceil(table width * block_size / 64)].
 void kv4_to_e4m3_pages(torch::Tensor k4, torch::Tensor v4, torch::Tensor block_tables,
                        torch::Tensor seq_lens, torch::Tensor k8, torch::Tensor v8,
                        torch::Tensor bt_out) {
   using namespace fmha;
   const int B = block_tables.size(0), nb = block_tables.size(1), Hkv = k4.size(1);
+  const int bs = k4.size(2);
   TORCH_CHECK(k4.scalar_type() == at::kByte && v4.scalar_type() == at::kByte && k4.dim() == 4 &&
-                  k4.size(2) == PAGE && k4.size(3) == D / 2 + D / 4 && k4.is_contiguous() &&
-                  v4.is_contiguous(), "kv4_to_e4m3_pages: 4-bit cache [blocks, Hkv, 64, 192]");
+                  k4.size(3) == D / 2 + D / 4 && k4.is_contiguous() && v4.is_contiguous() && bs >= 1,
+              "kv4_to_e4m3_pages: 4-bit cache [blocks, Hkv, block_size, 192]");
+  const int p64 = (nb * bs + PAGE - 1) / PAGE;
   TORCH_CHECK(k8.scalar_type() == at::kFloat8_e4m3fn && v8.scalar_type() == at::kFloat8_e4m3fn &&
                   k8.size(1) == Hkv && k8.size(2) == PAGE && k8.size(3) == D && k8.is_contiguous() &&
-                  v8.is_contiguous() && k8.size(0) >= (int64_t)B * nb, "kv4_to_e4m3_pages: e4m3 pages");
-  TORCH_CHECK(bt_out.sizes() == block_tables.sizes() && bt_out.stride(0) == block_tables.stride(0) &&
-                  bt_out.scalar_type() == at::kInt, "kv4_to_e4m3_pages: block table");
+                  v8.is_contiguous() && k8.size(0) >= (int64_t)B * p64, "kv4_to_e4m3_pages: e4m3 pages");
+  TORCH_CHECK(bt_out.dim() == 2 && bt_out.size(0) == B && bt_out.size(1) >= p64 &&
+                  bt_out.stride(1) == 1 && bt_out.scalar_type() == at::kInt,
+              "kv4_to_e4m3_pages: 64-key block table");
+  TORCH_CHECK(block_tables.stride(1) == 1 && block_tables.scalar_type() == at::kInt,
+              "kv4_to_e4m3_pages: block table rows");
   if (B == 0 || nb == 0) return;
   const at::cuda::CUDAGuard guard(k4.device());
-  C10_CUDA_CHECK(launch_pdl(kv4_to_e4m3_pages_kernel, dim3(nb, B, Hkv), dim3(256), 0,
+  C10_CUDA_CHECK(launch_pdl(kv4_to_e4m3_pages_kernel, dim3(p64, B, Hkv), dim3(256), 0,
                             at::cuda::getCurrentCUDAStream(), (const uint8_t*)k4.data_ptr(),
                             (const uint8_t*)v4.data_ptr(), block_tables.data_ptr<int>(),
-                            (int)block_tables.stride(0), seq_lens.data_ptr<int>(), Hkv,
+                            (int)block_tables.stride(0), nb, bs, seq_lens.data_ptr<int>(), Hkv,
                             (uint8_t*)k8.data_ptr(), (uint8_t*)v8.data_ptr(),
-                            bt_out.data_ptr<int>()));
+                            bt_out.data_ptr<int>(), (int)bt_out.stride(0)));
 }
 
 }  // namespace rad

@@ -437,20 +437,24 @@ def paged_attention(q, k_cache, v_cache, meta, scale: float, causal: bool = True
     decode = (meta.num_tokens == meta.num_seqs and Hq // k_cache.shape[1] <= 16
               and _ATTN_DECODE)
     if (not decode and _FMHA and causal and window == 0 and meta.num_splits == 1 and D == 256
-            and k_cache.shape[2] == 64 and k_cache.dtype in (torch.float8_e4m3fn, torch.uint8)):
+            and ((k_cache.shape[2] == 64 and k_cache.dtype == torch.float8_e4m3fn)
+                 or k_cache.dtype == torch.uint8)):
         # prefill on tcgen05 (e4m3 QK / PV legs, TMEM accumulators, TMA-fed pages)
         kc, vc, bt = k_cache, v_cache, meta.block_tables
         if k_cache.dtype == torch.uint8:
-            # 4-bit cache: the pages this chunk reaches, dequantised once into e4m3 pages
+            # 4-bit cache (any page size): the keys this chunk reaches, dequantised once into
+            # 64-key e4m3 pages renumbered per sequence
             B, nb = bt.shape
             Hkv = k_cache.shape[1]
+            p64 = (nb * k_cache.shape[2] + 63) // 64
             page = Hkv * 64 * D
-            ws = workspace(q.device, "kv4_e4m3", (2 * B * nb * page + 3) // 4 + B * nb + 64)
+            npg = B * p64
+            ws = workspace(q.device, "kv4_e4m3", (2 * npg * page + 255) // 256 * 64 + npg + 64)
             raw = ws.view(torch.uint8)
-            kc = raw[:B * nb * page].view(torch.float8_e4m3fn).view(B * nb, Hkv, 64, D)
-            vc = raw[B * nb * page:2 * B * nb * page].view(torch.float8_e4m3fn).view(B * nb, Hkv, 64, D)
-            off = (2 * B * nb * page + 255) // 256 * 64          # int32 words, 256-byte aligned
-            bt = ws[off:off + B * nb].view(B, nb)
+            kc = raw[:npg * page].view(torch.float8_e4m3fn).view(npg, Hkv, 64, D)
+            vc = raw[npg * page:2 * npg * page].view(torch.float8_e4m3fn).view(npg, Hkv, 64, D)
+            off = (2 * npg * page + 255) // 256 * 64          # int32 words, 256-byte aligned
+            bt = ws[off:off + npg].view(B, p64)
             ext().kv4_to_e4m3_pages(k_cache, v_cache, meta.block_tables, meta.seq_lens, kc, vc, bt)
         ext().fmha_prefill(q, kc, vc, bt, meta.seq_lens, meta.query_start_loc, meta.tile_seq,
                            meta.tile_row0, scale, out, status_word(q.device))
