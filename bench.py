@@ -235,8 +235,8 @@ def main():
 
     if args.prefill_profile:
         barrier()
-        eng.add_request(rand_prompt(args.prompt_len), SamplingParams(temperature=0, max_tokens=1,
-                                                                      ignore_eos=True), "pfp")
+        eng.add_request(rand_prompt(pf_lens[-1]), SamplingParams(temperature=0, max_tokens=1,
+                                                                   ignore_eos=True), "pfp")
         profile_steps(eng, args.prefill_profile if rank == 0 else None,
                       lambda: eng.has_unfinished_requests())
 

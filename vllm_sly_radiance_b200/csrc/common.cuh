@@ -84,7 +84,25 @@ DEVI uint64_t wait_limit_ns(const int* status, int slot, uint64_t dflt) {
   return us > 0 ? (uint64_t)us * 1000ull : dflt;
 }
 
-// Bounded wait (200 ms of wall clock by default).  Returns false (and flags *err) on timeout.
+// Named-barrier sync of `nthreads` threads (barrier `id`) that ORs a per-thread flag: every
+// participant gets the same answer, so a loop that leaves on it leaves in all of its warps
+// together (a warp that left alone would strand the others at the next sync of the barrier).
+DEVI bool bar_sync_or(int id, int nthreads, bool flag) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.b32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((int)flag), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
+// Bounded wait (200 ms of wall clock by default).  A warp whose partner warps wait on the
+// preceding kernel (griddepcontrol.wait) waits on it too before its first bounded wait, so the
+// bound never covers the preceding kernel's run time.  Returns false (and flags *err) on timeout.
 DEVI bool mbar_wait(uint64_t* bar, uint32_t phase, int* err) {
   if (mbar_try_wait(bar, phase)) return true;
   const uint64_t t0 = globaltimer_ns();

@@ -311,6 +311,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (elect_one()) {
+      pdl_wait();                      // the activation tiles land after the preceding kernel
       bool ok = true;
       for (int i = 0; i < nk; ++i) {
         const int s = i % C::STAGES;
@@ -419,10 +420,10 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
       for (int i = 0; i < nk; ++i) {
         const int s = i % C::STAGES;
         const uint32_t ph = (i / C::STAGES) & 1;
-        if (!mbar_wait(&empty_bar[s], ph ^ 1, status)) { *abort_flag = 1; break; }
+        const bool got = mbar_wait(&empty_bar[s], ph ^ 1, status);
         const int jb = (kt0 + i) * (BK / 8);
         const int c = (pt - jb) & 127;                  // chunk of this stage owned by pt, if < 16
-        if (c < BK / 8) {
+        if (got && c < BK / 8) {
           const int j = jb + c;
           uint2 val = make_uint2(0, 0);
 #pragma unroll
@@ -432,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, Cfg<BN>::MIN_BLOCKS)
           *reinterpret_cast<uint2*>(slot + (c >> 1) * 16 + (c & 1) * 8) = val;   // row 0: no swizzle
         }
         fence_proxy_async();                            // generic-proxy writes -> tensor core
-        asm volatile("bar.sync 2, 128;" ::: "memory");
+        if (bar_sync_or(2, 128, !got)) { *abort_flag = 1; break; }   // all four warps leave together
         if (pt == 0) mbar_arrive(&full_bar[s]);
       }
     }
@@ -697,6 +698,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(
   const uint32_t tmem_acc = bars->tmem;
   const uint32_t tmem_sfa = tmem_acc + P_SFA_COL;
   const uint32_t tmem_sfb = tmem_acc + P_SFB_COL;
+  // a failed wait stops both CTAs of the pair: the flag is raised here and in the partner
+  const uint32_t abort_peer = mapa_shared(smem_u32(&bars->abort), rank ^ 1u);
+  auto pair_abort = [&]() {
+    *(volatile int*)&bars->abort = 1;
+    asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(abort_peer), "r"(1) : "memory");
+  };
   if (warp >= 2) {              // activation scale factors: UE8M0 1.0 everywhere
     const int q = warp & 3;
     uint32_t ones[8];
@@ -726,7 +733,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(
         for (int kt = 0; kt < k_tiles; ++kt, ++it) {
           const int s = it % P_STAGES;
           const uint32_t ph = (it / P_STAGES) & 1;
-          if (!mbar_wait(&bars->empty[s], ph ^ 1, status)) { bars->abort = 1; break; }
+          if (!mbar_wait(&bars->empty[s], ph ^ 1, status)) { pair_abort(); break; }
           uint8_t* st = smem + s * P_STAGE;
           const uint32_t full = mapa_shared(smem_u32(&bars->full[s]), 0);
           if (rank == 0) mbar_arrive_expect_tx(&bars->full[s], tx);
@@ -740,11 +747,12 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(
   } else if (warp == 1) {
     // ---------------- MMA issuer (leader) ----------------
     if (rank == 0 && elect_one()) {
+      pdl_wait();                                     // the producers' tiles follow it
       const uint32_t empty_peer0 = mapa_shared(smem_u32(&bars->empty[0]), 1);
       const uint32_t accf_peer0 = mapa_shared(smem_u32(&bars->acc_full[0]), 1);
       uint32_t it = 0, tc = 0;
       bool ok = true;
-      for (int t = pair; t < num_tiles && ok; t += npairs, ++tc) {
+      for (int t = pair; t < num_tiles && ok && !*(volatile int*)&bars->abort; t += npairs, ++tc) {
         const int ab = tc & 1;                        // accumulator of this tile
         if (!mbar_wait(&bars->acc_empty[ab], ((tc >> 1) & 1) ^ 1, status)) { ok = false; break; }
         tc_fence_after();
@@ -770,7 +778,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(
         commit_pair(smem_u32(&bars->acc_full[ab]));
         commit_pair(accf_peer0 + (uint32_t)(ab * sizeof(uint64_t)));
       }
-      if (!ok) bars->abort = 1;
+      if (!ok) pair_abort();
     }
   } else {
     // ---------------- epilogue (both CTAs) ----------------
@@ -784,7 +792,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(
       const int ab = tc & 1;
       const uint32_t lane_base = lane_base0 + (uint32_t)(ab * P_BN);
       const bool got = mbar_wait(&bars->acc_full[ab], (tc >> 1) & 1, status);
-      if (!got) bars->abort = 1;
+      if (!got) pair_abort();
       tc_fence_after();
       const int n = (t % n_tiles) * P_WROWS + (int)rank * BM + row;
       const int mt0 = (t / n_tiles) * P_BN;
@@ -816,9 +824,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_pair_kernel(
       }
       // the accumulator is free for the pair's next tile once all four warps have read it
       tc_fence_before();
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      const bool stop = bar_sync_or(1, 128, *(volatile int*)&bars->abort != 0);
       if (threadIdx.x == 64) mbar_arrive_cluster(acc_empty0 + (uint32_t)(ab * sizeof(uint64_t)));
-      if (*(volatile int*)&bars->abort) break;
+      if (stop) break;                                 // the same answer in all four warps
     }
   }
 

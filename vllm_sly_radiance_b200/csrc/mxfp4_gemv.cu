@@ -206,6 +206,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer: one accumulation per segment (a run of units of one tile) ----
     if (elect_one()) {
+      pdl_wait();                 // the activation tiles land after the preceding kernel
       bool ok = true;
       int seg = 0;
       for (int i = 0; i < nu && ok; ++seg) {
