@@ -106,6 +106,37 @@ DEVI float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// Softmax arithmetic on the sm_100 paired / three-input forms: one instruction per two scores
+// for the scale-and-shift and the running sums, one per two for the row maximum.
+DEVI float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+DEVI float2 fadd2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+DEVI float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+// two non-negative, finite P values -> e4m3 pair, lo in the low byte (saturating at 448)
+DEVI uint32_t p_to_e4m3x2(float lo, float hi) {
+  uint16_t d;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(d) : "f"(hi), "f"(lo));
+  return d;
+}
 
 struct Bars {
   uint64_t q_full;
@@ -290,8 +321,11 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
     mbar_arrive(&bar->q_full);
 
     constexpr int HC = BN / 2;                         // key columns per half
-    float m_run = -INFINITY, l_run = 0.f;              // l_run: this half's share of the sum
+    static_assert(HC == 64, "softmax half-tile of 64 keys");
+    // l_run: this half's share of the row sum of 256 p (the e4m3 P operand's scale)
+    float m_run = -INFINITY, l_run = 0.f;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const float2 sc2 = make_float2(scale_log2, scale_log2);
     // Every softmax thread runs all nt iterations and reaches each named barrier: a failed wait
     // only turns the rest of the work off (ok is warp-uniform), so no barrier is left short.
     bool ok = true;
@@ -299,6 +333,10 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
       const int sb = j & 1;
       if (ok) ok = mbar_wait(&bar->s_full[sb], (j >> 1) & 1, status);
       ok = __all_sync(0xffffffffu, ok);
+      const int kbase = j * BN + hf * HC;
+      // keys [kbase, kbase + 64) all live for every valid row of the warp: no causal mask
+      const bool unmasked =
+          __all_sync(0xffffffffu, !valid || (kbase + HC - 1 <= pos && kbase + HC <= L));
       float sv[HC];
       if (ok) {
         tc_fence_after();
@@ -307,10 +345,14 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
           uint32_t u[32];
           tmem_ld_x32(tmem + lane_base + S_COL + sb * BN + hf * HC + c * 32, u);
           tmem_ld_wait();
+          if (unmasked) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const int key = j * BN + hf * HC + c * 32 + e;
-            sv[c * 32 + e] = (valid && key <= pos && key < L) ? __uint_as_float(u[e]) : -INFINITY;
+            for (int e = 0; e < 32; ++e) sv[c * 32 + e] = __uint_as_float(u[e]);
+          } else {
+            // live keys: key <= pos and key < L, i.e. e < lim within these 32
+            const int lim = valid ? min(pos + 1, L) - (kbase + c * 32) : 0;
+#pragma unroll
+            for (int e = 0; e < 32; ++e) sv[c * 32 + e] = e < lim ? __uint_as_float(u[e]) : -INFINITY;
           }
         }
         tc_fence_before();
@@ -321,26 +363,44 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
       }
       float mx8[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) mx8[e] = sv[e];
-#pragma unroll
-      for (int e = 8; e < HC; ++e) mx8[e & 7] = fmaxf(mx8[e & 7], sv[e]);
-      float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                       fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+      for (int k = 0; k < 8; ++k) {
+        float t = fmax3(sv[k], sv[k + 8], sv[k + 16]);
+        t = fmax3(t, sv[k + 24], sv[k + 32]);
+        t = fmax3(t, sv[k + 40], sv[k + 48]);
+        mx8[k] = fmaxf(t, sv[k + 56]);
+      }
+      float mx = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]),
+                       fmaxf(mx8[6], mx8[7]));
       bar->row_max[sb][hf][r] = mx;
       asm volatile("bar.sync 1, %0;" ::"n"(kSoftThreads) : "memory");
       mx = fmaxf(mx, bar->row_max[sb][hf ^ 1][r]);
       const float m_new = fmaxf(m_run, mx * scale_log2);   // scale > 0: max commutes with it
       const float mref = m_new == -INFINITY ? 0.f : m_new;
       const float alpha = ex2_approx(m_run - mref);  // m_run = -inf -> 0 (O is still zero)
-      float ps8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      // 256 p = 2^(s * scale_log2 - mref + 8): the x256 of the e4m3 P operand rides in the
+      // exponent; masked scores give ex2(-inf) = 0.  P goes to e4m3 as it is made.
+      const float2 off2 = make_float2(8.f - mref, 8.f - mref);
+      float2 acc0 = make_float2(0.f, 0.f), acc1 = acc0, acc2 = acc0, acc3 = acc0;
+      uint32_t pw[HC / 4];
 #pragma unroll
-      for (int e = 0; e < HC; ++e) {
-        const float p = ex2_approx(fmaf(sv[e], scale_log2, -mref));   // masked: ex2(-inf) = 0
-        sv[e] = p;
-        ps8[e & 7] += p;
+      for (int e = 0; e < HC; e += 8) {
+        const float2 x0 = ffma2(make_float2(sv[e], sv[e + 1]), sc2, off2);
+        const float2 x1 = ffma2(make_float2(sv[e + 2], sv[e + 3]), sc2, off2);
+        const float2 x2 = ffma2(make_float2(sv[e + 4], sv[e + 5]), sc2, off2);
+        const float2 x3 = ffma2(make_float2(sv[e + 6], sv[e + 7]), sc2, off2);
+        const float2 p0 = make_float2(ex2_approx(x0.x), ex2_approx(x0.y));
+        const float2 p1 = make_float2(ex2_approx(x1.x), ex2_approx(x1.y));
+        const float2 p2 = make_float2(ex2_approx(x2.x), ex2_approx(x2.y));
+        const float2 p3 = make_float2(ex2_approx(x3.x), ex2_approx(x3.y));
+        acc0 = fadd2(acc0, p0);
+        acc1 = fadd2(acc1, p1);
+        acc2 = fadd2(acc2, p2);
+        acc3 = fadd2(acc3, p3);
+        pw[e / 4] = p_to_e4m3x2(p0.x, p0.y) | (p_to_e4m3x2(p1.x, p1.y) << 16);
+        pw[e / 4 + 1] = p_to_e4m3x2(p2.x, p2.y) | (p_to_e4m3x2(p3.x, p3.y) << 16);
       }
-      const float psum = ((ps8[0] + ps8[1]) + (ps8[2] + ps8[3])) + ((ps8[4] + ps8[5]) + (ps8[6] + ps8[7]));
-      l_run = l_run * alpha + psum;
+      const float2 accs = fadd2(fadd2(acc0, acc1), fadd2(acc2, acc3));
+      l_run = l_run * alpha + (accs.x + accs.y);
       m_run = m_new;
       // P / O of the previous tile are free once its PV MMAs are done
       if (ok && j > 0) ok = mbar_wait(&bar->pv_done, (j - 1) & 1, status);
@@ -361,27 +421,24 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
         }
       }
       if (!ok) continue;                             // no barrier below: safe to skip
-      // P * 256 -> e4m3, this half's 64 columns of row r of the swizzled P tile
+      // this half's 64 e4m3 columns of row r of the swizzled P tile
 #pragma unroll
       for (int c = 0; c < HC / 16; ++c) {
-        uint16_t pk[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e)
-          pk[e] = f32x2_to_e4m3x2(sv[c * 16 + 2 * e] * 256.f, sv[c * 16 + 2 * e + 1] * 256.f);
         const int cc = hf * (HC / 16) + c;
-        *reinterpret_cast<uint4*>(sP + r * 128 + ((cc ^ (r & 7)) * 16)) = *reinterpret_cast<uint4*>(pk);
+        *reinterpret_cast<uint4*>(sP + r * 128 + ((cc ^ (r & 7)) * 16)) =
+            make_uint4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]);
       }
       fence_proxy_async();
       tc_fence_before();
       mbar_arrive(&bar->p_full);
     }
-    // ---- epilogue: O / (256 l) -> bf16, l = the two halves' sums ----
+    // ---- epilogue: O / l -> bf16, l = the two halves' sums of 256 p ----
     bar->row_sum[hf][r] = l_run;
     asm volatile("bar.sync 1, %0;" ::"n"(kSoftThreads) : "memory");
     const float l_tot = l_run + bar->row_sum[hf ^ 1][r];
     if (ok && nt > 0) ok = mbar_wait(&bar->pv_done, (nt - 1) & 1, status);
     tc_fence_after();
-    const float inv = (ok && l_tot > 0.f) ? 1.f / (256.f * l_tot) : 0.f;
+    const float inv = (ok && l_tot > 0.f) ? 1.f / l_tot : 0.f;      // l_tot sums 256 p
     __nv_bfloat16* dst = out + ((size_t)(s0 + i) * Hq + head) * D + hf * (D / 2);
     for (int c = 0; c < D / 64; ++c) {
       uint32_t u[32];
