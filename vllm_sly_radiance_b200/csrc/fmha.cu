@@ -52,7 +52,11 @@ constexpr int STAGES = 2;
 constexpr int kSoftThreads = 256;      // softmax / epilogue warps 0-7
 constexpr int kTmaWarp = 8, kMmaWarp = 9;
 constexpr int kThreads = kSoftThreads + 64;
-constexpr int SMEM_BYTES = 1024 + Q_BYTES + STAGES * 2 * KV_BYTES + P_BYTES + 4096;   // + barriers
+constexpr int P_BUFS = 2;              // P tiles: softmax(j) writes one while PV(j - 1) reads the other
+constexpr int SMEM_BYTES = 1024 + Q_BYTES + STAGES * 2 * KV_BYTES + P_BUFS * P_BYTES + 4096;   // + barriers
+// The running row maximum is raised (and O rescaled) only when a tile's maximum exceeds it by more
+// than this many log2 units; P = 2^(s - m + 8) then stays below 2^8.75 = 430 < 448 (e4m3 max).
+constexpr float kRescaleLog2 = 0.75f;
 constexpr uint32_t O_COL = 0, S_COL = 256;      // TMEM: O [0, 256), S buffers [256, 384), [384, 512)
 
 // kind::f8f6f4 instruction descriptor: e4m3 x e4m3 -> fp32, M = 128
@@ -142,7 +146,7 @@ struct Bars {
   uint64_t q_full;
   uint64_t k_full[STAGES], v_full[STAGES], kv_empty[STAGES];
   uint64_t s_full[2], s_empty[2];
-  uint64_t p_full, pv_done;
+  uint64_t p_full[P_BUFS], pv_done[P_BUFS];
   float row_max[2][2][BM];      // [S buffer][half][row]: the halves' partial row maxima
   float row_sum[2][BM];         // [half][row]: the halves' final sums
   uint32_t tmem_slot;
@@ -161,7 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
   uint8_t* sQ = smem;
   uint8_t* sKV = sQ + Q_BYTES;                       // stage s: K at s * 2 * KV_BYTES, V after it
   uint8_t* sP = sKV + STAGES * 2 * KV_BYTES;
-  Bars* bar = reinterpret_cast<Bars*>(sP + P_BYTES);
+  Bars* bar = reinterpret_cast<Bars*>(sP + P_BUFS * P_BYTES);
 
   pdl_wait();     // q (prologue) and the cache writes precede this kernel
   pdl_trigger();
@@ -193,8 +197,10 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
       mbar_init(&bar->s_full[s], 1);
       mbar_init(&bar->s_empty[s], kSoftThreads);
     }
-    mbar_init(&bar->p_full, kSoftThreads);
-    mbar_init(&bar->pv_done, 1);
+    for (int s = 0; s < P_BUFS; ++s) {
+      mbar_init(&bar->p_full[s], kSoftThreads);
+      mbar_init(&bar->pv_done[s], 1);
+    }
     bar->abort = 0;
     fence_mbar_init();
   }
@@ -266,17 +272,17 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
       if (ok && nt > 0) ok = issue_s(0);
       for (int j = 0; j < nt && ok; ++j) {
         if (j + 1 < nt && !issue_s(j + 1)) { ok = false; break; }
-        const int s = j % STAGES;
-        if (!mbar_wait(&bar->p_full, j & 1, status) ||
+        const int s = j % STAGES, pb = j & 1;
+        if (!mbar_wait(&bar->p_full[pb], (j >> 1) & 1, status) ||
             !mbar_wait(&bar->v_full[s], (j / STAGES) & 1, status)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t pa = smem_u32(sP);
+        const uint32_t pa = smem_u32(sP + pb * P_BYTES);
         const uint32_t va = smem_u32(sKV + s * 2 * KV_BYTES + KV_BYTES);
 #pragma unroll
         for (int kk = 0; kk < BN / 32; ++kk)
           mma_f8(tmem + O_COL, sdesc_sw128(pa + kk * 32), sdesc_sw128_mn(va + kk * 32 * 128, HALF),
                  idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(&bar->pv_done);
+        mma_commit(&bar->pv_done[pb]);
         mma_commit(&bar->kv_empty[s]);
       }
       if (!ok) bar->abort = 1;
@@ -340,19 +346,23 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
       float sv[HC];
       if (ok) {
         tc_fence_after();
+        uint32_t u0[32], u1[32];
+        tmem_ld_x32(tmem + lane_base + S_COL + sb * BN + hf * HC, u0);
+        tmem_ld_x32(tmem + lane_base + S_COL + sb * BN + hf * HC + 32, u1);
+        tmem_ld_wait();
+        if (unmasked) {
 #pragma unroll
-        for (int c = 0; c < HC / 32; ++c) {
-          uint32_t u[32];
-          tmem_ld_x32(tmem + lane_base + S_COL + sb * BN + hf * HC + c * 32, u);
-          tmem_ld_wait();
-          if (unmasked) {
+          for (int e = 0; e < 32; ++e) {
+            sv[e] = __uint_as_float(u0[e]);
+            sv[32 + e] = __uint_as_float(u1[e]);
+          }
+        } else {
+          // live keys: key <= pos and key < L, i.e. e < lim within this half-tile
+          const int lim = valid ? min(pos + 1, L) - kbase : 0;
 #pragma unroll
-            for (int e = 0; e < 32; ++e) sv[c * 32 + e] = __uint_as_float(u[e]);
-          } else {
-            // live keys: key <= pos and key < L, i.e. e < lim within these 32
-            const int lim = valid ? min(pos + 1, L) - (kbase + c * 32) : 0;
-#pragma unroll
-            for (int e = 0; e < 32; ++e) sv[c * 32 + e] = e < lim ? __uint_as_float(u[e]) : -INFINITY;
+          for (int e = 0; e < 32; ++e) {
+            sv[e] = e < lim ? __uint_as_float(u0[e]) : -INFINITY;
+            sv[32 + e] = e + 32 < lim ? __uint_as_float(u1[e]) : -INFINITY;
           }
         }
         tc_fence_before();
@@ -374,9 +384,14 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
       bar->row_max[sb][hf][r] = mx;
       asm volatile("bar.sync 1, %0;" ::"n"(kSoftThreads) : "memory");
       mx = fmaxf(mx, bar->row_max[sb][hf ^ 1][r]);
-      const float m_new = fmaxf(m_run, mx * scale_log2);   // scale > 0: max commutes with it
+      // scale > 0: the max commutes with it.  The running maximum moves only when the tile's
+      // exceeds it by more than kRescaleLog2 (both halves of a row decide alike: same inputs).
+      const float mx_s = mx * scale_log2;
+      const bool grow = mx_s > m_run + kRescaleLog2;       // m_run = -inf: any finite maximum
+      const float m_new = grow ? mx_s : m_run;
       const float mref = m_new == -INFINITY ? 0.f : m_new;
-      const float alpha = ex2_approx(m_run - mref);  // m_run = -inf -> 0 (O is still zero)
+      const bool need = grow && m_run != -INFINITY;        // O holds terms at the old maximum
+      const float alpha = need ? ex2_approx(m_run - m_new) : (grow ? 0.f : 1.f);
       // 256 p = 2^(s * scale_log2 - mref + 8): the x256 of the e4m3 P operand rides in the
       // exponent; masked scores give ex2(-inf) = 0.  P goes to e4m3 as it is made.
       const float2 off2 = make_float2(8.f - mref, 8.f - mref);
@@ -402,19 +417,24 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
       const float2 accs = fadd2(fadd2(acc0, acc1), fadd2(acc2, acc3));
       l_run = l_run * alpha + (accs.x + accs.y);
       m_run = m_new;
-      // P / O of the previous tile are free once its PV MMAs are done
-      if (ok && j > 0) ok = mbar_wait(&bar->pv_done, (j - 1) & 1, status);
+      // O may be rescaled once PV(j - 1) is done; P buffer pb is free once PV(j - 2) is done
+      // (implied by PV(j - 1): the MMAs complete in issue order)
+      const int pb = j & 1;
+      const bool resc = __any_sync(0xffffffffu, need) && j > 0;
+      if (ok && resc) ok = mbar_wait(&bar->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, status);
+      else if (ok && j >= 2) ok = mbar_wait(&bar->pv_done[pb], ((j >> 1) - 1) & 1, status);
       ok = __all_sync(0xffffffffu, ok);
-      if (ok && j > 0) {
+      if (ok && resc) {
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha < 1.f)) {
+        {
+          const float a_o = need ? alpha : 1.f;
           for (int c = 0; c < D / 64; ++c) {
             uint32_t u[32];
             const uint32_t col = O_COL + hf * (D / 2) + c * 32;
             tmem_ld_x32(tmem + lane_base + col, u);
             tmem_ld_wait();
 #pragma unroll
-            for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * alpha);
+            for (int e = 0; e < 32; ++e) u[e] = __float_as_uint(__uint_as_float(u[e]) * a_o);
             tmem_st_x32(tmem + lane_base + col, u);
           }
           tmem_st_wait();
@@ -425,18 +445,18 @@ __global__ void __launch_bounds__(kThreads, 1) fmha_prefill_kernel(
 #pragma unroll
       for (int c = 0; c < HC / 16; ++c) {
         const int cc = hf * (HC / 16) + c;
-        *reinterpret_cast<uint4*>(sP + r * 128 + ((cc ^ (r & 7)) * 16)) =
+        *reinterpret_cast<uint4*>(sP + pb * P_BYTES + r * 128 + ((cc ^ (r & 7)) * 16)) =
             make_uint4(pw[4 * c], pw[4 * c + 1], pw[4 * c + 2], pw[4 * c + 3]);
       }
       fence_proxy_async();
       tc_fence_before();
-      mbar_arrive(&bar->p_full);
+      mbar_arrive(&bar->p_full[pb]);
     }
     // ---- epilogue: O / l -> bf16, l = the two halves' sums of 256 p ----
     bar->row_sum[hf][r] = l_run;
     asm volatile("bar.sync 1, %0;" ::"n"(kSoftThreads) : "memory");
     const float l_tot = l_run + bar->row_sum[hf ^ 1][r];
-    if (ok && nt > 0) ok = mbar_wait(&bar->pv_done, (nt - 1) & 1, status);
+    if (ok && nt > 0) ok = mbar_wait(&bar->pv_done[(nt - 1) & 1], ((nt - 1) >> 1) & 1, status);
     tc_fence_after();
     const float inv = (ok && l_tot > 0.f) ? 1.f / l_tot : 0.f;      // l_tot sums 256 p
     __nv_bfloat16* dst = out + ((size_t)(s0 + i) * Hq + head) * D + hf * (D / 2);
